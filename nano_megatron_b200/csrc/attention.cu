@@ -1,0 +1,728 @@
+// Causal flash attention, forward and backward, for sm_100a.
+//
+// Layout: q, k, v are read in place from the fused QKV projection output
+// ([tokens, (Hq + 2 Hkv) * D] bf16, arbitrary row/batch strides), so no
+// transpose or repeat_interleave is ever materialised; GQA is native (a KV
+// head serves Hq / Hkv query heads). Causality is decided by absolute
+// positions (q_offset + i vs k_offset + j) so the same kernels serve local
+// attention and the context-parallel all-gather / ring variants; key blocks
+// that lie entirely above the diagonal are skipped.
+//
+// Softmax runs in base 2: scores are pre-multiplied by softmax_scale*log2(e);
+// the saved log-sum-exp `lse` is in the same base-2 units.
+//
+// Backward (one CTA per key block and KV head, looping over the query heads
+// of its group): dK/dV accumulate in registers, dQ is accumulated in fp32
+// with vector reductions and converted (plus inverse RoPE) by a small tail
+// kernel. Inverse RoPE for dK is applied in registers before the store, so the
+// QKV weight-gradient GEMM consumes pre-rotation gradients directly.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+
+#include "common.cuh"
+
+namespace nmb {
+namespace attn {
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool pred) {
+  const uint32_t s = smem_u32(smem);
+  const int n = pred ? 16 : 0;
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(n)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Swizzled [rows x D] bf16 tile: 16-byte chunk c of row r lives at chunk
+// (c & ~7) | ((c ^ r) & 7). Returns a byte offset.
+template <int D>
+__device__ __forceinline__ uint32_t swz(int row, int col) {
+  const int chunk = col >> 3;
+  const int phys = (chunk & ~7) | ((chunk ^ row) & 7);
+  return static_cast<uint32_t>(row * D * 2 + phys * 16 + (col & 7) * 2);
+}
+
+struct FwdParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  int64_t q_row, k_row, v_row, q_batch, k_batch, v_batch;
+  __nv_bfloat16* o;
+  int64_t o_row, o_batch;
+  float* lse;  // [B, Hq, Sq] base-2
+  int B, Hq, Hkv, Sq, Sk;
+  int q_offset, k_offset;
+  int causal;
+  float scale_log2;
+};
+
+// Load a [ROWS x D] tile (rows starting at r0 of a strided matrix) into swizzled smem.
+template <int ROWS, int D, int NT>
+__device__ __forceinline__ void load_tile(uint8_t* smem, const __nv_bfloat16* base, int64_t row_stride,
+                                          int r0, int rmax) {
+  constexpr int kChunks = ROWS * D / 8;
+  for (int i = threadIdx.x; i < kChunks; i += NT) {
+    const int r = i / (D / 8);
+    const int c = (i % (D / 8)) * 8;
+    const int gr = r0 + r;
+    const bool ok = gr < rmax;
+    const __nv_bfloat16* src = base + static_cast<int64_t>(ok ? gr : 0) * row_stride + c;
+    cp_async16(smem + swz<D>(r, c), src, ok);
+  }
+}
+
+// Forward: 128 query rows per CTA (8 warps x 16 rows), 64-key blocks, double buffered.
+template <int D>
+__global__ void __launch_bounds__(256) flash_fwd_kernel(const FwdParams p) {
+  constexpr int BM = 128, BN = 64, NT = 256;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sQ = smem;
+  uint8_t* sK = sQ + BM * D * 2;
+  uint8_t* sV = sK + 2 * BN * D * 2;
+
+  const int mb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int kvh = h / (p.Hq / p.Hkv);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int m0 = mb * BM;
+
+  const __nv_bfloat16* qb = p.q + b * p.q_batch + static_cast<int64_t>(h) * D;
+  const __nv_bfloat16* kb = p.k + b * p.k_batch + static_cast<int64_t>(kvh) * D;
+  const __nv_bfloat16* vb = p.v + b * p.v_batch + static_cast<int64_t>(kvh) * D;
+
+  // Key range this query block can see.
+  int n_end = p.Sk;
+  if (p.causal) {
+    const int last_q_pos = p.q_offset + min(m0 + BM, p.Sq) - 1;
+    n_end = min(p.Sk, last_q_pos - p.k_offset + 1);
+  }
+  const int num_nb = n_end > 0 ? (n_end + BN - 1) / BN : 0;
+
+  load_tile<BM, D, NT>(sQ, qb, p.q_row, m0, p.Sq);
+  cp_async_commit();
+  if (num_nb > 0) {
+    load_tile<BN, D, NT>(sK, kb, p.k_row, 0, p.Sk);
+    load_tile<BN, D, NT>(sV, vb, p.v_row, 0, p.Sk);
+  }
+  cp_async_commit();
+  cp_async_wait<1>();
+  __syncthreads();
+
+  // Q fragments for this warp's 16 rows.
+  uint32_t qf[D / 16][4];
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+    const int c = kk * 16 + (lane >> 4) * 8;
+    ldsm_x4(smem_u32(sQ) + swz<D>(r, c), qf[kk][0], qf[kk][1], qf[kk][2], qf[kk][3]);
+  }
+
+  float o_acc[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o_acc[i][0] = o_acc[i][1] = o_acc[i][2] = o_acc[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+  const int qpos0 = p.q_offset + m0 + warp * 16 + g;  // row g; row g+8 is qpos0+8
+
+  for (int nb = 0; nb < num_nb; ++nb) {
+    const int buf = nb & 1;
+    if (nb + 1 < num_nb) {
+      load_tile<BN, D, NT>(sK + (buf ^ 1) * BN * D * 2, kb, p.k_row, (nb + 1) * BN, p.Sk);
+      load_tile<BN, D, NT>(sV + (buf ^ 1) * BN * D * 2, vb, p.v_row, (nb + 1) * BN, p.Sk);
+    }
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncthreads();
+    const uint32_t kbase = smem_u32(sK + buf * BN * D * 2);
+    const uint32_t vbase = smem_u32(sV + buf * BN * D * 2);
+
+    float s[BN / 8][4];
+#pragma unroll
+    for (int j = 0; j < BN / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < D / 16; ++kk) {
+#pragma unroll
+      for (int jp = 0; jp < BN / 16; ++jp) {
+        uint32_t b0, b1, b2, b3;
+        const int r = jp * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int c = kk * 16 + ((lane >> 3) & 1) * 8;
+        ldsm_x4(kbase + swz<D>(r, c), b0, b1, b2, b3);
+        mma_bf16(s[2 * jp], qf[kk], b0, b1);
+        mma_bf16(s[2 * jp + 1], qf[kk], b2, b3);
+      }
+    }
+    // Scale, mask, online softmax.
+    const int n0 = nb * BN;
+    const bool need_mask = (n0 + BN > p.Sk) ||
+                           (p.causal && (p.k_offset + n0 + BN - 1 > p.q_offset + m0 + warp * 16));
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int j = 0; j < BN / 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float x = s[j][e] * p.scale_log2;
+        if (need_mask) {
+          const int kcol = n0 + j * 8 + 2 * t + (e & 1);
+          const int qp = qpos0 + (e >> 1) * 8;
+          if (kcol >= p.Sk || (p.causal && p.k_offset + kcol > qp)) x = -INFINITY;
+        }
+        s[j][e] = x;
+        mx[e >> 1] = fmaxf(mx[e >> 1], x);
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+    }
+    float corr[2], mnew[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mnew[r] = fmaxf(m_run[r], mx[r]);
+      corr[r] = (m_run[r] == -INFINITY) ? 0.f : fast_exp2(m_run[r] - mnew[r]);
+      if (mnew[r] == -INFINITY) corr[r] = 1.f;
+      m_run[r] = mnew[r];
+    }
+    float rs[2] = {0.f, 0.f};
+    uint32_t pf[BN / 16][4];
+#pragma unroll
+    for (int j = 0; j < BN / 8; ++j) {
+      float pv[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float mm = mnew[e >> 1];
+        pv[e] = (mm == -INFINITY) ? 0.f : fast_exp2(s[j][e] - mm);
+        rs[e >> 1] += pv[e];
+      }
+      pf[j >> 1][(j & 1) * 2 + 0] = pack_bf16x2(pv[0], pv[1]);
+      pf[j >> 1][(j & 1) * 2 + 1] = pack_bf16x2(pv[2], pv[3]);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) l_run[r] = l_run[r] * corr[r] + rs[r];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o_acc[i][0] *= corr[0];
+      o_acc[i][1] *= corr[0];
+      o_acc[i][2] *= corr[1];
+      o_acc[i][3] *= corr[1];
+    }
+    // O += P V
+#pragma unroll
+    for (int kk = 0; kk < BN / 16; ++kk) {
+      uint32_t a[4] = {pf[kk][0], pf[kk][1], pf[kk][2], pf[kk][3]};
+#pragma unroll
+      for (int dp = 0; dp < D / 16; ++dp) {
+        uint32_t b0, b1, b2, b3;
+        const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int c = dp * 16 + (lane >> 4) * 8;
+        ldsm_x4_t(vbase + swz<D>(r, c), b0, b1, b2, b3);
+        mma_bf16(o_acc[2 * dp], a, b0, b1);
+        mma_bf16(o_acc[2 * dp + 1], a, b2, b3);
+      }
+    }
+    __syncthreads();
+  }
+
+  // Finalise: full row sums, normalise, store O and LSE.
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 1);
+    l_run[r] += __shfl_xor_sync(0xffffffffu, l_run[r], 2);
+  }
+  __nv_bfloat16* ob = p.o + b * p.o_batch + static_cast<int64_t>(h) * D;
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int row = m0 + warp * 16 + g + r * 8;
+    if (row >= p.Sq) continue;
+    const float inv = l_run[r] > 0.f ? 1.f / l_run[r] : 0.f;
+    __nv_bfloat16* orow = ob + static_cast<int64_t>(row) * p.o_row;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      *reinterpret_cast<uint32_t*>(orow + i * 8 + 2 * t) =
+          pack_bf16x2(o_acc[i][2 * r] * inv, o_acc[i][2 * r + 1] * inv);
+    }
+    if (t == 0) {
+      const float lse = l_run[r] > 0.f ? m_run[r] + __log2f(l_run[r]) : -INFINITY;
+      p.lse[(static_cast<int64_t>(b) * p.Hq + h) * p.Sq + row] = lse;
+    }
+  }
+}
+
+// ------------------------------------------------------------------ backward
+struct BwdParams {
+  const __nv_bfloat16* q;
+  const __nv_bfloat16* k;
+  const __nv_bfloat16* v;
+  const __nv_bfloat16* o;
+  const __nv_bfloat16* dout;
+  int64_t q_row, k_row, v_row, q_batch, k_batch, v_batch;
+  int64_t o_row, o_batch, do_row, do_batch;
+  const float* lse;    // [B, Hq, Sq]
+  float* delta;        // [B, Hq, Sq]
+  float* dq_acc;       // [B, Sq, Hq, D] fp32
+  __nv_bfloat16* dq;   // output pointers (strided like q/k/v)
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  int64_t dq_row, dk_row, dv_row, dq_batch, dk_batch, dv_batch;
+  int B, Hq, Hkv, Sq, Sk;
+  int q_offset, k_offset;
+  int causal;
+  float scale_log2;
+  float scale;
+  // optional inverse RoPE applied to dq / dk on the way out
+  const int* q_pos;   // [Sq] or null
+  const int* k_pos;   // [Sk] or null
+  const float* inv_freq;
+};
+
+// delta = rowsum(dO * O); also zero the fp32 dQ accumulator.
+template <int D>
+__global__ void flash_bwd_pre_kernel(const BwdParams p) {
+  const int row = blockIdx.x * 8 + threadIdx.x / 32;  // one warp per (b, s, h)
+  const int lane = threadIdx.x & 31;
+  const int total = p.B * p.Sq * p.Hq;
+  if (row >= total) return;
+  const int h = row % p.Hq;
+  const int s = (row / p.Hq) % p.Sq;
+  const int b = row / (p.Hq * p.Sq);
+  const __nv_bfloat16* orow = p.o + b * p.o_batch + static_cast<int64_t>(s) * p.o_row + h * D;
+  const __nv_bfloat16* drow = p.dout + b * p.do_batch + static_cast<int64_t>(s) * p.do_row + h * D;
+  float acc = 0.f;
+  for (int d = lane * 2; d < D; d += 64) {
+    const uint32_t ov = *reinterpret_cast<const uint32_t*>(orow + d);
+    const uint32_t dv = *reinterpret_cast<const uint32_t*>(drow + d);
+    acc += bf16_lo(ov) * bf16_lo(dv) + bf16_hi(ov) * bf16_hi(dv);
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) p.delta[(static_cast<int64_t>(b) * p.Hq + h) * p.Sq + s] = acc;
+  float* dqa = p.dq_acc + ((static_cast<int64_t>(b) * p.Sq + s) * p.Hq + h) * D;
+  for (int d = lane; d < D; d += 32) dqa[d] = 0.f;
+}
+
+__device__ __forceinline__ void red_add_v2(float* addr, float a, float b) {
+  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(addr), "f"(a), "f"(b) : "memory");
+}
+
+// Rotate-half inverse rotation of a pair (x1 at col c, x2 at col c + D/2).
+__device__ __forceinline__ void inv_rope_pair(float& x1, float& x2, float ang) {
+  float sn, cs;
+  sincosf(ang, &sn, &cs);
+  const float a = x1 * cs + x2 * sn;
+  const float b = x2 * cs - x1 * sn;
+  x1 = a;
+  x2 = b;
+}
+
+template <int D>
+__global__ void __launch_bounds__(128) flash_bwd_kernel(const BwdParams p) {
+  constexpr int BM = 64, BN = 64, NT = 128;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + BN * D * 2;
+  uint8_t* sQ = sV + BN * D * 2;
+  uint8_t* sdO = sQ + BM * D * 2;
+  uint8_t* sdS = sdO + BM * D * 2;  // [BN kv rows x BM q cols] bf16, swizzled with D=BM
+  float* sLse = reinterpret_cast<float*>(sdS + BN * BM * 2);
+  float* sDelta = sLse + BM;
+
+  const int nb = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int group = p.Hq / p.Hkv;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int n0 = nb * BN;
+
+  const __nv_bfloat16* kb = p.k + b * p.k_batch + static_cast<int64_t>(kvh) * D;
+  const __nv_bfloat16* vb = p.v + b * p.v_batch + static_cast<int64_t>(kvh) * D;
+  load_tile<BN, D, NT>(sK, kb, p.k_row, n0, p.Sk);
+  load_tile<BN, D, NT>(sV, vb, p.v_row, n0, p.Sk);
+  cp_async_commit();
+
+  float dk_acc[D / 8][4], dv_acc[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) dk_acc[i][e] = dv_acc[i][e] = 0.f;
+
+  // First query block that can see this key block.
+  int m_begin = 0;
+  if (p.causal) {
+    const int first_q = p.k_offset + n0 - p.q_offset;
+    m_begin = max(0, first_q) / BM;
+  }
+  const int num_mb = (p.Sq + BM - 1) / BM;
+  const int kv_row = n0 + warp * 16;  // this warp's first key row
+
+  for (int hh = 0; hh < group; ++hh) {
+    const int h = kvh * group + hh;
+    const __nv_bfloat16* qb = p.q + b * p.q_batch + static_cast<int64_t>(h) * D;
+    const __nv_bfloat16* dob = p.dout + b * p.do_batch + static_cast<int64_t>(h) * D;
+    const float* lse_b = p.lse + (static_cast<int64_t>(b) * p.Hq + h) * p.Sq;
+    const float* delta_b = p.delta + (static_cast<int64_t>(b) * p.Hq + h) * p.Sq;
+    for (int mb = m_begin; mb < num_mb; ++mb) {
+      const int m0 = mb * BM;
+      __syncthreads();
+      load_tile<BM, D, NT>(sQ, qb, p.q_row, m0, p.Sq);
+      load_tile<BM, D, NT>(sdO, dob, p.do_row, m0, p.Sq);
+      cp_async_commit();
+      for (int i = threadIdx.x; i < BM; i += NT) {
+        const int r = m0 + i;
+        sLse[i] = r < p.Sq ? lse_b[r] : INFINITY;
+        sDelta[i] = r < p.Sq ? delta_b[r] : 0.f;
+      }
+      cp_async_wait<0>();
+      __syncthreads();
+      const uint32_t kbase = smem_u32(sK), vbase = smem_u32(sV);
+      const uint32_t qbase = smem_u32(sQ), dobase = smem_u32(sdO);
+
+      // S^T = K Q^T (warp: 16 key rows x 64 query cols)
+      float st[BM / 8][4];
+      float dpt[BM / 8][4];
+#pragma unroll
+      for (int j = 0; j < BM / 8; ++j)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) st[j][e] = dpt[j][e] = 0.f;
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        uint32_t a[4], av[4];
+        {
+          const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int c = kk * 16 + (lane >> 4) * 8;
+          ldsm_x4(kbase + swz<D>(r, c), a[0], a[1], a[2], a[3]);
+          ldsm_x4(vbase + swz<D>(r, c), av[0], av[1], av[2], av[3]);
+        }
+#pragma unroll
+        for (int jp = 0; jp < BM / 16; ++jp) {
+          uint32_t b0, b1, b2, b3;
+          const int r = jp * 16 + (lane & 7) + (lane >> 4) * 8;
+          const int c = kk * 16 + ((lane >> 3) & 1) * 8;
+          ldsm_x4(qbase + swz<D>(r, c), b0, b1, b2, b3);
+          mma_bf16(st[2 * jp], a, b0, b1);
+          mma_bf16(st[2 * jp + 1], a, b2, b3);
+          ldsm_x4(dobase + swz<D>(r, c), b0, b1, b2, b3);
+          mma_bf16(dpt[2 * jp], av, b0, b1);
+          mma_bf16(dpt[2 * jp + 1], av, b2, b3);
+        }
+      }
+      // P^T and dS^T
+      uint32_t pa[BM / 16][4], dsa[BM / 16][4];
+#pragma unroll
+      for (int j = 0; j < BM / 8; ++j) {
+        float pv[4], dsv[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int krow = kv_row + g + (e >> 1) * 8;
+          const int qcol = j * 8 + 2 * t + (e & 1);
+          const int qg = m0 + qcol;
+          float pr = fast_exp2(st[j][e] * p.scale_log2 - sLse[qcol]);
+          if (qg >= p.Sq || krow >= p.Sk || (p.causal && p.k_offset + krow > p.q_offset + qg))
+            pr = 0.f;
+          pv[e] = pr;
+          dsv[e] = pr * (dpt[j][e] - sDelta[qcol]);
+        }
+        pa[j >> 1][(j & 1) * 2 + 0] = pack_bf16x2(pv[0], pv[1]);
+        pa[j >> 1][(j & 1) * 2 + 1] = pack_bf16x2(pv[2], pv[3]);
+        dsa[j >> 1][(j & 1) * 2 + 0] = pack_bf16x2(dsv[0], dsv[1]);
+        dsa[j >> 1][(j & 1) * 2 + 1] = pack_bf16x2(dsv[2], dsv[3]);
+        // stash dS^T (bf16) for the dQ product
+        const int r0 = warp * 16 + g;
+        const int c0 = j * 8 + 2 * t;
+        *reinterpret_cast<uint32_t*>(sdS + swz<BM>(r0, c0)) = dsa[j >> 1][(j & 1) * 2 + 0];
+        *reinterpret_cast<uint32_t*>(sdS + swz<BM>(r0 + 8, c0)) = dsa[j >> 1][(j & 1) * 2 + 1];
+      }
+      // dV += P^T dO ; dK += dS^T Q
+#pragma unroll
+      for (int kk = 0; kk < BM / 16; ++kk) {
+#pragma unroll
+        for (int dp = 0; dp < D / 16; ++dp) {
+          uint32_t b0, b1, b2, b3;
+          const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+          const int c = dp * 16 + (lane >> 4) * 8;
+          ldsm_x4_t(dobase + swz<D>(r, c), b0, b1, b2, b3);
+          mma_bf16(dv_acc[2 * dp], pa[kk], b0, b1);
+          mma_bf16(dv_acc[2 * dp + 1], pa[kk], b2, b3);
+          ldsm_x4_t(qbase + swz<D>(r, c), b0, b1, b2, b3);
+          mma_bf16(dk_acc[2 * dp], dsa[kk], b0, b1);
+          mma_bf16(dk_acc[2 * dp + 1], dsa[kk], b2, b3);
+        }
+      }
+      __syncthreads();
+      // dQ[q rows of this warp] += dS K, in two halves of D to bound registers.
+      const uint32_t dsbase = smem_u32(sdS);
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        float dq[D / 16][4];
+#pragma unroll
+        for (int i = 0; i < D / 16; ++i) dq[i][0] = dq[i][1] = dq[i][2] = dq[i][3] = 0.f;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          uint32_t a[4];
+          {
+            const int r = kk * 16 + (lane & 7) + (lane >> 4) * 8;       // kv row
+            const int c = warp * 16 + ((lane >> 3) & 1) * 8;            // q col
+            ldsm_x4_t(dsbase + swz<BM>(r, c), a[0], a[1], a[2], a[3]);
+          }
+#pragma unroll
+          for (int dp = 0; dp < D / 32; ++dp) {
+            uint32_t b0, b1, b2, b3;
+            const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+            const int c = half * (D / 2) + dp * 16 + (lane >> 4) * 8;
+            ldsm_x4_t(kbase + swz<D>(r, c), b0, b1, b2, b3);
+            mma_bf16(dq[2 * dp], a, b0, b1);
+            mma_bf16(dq[2 * dp + 1], a, b2, b3);
+          }
+        }
+#pragma unroll
+        for (int r = 0; r < 2; ++r) {
+          const int qrow = m0 + warp * 16 + g + r * 8;
+          if (qrow >= p.Sq) continue;
+          float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Sq + qrow) * p.Hq + h) * D +
+                       half * (D / 2);
+#pragma unroll
+          for (int i = 0; i < D / 16; ++i)
+            red_add_v2(dst + i * 8 + 2 * t, dq[i][2 * r] * p.scale, dq[i][2 * r + 1] * p.scale);
+        }
+      }
+    }
+  }
+
+  // Store dK (with optional inverse RoPE) and dV for this warp's 16 key rows.
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    const int krow = kv_row + g + r * 8;
+    if (krow >= p.Sk) continue;
+    if (p.k_pos != nullptr) {
+      const float pos = static_cast<float>(__ldg(p.k_pos + krow));
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int c = i * 8 + 2 * t + e;  // c < D/2
+          float x1 = dk_acc[i][2 * r + e], x2 = dk_acc[i + D / 16][2 * r + e];
+          inv_rope_pair(x1, x2, pos * __ldg(p.inv_freq + c));
+          dk_acc[i][2 * r + e] = x1;
+          dk_acc[i + D / 16][2 * r + e] = x2;
+        }
+      }
+    }
+    __nv_bfloat16* dkr = p.dk + b * p.dk_batch + static_cast<int64_t>(krow) * p.dk_row +
+                         static_cast<int64_t>(kvh) * D;
+    __nv_bfloat16* dvr = p.dv + b * p.dv_batch + static_cast<int64_t>(krow) * p.dv_row +
+                         static_cast<int64_t>(kvh) * D;
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      *reinterpret_cast<uint32_t*>(dkr + i * 8 + 2 * t) =
+          pack_bf16x2(dk_acc[i][2 * r] * p.scale, dk_acc[i][2 * r + 1] * p.scale);
+      *reinterpret_cast<uint32_t*>(dvr + i * 8 + 2 * t) =
+          pack_bf16x2(dv_acc[i][2 * r], dv_acc[i][2 * r + 1]);
+    }
+  }
+}
+
+// dq_acc (fp32) -> dq (bf16) with optional inverse RoPE. One thread per pair.
+template <int D>
+__global__ void flash_bwd_dq_kernel(const BwdParams p) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t total = static_cast<int64_t>(p.B) * p.Sq * p.Hq * (D / 2);
+  if (idx >= total) return;
+  const int c = idx % (D / 2);
+  const int h = (idx / (D / 2)) % p.Hq;
+  const int s = (idx / ((D / 2) * p.Hq)) % p.Sq;
+  const int b = idx / (static_cast<int64_t>(D / 2) * p.Hq * p.Sq);
+  const float* src = p.dq_acc + ((static_cast<int64_t>(b) * p.Sq + s) * p.Hq + h) * D;
+  float x1 = src[c], x2 = src[c + D / 2];
+  if (p.q_pos != nullptr)
+    inv_rope_pair(x1, x2, static_cast<float>(__ldg(p.q_pos + s)) * __ldg(p.inv_freq + c));
+  __nv_bfloat16* dst = p.dq + b * p.dq_batch + static_cast<int64_t>(s) * p.dq_row + h * D;
+  dst[c] = __float2bfloat16_rn(x1);
+  dst[c + D / 2] = __float2bfloat16_rn(x2);
+}
+
+}  // namespace attn
+}  // namespace nmb
+
+using namespace nmb;
+using namespace nmb::attn;
+
+static void check_rows(const at::Tensor& t, const char* name, int64_t D) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16, name, " must be CUDA bf16");
+  TORCH_CHECK(t.dim() == 4, name, " must be [B, S, H, D]");
+  TORCH_CHECK(t.size(3) == D && t.stride(3) == 1 && t.stride(2) == D, name,
+              " must have contiguous heads");
+  TORCH_CHECK(t.stride(1) % 8 == 0 && t.stride(0) % 8 == 0, name, " strides must be 16-byte");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name, " must be 16-byte aligned");
+}
+
+// q: [B, Sq, Hq, D], k/v: [B, Sk, Hkv, D] (strided views), o: [B, Sq, Hq, D], lse: [B, Hq, Sq] f32
+void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
+                    double softmax_scale, bool causal, int64_t q_offset, int64_t k_offset) {
+  const int64_t D = q.size(3);
+  TORCH_CHECK(D == 64 || D == 128, "flash_attn_fwd: head_dim must be 64 or 128");
+  check_rows(q, "q", D);
+  check_rows(k, "k", D);
+  check_rows(v, "v", D);
+  check_rows(o, "o", D);
+  FwdParams p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  p.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  p.o = reinterpret_cast<__nv_bfloat16*>(o.data_ptr());
+  p.q_row = q.stride(1);
+  p.q_batch = q.stride(0);
+  p.k_row = k.stride(1);
+  p.k_batch = k.stride(0);
+  p.v_row = v.stride(1);
+  p.v_batch = v.stride(0);
+  p.o_row = o.stride(1);
+  p.o_batch = o.stride(0);
+  p.lse = lse.data_ptr<float>();
+  p.B = q.size(0);
+  p.Sq = q.size(1);
+  p.Hq = q.size(2);
+  p.Sk = k.size(1);
+  p.Hkv = k.size(2);
+  TORCH_CHECK(p.Hq % p.Hkv == 0, "query heads must be a multiple of kv heads");
+  p.q_offset = q_offset;
+  p.k_offset = k_offset;
+  p.causal = causal ? 1 : 0;
+  p.scale_log2 = static_cast<float>(softmax_scale) * kLog2e;
+  if (p.B == 0 || p.Sq == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  dim3 grid((p.Sq + 127) / 128, p.Hq, p.B);
+  if (D == 64) {
+    const int smem = (128 + 4 * 64) * 64 * 2;
+    auto kern = flash_fwd_kernel<64>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<grid, 256, smem, stream>>>(p);
+  } else {
+    const int smem = (128 + 4 * 64) * 128 * 2;
+    auto kern = flash_fwd_kernel<128>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<grid, 256, smem, stream>>>(p);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Backward. dq/dk/dv are [B, S, H, D] strided views (typically slices of one
+// fused dQKV buffer). `q_pos`/`k_pos` (int32 positions) + `inv_freq` enable the
+// fused inverse RoPE on dq/dk.
+void flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor dout,
+                    at::Tensor lse, at::Tensor dq, at::Tensor dk, at::Tensor dv,
+                    at::Tensor delta_ws, at::Tensor dq_acc_ws, double softmax_scale, bool causal,
+                    int64_t q_offset, int64_t k_offset, c10::optional<at::Tensor> q_pos,
+                    c10::optional<at::Tensor> k_pos, c10::optional<at::Tensor> inv_freq) {
+  const int64_t D = q.size(3);
+  TORCH_CHECK(D == 64 || D == 128, "flash_attn_bwd: head_dim must be 64 or 128");
+  check_rows(q, "q", D);
+  check_rows(k, "k", D);
+  check_rows(v, "v", D);
+  check_rows(o, "o", D);
+  check_rows(dout, "dout", D);
+  check_rows(dq, "dq", D);
+  check_rows(dk, "dk", D);
+  check_rows(dv, "dv", D);
+  BwdParams p{};
+  p.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  p.k = reinterpret_cast<const __nv_bfloat16*>(k.data_ptr());
+  p.v = reinterpret_cast<const __nv_bfloat16*>(v.data_ptr());
+  p.o = reinterpret_cast<const __nv_bfloat16*>(o.data_ptr());
+  p.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  p.q_row = q.stride(1);
+  p.q_batch = q.stride(0);
+  p.k_row = k.stride(1);
+  p.k_batch = k.stride(0);
+  p.v_row = v.stride(1);
+  p.v_batch = v.stride(0);
+  p.o_row = o.stride(1);
+  p.o_batch = o.stride(0);
+  p.do_row = dout.stride(1);
+  p.do_batch = dout.stride(0);
+  p.lse = lse.data_ptr<float>();
+  p.B = q.size(0);
+  p.Sq = q.size(1);
+  p.Hq = q.size(2);
+  p.Sk = k.size(1);
+  p.Hkv = k.size(2);
+  TORCH_CHECK(delta_ws.numel() >= static_cast<int64_t>(p.B) * p.Hq * p.Sq, "delta workspace too small");
+  TORCH_CHECK(dq_acc_ws.numel() >= static_cast<int64_t>(p.B) * p.Hq * p.Sq * D,
+              "dq accumulator workspace too small");
+  p.delta = delta_ws.data_ptr<float>();
+  p.dq_acc = dq_acc_ws.data_ptr<float>();
+  p.dq = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  p.dq_row = dq.stride(1);
+  p.dq_batch = dq.stride(0);
+  p.dk_row = dk.stride(1);
+  p.dk_batch = dk.stride(0);
+  p.dv_row = dv.stride(1);
+  p.dv_batch = dv.stride(0);
+  p.q_offset = q_offset;
+  p.k_offset = k_offset;
+  p.causal = causal ? 1 : 0;
+  p.scale = static_cast<float>(softmax_scale);
+  p.scale_log2 = static_cast<float>(softmax_scale) * kLog2e;
+  p.q_pos = q_pos.has_value() ? q_pos->data_ptr<int>() : nullptr;
+  p.k_pos = k_pos.has_value() ? k_pos->data_ptr<int>() : nullptr;
+  p.inv_freq = inv_freq.has_value() ? inv_freq->data_ptr<float>() : nullptr;
+  TORCH_CHECK((p.q_pos == nullptr && p.k_pos == nullptr) || p.inv_freq != nullptr,
+              "inverse RoPE needs inv_freq");
+  if (p.B == 0 || p.Sq == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int rows = p.B * p.Sq * p.Hq;
+  dim3 grid((p.Sk + 63) / 64, p.Hkv, p.B);
+  const int64_t pairs = static_cast<int64_t>(rows) * (D / 2);
+  if (D == 64) {
+    flash_bwd_pre_kernel<64><<<(rows + 7) / 8, 256, 0, stream>>>(p);
+    const int smem = (4 * 64 * 64 + 64 * 64) * 2 + 2 * 64 * 4;
+    auto kern = flash_bwd_kernel<64>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<grid, 128, smem, stream>>>(p);
+    flash_bwd_dq_kernel<64><<<(pairs + 255) / 256, 256, 0, stream>>>(p);
+  } else {
+    flash_bwd_pre_kernel<128><<<(rows + 7) / 8, 256, 0, stream>>>(p);
+    const int smem = (4 * 64 * 128 + 64 * 64) * 2 + 2 * 64 * 4;
+    auto kern = flash_bwd_kernel<128>;
+    C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<grid, 128, smem, stream>>>(p);
+    flash_bwd_dq_kernel<128><<<(pairs + 255) / 256, 256, 0, stream>>>(p);
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

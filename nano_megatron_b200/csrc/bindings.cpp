@@ -1,0 +1,55 @@
+// Python bindings of the sm_100a kernel library (module nano_megatron_b200._C).
+#include <torch/extension.h>
+
+void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int64_t epi,
+             c10::optional<at::Tensor> residual, c10::optional<at::Tensor> alpha_t, double alpha,
+             double beta, c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
+             c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
+             int64_t head_dim, int64_t rope_cols, at::Tensor status, int64_t bn_override,
+             int64_t max_ctas);
+void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
+                    double softmax_scale, bool causal, int64_t q_offset, int64_t k_offset);
+void flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor dout,
+                    at::Tensor lse, at::Tensor dq, at::Tensor dk, at::Tensor dv,
+                    at::Tensor delta_ws, at::Tensor dq_acc_ws, double softmax_scale, bool causal,
+                    int64_t q_offset, int64_t k_offset, c10::optional<at::Tensor> q_pos,
+                    c10::optional<at::Tensor> k_pos, c10::optional<at::Tensor> inv_freq);
+void rmsnorm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps);
+void rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, at::Tensor rstd, at::Tensor dx,
+                 c10::optional<at::Tensor> dw);
+void swiglu_fwd(at::Tensor gu, at::Tensor h);
+void swiglu_bwd(at::Tensor gu, at::Tensor dh, at::Tensor dgu);
+void rope_inplace(at::Tensor x, int64_t ncols, int64_t head_dim, at::Tensor pos,
+                  at::Tensor inv_freq, bool inverse);
+void embedding_fwd(at::Tensor ids, at::Tensor w, int64_t vstart, at::Tensor out);
+void embedding_bwd(at::Tensor ids, at::Tensor dy, at::Tensor grad, int64_t vstart);
+void ce_stats(at::Tensor logits, at::Tensor labels, int64_t vstart, at::Tensor stats);
+void ce_finish(at::Tensor logits, at::Tensor labels, int64_t vstart, at::Tensor stats,
+               int64_t shards, at::Tensor loss_row, bool write_grad);
+void ce_fused(at::Tensor logits, at::Tensor labels, at::Tensor loss_row, bool write_grad);
+void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v,
+                c10::optional<at::Tensor> p_bf16, double lr, double beta1, double beta2,
+                double eps, double wd, int64_t step, c10::optional<at::Tensor> grad_scale,
+                c10::optional<at::Tensor> lr_t);
+at::Tensor sumsq_partials(at::Tensor x);
+void scale_inplace(at::Tensor x, double s);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "nano_megatron_b200 sm_100a kernels (tcgen05 GEMM, flash attention, fused ops)";
+  m.def("gemm_tc", &gemm_tc, "tcgen05 GEMM with fused epilogues");
+  m.def("flash_attn_fwd", &flash_attn_fwd);
+  m.def("flash_attn_bwd", &flash_attn_bwd);
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("rope_inplace", &rope_inplace);
+  m.def("embedding_fwd", &embedding_fwd);
+  m.def("embedding_bwd", &embedding_bwd);
+  m.def("ce_stats", &ce_stats);
+  m.def("ce_finish", &ce_finish);
+  m.def("ce_fused", &ce_fused);
+  m.def("adamw_step", &adamw_step);
+  m.def("sumsq_partials", &sumsq_partials);
+  m.def("scale_inplace", &scale_inplace);
+}

@@ -1,0 +1,568 @@
+// Persistent, warp-specialised bf16 GEMM for sm_100a on the 5th-generation
+// tensor cores (tcgen05 + TMEM), operands staged by TMA.
+//
+//   C[m, n] = epilogue( sum_k A(m, k) * B(n, k) )
+//
+// A(m, k) is read from a [M, K] row-major tensor (K-major) or from a [K, M]
+// tensor (MN-major); likewise B from [N, K] or [K, N]. All three products a
+// transformer linear layer needs map onto this one kernel without transposes:
+//   forward  y  = x W^T    A = x  (K-major), B = W  (K-major)
+//   dgrad    dx = dy W     A = dy (K-major), B = W  (MN-major)
+//   wgrad    dW = dy^T x   A = dy (MN-major), B = x (MN-major)
+//
+// Roles (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0   : TMA producer, one elected lane, ring of `kStages` smem stages
+//   warp 1   : TMEM allocator + MMA issuer (one elected lane issues tcgen05.mma)
+//   warps 2-5: epilogue; each thread owns one accumulator row (TMEM lane) and
+//              drains it with tcgen05.ld, applies the fused epilogue, stores.
+// The accumulator is double buffered in TMEM (2 x BN fp32 columns) so the
+// epilogue of tile i overlaps the main loop of tile i+1.
+//
+// Fused epilogues:
+//   kEpiBF16   : C(bf16) = alpha * acc (+ residual)
+//   kEpiF32Acc : C(fp32) = beta * C + alpha * acc   (weight-gradient accumulation)
+//   kEpiSwiGLU : B = [W_gate; W_up]; each BN tile carries BN/2 gate and BN/2 up
+//                columns; writes h = silu(g) * u and keeps [g | u] for backward
+//   kEpiRoPE   : rotate-half rotary embedding applied to the first `rope_cols`
+//                columns (q and k heads) of a fused QKV projection
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace nmb {
+
+enum EpiKind : int { kEpiBF16 = 0, kEpiF32Acc = 1, kEpiSwiGLU = 2, kEpiRoPE = 3 };
+
+struct GemmParams {
+  int M, N, K;               // N = output columns (for SwiGLU: F, the gate/up width)
+  void* C;                   // output
+  int64_t ldc;               // output row pitch, elements
+  const __nv_bfloat16* R;    // optional bf16 residual added in kEpiBF16
+  int64_t ldr;
+  const float* alpha_ptr;    // optional device scalar multiplying the accumulator
+  float alpha;
+  float beta;                // kEpiF32Acc: 0 overwrites, 1 accumulates
+  __nv_bfloat16* aux;        // kEpiSwiGLU: [M, 2F] store of gate | up
+  int64_t ld_aux;
+  int swiglu_up_row;         // kEpiSwiGLU: row of W_up inside B (= F)
+  const int* positions;      // kEpiRoPE: position of each sequence slot [seq_len]
+  int seq_len;
+  const float* inv_freq;     // kEpiRoPE: [head_dim / 2]
+  int head_dim;
+  int rope_cols;
+  int* status;
+  int num_m_tiles, num_n_tiles;
+};
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;                // one 128-byte swizzle row of bf16
+constexpr int kThreads = 192;
+constexpr int kUmmaK = 16;
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int kStages = BN == 256 ? 4 : 6;
+  static constexpr int kABytes = kBM * kBK * 2;
+  static constexpr int kBBytes = BN * kBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+// Store 32 fp32 values as bf16 to row pointer `dst` (cols [col, col+32)), predicated on N.
+__device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, int col, int ncols,
+                                                 const float (&v)[32]) {
+  if (col + 32 <= ncols && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+    uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      w.x = pack_bf16x2(v[q * 8 + 0], v[q * 8 + 1]);
+      w.y = pack_bf16x2(v[q * 8 + 2], v[q * 8 + 3]);
+      w.z = pack_bf16x2(v[q * 8 + 4], v[q * 8 + 5]);
+      w.w = pack_bf16x2(v[q * 8 + 6], v[q * 8 + 7]);
+      d4[q] = w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col + j < ncols) dst[j] = __float2bfloat16_rn(v[j]);
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
+                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int S = Cfg::kStages;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* smem_a = smem;
+  uint8_t* smem_b = smem + S * Cfg::kABytes;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S * Cfg::kStageBytes);
+  uint64_t* empty_bar = full_bar + S;
+  uint64_t* tfull_bar = empty_bar + S;   // [2]
+  uint64_t* tempty_bar = tfull_bar + 2;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+  const int num_kb = (p.K + kBK - 1) / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull_bar[a], 1);
+      mbar_init(&tempty_bar[a], 4);  // one arrive per epilogue warp
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int m0 = (t % p.num_m_tiles) * kBM;
+        const int nt = t / p.num_m_tiles;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.status, kStatusGemmProducerTimeout,
+                         abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], Cfg::kStageBytes);
+          uint8_t* sa = smem_a + stage * Cfg::kABytes;
+          uint8_t* sb = smem_b + stage * Cfg::kBBytes;
+          const int k0 = kb * kBK;
+          if constexpr (!A_MN) {
+            tma_load_2d(sa, &tmA, &full_bar[stage], k0, m0);
+          } else {
+            tma_load_2d(sa, &tmA, &full_bar[stage], m0, k0);
+            tma_load_2d(sa + kBK * 128, &tmA, &full_bar[stage], m0 + 64, k0);
+          }
+          if constexpr (EPI == kEpiSwiGLU) {
+            const int n0h = nt * (BN / 2);
+            tma_load_2d(sb, &tmB, &full_bar[stage], k0, n0h);
+            tma_load_2d(sb + (BN / 2) * 128, &tmB, &full_bar[stage], k0, p.swiglu_up_row + n0h);
+          } else if constexpr (!B_MN) {
+            tma_load_2d(sb, &tmB, &full_bar[stage], k0, nt * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + j * kBK * 128, &tmB, &full_bar[stage], nt * BN + j * 64, k0);
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one()) {
+      constexpr uint32_t idesc = umma_idesc_bf16(kBM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty_bar[acc], acc_phase ^ 1u, p.status, kStatusGemmMmaTimeout,
+                       abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, p.status, kStatusGemmMmaTimeout, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem_a + stage * Cfg::kABytes);
+          const uint32_t b_addr = smem_u32(smem_b + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < kBK / kUmmaK; ++kk) {
+            uint64_t adesc, bdesc;
+            if constexpr (!A_MN)
+              adesc = umma_desc_sw128(a_addr + kk * 32, 16, 1024);
+            else
+              adesc = umma_desc_sw128(a_addr + kk * 2048, kBK * 128, 1024);
+            if constexpr (!B_MN)
+              bdesc = umma_desc_sw128(b_addr + kk * 32, 16, 1024);
+            else
+              bdesc = umma_desc_sw128(b_addr + kk * 2048, kBK * 128, 1024);
+            umma_f16_ss(tmem_d, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty_bar[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull_bar[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const int lane = threadIdx.x & 31;
+    const float alpha = p.alpha_ptr != nullptr ? p.alpha * __ldg(p.alpha_ptr) : p.alpha;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull_bar[acc], acc_phase, p.status, kStatusGemmEpilogueTimeout,
+                     abort_flag))
+        break;
+      tc_fence_after();
+      const int m0 = (t % p.num_m_tiles) * kBM;
+      const int nt = t / p.num_m_tiles;
+      const int row = m0 + quarter * 32 + lane;
+      const bool row_ok = row < p.M;
+      const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
+
+      if constexpr (EPI == kEpiBF16 || EPI == kEpiF32Acc) {
+        const int n0 = nt * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, r);
+          tmem_wait_ld();
+          const int col = n0 + c * 32;
+          if (!row_ok || col >= p.N) continue;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
+          if constexpr (EPI == kEpiBF16) {
+            if (p.R != nullptr) {
+              const __nv_bfloat16* rr = p.R + static_cast<int64_t>(row) * p.ldr + col;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col + j < p.N) v[j] += __bfloat162float(rr[j]);
+            }
+            store_row32_bf16(reinterpret_cast<__nv_bfloat16*>(p.C) +
+                                 static_cast<int64_t>(row) * p.ldc + col,
+                             col, p.N, v);
+          } else {
+            float* cp = reinterpret_cast<float*>(p.C) + static_cast<int64_t>(row) * p.ldc + col;
+            if (col + 32 <= p.N) {
+              float4* c4 = reinterpret_cast<float4*>(cp);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                float4 o = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+                if (p.beta != 0.0f) {
+                  const float4 old = c4[q];
+                  o.x += p.beta * old.x;
+                  o.y += p.beta * old.y;
+                  o.z += p.beta * old.z;
+                  o.w += p.beta * old.w;
+                }
+                c4[q] = o;
+              }
+            } else {
+              for (int j = 0; j < 32; ++j)
+                if (col + j < p.N) cp[j] = v[j] + (p.beta != 0.0f ? p.beta * cp[j] : 0.0f);
+            }
+          }
+        }
+      } else if constexpr (EPI == kEpiSwiGLU) {
+        const int n0h = nt * (BN / 2);
+#pragma unroll 1
+        for (int c = 0; c < BN / 64; ++c) {
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, g);
+          tmem_ld_32x32b_x32(tbase + BN / 2 + c * 32, u);
+          tmem_wait_ld();
+          const int col = n0h + c * 32;
+          if (!row_ok || col >= p.N) continue;
+          float gv[32], uv[32], hv[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            gv[j] = __uint_as_float(g[j]);
+            uv[j] = __uint_as_float(u[j]);
+            // Round through bf16 so forward and backward see the same g, u.
+            gv[j] = __bfloat162float(__float2bfloat16_rn(gv[j]));
+            uv[j] = __bfloat162float(__float2bfloat16_rn(uv[j]));
+            hv[j] = silu_f(gv[j]) * uv[j];
+          }
+          store_row32_bf16(reinterpret_cast<__nv_bfloat16*>(p.C) +
+                               static_cast<int64_t>(row) * p.ldc + col,
+                           col, p.N, hv);
+          __nv_bfloat16* arow = p.aux + static_cast<int64_t>(row) * p.ld_aux;
+          store_row32_bf16(arow + col, col, p.N, gv);
+          store_row32_bf16(arow + p.N + col, col, p.N, uv);
+        }
+      } else {  // kEpiRoPE
+        const int n0 = nt * BN;
+        const int D = p.head_dim;
+        const int half_chunks = D / 64;  // 32-col chunks per half head
+        const int chunks_per_head = D / 32;
+        const int pos = row_ok ? __ldg(p.positions + (row % p.seq_len)) : 0;
+#pragma unroll 1
+        for (int h = 0; h < BN / D; ++h) {
+#pragma unroll 1
+          for (int j = 0; j < half_chunks; ++j) {
+            const int c_lo = h * chunks_per_head + j;
+            const int c_hi = c_lo + half_chunks;
+            uint32_t lo[32], hi[32];
+            tmem_ld_32x32b_x32(tbase + c_lo * 32, lo);
+            tmem_ld_32x32b_x32(tbase + c_hi * 32, hi);
+            tmem_wait_ld();
+            const int col_lo = n0 + c_lo * 32;
+            const int col_hi = n0 + c_hi * 32;
+            if (!row_ok || col_lo >= p.N) continue;
+            float a[32], b[32];
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              a[e] = __uint_as_float(lo[e]) * alpha;
+              b[e] = __uint_as_float(hi[e]) * alpha;
+            }
+            if (col_lo < p.rope_cols) {
+#pragma unroll 4
+              for (int e = 0; e < 32; ++e) {
+                const float ang = static_cast<float>(pos) * __ldg(p.inv_freq + j * 32 + e);
+                float sn, cs;
+                sincosf(ang, &sn, &cs);
+                const float x1 = a[e], x2 = b[e];
+                a[e] = x1 * cs - x2 * sn;
+                b[e] = x2 * cs + x1 * sn;
+              }
+            }
+            __nv_bfloat16* crow =
+                reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(row) * p.ldc;
+            store_row32_bf16(crow + col_lo, col_lo, p.N, a);
+            store_row32_bf16(crow + col_hi, col_hi, p.N, b);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult qres;
+    void* ptr = nullptr;
+    cudaError_t err = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                                       cudaEnableDefault, &qres);
+    TORCH_CHECK(err == cudaSuccess && qres == cudaDriverEntryPointSuccess && ptr != nullptr,
+                "nano_megatron_b200: cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix with row pitch `ld`
+// elements; box = [box_rows, 64 cols], 128-byte swizzle, zero fill out of bounds.
+static CUtensorMap make_tmap_2d(const void* base, int64_t rows, int64_t cols, int64_t ld,
+                                int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * 2)};
+  cuuint32_t box[2] = {64u, static_cast<cuuint32_t>(box_rows)};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base),
+                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", static_cast<int>(r),
+              ") rows=", rows, " cols=", cols, " ld=", ld);
+  return m;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
+                   cudaStream_t stream, int max_ctas) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, EPI>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    C10_CUDA_CHECK(
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+    attr_set = true;
+  }
+  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static void check_operand(const at::Tensor& t, const char* name) {
+  TORCH_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16, name, " must be bfloat16");
+  TORCH_CHECK(t.dim() == 2, name, " must be 2-D");
+  TORCH_CHECK(t.stride(1) == 1, name, " must have unit inner stride");
+  TORCH_CHECK((t.stride(0) * 2) % 16 == 0, name, " row pitch must be a multiple of 16 bytes");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(t.data_ptr()) % 16 == 0, name,
+              " must be 16-byte aligned");
+}
+
+// Dispatch on the run-time layout / epilogue to a compiled instantiation.
+template <bool A_MN, bool B_MN, int EPI>
+static void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
+                        cudaStream_t s, int max_ctas) {
+  if (bn == 256)
+    launch<256, A_MN, B_MN, EPI>(ta, tb, p, s, max_ctas);
+  else
+    launch<128, A_MN, B_MN, EPI>(ta, tb, p, s, max_ctas);
+}
+
+// Pick the N tile: 256 when it still leaves roughly a full wave of tiles.
+static int choose_bn(int M, int N, int epi) {
+  if (epi == kEpiSwiGLU) return 256;
+  const int mt = (M + kBM - 1) / kBM;
+  const int tiles256 = mt * ((N + 255) / 256);
+  if (N % 256 != 0 && N <= 128) return 128;
+  return tiles256 >= num_sms() * 0.9 ? 256 : 128;
+}
+
+}  // namespace nmb
+
+// Python-facing entry points ------------------------------------------------------------
+
+using namespace nmb;
+
+// C = alpha * A.B^T (+R) with layout flags; C dtype bf16 (epi 0/3) or fp32 (epi 1).
+// a_mn: `a` holds A as [K, M]; b_mn: `b` holds B as [K, N].
+void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int64_t epi,
+             c10::optional<at::Tensor> residual, c10::optional<at::Tensor> alpha_t, double alpha,
+             double beta, c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
+             c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
+             int64_t head_dim, int64_t rope_cols, at::Tensor status, int64_t bn_override,
+             int64_t max_ctas) {
+  check_operand(a, "A");
+  check_operand(b, "B");
+  const int64_t M = a_mn ? a.size(1) : a.size(0);
+  const int64_t K = a_mn ? a.size(0) : a.size(1);
+  const int64_t Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm_tc: K mismatch ", K, " vs ", Kb);
+  TORCH_CHECK(c.dim() == 2 && c.stride(1) == 1 && c.size(0) == M, "gemm_tc: bad C");
+  const int64_t N = c.size(1);
+  GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.C = c.data_ptr();
+  p.ldc = c.stride(0);
+  p.alpha = static_cast<float>(alpha);
+  p.beta = static_cast<float>(beta);
+  p.status = status.data_ptr<int>();
+  if (residual.has_value()) {
+    TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1);
+    p.R = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    p.ldr = residual->stride(0);
+  }
+  if (alpha_t.has_value()) {
+    TORCH_CHECK(alpha_t->scalar_type() == at::kFloat && alpha_t->is_cuda());
+    p.alpha_ptr = alpha_t->data_ptr<float>();
+  }
+  if (epi == kEpiF32Acc) {
+    TORCH_CHECK(c.scalar_type() == at::kFloat, "wgrad accumulation output must be fp32");
+  } else {
+    TORCH_CHECK(c.scalar_type() == at::kBFloat16, "output must be bf16");
+  }
+  int bn = bn_override > 0 ? static_cast<int>(bn_override) : choose_bn(p.M, p.N, epi);
+  if (epi == kEpiSwiGLU) {
+    TORCH_CHECK(!a_mn && !b_mn, "SwiGLU epilogue requires K-major operands");
+    TORCH_CHECK(aux.has_value(), "SwiGLU epilogue needs the gate|up store");
+    p.aux = reinterpret_cast<__nv_bfloat16*>(aux->data_ptr());
+    p.ld_aux = aux->stride(0);
+    p.swiglu_up_row = static_cast<int>(swiglu_up_row);
+    bn = 256;
+  }
+  if (epi == kEpiRoPE) {
+    TORCH_CHECK(positions.has_value() && inv_freq.has_value(), "RoPE epilogue inputs missing");
+    TORCH_CHECK(head_dim == 64 || head_dim == 128, "RoPE epilogue supports head_dim 64/128");
+    p.positions = positions->data_ptr<int>();
+    p.seq_len = static_cast<int>(positions->numel());
+    p.inv_freq = inv_freq->data_ptr<float>();
+    p.head_dim = static_cast<int>(head_dim);
+    p.rope_cols = static_cast<int>(rope_cols);
+    TORCH_CHECK(rope_cols % head_dim == 0 && N % head_dim == 0);
+  }
+  const int out_cols_per_tile = epi == kEpiSwiGLU ? bn / 2 : bn;
+  p.num_m_tiles = static_cast<int>((M + kBM - 1) / kBM);
+  p.num_n_tiles = static_cast<int>((N + out_cols_per_tile - 1) / out_cols_per_tile);
+  if (M == 0 || N == 0) return;
+
+  const at::cuda::CUDAGuard guard(a.device());
+  // Tensor maps. A: K-major -> [M, K] with box 128 rows; MN-major -> [K, M] box 64 rows.
+  CUtensorMap ta = a_mn ? make_tmap_2d(a.data_ptr(), K, M, a.stride(0), kBK)
+                        : make_tmap_2d(a.data_ptr(), M, K, a.stride(0), kBM);
+  CUtensorMap tb;
+  const int64_t b_rows_total = b_mn ? b.size(1) : b.size(0);
+  if (b_mn)
+    tb = make_tmap_2d(b.data_ptr(), K, b_rows_total, b.stride(0), kBK);
+  else
+    tb = make_tmap_2d(b.data_ptr(), b_rows_total, K, b.stride(0),
+                      epi == kEpiSwiGLU ? bn / 2 : bn);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int mc = static_cast<int>(max_ctas);
+  if (epi == kEpiSwiGLU) {
+    launch<256, false, false, kEpiSwiGLU>(ta, tb, p, stream, mc);
+  } else if (epi == kEpiRoPE) {
+    TORCH_CHECK(!a_mn && !b_mn, "RoPE epilogue requires K-major operands");
+    dispatch_bn<false, false, kEpiRoPE>(bn, ta, tb, p, stream, mc);
+  } else if (epi == kEpiBF16) {
+    if (!a_mn && !b_mn) dispatch_bn<false, false, kEpiBF16>(bn, ta, tb, p, stream, mc);
+    else if (!a_mn && b_mn) dispatch_bn<false, true, kEpiBF16>(bn, ta, tb, p, stream, mc);
+    else if (a_mn && !b_mn) dispatch_bn<true, false, kEpiBF16>(bn, ta, tb, p, stream, mc);
+    else dispatch_bn<true, true, kEpiBF16>(bn, ta, tb, p, stream, mc);
+  } else {
+    if (!a_mn && !b_mn) dispatch_bn<false, false, kEpiF32Acc>(bn, ta, tb, p, stream, mc);
+    else if (!a_mn && b_mn) dispatch_bn<false, true, kEpiF32Acc>(bn, ta, tb, p, stream, mc);
+    else if (a_mn && !b_mn) dispatch_bn<true, false, kEpiF32Acc>(bn, ta, tb, p, stream, mc);
+    else dispatch_bn<true, true, kEpiF32Acc>(bn, ta, tb, p, stream, mc);
+  }
+}

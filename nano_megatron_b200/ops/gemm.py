@@ -1,0 +1,98 @@
+"""tcgen05 GEMM entry points.
+
+The kernel computes ``C[m, n] = sum_k A(m, k) B(n, k)`` where either operand may
+be stored K-major (``[rows, K]``) or MN-major (``[K, rows]``), so the forward,
+input-gradient and weight-gradient products of a linear layer all run without
+transposes. Fused epilogues: bf16 store (optional residual add and device
+scalar scale), fp32 accumulate (weight gradients into fp32 main-grad buffers),
+SwiGLU (gate/up projection), rotary embedding (QKV projection).
+
+The reference computes these with ``nn.Linear`` / ``F.linear`` under autocast
+(src/nano_megatron/nn/kernels/torch_backend.py:19-20,
+src/nano_megatron/tensor_parallel/layers.py:214).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._ext import lib, status_word
+
+EPI_BF16, EPI_F32_ACC, EPI_SWIGLU, EPI_ROPE = 0, 1, 2, 3
+
+
+def gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    out: torch.Tensor,
+    *,
+    a_mn: bool = False,
+    b_mn: bool = False,
+    epilogue: int = EPI_BF16,
+    residual: torch.Tensor | None = None,
+    alpha: float = 1.0,
+    alpha_t: torch.Tensor | None = None,
+    beta: float = 0.0,
+    aux: torch.Tensor | None = None,
+    swiglu_up_row: int = 0,
+    positions: torch.Tensor | None = None,
+    inv_freq: torch.Tensor | None = None,
+    head_dim: int = 0,
+    rope_cols: int = 0,
+    block_n: int = 0,
+    max_ctas: int = 0,
+) -> torch.Tensor:
+    lib().gemm_tc(
+        a, a_mn, b, b_mn, out, epilogue, residual, alpha_t, float(alpha), float(beta), aux,
+        int(swiglu_up_row), positions, inv_freq, int(head_dim), int(rope_cols),
+        status_word(a.device), int(block_n), int(max_ctas),
+    )
+    return out
+
+
+def linear_fwd(x: torch.Tensor, weight: torch.Tensor, *, residual: torch.Tensor | None = None,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """``x @ weight.T`` (+ residual) for 2-D bf16 ``x`` [M, K] and ``weight`` [N, K]."""
+    if out is None:
+        out = torch.empty(x.shape[0], weight.shape[0], device=x.device, dtype=torch.bfloat16)
+    return gemm(x, weight, out, residual=residual)
+
+
+def linear_dgrad(dy: torch.Tensor, weight: torch.Tensor, *, out: torch.Tensor | None = None,
+                 alpha_t: torch.Tensor | None = None) -> torch.Tensor:
+    """``dy @ weight`` for ``dy`` [M, N] and ``weight`` [N, K] (weight read MN-major)."""
+    if out is None:
+        out = torch.empty(dy.shape[0], weight.shape[1], device=dy.device, dtype=torch.bfloat16)
+    return gemm(dy, weight, out, b_mn=True, alpha_t=alpha_t)
+
+
+def linear_wgrad(dy: torch.Tensor, x: torch.Tensor, main_grad: torch.Tensor, *,
+                 accumulate: bool = True, alpha_t: torch.Tensor | None = None) -> torch.Tensor:
+    """``main_grad (+)= dy.T @ x`` in fp32 (both operands read MN-major)."""
+    return gemm(dy, x, main_grad, a_mn=True, b_mn=True, epilogue=EPI_F32_ACC,
+                beta=1.0 if accumulate else 0.0, alpha_t=alpha_t)
+
+
+def swiglu_fwd(x: torch.Tensor, w_gate_up: torch.Tensor, ffn: int, *,
+               out: torch.Tensor | None = None, gate_up: torch.Tensor | None = None):
+    """h = silu(x Wg^T) * (x Wu^T) with ``w_gate_up = [Wg; Wu]`` ([2F, H]).
+
+    Returns ``(h [M, F], gate_up [M, 2F])``; ``gate_up`` is kept for backward.
+    """
+    m = x.shape[0]
+    if out is None:
+        out = torch.empty(m, ffn, device=x.device, dtype=torch.bfloat16)
+    if gate_up is None:
+        gate_up = torch.empty(m, 2 * ffn, device=x.device, dtype=torch.bfloat16)
+    gemm(x, w_gate_up, out, epilogue=EPI_SWIGLU, aux=gate_up, swiglu_up_row=ffn)
+    return out, gate_up
+
+
+def qkv_rope_fwd(x: torch.Tensor, w_qkv: torch.Tensor, positions: torch.Tensor,
+                 inv_freq: torch.Tensor, head_dim: int, rope_cols: int, *,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """Fused QKV projection with rotary embedding on the first ``rope_cols`` columns."""
+    if out is None:
+        out = torch.empty(x.shape[0], w_qkv.shape[0], device=x.device, dtype=torch.bfloat16)
+    return gemm(x, w_qkv, out, epilogue=EPI_ROPE, positions=positions, inv_freq=inv_freq,
+                head_dim=head_dim, rope_cols=rope_cols)
