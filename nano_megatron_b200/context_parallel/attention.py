@@ -1,0 +1,208 @@
+"""Context-parallel attention cores (all-gather and ring)."""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from nano_megatron_b200.ops import functional as F
+from nano_megatron_b200.tensor_parallel.comm import all_gather_dim0, reduce_scatter_dim0
+
+from .utils import chunk_ids, gathered_to_global_order, local_positions
+
+
+class _CPBase:
+    """Shared chunk bookkeeping; inverse RoPE is applied by the attention block."""
+
+    applies_inverse_rope = False
+
+    def __init__(self, group, *, load_balance: bool = False) -> None:
+        self.group = group
+        self.load_balance = load_balance
+
+    def local_positions(self, seq_local: int, rank: int, size: int) -> torch.Tensor:
+        return local_positions(seq_local, rank, size, self.load_balance)
+
+    def q_chunks(self, seq_local: int):
+        """(row start, rows, absolute position offset) of each local query chunk."""
+        size, rank = self.group.size, self.group.rank
+        if not self.load_balance:
+            return [(0, seq_local, rank * seq_local)]
+        c = seq_local // 2
+        a, b = chunk_ids(rank, size, True)
+        return [(0, c, a * c), (c, c, b * c)]
+
+
+def _kv_rows(q, k, v):
+    """The [S, B, 2*Hkv*D] strided row view holding k|v (adjacent in the QKV buffer)."""
+    B, S, hkv, D = k.shape
+    base = k.transpose(0, 1)  # [S, B, Hkv, D]
+    return torch.as_strided(base, (S, B, 2 * hkv * D), (base.stride(0), base.stride(1), 1))
+
+
+class AllGatherContextParallelAttention(_CPBase):
+    def _gather(self, k, v):
+        B, S, hkv, D = k.shape
+        kv = _kv_rows(None, k, v).contiguous()                     # [S, B, 2HkvD]
+        full = all_gather_dim0(kv, self.group)                     # rank-major
+        size = self.group.size
+        if self.load_balance:
+            c = S // 2
+            parts = full.view(size, 2, c, B, 2 * hkv * D)
+            order = gathered_to_global_order(size, True)
+            full = torch.cat([parts[r, h] for r, h in order], 0)
+        kvf = full.view(size * S, B, 2, hkv, D)
+        return kvf[:, :, 0].transpose(0, 1), kvf[:, :, 1].transpose(0, 1), full
+
+    def forward(self, q, k, v, o, mb):
+        kf, vf, full = self._gather(k, v)
+        o_bs = o.transpose(0, 1)
+        B, Sq, Hq, D = o_bs.shape
+        lse = torch.empty(B, Hq, Sq, device=q.device, dtype=torch.float32)
+        for start, rows, off in self.q_chunks(Sq):
+            oc, lc = F.attention_fwd(q[:, start:start + rows], kf, vf, causal=True,
+                                     q_offset=off, k_offset=0)
+            o_bs[:, start:start + rows].copy_(oc)
+            lse[:, :, start:start + rows].copy_(lc)
+        mb.extra["cp_kv_full"] = full
+        return lse
+
+    def backward(self, q, k, v, o, do, lse, dq, dk, dv, mb, inv_freq):
+        full = mb.extra.pop("cp_kv_full", None)
+        if full is None:
+            kf, vf, full = self._gather(k, v)
+        else:
+            B, S, hkv, D = k.shape
+            kvf = full.view(-1, B, 2, hkv, D)
+            kf, vf = kvf[:, :, 0].transpose(0, 1), kvf[:, :, 1].transpose(0, 1)
+        dfull = torch.zeros(full.shape, dtype=torch.float32, device=full.device)
+        B, Stot, hkv, D = kf.shape
+        dview = dfull.view(Stot, B, 2, hkv, D)
+        o_bs = o.transpose(0, 1)
+        for start, rows, off in self.q_chunks(q.shape[1]):
+            dkc = torch.empty(B, Stot, hkv, D, device=q.device, dtype=q.dtype)
+            dvc = torch.empty_like(dkc)
+            F.attention_bwd(q[:, start:start + rows], kf, vf, o_bs[:, start:start + rows],
+                            do[:, start:start + rows], lse[:, :, start:start + rows].contiguous(),
+                            dq[:, start:start + rows], dkc, dvc, causal=True, q_offset=off,
+                            k_offset=0)
+            dview[:, :, 0] += dkc.transpose(0, 1).float()
+            dview[:, :, 1] += dvc.transpose(0, 1).float()
+        size = self.group.size
+        S = k.shape[1]
+        if self.load_balance:
+            c = S // 2
+            chunks = dfull.view(2 * size, c, B, 2 * hkv * D)
+            order = gathered_to_global_order(size, True)
+            ranked = torch.empty_like(dfull).view(size, 2, c, B, 2 * hkv * D)
+            for g, (r, h) in enumerate(order):
+                ranked[r, h] = chunks[g]
+            dfull = ranked.view(size * S, B, 2 * hkv * D)
+        local = reduce_scatter_dim0(dfull.view(size * S, B, 2 * hkv * D), self.group)
+        lv = local.view(S, B, 2, hkv, D)
+        dk.copy_(lv[:, :, 0].transpose(0, 1))
+        dv.copy_(lv[:, :, 1].transpose(0, 1))
+
+
+def _merge(o_acc, lse_acc, o_new, lse_new):
+    """Combine two normalised partial attention outputs by their base-2 LSEs (in place)."""
+    m = torch.maximum(lse_acc, lse_new)
+    m_safe = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
+    w1 = torch.exp2(lse_acc - m_safe)
+    w2 = torch.exp2(lse_new - m_safe)
+    tot = w1 + w2
+    scale1 = torch.where(tot > 0, w1 / tot, torch.zeros_like(tot))
+    scale2 = torch.where(tot > 0, w2 / tot, torch.zeros_like(tot))
+    # lse [B, H, S] -> weights [B, S, H, 1]
+    o_acc.mul_(scale1.permute(0, 2, 1).unsqueeze(-1)).add_(
+        o_new.float() * scale2.permute(0, 2, 1).unsqueeze(-1))
+    lse_acc.copy_(torch.where(tot > 0, m_safe + torch.log2(tot), lse_acc))
+
+
+class RingContextParallelAttention(_CPBase):
+    """K/V rotate around the CP ring; partial outputs merged by LSE; masked blocks skipped."""
+
+    def _ring_pairs(self, rank_src: int, Sq: int, Sk: int):
+        """(q start, q rows, q offset, k start, k rows, k offset) sub-blocks vs a source rank."""
+        size = self.group.size
+        qs = self.q_chunks(Sq)
+        if not self.load_balance:
+            ks = [(0, Sk, rank_src * Sk)]
+        else:
+            c = Sk // 2
+            a, b = chunk_ids(rank_src, size, True)
+            ks = [(0, c, a * c), (c, c, b * c)]
+        out = []
+        for qstart, qrows, qoff in qs:
+            for kstart, krows, koff in ks:
+                if koff > qoff + qrows - 1:
+                    continue  # entirely above the causal diagonal
+                out.append((qstart, qrows, qoff, kstart, krows, koff))
+        return out
+
+    def _rotate(self, t: torch.Tensor) -> torch.Tensor:
+        g = self.group
+        nxt = g.ranks[(g.rank + 1) % g.size]
+        prv = g.ranks[(g.rank - 1) % g.size]
+        recv = torch.empty_like(t)
+        ops = [dist.P2POp(dist.isend, t, nxt, group=g.process_group),
+               dist.P2POp(dist.irecv, recv, prv, group=g.process_group)]
+        for w in dist.batch_isend_irecv(ops):
+            w.wait()
+        return recv
+
+    def forward(self, q, k, v, o, mb):
+        B, Sq, Hq, D = q.shape
+        hkv = k.shape[2]
+        kv = _kv_rows(q, k, v).contiguous()
+        o_acc = torch.zeros(B, Sq, Hq, D, device=q.device, dtype=torch.float32)
+        lse_acc = torch.full((B, Hq, Sq), float("-inf"), device=q.device, dtype=torch.float32)
+        g = self.group
+        cur = kv
+        for step in range(g.size):
+            src = (g.rank - step) % g.size
+            nxt = self._rotate(cur) if step + 1 < g.size else None
+            view = cur.view(-1, B, 2, hkv, D)
+            kb, vb = view[:, :, 0].transpose(0, 1), view[:, :, 1].transpose(0, 1)
+            for qs, qr, qo, ks, kr, ko in self._ring_pairs(src, Sq, kb.shape[1]):
+                on, ln = F.attention_fwd(q[:, qs:qs + qr], kb[:, ks:ks + kr], vb[:, ks:ks + kr],
+                                         causal=True, q_offset=qo, k_offset=ko)
+                _merge(o_acc[:, qs:qs + qr], lse_acc[:, :, qs:qs + qr], on, ln)
+            if nxt is not None:
+                cur = nxt
+        o.transpose(0, 1).copy_(o_acc.to(o.dtype))
+        return lse_acc
+
+    def backward(self, q, k, v, o, do, lse, dq, dk, dv, mb, inv_freq):
+        B, Sq, Hq, D = q.shape
+        hkv = k.shape[2]
+        g = self.group
+        kv = _kv_rows(q, k, v).contiguous()
+        dkv = torch.zeros(kv.shape, dtype=torch.float32, device=q.device)
+        dq_acc = torch.zeros(B, Sq, Hq, D, dtype=torch.float32, device=q.device)
+        o_bs = o.transpose(0, 1)
+        cur, cur_d = kv, dkv
+        for step in range(g.size):
+            src = (g.rank - step) % g.size
+            view = cur.view(-1, B, 2, hkv, D)
+            kb, vb = view[:, :, 0].transpose(0, 1), view[:, :, 1].transpose(0, 1)
+            dview = cur_d.view(-1, B, 2, hkv, D)
+            for qs, qr, qo, ks, kr, ko in self._ring_pairs(src, Sq, kb.shape[1]):
+                dqc = torch.empty(B, qr, Hq, D, device=q.device, dtype=q.dtype)
+                dkc = torch.empty(B, kr, hkv, D, device=q.device, dtype=q.dtype)
+                dvc = torch.empty_like(dkc)
+                F.attention_bwd(q[:, qs:qs + qr], kb[:, ks:ks + kr], vb[:, ks:ks + kr],
+                                o_bs[:, qs:qs + qr], do[:, qs:qs + qr],
+                                lse[:, :, qs:qs + qr].contiguous(), dqc, dkc, dvc, causal=True,
+                                q_offset=qo, k_offset=ko)
+                dq_acc[:, qs:qs + qr] += dqc.float()
+                dview[ks:ks + kr, :, 0] += dkc.transpose(0, 1).float()
+                dview[ks:ks + kr, :, 1] += dvc.transpose(0, 1).float()
+            # K/V and their gradient accumulators travel on together; after size
+            # rotations each accumulator is back on the rank that owns its K/V.
+            cur = self._rotate(cur) if step + 1 < g.size else cur
+            cur_d = self._rotate(cur_d)
+        dq.copy_(dq_acc.to(dq.dtype))
+        lv = cur_d.view(-1, B, 2, hkv, D)
+        dk.copy_(lv[:, :, 0].transpose(0, 1))
+        dv.copy_(lv[:, :, 1].transpose(0, 1))

@@ -629,12 +629,12 @@ void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::
     const int smem = (128 + 4 * 64) * 64 * 2;
     auto kern = flash_fwd_kernel<64>;
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kern<<<grid, 256, smem, stream>>>(p);
+    kern<<<grid, 256, smem, stream>>>(p); NMB_LAUNCHED(1);
   } else {
     const int smem = (128 + 4 * 64) * 128 * 2;
     auto kern = flash_fwd_kernel<128>;
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kern<<<grid, 256, smem, stream>>>(p);
+    kern<<<grid, 256, smem, stream>>>(p); NMB_LAUNCHED(1);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -710,19 +710,19 @@ void flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::
   dim3 grid((p.Sk + 63) / 64, p.Hkv, p.B);
   const int64_t pairs = static_cast<int64_t>(rows) * (D / 2);
   if (D == 64) {
-    flash_bwd_pre_kernel<64><<<(rows + 7) / 8, 256, 0, stream>>>(p);
+    flash_bwd_pre_kernel<64><<<(rows + 7) / 8, 256, 0, stream>>>(p); NMB_LAUNCHED(1);
     const int smem = (4 * 64 * 64 + 64 * 64) * 2 + 2 * 64 * 4;
     auto kern = flash_bwd_kernel<64>;
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kern<<<grid, 128, smem, stream>>>(p);
-    flash_bwd_dq_kernel<64><<<(pairs + 255) / 256, 256, 0, stream>>>(p);
+    kern<<<grid, 128, smem, stream>>>(p); NMB_LAUNCHED(1);
+    flash_bwd_dq_kernel<64><<<(pairs + 255) / 256, 256, 0, stream>>>(p); NMB_LAUNCHED(1);
   } else {
-    flash_bwd_pre_kernel<128><<<(rows + 7) / 8, 256, 0, stream>>>(p);
+    flash_bwd_pre_kernel<128><<<(rows + 7) / 8, 256, 0, stream>>>(p); NMB_LAUNCHED(1);
     const int smem = (4 * 64 * 128 + 64 * 64) * 2 + 2 * 64 * 4;
     auto kern = flash_bwd_kernel<128>;
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kern<<<grid, 128, smem, stream>>>(p);
-    flash_bwd_dq_kernel<128><<<(pairs + 255) / 256, 256, 0, stream>>>(p);
+    kern<<<grid, 128, smem, stream>>>(p); NMB_LAUNCHED(1);
+    flash_bwd_dq_kernel<128><<<(pairs + 255) / 256, 256, 0, stream>>>(p); NMB_LAUNCHED(1);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -1,12 +1,14 @@
 // Python bindings of the sm_100a kernel library (module nano_megatron_b200._C).
 #include <torch/extension.h>
 
+#include "launch_counter.h"
+
 void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int64_t epi,
              c10::optional<at::Tensor> residual, c10::optional<at::Tensor> alpha_t, double alpha,
              double beta, c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
              c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
-             int64_t head_dim, int64_t rope_cols, at::Tensor status, int64_t bn_override,
-             int64_t max_ctas);
+             int64_t head_dim, int64_t rope_cols, int64_t pos_div, at::Tensor status,
+             int64_t bn_override, int64_t max_ctas);
 void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
                     double softmax_scale, bool causal, int64_t q_offset, int64_t k_offset);
 void flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor dout,
@@ -16,7 +18,7 @@ void flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::
                     c10::optional<at::Tensor> k_pos, c10::optional<at::Tensor> inv_freq);
 void rmsnorm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps);
 void rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, at::Tensor rstd, at::Tensor dx,
-                 c10::optional<at::Tensor> dw);
+                 c10::optional<at::Tensor> dw, c10::optional<at::Tensor> dres);
 void swiglu_fwd(at::Tensor gu, at::Tensor h);
 void swiglu_bwd(at::Tensor gu, at::Tensor dh, at::Tensor dgu);
 void rope_inplace(at::Tensor x, int64_t ncols, int64_t head_dim, at::Tensor pos,
@@ -52,4 +54,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &adamw_step);
   m.def("sumsq_partials", &sumsq_partials);
   m.def("scale_inplace", &scale_inplace);
+  m.def("launch_count", []() { return nmb::launch_counter().load(); },
+        "number of kernel launches issued by this library so far");
 }

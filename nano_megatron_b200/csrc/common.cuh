@@ -8,12 +8,16 @@
 // false so the caller can unwind without hanging the GPU.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include "launch_counter.h"
+
 namespace nmb {
+
 
 // ---------------------------------------------------------------- status word
 // Error codes written into the device status word (first writer wins).

@@ -79,7 +79,9 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
                                    const __nv_bfloat16* __restrict__ w,
                                    const __nv_bfloat16* __restrict__ dy, int64_t lddy,
                                    const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx,
-                                   int64_t lddx, float* __restrict__ dw, int rows) {
+                                   int64_t lddx, float* __restrict__ dw,
+                                   const __nv_bfloat16* __restrict__ dres, int64_t lddres,
+                                   int rows) {
   constexpr int H = NCH * 256;
   __shared__ float sdw[H];
   for (int i = threadIdx.x; i < H; i += blockDim.x) sdw[i] = 0.f;
@@ -116,11 +118,20 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
     }
     dot = warp_sum(dot) / static_cast<float>(H);
     uint4* dr = reinterpret_cast<uint4*>(dx + static_cast<int64_t>(row) * lddx);
+    const uint4* rr =
+        dres != nullptr ? reinterpret_cast<const uint4*>(dres + static_cast<int64_t>(row) * lddres)
+                        : nullptr;
 #pragma unroll
     for (int c = 0; c < NCH; ++c) {
       float o[8];
 #pragma unroll
       for (int e = 0; e < 8; ++e) o[e] = r * (wg[c][e] - xh[c][e] * dot);
+      if (rr != nullptr) {
+        float rv[8];
+        unpack8(rr[c * 32 + lane], rv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] += rv[e];
+      }
       dr[c * 32 + lane] = pack8(o);
     }
   }
@@ -547,18 +558,19 @@ void rmsnorm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, doub
   float* rp = rstd.data_ptr<float>();
   const float e = static_cast<float>(eps);
   switch (H / 256) {
-    case 1: rmsnorm_fwd_kernel<1><<<blocks, threads, 0, s>>>(xp, ldx, wp, yp, ldy, rp, rows, e); break;
-    case 2: rmsnorm_fwd_kernel<2><<<blocks, threads, 0, s>>>(xp, ldx, wp, yp, ldy, rp, rows, e); break;
-    case 4: rmsnorm_fwd_kernel<4><<<blocks, threads, 0, s>>>(xp, ldx, wp, yp, ldy, rp, rows, e); break;
-    case 8: rmsnorm_fwd_kernel<8><<<blocks, threads, 0, s>>>(xp, ldx, wp, yp, ldy, rp, rows, e); break;
-    case 16: rmsnorm_fwd_kernel<16><<<blocks, threads, 0, s>>>(xp, ldx, wp, yp, ldy, rp, rows, e); break;
+    case 1: rmsnorm_fwd_kernel<1><<<blocks, threads, 0, s>>>(xp, ldx, wp, yp, ldy, rp, rows, e); NMB_LAUNCHED(1); break;
+    case 2: rmsnorm_fwd_kernel<2><<<blocks, threads, 0, s>>>(xp, ldx, wp, yp, ldy, rp, rows, e); NMB_LAUNCHED(1); break;
+    case 4: rmsnorm_fwd_kernel<4><<<blocks, threads, 0, s>>>(xp, ldx, wp, yp, ldy, rp, rows, e); NMB_LAUNCHED(1); break;
+    case 8: rmsnorm_fwd_kernel<8><<<blocks, threads, 0, s>>>(xp, ldx, wp, yp, ldy, rp, rows, e); NMB_LAUNCHED(1); break;
+    case 16: rmsnorm_fwd_kernel<16><<<blocks, threads, 0, s>>>(xp, ldx, wp, yp, ldy, rp, rows, e); NMB_LAUNCHED(1); break;
     default: TORCH_CHECK(false, "rmsnorm: unsupported hidden size ", H);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// dx = RMSNorm backward (+ dres, the residual branch's gradient, when given).
 void rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, at::Tensor rstd, at::Tensor dx,
-                 c10::optional<at::Tensor> dw) {
+                 c10::optional<at::Tensor> dw, c10::optional<at::Tensor> dres) {
   NMB_CHECK_BF16(x);
   NMB_CHECK_BF16(dy);
   NMB_CHECK_BF16(dx);
@@ -580,12 +592,19 @@ void rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, at::Tensor rstd, at:
   }
   const int64_t ldx = x.stride(-2), lddy = dy.stride(-2), lddx = dx.stride(-2);
   const float* rp = rstd.data_ptr<float>();
+  const __nv_bfloat16* rsp = nullptr;
+  int64_t ldr = 0;
+  if (dres.has_value()) {
+    NMB_CHECK_BF16(*dres);
+    rsp = reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr());
+    ldr = dres->stride(-2);
+  }
   switch (H / 256) {
-    case 1: rmsnorm_bwd_kernel<1><<<blocks, threads, 0, s>>>(xp, ldx, wp, gp, lddy, rp, dxp, lddx, dwp, rows); break;
-    case 2: rmsnorm_bwd_kernel<2><<<blocks, threads, 0, s>>>(xp, ldx, wp, gp, lddy, rp, dxp, lddx, dwp, rows); break;
-    case 4: rmsnorm_bwd_kernel<4><<<blocks, threads, 0, s>>>(xp, ldx, wp, gp, lddy, rp, dxp, lddx, dwp, rows); break;
-    case 8: rmsnorm_bwd_kernel<8><<<blocks, threads, 0, s>>>(xp, ldx, wp, gp, lddy, rp, dxp, lddx, dwp, rows); break;
-    case 16: rmsnorm_bwd_kernel<16><<<blocks, threads, 0, s>>>(xp, ldx, wp, gp, lddy, rp, dxp, lddx, dwp, rows); break;
+    case 1: rmsnorm_bwd_kernel<1><<<blocks, threads, 0, s>>>(xp, ldx, wp, gp, lddy, rp, dxp, lddx, dwp, rsp, ldr, rows); NMB_LAUNCHED(1); break;
+    case 2: rmsnorm_bwd_kernel<2><<<blocks, threads, 0, s>>>(xp, ldx, wp, gp, lddy, rp, dxp, lddx, dwp, rsp, ldr, rows); NMB_LAUNCHED(1); break;
+    case 4: rmsnorm_bwd_kernel<4><<<blocks, threads, 0, s>>>(xp, ldx, wp, gp, lddy, rp, dxp, lddx, dwp, rsp, ldr, rows); NMB_LAUNCHED(1); break;
+    case 8: rmsnorm_bwd_kernel<8><<<blocks, threads, 0, s>>>(xp, ldx, wp, gp, lddy, rp, dxp, lddx, dwp, rsp, ldr, rows); NMB_LAUNCHED(1); break;
+    case 16: rmsnorm_bwd_kernel<16><<<blocks, threads, 0, s>>>(xp, ldx, wp, gp, lddy, rp, dxp, lddx, dwp, rsp, ldr, rows); NMB_LAUNCHED(1); break;
     default: TORCH_CHECK(false, "rmsnorm_bwd: unsupported hidden size ", H);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -600,7 +619,7 @@ void swiglu_fwd(at::Tensor gu, at::Tensor h) {
   const int64_t work = static_cast<int64_t>(T) * (F / 8);
   swiglu_fwd_kernel<<<grid_for(work, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), gu.stride(0),
-      reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), h.stride(0), T, F);
+      reinterpret_cast<__nv_bfloat16*>(h.data_ptr()), h.stride(0), T, F); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -615,7 +634,7 @@ void swiglu_bwd(at::Tensor gu, at::Tensor dh, at::Tensor dgu) {
   swiglu_bwd_kernel<<<grid_for(work, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(gu.data_ptr()), gu.stride(0),
       reinterpret_cast<const __nv_bfloat16*>(dh.data_ptr()), dh.stride(0),
-      reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), dgu.stride(0), T, F);
+      reinterpret_cast<__nv_bfloat16*>(dgu.data_ptr()), dgu.stride(0), T, F); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -629,7 +648,7 @@ void rope_inplace(at::Tensor x, int64_t ncols, int64_t head_dim, at::Tensor pos,
   const int64_t work = static_cast<int64_t>(rows) * (ncols / 2);
   rope_kernel<<<grid_for(work, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), x.stride(0), rows, ncols, head_dim,
-      pos.data_ptr<int>(), pos.numel(), inv_freq.data_ptr<float>(), inverse ? -1.f : 1.f);
+      pos.data_ptr<int>(), pos.numel(), inv_freq.data_ptr<float>(), inverse ? -1.f : 1.f); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -644,7 +663,7 @@ void embedding_fwd(at::Tensor ids, at::Tensor w, int64_t vstart, at::Tensor out)
   const int blocks = std::max(1, std::min((T + 7) / 8, 148 * 16));
   embedding_fwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       ids.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), w.size(0),
-      vstart, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), T, H);
+      vstart, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), T, H); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -658,7 +677,7 @@ void embedding_bwd(at::Tensor ids, at::Tensor dy, at::Tensor grad, int64_t vstar
   const int blocks = std::max(1, std::min((T + 7) / 8, 148 * 16));
   embedding_bwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       ids.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
-      dy.stride(0), grad.data_ptr<float>(), grad.size(0), vstart, T, H);
+      dy.stride(0), grad.data_ptr<float>(), grad.size(0), vstart, T, H); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -669,7 +688,7 @@ void ce_stats(at::Tensor logits, at::Tensor labels, int64_t vstart, at::Tensor s
   const at::cuda::CUDAGuard guard(logits.device());
   ce_stats_kernel<256><<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
-      labels.data_ptr<int64_t>(), vstart, V, T, stats.data_ptr<float>());
+      labels.data_ptr<int64_t>(), vstart, V, T, stats.data_ptr<float>()); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -681,7 +700,7 @@ void ce_finish(at::Tensor logits, at::Tensor labels, int64_t vstart, at::Tensor 
   ce_finish_kernel<256><<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
       labels.data_ptr<int64_t>(), vstart, V, T, stats.data_ptr<float>(), shards,
-      loss_row.data_ptr<float>(), write_grad ? 1 : 0);
+      loss_row.data_ptr<float>(), write_grad ? 1 : 0); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -692,7 +711,7 @@ void ce_fused(at::Tensor logits, at::Tensor labels, at::Tensor loss_row, bool wr
   const at::cuda::CUDAGuard guard(logits.device());
   ce_fused_kernel<256><<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
-      labels.data_ptr<int64_t>(), V, T, loss_row.data_ptr<float>(), write_grad ? 1 : 0);
+      labels.data_ptr<int64_t>(), V, T, loss_row.data_ptr<float>(), write_grad ? 1 : 0); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -723,7 +742,7 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v,
   adamw_kernel<<<grid_for(n / 4 + 1, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       p.data_ptr<float>(), g.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(), pb, n,
       hp, grad_scale.has_value() ? grad_scale->data_ptr<float>() : nullptr,
-      lr_t.has_value() ? lr_t->data_ptr<float>() : nullptr);
+      lr_t.has_value() ? lr_t->data_ptr<float>() : nullptr); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -733,7 +752,7 @@ at::Tensor sumsq_partials(at::Tensor x) {
   const int blocks = grid_for(x.numel() / 4 + 1, 256);
   auto out = at::empty({blocks}, x.options());
   sumsq_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(x.data_ptr<float>(),
-                                                                    x.numel(), out.data_ptr<float>());
+                                                                    x.numel(), out.data_ptr<float>()); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   return out;
 }
@@ -742,6 +761,6 @@ void scale_inplace(at::Tensor x, double s) {
   TORCH_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous());
   const at::cuda::CUDAGuard guard(x.device());
   scale_kernel<<<grid_for(x.numel(), 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      x.data_ptr<float>(), x.numel(), static_cast<float>(s));
+      x.data_ptr<float>(), x.numel(), static_cast<float>(s)); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -50,6 +50,7 @@ struct GemmParams {
   int swiglu_up_row;         // kEpiSwiGLU: row of W_up inside B (= F)
   const int* positions;      // kEpiRoPE: position of each sequence slot [seq_len]
   int seq_len;
+  int pos_div;               // kEpiRoPE: row r has position positions[(r / pos_div) % seq_len]
   const float* inv_freq;     // kEpiRoPE: [head_dim / 2]
   int head_dim;
   int rope_cols;
@@ -327,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int D = p.head_dim;
         const int half_chunks = D / 64;  // 32-col chunks per half head
         const int chunks_per_head = D / 32;
-        const int pos = row_ok ? __ldg(p.positions + (row % p.seq_len)) : 0;
+        const int pos = row_ok ? __ldg(p.positions + ((row / p.pos_div) % p.seq_len)) : 0;
 #pragma unroll 1
         for (int h = 0; h < BN / D; ++h) {
 #pragma unroll 1
@@ -434,7 +435,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
   }
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p);
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -479,8 +480,8 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
              c10::optional<at::Tensor> residual, c10::optional<at::Tensor> alpha_t, double alpha,
              double beta, c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
              c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
-             int64_t head_dim, int64_t rope_cols, at::Tensor status, int64_t bn_override,
-             int64_t max_ctas) {
+             int64_t head_dim, int64_t rope_cols, int64_t pos_div, at::Tensor status,
+             int64_t bn_override, int64_t max_ctas) {
   check_operand(a, "A");
   check_operand(b, "B");
   const int64_t M = a_mn ? a.size(1) : a.size(0);
@@ -526,6 +527,7 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
     TORCH_CHECK(head_dim == 64 || head_dim == 128, "RoPE epilogue supports head_dim 64/128");
     p.positions = positions->data_ptr<int>();
     p.seq_len = static_cast<int>(positions->numel());
+    p.pos_div = static_cast<int>(pos_div > 0 ? pos_div : 1);
     p.inv_freq = inv_freq->data_ptr<float>();
     p.head_dim = static_cast<int>(head_dim);
     p.rope_cols = static_cast<int>(rope_cols);

@@ -1,0 +1,471 @@
+"""Data-parallel strategies: DDP, ZeRO-1, ZeRO-2 (ZeRO-3 lives in :mod:`.zero3`).
+
+Trainer-facing contract of the reference's DataParallelStrategy
+(src/nano_megatron/data_parallel/interface.py:17-178): ``configure_precision``,
+``setup``, ``forward_microbatch_context``, ``microbatch_context``, ``backward``,
+``finalize_gradients``, ``clip_grad_norm``, ``optimizer_step``,
+``set_learning_rate``/``learning_rate``, ``zero_grad``, ``state_dict``/
+``load_state_dict``.
+
+B200 design:
+* parameters and fp32 gradients live in flat buffers (:mod:`.buffers`); the
+  weight-gradient GEMMs accumulate straight into the reduction buffer;
+* the gradient reduction per bucket is one NCCL all-reduce (DDP, ZeRO-1) or
+  reduce-scatter (ZeRO-2/3) of the fp32 buffer, optionally launched on a side
+  stream as soon as a bucket's gradients are final (``overlap_grad_reduce``);
+* averaging, clipping and AdamW are one fused kernel over the flat fp32 master
+  (the clip coefficient and 1/DP are folded into its gradient scale, read on
+  the device): no host synchronisation anywhere in the step;
+* the updated compute-precision parameters are written by that same kernel
+  (DDP) or all-gathered from the owners' shards (ZeRO).
+"""
+
+from __future__ import annotations
+
+from contextlib import contextmanager
+
+import torch
+import torch.distributed as dist
+from torch import nn
+
+from nano_megatron_b200.ops import functional as F
+from nano_megatron_b200.parallel.group_plan import GroupKey
+
+from .buffers import FlatBuffers, unique_named_parameters
+from .common import clip_coefficient, local_sumsq, norm_ranges, reduce_model_parallel
+from .offload import ActivationOffloader, OffloadPolicy, OptimizerStateStorage
+
+_DTYPES = {"float32": torch.float32, "bfloat16": torch.bfloat16, "float16": torch.float16}
+
+
+def _torch_dtype(value) -> torch.dtype:
+    name = str(getattr(value, "value", value)).lower()
+    if name not in _DTYPES:
+        raise ValueError(f"unsupported precision dtype: {name!r}")
+    return _DTYPES[name]
+
+
+class DataParallelStrategy:
+    mode = "base"
+
+    def __init__(self, *, config=None, offload=None, parallel=None, parameter_domains=None) -> None:
+        self.config = config
+        self.parallel = parallel
+        self.parameter_domains = parameter_domains
+        self.offload_policy = OffloadPolicy.from_config(offload)
+        self.offload_policy.validate(self.mode)
+        self._activation_offloader = ActivationOffloader(self.offload_policy)
+        self._model: nn.Module | None = None
+        self._sync_this_backward = True
+        self.param_dtype: torch.dtype | None = None
+        self.compute_dtype: torch.dtype | None = None
+        self.grad_reduce_dtype: torch.dtype | None = None
+        self.buffers: FlatBuffers | None = None
+        self._lr = 0.0
+        self._lr_t: torch.Tensor | None = None
+        self.step_count = 0
+        self._grad_scale: torch.Tensor | None = None
+        self._reduced = False
+        self._pending: list = []
+        self._comm_stream = None
+
+    # ------------------------------------------------------------------ contract
+    def configure_precision(self, precision) -> None:
+        self.param_dtype = _torch_dtype(precision.params)
+        self.compute_dtype = _torch_dtype(precision.compute)
+        self.grad_reduce_dtype = _torch_dtype(precision.grad_reduce)
+
+    @property
+    def model(self) -> nn.Module:
+        if self._model is None:
+            raise RuntimeError("data-parallel strategy has not been set up")
+        return self._model
+
+    @property
+    def replica_group(self):
+        if self.parallel is None:
+            return None
+        try:
+            return self.parallel.group(GroupKey.DENSE_REPLICA)
+        except KeyError:
+            return None
+
+    @property
+    def replica_size(self) -> int:
+        g = self.replica_group
+        return 1 if g is None else g.size
+
+    def _model_dtype(self, device) -> torch.dtype:
+        """On CUDA the model always computes in the compute dtype (bf16) with fp32 masters."""
+        compute = self.compute_dtype or torch.bfloat16
+        params = self.param_dtype or compute
+        if device.type == "cuda":
+            return compute if compute in (torch.bfloat16, torch.float16) else torch.bfloat16
+        return params if params in (torch.float32, torch.float64) else torch.float32
+
+    def setup(self, model: nn.Module, optimizer_config, parameter_domains=None) -> nn.Module:
+        self.parameter_domains = parameter_domains or self.parameter_domains
+        self.optimizer_config = optimizer_config
+        named = unique_named_parameters(model)
+        device = named[0][1].device
+        if device.type == "cpu" and torch.cuda.is_available() and False:
+            device = torch.device("cuda")
+        model_dtype = self._model_dtype(device)
+        self._master_init = {id(p): p.detach().to(torch.float32 if p.dtype != torch.float64
+                                                   else torch.float64).clone() for _, p in named}
+        self._broadcast_from_replica_root(named)
+        bucket_bytes = int(getattr(self.config, "bucket_bytes", 256 * 1024 * 1024))
+        grad_dtype = torch.float64 if model_dtype == torch.float64 else torch.float32
+        self.buffers = FlatBuffers(named, domains=self.parameter_domains, parallel=self.parallel,
+                                   bucket_bytes=bucket_bytes, param_dtype=model_dtype,
+                                   grad_dtype=grad_dtype, device=device)
+        self._named = named
+        self._ranges = norm_ranges(self.buffers, self.parallel)
+        self._sp_slices = [(b, s) for b, s in self.buffers.slices() if s.sequence_parallel_grad]
+        self._init_optimizer_state()
+        self._lr = float(getattr(optimizer_config, "lr", 3e-4))
+        self._lr_t = torch.tensor([self._lr], dtype=torch.float32, device=device)
+        self._model = model
+        self.overlap = bool(getattr(self.config, "overlap_grad_reduce", False))
+        del self._master_init
+        return model
+
+    def _broadcast_from_replica_root(self, named) -> None:
+        g = self.replica_group
+        if g is None or g.size == 1:
+            return
+        for _, p in named:
+            dist.broadcast(p.data, src=g.ranks[0], group=g.process_group)
+
+    @contextmanager
+    def activation_context(self):
+        with self._activation_offloader.context():
+            yield
+
+    @contextmanager
+    def forward_microbatch_context(self, *, synchronize_gradients: bool, unit=None):
+        with self.activation_context():
+            yield
+
+    @contextmanager
+    def microbatch_context(self, *, is_last_microbatch: bool, unit=None):
+        prev = self._sync_this_backward
+        self._sync_this_backward = is_last_microbatch
+        try:
+            with self.activation_context():
+                yield
+        finally:
+            self._sync_this_backward = prev
+
+    def backward(self, loss: torch.Tensor) -> None:
+        loss.backward()
+
+    # ------------------------------------------------------------------ reduction
+    def _reduce_sequence_parallel_grads(self) -> None:
+        """SP norm/bias weights saw only their sequence shard: sum over TP once per step."""
+        if not self._sp_slices or self.parallel is None or self.parallel.tp.size == 1:
+            return
+        grads = [s.parameter.main_grad for _, s in self._sp_slices]
+        flat = torch.cat([g.reshape(-1) for g in grads])
+        dist.all_reduce(flat, group=self.parallel.tp.process_group)
+        off = 0
+        for g in grads:
+            n = g.numel()
+            g.copy_(flat[off:off + n].view_as(g))
+            off += n
+
+    def finalize_gradients(self) -> None:
+        self._reduce_sequence_parallel_grads()
+        self._reduce_buckets()
+        self._reduced = True
+
+    def _reduce_buckets(self) -> None:
+        g = self.replica_group
+        if g is None or g.size == 1:
+            return
+        for b in self.buffers.buckets:
+            dist.all_reduce(b.grad_data, group=g.process_group)
+
+    def _grad_view_for_norm(self) -> tuple[torch.Tensor, list]:
+        return self.buffers.grad_flat, self._ranges
+
+    def clip_grad_norm(self, max_norm: float | None) -> torch.Tensor:
+        """Global gradient norm of the *averaged* gradients (device tensor)."""
+        flat, ranges = self._grad_view_for_norm()
+        sq = local_sumsq(flat, ranges).reshape(1).to(torch.float32)
+        sq = self._reduce_norm_over_shards(sq)
+        sq = reduce_model_parallel(sq, self.parallel)
+        norm = sq.sqrt() / self.replica_size
+        coef = clip_coefficient(norm, max_norm)
+        self._grad_scale = (coef / self.replica_size).reshape(1).to(torch.float32)
+        return norm.reshape(())
+
+    def _reduce_norm_over_shards(self, sq):
+        return sq
+
+    # ------------------------------------------------------------------ optimizer
+    def _opt_hparams(self):
+        c = self.optimizer_config
+        b1, b2 = tuple(getattr(c, "betas", (0.9, 0.95)))
+        return (float(b1), float(b2), float(getattr(c, "eps", 1e-8)),
+                float(getattr(c, "weight_decay", 0.0)))
+
+    def set_learning_rate(self, learning_rate: float) -> None:
+        self._lr = float(learning_rate)
+        if self._lr_t is not None:
+            self._lr_t.fill_(self._lr)
+
+    @property
+    def learning_rate(self) -> float:
+        return self._lr
+
+    def zero_grad(self) -> None:
+        if self.buffers is not None:
+            self.buffers.zero_grad()
+        self._reduced = False
+        self._grad_scale = None
+
+    def _scale(self) -> torch.Tensor | None:
+        if self._grad_scale is not None:
+            return self._grad_scale
+        if self.replica_size > 1:
+            return torch.full((1,), 1.0 / self.replica_size, device=self.buffers.device)
+        return None
+
+
+class DDPStrategy(DataParallelStrategy):
+    """Replicated parameters; fp32 master, exp_avg, exp_avg_sq for every element."""
+
+    mode = "ddp"
+
+    def _init_optimizer_state(self) -> None:
+        buf = self.buffers
+        self.master = torch.zeros(buf.numel, dtype=buf.grad_dtype, device=buf.device)
+        for b, s in buf.slices():
+            self.master[b.offset + s.start:b.offset + s.end].copy_(
+                self._master_init[id(s.parameter)].reshape(-1))
+        self.exp_avg = torch.zeros_like(self.master)
+        self.exp_avg_sq = torch.zeros_like(self.master)
+
+    def optimizer_step(self) -> None:
+        if not self._reduced:
+            self.finalize_gradients()
+        self.step_count += 1
+        b1, b2, eps, wd = self._opt_hparams()
+        low = self.buffers.param_flat if self.buffers.param_flat.dtype != self.master.dtype else None
+        F.adamw_(self.master, self.buffers.grad_flat, self.exp_avg, self.exp_avg_sq, low,
+                 lr=self._lr, beta1=b1, beta2=b2, eps=eps, weight_decay=wd,
+                 step=self.step_count, grad_scale=self._scale(), lr_t=self._lr_t)
+        if low is None:
+            self.buffers.param_flat.copy_(self.master)
+
+    def state_dict(self) -> dict:
+        """torch.optim.AdamW-shaped state (one entry per unique parameter) + fp32 masters."""
+        b1, b2, eps, wd = self._opt_hparams()
+        state, ids = {}, []
+        for i, (b, s) in enumerate(self.buffers.slices()):
+            a, e = b.offset + s.start, b.offset + s.end
+            shape = s.parameter.shape
+            state[i] = {"step": torch.tensor(float(self.step_count)),
+                        "exp_avg": self.exp_avg[a:e].view(shape).detach().cpu().clone(),
+                        "exp_avg_sq": self.exp_avg_sq[a:e].view(shape).detach().cpu().clone(),
+                        "master_param": self.master[a:e].view(shape).detach().cpu().clone()}
+            ids.append(i)
+        groups = [{"lr": self._lr, "betas": (b1, b2), "eps": eps, "weight_decay": wd,
+                   "amsgrad": False, "maximize": False, "foreach": None, "capturable": False,
+                   "differentiable": False, "fused": None, "params": ids}]
+        return {"mode": self.mode, "optimizer": {"state": state, "param_groups": groups}}
+
+    def load_state_dict(self, state_dict) -> None:
+        if state_dict.get("mode") != self.mode:
+            raise ValueError(f"data-parallel state mode {state_dict.get('mode')!r} does not "
+                             f"match {self.mode!r}")
+        opt = state_dict["optimizer"]
+        for i, (b, s) in enumerate(self.buffers.slices()):
+            a, e = b.offset + s.start, b.offset + s.end
+            st = opt["state"].get(i) or opt["state"].get(str(i))
+            if st is None:
+                continue
+            self.exp_avg[a:e].copy_(st["exp_avg"].reshape(-1))
+            self.exp_avg_sq[a:e].copy_(st["exp_avg_sq"].reshape(-1))
+            if "master_param" in st:
+                self.master[a:e].copy_(st["master_param"].reshape(-1))
+            else:
+                self.master[a:e].copy_(s.parameter.detach().reshape(-1).float())
+            self.step_count = int(float(st["step"]))
+        self._lr = float(opt["param_groups"][0]["lr"])
+        self.set_learning_rate(self._lr)
+        self.sync_params_from_master()
+
+    def sync_params_from_master(self) -> None:
+        self.buffers.param_flat.copy_(self.master)
+
+    def load_model_parameters(self) -> None:
+        """Refresh the fp32 masters after parameters were overwritten (checkpoint load)."""
+        for b, s in self.buffers.slices():
+            self.master[b.offset + s.start:b.offset + s.end].copy_(
+                s.parameter.detach().reshape(-1))
+
+
+class ReplicatedStrategy(DDPStrategy):
+    """DDP semantics without a replica group (single replica)."""
+
+    mode = "replicated"
+
+
+class FlatShardZeROStrategy(DataParallelStrategy):
+    """ZeRO-1/2: fp32 master + Adam moments sharded over the replica group."""
+
+    mode = "zero"
+    reduce_scatter = False
+
+    def _init_optimizer_state(self) -> None:
+        buf = self.buffers
+        storage = OptimizerStateStorage(self.offload_policy, buf.device)
+        self.shards = []
+        for b in buf.buckets:
+            full = torch.zeros(b.padded_numel, dtype=buf.grad_dtype)
+            for s in b.slices:
+                full[s.start:s.end].copy_(self._master_init[id(s.parameter)].reshape(-1).cpu())
+            lo, hi = b.rank * b.shard_numel, (b.rank + 1) * b.shard_numel
+            master = storage.zeros(b.shard_numel).to(buf.grad_dtype)
+            master.copy_(full[lo:hi])
+            if not self.offload_policy.optimizer_state:
+                master = master.to(buf.device)
+            self.shards.append({"master": master, "exp_avg": storage.zeros(b.shard_numel),
+                                "exp_avg_sq": storage.zeros(b.shard_numel),
+                                "grad": torch.zeros(b.shard_numel, dtype=buf.grad_dtype,
+                                                    device=buf.device)})
+
+    def _reduce_buckets(self) -> None:
+        g = self.replica_group
+        for b, sh in zip(self.buffers.buckets, self.shards):
+            full = b.grad_data[:b.padded_numel]
+            if g is None or g.size == 1:
+                sh["grad"].copy_(full)
+                continue
+            if self.reduce_scatter and full.is_cuda:
+                dist.reduce_scatter_tensor(sh["grad"], full, group=g.process_group)
+            else:
+                dist.all_reduce(full, group=g.process_group)
+                sh["grad"].copy_(b.shard_view(full))
+
+    def _grad_view_for_norm(self):
+        # squared norm over this rank's shard of each bucket (counting rule per slice)
+        return None, None
+
+    def clip_grad_norm(self, max_norm: float | None) -> torch.Tensor:
+        dev = self.buffers.device
+        sq = torch.zeros(1, dtype=torch.float32, device=dev)
+        from .common import counts_toward_norm
+
+        for b, sh in zip(self.buffers.buckets, self.shards):
+            lo = b.rank * b.shard_numel
+            hi = lo + b.shard_numel
+            for s in b.slices:
+                a, e = max(s.start, lo), min(s.end, hi)
+                if a >= e or not counts_toward_norm(s, self.parallel):
+                    continue
+                sq += F.sumsq(sh["grad"][a - lo:e - lo])
+        g = self.replica_group
+        if g is not None and g.size > 1:
+            dist.all_reduce(sq, group=g.process_group)
+        sq = reduce_model_parallel(sq, self.parallel)
+        norm = sq.sqrt() / self.replica_size
+        coef = clip_coefficient(norm, max_norm)
+        self._grad_scale = (coef / self.replica_size).reshape(1).to(torch.float32)
+        return norm.reshape(())
+
+    def optimizer_step(self) -> None:
+        if not self._reduced:
+            self.finalize_gradients()
+        self.step_count += 1
+        b1, b2, eps, wd = self._opt_hparams()
+        g = self.replica_group
+        scale = self._scale()
+        for b, sh in zip(self.buffers.buckets, self.shards):
+            dev = sh["master"].device
+            grad = sh["grad"] if dev == sh["grad"].device else sh["grad"].to(dev)
+            sc = scale if scale is None or scale.device == dev else scale.to(dev)
+            lr_t = self._lr_t if self._lr_t.device == dev else None
+            F.adamw_(sh["master"], grad, sh["exp_avg"], sh["exp_avg_sq"], None, lr=self._lr,
+                     beta1=b1, beta2=b2, eps=eps, weight_decay=wd, step=self.step_count,
+                     grad_scale=sc, lr_t=lr_t)
+            low = sh["master"].to(device=b.param_data.device, dtype=b.param_data.dtype)
+            full = b.param_data[:b.padded_numel]
+            if g is None or g.size == 1:
+                full.copy_(low)
+            elif full.is_cuda:
+                dist.all_gather_into_tensor(full, low, group=g.process_group)
+            else:
+                parts = [torch.empty_like(low) for _ in range(g.size)]
+                dist.all_gather(parts, low, group=g.process_group)
+                full.copy_(torch.cat(parts))
+
+    def _gather_shard(self, b, t: torch.Tensor) -> torch.Tensor:
+        g = self.replica_group
+        if g is None or g.size == 1:
+            return t.detach().cpu().clone()
+        parts = [torch.empty_like(t) for _ in range(g.size)]
+        dist.all_gather(parts, t.contiguous(), group=g.process_group)
+        return torch.cat(parts).cpu()
+
+    def state_dict(self) -> dict:
+        buckets = {}
+        for b, sh in zip(self.buffers.buckets, self.shards):
+            entry = {"metadata": b.metadata()}
+            for k, key in (("master", "master_parameter"), ("exp_avg", "exp_avg"),
+                           ("exp_avg_sq", "exp_avg_sq")):
+                t = sh[k].to(self.buffers.device) if sh[k].device != self.buffers.device \
+                    else sh[k]
+                entry[key] = self._gather_shard(b, t)[:b.numel].clone()
+            buckets[b.index] = entry
+        return {"mode": self.mode, "step": self.step_count, "learning_rate": self._lr,
+                "buckets": buckets}
+
+    def load_state_dict(self, state_dict) -> None:
+        if state_dict.get("mode") != self.mode:
+            raise ValueError(f"data-parallel state mode {state_dict.get('mode')!r} does not "
+                             f"match {self.mode!r}")
+        self.step_count = int(state_dict["step"])
+        self.set_learning_rate(float(state_dict["learning_rate"]))
+        for b, sh in zip(self.buffers.buckets, self.shards):
+            entry = state_dict["buckets"].get(b.index) or state_dict["buckets"].get(str(b.index))
+            meta = entry["metadata"]
+            if meta["parameter_names"] != [s.name for s in b.slices] or meta["numel"] != b.numel:
+                raise ValueError("zero bucket boundaries must match the checkpoint")
+            lo = b.rank * b.shard_numel
+            for k, key in (("master", "master_parameter"), ("exp_avg", "exp_avg"),
+                           ("exp_avg_sq", "exp_avg_sq")):
+                full = torch.zeros(b.padded_numel, dtype=sh[k].dtype)
+                full[:b.numel].copy_(entry[key].reshape(-1)[:b.numel])
+                sh[k].copy_(full[lo:lo + b.shard_numel])
+        self.sync_params_from_master()
+
+    def sync_params_from_master(self) -> None:
+        g = self.replica_group
+        for b, sh in zip(self.buffers.buckets, self.shards):
+            low = sh["master"].to(device=b.param_data.device, dtype=b.param_data.dtype)
+            full = b.param_data[:b.padded_numel]
+            if g is None or g.size == 1:
+                full.copy_(low)
+            else:
+                parts = [torch.empty_like(low) for _ in range(g.size)]
+                dist.all_gather(parts, low, group=g.process_group)
+                full.copy_(torch.cat(parts))
+
+    def load_model_parameters(self) -> None:
+        for b, sh in zip(self.buffers.buckets, self.shards):
+            lo = b.rank * b.shard_numel
+            src = b.param_data[:b.padded_numel][lo:lo + b.shard_numel]
+            sh["master"].copy_(src.to(sh["master"].dtype))
+
+
+class Zero1Strategy(FlatShardZeROStrategy):
+    mode = "zero1"
+    reduce_scatter = False
+
+
+class Zero2Strategy(FlatShardZeROStrategy):
+    mode = "zero2"
+    reduce_scatter = True

@@ -1,0 +1,357 @@
+"""Fused per-block autograd functions of the GPT training path.
+
+One ``torch.autograd.Function`` per transformer sub-block keeps the Python
+overhead per layer to two calls and lets each block choose its own kernel
+schedule:
+
+* attention block: RMSNorm -> [SP all-gather] -> QKV GEMM with RoPE epilogue
+  -> causal flash attention (local or context-parallel core) -> out-proj GEMM
+  with the residual add in its epilogue -> [SP reduce-scatter / TP all-reduce];
+* MLP block: RMSNorm -> [SP all-gather] -> gate|up GEMM with SwiGLU epilogue
+  -> down GEMM with residual epilogue -> [SP reduce-scatter / TP all-reduce];
+* embedding (vocab-parallel gather + TP reduction) and LM head (final norm,
+  logits GEMM, vocab-parallel cross-entropy whose gradient overwrites the
+  logits in place, so no fp32 logits or softmax copy is ever stored).
+
+Weight gradients are accumulated straight into each parameter's fp32
+``main_grad`` (a view of the data-parallel gradient buffer) by the
+weight-gradient GEMM epilogue; autograd returns ``None`` for parameters.
+Activations are sequence-major ``[S, B, H]`` flattened to ``[S*B, H]``; under
+sequence parallelism each TP rank holds a contiguous block of S/TP rows.
+
+The reference computes the same math module by module
+(src/nano_megatron/models/gpt/layer.py:91-137, attention.py:153-209,
+mlp.py:42-78, model.py:171-250).
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+
+import torch
+
+from nano_megatron_b200.ops import functional as F
+from nano_megatron_b200.tensor_parallel.comm import all_gather_dim0, all_reduce, reduce_scatter_dim0
+from nano_megatron_b200.tensor_parallel.cross_entropy import vocab_parallel_ce_rows
+
+
+def main_grad_of(p: torch.Tensor) -> torch.Tensor:
+    """The fp32 gradient accumulator of ``p`` (created on first use if no buffer owns it)."""
+    g = getattr(p, "main_grad", None)
+    if g is None:
+        dt = torch.float64 if p.dtype == torch.float64 else torch.float32
+        g = torch.zeros(p.shape, dtype=dt, device=p.device)
+        p.main_grad = g
+    return g
+
+
+def _contiguous_run(tensors: list[torch.Tensor]) -> bool:
+    ptr = tensors[0].data_ptr()
+    for t in tensors:
+        if not t.is_contiguous() or t.data_ptr() != ptr:
+            return False
+        ptr += t.numel() * t.element_size()
+    return True
+
+
+def fused_rows(params: list[torch.Tensor]) -> torch.Tensor:
+    """Row-concatenation of 2-D weights: a zero-copy view when they are adjacent in memory."""
+    if _contiguous_run(params):
+        rows = sum(p.shape[0] for p in params)
+        return torch.as_strided(params[0].detach(), (rows, params[0].shape[1]),
+                                (params[0].shape[1], 1))
+    return torch.cat([p.detach() for p in params], 0)
+
+
+class FusedGrad:
+    """Row-concatenated main-grad target for several parameters.
+
+    If their accumulators are adjacent it is a view; otherwise a scratch buffer
+    that :meth:`flush` adds back into each parameter's accumulator."""
+
+    def __init__(self, params: list[torch.Tensor]):
+        self.params = params
+        grads = [main_grad_of(p) for p in params]
+        if _contiguous_run(grads):
+            rows = sum(g.shape[0] for g in grads)
+            self.target = torch.as_strided(grads[0], (rows,) + tuple(grads[0].shape[1:]),
+                                           grads[0].stride())
+            self.scratch = False
+        else:
+            self.target = torch.zeros((sum(g.shape[0] for g in grads),) + tuple(grads[0].shape[1:]),
+                                      dtype=grads[0].dtype, device=grads[0].device)
+            self.scratch = True
+
+    def flush(self) -> None:
+        if not self.scratch:
+            return
+        off = 0
+        for p in self.params:
+            n = p.shape[0]
+            main_grad_of(p).add_(self.target[off:off + n])
+            off += n
+
+
+@dataclass
+class TPInfo:
+    group: object | None
+    size: int
+    sequence_parallel: bool
+
+    def gather(self, x):
+        return all_gather_dim0(x, self.group) if self.sequence_parallel and self.size > 1 else x
+
+    def reduce_out(self, y):
+        """Reduction after a row-parallel GEMM (forward)."""
+        if self.size == 1:
+            return y
+        return reduce_scatter_dim0(y, self.group) if self.sequence_parallel else \
+            all_reduce(y, self.group)
+
+    def reduce_in_grad(self, dx):
+        """Reduction of the input gradient of a column-parallel GEMM (backward)."""
+        if self.size == 1:
+            return dx
+        return reduce_scatter_dim0(dx, self.group) if self.sequence_parallel else \
+            all_reduce(dx, self.group)
+
+
+@dataclass
+class MicrobatchInfo:
+    """Per-microbatch runtime facts shared by all blocks of one forward."""
+
+    batch: int                 # B
+    seq: int                   # S_local (this CP rank's sequence length, before SP)
+    positions: torch.Tensor    # int32 [S_local], absolute positions of local tokens
+    cp_chunks: tuple = ()      # ((start_row, length, position_offset), ...) of local chunks
+    microbatch_index: int = 0
+    extra: dict = field(default_factory=dict)
+
+
+# ---------------------------------------------------------------- attention core
+class LocalAttentionCore:
+    """Causal flash attention over the local sequence (no context parallelism)."""
+
+    applies_inverse_rope = True
+
+    def forward(self, q, k, v, o, mb: MicrobatchInfo):
+        o_bs = o.transpose(0, 1)
+        B, S, Hq, D = o_bs.shape
+        lse = torch.empty(B, Hq, S, device=q.device, dtype=torch.float32)
+        if q.is_cuda:
+            from nano_megatron_b200.ops._ext import lib
+            lib().flash_attn_fwd(q, k, v, o_bs, lse, D ** -0.5, True, 0, 0)
+        else:
+            out, lse2 = F.attention_fwd(q, k, v, causal=True)
+            o_bs.copy_(out)
+            lse.copy_(lse2)
+        return lse
+
+    def backward(self, q, k, v, o, do, lse, dq, dk, dv, mb: MicrobatchInfo, inv_freq):
+        F.attention_bwd(q, k, v, o.transpose(0, 1), do, lse, dq, dk, dv, causal=True,
+                        q_pos=mb.positions, k_pos=mb.positions, inv_freq=inv_freq)
+
+
+def _split_qkv(qkv2d: torch.Tensor, S: int, B: int, hq: int, hkv: int, D: int):
+    v4 = qkv2d.view(S, B, hq + 2 * hkv, D)
+    q = v4[:, :, :hq].transpose(0, 1)
+    k = v4[:, :, hq:hq + hkv].transpose(0, 1)
+    v = v4[:, :, hq + hkv:].transpose(0, 1)
+    return q, k, v
+
+
+@dataclass
+class AttnSpec:
+    hidden: int
+    heads: int          # local query heads
+    kv_heads: int       # local kv heads
+    head_dim: int
+    eps: float
+    tp: TPInfo
+    core: object
+    dropout: float = 0.0
+
+
+class AttentionBlockFn(torch.autograd.Function):
+    """h_out = h + out_proj(attn(rope(qkv(norm(h))))) with TP/SP collectives."""
+
+    @staticmethod
+    def forward(ctx, h, w_norm, w_q, w_k, w_v, w_out, b_out, spec: AttnSpec, mb: MicrobatchInfo,
+                inv_freq, dropout_fn):
+        H = spec.hidden
+        h2 = h.reshape(-1, H)
+        xn, rstd = F.rmsnorm(h2, w_norm, spec.eps)
+        xg = spec.tp.gather(xn)
+        w_qkv = fused_rows([w_q, w_k, w_v])
+        D, hq, hkv = spec.head_dim, spec.heads, spec.kv_heads
+        qkv = F.qkv_rope_linear(xg, w_qkv, mb.positions, inv_freq, D, (hq + hkv) * D,
+                                pos_div=mb.batch)
+        q, k, v = _split_qkv(qkv, mb.seq, mb.batch, hq, hkv, D)
+        o = torch.empty(mb.seq, mb.batch, hq, D, device=h.device, dtype=qkv.dtype)
+        lse = spec.core.forward(q, k, v, o, mb)
+        ctx2 = o.view(mb.seq * mb.batch, hq * D)
+        fuse_residual = spec.tp.size == 1 and b_out is None and dropout_fn is None
+        if fuse_residual:
+            out = F.linear(ctx2, w_out.detach(), residual=h2)
+        else:
+            y = spec.tp.reduce_out(F.linear(ctx2, w_out.detach()))
+            if b_out is not None:
+                y = y + b_out.detach()
+            if dropout_fn is not None:
+                y = dropout_fn(y)
+            out = h2 + y
+        ctx.spec, ctx.mb, ctx.inv_freq = spec, mb, inv_freq
+        ctx.params = (w_norm, w_q, w_k, w_v, w_out, b_out)
+        ctx.dropout_fn = dropout_fn
+        ctx.save_for_backward(h2, rstd, xg, qkv, o, lse)
+        return out.view(h.shape)
+
+    @staticmethod
+    def backward(ctx, dout):
+        spec, mb = ctx.spec, ctx.mb
+        h2, rstd, xg, qkv, o, lse = ctx.saved_tensors
+        w_norm, w_q, w_k, w_v, w_out, b_out = ctx.params
+        D, hq, hkv = spec.head_dim, spec.heads, spec.kv_heads
+        dh = dout.reshape(h2.shape).contiguous()
+        dy = dh
+        if ctx.dropout_fn is not None:
+            dy = ctx.dropout_fn.backward(dy)
+        if b_out is not None:
+            F.bias_grad(dy, main_grad_of(b_out))
+        dyg = spec.tp.gather(dy)
+        ctx2 = o.view(mb.seq * mb.batch, hq * D)
+        d_ctx = F.linear_dgrad(dyg, w_out.detach())
+        F.linear_wgrad(dyg, ctx2, main_grad_of(w_out))
+        q, k, v = _split_qkv(qkv, mb.seq, mb.batch, hq, hkv, D)
+        dqkv = torch.empty_like(qkv)
+        dq, dk, dv = _split_qkv(dqkv, mb.seq, mb.batch, hq, hkv, D)
+        do = d_ctx.view(mb.seq, mb.batch, hq, D).transpose(0, 1)
+        spec.core.backward(q, k, v, o, do, lse, dq, dk, dv, mb, ctx.inv_freq)
+        del d_ctx
+        if not getattr(spec.core, "applies_inverse_rope", True):
+            F.rope_(dqkv, (hq + hkv) * D, D, mb.positions, ctx.inv_freq, inverse=True,
+                    pos_div=mb.batch)
+        w_qkv = fused_rows([w_q, w_k, w_v])
+        dxg = F.linear_dgrad(dqkv, w_qkv)
+        g = FusedGrad([w_q, w_k, w_v])
+        F.linear_wgrad(dqkv, xg, g.target)
+        g.flush()
+        dxn = spec.tp.reduce_in_grad(dxg)
+        dh_in = F.rmsnorm_bwd(h2, w_norm.detach(), dxn, rstd, main_grad_of(w_norm), dres=dh)
+        return (dh_in.view(dout.shape), None, None, None, None, None, None, None, None, None, None)
+
+
+@dataclass
+class MLPSpec:
+    hidden: int
+    ffn: int            # local FFN width (F / TP)
+    eps: float
+    tp: TPInfo
+
+
+class MLPBlockFn(torch.autograd.Function):
+    """h_out = h + down(silu(gate(norm(h))) * up(norm(h))) with TP/SP collectives."""
+
+    @staticmethod
+    def forward(ctx, h, w_norm, w_gate, w_up, w_down, b_down, spec: MLPSpec, dropout_fn):
+        H = spec.hidden
+        h2 = h.reshape(-1, H)
+        xn, rstd = F.rmsnorm(h2, w_norm, spec.eps)
+        xg = spec.tp.gather(xn)
+        w_gu = fused_rows([w_gate, w_up])
+        hmid, gu = F.swiglu_linear(xg, w_gu, spec.ffn)
+        fuse_residual = spec.tp.size == 1 and b_down is None and dropout_fn is None
+        if fuse_residual:
+            out = F.linear(hmid, w_down.detach(), residual=h2)
+        else:
+            y = spec.tp.reduce_out(F.linear(hmid, w_down.detach()))
+            if b_down is not None:
+                y = y + b_down.detach()
+            if dropout_fn is not None:
+                y = dropout_fn(y)
+            out = h2 + y
+        ctx.spec = spec
+        ctx.params = (w_norm, w_gate, w_up, w_down, b_down)
+        ctx.dropout_fn = dropout_fn
+        ctx.save_for_backward(h2, rstd, xg, gu, hmid)
+        return out.view(h.shape)
+
+    @staticmethod
+    def backward(ctx, dout):
+        spec = ctx.spec
+        h2, rstd, xg, gu, hmid = ctx.saved_tensors
+        w_norm, w_gate, w_up, w_down, b_down = ctx.params
+        dh = dout.reshape(h2.shape).contiguous()
+        dy = dh
+        if ctx.dropout_fn is not None:
+            dy = ctx.dropout_fn.backward(dy)
+        if b_down is not None:
+            F.bias_grad(dy, main_grad_of(b_down))
+        dyg = spec.tp.gather(dy)
+        dmid = F.linear_dgrad(dyg, w_down.detach())
+        F.linear_wgrad(dyg, hmid, main_grad_of(w_down))
+        dgu = F.swiglu_bwd(gu, dmid, inplace=True)
+        del dmid
+        w_gu = fused_rows([w_gate, w_up])
+        dxg = F.linear_dgrad(dgu, w_gu)
+        g = FusedGrad([w_gate, w_up])
+        F.linear_wgrad(dgu, xg, g.target)
+        g.flush()
+        dxn = spec.tp.reduce_in_grad(dxg)
+        dh_in = F.rmsnorm_bwd(h2, w_norm.detach(), dxn, rstd, main_grad_of(w_norm), dres=dh)
+        return dh_in.view(dout.shape), None, None, None, None, None, None, None
+
+
+class EmbeddingFn(torch.autograd.Function):
+    """Vocab-parallel lookup of sequence-major ids, summed over TP (RS under SP)."""
+
+    @staticmethod
+    def forward(ctx, ids, weight, vstart: int, tp: TPInfo):
+        out = F.embedding(ids, weight.detach(), vstart)
+        out = tp.reduce_out(out)
+        ctx.vstart, ctx.tp, ctx.weight = vstart, tp, weight
+        ctx.save_for_backward(ids)
+        return out
+
+    @staticmethod
+    def backward(ctx, dy):
+        (ids,) = ctx.saved_tensors
+        dyg = ctx.tp.gather(dy.reshape(-1, dy.shape[-1]).contiguous())
+        F.embedding_bwd(ids, dyg, main_grad_of(ctx.weight), ctx.vstart)
+        return None, None, None, None
+
+
+class HeadLossFn(torch.autograd.Function):
+    """Final RMSNorm + vocab-parallel logits + cross-entropy (mean over valid tokens).
+
+    The CE kernel replaces the logits by ``softmax - onehot`` in place; backward
+    scales it by ``grad / count`` inside the dgrad/wgrad GEMM epilogues."""
+
+    @staticmethod
+    def forward(ctx, h, w_norm, w_lm, labels, eps: float, tp: TPInfo):
+        H = h.shape[-1]
+        h2 = h.reshape(-1, H)
+        xn, rstd = F.rmsnorm(h2, w_norm.detach(), eps)
+        xg = tp.gather(xn)
+        logits = F.linear(xg, w_lm.detach())
+        rows = vocab_parallel_ce_rows(logits, labels, tp.group if tp.size > 1 else None,
+                                      write_grad=True)
+        count = (labels >= 0).sum().to(rows.dtype)
+        loss = rows.sum() / count.clamp_min(1.0)
+        ctx.tp, ctx.eps, ctx.params = tp, eps, (w_norm, w_lm)
+        ctx.hshape = h.shape
+        ctx.save_for_backward(h2, rstd, xg, logits, count)
+        return loss
+
+    @staticmethod
+    def backward(ctx, g):
+        h2, rstd, xg, dlogits, count = ctx.saved_tensors
+        w_norm, w_lm = ctx.params
+        alpha = (g.to(torch.float32) / count.clamp_min(1.0).to(torch.float32)).reshape(1)
+        if not dlogits.is_cuda:
+            alpha = alpha.to(dlogits.dtype) if dlogits.dtype == torch.float64 else alpha
+        dxg = F.linear_dgrad(dlogits, w_lm.detach(), alpha_t=alpha)
+        F.linear_wgrad(dlogits, xg, main_grad_of(w_lm), alpha_t=alpha)
+        dxn = ctx.tp.reduce_in_grad(dxg)
+        dh = F.rmsnorm_bwd(h2, w_norm.detach(), dxn, rstd, main_grad_of(w_norm))
+        return dh.view(ctx.hshape), None, None, None, None, None

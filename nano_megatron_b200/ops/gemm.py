@@ -39,12 +39,13 @@ def gemm(
     inv_freq: torch.Tensor | None = None,
     head_dim: int = 0,
     rope_cols: int = 0,
+    pos_div: int = 1,
     block_n: int = 0,
     max_ctas: int = 0,
 ) -> torch.Tensor:
     lib().gemm_tc(
         a, a_mn, b, b_mn, out, epilogue, residual, alpha_t, float(alpha), float(beta), aux,
-        int(swiglu_up_row), positions, inv_freq, int(head_dim), int(rope_cols),
+        int(swiglu_up_row), positions, inv_freq, int(head_dim), int(rope_cols), int(pos_div),
         status_word(a.device), int(block_n), int(max_ctas),
     )
     return out
@@ -89,10 +90,10 @@ def swiglu_fwd(x: torch.Tensor, w_gate_up: torch.Tensor, ffn: int, *,
 
 
 def qkv_rope_fwd(x: torch.Tensor, w_qkv: torch.Tensor, positions: torch.Tensor,
-                 inv_freq: torch.Tensor, head_dim: int, rope_cols: int, *,
+                 inv_freq: torch.Tensor, head_dim: int, rope_cols: int, *, pos_div: int = 1,
                  out: torch.Tensor | None = None) -> torch.Tensor:
     """Fused QKV projection with rotary embedding on the first ``rope_cols`` columns."""
     if out is None:
         out = torch.empty(x.shape[0], w_qkv.shape[0], device=x.device, dtype=torch.bfloat16)
     return gemm(x, w_qkv, out, epilogue=EPI_ROPE, positions=positions, inv_freq=inv_freq,
-                head_dim=head_dim, rope_cols=rope_cols)
+                head_dim=head_dim, rope_cols=rope_cols, pos_div=pos_div)

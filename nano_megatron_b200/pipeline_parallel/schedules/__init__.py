@@ -1,0 +1,15 @@
+"""Pipeline schedules (GPipe, 1F1B, interleaved 1F1B) and the executor."""
+
+from .base import LossAccumulator, extract_loss
+from .no_pipeline import NoPipelineSchedule
+
+
+def build_schedule(config, model, parallel, data_parallel):
+    if parallel.pp.size == 1 and config.pipeline.virtual_stages_per_rank == 1:
+        return NoPipelineSchedule(model, data_parallel)
+    from .executor import build_pipeline_schedule
+
+    return build_pipeline_schedule(config, model, parallel, data_parallel)
+
+
+__all__ = ["LossAccumulator", "NoPipelineSchedule", "build_schedule", "extract_loss"]

@@ -1,0 +1,59 @@
+"""Assemble a training job from a :class:`TrainConfig` (the ``run`` path of the CLI).
+
+Order of the reference's CLI (src/nano_megatron/cli/train.py:89-202): runtime ->
+parallel context -> ParallelRNG -> ``torch.manual_seed(seed(DENSE_INIT))`` ->
+context-parallel attention -> model builder (CPU init, fp32) -> data-parallel
+strategy. The model is moved to the device and flattened into the strategy's
+buffers in compute precision (bf16 on CUDA) with fp32 masters.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from nano_megatron_b200.context_parallel import build_context_parallel_attention
+from nano_megatron_b200.data_parallel import build_data_parallel_strategy
+from nano_megatron_b200.models.gpt import DenseGPTComponents, GPTModelBuilder
+from nano_megatron_b200.parallel.context import ParallelContext
+from nano_megatron_b200.parallel.domains import ParameterDomainRegistry
+from nano_megatron_b200.parallel.rng import ParallelRNG, RNGStream
+
+
+@dataclass
+class TrainingComponents:
+    runtime: object
+    parallel: ParallelContext
+    rng: ParallelRNG
+    model: torch.nn.Module
+    built: object
+    data_parallel: object
+
+
+def build_model(config, parallel, rng, *, device):
+    torch.manual_seed(rng.seed(RNGStream.DENSE_INIT))
+    cp_attention = build_context_parallel_attention(config.context_parallel, parallel)
+    components = DenseGPTComponents(cp_attention=cp_attention)
+    builder = GPTModelBuilder(components, parameter_domains=ParameterDomainRegistry(),
+                              activation_checkpoint_config=config.activation_checkpoint)
+    if config.pipeline.virtual_stages_per_rank > 1:
+        built = builder.build_pipeline(config.model, parallel, None,
+                                       virtual_stages_per_rank=config.pipeline
+                                       .virtual_stages_per_rank, rng=rng,
+                                       cp_attention=cp_attention)
+    else:
+        built = builder.build_stage(config.model, parallel, None, rng=rng,
+                                    cp_attention=cp_attention)
+    model = built.model.to(device=device)
+    return model, built
+
+
+def build_training_components(config, runtime) -> TrainingComponents:
+    parallel = ParallelContext.create(runtime, config.parallel)
+    rng = ParallelRNG.from_context(config.training.seed, parallel)
+    model, built = build_model(config, parallel, rng, device=runtime.device)
+    strategy = build_data_parallel_strategy(config.data_parallel, config.offload, parallel,
+                                            built.parameter_domains)
+    strategy.configure_precision(config.precision)
+    return TrainingComponents(runtime, parallel, rng, model, built, strategy)

@@ -1,0 +1,358 @@
+"""Training loop: train_step / evaluate / fit with device-side metrics.
+
+Behaviour of the reference Trainer (src/nano_megatron/training/trainer.py:
+117-894): the step routes the batch (source rank -> batch-replica peers, CP
+slicing), splits microbatches, zeroes grads, runs the pipeline schedule,
+synchronises tied embeddings, finalises the data-parallel reduction, clips,
+steps the optimizer and the LR schedule, and aggregates token-weighted loss
+metrics. Differences, B200-first: the step never synchronises with the host
+(loss sums, token counts and the gradient norm stay on the device until a log
+interval), it is timed with CUDA events (max over ranks), and checkpoint /
+validation / metric-history hooks run between steps.
+"""
+
+from __future__ import annotations
+
+import math
+import time
+from dataclasses import dataclass, field
+from typing import Any
+
+import torch
+import torch.distributed as dist
+
+from nano_megatron_b200.parallel.group_plan import GroupKey
+from nano_megatron_b200.utils.timing import DeviceStepTimer, max_over_ranks
+
+from .batch_router import BatchRouter
+from .lr_scheduler import LearningRateScheduler
+from .metrics import aggregate_loss_metrics
+from .microbatches import split_microbatches
+
+
+@dataclass
+class TrainerState:
+    step: int = 0
+    consumed_samples: int = 0
+    consumed_tokens: int = 0
+    data_fingerprint: str | None = None
+    data_epoch: int = 0
+    data_shuffle_seed: int | None = None
+    data_sample_offset: int = 0
+    data_samples_per_epoch: int | None = None
+    lr_scheduler: dict | None = None
+    wandb_run_id: str | None = None
+    metrics_history: dict | None = None
+    best_validation_loss: float | None = None
+    best_validation_step: int | None = None
+    best_validation_checkpoint: str | None = None
+
+    _FIELDS = ("step", "consumed_samples", "consumed_tokens", "data_fingerprint", "data_epoch",
+               "data_shuffle_seed", "data_sample_offset", "data_samples_per_epoch",
+               "lr_scheduler", "wandb_run_id", "metrics_history", "best_validation_loss",
+               "best_validation_step", "best_validation_checkpoint")
+
+    def state_dict(self) -> dict[str, Any]:
+        out = {k: getattr(self, k) for k in self._FIELDS}
+        for k in ("lr_scheduler", "metrics_history"):
+            if out[k] is not None:
+                out[k] = dict(out[k])
+        return out
+
+    def load_state_dict(self, state: dict[str, Any]) -> None:
+        for k in ("step", "consumed_samples", "consumed_tokens", "data_epoch",
+                  "data_sample_offset"):
+            v = int(state.get(k, 0))
+            if v < 0:
+                raise ValueError(f"trainer {k} must be non-negative")
+            setattr(self, k, v)
+        seed = state.get("data_shuffle_seed")
+        if seed is not None and int(seed) < 0:
+            raise ValueError("trainer data_shuffle_seed must be non-negative or null")
+        self.data_shuffle_seed = None if seed is None else int(seed)
+        spe = state.get("data_samples_per_epoch")
+        if spe is not None and int(spe) < 1:
+            raise ValueError("trainer data_samples_per_epoch must be positive or null")
+        self.data_samples_per_epoch = None if spe is None else int(spe)
+        fp = state.get("data_fingerprint")
+        if fp is not None and (not isinstance(fp, str) or not fp):
+            raise ValueError("trainer data_fingerprint must be a non-empty string or null")
+        self.data_fingerprint = fp
+        sched = state.get("lr_scheduler")
+        if sched is not None and not isinstance(sched, dict):
+            raise ValueError("trainer lr_scheduler state must be a mapping or null")
+        self.lr_scheduler = None if sched is None else dict(sched)
+        rid = state.get("wandb_run_id")
+        if rid is not None and (not isinstance(rid, str) or not rid):
+            raise ValueError("trainer wandb_run_id must be a non-empty string or null")
+        self.wandb_run_id = rid
+        mh = state.get("metrics_history")
+        if mh is not None and not isinstance(mh, dict):
+            raise ValueError("trainer metrics_history state must be a mapping or null")
+        self.metrics_history = None if mh is None else dict(mh)
+        bl, bs, bc = (state.get("best_validation_loss"), state.get("best_validation_step"),
+                      state.get("best_validation_checkpoint"))
+        if bl is None and bs is None:
+            if bc is not None:
+                raise ValueError("trainer best_validation_checkpoint requires best validation "
+                                 "metrics")
+            self.best_validation_loss = self.best_validation_step = None
+            self.best_validation_checkpoint = None
+            return
+        if isinstance(bl, bool) or not isinstance(bl, (int, float)) or not math.isfinite(bl) \
+                or bl < 0:
+            raise ValueError("trainer best_validation_loss must be finite and non-negative")
+        if isinstance(bs, bool) or not isinstance(bs, int) or bs < 0:
+            raise ValueError("trainer best_validation_step must be a non-negative integer")
+        self.best_validation_loss, self.best_validation_step = float(bl), bs
+        self.best_validation_checkpoint = bc
+
+
+def _move_to_device(batch, device):
+    if isinstance(batch, torch.Tensor):
+        return batch.to(device, non_blocking=True)
+    if isinstance(batch, dict):
+        return {k: _move_to_device(v, device) for k, v in batch.items()}
+    return batch
+
+
+class Trainer:
+    def __init__(self, *, config, model, parallel, data_parallel, checkpoint=None,
+                 data_iterator=None, metrics_path=None, resume_metrics_path=None, rng=None,
+                 device=None) -> None:
+        self.config = config
+        self.model = model
+        self.parallel = parallel
+        self.data_parallel = data_parallel
+        self.checkpoint = checkpoint
+        self.data_iterator = data_iterator
+        self.rng = rng
+        self.state = TrainerState()
+        self.device = device or next(model.parameters()).device
+        data_parallel.configure_precision(config.precision)
+        self.prepare_pipeline_stage()
+        data_parallel.setup(model, config.optimizer, getattr(data_parallel, "parameter_domains",
+                                                             None))
+        self.batch_router = BatchRouter(parallel, load_balance=bool(
+            getattr(config.context_parallel, "load_balance", False)))
+        self.schedule = self._build_schedule()
+        self.lr_scheduler = LearningRateScheduler(config=config.lr_scheduler,
+                                                  optimizer_config=config.optimizer,
+                                                  data_parallel=data_parallel,
+                                                  max_steps=config.training.max_steps)
+        self.timer = DeviceStepTimer(self.device)
+        self.last_step_ms: float | None = None
+        self.metrics_path = metrics_path
+        self.resume_metrics_path = resume_metrics_path
+        self.validation_data = None
+        self._hooks: list = []
+
+    # ------------------------------------------------------------------ setup
+    def prepare_pipeline_stage(self) -> None:
+        sync = getattr(self.model, "synchronize_tied_embedding_weights", None)
+        if callable(sync):
+            sync()
+
+    def _build_schedule(self):
+        from nano_megatron_b200.pipeline_parallel.schedules import build_schedule
+
+        return build_schedule(self.config, self.model, self.parallel, self.data_parallel)
+
+    @property
+    def micro_batch_size(self) -> int:
+        return self.config.training.micro_batch_size
+
+    # ------------------------------------------------------------------ steps
+    def _prepare_batch(self, batch):
+        batch = self.batch_router.route(batch)
+        batch = _move_to_device(batch, self.device)
+        micro = split_microbatches(batch, self.micro_batch_size)
+        out = []
+        for i, mb in enumerate(micro):
+            mb = dict(mb) if isinstance(mb, dict) else mb
+            if isinstance(mb, dict):
+                mb["_microbatch_index"] = i
+            out.append(mb)
+        return out
+
+    def train_step(self, batch) -> dict[str, Any]:
+        """One optimizer update. Returns device tensors (``loss``, ``grad_norm``...)."""
+        self.model.train()
+        micro = self._prepare_batch(batch)
+        dp = self.data_parallel
+        dp.zero_grad()
+        acc = self.schedule.forward_backward(micro, forward_only=False)
+        sync = getattr(self.model, "synchronize_tied_embedding_gradients", None)
+        if callable(sync):
+            sync()
+        dp.finalize_gradients()
+        clip = self.config.optimizer.clip_grad_norm
+        grad_norm = dp.clip_grad_norm(clip)
+        dp.optimizer_step()
+        self.state.step += 1
+        self.lr_scheduler.set_completed_steps(self.state.step)
+        self.state.lr_scheduler = self.lr_scheduler.state_dict()
+        gbs = self.config.training.micro_batch_size * \
+            self.config.training.gradient_accumulation_steps * \
+            self.parallel.dp.size * self.parallel.ep.size
+        self.state.consumed_samples += gbs
+        self.state.consumed_tokens += gbs * self.config.model.seq_length
+        loss_sum, count = aggregate_loss_metrics(acc, self.parallel, self.device)
+        return {"loss_sum": loss_sum, "token_count": count, "grad_norm": grad_norm,
+                "learning_rate": dp.learning_rate}
+
+    @torch.no_grad()
+    def evaluate_step(self, batch) -> tuple[torch.Tensor, torch.Tensor]:
+        self.model.eval()
+        micro = self._prepare_batch(batch)
+        acc = self.schedule.forward_backward(micro, forward_only=True)
+        return aggregate_loss_metrics(acc, self.parallel, self.device)
+
+    def evaluate(self, batches) -> dict[str, float]:
+        total, count = 0.0, 0.0
+        for b in batches:
+            s, c = self.evaluate_step(b)
+            total += float(s)
+            count += float(c)
+        loss = total / max(count, 1.0)
+        return {"loss": loss, "perplexity": math.exp(min(loss, 50.0)), "token_count": count}
+
+    def timed_train_step(self, batch) -> tuple[dict[str, Any], float]:
+        """``train_step`` bracketed by CUDA events; returns (metrics, device ms)."""
+        self.timer.start()
+        out = self.train_step(batch)
+        self.timer.stop()
+        ms = self.timer.elapsed_ms()
+        self.last_step_ms = ms
+        return out, ms
+
+    def bind_data_iterator(self, data, *, data_fingerprint: str | None = None) -> None:
+        if self.state.data_fingerprint is not None and data_fingerprint is not None and \
+                self.state.data_fingerprint != data_fingerprint:
+            raise RuntimeError("data fingerprint changed across resume")
+        self.state.data_fingerprint = data_fingerprint
+        restore = getattr(data, "load_state_dict", None)
+        if callable(restore) and self.state.step > 0:
+            restore({"epoch": self.state.data_epoch, "seed": self.state.data_shuffle_seed,
+                     "sample_offset": self.state.data_sample_offset})
+        self._data = data
+        self.data_iterator = iter(data)
+
+    def bind_validation_data(self, data) -> None:
+        self.validation_data = data
+
+    def _record_data_state(self) -> None:
+        data = getattr(self, "_data", None)
+        get = getattr(data, "state_dict", None)
+        if callable(get):
+            st = get()
+            self.state.data_epoch = int(st.get("epoch", 0))
+            self.state.data_shuffle_seed = st.get("seed")
+            self.state.data_sample_offset = int(st.get("sample_offset", 0))
+            self.state.data_samples_per_epoch = st.get("samples_per_epoch")
+
+    def fit(self, *, max_steps: int | None = None, log=print) -> TrainerState:
+        target = max_steps if max_steps is not None else self.config.training.max_steps
+        interval = self.config.training.log_interval
+        pending: list = []
+        t0 = time.perf_counter()
+        device_ms = 0.0
+        while self.state.step < target:
+            batch = next(self.data_iterator) if self.batch_router.is_source else None
+            out, ms = self.timed_train_step(batch)
+            self._record_data_state()
+            device_ms += ms
+            pending.append(out)
+            if self.state.step % interval == 0 or self.state.step == target:
+                self._log(pending, time.perf_counter() - t0, device_ms, log)
+                pending, device_ms, t0 = [], 0.0, time.perf_counter()
+            self._after_step()
+        self.flush()
+        return self.state
+
+    def _after_step(self) -> None:
+        for hook in self._hooks:
+            hook(self)
+        cp = self.checkpoint
+        if cp is not None:
+            iv = self.config.checkpoint.save_interval
+            if iv and self.state.step % iv == 0:
+                self.save_checkpoint()
+        vc = self.config.validation
+        if self.validation_data is not None and vc.interval and self.state.step % vc.interval == 0:
+            self.run_validation()
+
+    def run_validation(self) -> dict[str, float]:
+        batches = []
+        it = iter(self.validation_data)
+        for _ in range(self.config.validation.batches):
+            try:
+                batches.append(next(it))
+            except StopIteration:
+                break
+        metrics = self.evaluate(batches)
+        best = self.state.best_validation_loss
+        if best is None or metrics["loss"] < best:
+            self.state.best_validation_loss = metrics["loss"]
+            self.state.best_validation_step = self.state.step
+            if self.checkpoint is not None and self.config.checkpoint.save_best_validation:
+                path = self.save_checkpoint()
+                self.state.best_validation_checkpoint = str(path) if path else None
+        return metrics
+
+    def _log(self, pending, host_s, device_ms, log) -> None:
+        loss_sum = sum(float(p["loss_sum"]) for p in pending)
+        count = sum(float(p["token_count"]) for p in pending)
+        loss = loss_sum / max(count, 1.0)
+        gn = float(pending[-1]["grad_norm"])
+        n = len(pending)
+        gbs = self.config.training.micro_batch_size * \
+            self.config.training.gradient_accumulation_steps * \
+            self.parallel.dp.size * self.parallel.ep.size
+        tokens = n * gbs * self.config.model.seq_length
+        dev_max = max_over_ranks(device_ms, self.device)
+        metrics = {"step": self.state.step, "loss": loss,
+                   "perplexity": math.exp(min(loss, 50.0)), "token_count": count,
+                   "grad_norm": gn, "learning_rate": pending[-1]["learning_rate"],
+                   "samples_per_second": n * gbs / max(host_s, 1e-9),
+                   "tokens_per_second": tokens / max(host_s, 1e-9),
+                   "tokens_per_second_device": tokens / max(dev_max / 1000.0, 1e-9)}
+        if self.device.type == "cuda":
+            gib = 1024 ** 3
+            metrics.update({
+                "gpu_memory_allocated_gib": torch.cuda.memory_allocated(self.device) / gib,
+                "gpu_memory_peak_allocated_gib": torch.cuda.max_memory_allocated(self.device) / gib,
+                "gpu_memory_reserved_gib": torch.cuda.memory_reserved(self.device) / gib,
+                "gpu_memory_peak_reserved_gib": torch.cuda.max_memory_reserved(self.device) / gib})
+        self.last_metrics = metrics
+        if self.parallel.rank == 0 and log is not None:
+            log(" ".join(f"{k}={v:.6g}" if isinstance(v, float) else f"{k}={v}"
+                         for k, v in metrics.items()))
+        history = getattr(self, "metric_history", None)
+        if history is not None:
+            history.append(metrics, trainer_state=self.state.state_dict())
+
+    # ------------------------------------------------------------------ checkpoints
+    def save_checkpoint(self):
+        if self.checkpoint is None:
+            return None
+        return self.checkpoint.save(step=self.state.step, model=self.model,
+                                    data_parallel=self.data_parallel,
+                                    trainer_state=self.state.state_dict(), rng=self.rng)
+
+    def load_checkpoint(self, path) -> None:
+        loaded = self.checkpoint.load(path, model=self.model, data_parallel=self.data_parallel,
+                                      rng=self.rng)
+        self.state.load_state_dict(loaded["trainer_state"])
+        if self.state.lr_scheduler is not None:
+            self.lr_scheduler.load_state_dict(self.state.lr_scheduler,
+                                              expected_completed_steps=self.state.step)
+        else:
+            self.lr_scheduler.set_completed_steps(self.state.step)
+
+    def flush(self) -> None:
+        if self.checkpoint is not None and hasattr(self.checkpoint, "flush"):
+            self.checkpoint.flush()
+
+    def close(self) -> None:
+        self.flush()

@@ -177,7 +177,7 @@ def test_rmsnorm(h):
     ref.backward(dy.float())
     dx = torch.empty_like(x)
     dw = torch.zeros(h, device=DEV)
-    lib().rmsnorm_bwd(x, w, dy, rstd, dx, dw)
+    lib().rmsnorm_bwd(x, w, dy, rstd, dx, dw, None)
     assert _rel(dx, xr.grad) < 1e-2
     assert _rel(dw, wr.grad) < 1e-2
 
