@@ -726,3 +726,127 @@ void flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the backward (declared and documented in noalloc.h).
+// Same three kernels as flash_attn_bwd above; its two temporaries live in a
+// fixed device array owned by this file instead of caller-provided workspaces.
+#include <mutex>
+
+#include "noalloc.h"
+
+namespace nmb {
+namespace attn {
+
+static __device__ __align__(256) float g_noalloc_scratch[NMB_NOALLOC_SCRATCH_FLOATS];
+
+constexpr int kNoAllocMaxDevices = 64;
+static float* g_noalloc_scratch_addr[kNoAllocMaxDevices] = {nullptr};
+static std::mutex g_noalloc_mutex;
+
+// Device address of the scratch array for the current device (set up once).
+static float* noalloc_scratch_for_current_device(int* err) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNoAllocMaxDevices) {
+    *err = NMB_NOALLOC_SETUP_FAILED;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+  if (g_noalloc_scratch_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    const cudaError_t rc = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (rc != cudaSuccess || ptr == nullptr) {
+      *err = NMB_NOALLOC_SETUP_FAILED;
+      return nullptr;
+    }
+    g_noalloc_scratch_addr[dev] = static_cast<float*>(ptr);
+  }
+  return g_noalloc_scratch_addr[dev];
+}
+
+template <int D>
+static int noalloc_launch(const BwdParams& p, cudaStream_t stream) {
+  const int rows = p.B * p.Sq * p.Hq;
+  const int64_t pairs = static_cast<int64_t>(rows) * (D / 2);
+  const int smem = (4 * 64 * D + 64 * 64) * 2 + 2 * 64 * 4;
+  if (cudaFuncSetAttribute(flash_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           smem) != cudaSuccess)
+    return NMB_NOALLOC_LAUNCH_FAILED;
+  dim3 grid((p.Sk + 63) / 64, p.Hkv, p.B);
+  flash_bwd_pre_kernel<D><<<(rows + 7) / 8, 256, 0, stream>>>(p);
+  flash_bwd_kernel<D><<<grid, 128, smem, stream>>>(p);
+  flash_bwd_dq_kernel<D><<<(pairs + 255) / 256, 256, 0, stream>>>(p);
+  NMB_LAUNCHED(3);
+  return cudaGetLastError() == cudaSuccess ? NMB_NOALLOC_OK : NMB_NOALLOC_LAUNCH_FAILED;
+}
+
+}  // namespace attn
+}  // namespace nmb
+
+extern "C" int nmb_flash_attn_bwd_noalloc(const void* q, const void* k, const void* v,
+                                          const void* o, const void* dout, const float* lse,
+                                          void* dq, void* dk, void* dv, int batch, int seq_q,
+                                          int seq_k, int heads_q, int heads_kv, int head_dim,
+                                          float softmax_scale, int causal, int q_offset,
+                                          int k_offset, cudaStream_t stream) {
+  using namespace nmb::attn;
+  const void* ptrs[] = {q, k, v, o, dout, lse, dq, dk, dv};
+  for (const void* ptr : ptrs)
+    if (ptr == nullptr || (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0)
+      return NMB_NOALLOC_BAD_ARGUMENT;
+  if ((head_dim != 64 && head_dim != 128) || batch < 0 || seq_q < 0 || seq_k < 0 ||
+      heads_q <= 0 || heads_kv <= 0 || heads_q % heads_kv != 0)
+    return NMB_NOALLOC_BAD_ARGUMENT;
+  const long long rows = static_cast<long long>(batch) * seq_q * heads_q;
+  const long long delta_floats = (rows + 63) / 64 * 64;  // keeps dq_acc 256-byte aligned
+  if (delta_floats + rows * head_dim > NMB_NOALLOC_SCRATCH_FLOATS) return NMB_NOALLOC_TOO_LARGE;
+  if (rows == 0) return NMB_NOALLOC_OK;
+  int err = NMB_NOALLOC_OK;
+  float* scratch = noalloc_scratch_for_current_device(&err);
+  if (scratch == nullptr) return err;
+
+  BwdParams p{};
+  const int64_t D = head_dim;
+  p.q = static_cast<const __nv_bfloat16*>(q);
+  p.k = static_cast<const __nv_bfloat16*>(k);
+  p.v = static_cast<const __nv_bfloat16*>(v);
+  p.o = static_cast<const __nv_bfloat16*>(o);
+  p.dout = static_cast<const __nv_bfloat16*>(dout);
+  p.q_row = p.o_row = p.do_row = p.dq_row = heads_q * D;
+  p.q_batch = p.o_batch = p.do_batch = p.dq_batch = static_cast<int64_t>(seq_q) * heads_q * D;
+  p.k_row = p.v_row = p.dk_row = p.dv_row = heads_kv * D;
+  p.k_batch = p.v_batch = p.dk_batch = p.dv_batch = static_cast<int64_t>(seq_k) * heads_kv * D;
+  p.lse = lse;
+  p.delta = scratch;
+  p.dq_acc = scratch + delta_floats;
+  p.dq = static_cast<__nv_bfloat16*>(dq);
+  p.dk = static_cast<__nv_bfloat16*>(dk);
+  p.dv = static_cast<__nv_bfloat16*>(dv);
+  p.B = batch;
+  p.Sq = seq_q;
+  p.Sk = seq_k;
+  p.Hq = heads_q;
+  p.Hkv = heads_kv;
+  p.q_offset = q_offset;
+  p.k_offset = k_offset;
+  p.causal = causal ? 1 : 0;
+  p.scale = softmax_scale;
+  p.scale_log2 = softmax_scale * kLog2e;
+  return head_dim == 64 ? noalloc_launch<64>(p, stream) : noalloc_launch<128>(p, stream);
+}
+
+extern "C" const char* nmb_noalloc_strerror(int code) {
+  switch (code) {
+    case NMB_NOALLOC_OK: return "ok";
+    case NMB_NOALLOC_BAD_ARGUMENT:
+      return "bad argument: null or non-16-byte-aligned pointer, head_dim not 64/128, or "
+             "heads_q not a multiple of heads_kv";
+    case NMB_NOALLOC_TOO_LARGE:
+      return "problem too large for the fixed scratch: needs B*Hq*Sq*(D+1) floats (+64) <= "
+             "NMB_NOALLOC_SCRATCH_FLOATS (8 Mi floats)";
+    case NMB_NOALLOC_SETUP_FAILED:
+      return "could not resolve the scratch array's device address on the current device";
+    case NMB_NOALLOC_LAUNCH_FAILED: return "kernel launch failed";
+    default: return "unknown error";
+  }
+}
