@@ -302,12 +302,32 @@ def attention_bwd(q, k, v, o, do, lse, dq, dk, dv, *, causal: bool, q_offset: in
         lib().flash_attn_bwd(q, k, v, o, do, lse, dq, dk, dv, delta, dq_acc, scale, causal,
                              q_offset, k_offset, q_pos, k_pos, inv_freq)
         return
-    with torch.enable_grad():
-        qr = q.detach().requires_grad_()
-        kr = k.detach().requires_grad_()
-        vr = v.detach().requires_grad_()
-        out, _ = _attn_math(qr, kr, vr, causal, q_offset, k_offset, scale)
-        gq, gk, gv = torch.autograd.grad(out, (qr, kr, vr), do.to(out.dtype))
+    # Explicit flash-attention backward using the given (global) log-sum-exp, so a
+    # partial key block (ring attention) gets its share of the global softmax.
+    cd = torch.float64 if q.dtype == torch.float64 else torch.float32
+    Hkv = k.shape[2]
+    rep = Hq // Hkv
+    qf = q.to(cd).transpose(1, 2)                                   # [B, Hq, Sq, D]
+    kf = k.to(cd).repeat_interleave(rep, 2).transpose(1, 2)        # [B, Hq, Sk, D]
+    vf = v.to(cd).repeat_interleave(rep, 2).transpose(1, 2)
+    of = o.to(cd).transpose(1, 2)
+    dof = do.to(cd).transpose(1, 2)
+    s = (qf @ kf.transpose(-1, -2)) * scale
+    p = torch.exp2(s * math.log2(math.e) - lse.to(cd)[..., None])
+    if causal:
+        qp = torch.arange(q.shape[1]) + q_offset
+        kp = torch.arange(k.shape[1]) + k_offset
+        p = p.masked_fill((kp[None, :] > qp[:, None]).to(p.device), 0.0)
+    p = p.nan_to_num(0.0)
+    dvf = p.transpose(-1, -2) @ dof
+    dp = dof @ vf.transpose(-1, -2)
+    delta = (dof * of).sum(-1, keepdim=True)
+    ds = p * (dp - delta)
+    dqf = (ds @ kf) * scale
+    dkf = (ds.transpose(-1, -2) @ qf) * scale
+    gq = dqf.transpose(1, 2)
+    gk = dkf.view(B, Hkv, rep, -1, D).sum(2).transpose(1, 2)
+    gv = dvf.view(B, Hkv, rep, -1, D).sum(2).transpose(1, 2)
     for dst, src, pos in ((dq, gq, q_pos), (dk, gk, k_pos), (dv, gv, None)):
         if pos is not None:
             flat = src.to(dst.dtype).reshape(B * src.shape[1], -1).clone()

@@ -30,10 +30,11 @@ def vocab_parallel_ce_rows(logits2d: torch.Tensor, labels1d: torch.Tensor, group
         return F.ce_local(logits2d, labels1d, write_grad)
     vstart = group.rank * logits2d.shape[1]
     stats = F.ce_stats(logits2d, labels1d, vstart)
-    gathered = torch.empty((group.size,) + tuple(stats.shape), dtype=stats.dtype,
-                           device=stats.device)
+    gathered = torch.empty((group.size * stats.shape[0],) + tuple(stats.shape[1:]),
+                           dtype=stats.dtype, device=stats.device)
     dist.all_gather_into_tensor(gathered, stats.contiguous(), group=group.process_group)
-    return F.ce_finish(logits2d, labels1d, vstart, gathered, write_grad)
+    return F.ce_finish(logits2d, labels1d, vstart, gathered.view(group.size, *stats.shape),
+                       write_grad)
 
 
 class _VocabParallelCEFn(torch.autograd.Function):
