@@ -850,3 +850,72 @@ extern "C" const char* nmb_noalloc_strerror(int code) {
     default: return "unknown error";
   }
 }
+
+// ---------------------------------------------------------------------------
+// Stand-alone pieces of the backward used with the tcgen05 dK/dV/dQ kernel
+// (attention_tc_bwd.cu): preparation (delta = rowsum(dO * O), zero the fp32 dQ
+// accumulator) and the final dQ conversion (with optional inverse RoPE).
+static BwdParams prep_params(const at::Tensor& o, const at::Tensor& dout, at::Tensor& delta,
+                             at::Tensor& dq_acc) {
+  BwdParams p{};
+  p.o = reinterpret_cast<const __nv_bfloat16*>(o.data_ptr());
+  p.dout = reinterpret_cast<const __nv_bfloat16*>(dout.data_ptr());
+  p.o_row = o.stride(1);
+  p.o_batch = o.stride(0);
+  p.do_row = dout.stride(1);
+  p.do_batch = dout.stride(0);
+  p.B = o.size(0);
+  p.Sq = o.size(1);
+  p.Hq = o.size(2);
+  p.delta = delta.data_ptr<float>();
+  p.dq_acc = dq_acc.data_ptr<float>();
+  return p;
+}
+
+void flash_attn_bwd_prep(at::Tensor o, at::Tensor dout, at::Tensor delta, at::Tensor dq_acc) {
+  const int64_t D = o.size(3);
+  TORCH_CHECK(D == 64 || D == 128);
+  check_rows(o, "o", D);
+  check_rows(dout, "dout", D);
+  BwdParams p = prep_params(o, dout, delta, dq_acc);
+  TORCH_CHECK(delta.numel() >= static_cast<int64_t>(p.B) * p.Hq * p.Sq);
+  TORCH_CHECK(dq_acc.numel() >= static_cast<int64_t>(p.B) * p.Hq * p.Sq * D);
+  if (p.B == 0 || p.Sq == 0) return;
+  const at::cuda::CUDAGuard guard(o.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int rows = p.B * p.Sq * p.Hq;
+  if (D == 64)
+    flash_bwd_pre_kernel<64><<<(rows + 7) / 8, 256, 0, stream>>>(p);
+  else
+    flash_bwd_pre_kernel<128><<<(rows + 7) / 8, 256, 0, stream>>>(p);
+  NMB_LAUNCHED(1);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void flash_attn_bwd_dq_convert(at::Tensor dq_acc, at::Tensor dq, c10::optional<at::Tensor> q_pos,
+                               c10::optional<at::Tensor> inv_freq) {
+  const int64_t D = dq.size(3);
+  TORCH_CHECK(D == 64 || D == 128);
+  check_rows(dq, "dq", D);
+  BwdParams p{};
+  p.dq_acc = dq_acc.data_ptr<float>();
+  p.dq = reinterpret_cast<__nv_bfloat16*>(dq.data_ptr());
+  p.dq_row = dq.stride(1);
+  p.dq_batch = dq.stride(0);
+  p.B = dq.size(0);
+  p.Sq = dq.size(1);
+  p.Hq = dq.size(2);
+  p.q_pos = q_pos.has_value() ? q_pos->data_ptr<int>() : nullptr;
+  p.inv_freq = inv_freq.has_value() ? inv_freq->data_ptr<float>() : nullptr;
+  TORCH_CHECK(p.q_pos == nullptr || p.inv_freq != nullptr);
+  if (p.B == 0 || p.Sq == 0) return;
+  const at::cuda::CUDAGuard guard(dq.device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const int64_t pairs = static_cast<int64_t>(p.B) * p.Sq * p.Hq * (D / 2);
+  if (D == 64)
+    flash_bwd_dq_kernel<64><<<(pairs + 255) / 256, 256, 0, stream>>>(p);
+  else
+    flash_bwd_dq_kernel<128><<<(pairs + 255) / 256, 256, 0, stream>>>(p);
+  NMB_LAUNCHED(1);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

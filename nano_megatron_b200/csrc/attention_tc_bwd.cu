@@ -1,0 +1,489 @@
+// Causal flash-attention backward on the 5th-generation tensor cores (tcgen05 + TMEM).
+//
+// One CTA per (128-key block, KV head, batch); it loops over the query heads of
+// its GQA group and over the 128-query blocks that can see its keys. Per query
+// block, with K, V resident in shared memory:
+//   MMA  : S^T = K Q^T and dP^T = V dO^T            -> TMEM cols [0,128) / [128,256)
+//   warps: each thread owns one key row; P^T = exp2(S^T*c - lse), dS^T =
+//          P^T (dP^T - delta) -> bf16 tiles in shared memory (UMMA SW128 layout)
+//   MMA  : dV += P^T dO ; dK += dS^T Q                -> TMEM (resident accumulators)
+//          dQ  = dS K                                  -> TMEM cols [0, D) (reuses S^T)
+//   warps: each thread owns one query row of dQ and adds it (x softmax scale)
+//          into the fp32 dQ accumulator in global memory with vector reductions.
+// At the end dK (x scale, inverse RoPE when positions are given) and dV are
+// written as bf16. The dQ accumulator is prepared (zeroed, delta = rowsum(dO*O))
+// and converted (with inverse RoPE) by the helper kernels of attention.cu.
+//
+// Operand layouts (all 128-byte swizzled, loaded by TMA): K/Q/dO/V tiles serve
+// as K-major operands for S^T / dP^T and as MN-major operands for dV / dK / dQ;
+// the P^T / dS^T tiles are K-major A for dV / dK and MN-major A for dQ.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace nmb {
+namespace fabw {
+
+constexpr int kBN = 128;  // keys per CTA
+constexpr int kBM = 128;  // queries per step
+constexpr int kThreads = 192;
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int D>
+struct Cfg {
+  static constexpr int kTile = 128 * D * 2;             // one 128-row bf16 tile
+  static constexpr int kPTile = kBN * kBM * 2;           // P^T or dS^T
+  static constexpr int kSmem = 4 * kTile + 2 * kPTile + 2 * kBM * 4 + 1024 + 256;
+  static constexpr int kTmemCols = 512;
+  // TMEM columns: S^T [0,128), dP^T [128,256), dQ reuses [0, D); dV [256, 256+D);
+  // dK [256+D, 256+2D).
+  static constexpr int kColS = 0, kColDP = 128, kColDQ = 0, kColDV = 256, kColDK = 256 + D;
+};
+
+struct Params {
+  const float* lse;     // [B, Hq, Sq] base 2
+  const float* delta;   // [B, Hq, Sq]
+  float* dq_acc;        // [B, Sq, Hq, D]
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  int64_t dk_row, dk_batch, dv_row, dv_batch;
+  int B, Hq, Hkv, Sq, Sk;
+  int q_offset, k_offset;
+  int causal;
+  float scale_log2, scale;
+  const int* k_pos;
+  const float* inv_freq;
+  int* status;
+};
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const void* desc, uint64_t* bar,
+                                            int32_t c0, int32_t c1, int32_t c2, int32_t c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
+}
+
+// Write a 128-value bf16 row (packed pairs) into a [128 rows x 128 cols] SW128 tile.
+__device__ __forceinline__ void store_row_sw128(uint8_t* tile, int row, const uint32_t* pk) {
+#pragma unroll
+  for (int ch = 0; ch < 16; ++ch) {
+    const int atom = ch >> 3, c8 = ch & 7;
+    uint8_t* dst = tile + atom * (128 * 128) + row * 128 + ((c8 ^ (row & 7)) << 4);
+    *reinterpret_cast<uint4*>(dst) = make_uint4(pk[ch * 4], pk[ch * 4 + 1], pk[ch * 4 + 2],
+                                                pk[ch * 4 + 3]);
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(kThreads, 1)
+    flash_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
+                        const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV,
+                        const __grid_constant__ CUtensorMap tmDO, const Params p) {
+  using C = Cfg<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + C::kTile;
+  uint8_t* sQ = sV + C::kTile;
+  uint8_t* sDO = sQ + C::kTile;
+  uint8_t* sP = sDO + C::kTile;
+  uint8_t* sDS = sP + C::kPTile;
+  float* sLse = reinterpret_cast<float*>(sDS + C::kPTile);
+  float* sDelta = sLse + kBM;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + kBM);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* qdo_full = bars + 1;
+  uint64_t* qdo_empty = bars + 2;
+  uint64_t* sdp_full = bars + 3;   // S^T and dP^T in TMEM
+  uint64_t* pds_full = bars + 4;   // P^T and dS^T in smem (4 warp arrivals)
+  uint64_t* mm_done = bars + 5;    // dV/dK/dQ MMAs of a step complete
+  uint64_t* dq_free = bars + 6;    // dQ drained from TMEM (4 warp arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int nb = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  const int group = p.Hq / p.Hkv;
+  const int n0 = nb * kBN;
+  const int warp = threadIdx.x / 32;
+  int m_begin = 0;
+  if (p.causal) m_begin = max(0, p.k_offset + n0 - p.q_offset) / kBM;
+  const int num_mb = (p.Sq + kBM - 1) / kBM;
+  const int steps_per_head = max(0, num_mb - m_begin);
+  const int total_steps = steps_per_head * group;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 7; ++i) mbar_init(&bars[i], (i == 4 || i == 6) ? 4 : 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (elect_one() && total_steps > 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * C::kTile);
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_4d(sK + c * 128 * 128, &tmK, kv_full, c * 64, kvh, n0, b);
+        tma_load_4d(sV + c * 128 * 128, &tmV, kv_full, c * 64, kvh, n0, b);
+      }
+      for (int t = 0; t < total_steps; ++t) {
+        const int h = kvh * group + t / steps_per_head;
+        const int m0 = (m_begin + t % steps_per_head) * kBM;
+        if (!mbar_wait(qdo_empty, (t & 1) ^ 1u, p.status, kStatusAttnTimeout, abort_flag)) break;
+        mbar_arrive_expect_tx(qdo_full, 2 * C::kTile);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_4d(sQ + c * 128 * 128, &tmQ, qdo_full, c * 64, h, m0, b);
+          tma_load_4d(sDO + c * 128 * 128, &tmDO, qdo_full, c * 64, h, m0, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (elect_one() && total_steps > 0) {
+      constexpr uint32_t id_s = umma_idesc_bf16(kBN, kBM, false, false);  // K-major A, B
+      constexpr uint32_t id_acc = umma_idesc_bf16(kBN, D, false, true);   // dV, dK
+      constexpr uint32_t id_dq = umma_idesc_bf16(kBM, D, true, true);     // dQ
+      bool ok = mbar_wait(kv_full, 0, p.status, kStatusAttnTimeout, abort_flag);
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ),
+                     aDO = smem_u32(sDO), aP = smem_u32(sP), aDS = smem_u32(sDS);
+      for (int t = 0; t < total_steps && ok; ++t) {
+        ok = mbar_wait(qdo_full, t & 1, p.status, kStatusAttnTimeout, abort_flag);
+        if (ok && t > 0) ok = mbar_wait(dq_free, (t - 1) & 1, p.status, kStatusAttnTimeout,
+                                        abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        // S^T = K Q^T ; dP^T = V dO^T   (M = keys, N = queries, K = D)
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+          umma_f16_ss(tmem + C::kColS, umma_desc_sw128(aK + off, 16, 1024),
+                      umma_desc_sw128(aQ + off, 16, 1024), id_s, kk > 0);
+          umma_f16_ss(tmem + C::kColDP, umma_desc_sw128(aV + off, 16, 1024),
+                      umma_desc_sw128(aDO + off, 16, 1024), id_s, kk > 0);
+        }
+        umma_commit(sdp_full);
+        ok = mbar_wait(pds_full, t & 1, p.status, kStatusAttnTimeout, abort_flag);
+        if (!ok) break;
+        tc_fence_after();
+        // dV += P^T dO ; dK += dS^T Q     (M = keys, N = D, K = queries)
+#pragma unroll
+        for (int kk = 0; kk < kBM / 16; ++kk) {
+          const uint32_t aoff = (kk >> 2) * (128 * 128) + (kk & 3) * 32;
+          const uint32_t boff = kk * 2048;
+          umma_f16_ss(tmem + C::kColDV, umma_desc_sw128(aP + aoff, 16, 1024),
+                      umma_desc_sw128(aDO + boff, 128 * 128, 1024), id_acc, (t | kk) != 0);
+          umma_f16_ss(tmem + C::kColDK, umma_desc_sw128(aDS + aoff, 16, 1024),
+                      umma_desc_sw128(aQ + boff, 128 * 128, 1024), id_acc, (t | kk) != 0);
+        }
+        // dQ = dS K   (M = queries (dS^T read MN-major), N = D, K = keys)
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk) {
+          const uint32_t off = kk * 2048;
+          umma_f16_ss(tmem + C::kColDQ, umma_desc_sw128(aDS + off, 128 * 128, 1024),
+                      umma_desc_sw128(aK + off, 128 * 128, 1024), id_dq, kk > 0);
+        }
+        umma_commit(mm_done);
+        umma_commit(qdo_empty);
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- softmax / dQ / epilogue
+    const int quarter = warp & 3;
+    const int lane = threadIdx.x & 31;
+    const int row = quarter * 32 + lane;  // TMEM lane: key row (S^T, dP^T, dV, dK) / query row (dQ)
+    const uint32_t lo = static_cast<uint32_t>(quarter * 32) << 16;
+    const int krow = n0 + row;
+    const int kpos = p.k_offset + krow;
+    bool ok = true;
+    for (int t = 0; t < total_steps; ++t) {
+      const int h = kvh * group + t / steps_per_head;
+      const int m0 = (m_begin + t % steps_per_head) * kBM;
+      // lse / delta of this query block (read by all 128 threads, one each)
+      {
+        const int64_t base = (static_cast<int64_t>(b) * p.Hq + h) * p.Sq;
+        const int q = m0 + row;
+        sLse[row] = q < p.Sq ? p.lse[base + q] : INFINITY;
+        sDelta[row] = q < p.Sq ? p.delta[base + q] : 0.f;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (ok) ok = mbar_wait(sdp_full, t & 1, p.status, kStatusAttnTimeout, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);  // keep TMEM ops warp-uniform
+      if (!ok) continue;  // keep joining the named barrier until the loop ends
+      tc_fence_after();
+      // previous step's MMAs must be done with the P^T / dS^T tiles
+      if (t > 0) {
+        ok = mbar_wait(mm_done, (t - 1) & 1, p.status, kStatusAttnTimeout, abort_flag);
+        ok = __all_sync(0xffffffffu, ok);  // keep TMEM ops warp-uniform
+      if (!ok) continue;  // keep joining the named barrier until the loop ends
+      }
+      const bool diag = p.causal && (p.k_offset + n0 + kBN - 1 > p.q_offset + m0);
+      const bool tail = (m0 + kBM > p.Sq) || (n0 + kBN > p.Sk);
+      uint32_t ppk[kBM / 2], dpk[kBM / 2];
+#pragma unroll
+      for (int c = 0; c < kBM / 32; ++c) {
+        uint32_t sr[32], dr[32];
+        tmem_ld_32x32b_x32(tmem + lo + C::kColS + c * 32, sr);
+        tmem_ld_32x32b_x32(tmem + lo + C::kColDP + c * 32, dr);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int qc = c * 32 + e + u;
+            float pr = ex2(__uint_as_float(sr[e + u]) * p.scale_log2 - sLse[qc]);
+            if ((diag || tail) &&
+                (m0 + qc >= p.Sq || krow >= p.Sk || (p.causal && kpos > p.q_offset + m0 + qc)))
+              pr = 0.f;
+            pv[u] = pr;
+            dsv[u] = pr * (__uint_as_float(dr[e + u]) - sDelta[qc]);
+          }
+          ppk[(c * 32 + e) / 2] = pack_bf16x2(pv[0], pv[1]);
+          dpk[(c * 32 + e) / 2] = pack_bf16x2(dsv[0], dsv[1]);
+        }
+      }
+      store_row_sw128(sP, row, ppk);
+      store_row_sw128(sDS, row, dpk);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(pds_full);
+      // drain dQ (thread = query row m0 + row)
+      ok = mbar_wait(mm_done, t & 1, p.status, kStatusAttnTimeout, abort_flag);
+      ok = __all_sync(0xffffffffu, ok);  // keep TMEM ops warp-uniform
+      if (!ok) continue;  // keep joining the named barrier until the loop ends
+      tc_fence_after();
+      const int q = m0 + row;
+      float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Sq + q) * p.Hq + h) * D;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tmem + lo + C::kColDQ + c * 32, r);
+        tmem_wait_ld();
+        if (q < p.Sq) {
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            red_add_v4(dst + c * 32 + e, __uint_as_float(r[e]) * p.scale,
+                       __uint_as_float(r[e + 1]) * p.scale, __uint_as_float(r[e + 2]) * p.scale,
+                       __uint_as_float(r[e + 3]) * p.scale);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+    }
+    // ---- epilogue: dK (scaled, inverse RoPE) and dV for this thread's key row
+    if (ok) {
+      const bool have = total_steps > 0;
+      if (have) tc_fence_after();
+      // TMEM loads are warp-collective: every lane loads, only valid rows store.
+      const bool row_ok = krow < p.Sk;
+      const int krc = row_ok ? krow : 0;
+      {
+        __nv_bfloat16* dkr = p.dk + b * p.dk_batch + static_cast<int64_t>(krc) * p.dk_row +
+                             static_cast<int64_t>(kvh) * D;
+        __nv_bfloat16* dvr = p.dv + b * p.dv_batch + static_cast<int64_t>(krc) * p.dv_row +
+                             static_cast<int64_t>(kvh) * D;
+        const float pos = p.k_pos != nullptr ? static_cast<float>(__ldg(p.k_pos + krc)) : 0.f;
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          uint32_t a[32], bb[32];
+          float x1[32], x2[32];
+          if (have) {
+            tmem_ld_32x32b_x32(tmem + lo + C::kColDK + c * 32, a);
+            tmem_ld_32x32b_x32(tmem + lo + C::kColDK + D / 2 + c * 32, bb);
+            tmem_wait_ld();
+          }
+#pragma unroll
+          for (int e = 0; e < 32; ++e) {
+            x1[e] = have ? __uint_as_float(a[e]) * p.scale : 0.f;
+            x2[e] = have ? __uint_as_float(bb[e]) * p.scale : 0.f;
+          }
+          if (p.k_pos != nullptr) {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) {
+              float sn, cs;
+              sincosf(pos * __ldg(p.inv_freq + c * 32 + e), &sn, &cs);
+              const float u = x1[e] * cs + x2[e] * sn;
+              const float w = x2[e] * cs - x1[e] * sn;
+              x1[e] = u;
+              x2[e] = w;
+            }
+          }
+#pragma unroll
+          for (int e = 0; e < 32 && row_ok; e += 8) {
+            *reinterpret_cast<uint4*>(dkr + c * 32 + e) =
+                make_uint4(pack_bf16x2(x1[e], x1[e + 1]), pack_bf16x2(x1[e + 2], x1[e + 3]),
+                           pack_bf16x2(x1[e + 4], x1[e + 5]), pack_bf16x2(x1[e + 6], x1[e + 7]));
+            *reinterpret_cast<uint4*>(dkr + D / 2 + c * 32 + e) =
+                make_uint4(pack_bf16x2(x2[e], x2[e + 1]), pack_bf16x2(x2[e + 2], x2[e + 3]),
+                           pack_bf16x2(x2[e + 4], x2[e + 5]), pack_bf16x2(x2[e + 6], x2[e + 7]));
+          }
+        }
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t r[32];
+          if (have) {
+            tmem_ld_32x32b_x32(tmem + lo + C::kColDV + c * 32, r);
+            tmem_wait_ld();
+          }
+#pragma unroll
+          for (int e = 0; e < 32 && row_ok; e += 8) {
+            float f[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u) f[u] = have ? __uint_as_float(r[e + u]) : 0.f;
+            *reinterpret_cast<uint4*>(dvr + c * 32 + e) =
+                make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                           pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::kTmemCols);
+  }
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &ptr, 12000,
+                                                     cudaEnableDefault, &q);
+    TORCH_CHECK(e == cudaSuccess && q == cudaDriverEntryPointSuccess && ptr != nullptr,
+                "cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+static CUtensorMap make_map(const at::Tensor& t) {
+  CUtensorMap m;
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(t.size(3)), static_cast<cuuint64_t>(t.size(2)),
+                        static_cast<cuuint64_t>(t.size(1)), static_cast<cuuint64_t>(t.size(0))};
+  cuuint64_t strides[3] = {static_cast<cuuint64_t>(t.stride(2) * 2),
+                           static_cast<cuuint64_t>(t.stride(1) * 2),
+                           static_cast<cuuint64_t>(t.stride(0) * 2)};
+  cuuint32_t box[4] = {64u, 1u, 128u, 1u};
+  cuuint32_t estr[4] = {1u, 1u, 1u, 1u};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, t.data_ptr(), dims, strides,
+                           box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "flash_attn_bwd_tc: tensor map encode failed (", (int)r, ")");
+  return m;
+}
+
+}  // namespace fabw
+}  // namespace nmb
+
+using namespace nmb;
+using namespace nmb::fabw;
+
+// dK / dV of the causal attention (tcgen05). `delta` (rowsum(dO*O)) and the
+// zeroed fp32 `dq_acc` must be prepared by the caller (flash_attn_bwd_prep).
+void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor dout,
+                          at::Tensor lse, at::Tensor delta, at::Tensor dq_acc, at::Tensor dk,
+                          at::Tensor dv, double softmax_scale, bool causal, int64_t q_offset,
+                          int64_t k_offset, c10::optional<at::Tensor> k_pos,
+                          c10::optional<at::Tensor> inv_freq, at::Tensor status) {
+  const int64_t D = q.size(3);
+  TORCH_CHECK(D == 64 || D == 128, "flash_attn_bwd_tc: head_dim must be 64 or 128");
+  for (const at::Tensor* t : {&q, &k, &v, &dout, &dk, &dv}) {
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kBFloat16 && t->dim() == 4);
+    TORCH_CHECK(t->stride(3) == 1 && t->stride(2) == D, "heads must be contiguous [.., H, D]");
+    TORCH_CHECK(t->stride(1) % 8 == 0 && t->stride(0) % 8 == 0, "strides must be 16-byte");
+    TORCH_CHECK(reinterpret_cast<uintptr_t>(t->data_ptr()) % 16 == 0, "16-byte alignment");
+  }
+  Params p{};
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.dq_acc = dq_acc.data_ptr<float>();
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  p.dk_row = dk.stride(1);
+  p.dk_batch = dk.stride(0);
+  p.dv_row = dv.stride(1);
+  p.dv_batch = dv.stride(0);
+  p.B = q.size(0);
+  p.Sq = q.size(1);
+  p.Hq = q.size(2);
+  p.Sk = k.size(1);
+  p.Hkv = k.size(2);
+  p.q_offset = q_offset;
+  p.k_offset = k_offset;
+  p.causal = causal ? 1 : 0;
+  p.scale = static_cast<float>(softmax_scale);
+  p.scale_log2 = static_cast<float>(softmax_scale) * kLog2e;
+  p.k_pos = k_pos.has_value() ? k_pos->data_ptr<int>() : nullptr;
+  p.inv_freq = inv_freq.has_value() ? inv_freq->data_ptr<float>() : nullptr;
+  TORCH_CHECK(p.k_pos == nullptr || p.inv_freq != nullptr);
+  p.status = status.data_ptr<int>();
+  if (p.B == 0 || p.Sk == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  ensure_current_context(q.device().index());
+  CUtensorMap mq = make_map(q), mk = make_map(k), mv = make_map(v), mdo = make_map(dout);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  dim3 grid((p.Sk + kBN - 1) / kBN, p.Hkv, p.B);
+  if (D == 64) {
+    static bool set = false;
+    if (!set) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_tc_kernel<64>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          Cfg<64>::kSmem));
+      set = true;
+    }
+    flash_bwd_tc_kernel<64><<<grid, kThreads, Cfg<64>::kSmem, stream>>>(mq, mk, mv, mdo, p);
+  } else {
+    static bool set = false;
+    if (!set) {
+      C10_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_tc_kernel<128>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          Cfg<128>::kSmem));
+      set = true;
+    }
+    flash_bwd_tc_kernel<128><<<grid, kThreads, Cfg<128>::kSmem, stream>>>(mq, mk, mv, mdo, p);
+  }
+  NMB_LAUNCHED(1);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}

@@ -16,6 +16,17 @@ void flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::
                     at::Tensor delta_ws, at::Tensor dq_acc_ws, double softmax_scale, bool causal,
                     int64_t q_offset, int64_t k_offset, c10::optional<at::Tensor> q_pos,
                     c10::optional<at::Tensor> k_pos, c10::optional<at::Tensor> inv_freq);
+void flash_attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
+                       double softmax_scale, bool causal, int64_t q_offset, int64_t k_offset,
+                       at::Tensor status);
+void flash_attn_bwd_prep(at::Tensor o, at::Tensor dout, at::Tensor delta, at::Tensor dq_acc);
+void flash_attn_bwd_dq_convert(at::Tensor dq_acc, at::Tensor dq, c10::optional<at::Tensor> q_pos,
+                               c10::optional<at::Tensor> inv_freq);
+void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor dout,
+                          at::Tensor lse, at::Tensor delta, at::Tensor dq_acc, at::Tensor dk,
+                          at::Tensor dv, double softmax_scale, bool causal, int64_t q_offset,
+                          int64_t k_offset, c10::optional<at::Tensor> k_pos,
+                          c10::optional<at::Tensor> inv_freq, at::Tensor status);
 void rmsnorm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps);
 void rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, at::Tensor rstd, at::Tensor dx,
                  c10::optional<at::Tensor> dw, c10::optional<at::Tensor> dres);
@@ -41,6 +52,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_tc", &gemm_tc, "tcgen05 GEMM with fused epilogues");
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
+  m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc, "tcgen05/TMEM causal flash attention forward");
+  m.def("flash_attn_bwd_prep", &flash_attn_bwd_prep);
+  m.def("flash_attn_bwd_dq_convert", &flash_attn_bwd_dq_convert);
+  m.def("flash_attn_bwd_tc_kv", &flash_attn_bwd_tc_kv, "tcgen05/TMEM attention backward (dK, dV, dQ acc)");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("swiglu_fwd", &swiglu_fwd);

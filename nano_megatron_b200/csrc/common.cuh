@@ -19,6 +19,15 @@
 namespace nmb {
 
 
+// Make the device's primary context current on the calling host thread.
+// Driver-API calls such as cuTensorMapEncodeTiled crash in a thread that has no
+// current context yet (e.g. an autograd worker whose first CUDA call is ours,
+// since device guards skip cudaSetDevice when the index already matches).
+inline void ensure_current_context(int device) {
+  CUcontext ctx = nullptr;
+  if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS || ctx == nullptr) cudaSetDevice(device);
+}
+
 // ---------------------------------------------------------------- status word
 // Error codes written into the device status word (first writer wins).
 enum StatusCode : int {

@@ -539,6 +539,7 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
   if (M == 0 || N == 0) return;
 
   const at::cuda::CUDAGuard guard(a.device());
+  ensure_current_context(a.device().index());
   // Tensor maps. A: K-major -> [M, K] with box 128 rows; MN-major -> [K, M] box 64 rows.
   CUtensorMap ta = a_mn ? make_tmap_2d(a.data_ptr(), K, M, a.stride(0), kBK)
                         : make_tmap_2d(a.data_ptr(), M, K, a.stride(0), kBM);

@@ -15,6 +15,7 @@ import math
 
 import torch
 
+from . import functional as F
 from . import gemm as G
 from ._ext import lib
 
@@ -63,11 +64,16 @@ def attn_cases(iters: int) -> dict:
         fl = 4 * b * h * s * s * d / 2
         tag = f"{b}x{s}x{h}/{hkv}x{d}"
         res[f"attn_fwd_{tag}"] = fl / _time(
+            lambda: F.flash_fwd(q, k, v, o, lse, sc, True), iters) / 1e9
+        res[f"attn_fwd_mma_{tag}"] = fl / _time(
             lambda: lib().flash_attn_fwd(q, k, v, o, lse, sc, True, 0, 0), iters) / 1e9
         dqkv = torch.empty_like(qkv)
         delta = torch.empty(b * h * s, device="cuda")
         acc = torch.empty(b * s * h * d, device="cuda")
         res[f"attn_bwd_{tag}"] = 2.5 * fl / _time(
+            lambda: F.attention_bwd(q, k, v, o, o, lse, dqkv[:, :, :h], dqkv[:, :, h:h + hkv],
+                                    dqkv[:, :, h + hkv:], causal=True), iters) / 1e9
+        res[f"attn_bwd_mma_{tag}"] = 2.5 * fl / _time(
             lambda: lib().flash_attn_bwd(q, k, v, o, o, lse, dqkv[:, :, :h],
                                          dqkv[:, :, h:h + hkv], dqkv[:, :, h + hkv:], delta, acc,
                                          sc, True, 0, 0, None, None, None), iters) / 1e9
@@ -107,8 +113,7 @@ def main() -> None:
         o = torch.empty(b, s, h, d, device="cuda", dtype=torch.bfloat16)
         lse = torch.empty(b, h, s, device="cuda")
         for _ in range(3):
-            lib().flash_attn_fwd(qkv[:, :, :h], qkv[:, :, h:2 * h], qkv[:, :, 2 * h:], o, lse,
-                                 0.125, True, 0, 0)
+            F.flash_fwd(qkv[:, :, :h], qkv[:, :, h:2 * h], qkv[:, :, 2 * h:], o, lse, 0.125, True)
         torch.cuda.synchronize()
         return
     out = {}

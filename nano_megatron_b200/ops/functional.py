@@ -255,6 +255,15 @@ def ce_finish(logits: torch.Tensor, labels: torch.Tensor, vstart: int, all_stats
 
 
 # ------------------------------------------------------------------ attention
+def flash_fwd(q, k, v, o, lse, scale: float, causal: bool, q_offset: int = 0,
+              k_offset: int = 0) -> None:
+    """tcgen05/TMEM flash-attention forward into ``o`` ([B,S,H,D] view) and ``lse``."""
+    from ._ext import status_word
+
+    lib().flash_attn_fwd_tc(q, k, v, o, lse, scale, causal, q_offset, k_offset,
+                            status_word(q.device))
+
+
 def attention_fwd(q, k, v, *, causal: bool, q_offset: int = 0, k_offset: int = 0,
                   softmax_scale: float | None = None):
     """q [B,Sq,Hq,D], k/v [B,Sk,Hkv,D] (strided views). Returns (o [B,Sq,Hq,D], lse).
@@ -265,7 +274,7 @@ def attention_fwd(q, k, v, *, causal: bool, q_offset: int = 0, k_offset: int = 0
     if _cuda(q):
         o = torch.empty(B, Sq, Hq, D, device=q.device, dtype=q.dtype)
         lse = torch.empty(B, Hq, Sq, device=q.device, dtype=torch.float32)
-        lib().flash_attn_fwd(q, k, v, o, lse, scale, causal, q_offset, k_offset)
+        flash_fwd(q, k, v, o, lse, scale, causal, q_offset, k_offset)
         return o, lse
     o, lse = _attn_math(q, k, v, causal, q_offset, k_offset, scale)
     return o.to(q.dtype), lse
@@ -299,8 +308,13 @@ def attention_bwd(q, k, v, o, do, lse, dq, dk, dv, *, causal: bool, q_offset: in
     if _cuda(q):
         delta = torch.empty(B * Hq * Sq, device=q.device, dtype=torch.float32)
         dq_acc = torch.empty(B * Sq * Hq * D, device=q.device, dtype=torch.float32)
-        lib().flash_attn_bwd(q, k, v, o, do, lse, dq, dk, dv, delta, dq_acc, scale, causal,
-                             q_offset, k_offset, q_pos, k_pos, inv_freq)
+        from ._ext import status_word
+
+        L = lib()
+        L.flash_attn_bwd_prep(o, do, delta, dq_acc)
+        L.flash_attn_bwd_tc_kv(q, k, v, do, lse, delta, dq_acc, dk, dv, scale, causal,
+                               q_offset, k_offset, k_pos, inv_freq, status_word(q.device))
+        L.flash_attn_bwd_dq_convert(dq_acc, dq, q_pos, inv_freq)
         return
     # Explicit flash-attention backward using the given (global) log-sum-exp, so a
     # partial key block (ring attention) gets its share of the global softmax.

@@ -15,11 +15,15 @@ gradient-synchronising one, tied-embedding hooks around the step.
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from ..p2p import P2PCommunicator
 from .base import LossAccumulator, batch_labels, extract_loss
 from .plans import build_1f1b_plan, build_gpipe_plan, build_interleaved_plan, validate_plan
+
+_DEBUG = os.environ.get("NMB_PP_DEBUG", "0") == "1"
 
 
 class PipelineScheduleExecutor:
@@ -87,6 +91,8 @@ class PipelineScheduleExecutor:
                   for c in range(self.chunks)} if not forward_only else {}
         pending = None  # (action index, (work, buffer)) of a pre-posted receive
         for i, a in enumerate(plan):
+            if _DEBUG:
+                print(f"[pp rank {self.parallel.rank} stage {self.rank}] {a}", flush=True)
             if self._needs_recv(a):
                 if pending is not None and pending[0] == i:
                     work, buf = pending[1]

@@ -120,14 +120,19 @@ def _attn_ref(q, k, v, causal=True, q_off=0, k_off=0):
 
 @pytest.mark.parametrize("d,hq,hkv,s,b", [(64, 4, 4, 512, 2), (128, 8, 2, 300, 1),
                                           (64, 2, 1, 1024, 1), (128, 4, 4, 128, 3)])
-def test_flash_attention_fwd_bwd(d, hq, hkv, s, b):
+@pytest.mark.parametrize("fwd", ["tcgen05", "mma"])
+def test_flash_attention_fwd_bwd(d, hq, hkv, s, b, fwd):
     torch.manual_seed(5)
     qkv = torch.randn(b, s, hq + 2 * hkv, d, device=DEV).bfloat16()
     q, k, v = qkv[:, :, :hq], qkv[:, :, hq:hq + hkv], qkv[:, :, hq + hkv:]
     o = torch.empty(b, s, hq, d, device=DEV, dtype=torch.bfloat16)
     lse = torch.empty(b, hq, s, device=DEV)
     scale = 1.0 / math.sqrt(d)
-    lib().flash_attn_fwd(q, k, v, o, lse, scale, True, 0, 0)
+    if fwd == "tcgen05":
+        lib().flash_attn_fwd_tc(q, k, v, o, lse, scale, True, 0, 0,
+                                status_word(torch.device(DEV)))
+    else:
+        lib().flash_attn_fwd(q, k, v, o, lse, scale, True, 0, 0)
     qr = q.detach().float().requires_grad_()
     kr = k.detach().float().requires_grad_()
     vr = v.detach().float().requires_grad_()
@@ -155,10 +160,15 @@ def test_flash_attention_offsets_noncausal():
     v = torch.randn(b, sk, hkv, d, device=DEV).bfloat16()
     o = torch.empty_like(q)
     lse = torch.empty(b, hq, s, device=DEV)
-    lib().flash_attn_fwd(q, k, v, o, lse, 1 / 8.0, True, 256, 0)
-    assert _rel(o, _attn_ref(q, k, v, True, 256, 0)) < 1e-2
-    lib().flash_attn_fwd(q, k, v, o, lse, 1 / 8.0, False, 0, 0)
-    assert _rel(o, _attn_ref(q, k, v, False)) < 1e-2
+    st = status_word(torch.device(DEV))
+    for fn in (lambda *a: lib().flash_attn_fwd(*a), lambda *a: lib().flash_attn_fwd_tc(*a, st)):
+        fn(q, k, v, o, lse, 1 / 8.0, True, 256, 0)
+        assert _rel(o, _attn_ref(q, k, v, True, 256, 0)) < 1e-2
+        fn(q, k, v, o, lse, 1 / 8.0, False, 0, 0)
+        assert _rel(o, _attn_ref(q, k, v, False)) < 1e-2
+        fn(q, k, v, o, lse, 1 / 8.0, True, 0, 300)  # keys beyond every query: empty rows
+        assert o.float().abs().max().item() == 0.0
+    assert int(st.item()) == 0
 
 
 @pytest.mark.parametrize("h", [256, 1024, 2048, 4096])
