@@ -47,25 +47,33 @@ class P2PCommunicator:
         return self.pp.ranks[pp_index % self.pp.size]
 
     # primitives -------------------------------------------------------------
+    # Every point-to-point op goes through batch_isend_irecv: batched P2P runs on the
+    # group's (already initialised) communicator, whereas an unbatched send/recv makes
+    # torch create a fresh 2-rank communicator lazily -- and creating one while a
+    # pre-posted receive kernel spins on the peer's GPU deadlocks both ranks.
+    @staticmethod
+    def _op(fn, t: torch.Tensor, peer: int, group):
+        return dist.batch_isend_irecv([dist.P2POp(fn, t, peer, group=group.process_group)])[0]
+
     def _isend(self, t: torch.Tensor, dst: int, group) -> None:
         t = t.contiguous()
         if self.dynamic:
             hdr = torch.zeros(HEADER_LEN, dtype=torch.int64, device=t.device)
             hdr[0], hdr[1] = HEADER_VERSION, t.ndim
             hdr[2:2 + t.ndim] = torch.tensor(t.shape, dtype=torch.int64)
-            self._sends.append((dist.isend(hdr, dst, group=group.process_group), hdr))
-        self._sends.append((dist.isend(t, dst, group=group.process_group), t))
+            self._sends.append((self._op(dist.isend, hdr, dst, group), hdr))
+        self._sends.append((self._op(dist.isend, t, dst, group), t))
 
     def _irecv(self, shape, src: int, group):
         if self.dynamic:
             hdr = torch.empty(HEADER_LEN, dtype=torch.int64, device=self.device)
-            dist.recv(hdr, src, group=group.process_group)
+            self._op(dist.irecv, hdr, src, group).wait()
             if int(hdr[0]) != HEADER_VERSION:
                 raise RuntimeError("pipeline header version mismatch")
             nd = int(hdr[1])
             shape = tuple(int(x) for x in hdr[2:2 + nd].tolist())
         buf = torch.empty(shape, dtype=self.dtype, device=self.device)
-        work = dist.irecv(buf, src, group=group.process_group)
+        work = self._op(dist.irecv, buf, src, group)
         return work, buf
 
     def send_activation(self, t: torch.Tensor, dst_pp: int) -> None:
@@ -86,8 +94,28 @@ class P2PCommunicator:
             work.wait()
 
     def warmup(self) -> None:
-        """Create the communicators in a fixed order on every rank (1-element all-reduce)."""
-        for g in (self.pp, self.grad_group):
-            if g.size > 1 and g.process_group is not None:
+        """Initialise every multi-rank communicator this rank uses, in one fixed order on
+        all ranks, before the first pipeline transfer (a 1-element all-reduce each): the
+        TP/CP/EP/DP/replica groups first, then the two pipeline channels. No lazy
+        communicator creation can then happen while a receive is outstanding."""
+        from nano_megatron_b200.parallel.group_plan import GroupKey
+
+        keys = (GroupKey.TP, GroupKey.CP, GroupKey.EP, GroupKey.DP_AXIS, GroupKey.TP_CP,
+                GroupKey.TP_EP, GroupKey.DENSE_REPLICA, GroupKey.EXPERT_REPLICA,
+                GroupKey.BATCH_REPLICA, GroupKey.EMBEDDING)
+        groups = []
+        for k in keys:
+            try:
+                groups.append(self.parallel.group(k))
+            except KeyError:
+                continue
+        groups += [self.pp, self.grad_group]
+        seen = set()
+        for g in groups:
+            pg = g.process_group
+            if g.size > 1 and pg is not None and id(pg) not in seen:
+                seen.add(id(pg))
                 t = torch.zeros(1, device=self.device)
-                dist.all_reduce(t, group=g.process_group)
+                dist.all_reduce(t, group=pg)
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)

@@ -5,9 +5,9 @@ the previous *logical* stage (pp_rank - 1 of the same chunk, or the last rank's
 previous chunk when wrapping around under interleaving), runs the stage and
 sends its output to the next logical stage; a backward receives the output
 gradient from the next logical stage (the last logical stage starts from its
-loss), runs autograd and sends the input gradient back. The receive an action
-needs is posted as soon as the previous action that produced work finished
-(``overlap_p2p``) so it overlaps the current compute. Semantics follow the
+loss), runs autograd and sends the input gradient back. Sends are
+asynchronous (a bounded number stay in flight, overlapping the next compute);
+receives are posted right before the action that needs them. Semantics follow the
 reference executor (src/nano_megatron/pipeline_parallel/schedules/executor.py:
 270-587): loss scaled by 1/M, the last backward of each chunk marked as the
 gradient-synchronising one, tied-embedding hooks around the step.
@@ -101,10 +101,13 @@ class PipelineScheduleExecutor:
                 work.wait()
             else:
                 buf = None
+            # Receives are posted right before the action that consumes them, never
+            # ahead of compute: a receive kernel left spinning on the GPU while this
+            # host blocks on an implicit device synchronisation (first-use kernel
+            # loading, allocator growth) can deadlock against a peer that is itself
+            # blocked setting up the matching NCCL connection. Sends stay
+            # asynchronous, which is what overlaps transfers with compute.
             pending = None
-            # post the next receive early so it overlaps this action's compute
-            if self.overlap and i + 1 < len(plan) and self._needs_recv(plan[i + 1]):
-                pending = (i + 1, self._post(plan[i + 1]))
             if a.kind == "F":
                 self._forward(a, buf, microbatches, m, acc, records, forward_only, last_b, plan)
             else:
