@@ -233,8 +233,12 @@ class Trainer:
         self.state.data_fingerprint = data_fingerprint
         restore = getattr(data, "load_state_dict", None)
         if callable(restore) and self.state.step > 0:
-            restore({"epoch": self.state.data_epoch, "seed": self.state.data_shuffle_seed,
-                     "sample_offset": self.state.data_sample_offset})
+            st = {"epoch": self.state.data_epoch, "sample_offset": self.state.data_sample_offset}
+            if self.state.data_shuffle_seed is not None:
+                st["shuffle_seed"] = self.state.data_shuffle_seed
+            if self.state.data_samples_per_epoch is not None:
+                st["samples_per_epoch"] = self.state.data_samples_per_epoch
+            restore(st)
         self._data = data
         self.data_iterator = iter(data)
 
@@ -247,7 +251,7 @@ class Trainer:
         if callable(get):
             st = get()
             self.state.data_epoch = int(st.get("epoch", 0))
-            self.state.data_shuffle_seed = st.get("seed")
+            self.state.data_shuffle_seed = st.get("shuffle_seed", st.get("seed"))
             self.state.data_sample_offset = int(st.get("sample_offset", 0))
             self.state.data_samples_per_epoch = st.get("samples_per_epoch")
 

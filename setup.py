@@ -3,7 +3,7 @@
 from pathlib import Path
 
 from setuptools import find_packages, setup
-from torch.utils.cpp_extension import BuildExtension, CUDAExtension
+from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
 
 ROOT = Path(__file__).resolve().parent
 CSRC = ROOT / "nano_megatron_b200" / "csrc"
@@ -31,11 +31,22 @@ def extension() -> CUDAExtension:
     )
 
 
+def host_extension() -> CppExtension:
+    """Host-only runtime (data loading); no CUDA dependency, so it imports on CPU hosts."""
+    sources = sorted(str(p.relative_to(ROOT)) for p in (CSRC / "host").glob("*.cpp"))
+    return CppExtension(
+        name="nano_megatron_b200._native",
+        sources=sources,
+        extra_compile_args={"cxx": ["-O3", "-std=c++17", "-pthread"]},
+        extra_link_args=["-pthread"],
+    )
+
+
 setup(
     name="nano-megatron-b200",
     version="0.1.0",
     packages=find_packages(include=["nano_megatron_b200", "nano_megatron_b200.*"]),
-    ext_modules=[extension()],
+    ext_modules=[extension(), host_extension()],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
     entry_points={
         "console_scripts": [
