@@ -454,6 +454,10 @@ def portable_run_config(run_config):
         sec = d.get(section)
         if isinstance(sec, dict) and sec.get(name, default) == default:
             sec.pop(name, None)
+    # kernels.backend "b200" names this framework's kernel set; the reference's schema
+    # knows only "torch", its own default kernels, which is what a reader should use.
+    if isinstance(d.get("kernels"), dict) and d["kernels"].get("backend") == "b200":
+        d["kernels"]["backend"] = "torch"
     return d
 
 

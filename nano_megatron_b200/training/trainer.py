@@ -15,6 +15,7 @@ from __future__ import annotations
 
 import math
 import time
+from pathlib import Path
 from dataclasses import dataclass, field
 from typing import Any
 
@@ -144,6 +145,16 @@ class Trainer:
         self.last_step_ms: float | None = None
         self.metrics_path = metrics_path
         self.resume_metrics_path = resume_metrics_path
+        from .wandb_logger import WandbLogger
+
+        self.logger = WandbLogger(getattr(config, "wandb", None), run_config=config,
+                                  is_primary=parallel.rank == 0,
+                                  metrics_path=None if metrics_path is None else Path(metrics_path),
+                                  resume_metrics_path=None if resume_metrics_path is None
+                                  else Path(resume_metrics_path))
+        self._restored_step: int | None = None
+        self._restored_run_id: str | None = None
+        self._restored_history = None
         self.validation_data = None
         self._hooks: list = []
 
@@ -255,12 +266,27 @@ class Trainer:
             self.state.data_sample_offset = int(st.get("sample_offset", 0))
             self.state.data_samples_per_epoch = st.get("samples_per_epoch")
 
+    def start_logging(self) -> None:
+        """Open the metric history (replaying a resumed checkpoint's prefix) and W&B."""
+        rid = self.logger.start(checkpoint_run_id=self._restored_run_id,
+                                checkpoint_step=self._restored_step,
+                                checkpoint_metrics_state=self._restored_history, model=self.model)
+        self.state.wandb_run_id = rid
+
     def fit(self, *, max_steps: int | None = None, log=print) -> TrainerState:
+        """Train to ``max_steps``: log every ``log_interval`` steps, validate every
+        ``validation.interval`` steps (saving and pinning an improved checkpoint), save every
+        ``checkpoint.save_interval`` steps and once more at the end (``save_final``).
+        Order of events per step follows the reference trainer
+        (src/nano_megatron/training/trainer.py:580-700)."""
+        self.start_logging()
         target = max_steps if max_steps is not None else self.config.training.max_steps
         interval = self.config.training.log_interval
         pending: list = []
         t0 = time.perf_counter()
         device_ms = 0.0
+        first_step = self.state.step
+        self._last_saved = None
         while self.state.step < target:
             batch = next(self.data_iterator) if self.batch_router.is_source else None
             out, ms = self.timed_train_step(batch)
@@ -270,23 +296,28 @@ class Trainer:
             if self.state.step % interval == 0 or self.state.step == target:
                 self._log(pending, time.perf_counter() - t0, device_ms, log)
                 pending, device_ms, t0 = [], 0.0, time.perf_counter()
-            self._after_step()
+            self._after_step(log)
+        ck = self.config.checkpoint
+        if self.checkpoint is not None and ck.save_final and self.state.step > first_step and \
+                self._last_saved != self.state.step:
+            self.save_checkpoint()
         self.flush()
         return self.state
 
-    def _after_step(self) -> None:
+    def _after_step(self, log=print) -> None:
         for hook in self._hooks:
             hook(self)
+        vc = self.config.validation
+        if self.validation_data is not None and vc.interval and self.state.step % vc.interval == 0:
+            self.run_validation(log)
         cp = self.checkpoint
         if cp is not None:
             iv = self.config.checkpoint.save_interval
-            if iv and self.state.step % iv == 0:
+            if iv and self.state.step % iv == 0 and \
+                    getattr(self, "_last_saved", None) != self.state.step:
                 self.save_checkpoint()
-        vc = self.config.validation
-        if self.validation_data is not None and vc.interval and self.state.step % vc.interval == 0:
-            self.run_validation()
 
-    def run_validation(self) -> dict[str, float]:
+    def run_validation(self, log=print) -> dict[str, float]:
         batches = []
         it = iter(self.validation_data)
         for _ in range(self.config.validation.batches):
@@ -295,13 +326,26 @@ class Trainer:
             except StopIteration:
                 break
         metrics = self.evaluate(batches)
+        if self.parallel.rank == 0 and log is not None:
+            log("validation " + " ".join(f"{k}={v:.6g}" for k, v in metrics.items()))
+        self.logger.log("validation", metrics, state=self.state)
         best = self.state.best_validation_loss
         if best is None or metrics["loss"] < best:
-            self.state.best_validation_loss = metrics["loss"]
+            self.state.best_validation_loss = float(metrics["loss"])
             self.state.best_validation_step = self.state.step
             if self.checkpoint is not None and self.config.checkpoint.save_best_validation:
+                self.state.best_validation_checkpoint = str(
+                    Path(self.checkpoint.directory) / f"step_{self.state.step:08d}")
                 path = self.save_checkpoint()
-                self.state.best_validation_checkpoint = str(path) if path else None
+                pinned = self.checkpoint.pin_best_validation(self.state.step,
+                                                             self.state.best_validation_loss)
+                if Path(pinned) != Path(path):
+                    raise RuntimeError("best-validation pin returned a different checkpoint "
+                                       "path")
+                self.logger.update_summary({"checkpoint/best_validation": str(path),
+                                            "checkpoint/best_validation_loss":
+                                                self.state.best_validation_loss,
+                                            "checkpoint/best_validation_step": self.state.step})
         return metrics
 
     def _log(self, pending, host_s, device_ms, log) -> None:
@@ -332,22 +376,29 @@ class Trainer:
         if self.parallel.rank == 0 and log is not None:
             log(" ".join(f"{k}={v:.6g}" if isinstance(v, float) else f"{k}={v}"
                          for k, v in metrics.items()))
-        history = getattr(self, "metric_history", None)
-        if history is not None:
-            history.append(metrics, trainer_state=self.state.state_dict())
+        self.logger.log("train", {k: float(v) for k, v in metrics.items() if k != "step"},
+                        state=self.state)
 
     # ------------------------------------------------------------------ checkpoints
     def save_checkpoint(self):
         if self.checkpoint is None:
             return None
-        return self.checkpoint.save(step=self.state.step, model=self.model,
+        self.state.metrics_history = self.logger.history_state()
+        path = self.checkpoint.save(step=self.state.step, model=self.model,
                                     data_parallel=self.data_parallel,
                                     trainer_state=self.state.state_dict(), rng=self.rng)
+        self._last_saved = self.state.step
+        self.logger.update_summary({"checkpoint/latest": str(path),
+                                    "checkpoint/step": self.state.step})
+        return path
 
     def load_checkpoint(self, path) -> None:
         loaded = self.checkpoint.load(path, model=self.model, data_parallel=self.data_parallel,
                                       rng=self.rng)
         self.state.load_state_dict(loaded["trainer_state"])
+        self._restored_step = self.state.step
+        self._restored_run_id = self.state.wandb_run_id
+        self._restored_history = self.state.metrics_history
         if self.state.lr_scheduler is not None:
             self.lr_scheduler.load_state_dict(self.state.lr_scheduler,
                                               expected_completed_steps=self.state.step)
@@ -359,4 +410,10 @@ class Trainer:
             self.checkpoint.flush()
 
     def close(self) -> None:
-        self.flush()
+        try:
+            self.flush()
+        finally:
+            self.logger.finish()
+            close = getattr(getattr(self, "_data", None), "close", None)
+            if callable(close):
+                close()

@@ -54,6 +54,8 @@ setup(
             "nano-megatron-export=nano_megatron_b200.cli.export:main",
             "nano-megatron-generate=nano_megatron_b200.cli.generate:main",
             "nano-megatron-tokenizer=nano_megatron_b200.cli.tokenizer:main",
+            "nano-megatron-tinystories=nano_megatron_b200.cli.tinystories:main",
+            "nano-megatron-validate-nccl=nano_megatron_b200.distributed.validate_nccl:main",
         ]
     },
 )
