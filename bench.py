@@ -195,7 +195,10 @@ def run_ours(args, rank, world, local):
     from nano_megatron_b200.training import Trainer
     from nano_megatron_b200.training.engine import build_training_components
 
-    cfg = config_from_dict(make_config_dict(args.gpus, args.steps + args.warmup))
+    d = make_config_dict(args.gpus, args.steps + args.warmup)
+    d["kernels"] = {"backend": "b200", "fused_tp_comm": not args.no_fused_tp,
+                    "cuda_graphs": not args.no_cuda_graphs}
+    cfg = config_from_dict(d)
     runtime = DistributedRuntime(cfg.distributed).initialize()
     comps = build_training_components(cfg, runtime)
     device = runtime.device
@@ -311,6 +314,12 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-fused-tp", action="store_true",
+                    help="diagnostic: NCCL all-gather/reduce-scatter instead of the fused "
+                         "NVLink AG->GEMM / GEMM->RS kernels")
+    ap.add_argument("--no-cuda-graphs", action="store_true",
+                    help="diagnostic: launch every kernel from Python instead of replaying one "
+                         "CUDA graph per microbatch")
     args = ap.parse_args()
     rank, world, local = dist_env()
     if world != args.gpus:

@@ -439,7 +439,8 @@ class CheckpointManager:
 # Config fields this framework adds to the reference's schema, with their defaults.
 # They are left out of the manifest's run_config while at the default, so that the
 # reference's own config loader (which rejects unknown fields) can read the manifest.
-_EXTENSION_FIELDS = {("kernels", "cuda_graphs"): True, ("context_parallel", "load_balance"): False}
+_EXTENSION_FIELDS = {("kernels", "cuda_graphs"): True, ("kernels", "fused_tp_comm"): True,
+                     ("context_parallel", "load_balance"): False}
 
 
 def portable_run_config(run_config):

@@ -246,10 +246,14 @@ class PrecisionConfig:
 class KernelConfig:
     backend: KernelBackend = KernelBackend.TORCH
     cuda_graphs: bool = True
+    # Sequence-parallel TP collectives fused into the GEMMs over NVLink symmetric memory
+    # (AG->GEMM, GEMM->RS); off = NCCL all-gather / reduce-scatter around plain GEMMs.
+    fused_tp_comm: bool = True
 
     def __post_init__(self) -> None:
         _set(self, "backend", _enum("kernels.backend", KernelBackend, self.backend))
         _bool("kernels.cuda_graphs", self.cuda_graphs)
+        _bool("kernels.fused_tp_comm", self.fused_tp_comm)
 
 
 @dataclass(frozen=True, slots=True)

@@ -45,6 +45,21 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v,
                 double eps, double wd, int64_t step, c10::optional<at::Tensor> grad_scale,
                 c10::optional<at::Tensor> lr_t);
 at::Tensor sumsq_partials(at::Tensor x);
+void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda, at::Tensor b,
+                bool b_mn, at::Tensor c, int64_t epi, c10::optional<at::Tensor> xfull,
+                c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
+                c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
+                int64_t head_dim, int64_t rope_cols, int64_t pos_div, int64_t rank,
+                int64_t flags_ptr, int64_t epoch, at::Tensor status);
+void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
+                std::vector<int64_t> staging_ptrs, int64_t rows_per_rank, int64_t n_out,
+                int64_t rank, at::Tensor status);
+std::tuple<at::Tensor, pybind11::bytes> symm_alloc(int64_t bytes, int64_t device);
+int64_t symm_open(pybind11::bytes handle, int64_t device);
+void symm_close(int64_t ptr, int64_t device);
+void peer_signal(std::vector<int64_t> targets, int64_t epoch);
+void rs_reduce(int64_t staging_ptr, int64_t tp, at::Tensor out, c10::optional<at::Tensor> residual,
+               int64_t flags_ptr, int64_t epoch, at::Tensor status);
 void scale_inplace(at::Tensor x, double s);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -69,6 +84,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &adamw_step);
   m.def("sumsq_partials", &sumsq_partials);
   m.def("scale_inplace", &scale_inplace);
+  m.def("gemm_tc_ag", &gemm_tc_ag, "AG->GEMM: A rows gathered from TP peers' symmetric shards");
+  m.def("gemm_tc_rs", &gemm_tc_rs, "GEMM->RS: partial tiles stored into the owner's staging");
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("peer_signal", &peer_signal);
+  m.def("rs_reduce", &rs_reduce);
   m.def("launch_count", []() { return nmb::launch_counter().load(); },
-        "number of kernel launches issued by this library so far");
+        "number of kernel launches issued by this library so far (graph replays included)");
+  m.def("record_graph_launches", [](int64_t n) { nmb::launch_counter() += n; },
+        "count `n` library kernels launched by one CUDA-graph replay");
 }

@@ -43,6 +43,9 @@ enum StatusCode : int {
 // Wall-clock budget for any single wait, in nanoseconds (2 s). Pipeline waits
 // inside one kernel finish in microseconds; this only trips on a real fault.
 constexpr unsigned long long kWaitBudgetNs = 2000000000ull;
+// Budget for waits on another GPU's flag (1 s): shorter than the in-kernel pipeline
+// waits, so when a peer is missing the peer wait is the one that reports.
+constexpr unsigned long long kPeerWaitBudgetNs = 1000000000ull;
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
@@ -139,6 +142,66 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* desc, ui
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(desc)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// 2-D tiled TMA store of a swizzled smem tile to global memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const void* desc, const void* smem_src, int32_t x,
+                                             int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(desc)),
+      "r"(smem_u32(smem_src)), "r"(x), "r"(y)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_store_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+
+// Wait until every committed bulk store has finished *reading* its shared-memory source.
+__device__ __forceinline__ void tma_store_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+
+// Order generic-proxy writes (e.g. a peer's stores observed through an acquire) before
+// subsequent async-proxy (TMA) reads of global memory by this thread.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// ------------------------------------------------------------ peer flags (NVLink)
+// A flag word lives in a rank's symmetric buffer; peers write it with a system-scope
+// release store after their data stores, the owner polls it with acquire loads.
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ void fence_sc_sys() { asm volatile("fence.sc.sys;" ::: "memory"); }
+
+// Bounded wait until *flag has reached `epoch` (wrap-safe compare). Returns false after
+// recording `code` when the budget runs out or another role aborted.
+__device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch, int* status,
+                                          int code, volatile int* abort_flag) {
+  if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+  const unsigned long long start = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
+    if ((it & 63u) == 0u) {
+      if (abort_flag != nullptr && *abort_flag) return false;
+      if (globaltimer_ns() - start > kPeerWaitBudgetNs) {
+        record_status(status, code);
+        if (abort_flag != nullptr) *abort_flag = 1;
+        return false;
+      }
+    }
+    __nanosleep(64);
+  }
 }
 
 // ------------------------------------------------------------------ tcgen05

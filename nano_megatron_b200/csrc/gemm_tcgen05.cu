@@ -25,6 +25,19 @@
 //                columns; writes h = silu(g) * u and keeps [g | u] for backward
 //   kEpiRoPE   : rotate-half rotary embedding applied to the first `rope_cols`
 //                columns (q and k heads) of a fused QKV projection
+//   kEpiPeer   : GEMM -> reduce-scatter. Output row r belongs to TP rank
+//                r / comm_rows; the bf16 partial tile is stored straight into that
+//                rank's symmetric staging buffer (slot = this rank) over NVLink, so
+//                the transfer overlaps the remaining tiles; a flag-gated reduce
+//                kernel on the owner sums the slots (comm_ops.cu).
+//
+// Gathered A (template GATHER, AG -> GEMM): A's rows are split over the TP ranks,
+// rank r's [comm_rows, K] shard living in r's symmetric buffer. The producer
+// TMA-loads each tile from its owner's shard (a peer pointer mapped into this
+// process; plain TMA, no multicast) after a bounded wait on the owner's "shard
+// ready" flag, starting with this rank's own rows. For n-tile 0 the MMA warp also
+// TMA-stores the staged A tile into a local [M, K] buffer, materialising the
+// gathered input that the backward pass needs without a separate all-gather.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -34,7 +47,9 @@
 
 namespace nmb {
 
-enum EpiKind : int { kEpiBF16 = 0, kEpiF32Acc = 1, kEpiSwiGLU = 2, kEpiRoPE = 3 };
+enum EpiKind : int { kEpiBF16 = 0, kEpiF32Acc = 1, kEpiSwiGLU = 2, kEpiRoPE = 3, kEpiPeer = 4 };
+
+constexpr int kMaxTP = 8;
 
 struct GemmParams {
   int M, N, K;               // N = output columns (for SwiGLU: F, the gate/up width)
@@ -56,6 +71,20 @@ struct GemmParams {
   int rope_cols;
   int* status;
   int num_m_tiles, num_n_tiles;
+  // Tensor-parallel communication (gathered A / peer epilogue).
+  int comm_rows;                        // rows of A (gather) or C (peer) owned per TP rank
+  int comm_rank, comm_size;
+  const uint32_t* flags;                // gather: this rank's flags, slot r = rank r's epoch
+  uint32_t epoch;
+  int m_rotate;                         // gather: first M tile (own rows first)
+  int store_gathered;                   // gather: TMA-store A tiles into `xfull`
+  __nv_bfloat16* peer_out[kMaxTP];      // peer epilogue: staging base of each rank
+};
+
+// Per-rank tensor maps of the gathered A operand and of the local gathered copy.
+struct CommMaps {
+  CUtensorMap a[kMaxTP];
+  CUtensorMap xfull;
 };
 
 constexpr int kBM = 128;
@@ -96,10 +125,19 @@ __device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, int col, in
   }
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <bool GATHER>
+__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& m0, int& nt) {
+  int mt = t % p.num_m_tiles;
+  if constexpr (GATHER) mt = (mt + p.m_rotate) % p.num_m_tiles;
+  m0 = mt * kBM;
+  nt = t / p.num_m_tiles;
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
-                        const __grid_constant__ CUtensorMap tmB, const GemmParams p) {
+                        const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CommMaps cm, const GemmParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -147,9 +185,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      uint32_t ready = GATHER ? (1u << p.comm_rank) : 0u;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int m0 = (t % p.num_m_tiles) * kBM;
-        const int nt = t / p.num_m_tiles;
+        int m0, nt;
+        tile_coords<GATHER>(t, p, m0, nt);
+        int owner = 0;
+        if constexpr (GATHER) {
+          owner = m0 / p.comm_rows;
+          if (!((ready >> owner) & 1u)) {
+            if (!wait_flag(p.flags + owner, p.epoch, p.status, kStatusPeerFlagTimeout,
+                           abort_flag)) {
+              ok = false;
+              break;
+            }
+            fence_proxy_async_global();
+            ready |= 1u << owner;
+          }
+        }
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.status, kStatusGemmProducerTimeout,
                          abort_flag)) {
@@ -160,7 +212,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sa = smem_a + stage * Cfg::kABytes;
           uint8_t* sb = smem_b + stage * Cfg::kBBytes;
           const int k0 = kb * kBK;
-          if constexpr (!A_MN) {
+          if constexpr (GATHER) {
+            tma_load_2d(sa, &cm.a[owner], &full_bar[stage], k0, m0 - owner * p.comm_rows);
+          } else if constexpr (!A_MN) {
             tma_load_2d(sa, &tmA, &full_bar[stage], k0, m0);
           } else {
             tma_load_2d(sa, &tmA, &full_bar[stage], m0, k0);
@@ -202,12 +256,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + acc * BN;
+        int m0 = 0, nt = 0;
+        tile_coords<GATHER>(t, p, m0, nt);
+        const bool store_a = GATHER && p.store_gathered && nt == 0;
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, p.status, kStatusGemmMmaTimeout, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          if (store_a) {
+            tma_store_2d(&cm.xfull, smem_a + stage * Cfg::kABytes, kb * kBK, m0);
+            tma_store_commit();
+          }
           const uint32_t a_addr = smem_u32(smem_a + stage * Cfg::kABytes);
           const uint32_t b_addr = smem_u32(smem_b + stage * Cfg::kBBytes);
 #pragma unroll
@@ -223,6 +284,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               bdesc = umma_desc_sw128(b_addr + kk * 2048, kBK * 128, 1024);
             umma_f16_ss(tmem_d, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
+          if (store_a) tma_store_wait_read();  // the stage is refilled once released
           umma_commit(&empty_bar[stage]);
           if (++stage == S) {
             stage = 0;
@@ -246,13 +308,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                      abort_flag))
         break;
       tc_fence_after();
-      const int m0 = (t % p.num_m_tiles) * kBM;
-      const int nt = t / p.num_m_tiles;
+      int m0, nt;
+      tile_coords<GATHER>(t, p, m0, nt);
       const int row = m0 + quarter * 32 + lane;
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
 
-      if constexpr (EPI == kEpiBF16 || EPI == kEpiF32Acc) {
+      if constexpr (EPI == kEpiBF16 || EPI == kEpiF32Acc || EPI == kEpiPeer) {
         const int n0 = nt * BN;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -264,7 +326,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
-          if constexpr (EPI == kEpiBF16) {
+          if constexpr (EPI == kEpiPeer) {
+            const int owner = row / p.comm_rows;
+            __nv_bfloat16* dst =
+                p.peer_out[owner] +
+                static_cast<int64_t>(p.comm_rank * p.comm_rows + row - owner * p.comm_rows) *
+                    p.ldc +
+                col;
+            store_row32_bf16(dst, col, p.N, v);
+          } else if constexpr (EPI == kEpiBF16) {
             if (p.R != nullptr) {
               const __nv_bfloat16* rr = p.R + static_cast<int64_t>(row) * p.ldr + col;
 #pragma unroll
@@ -422,11 +492,13 @@ static int num_sms() {
   return n;
 }
 
-template <int BN, bool A_MN, bool B_MN, int EPI>
+template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER = false>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
-                   cudaStream_t stream, int max_ctas) {
+                   cudaStream_t stream, int max_ctas, const CommMaps* cmp = nullptr) {
   using Cfg = GemmCfg<BN>;
-  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, EPI>;
+  auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, EPI, GATHER>;
+  static CommMaps empty_maps{};
+  const CommMaps& cm = cmp != nullptr ? *cmp : empty_maps;
   static bool attr_set = false;
   if (!attr_set) {
     C10_CUDA_CHECK(
@@ -435,7 +507,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
   }
   const int tiles = p.num_m_tiles * p.num_n_tiles;
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, p); NMB_LAUNCHED(1);
+  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, cm, p); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -450,13 +522,13 @@ static void check_operand(const at::Tensor& t, const char* name) {
 }
 
 // Dispatch on the run-time layout / epilogue to a compiled instantiation.
-template <bool A_MN, bool B_MN, int EPI>
+template <bool A_MN, bool B_MN, int EPI, bool GATHER = false>
 static void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
-                        cudaStream_t s, int max_ctas) {
+                        cudaStream_t s, int max_ctas, const CommMaps* cm = nullptr) {
   if (bn == 256)
-    launch<256, A_MN, B_MN, EPI>(ta, tb, p, s, max_ctas);
+    launch<256, A_MN, B_MN, EPI, GATHER>(ta, tb, p, s, max_ctas, cm);
   else
-    launch<128, A_MN, B_MN, EPI>(ta, tb, p, s, max_ctas);
+    launch<128, A_MN, B_MN, EPI, GATHER>(ta, tb, p, s, max_ctas, cm);
 }
 
 // Pick the N tile: 256 when it still leaves roughly a full wave of tiles.
@@ -568,4 +640,140 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
     else if (a_mn && !b_mn) dispatch_bn<true, false, kEpiF32Acc>(bn, ta, tb, p, stream, mc);
     else dispatch_bn<true, true, kEpiF32Acc>(bn, ta, tb, p, stream, mc);
   }
+}
+
+// AG -> GEMM: C[M, N] = epilogue(A_gathered . B^T), A_gathered = concat over TP ranks of
+// the [R, K] shards at `shard_ptrs[r]` (row pitch `lda`; rank r's shard is ready once
+// its slot in this rank's flag array `flags_ptr` reaches `epoch`). With `xfull`, the
+// gathered A is also written to that local [M, K] tensor. Epilogues: bf16 (dgrad of a
+// row-parallel layer, `b_mn`), RoPE (QKV) or SwiGLU (gate|up).
+void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda, at::Tensor b,
+                bool b_mn, at::Tensor c, int64_t epi, c10::optional<at::Tensor> xfull,
+                c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
+                c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
+                int64_t head_dim, int64_t rope_cols, int64_t pos_div, int64_t rank,
+                int64_t flags_ptr, int64_t epoch, at::Tensor status) {
+  check_operand(a_local, "A shard");
+  check_operand(b, "B");
+  const int tp = static_cast<int>(shard_ptrs.size());
+  TORCH_CHECK(tp >= 1 && tp <= kMaxTP, "gemm_tc_ag: 1..8 ranks");
+  TORCH_CHECK(rank >= 0 && rank < tp);
+  const int64_t R = a_local.size(0), K = a_local.size(1), M = R * tp;
+  TORCH_CHECK(R % kBM == 0, "gemm_tc_ag: rows per rank must be a multiple of 128");
+  TORCH_CHECK((lda * 2) % 16 == 0 && lda >= K);
+  const int64_t Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm_tc_ag: K mismatch");
+  TORCH_CHECK(c.dim() == 2 && c.stride(1) == 1 && c.size(0) == M && c.scalar_type() == at::kBFloat16,
+              "gemm_tc_ag: bad C");
+  for (auto ptr : shard_ptrs) TORCH_CHECK(ptr % 16 == 0, "shard pointers must be 16-byte aligned");
+  const int64_t N = c.size(1);
+  GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.C = c.data_ptr();
+  p.ldc = c.stride(0);
+  p.alpha = 1.0f;
+  p.status = status.data_ptr<int>();
+  p.comm_rows = static_cast<int>(R);
+  p.comm_rank = static_cast<int>(rank);
+  p.comm_size = tp;
+  p.flags = reinterpret_cast<const uint32_t*>(flags_ptr);
+  p.epoch = static_cast<uint32_t>(epoch);
+  p.m_rotate = static_cast<int>(rank * (R / kBM));
+  int bn = choose_bn(p.M, p.N, epi);
+  if (epi == kEpiSwiGLU) {
+    TORCH_CHECK(!b_mn && aux.has_value());
+    p.aux = reinterpret_cast<__nv_bfloat16*>(aux->data_ptr());
+    p.ld_aux = aux->stride(0);
+    p.swiglu_up_row = static_cast<int>(swiglu_up_row);
+    bn = 256;
+  } else if (epi == kEpiRoPE) {
+    TORCH_CHECK(!b_mn && positions.has_value() && inv_freq.has_value());
+    TORCH_CHECK(head_dim == 64 || head_dim == 128);
+    p.positions = positions->data_ptr<int>();
+    p.seq_len = static_cast<int>(positions->numel());
+    p.pos_div = static_cast<int>(pos_div > 0 ? pos_div : 1);
+    p.inv_freq = inv_freq->data_ptr<float>();
+    p.head_dim = static_cast<int>(head_dim);
+    p.rope_cols = static_cast<int>(rope_cols);
+  } else {
+    TORCH_CHECK(epi == kEpiBF16, "gemm_tc_ag: epilogue must be bf16, RoPE or SwiGLU");
+  }
+  const int out_cols = epi == kEpiSwiGLU ? bn / 2 : bn;
+  p.num_m_tiles = static_cast<int>(M / kBM);
+  p.num_n_tiles = static_cast<int>((N + out_cols - 1) / out_cols);
+  if (M == 0 || N == 0) return;
+  const at::cuda::CUDAGuard guard(a_local.device());
+  ensure_current_context(a_local.device().index());
+  CommMaps cm{};
+  for (int r = 0; r < tp; ++r)
+    cm.a[r] = make_tmap_2d(reinterpret_cast<const void*>(shard_ptrs[r]), R, K, lda, kBM);
+  if (xfull.has_value()) {
+    check_operand(*xfull, "xfull");
+    TORCH_CHECK(xfull->size(0) == M && xfull->size(1) == K);
+    cm.xfull = make_tmap_2d(xfull->data_ptr(), M, K, xfull->stride(0), kBM);
+    p.store_gathered = 1;
+  }
+  const int64_t b_rows = b_mn ? b.size(1) : b.size(0);
+  CUtensorMap tb = b_mn ? make_tmap_2d(b.data_ptr(), K, b_rows, b.stride(0), kBK)
+                        : make_tmap_2d(b.data_ptr(), b_rows, K, b.stride(0),
+                                       epi == kEpiSwiGLU ? bn / 2 : bn);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  const CUtensorMap& ta = cm.a[rank];
+  if (epi == kEpiSwiGLU)
+    launch<256, false, false, kEpiSwiGLU, true>(ta, tb, p, stream, 0, &cm);
+  else if (epi == kEpiRoPE)
+    dispatch_bn<false, false, kEpiRoPE, true>(bn, ta, tb, p, stream, 0, &cm);
+  else if (b_mn)
+    dispatch_bn<false, true, kEpiBF16, true>(bn, ta, tb, p, stream, 0, &cm);
+  else
+    dispatch_bn<false, false, kEpiBF16, true>(bn, ta, tb, p, stream, 0, &cm);
+}
+
+// GEMM -> RS: partial C = A . B^T for all M rows; row r's bf16 partial goes to rank
+// (r / rows_per_rank)'s staging buffer `staging_ptrs[owner]`, laid out [tp][rows][N]
+// with this rank's slot `rank`. The owner reduces the slots with rs_reduce.
+void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
+                std::vector<int64_t> staging_ptrs, int64_t rows_per_rank, int64_t n_out,
+                int64_t rank, at::Tensor status) {
+  check_operand(a, "A");
+  check_operand(b, "B");
+  const int tp = static_cast<int>(staging_ptrs.size());
+  TORCH_CHECK(tp >= 1 && tp <= kMaxTP && rank >= 0 && rank < tp);
+  const int64_t M = a_mn ? a.size(1) : a.size(0);
+  const int64_t K = a_mn ? a.size(0) : a.size(1);
+  TORCH_CHECK(K == (b_mn ? b.size(0) : b.size(1)), "gemm_tc_rs: K mismatch");
+  TORCH_CHECK(M == rows_per_rank * tp, "gemm_tc_rs: M must equal tp * rows_per_rank");
+  TORCH_CHECK((n_out * 2) % 16 == 0, "gemm_tc_rs: N must be a multiple of 8");
+  for (auto ptr : staging_ptrs) TORCH_CHECK(ptr % 16 == 0, "staging must be 16-byte aligned");
+  GemmParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(n_out);
+  p.K = static_cast<int>(K);
+  p.ldc = n_out;
+  p.alpha = 1.0f;
+  p.status = status.data_ptr<int>();
+  p.comm_rows = static_cast<int>(rows_per_rank);
+  p.comm_rank = static_cast<int>(rank);
+  p.comm_size = tp;
+  for (int r = 0; r < tp; ++r)
+    p.peer_out[r] = reinterpret_cast<__nv_bfloat16*>(staging_ptrs[r]);
+  const int bn = choose_bn(p.M, p.N, kEpiPeer);
+  p.num_m_tiles = static_cast<int>((M + kBM - 1) / kBM);
+  p.num_n_tiles = static_cast<int>((n_out + bn - 1) / bn);
+  if (M == 0 || n_out == 0) return;
+  const at::cuda::CUDAGuard guard(a.device());
+  ensure_current_context(a.device().index());
+  CUtensorMap ta = a_mn ? make_tmap_2d(a.data_ptr(), K, M, a.stride(0), kBK)
+                        : make_tmap_2d(a.data_ptr(), M, K, a.stride(0), kBM);
+  const int64_t b_rows = b_mn ? b.size(1) : b.size(0);
+  CUtensorMap tb = b_mn ? make_tmap_2d(b.data_ptr(), K, b_rows, b.stride(0), kBK)
+                        : make_tmap_2d(b.data_ptr(), b_rows, K, b.stride(0), bn);
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream();
+  TORCH_CHECK(!a_mn, "gemm_tc_rs: A must be K-major");
+  if (b_mn)
+    dispatch_bn<false, true, kEpiPeer>(bn, ta, tb, p, stream, 0);
+  else
+    dispatch_bn<false, false, kEpiPeer>(bn, ta, tb, p, stream, 0);
 }

@@ -47,6 +47,9 @@ def _torch_dtype(value) -> torch.dtype:
 
 class DataParallelStrategy:
     mode = "base"
+    # True when forward/backward of a microbatch issues no collective and no host sync, so
+    # it can be captured in a CUDA graph (gradients are reduced in finalize_gradients).
+    graph_safe_microbatches = False
 
     def __init__(self, *, config=None, offload=None, parallel=None, parameter_domains=None) -> None:
         self.config = config
@@ -236,6 +239,8 @@ class DataParallelStrategy:
 class DDPStrategy(DataParallelStrategy):
     """Replicated parameters; fp32 master, exp_avg, exp_avg_sq for every element."""
 
+    graph_safe_microbatches = True
+
     mode = "ddp"
 
     def _init_optimizer_state(self) -> None:
@@ -316,6 +321,7 @@ class ReplicatedStrategy(DDPStrategy):
 class FlatShardZeROStrategy(DataParallelStrategy):
     """ZeRO-1/2: fp32 master + Adam moments sharded over the replica group."""
 
+    graph_safe_microbatches = True
     mode = "zero"
     reduce_scatter = False
 

@@ -16,4 +16,5 @@ from .strategies import Zero2Strategy
 
 class Zero3Strategy(Zero2Strategy):
     mode = "zero3"
+    graph_safe_microbatches = False
     reduce_scatter = True

@@ -1,0 +1,129 @@
+"""Symmetric device memory across the ranks of one (tensor-parallel) group.
+
+Each rank allocates one zeroed device buffer, exports a CUDA IPC handle, and
+opens every peer's handle, so all ranks can load and store every rank's buffer
+over NVLink (P2P through NVSwitch). Buffer layout (identical on all ranks):
+
+    [ flags: 16 channels x 8 source slots x uint32 | pad to 4 KiB ]
+    [ reduce-scatter staging: 2 parities x TP x rows x cols bf16 ]
+    [ all-gather shards:       2 parities x rows x cols bf16      ]
+
+A channel's epoch counter advances once per collective call on every rank
+(all ranks issue the same calls in the same order); parity = epoch & 1 selects
+the data half, so call k+1 never overwrites data call k may still be reading
+(a rank only reaches call k+2 after every peer has signalled call k+1, which it
+does after finishing call k). ``emulated`` builds TP workspaces inside one
+process on one GPU -- every "peer" buffer is local -- so the fused kernels'
+indexing and reductions can be checked without several GPUs; there the calls
+of the emulated ranks are issued phase by phase so no kernel ever waits for a
+kernel that has not been launched.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+FLAG_BYTES = 4096
+MAX_TP = 8
+CH_RS, CH_AG, CH_AG_BWD = 0, 1, 2
+
+
+class SymmetricWorkspace:
+    def __init__(self, *, rank: int, size: int, ptrs: list[int], owner: torch.Tensor,
+                 device: torch.device, rs_bytes: int, ag_bytes: int, opened: list[int]) -> None:
+        self.rank, self.size = rank, size
+        self.ptrs = ptrs              # base address of every rank's buffer, mapped here
+        self.owner = owner            # keeps this rank's allocation alive
+        self.device = device
+        self.rs_bytes, self.ag_bytes = rs_bytes, ag_bytes
+        self._opened = opened         # peer mappings to close
+        self.epoch = [0] * 16
+        from nano_megatron_b200.ops._ext import status_word
+
+        self.status = status_word(device)
+
+    # ------------------------------------------------------------------ construction
+    @staticmethod
+    def total_bytes(rs_bytes: int, ag_bytes: int) -> int:
+        return FLAG_BYTES + 2 * rs_bytes + 2 * ag_bytes
+
+    @classmethod
+    def create(cls, group, *, rs_bytes: int, ag_bytes: int, device: torch.device
+               ) -> "SymmetricWorkspace":
+        """Collective over ``group`` (a ParallelGroup with an NCCL process group)."""
+        from nano_megatron_b200.ops._ext import lib
+
+        if group.size > MAX_TP:
+            raise ValueError(f"symmetric workspace supports at most {MAX_TP} ranks")
+        rs_bytes, ag_bytes = _align(rs_bytes), _align(ag_bytes)
+        dev = torch.device(device)
+        buf, handle = lib().symm_alloc(cls.total_bytes(rs_bytes, ag_bytes), dev.index)
+        handles: list = [None] * group.size
+        dist.all_gather_object(handles, bytes(handle), group=group.process_group)
+        ptrs, opened = [], []
+        for r, h in enumerate(handles):
+            if r == group.rank:
+                ptrs.append(buf.data_ptr())
+            else:
+                p = lib().symm_open(h, dev.index)
+                opened.append(p)
+                ptrs.append(p)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group.process_group, device_ids=[dev.index])
+        return cls(rank=group.rank, size=group.size, ptrs=ptrs, owner=buf, device=dev,
+                   rs_bytes=rs_bytes, ag_bytes=ag_bytes, opened=opened)
+
+    @classmethod
+    def emulated(cls, size: int, *, rs_bytes: int, ag_bytes: int, device: torch.device
+                 ) -> list["SymmetricWorkspace"]:
+        rs_bytes, ag_bytes = _align(rs_bytes), _align(ag_bytes)
+        dev = torch.device(device)
+        bufs = [torch.zeros(cls.total_bytes(rs_bytes, ag_bytes), dtype=torch.uint8, device=dev)
+                for _ in range(size)]
+        ptrs = [b.data_ptr() for b in bufs]
+        return [cls(rank=r, size=size, ptrs=ptrs, owner=bufs[r], device=dev, rs_bytes=rs_bytes,
+                    ag_bytes=ag_bytes, opened=[]) for r in range(size)]
+
+    def close(self) -> None:
+        from nano_megatron_b200.ops._ext import lib
+
+        for p in self._opened:
+            lib().symm_close(p, self.device.index)
+        self._opened = []
+
+    # ------------------------------------------------------------------ addressing
+    def next_epoch(self, channel: int) -> int:
+        self.epoch[channel] = (self.epoch[channel] + 1) & 0x7FFFFFFF or 1
+        return self.epoch[channel]
+
+    def flags(self, rank: int, channel: int) -> int:
+        return self.ptrs[rank] + channel * MAX_TP * 4
+
+    def signal_targets(self, channel: int) -> list[int]:
+        return [self.flags(d, channel) + self.rank * 4 for d in range(self.size)]
+
+    def rs_staging(self, rank: int, epoch: int) -> int:
+        return self.ptrs[rank] + FLAG_BYTES + (epoch & 1) * self.rs_bytes
+
+    def ag_shard(self, rank: int, epoch: int) -> int:
+        return self.ptrs[rank] + FLAG_BYTES + 2 * self.rs_bytes + (epoch & 1) * self.ag_bytes
+
+    def ag_shard_tensor(self, epoch: int, rows: int, cols: int) -> torch.Tensor:
+        """This rank's shard slot as a [rows, cols] bf16 tensor view."""
+        need = rows * cols * 2
+        if need > self.ag_bytes:
+            raise ValueError(f"all-gather shard needs {need} bytes; workspace has "
+                             f"{self.ag_bytes}")
+        off = FLAG_BYTES + 2 * self.rs_bytes + (epoch & 1) * self.ag_bytes
+        return self.owner[off:off + need].view(torch.bfloat16).view(rows, cols)
+
+    def check_rs(self, rows: int, cols: int) -> None:
+        need = self.size * rows * cols * 2
+        if need > self.rs_bytes:
+            raise ValueError(f"reduce-scatter staging needs {need} bytes; workspace has "
+                             f"{self.rs_bytes}")
+
+
+def _align(n: int, a: int = 1 << 21) -> int:
+    return max(a, (int(n) + a - 1) // a * a)

@@ -13,6 +13,14 @@ schedule:
   logits GEMM, vocab-parallel cross-entropy whose gradient overwrites the
   logits in place, so no fp32 logits or softmax copy is ever stored).
 
+Under sequence parallelism with a symmetric workspace attached (CUDA, TP > 1),
+the SP collectives are fused into the GEMMs over NVLink: the norm output's
+all-gather into the QKV / gate|up GEMM (TMA loads from the peers' shards, the
+gathered input kept for the weight gradient), the out/down projection's
+reduce-scatter into its GEMM epilogue (plus the residual add), and in the
+backward pass the dY all-gather into the dgrad GEMM and the dX reduce-scatter
+into the QKV / gate|up dgrad GEMM (:mod:`nano_megatron_b200.ops.comm_gemm`).
+
 Weight gradients are accumulated straight into each parameter's fp32
 ``main_grad`` (a view of the data-parallel gradient buffer) by the
 weight-gradient GEMM epilogue; autograd returns ``None`` for parameters.
@@ -31,6 +39,7 @@ from dataclasses import dataclass, field
 import torch
 
 from nano_megatron_b200.ops import functional as F
+from nano_megatron_b200.ops import comm_gemm as CG
 from nano_megatron_b200.tensor_parallel.comm import all_gather_dim0, all_reduce, reduce_scatter_dim0
 from nano_megatron_b200.tensor_parallel.cross_entropy import vocab_parallel_ce_rows
 
@@ -97,6 +106,12 @@ class TPInfo:
     group: object | None
     size: int
     sequence_parallel: bool
+    workspace: object | None = None   # SymmetricWorkspace for the fused SP collectives
+
+    def fused(self, x: torch.Tensor) -> bool:
+        """Use the fused AG->GEMM / GEMM->RS kernels for this local row block."""
+        return (self.workspace is not None and self.sequence_parallel and self.size > 1 and
+                x.is_cuda and x.shape[0] % 128 == 0)
 
     def gather(self, x):
         return all_gather_dim0(x, self.group) if self.sequence_parallel and self.size > 1 else x
@@ -180,11 +195,17 @@ class AttentionBlockFn(torch.autograd.Function):
         H = spec.hidden
         h2 = h.reshape(-1, H)
         xn, rstd = F.rmsnorm(h2, w_norm, spec.eps)
-        xg = spec.tp.gather(xn)
         w_qkv = fused_rows([w_q, w_k, w_v])
         D, hq, hkv = spec.head_dim, spec.heads, spec.kv_heads
-        qkv = F.qkv_rope_linear(xg, w_qkv, mb.positions, inv_freq, D, (hq + hkv) * D,
-                                pos_div=mb.batch)
+        fused = spec.tp.fused(xn) and D in (64, 128)
+        if fused:
+            qkv, xg = CG.allgather_gemm(spec.tp.workspace, xn, w_qkv, epi="rope",
+                                        positions=mb.positions, inv_freq=inv_freq, head_dim=D,
+                                        rope_cols=(hq + hkv) * D, pos_div=mb.batch)
+        else:
+            xg = spec.tp.gather(xn)
+            qkv = F.qkv_rope_linear(xg, w_qkv, mb.positions, inv_freq, D, (hq + hkv) * D,
+                                    pos_div=mb.batch)
         q, k, v = _split_qkv(qkv, mb.seq, mb.batch, hq, hkv, D)
         o = torch.empty(mb.seq, mb.batch, hq, D, device=h.device, dtype=qkv.dtype)
         lse = spec.core.forward(q, k, v, o, mb)
@@ -192,6 +213,8 @@ class AttentionBlockFn(torch.autograd.Function):
         fuse_residual = spec.tp.size == 1 and b_out is None and dropout_fn is None
         if fuse_residual:
             out = F.linear(ctx2, w_out.detach(), residual=h2)
+        elif fused and b_out is None and dropout_fn is None:
+            out = CG.gemm_reduce_scatter(spec.tp.workspace, ctx2, w_out.detach(), residual=h2)
         else:
             y = spec.tp.reduce_out(F.linear(ctx2, w_out.detach()))
             if b_out is not None:
@@ -217,9 +240,13 @@ class AttentionBlockFn(torch.autograd.Function):
             dy = ctx.dropout_fn.backward(dy)
         if b_out is not None:
             F.bias_grad(dy, main_grad_of(b_out))
-        dyg = spec.tp.gather(dy)
         ctx2 = o.view(mb.seq * mb.batch, hq * D)
-        d_ctx = F.linear_dgrad(dyg, w_out.detach())
+        fused = spec.tp.fused(dy)
+        if fused:
+            d_ctx, dyg = CG.allgather_gemm(spec.tp.workspace, dy, w_out.detach(), b_mn=True)
+        else:
+            dyg = spec.tp.gather(dy)
+            d_ctx = F.linear_dgrad(dyg, w_out.detach())
         F.linear_wgrad(dyg, ctx2, main_grad_of(w_out))
         q, k, v = _split_qkv(qkv, mb.seq, mb.batch, hq, hkv, D)
         dqkv = torch.empty_like(qkv)
@@ -231,11 +258,13 @@ class AttentionBlockFn(torch.autograd.Function):
             F.rope_(dqkv, (hq + hkv) * D, D, mb.positions, ctx.inv_freq, inverse=True,
                     pos_div=mb.batch)
         w_qkv = fused_rows([w_q, w_k, w_v])
-        dxg = F.linear_dgrad(dqkv, w_qkv)
+        if fused:
+            dxn = CG.gemm_reduce_scatter(spec.tp.workspace, dqkv, w_qkv, b_mn=True)
+        else:
+            dxn = spec.tp.reduce_in_grad(F.linear_dgrad(dqkv, w_qkv))
         g = FusedGrad([w_q, w_k, w_v])
         F.linear_wgrad(dqkv, xg, g.target)
         g.flush()
-        dxn = spec.tp.reduce_in_grad(dxg)
         dh_in = F.rmsnorm_bwd(h2, w_norm.detach(), dxn, rstd, main_grad_of(w_norm), dres=dh)
         return (dh_in.view(dout.shape), None, None, None, None, None, None, None, None, None, None)
 
@@ -256,12 +285,21 @@ class MLPBlockFn(torch.autograd.Function):
         H = spec.hidden
         h2 = h.reshape(-1, H)
         xn, rstd = F.rmsnorm(h2, w_norm, spec.eps)
-        xg = spec.tp.gather(xn)
         w_gu = fused_rows([w_gate, w_up])
-        hmid, gu = F.swiglu_linear(xg, w_gu, spec.ffn)
+        fused = spec.tp.fused(xn) and spec.ffn % 128 == 0
+        if fused:
+            gu = torch.empty(xn.shape[0] * spec.tp.size, 2 * spec.ffn, device=xn.device,
+                             dtype=xn.dtype)
+            hmid, xg = CG.allgather_gemm(spec.tp.workspace, xn, w_gu, epi="swiglu",
+                                         n_out=spec.ffn, aux=gu, swiglu_up_row=spec.ffn)
+        else:
+            xg = spec.tp.gather(xn)
+            hmid, gu = F.swiglu_linear(xg, w_gu, spec.ffn)
         fuse_residual = spec.tp.size == 1 and b_down is None and dropout_fn is None
         if fuse_residual:
             out = F.linear(hmid, w_down.detach(), residual=h2)
+        elif fused and b_down is None and dropout_fn is None:
+            out = CG.gemm_reduce_scatter(spec.tp.workspace, hmid, w_down.detach(), residual=h2)
         else:
             y = spec.tp.reduce_out(F.linear(hmid, w_down.detach()))
             if b_down is not None:
@@ -286,17 +324,23 @@ class MLPBlockFn(torch.autograd.Function):
             dy = ctx.dropout_fn.backward(dy)
         if b_down is not None:
             F.bias_grad(dy, main_grad_of(b_down))
-        dyg = spec.tp.gather(dy)
-        dmid = F.linear_dgrad(dyg, w_down.detach())
+        fused = spec.tp.fused(dy) and spec.ffn % 128 == 0
+        if fused:
+            dmid, dyg = CG.allgather_gemm(spec.tp.workspace, dy, w_down.detach(), b_mn=True)
+        else:
+            dyg = spec.tp.gather(dy)
+            dmid = F.linear_dgrad(dyg, w_down.detach())
         F.linear_wgrad(dyg, hmid, main_grad_of(w_down))
         dgu = F.swiglu_bwd(gu, dmid, inplace=True)
         del dmid
         w_gu = fused_rows([w_gate, w_up])
-        dxg = F.linear_dgrad(dgu, w_gu)
+        if fused:
+            dxn = CG.gemm_reduce_scatter(spec.tp.workspace, dgu, w_gu, b_mn=True)
+        else:
+            dxn = spec.tp.reduce_in_grad(F.linear_dgrad(dgu, w_gu))
         g = FusedGrad([w_gate, w_up])
         F.linear_wgrad(dgu, xg, g.target)
         g.flush()
-        dxn = spec.tp.reduce_in_grad(dxg)
         dh_in = F.rmsnorm_bwd(h2, w_norm.detach(), dxn, rstd, main_grad_of(w_norm), dres=dh)
         return dh_in.view(dout.shape), None, None, None, None, None, None, None
 

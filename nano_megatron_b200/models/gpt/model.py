@@ -215,7 +215,8 @@ class GPTModel(nn.Module):
     # ------------------------------------------------------------------ helpers
     def _tp_info(self) -> B.TPInfo:
         tp = self.parallel.tp
-        return B.TPInfo(tp if tp.size > 1 else None, tp.size, self.sequence_parallel)
+        return B.TPInfo(tp if tp.size > 1 else None, tp.size, self.sequence_parallel,
+                        getattr(self, "tp_workspace", None))
 
     def _specs(self):
         tpi = self._tp_info()

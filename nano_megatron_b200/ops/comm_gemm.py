@@ -1,0 +1,94 @@
+"""Fused tensor-parallel GEMM + collective ops over a :class:`SymmetricWorkspace`.
+
+* ``gemm_reduce_scatter``: ``out[R, N] = sum_r (A_r B_r^T)[rows of this rank] (+ residual)``
+  -- the row-parallel projection under sequence parallelism (out_proj / down_proj
+  forward, QKV / gate-up dgrad). One tcgen05 GEMM whose epilogue stores each bf16
+  partial tile into its owner's staging slot over NVLink, then a flag-gated
+  reduce on the owner that also adds the residual.
+* ``allgather_gemm``: ``out[M, N] = epilogue(concat_r(X_r) B^T)`` -- the
+  column-parallel projection under sequence parallelism (QKV with RoPE, gate|up
+  with SwiGLU, out/down dgrad). The local shard is published into the symmetric
+  buffer and signalled; the GEMM's TMA producer reads each peer's rows straight
+  from that peer's buffer once its flag arrives, own rows first, and the gathered
+  input is written to a local tensor for the backward pass.
+
+Each op is split into ``issue`` / ``finish`` phases so single-GPU tests can run
+emulated ranks phase by phase; the public functions run both.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from nano_megatron_b200.distributed.symmetric import CH_AG, CH_RS
+
+from ._ext import lib
+
+EPI = {"bf16": 0, "rope": 3, "swiglu": 2}
+
+
+def rs_issue(ws, a: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,
+             n_out: int | None = None) -> tuple[int, int, int]:
+    """GEMM with the peer epilogue + signal. Returns (epoch, rows_per_rank, n_out)."""
+    M = a.shape[0]
+    if M % ws.size:
+        raise ValueError(f"rows {M} not divisible by TP size {ws.size}")
+    rows = M // ws.size
+    n = n_out if n_out is not None else (b.shape[1] if b_mn else b.shape[0])
+    ws.check_rs(rows, n)
+    epoch = ws.next_epoch(CH_RS)
+    lib().gemm_tc_rs(a, False, b, b_mn, [ws.rs_staging(r, epoch) for r in range(ws.size)], rows,
+                     n, ws.rank, ws.status)
+    lib().peer_signal(ws.signal_targets(CH_RS), epoch)
+    return epoch, rows, n
+
+
+def rs_finish(ws, epoch: int, out: torch.Tensor, residual: torch.Tensor | None = None) -> None:
+    lib().rs_reduce(ws.rs_staging(ws.rank, epoch), ws.size, out, residual, ws.flags(ws.rank, CH_RS),
+                    epoch, ws.status)
+
+
+def gemm_reduce_scatter(ws, a: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,
+                        residual: torch.Tensor | None = None,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    epoch, rows, n = rs_issue(ws, a, b, b_mn=b_mn)
+    if out is None:
+        out = torch.empty(rows, n, device=a.device, dtype=torch.bfloat16)
+    rs_finish(ws, epoch, out, residual)
+    return out
+
+
+def ag_issue(ws, x_local: torch.Tensor, channel: int = CH_AG) -> int:
+    """Publish this rank's shard into its symmetric slot and signal every rank."""
+    epoch = ws.next_epoch(channel)
+    R, K = x_local.shape
+    ws.ag_shard_tensor(epoch, R, K).copy_(x_local)
+    lib().peer_signal(ws.signal_targets(channel), epoch)
+    return epoch
+
+
+def ag_finish(ws, epoch: int, x_local: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
+              b_mn: bool = False, epi: str = "bf16", xfull: torch.Tensor | None = None,
+              aux: torch.Tensor | None = None, swiglu_up_row: int = 0,
+              positions: torch.Tensor | None = None, inv_freq: torch.Tensor | None = None,
+              head_dim: int = 0, rope_cols: int = 0, pos_div: int = 1,
+              channel: int = CH_AG) -> None:
+    R, K = x_local.shape
+    lib().gemm_tc_ag(x_local, [ws.ag_shard(r, epoch) for r in range(ws.size)], K, b, b_mn, out,
+                     EPI[epi], xfull, aux, swiglu_up_row, positions, inv_freq, head_dim,
+                     rope_cols, pos_div, ws.rank, ws.flags(ws.rank, channel), epoch, ws.status)
+
+
+def allgather_gemm(ws, x_local: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,
+                   epi: str = "bf16", n_out: int | None = None, store_gathered: bool = True,
+                   **kw) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """Returns (out [TP*R, N], gathered input [TP*R, K] or None)."""
+    R, K = x_local.shape
+    M = R * ws.size
+    n = n_out if n_out is not None else (b.shape[1] if b_mn else b.shape[0])
+    out = torch.empty(M, n, device=x_local.device, dtype=torch.bfloat16)
+    xfull = torch.empty(M, K, device=x_local.device, dtype=torch.bfloat16) \
+        if store_gathered else None
+    epoch = ag_issue(ws, x_local)
+    ag_finish(ws, epoch, x_local, b, out, b_mn=b_mn, epi=epi, xfull=xfull, **kw)
+    return out, xfull

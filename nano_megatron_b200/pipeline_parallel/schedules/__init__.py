@@ -6,7 +6,12 @@ from .no_pipeline import NoPipelineSchedule
 
 def build_schedule(config, model, parallel, data_parallel):
     if parallel.pp.size == 1 and config.pipeline.virtual_stages_per_rank == 1:
-        return NoPipelineSchedule(model, data_parallel)
+        from nano_megatron_b200.training.cuda_graphs import graphs_supported
+
+        device = next(model.parameters()).device
+        return NoPipelineSchedule(model, data_parallel,
+                                  use_graphs=graphs_supported(config, model, data_parallel,
+                                                              device))
     from .executor import build_pipeline_schedule
 
     return build_pipeline_schedule(config, model, parallel, data_parallel)

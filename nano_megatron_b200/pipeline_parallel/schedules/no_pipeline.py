@@ -4,19 +4,43 @@ from __future__ import annotations
 
 import torch
 
-from .base import LossAccumulator, extract_loss
+from .base import LossAccumulator, batch_labels, extract_loss
 
 
 class NoPipelineSchedule:
-    def __init__(self, stage, data_parallel) -> None:
+    """Gradient accumulation over microbatches; with ``use_graphs`` each training microbatch
+    is one CUDA-graph replay (:mod:`nano_megatron_b200.training.cuda_graphs`)."""
+
+    def __init__(self, stage, data_parallel, *, use_graphs: bool = False) -> None:
         self.stage = stage
         self.data_parallel = data_parallel
+        self.use_graphs = use_graphs
+        self._graphs: dict = {}
+
+    def _graphed(self, microbatches, acc: LossAccumulator) -> None:
+        from nano_megatron_b200.training.cuda_graphs import GraphedMicrobatch, graph_key
+
+        m = len(microbatches)
+        keys = [(graph_key(mb), m) for mb in microbatches]
+        # Capture every missing shape before running any microbatch: a capture's warm-up
+        # zeroes the gradient buffers, which must not erase this step's accumulation.
+        for key, mb in zip(keys, microbatches):
+            if key not in self._graphs:
+                device = next(self.stage.parameters()).device
+                g = GraphedMicrobatch(self.stage, self.data_parallel, mb, m, device)
+                g.capture(mb)
+                self._graphs[key] = g
+        for key, mb in zip(keys, microbatches):
+            acc.add(self._graphs[key].run(mb).clone(), batch_labels(mb))
 
     def forward_backward(self, microbatches, *, forward_only: bool = False
                          ) -> LossAccumulator:
         acc = LossAccumulator()
         m = len(microbatches)
         dp = self.data_parallel
+        if self.use_graphs and not forward_only:
+            self._graphed(microbatches, acc)
+            return acc
         for i, mb in enumerate(microbatches):
             last = i == m - 1
             if forward_only:

@@ -56,4 +56,7 @@ def build_training_components(config, runtime) -> TrainingComponents:
     strategy = build_data_parallel_strategy(config.data_parallel, config.offload, parallel,
                                             built.parameter_domains)
     strategy.configure_precision(config.precision)
+    from nano_megatron_b200.tensor_parallel.fused import attach_tp_workspace
+
+    attach_tp_workspace(model, config, parallel, torch.device(runtime.device))
     return TrainingComponents(runtime, parallel, rng, model, built, strategy)

@@ -1,0 +1,146 @@
+"""Fused TP collectives (AG->GEMM, GEMM->RS) against fp32 PyTorch references.
+
+The TP ranks are emulated inside one process on one GPU: every "peer" buffer
+is a local allocation and the ranks' kernels are issued phase by phase (all
+publishes/GEMMs first, then the consumers), so every flag a kernel waits on is
+already set when it runs -- no kernel ever waits on one launched after it. The
+real multi-process path (IPC-mapped peers on several GPUs) is covered by
+``test_comm_gemm_multigpu.py``.
+"""
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from nano_megatron_b200.distributed.symmetric import SymmetricWorkspace  # noqa: E402
+from nano_megatron_b200.ops import comm_gemm as CG  # noqa: E402
+from nano_megatron_b200.ops import functional as F  # noqa: E402
+from nano_megatron_b200.ops._ext import status_word  # noqa: E402
+
+DEV = torch.device("cuda")
+MB = 1 << 20
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
+
+
+def _ok():
+    torch.cuda.synchronize()
+    assert int(status_word(DEV).item()) == 0
+
+
+@pytest.mark.parametrize("tp", [2, 4])
+@pytest.mark.parametrize("b_mn", [False, True])
+def test_gemm_reduce_scatter(tp, b_mn):
+    torch.manual_seed(tp)
+    ws = SymmetricWorkspace.emulated(tp, rs_bytes=16 * MB, ag_bytes=8 * MB, device=DEV)
+    R, K, N = 256, 512, 384
+    M = R * tp
+    for it in range(3):  # exercises both parities and epoch advance
+        a = [torch.randn(M, K, device=DEV).bfloat16() for _ in range(tp)]
+        w = [torch.randn(N, K, device=DEV).bfloat16() for _ in range(tp)]
+        res = [torch.randn(R, N, device=DEV).bfloat16() for _ in range(tp)]
+        bstore = [x.t().contiguous() if b_mn else x for x in w]
+        issued = [CG.rs_issue(ws[r], a[r], bstore[r], b_mn=b_mn) for r in range(tp)]
+        outs = [torch.empty(R, N, device=DEV, dtype=torch.bfloat16) for _ in range(tp)]
+        for r in range(tp):
+            CG.rs_finish(ws[r], issued[r][0], outs[r], res[r])
+        _ok()
+        full = sum(a[r].float() @ w[r].float().t() for r in range(tp))
+        for r in range(tp):
+            ref = full[r * R:(r + 1) * R] + res[r].float()
+            assert _rel(outs[r], ref) < 1e-2, (it, r)
+
+
+@pytest.mark.parametrize("tp", [2, 4])
+def test_allgather_gemm_bf16_and_gathered_copy(tp):
+    torch.manual_seed(10 + tp)
+    ws = SymmetricWorkspace.emulated(tp, rs_bytes=2 * MB, ag_bytes=8 * MB, device=DEV)
+    R, K, N = 256, 576, 640
+    for it in range(3):
+        x = [torch.randn(R, K, device=DEV).bfloat16() for _ in range(tp)]
+        w = torch.randn(N, K, device=DEV).bfloat16()
+        epochs = [CG.ag_issue(ws[r], x[r]) for r in range(tp)]
+        outs, xf = [], []
+        for r in range(tp):
+            o = torch.empty(R * tp, N, device=DEV, dtype=torch.bfloat16)
+            g = torch.empty(R * tp, K, device=DEV, dtype=torch.bfloat16)
+            CG.ag_finish(ws[r], epochs[r], x[r], w, o, xfull=g)
+            outs.append(o)
+            xf.append(g)
+        _ok()
+        xcat = torch.cat(x)
+        ref = xcat.float() @ w.float().t()
+        for r in range(tp):
+            assert torch.equal(xf[r], xcat), (it, r)
+            assert _rel(outs[r], ref) < 1e-2, (it, r)
+
+
+def test_allgather_gemm_dgrad_layout():
+    """dgrad of a row-parallel layer: A = dy (gathered), B = W stored [N_local, K] (MN-major)."""
+    tp, R, n_local, K = 2, 384, 512, 1024
+    ws = SymmetricWorkspace.emulated(tp, rs_bytes=2 * MB, ag_bytes=8 * MB, device=DEV)
+    dy = [torch.randn(R, K, device=DEV).bfloat16() for _ in range(tp)]
+    w = torch.randn(K, n_local, device=DEV).bfloat16()       # weight [out=K, in_local]
+    epochs = [CG.ag_issue(ws[r], dy[r]) for r in range(tp)]
+    outs = []
+    for r in range(tp):
+        o = torch.empty(R * tp, n_local, device=DEV, dtype=torch.bfloat16)
+        CG.ag_finish(ws[r], epochs[r], dy[r], w, o, b_mn=True)
+        outs.append(o)
+    _ok()
+    ref = torch.cat(dy).float() @ w.float()
+    for o in outs:
+        assert _rel(o, ref) < 1e-2
+
+
+def test_allgather_gemm_rope_and_swiglu_match_local_kernels():
+    tp, R, H, D = 2, 256, 512, 64
+    hq, hkv = 8, 4
+    ws = SymmetricWorkspace.emulated(tp, rs_bytes=2 * MB, ag_bytes=8 * MB, device=DEV)
+    torch.manual_seed(3)
+    x = [torch.randn(R, H, device=DEV).bfloat16() for _ in range(tp)]
+    xcat = torch.cat(x)
+    wqkv = (torch.randn((hq + 2 * hkv) * D, H, device=DEV) * 0.05).bfloat16()
+    B = 4
+    pos = torch.arange(R * tp // B, device=DEV, dtype=torch.int32)
+    inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device=DEV).float() / D))
+    ref = F.qkv_rope_linear(xcat, wqkv, pos, inv, D, (hq + hkv) * D, pos_div=B)
+    epochs = [CG.ag_issue(ws[r], x[r]) for r in range(tp)]
+    for r in range(tp):
+        o = torch.empty(R * tp, wqkv.shape[0], device=DEV, dtype=torch.bfloat16)
+        CG.ag_finish(ws[r], epochs[r], x[r], wqkv, o, epi="rope", positions=pos, inv_freq=inv,
+                     head_dim=D, rope_cols=(hq + hkv) * D, pos_div=B)
+        _ok()
+        assert _rel(o, ref) < 1e-3
+    ffn = 768
+    wgu = (torch.randn(2 * ffn, H, device=DEV) * 0.05).bfloat16()
+    h_ref, gu_ref = F.swiglu_linear(xcat, wgu, ffn)
+    epochs = [CG.ag_issue(ws[r], x[r]) for r in range(tp)]
+    for r in range(tp):
+        h = torch.empty(R * tp, ffn, device=DEV, dtype=torch.bfloat16)
+        gu = torch.empty(R * tp, 2 * ffn, device=DEV, dtype=torch.bfloat16)
+        CG.ag_finish(ws[r], epochs[r], x[r], wgu, h, epi="swiglu", aux=gu, swiglu_up_row=ffn)
+        _ok()
+        assert _rel(h, h_ref) < 1e-3 and _rel(gu, gu_ref) < 1e-3
+
+
+def test_missing_peer_times_out_with_status():
+    """A peer that never publishes: the bounded wait gives up (~2 s), records 0x301 and
+    the kernel returns; the context stays usable."""
+    tp, R, K, N = 2, 128, 256, 256
+    ws = SymmetricWorkspace.emulated(tp, rs_bytes=2 * MB, ag_bytes=2 * MB, device=DEV)
+    x = torch.randn(R, K, device=DEV).bfloat16()
+    w = torch.randn(N, K, device=DEV).bfloat16()
+    epoch = CG.ag_issue(ws[0], x)          # rank 1 never publishes this epoch
+    o = torch.empty(R * tp, N, device=DEV, dtype=torch.bfloat16)
+    CG.ag_finish(ws[0], epoch, x, w, o)
+    torch.cuda.synchronize()
+    st = status_word(DEV)
+    assert int(st.item()) == 0x301
+    st.zero_()
+    y = torch.randn(64, 64, device=DEV) @ torch.randn(64, 64, device=DEV)  # context still fine
+    torch.cuda.synchronize()
+    assert torch.isfinite(y).all()

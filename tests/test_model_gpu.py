@@ -49,3 +49,48 @@ def test_cuda_model_matches_cpu_fp32(model):
         got = p.main_grad.float().cpu()
         rel = ((got - ref).norm() / (ref.norm() + 1e-12)).item()
         assert rel < 5e-2, f"{name}: rel grad err {rel}"
+
+
+def _trainer(graphs: bool):
+    from nano_megatron_b200.training import Trainer
+
+    cfg = config_from_dict({
+        "model": {"layers": 2, "hidden_size": 256, "ffn_hidden_size": 688, "heads": 4,
+                  "kv_heads": 2, "seq_length": 128, "vocab_size": 1024},
+        "distributed": {"device": "cuda", "backend": "nccl"},
+        "kernels": {"backend": "b200", "cuda_graphs": graphs},
+        "training": {"micro_batch_size": 2, "gradient_accumulation_steps": 3, "seed": 11},
+        "optimizer": {"lr": 1e-3, "clip_grad_norm": 1.0}})
+    rt = DistributedRuntime(cfg.distributed).initialize()
+    comps = build_training_components(cfg, rt)
+    tr = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
+                 data_parallel=comps.data_parallel, rng=comps.rng)
+    return comps, tr
+
+
+def test_cuda_graph_steps_match_eager_steps():
+    """Three optimizer steps replayed from per-microbatch CUDA graphs == eager steps."""
+    from nano_megatron_b200.ops._ext import lib
+
+    g = torch.Generator().manual_seed(4)
+    batches = [torch.randint(0, 1024, (6, 129), generator=g) for _ in range(3)]
+    losses, params = {}, {}
+    for graphs in (False, True):
+        comps, tr = _trainer(graphs)
+        assert tr.schedule.use_graphs == graphs
+        ls = []
+        for ids in batches:
+            out = tr.train_step({"input_ids": ids[:, :-1], "labels": ids[:, 1:]})
+            ls.append(float(out["loss_sum"] / out["token_count"]))
+        torch.cuda.synchronize()
+        losses[graphs] = ls
+        params[graphs] = {n: p.detach().float().cpu() for n, p in comps.model.named_parameters()}
+        if graphs:
+            before = lib().launch_count()
+            tr.train_step({"input_ids": batches[0][:, :-1], "labels": batches[0][:, 1:]})
+            assert lib().launch_count() - before > 3 * 20  # replays are counted
+    for a, b in zip(losses[False], losses[True]):
+        assert abs(a - b) < 1e-3 * abs(a), (losses[False], losses[True])
+    for n, p in params[False].items():
+        rel = ((params[True][n] - p).norm() / (p.norm() + 1e-12)).item()
+        assert rel < 1e-3, (n, rel)

@@ -1,0 +1,104 @@
+"""TP2 + sequence parallelism on two GPUs: fused NVLink collectives vs NCCL collectives.
+
+Same weights, same batch: the training-step loss and the merged weight
+gradients with ``kernels.fused_tp_comm`` on must match the run with it off
+(bf16 tolerance). Child processes, one per GPU, bounded by timeouts.
+"""
+
+import os
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _cfg(fused: bool):
+    from nano_megatron_b200.config import config_from_dict
+
+    return config_from_dict({
+        "distributed": {"backend": "nccl", "device": "cuda", "timeout_minutes": 2},
+        "parallel": {"tensor": 2, "pipeline": 1, "context": 1, "expert": 1, "data": 1,
+                     "sequence_parallel": True},
+        "model": {"layers": 2, "hidden_size": 256, "ffn_hidden_size": 512, "heads": 4,
+                  "kv_heads": 2, "seq_length": 256, "vocab_size": 512},
+        "precision": {"params": "bfloat16", "compute": "bfloat16", "grad_reduce": "float32"},
+        "kernels": {"backend": "b200", "fused_tp_comm": fused},
+        "training": {"micro_batch_size": 2, "gradient_accumulation_steps": 2, "seed": 7},
+        "optimizer": {"lr": 1e-3}})
+
+
+def _worker(rank, world, port, out_dir, errq):
+    import traceback
+
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank),
+                          WORLD_SIZE=str(world), LOCAL_RANK=str(rank), NCCL_NVLS_ENABLE="0")
+        from nano_megatron_b200.distributed import DistributedRuntime
+        from nano_megatron_b200.training import Trainer
+        from nano_megatron_b200.training.engine import build_training_components
+
+        g = torch.Generator().manual_seed(5)
+        ids = torch.randint(0, 512, (4, 257), generator=g)
+        batch = {"input_ids": ids[:, :-1].contiguous(), "labels": ids[:, 1:].contiguous()}
+        runtime = DistributedRuntime(_cfg(True).distributed).initialize()
+        results = {}
+        for fused in (False, True):
+            cfg = _cfg(fused)
+            comps = build_training_components(cfg, runtime)
+            assert (getattr(comps.model.model, "tp_workspace", None) is not None) == fused
+            tr = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
+                         data_parallel=comps.data_parallel, rng=comps.rng)
+            micro = tr._prepare_batch(batch)
+            comps.data_parallel.zero_grad()
+            acc = tr.schedule.forward_backward(micro)
+            comps.data_parallel.finalize_gradients()
+            from nano_megatron_b200.training.metrics import aggregate_loss_metrics
+
+            s, c = aggregate_loss_metrics(acc, comps.parallel, runtime.device)
+            grads = {n: p.main_grad.detach().float().cpu().clone()
+                     for n, p in comps.model.named_parameters()}
+            results[fused] = (float(s / c), grads)
+        from nano_megatron_b200.ops._ext import check_status
+
+        check_status(runtime.device)
+        torch.save(results, os.path.join(out_dir, f"r{rank}.pt"))
+        runtime.close()
+    except Exception:  # noqa: BLE001
+        errq.put((rank, traceback.format_exc()))
+        raise
+
+
+def test_fused_tp_matches_nccl_tp(tmp_path):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    import random
+
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = random.randint(20000, 40000)
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, str(tmp_path), errq))
+             for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(300)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    if not errq.empty():
+        r, tb = errq.get()
+        raise AssertionError(f"rank {r} failed:\n{tb}")
+    assert not alive and all(p.exitcode == 0 for p in procs)
+    for r in range(WORLD):
+        res = torch.load(tmp_path / f"r{r}.pt")
+        (l0, g0), (l1, g1) = res[False], res[True]
+        assert abs(l0 - l1) < 2e-2 * abs(l0), (l0, l1)
+        for n in g0:
+            a, b = g0[n], g1[n]
+            rel = ((a - b).norm() / (a.norm() + 1e-12)).item()
+            assert rel < 5e-2, (r, n, rel)
