@@ -21,6 +21,7 @@ write from one background thread, and publish manifest + ``.complete`` in
 
 from __future__ import annotations
 
+import contextlib
 import copy
 import json
 import math
@@ -191,8 +192,10 @@ class CheckpointManager:
         registry = getattr(data_parallel, "parameter_domains", None)
         canon = _canonical(model)
         dtype = _param_dtype(self.run_config)
-        sharded = ShardedState.from_model(canon, parameter_domains=registry,
-                                          parallel=self.parallel, dtype=dtype)
+        full = getattr(data_parallel, "full_parameters", None)
+        with full() if callable(full) else contextlib.nullcontext():
+            sharded = ShardedState.from_model(canon, parameter_domains=registry,
+                                              parallel=self.parallel, dtype=dtype)
         dp_state = data_parallel.state_dict()
         payloads: list[tuple[Any, Path]] = []
         c = self.parallel.coordinate
@@ -341,7 +344,8 @@ class CheckpointManager:
             raise ValueError(f"unsupported checkpoint backend {manifest.storage_backend!r}")
         if not isinstance(model_state, Mapping) or not isinstance(dp_state, Mapping):
             raise ValueError("checkpoint is missing model or data-parallel state")
-        with torch.no_grad():
+        full = getattr(data_parallel, "full_parameters", None)
+        with torch.no_grad(), (full() if callable(full) else contextlib.nullcontext()):
             canon.load_state_dict(dict(model_state))
         data_parallel.load_state_dict(dict(dp_state))
         self._load_runtime(path, manifest, rng)

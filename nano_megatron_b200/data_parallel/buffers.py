@@ -88,7 +88,9 @@ class FlatBuffers:
 
     def __init__(self, named_params: list[tuple[str, nn.Parameter]], *, domains, parallel,
                  bucket_bytes: int, param_dtype: torch.dtype, grad_dtype: torch.dtype,
-                 device: torch.device) -> None:
+                 device: torch.device, unit_key=None) -> None:
+        """``unit_key(name)``: optional; a new bucket also starts whenever it changes, so
+        buckets never straddle two sharding units (ZeRO-3 gathers one unit at a time)."""
         self.param_dtype = param_dtype
         self.grad_dtype = grad_dtype
         self.device = device
@@ -105,12 +107,14 @@ class FlatBuffers:
         layout = []  # (bucket, [(slice, numel)])
         esize = torch.empty((), dtype=param_dtype).element_size()
         for domain, group, items in groups.values():
-            current, cur_bytes = [], 0
+            current, cur_bytes, cur_unit = [], 0, None
             for name, p, placement in items:
                 nbytes = p.numel() * esize
-                if current and cur_bytes + nbytes > bucket_bytes:
+                unit = unit_key(name) if unit_key is not None else None
+                if current and (cur_bytes + nbytes > bucket_bytes or unit != cur_unit):
                     layout.append((domain, group, current))
                     current, cur_bytes = [], 0
+                cur_unit = unit
                 current.append((name, p, placement))
                 cur_bytes += nbytes
             if current:

@@ -22,6 +22,8 @@ B200 design:
 
 from __future__ import annotations
 
+import contextlib
+
 from contextlib import contextmanager
 
 import torch
@@ -121,7 +123,8 @@ class DataParallelStrategy:
         grad_dtype = torch.float64 if model_dtype == torch.float64 else torch.float32
         self.buffers = FlatBuffers(named, domains=self.parameter_domains, parallel=self.parallel,
                                    bucket_bytes=bucket_bytes, param_dtype=model_dtype,
-                                   grad_dtype=grad_dtype, device=device)
+                                   grad_dtype=grad_dtype, device=device,
+                                   unit_key=self._bucket_unit_key())
         self._named = named
         self._ranges = norm_ranges(self.buffers, self.parallel)
         self._sp_slices = [(b, s) for b, s in self.buffers.slices() if s.sequence_parallel_grad]
@@ -132,6 +135,15 @@ class DataParallelStrategy:
         self.overlap = bool(getattr(self.config, "overlap_grad_reduce", False))
         del self._master_init
         return model
+
+    def _bucket_unit_key(self):
+        """Optional name -> unit function forcing bucket cuts at unit boundaries."""
+        return None
+
+    def full_parameters(self):
+        """Context in which every parameter holds its full value (checkpoint I/O, export).
+        Only ZeRO-3 shards parameters; the other strategies always hold them whole."""
+        return contextlib.nullcontext()
 
     def _broadcast_from_replica_root(self, named) -> None:
         g = self.replica_group

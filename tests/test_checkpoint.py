@@ -110,24 +110,27 @@ def test_retention_and_best_validation_pin(tmp_path):
     assert tr.checkpoint.best_validation()["checkpoint"] == paths[0].name
 
 
-def _reshard_save(rank, world, root):
-    cfg = _cfg(root, tp=2, dp=2, mode="zero1")
+def _reshard_save(rank, world, root, mode="zero1"):
+    cfg = _cfg(root, tp=2, dp=2, mode=mode)
     comps, tr = _build(cfg)
     for s in range(2):
         tr.train_step(_local(_batch(s), comps.parallel))
     tr.save_checkpoint()
-    st = {"params": {k: v.clone() for k, v in comps.model.state_dict().items()},
-          "dp": comps.data_parallel.state_dict()}
+    with comps.data_parallel.full_parameters():
+        params = {k: v.clone() for k, v in comps.model.state_dict().items()}
+    st = {"params": params, "dp": comps.data_parallel.state_dict()}
     if comps.parallel.coordinate.dp == 0:
         torch.save(st, os.path.join(root, f"expect_tp{comps.parallel.coordinate.tp}.pt"))
 
 
-def _reshard_load(rank, world, root):
-    cfg = _cfg(root, tp=2, dp=1, mode="zero1")
+def _reshard_load(rank, world, root, mode="zero1"):
+    cfg = _cfg(root, tp=2, dp=1, mode=mode)
     comps, tr = _build(cfg)
     tr.load_checkpoint(tr.checkpoint.latest())
     exp = torch.load(os.path.join(root, f"expect_tp{comps.parallel.coordinate.tp}.pt"))
-    for k, v in comps.model.state_dict().items():
+    with comps.data_parallel.full_parameters():
+        got = {k: v.clone() for k, v in comps.model.state_dict().items()}
+    for k, v in got.items():
         torch.testing.assert_close(v, exp["params"][k], rtol=0, atol=0)
     got = comps.data_parallel.state_dict()
     for b, e in exp["dp"]["buckets"].items():
@@ -138,10 +141,11 @@ def _reshard_load(rank, world, root):
 
 
 @pytest.mark.distributed
-def test_zero1_dp_reshard_gloo(tmp_path):
+@pytest.mark.parametrize("mode", ["zero1", "zero3"])
+def test_zero_dp_reshard_gloo(tmp_path, mode):
     root = str(tmp_path)
-    run_ranks(4, _reshard_save, root)
-    run_ranks(2, _reshard_load, root)
+    run_ranks(4, _reshard_save, root, mode)
+    run_ranks(2, _reshard_load, root, mode)
 
 
 def _failing_save(rank, world, root):

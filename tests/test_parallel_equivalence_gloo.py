@@ -145,6 +145,12 @@ LAYOUTS = {
     "tp2_cp2_sp_ring": ({"parallel": {"tensor": 2, "context": 2, "sequence_parallel": True},
                          "cp": {"backend": "ring"}}, 4),
     "pp2_dp2_zero2": ({"parallel": {"pipeline": 2, "data": 2}, "dp_mode": "zero2"}, 4),
+    "dp2_zero3": ({"parallel": {"data": 2}, "dp_mode": "zero3"}, 2),
+    "tp2_dp2_zero3_sp": ({"parallel": {"tensor": 2, "data": 2, "sequence_parallel": True},
+                          "dp_mode": "zero3"}, 4),
+    "pp2_dp2_zero3_interleaved": ({"parallel": {"pipeline": 2, "data": 2}, "dp_mode": "zero3",
+                                   "pipeline": {"schedule": "interleaved_1f1b",
+                                                "virtual_stages_per_rank": 2}}, 4),
 }
 
 
