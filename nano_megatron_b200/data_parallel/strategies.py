@@ -140,6 +140,11 @@ class DataParallelStrategy:
         """Optional name -> unit function forcing bucket cuts at unit boundaries."""
         return None
 
+    def eager_last_microbatch(self) -> bool:
+        """True when the last microbatch's backward communicates (overlap reducer), so a
+        CUDA-graph schedule must run it eagerly."""
+        return False
+
     def full_parameters(self):
         """Context in which every parameter holds its full value (checkpoint I/O, export).
         Only ZeRO-3 shards parameters; the other strategies always hold them whole."""
@@ -190,16 +195,79 @@ class DataParallelStrategy:
             off += n
 
     def finalize_gradients(self) -> None:
+        # Overlapped bucket reductions finish first: the sequence-parallel norm-gradient
+        # sum over TP below rewrites some of the same gradient memory (the two sums commute).
+        early = self._wait_inflight()
         self._reduce_sequence_parallel_grads()
-        self._reduce_buckets()
+        self._reduce_buckets(skip=early)
         self._reduced = True
 
-    def _reduce_buckets(self) -> None:
+    def _wait_inflight(self) -> set:
+        done = set()
+        for idx, work in getattr(self, "_inflight", {}).items():
+            work.wait()
+            done.add(idx)
+        if hasattr(self, "_inflight"):
+            self._inflight.clear()
+        return done
+
+    def _reduce_buckets(self, skip: set = frozenset()) -> None:
         g = self.replica_group
         if g is None or g.size == 1:
             return
         for b in self.buffers.buckets:
-            dist.all_reduce(b.grad_data, group=g.process_group)
+            if b.index not in skip:
+                dist.all_reduce(b.grad_data, group=g.process_group)
+
+    # ------------------------------------------------------------------ overlap reducer
+    def _overlap_active(self) -> bool:
+        g = self.replica_group
+        return self.overlap and g is not None and g.size > 1
+
+    def _register_overlap_hooks(self, model) -> None:
+        """With ``overlap_grad_reduce``: buckets are cut per transformer layer, and during
+        the last microbatch's backward each layer's buckets start their all-reduce (async,
+        NCCL's stream) as soon as the layer's input gradient exists -- i.e. its weight
+        gradients are final -- overlapping the reduction with the backward of the layers
+        below. Buckets holding a tied parameter, and the embedding/head buckets, reduce in
+        ``finalize_gradients`` (after the tied-embedding gradient sync), as in the
+        reference's reducer (src/nano_megatron/data_parallel/buckets.py:406-525)."""
+        from nano_megatron_b200.models.gpt.model import GPTLayer
+
+        from .zero3 import unit_of_name
+
+        names = {id(p): n for n, p in self._named}
+        by_unit: dict = {}
+        for b in self.buffers.buckets:
+            if b.defer_until_finalize:
+                continue
+            by_unit.setdefault(unit_of_name(names[id(b.slices[0].parameter)]), []).append(b)
+        self._inflight: dict = {}
+        g = self.replica_group
+
+        def launch(key):
+            for b in by_unit.get(key, ()):
+                if b.index not in self._inflight:
+                    self._inflight[b.index] = dist.all_reduce(b.grad_data, group=g.process_group,
+                                                              async_op=True)
+
+        for mod in model.modules():
+            if not isinstance(mod, GPTLayer):
+                continue
+            key = unit_of_name(names[id(next(iter(mod.parameters())))])
+
+            def post(_mod, args, out, key=key):
+                inp = args[0] if args and isinstance(args[0], torch.Tensor) else None
+                if inp is not None and inp.requires_grad and torch.is_grad_enabled():
+                    def done(grad, key=key):
+                        if self._sync_this_backward:
+                            launch(key)
+                        return grad
+
+                    inp.register_hook(done)
+                return out
+
+            mod.register_forward_hook(post)
 
     def _grad_view_for_norm(self) -> tuple[torch.Tensor, list]:
         return self.buffers.grad_flat, self._ranges
@@ -254,6 +322,22 @@ class DDPStrategy(DataParallelStrategy):
     graph_safe_microbatches = True
 
     mode = "ddp"
+
+    def _bucket_unit_key(self):
+        if bool(getattr(self.config, "overlap_grad_reduce", False)):
+            from .zero3 import unit_of_name
+
+            return unit_of_name
+        return None
+
+    def setup(self, model, optimizer_config, parameter_domains=None):
+        super().setup(model, optimizer_config, parameter_domains)
+        if self._overlap_active():
+            self._register_overlap_hooks(model)
+        return model
+
+    def eager_last_microbatch(self) -> bool:
+        return self._overlap_active()
 
     def _init_optimizer_state(self) -> None:
         buf = self.buffers
@@ -355,7 +439,7 @@ class FlatShardZeROStrategy(DataParallelStrategy):
                                 "grad": torch.zeros(b.shard_numel, dtype=buf.grad_dtype,
                                                     device=buf.device)})
 
-    def _reduce_buckets(self) -> None:
+    def _reduce_buckets(self, skip: set = frozenset()) -> None:
         g = self.replica_group
         for b, sh in zip(self.buffers.buckets, self.shards):
             full = b.grad_data[:b.padded_numel]

@@ -22,15 +22,26 @@ class NoPipelineSchedule:
 
         m = len(microbatches)
         keys = [(graph_key(mb), m) for mb in microbatches]
+        if self.data_parallel.eager_last_microbatch():
+            keys[-1] = None
         # Capture every missing shape before running any microbatch: a capture's warm-up
         # zeroes the gradient buffers, which must not erase this step's accumulation.
         for key, mb in zip(keys, microbatches):
-            if key not in self._graphs:
+            if key is not None and key not in self._graphs:
                 device = next(self.stage.parameters()).device
                 g = GraphedMicrobatch(self.stage, self.data_parallel, mb, m, device)
                 g.capture(mb)
                 self._graphs[key] = g
-        for key, mb in zip(keys, microbatches):
+        eager_last = self.data_parallel.eager_last_microbatch()
+        for i, (key, mb) in enumerate(zip(keys, microbatches)):
+            if eager_last and i == m - 1:
+                # the overlap reducer communicates from this backward: not graph-replayable
+                dp = self.data_parallel
+                with dp.forward_microbatch_context(synchronize_gradients=True):
+                    loss = extract_loss(self.stage(None, mb), mb, m, acc)
+                with dp.microbatch_context(is_last_microbatch=True):
+                    dp.backward(loss)
+                continue
             acc.add(self._graphs[key].run(mb).clone(), batch_labels(mb))
 
     def forward_backward(self, microbatches, *, forward_only: bool = False

@@ -36,7 +36,9 @@ def _config(layout: dict):
          "precision": {"params": "float32", "compute": "float32"},
          "distributed": {"device": "cpu", "backend": "gloo"},
          "training": {"micro_batch_size": MB, "gradient_accumulation_steps": GB // (MB * dp)},
-         "data_parallel": {"mode": layout.get("dp_mode", "ddp")},
+         "data_parallel": {"mode": layout.get("dp_mode", "ddp"),
+                           "overlap_grad_reduce": layout.get("dp_overlap", False),
+                           "bucket_bytes": 1 << 14 if layout.get("dp_overlap") else 1 << 28},
          "pipeline": layout.get("pipeline", {}),
          "context_parallel": layout.get("cp", {}),
          "optimizer": {"lr": 1e-3, "clip_grad_norm": None}}
@@ -86,6 +88,8 @@ def _worker(rank, world, layout, full_path, out_dir):
     dp = comps.data_parallel
     dp.zero_grad()
     acc = tr.schedule.forward_backward(micro)
+    if layout.get("dp_overlap"):
+        assert len(getattr(dp, "_inflight", {})) > 0, "overlap reducer launched nothing"
     comps.model.synchronize_tied_embedding_gradients()
     dp.finalize_gradients()
     from nano_megatron_b200.training.metrics import aggregate_loss_metrics
@@ -146,6 +150,9 @@ LAYOUTS = {
                          "cp": {"backend": "ring"}}, 4),
     "pp2_dp2_zero2": ({"parallel": {"pipeline": 2, "data": 2}, "dp_mode": "zero2"}, 4),
     "dp2_zero3": ({"parallel": {"data": 2}, "dp_mode": "zero3"}, 2),
+    "dp2_ddp_overlap": ({"parallel": {"data": 2}, "dp_overlap": True}, 2),
+    "tp2_dp2_ddp_overlap_sp": ({"parallel": {"tensor": 2, "data": 2, "sequence_parallel": True},
+                                "dp_overlap": True}, 4),
     "tp2_dp2_zero3_sp": ({"parallel": {"tensor": 2, "data": 2, "sequence_parallel": True},
                           "dp_mode": "zero3"}, 4),
     "pp2_dp2_zero3_interleaved": ({"parallel": {"pipeline": 2, "data": 2}, "dp_mode": "zero3",
