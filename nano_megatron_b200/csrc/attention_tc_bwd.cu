@@ -34,13 +34,20 @@ constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
 struct Cfg {
+  // D = 64 runs pipelined: Q/dO double-buffered in shared memory and dQ in its own TMEM
+  // columns, so the next step's loads and S^T/dP^T MMAs overlap this step's dQ drain.
+  // D = 128 has neither the shared memory nor the TMEM for that and runs step by step.
+  static constexpr bool kPipe = D == 64;
+  static constexpr int kQStages = kPipe ? 2 : 1;
   static constexpr int kTile = 128 * D * 2;             // one 128-row bf16 tile
   static constexpr int kPTile = kBN * kBM * 2;           // P^T or dS^T
-  static constexpr int kSmem = 4 * kTile + 2 * kPTile + 2 * kBM * 4 + 1024 + 256;
+  static constexpr int kSmem =
+      (2 + 2 * kQStages) * kTile + 2 * kPTile + 2 * kBM * 4 + 1024 + 256;
   static constexpr int kTmemCols = 512;
-  // TMEM columns: S^T [0,128), dP^T [128,256), dQ reuses [0, D); dV [256, 256+D);
-  // dK [256+D, 256+2D).
-  static constexpr int kColS = 0, kColDP = 128, kColDQ = 0, kColDV = 256, kColDK = 256 + D;
+  // TMEM columns: S^T [0,128), dP^T [128,256), dV [256, 256+D), dK [256+D, 256+2D);
+  // dQ at [384, 448) when pipelined (D = 64), else it reuses S^T's [0, D).
+  static constexpr int kColS = 0, kColDP = 128, kColDV = 256, kColDK = 256 + D;
+  static constexpr int kColDQ = kPipe ? 384 : 0;
 };
 
 struct Params {
@@ -106,26 +113,29 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
+  constexpr int QS = C::kQStages;
   uint8_t* sK = smem;
   uint8_t* sV = sK + C::kTile;
-  uint8_t* sQ = sV + C::kTile;
-  uint8_t* sDO = sQ + C::kTile;
-  uint8_t* sP = sDO + C::kTile;
+  uint8_t* sQ0 = sV + C::kTile;                  // QS stages of Q, then QS stages of dO
+  uint8_t* sDO0 = sQ0 + QS * C::kTile;
+  uint8_t* sP = sDO0 + QS * C::kTile;
   uint8_t* sDS = sP + C::kPTile;
   float* sLse = reinterpret_cast<float*>(sDS + C::kPTile);
   float* sDelta = sLse + kBM;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sDelta + kBM);
   uint64_t* kv_full = bars + 0;
-  uint64_t* qdo_full = bars + 1;
-  uint64_t* qdo_empty = bars + 2;
-  uint64_t* sdp_full = bars + 3;   // S^T and dP^T in TMEM
-  uint64_t* pds_full = bars + 4;   // P^T and dS^T in smem (4 warp arrivals)
-  uint64_t* mm_done = bars + 5;    // dV/dK/dQ MMAs of a step complete
-  uint64_t* dq_free = bars + 6;    // dQ drained from TMEM (4 warp arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  uint64_t* qdo_full = bars + 1;   // [QS]
+  uint64_t* qdo_empty = bars + 3;  // [QS]
+  uint64_t* sdp_full = bars + 5;   // S^T and dP^T in TMEM
+  uint64_t* pds_full = bars + 6;   // P^T and dS^T in smem (4 warp arrivals)
+  uint64_t* mm_done = bars + 7;    // dV/dK/dQ MMAs of a step complete
+  uint64_t* dq_free = bars + 8;    // dQ drained from TMEM (4 warp arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
-  const int nb = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+  // Key block is the slowest grid index: the (causally) longest CTAs, key block 0,
+  // start first, which shortens the tail of the launch.
+  const int nb = blockIdx.y, kvh = blockIdx.x % p.Hkv, b = blockIdx.x / p.Hkv;
   const int group = p.Hq / p.Hkv;
   const int n0 = nb * kBN;
   const int warp = threadIdx.x / 32;
@@ -136,7 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int total_steps = steps_per_head * group;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 7; ++i) mbar_init(&bars[i], (i == 4 || i == 6) ? 4 : 1);
+    for (int i = 0; i < 9; ++i) mbar_init(&bars[i], (i == 6 || i == 8) ? 4 : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -165,12 +175,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = 0; t < total_steps; ++t) {
         const int h = kvh * group + t / steps_per_head;
         const int m0 = (m_begin + t % steps_per_head) * kBM;
-        if (!mbar_wait(qdo_empty, (t & 1) ^ 1u, p.status, kStatusAttnTimeout, abort_flag)) break;
-        mbar_arrive_expect_tx(qdo_full, 2 * C::kTile);
+        const int st = t % QS;
+        const uint32_t ph = static_cast<uint32_t>(t / QS) & 1u;
+        if (!mbar_wait(&qdo_empty[st], ph ^ 1u, p.status, kStatusAttnTimeout, abort_flag)) break;
+        mbar_arrive_expect_tx(&qdo_full[st], 2 * C::kTile);
+        uint8_t* sQ = sQ0 + st * C::kTile;
+        uint8_t* sDO = sDO0 + st * C::kTile;
 #pragma unroll
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(sQ + c * 128 * 128, &tmQ, qdo_full, c * 64, h, m0, b);
-          tma_load_4d(sDO + c * 128 * 128, &tmDO, qdo_full, c * 64, h, m0, b);
+          tma_load_4d(sQ + c * 128 * 128, &tmQ, &qdo_full[st], c * 64, h, m0, b);
+          tma_load_4d(sDO + c * 128 * 128, &tmDO, &qdo_full[st], c * 64, h, m0, b);
         }
       }
     }
@@ -181,12 +195,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t id_acc = umma_idesc_bf16(kBN, D, false, true);   // dV, dK
       constexpr uint32_t id_dq = umma_idesc_bf16(kBM, D, true, true);     // dQ
       bool ok = mbar_wait(kv_full, 0, p.status, kStatusAttnTimeout, abort_flag);
-      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aQ = smem_u32(sQ),
-                     aDO = smem_u32(sDO), aP = smem_u32(sP), aDS = smem_u32(sDS);
+      const uint32_t aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP),
+                     aDS = smem_u32(sDS);
       for (int t = 0; t < total_steps && ok; ++t) {
-        ok = mbar_wait(qdo_full, t & 1, p.status, kStatusAttnTimeout, abort_flag);
-        if (ok && t > 0) ok = mbar_wait(dq_free, (t - 1) & 1, p.status, kStatusAttnTimeout,
-                                        abort_flag);
+        const int st = t % QS;
+        const uint32_t aQ = smem_u32(sQ0 + st * C::kTile), aDO = smem_u32(sDO0 + st * C::kTile);
+        ok = mbar_wait(&qdo_full[st], static_cast<uint32_t>(t / QS) & 1u, p.status,
+                       kStatusAttnTimeout, abort_flag);
+        // Unpipelined: S^T shares TMEM with the previous step's dQ, which must be drained.
+        if (ok && !C::kPipe && t > 0)
+          ok = mbar_wait(dq_free, (t - 1) & 1, p.status, kStatusAttnTimeout, abort_flag);
         if (!ok) break;
         tc_fence_after();
         // S^T = K Q^T ; dP^T = V dO^T   (M = keys, N = queries, K = D)
@@ -200,6 +218,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         umma_commit(sdp_full);
         ok = mbar_wait(pds_full, t & 1, p.status, kStatusAttnTimeout, abort_flag);
+        // Pipelined: the previous dQ (own columns) must be drained before this step's dQ.
+        if (ok && C::kPipe && t > 0)
+          ok = mbar_wait(dq_free, (t - 1) & 1, p.status, kStatusAttnTimeout, abort_flag);
         if (!ok) break;
         tc_fence_after();
         // dV += P^T dO ; dK += dS^T Q     (M = keys, N = D, K = queries)
@@ -220,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                       umma_desc_sw128(aK + off, 128 * 128, 1024), id_dq, kk > 0);
         }
         umma_commit(mm_done);
-        umma_commit(qdo_empty);
+        umma_commit(&qdo_empty[st]);
       }
     }
   } else {
@@ -464,7 +485,8 @@ void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor d
   ensure_current_context(q.device().index());
   CUtensorMap mq = make_map(q), mk = make_map(k), mv = make_map(v), mdo = make_map(dout);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  dim3 grid((p.Sk + kBN - 1) / kBN, p.Hkv, p.B);
+  TORCH_CHECK(static_cast<int64_t>(p.Hkv) * p.B < (1ll << 31) && (p.Sk + kBN - 1) / kBN < 65536);
+  dim3 grid(p.Hkv * p.B, (p.Sk + kBN - 1) / kBN, 1);
   if (D == 64) {
     static bool set = false;
     if (!set) {

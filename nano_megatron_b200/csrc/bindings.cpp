@@ -8,7 +8,7 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
              double beta, c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
              c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
              int64_t head_dim, int64_t rope_cols, int64_t pos_div, at::Tensor status,
-             int64_t bn_override, int64_t max_ctas);
+             int64_t bn_override, int64_t max_ctas, c10::optional<at::Tensor> rope_cs);
 void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
                     double softmax_scale, bool causal, int64_t q_offset, int64_t k_offset);
 void flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor dout,
@@ -50,7 +50,8 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda
                 c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
                 c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
                 int64_t head_dim, int64_t rope_cols, int64_t pos_div, int64_t rank,
-                int64_t flags_ptr, int64_t epoch, at::Tensor status);
+                int64_t flags_ptr, int64_t epoch, at::Tensor status,
+                c10::optional<at::Tensor> rope_cs);
 void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
                 std::vector<int64_t> staging_ptrs, int64_t rows_per_rank, int64_t n_out,
                 int64_t rank, at::Tensor status);
@@ -64,7 +65,12 @@ void scale_inplace(at::Tensor x, double s);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nano_megatron_b200 sm_100a kernels (tcgen05 GEMM, flash attention, fused ops)";
-  m.def("gemm_tc", &gemm_tc, "tcgen05 GEMM with fused epilogues");
+  m.def("gemm_tc", &gemm_tc, "tcgen05 GEMM with fused epilogues", py::arg("a"), py::arg("a_mn"),
+        py::arg("b"), py::arg("b_mn"), py::arg("c"), py::arg("epi"), py::arg("residual"),
+        py::arg("alpha_t"), py::arg("alpha"), py::arg("beta"), py::arg("aux"),
+        py::arg("swiglu_up_row"), py::arg("positions"), py::arg("inv_freq"), py::arg("head_dim"),
+        py::arg("rope_cols"), py::arg("pos_div"), py::arg("status"), py::arg("bn_override"),
+        py::arg("max_ctas"), py::arg("rope_cs") = py::none());
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
   m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc, "tcgen05/TMEM causal flash attention forward");
@@ -84,7 +90,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &adamw_step);
   m.def("sumsq_partials", &sumsq_partials);
   m.def("scale_inplace", &scale_inplace);
-  m.def("gemm_tc_ag", &gemm_tc_ag, "AG->GEMM: A rows gathered from TP peers' symmetric shards");
+  m.def("gemm_tc_ag", &gemm_tc_ag, "AG->GEMM: A rows gathered from TP peers' symmetric shards",
+        py::arg("a_local"), py::arg("shard_ptrs"), py::arg("lda"), py::arg("b"), py::arg("b_mn"),
+        py::arg("c"), py::arg("epi"), py::arg("xfull"), py::arg("aux"), py::arg("swiglu_up_row"),
+        py::arg("positions"), py::arg("inv_freq"), py::arg("head_dim"), py::arg("rope_cols"),
+        py::arg("pos_div"), py::arg("rank"), py::arg("flags_ptr"), py::arg("epoch"),
+        py::arg("status"), py::arg("rope_cs") = py::none());
   m.def("gemm_tc_rs", &gemm_tc_rs, "GEMM->RS: partial tiles stored into the owner's staging");
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);

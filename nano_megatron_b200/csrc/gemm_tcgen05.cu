@@ -79,6 +79,8 @@ struct GemmParams {
   int m_rotate;                         // gather: first M tile (own rows first)
   int store_gathered;                   // gather: TMA-store A tiles into `xfull`
   __nv_bfloat16* peer_out[kMaxTP];      // peer epilogue: staging base of each rank
+  int splits;                           // split-K factor (kEpiF32Acc with beta = 1 only)
+  const float2* rope_cs;                // kEpiRoPE: (cos, sin) table [seq_len][head_dim / 2]
 };
 
 // Per-rank tensor maps of the gathered A operand and of the local gathered copy.
@@ -125,12 +127,32 @@ __device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, int col, in
   }
 }
 
+// Work item t -> output tile (m0, nt) and K-split ks. Splits are the slowest index so the
+// concurrently running CTAs of one split share A/B panels in L2.
 template <bool GATHER>
-__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& m0, int& nt) {
+__device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& m0, int& nt,
+                                            int& ks) {
+  const int per_split = p.num_m_tiles * p.num_n_tiles;
+  ks = t / per_split;
+  t -= ks * per_split;
   int mt = t % p.num_m_tiles;
   if constexpr (GATHER) mt = (mt + p.m_rotate) % p.num_m_tiles;
   m0 = mt * kBM;
   nt = t / p.num_m_tiles;
+}
+
+__device__ __forceinline__ void split_range(const GemmParams& p, int num_kb, int ks, int& kb0,
+                                            int& kb1) {
+  const int per = (num_kb + p.splits - 1) / p.splits;
+  kb0 = ks * per;
+  kb1 = min(num_kb, kb0 + per);
+}
+
+// Vectorised fp32 atomic add (sm_90+): out[0..3] += v (16-byte aligned).
+__device__ __forceinline__ void red_add_v4(float* out, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(out), "f"(a), "f"(b),
+               "f"(c), "f"(d)
+               : "memory");
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER>
@@ -153,7 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32;
-  const int num_tiles = p.num_m_tiles * p.num_n_tiles;
+  const int num_tiles = p.num_m_tiles * p.num_n_tiles * p.splits;
   const int num_kb = (p.K + kBK - 1) / kBK;
 
   if (threadIdx.x == 0) {
@@ -187,8 +209,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       bool ok = true;
       uint32_t ready = GATHER ? (1u << p.comm_rank) : 0u;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        int m0, nt;
-        tile_coords<GATHER>(t, p, m0, nt);
+        int m0, nt, ks, kb0, kb1;
+        tile_coords<GATHER>(t, p, m0, nt, ks);
+        split_range(p, num_kb, ks, kb0, kb1);
         int owner = 0;
         if constexpr (GATHER) {
           owner = m0 / p.comm_rows;
@@ -202,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ready |= 1u << owner;
           }
         }
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1u, p.status, kStatusGemmProducerTimeout,
                          abort_flag)) {
             ok = false;
@@ -256,10 +279,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + acc * BN;
-        int m0 = 0, nt = 0;
-        tile_coords<GATHER>(t, p, m0, nt);
+        int m0 = 0, nt = 0, ks = 0, kb0 = 0, kb1 = 0;
+        tile_coords<GATHER>(t, p, m0, nt, ks);
+        split_range(p, num_kb, ks, kb0, kb1);
         const bool store_a = GATHER && p.store_gathered && nt == 0;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full_bar[stage], phase, p.status, kStatusGemmMmaTimeout, abort_flag)) {
             ok = false;
             break;
@@ -282,7 +306,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               bdesc = umma_desc_sw128(b_addr + kk * 32, 16, 1024);
             else
               bdesc = umma_desc_sw128(b_addr + kk * 2048, kBK * 128, 1024);
-            umma_f16_ss(tmem_d, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            umma_f16_ss(tmem_d, adesc, bdesc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           if (store_a) tma_store_wait_read();  // the stage is refilled once released
           umma_commit(&empty_bar[stage]);
@@ -308,8 +332,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                      abort_flag))
         break;
       tc_fence_after();
-      int m0, nt;
-      tile_coords<GATHER>(t, p, m0, nt);
+      int m0, nt, ks;
+      tile_coords<GATHER>(t, p, m0, nt, ks);
       const int row = m0 + quarter * 32 + lane;
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
@@ -346,7 +370,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                              col, p.N, v);
           } else {
             float* cp = reinterpret_cast<float*>(p.C) + static_cast<int64_t>(row) * p.ldc + col;
-            if (col + 32 <= p.N) {
+            if (p.splits > 1) {  // split-K partial sums: accumulate in L2 with atomics
+              if (col + 32 <= p.N && (reinterpret_cast<uintptr_t>(cp) & 15u) == 0) {
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                  red_add_v4(cp + 4 * q, v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+              } else {
+                for (int j = 0; j < 32; ++j)
+                  if (col + j < p.N) atomicAdd(cp + j, v[j]);
+              }
+            } else if (col + 32 <= p.N) {
               float4* c4 = reinterpret_cast<float4*>(cp);
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
@@ -398,7 +431,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int D = p.head_dim;
         const int half_chunks = D / 64;  // 32-col chunks per half head
         const int chunks_per_head = D / 32;
-        const int pos = row_ok ? __ldg(p.positions + ((row / p.pos_div) % p.seq_len)) : 0;
+        const int slot = row_ok ? (row / p.pos_div) % p.seq_len : 0;
+        const int pos = row_ok ? __ldg(p.positions + slot) : 0;
 #pragma unroll 1
         for (int h = 0; h < BN / D; ++h) {
 #pragma unroll 1
@@ -419,14 +453,30 @@ __global__ void __launch_bounds__(kThreads, 1)
               b[e] = __uint_as_float(hi[e]) * alpha;
             }
             if (col_lo < p.rope_cols) {
+              if (p.rope_cs != nullptr) {  // precomputed (cos, sin) of this row's slot
+                const float4* cs4 = reinterpret_cast<const float4*>(
+                    p.rope_cs + static_cast<int64_t>(slot) * (D / 2) + j * 32);
+#pragma unroll
+                for (int e = 0; e < 32; e += 2) {
+                  const float4 c = __ldg(cs4 + e / 2);  // (cos_e, sin_e, cos_e+1, sin_e+1)
+                  float x1 = a[e], x2 = b[e];
+                  a[e] = x1 * c.x - x2 * c.y;
+                  b[e] = x2 * c.x + x1 * c.y;
+                  x1 = a[e + 1];
+                  x2 = b[e + 1];
+                  a[e + 1] = x1 * c.z - x2 * c.w;
+                  b[e + 1] = x2 * c.z + x1 * c.w;
+                }
+              } else {
 #pragma unroll 4
-              for (int e = 0; e < 32; ++e) {
-                const float ang = static_cast<float>(pos) * __ldg(p.inv_freq + j * 32 + e);
-                float sn, cs;
-                sincosf(ang, &sn, &cs);
-                const float x1 = a[e], x2 = b[e];
-                a[e] = x1 * cs - x2 * sn;
-                b[e] = x2 * cs + x1 * sn;
+                for (int e = 0; e < 32; ++e) {
+                  const float ang = static_cast<float>(pos) * __ldg(p.inv_freq + j * 32 + e);
+                  float sn, cs;
+                  sincosf(ang, &sn, &cs);
+                  const float x1 = a[e], x2 = b[e];
+                  a[e] = x1 * cs - x2 * sn;
+                  b[e] = x2 * cs + x1 * sn;
+                }
               }
             }
             __nv_bfloat16* crow =
@@ -505,7 +555,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
     attr_set = true;
   }
-  const int tiles = p.num_m_tiles * p.num_n_tiles;
+  const int tiles = p.num_m_tiles * p.num_n_tiles * p.splits;
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
   kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, cm, p); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
@@ -531,13 +581,34 @@ static void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, Ge
     launch<128, A_MN, B_MN, EPI, GATHER>(ta, tb, p, s, max_ctas, cm);
 }
 
-// Pick the N tile: 256 when it still leaves roughly a full wave of tiles.
+// Split-K factor for an fp32-accumulating GEMM: the smallest split (<= 8, >= 4 K-blocks
+// each) that fills the SMs' waves clearly better than no split.
+static int choose_splits(int tiles, int num_kb) {
+  const int sms = num_sms();
+  auto eff = [&](int s) {
+    const int work = tiles * s;
+    return static_cast<double>(work) / (static_cast<double>((work + sms - 1) / sms) * sms);
+  };
+  int best = 1;
+  double best_eff = eff(1);
+  for (int s = 2; s <= 8 && num_kb / s >= 4; ++s) {
+    if (eff(s) > best_eff + 0.05) {
+      best = s;
+      best_eff = eff(s);
+    }
+  }
+  return best;
+}
+
+// Pick the N tile. Measured on B200 (bf16 out, M = 4096, N in 1024..8192, K in 1024..2736):
+// 128 x 256 tiles beat 128 x 128 tiles at every shape (the MMA issues twice the work per
+// instruction for the same A traffic), even when that leaves part of the last wave idle.
+// fp32-accumulating weight-gradient GEMMs use 128 x 128 tiles plus split-K instead.
 static int choose_bn(int M, int N, int epi) {
+  (void)M;
   if (epi == kEpiSwiGLU) return 256;
-  const int mt = (M + kBM - 1) / kBM;
-  const int tiles256 = mt * ((N + 255) / 256);
-  if (N % 256 != 0 && N <= 128) return 128;
-  return tiles256 >= num_sms() * 0.9 ? 256 : 128;
+  if (epi == kEpiF32Acc) return 128;
+  return N > 128 ? 256 : 128;
 }
 
 }  // namespace nmb
@@ -553,7 +624,7 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
              double beta, c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
              c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
              int64_t head_dim, int64_t rope_cols, int64_t pos_div, at::Tensor status,
-             int64_t bn_override, int64_t max_ctas) {
+             int64_t bn_override, int64_t max_ctas, c10::optional<at::Tensor> rope_cs) {
   check_operand(a, "A");
   check_operand(b, "B");
   const int64_t M = a_mn ? a.size(1) : a.size(0);
@@ -571,6 +642,7 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
   p.alpha = static_cast<float>(alpha);
   p.beta = static_cast<float>(beta);
   p.status = status.data_ptr<int>();
+  p.splits = 1;
   if (residual.has_value()) {
     TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->stride(1) == 1);
     p.R = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
@@ -604,6 +676,17 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
     p.head_dim = static_cast<int>(head_dim);
     p.rope_cols = static_cast<int>(rope_cols);
     TORCH_CHECK(rope_cols % head_dim == 0 && N % head_dim == 0);
+    if (rope_cs.has_value()) {
+      TORCH_CHECK(rope_cs->scalar_type() == at::kFloat && rope_cs->is_contiguous() &&
+                      rope_cs->numel() == positions->numel() * head_dim,
+                  "rope table must be fp32 [seq_len, head_dim/2, 2]");
+      p.rope_cs = reinterpret_cast<const float2*>(rope_cs->data_ptr<float>());
+    }
+  }
+  if (epi == kEpiF32Acc && beta == 1.0) {
+    bn = bn_override > 0 ? static_cast<int>(bn_override) : 128;
+    const int tiles = static_cast<int>(((M + kBM - 1) / kBM) * ((N + bn - 1) / bn));
+    p.splits = choose_splits(tiles, static_cast<int>((K + kBK - 1) / kBK));
   }
   const int out_cols_per_tile = epi == kEpiSwiGLU ? bn / 2 : bn;
   p.num_m_tiles = static_cast<int>((M + kBM - 1) / kBM);
@@ -652,7 +735,8 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda
                 c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
                 c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
                 int64_t head_dim, int64_t rope_cols, int64_t pos_div, int64_t rank,
-                int64_t flags_ptr, int64_t epoch, at::Tensor status) {
+                int64_t flags_ptr, int64_t epoch, at::Tensor status,
+                c10::optional<at::Tensor> rope_cs) {
   check_operand(a_local, "A shard");
   check_operand(b, "B");
   const int tp = static_cast<int>(shard_ptrs.size());
@@ -681,6 +765,7 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda
   p.flags = reinterpret_cast<const uint32_t*>(flags_ptr);
   p.epoch = static_cast<uint32_t>(epoch);
   p.m_rotate = static_cast<int>(rank * (R / kBM));
+  p.splits = 1;
   int bn = choose_bn(p.M, p.N, epi);
   if (epi == kEpiSwiGLU) {
     TORCH_CHECK(!b_mn && aux.has_value());
@@ -697,6 +782,11 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda
     p.inv_freq = inv_freq->data_ptr<float>();
     p.head_dim = static_cast<int>(head_dim);
     p.rope_cols = static_cast<int>(rope_cols);
+    if (rope_cs.has_value()) {
+      TORCH_CHECK(rope_cs->scalar_type() == at::kFloat && rope_cs->is_contiguous() &&
+                  rope_cs->numel() == positions->numel() * head_dim);
+      p.rope_cs = reinterpret_cast<const float2*>(rope_cs->data_ptr<float>());
+    }
   } else {
     TORCH_CHECK(epi == kEpiBF16, "gemm_tc_ag: epilogue must be bf16, RoPE or SwiGLU");
   }
@@ -757,6 +847,7 @@ void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
   p.comm_rows = static_cast<int>(rows_per_rank);
   p.comm_rank = static_cast<int>(rank);
   p.comm_size = tp;
+  p.splits = 1;
   for (int r = 0; r < tp; ++r)
     p.peer_out[r] = reinterpret_cast<__nv_bfloat16*>(staging_ptrs[r]);
   const int bn = choose_bn(p.M, p.N, kEpiPeer);

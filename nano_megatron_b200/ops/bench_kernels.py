@@ -50,6 +50,19 @@ def gemm_cases(iters: int) -> dict:
         res[f"wgrad_{m}x{n}x{k}"] = fl / _time(
             lambda: G.gemm(at, bt, cf, a_mn=True, b_mn=True, epilogue=G.EPI_F32_ACC, beta=1.0),
             iters) / 1e9
+    # weight gradients of the 311M layers: dW[N_out, K_in] = dY^T X over 4096 tokens
+    for m, n, k in [(1024, 1024, 4096), (3072, 1024, 4096), (5472, 1024, 4096),
+                    (1024, 2736, 4096)]:
+        dy = torch.randn(k, m, device="cuda").bfloat16()
+        x = torch.randn(k, n, device="cuda").bfloat16()
+        cf = torch.zeros(m, n, device="cuda")
+        cb = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        fl = 2 * m * n * k
+        res[f"wgrad_model_{m}x{n}x{k}"] = fl / _time(
+            lambda: G.gemm(dy, x, cf, a_mn=True, b_mn=True, epilogue=G.EPI_F32_ACC, beta=1.0),
+            iters) / 1e9
+        res[f"cublas_wgrad_{m}x{n}x{k}"] = fl / _time(
+            lambda: torch.matmul(dy.t(), x, out=cb), iters) / 1e9
     return res
 
 

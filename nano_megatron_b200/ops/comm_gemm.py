@@ -74,9 +74,15 @@ def ag_finish(ws, epoch: int, x_local: torch.Tensor, b: torch.Tensor, out: torch
               head_dim: int = 0, rope_cols: int = 0, pos_div: int = 1,
               channel: int = CH_AG) -> None:
     R, K = x_local.shape
+    table = None
+    if epi == "rope":
+        from .gemm import rope_table
+
+        table = rope_table(positions, inv_freq)
     lib().gemm_tc_ag(x_local, [ws.ag_shard(r, epoch) for r in range(ws.size)], K, b, b_mn, out,
                      EPI[epi], xfull, aux, swiglu_up_row, positions, inv_freq, head_dim,
-                     rope_cols, pos_div, ws.rank, ws.flags(ws.rank, channel), epoch, ws.status)
+                     rope_cols, pos_div, ws.rank, ws.flags(ws.rank, channel), epoch, ws.status,
+                     table)
 
 
 def allgather_gemm(ws, x_local: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,

@@ -42,13 +42,35 @@ def gemm(
     pos_div: int = 1,
     block_n: int = 0,
     max_ctas: int = 0,
+    rope_cs: torch.Tensor | None = None,
 ) -> torch.Tensor:
     lib().gemm_tc(
         a, a_mn, b, b_mn, out, epilogue, residual, alpha_t, float(alpha), float(beta), aux,
         int(swiglu_up_row), positions, inv_freq, int(head_dim), int(rope_cols), int(pos_div),
-        status_word(a.device), int(block_n), int(max_ctas),
+        status_word(a.device), int(block_n), int(max_ctas), rope_cs,
     )
     return out
+
+
+_ROPE_TABLES: dict = {}
+
+
+def rope_table(positions: torch.Tensor, inv_freq: torch.Tensor) -> torch.Tensor:
+    """fp32 ``[len(positions), D/2, 2]`` table of (cos, sin)(position * inv_freq).
+
+    Built once per positions tensor (the model caches those per sequence layout) and
+    kept with a reference to it, so its address cannot be reused by another tensor
+    while the entry lives."""
+    key = (positions.data_ptr(), positions.numel(), inv_freq.data_ptr(), positions.device)
+    hit = _ROPE_TABLES.get(key)
+    if hit is not None:
+        return hit[2]
+    ang = positions.to(torch.float32)[:, None] * inv_freq.to(torch.float32)[None, :]
+    table = torch.stack([torch.cos(ang), torch.sin(ang)], dim=-1).contiguous()
+    if len(_ROPE_TABLES) >= 64:
+        _ROPE_TABLES.pop(next(iter(_ROPE_TABLES)))
+    _ROPE_TABLES[key] = (positions, inv_freq, table)
+    return table
 
 
 def linear_fwd(x: torch.Tensor, weight: torch.Tensor, *, residual: torch.Tensor | None = None,
@@ -96,4 +118,5 @@ def qkv_rope_fwd(x: torch.Tensor, w_qkv: torch.Tensor, positions: torch.Tensor,
     if out is None:
         out = torch.empty(x.shape[0], w_qkv.shape[0], device=x.device, dtype=torch.bfloat16)
     return gemm(x, w_qkv, out, epilogue=EPI_ROPE, positions=positions, inv_freq=inv_freq,
-                head_dim=head_dim, rope_cols=rope_cols, pos_div=pos_div)
+                head_dim=head_dim, rope_cols=rope_cols, pos_div=pos_div,
+                rope_cs=rope_table(positions, inv_freq))
