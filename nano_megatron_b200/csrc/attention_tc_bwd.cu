@@ -92,6 +92,20 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                : "memory");
 }
 
+// Write 32 bf16 values (16 packed pairs) = columns [32c, 32c+32) of row `row` into a
+// [128 rows x 128 cols] SW128 tile (two 64-column swizzle atoms).
+__device__ __forceinline__ void store_chunk_sw128(uint8_t* tile, int row, int c,
+                                                  const uint32_t* pk) {
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int ch = c * 4 + q;
+    const int atom = ch >> 3, c8 = ch & 7;
+    uint8_t* dst = tile + atom * (128 * 128) + row * 128 + ((c8 ^ (row & 7)) << 4);
+    *reinterpret_cast<uint4*>(dst) = make_uint4(pk[q * 4], pk[q * 4 + 1], pk[q * 4 + 2],
+                                                pk[q * 4 + 3]);
+  }
+}
+
 // Write a 128-value bf16 row (packed pairs) into a [128 rows x 128 cols] SW128 tile.
 __device__ __forceinline__ void store_row_sw128(uint8_t* tile, int row, const uint32_t* pk) {
 #pragma unroll
@@ -276,13 +290,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       const bool diag = p.causal && (p.k_offset + n0 + kBN - 1 > p.q_offset + m0);
       const bool tail = (m0 + kBM > p.Sq) || (n0 + kBN > p.Sk);
-      uint32_t ppk[kBM / 2], dpk[kBM / 2];
-#pragma unroll
+      // One 32-query chunk at a time: exponentiate, form dS, and store both bf16 chunks
+      // straight into the swizzled P^T / dS^T tiles (keeps register pressure low).
+#pragma unroll 1
       for (int c = 0; c < kBM / 32; ++c) {
         uint32_t sr[32], dr[32];
         tmem_ld_32x32b_x32(tmem + lo + C::kColS + c * 32, sr);
         tmem_ld_32x32b_x32(tmem + lo + C::kColDP + c * 32, dr);
         tmem_wait_ld();
+        uint32_t ppk[16], dpk[16];
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
           float pv[2], dsv[2];
@@ -296,12 +312,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             pv[u] = pr;
             dsv[u] = pr * (__uint_as_float(dr[e + u]) - sDelta[qc]);
           }
-          ppk[(c * 32 + e) / 2] = pack_bf16x2(pv[0], pv[1]);
-          dpk[(c * 32 + e) / 2] = pack_bf16x2(dsv[0], dsv[1]);
+          ppk[e / 2] = pack_bf16x2(pv[0], pv[1]);
+          dpk[e / 2] = pack_bf16x2(dsv[0], dsv[1]);
         }
+        store_chunk_sw128(sP, row, c, ppk);
+        store_chunk_sw128(sDS, row, c, dpk);
       }
-      store_row_sw128(sP, row, ppk);
-      store_row_sw128(sDS, row, dpk);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();

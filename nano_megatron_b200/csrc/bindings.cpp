@@ -62,6 +62,7 @@ void peer_signal(std::vector<int64_t> targets, int64_t epoch);
 void rs_reduce(int64_t staging_ptr, int64_t tp, at::Tensor out, c10::optional<at::Tensor> residual,
                int64_t flags_ptr, int64_t epoch, at::Tensor status);
 void scale_inplace(at::Tensor x, double s);
+void dropout_apply(at::Tensor x, at::Tensor y, double p, int64_t seed);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nano_megatron_b200 sm_100a kernels (tcgen05 GEMM, flash attention, fused ops)";
@@ -90,6 +91,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &adamw_step);
   m.def("sumsq_partials", &sumsq_partials);
   m.def("scale_inplace", &scale_inplace);
+  m.def("dropout_apply", &dropout_apply, "counter-based (Philox-4x32-10) dropout, mask = f(seed, index)");
   m.def("gemm_tc_ag", &gemm_tc_ag, "AG->GEMM: A rows gathered from TP peers' symmetric shards",
         py::arg("a_local"), py::arg("shard_ptrs"), py::arg("lda"), py::arg("b"), py::arg("b_mn"),
         py::arg("c"), py::arg("epi"), py::arg("xfull"), py::arg("aux"), py::arg("swiglu_up_row"),

@@ -88,58 +88,101 @@ __global__ void rmsnorm_bwd_kernel(const __nv_bfloat16* __restrict__ x, int64_t 
   __syncthreads();
   const int lane = threadIdx.x & 31;
   const int warps = blockDim.x / 32;
-  float wf[NCH][8];
-  float dwacc[NCH][8];
+  // Narrow rows keep the weight in registers; wide rows re-read it (L1) to save registers.
+  constexpr int WREG = NCH <= 4 ? NCH : 1;
+  float wf[WREG][8];
+  float dwacc[WREG][8];  // wide rows accumulate the weight gradient in shared memory
   const uint4* wr = reinterpret_cast<const uint4*>(w);
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
-    unpack8(wr[c * 32 + lane], wf[c]);
+    if constexpr (NCH <= 4) {
+      unpack8(wr[c * 32 + lane], wf[c]);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) dwacc[c][e] = 0.f;
+      for (int e = 0; e < 8; ++e) dwacc[c][e] = 0.f;
+    }
   }
   for (int row = blockIdx.x * warps + threadIdx.x / 32; row < rows; row += gridDim.x * warps) {
     const uint4* xr = reinterpret_cast<const uint4*>(x + static_cast<int64_t>(row) * ldx);
     const uint4* gr = reinterpret_cast<const uint4*>(dy + static_cast<int64_t>(row) * lddy);
     const float r = rstd[row];
-    float xh[NCH][8], wg[NCH][8];
-    float dot = 0.f;
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      float xv[8], gv[8];
-      unpack8(xr[c * 32 + lane], xv);
-      unpack8(gr[c * 32 + lane], gv);
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        xh[c][e] = xv[e] * r;
-        wg[c][e] = wf[c][e] * gv[e];
-        dot += xh[c][e] * wg[c][e];
-        dwacc[c][e] += gv[e] * round_bf16(xh[c][e]);
-      }
-    }
-    dot = warp_sum(dot) / static_cast<float>(H);
     uint4* dr = reinterpret_cast<uint4*>(dx + static_cast<int64_t>(row) * lddx);
     const uint4* rr =
         dres != nullptr ? reinterpret_cast<const uint4*>(dres + static_cast<int64_t>(row) * lddres)
                         : nullptr;
+    if constexpr (NCH <= 4) {
+      // Narrow rows: keep x_hat and w*dy of the row in registers between the two sweeps.
+      float xh[NCH][8], wg[NCH][8];
+      float dot = 0.f;
 #pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      float o[8];
+      for (int c = 0; c < NCH; ++c) {
+        float xv[8], gv[8];
+        unpack8(xr[c * 32 + lane], xv);
+        unpack8(gr[c * 32 + lane], gv);
 #pragma unroll
-      for (int e = 0; e < 8; ++e) o[e] = r * (wg[c][e] - xh[c][e] * dot);
-      if (rr != nullptr) {
-        float rv[8];
-        unpack8(rr[c * 32 + lane], rv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) o[e] += rv[e];
+        for (int e = 0; e < 8; ++e) {
+          xh[c][e] = xv[e] * r;
+          wg[c][e] = wf[c][e] * gv[e];
+          dot += xh[c][e] * wg[c][e];
+          dwacc[c][e] += gv[e] * round_bf16(xh[c][e]);
+        }
       }
-      dr[c * 32 + lane] = pack8(o);
+      dot = warp_sum(dot) / static_cast<float>(H);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        float o[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = r * (wg[c][e] - xh[c][e] * dot);
+        if (rr != nullptr) {
+          float rv[8];
+          unpack8(rr[c * 32 + lane], rv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] += rv[e];
+        }
+        dr[c * 32 + lane] = pack8(o);
+      }
+    } else {
+      // Wide rows (H >= 2048): two sweeps re-reading x and dy (L1-resident) so only the
+      // weight-gradient accumulators stay live across the row.
+      float dot = 0.f;
+#pragma unroll 4
+      for (int c = 0; c < NCH; ++c) {
+        float xv[8], gv[8], wv[8];
+        unpack8(xr[c * 32 + lane], xv);
+        unpack8(gr[c * 32 + lane], gv);
+        unpack8(wr[c * 32 + lane], wv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float xhv = xv[e] * r;
+          dot += xhv * (wv[e] * gv[e]);
+          if (dw != nullptr) atomicAdd(&sdw[(c * 32 + lane) * 8 + e], gv[e] * round_bf16(xhv));
+        }
+      }
+      dot = warp_sum(dot) / static_cast<float>(H);
+#pragma unroll 4
+      for (int c = 0; c < NCH; ++c) {
+        float xv[8], gv[8], wv[8], o[8];
+        unpack8(xr[c * 32 + lane], xv);
+        unpack8(gr[c * 32 + lane], gv);
+        unpack8(wr[c * 32 + lane], wv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) o[e] = r * (wv[e] * gv[e] - xv[e] * r * dot);
+        if (rr != nullptr) {
+          float rv[8];
+          unpack8(rr[c * 32 + lane], rv);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) o[e] += rv[e];
+        }
+        dr[c * 32 + lane] = pack8(o);
+      }
     }
   }
   if (dw != nullptr) {
+    if constexpr (NCH <= 4) {
 #pragma unroll
-    for (int c = 0; c < NCH; ++c)
+      for (int c = 0; c < NCH; ++c)
 #pragma unroll
-      for (int e = 0; e < 8; ++e) atomicAdd(&sdw[(c * 32 + lane) * 8 + e], dwacc[c][e]);
+        for (int e = 0; e < 8; ++e) atomicAdd(&sdw[(c * 32 + lane) * 8 + e], dwacc[c][e]);
+    }
     __syncthreads();
     for (int i = threadIdx.x; i < H; i += blockDim.x) atomicAdd(&dw[i], sdw[i]);
   }
@@ -762,5 +805,72 @@ void scale_inplace(at::Tensor x, double s) {
   const at::cuda::CUDAGuard guard(x.device());
   scale_kernel<<<grid_for(x.numel(), 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       x.data_ptr<float>(), x.numel(), static_cast<float>(s)); NMB_LAUNCHED(1);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------ dropout (Philox)
+// Counter-based dropout: element i keeps with probability 1 - p according to
+// Philox-4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as easy as
+// 1, 2, 3", SC 2011) keyed by a 64-bit seed, counter = i / 4, lane = i % 4. The mask is
+// a pure function of (seed, i), so the backward pass regenerates it instead of storing
+// it. y = x * keep / (1 - p).
+namespace nmb {
+namespace fused {
+
+__device__ __forceinline__ uint4 philox4x32_10(uint4 ctr, uint2 key) {
+  constexpr uint32_t kM0 = 0xD2511F53u, kM1 = 0xCD9E8D57u;  // multipliers (paper, Table 2)
+  constexpr uint32_t kW0 = 0x9E3779B9u, kW1 = 0xBB67AE85u;  // key schedule (Weyl) constants
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t hi0 = __umulhi(kM0, ctr.x), lo0 = kM0 * ctr.x;
+    const uint32_t hi1 = __umulhi(kM1, ctr.z), lo1 = kM1 * ctr.z;
+    ctr = make_uint4(hi1 ^ ctr.y ^ key.x, lo1, hi0 ^ ctr.w ^ key.y, lo0);
+    key.x += kW0;
+    key.y += kW1;
+  }
+  return ctr;
+}
+
+__global__ void dropout_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat16* __restrict__ y,
+                               int64_t n, uint32_t keep_threshold, float scale, uint2 key) {
+  const int64_t groups = (n + 3) / 4;
+  for (int64_t g = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; g < groups;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const uint4 r = philox4x32_10(
+        make_uint4(static_cast<uint32_t>(g), static_cast<uint32_t>(g >> 32), 0u, 0u), key);
+    const uint32_t u[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int64_t i = g * 4 + j;
+      if (i < n) {
+        const float v = __bfloat162float(x[i]);
+        y[i] = __float2bfloat16_rn(u[j] < keep_threshold ? v * scale : 0.0f);
+      }
+    }
+  }
+}
+
+}  // namespace fused
+}  // namespace nmb
+
+// y = dropout(x) with the mask of (seed, element index); call with dy/dx for the backward.
+void dropout_apply(at::Tensor x, at::Tensor y, double p, int64_t seed) {
+  NMB_CHECK_BF16(x);
+  NMB_CHECK_BF16(y);
+  TORCH_CHECK(x.is_contiguous() && y.is_contiguous() && x.numel() == y.numel());
+  TORCH_CHECK(p >= 0.0 && p < 1.0, "dropout probability must be in [0, 1)");
+  const int64_t n = x.numel();
+  if (n == 0) return;
+  const double keep = 1.0 - p;
+  const uint32_t thr = keep >= 1.0 ? 0xFFFFFFFFu
+                                   : static_cast<uint32_t>(keep * 4294967296.0);
+  const uint64_t s = static_cast<uint64_t>(seed);
+  const at::cuda::CUDAGuard guard(x.device());
+  const int64_t groups = (n + 3) / 4;
+  nmb::fused::dropout_kernel<<<grid_for(groups, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+      reinterpret_cast<__nv_bfloat16*>(y.data_ptr()), n, thr, static_cast<float>(1.0 / keep),
+      make_uint2(static_cast<uint32_t>(s), static_cast<uint32_t>(s >> 32)));
+  NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

@@ -15,12 +15,28 @@ import torch
 
 
 class DropoutMask:
-    """Callable forward (``y * mask / (1-p)``) with the matching ``backward``."""
+    """Callable forward (``y * mask / (1-p)``) with the matching ``backward``.
+
+    On CUDA (bf16) the mask is a pure function of (seed, element index) computed by the
+    Philox kernel (``_C.dropout_apply``) in both passes, so nothing is stored; on CPU a
+    seeded torch generator draws the mask and it is kept for the backward pass."""
 
     def __init__(self, p: float, seed: int) -> None:
         self.p = float(p)
-        self.seed = int(seed)
+        self.seed = int(seed) & ((1 << 63) - 1)
         self.mask: torch.Tensor | None = None
+
+    @staticmethod
+    def _kernel_ok(t: torch.Tensor) -> bool:
+        return t.is_cuda and t.dtype == torch.bfloat16
+
+    def _kernel(self, t: torch.Tensor) -> torch.Tensor:
+        from nano_megatron_b200.ops._ext import lib
+
+        src = t.contiguous()
+        out = torch.empty_like(src)
+        lib().dropout_apply(src, out, self.p, self.seed)
+        return out
 
     def _make(self, like: torch.Tensor) -> torch.Tensor:
         gen = torch.Generator(device=like.device)
@@ -29,10 +45,14 @@ class DropoutMask:
         return keep.to(like.dtype) / (1.0 - self.p)
 
     def __call__(self, y: torch.Tensor) -> torch.Tensor:
+        if self._kernel_ok(y):
+            return self._kernel(y)
         self.mask = self._make(y)
         return y * self.mask
 
     def backward(self, dy: torch.Tensor) -> torch.Tensor:
+        if self._kernel_ok(dy):
+            return self._kernel(dy)
         mask = self.mask if self.mask is not None else self._make(dy)
         return dy * mask
 

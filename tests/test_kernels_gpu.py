@@ -263,3 +263,22 @@ def test_adamw_matches_torch():
     assert _rel(pb, ref.detach()) < 1e-2
     parts = lib().sumsq_partials(g)
     assert abs(parts.sum().item() - g.pow(2).sum().item()) / g.pow(2).sum().item() < 1e-5
+
+
+def test_philox_dropout_statistics_and_replay():
+    """Keep rate ~ 1-p, kept values scaled by 1/(1-p), the mask replays bit-exactly from the
+    seed (so backward needs no stored mask), and different seeds give different masks."""
+    from nano_megatron_b200.nn.dropout import DropoutMask
+
+    x = torch.ones(1 << 20, device=DEV, dtype=torch.bfloat16)
+    p = 0.1
+    d = DropoutMask(p, seed=1234)
+    y = d(x)
+    kept = (y != 0).float().mean().item()
+    assert abs(kept - (1 - p)) < 3e-3
+    assert torch.allclose(y[y != 0].float(), torch.full_like(y[y != 0].float(), 1 / (1 - p)),
+                          rtol=1e-2)
+    g = d.backward(x)
+    assert torch.equal(g, y)                      # same mask from (seed, index)
+    y2 = DropoutMask(p, seed=1235)(x)
+    assert not torch.equal(y2 != 0, y != 0)
