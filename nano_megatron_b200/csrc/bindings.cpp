@@ -45,22 +45,26 @@ void adamw_step(at::Tensor p, at::Tensor g, at::Tensor m, at::Tensor v,
                 double eps, double wd, int64_t step, c10::optional<at::Tensor> grad_scale,
                 c10::optional<at::Tensor> lr_t);
 at::Tensor sumsq_partials(at::Tensor x);
-void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda, at::Tensor b,
-                bool b_mn, at::Tensor c, int64_t epi, c10::optional<at::Tensor> xfull,
+void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
+                std::vector<int64_t> shard_ptrs_odd, int64_t lda, at::Tensor b, bool b_mn,
+                at::Tensor c, int64_t epi, c10::optional<at::Tensor> xfull,
                 c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
                 c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
                 int64_t head_dim, int64_t rope_cols, int64_t pos_div, int64_t rank,
-                int64_t flags_ptr, int64_t epoch, at::Tensor status,
+                int64_t flags_ptr, int64_t epoch_ptr, at::Tensor status,
                 c10::optional<at::Tensor> rope_cs);
 void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
-                std::vector<int64_t> staging_ptrs, int64_t rows_per_rank, int64_t n_out,
-                int64_t rank, at::Tensor status);
+                std::vector<int64_t> staging_ptrs, std::vector<int64_t> staging_ptrs_odd,
+                int64_t rows_per_rank, int64_t n_out, int64_t rank, int64_t epoch_ptr,
+                at::Tensor status);
 std::tuple<at::Tensor, pybind11::bytes> symm_alloc(int64_t bytes, int64_t device);
 int64_t symm_open(pybind11::bytes handle, int64_t device);
 void symm_close(int64_t ptr, int64_t device);
-void peer_signal(std::vector<int64_t> targets, int64_t epoch);
-void rs_reduce(int64_t staging_ptr, int64_t tp, at::Tensor out, c10::optional<at::Tensor> residual,
-               int64_t flags_ptr, int64_t epoch, at::Tensor status);
+void peer_signal(std::vector<int64_t> targets, int64_t epoch_ptr);
+void ag_publish(at::Tensor x, int64_t even_ptr, int64_t odd_ptr, int64_t epoch_ptr);
+void rs_reduce(int64_t staging_even, int64_t staging_odd, int64_t tp, at::Tensor out,
+               c10::optional<at::Tensor> residual, int64_t flags_ptr, int64_t epoch_ptr,
+               at::Tensor status);
 void scale_inplace(at::Tensor x, double s);
 void dropout_apply(at::Tensor x, at::Tensor y, double p, int64_t seed);
 
@@ -93,16 +97,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("scale_inplace", &scale_inplace);
   m.def("dropout_apply", &dropout_apply, "counter-based (Philox-4x32-10) dropout, mask = f(seed, index)");
   m.def("gemm_tc_ag", &gemm_tc_ag, "AG->GEMM: A rows gathered from TP peers' symmetric shards",
-        py::arg("a_local"), py::arg("shard_ptrs"), py::arg("lda"), py::arg("b"), py::arg("b_mn"),
-        py::arg("c"), py::arg("epi"), py::arg("xfull"), py::arg("aux"), py::arg("swiglu_up_row"),
-        py::arg("positions"), py::arg("inv_freq"), py::arg("head_dim"), py::arg("rope_cols"),
-        py::arg("pos_div"), py::arg("rank"), py::arg("flags_ptr"), py::arg("epoch"),
-        py::arg("status"), py::arg("rope_cs") = py::none());
+        py::arg("a_local"), py::arg("shard_ptrs"), py::arg("shard_ptrs_odd"), py::arg("lda"),
+        py::arg("b"), py::arg("b_mn"), py::arg("c"), py::arg("epi"), py::arg("xfull"),
+        py::arg("aux"), py::arg("swiglu_up_row"), py::arg("positions"), py::arg("inv_freq"),
+        py::arg("head_dim"), py::arg("rope_cols"), py::arg("pos_div"), py::arg("rank"),
+        py::arg("flags_ptr"), py::arg("epoch_ptr"), py::arg("status"),
+        py::arg("rope_cs") = py::none());
   m.def("gemm_tc_rs", &gemm_tc_rs, "GEMM->RS: partial tiles stored into the owner's staging");
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
   m.def("peer_signal", &peer_signal);
+  m.def("ag_publish", &ag_publish);
   m.def("rs_reduce", &rs_reduce);
   m.def("launch_count", []() { return nmb::launch_counter().load(); },
         "number of kernel launches issued by this library so far (graph replays included)");

@@ -75,17 +75,20 @@ struct GemmParams {
   int comm_rows;                        // rows of A (gather) or C (peer) owned per TP rank
   int comm_rank, comm_size;
   const uint32_t* flags;                // gather: this rank's flags, slot r = rank r's epoch
-  uint32_t epoch;
+  const uint32_t* epoch_ptr;            // device epoch counter of the collective's channel
   int m_rotate;                         // gather: first M tile (own rows first)
   int store_gathered;                   // gather: TMA-store A tiles into `xfull`
-  __nv_bfloat16* peer_out[kMaxTP];      // peer epilogue: staging base of each rank
+  __nv_bfloat16* peer_out[2][kMaxTP];   // peer epilogue: [parity][rank] staging bases
   int splits;                           // split-K factor (kEpiF32Acc with beta = 1 only)
   const float2* rope_cs;                // kEpiRoPE: (cos, sin) table [seq_len][head_dim / 2]
 };
 
 // Per-rank tensor maps of the gathered A operand and of the local gathered copy.
+// The epoch lives in device memory (advanced by the signal kernel), so a launch carries
+// no per-call value and the whole sequence can be captured in a CUDA graph; the data
+// buffers alternate by epoch parity, hence two sets of shard maps / staging pointers.
 struct CommMaps {
-  CUtensorMap a[kMaxTP];
+  CUtensorMap a[2][kMaxTP];
   CUtensorMap xfull;
 };
 
@@ -208,6 +211,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       uint32_t ready = GATHER ? (1u << p.comm_rank) : 0u;
+      uint32_t epoch = 0;
+      if constexpr (GATHER) epoch = *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr);
+      const int par = static_cast<int>(epoch & 1u);
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int m0, nt, ks, kb0, kb1;
         tile_coords<GATHER>(t, p, m0, nt, ks);
@@ -216,7 +222,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (GATHER) {
           owner = m0 / p.comm_rows;
           if (!((ready >> owner) & 1u)) {
-            if (!wait_flag(p.flags + owner, p.epoch, p.status, kStatusPeerFlagTimeout,
+            if (!wait_flag(p.flags + owner, epoch, p.status, kStatusPeerFlagTimeout,
                            abort_flag)) {
               ok = false;
               break;
@@ -236,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = smem_b + stage * Cfg::kBBytes;
           const int k0 = kb * kBK;
           if constexpr (GATHER) {
-            tma_load_2d(sa, &cm.a[owner], &full_bar[stage], k0, m0 - owner * p.comm_rows);
+            tma_load_2d(sa, &cm.a[par][owner], &full_bar[stage], k0, m0 - owner * p.comm_rows);
           } else if constexpr (!A_MN) {
             tma_load_2d(sa, &tmA, &full_bar[stage], k0, m0);
           } else {
@@ -324,6 +330,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int lane = threadIdx.x & 31;
     const float alpha = p.alpha_ptr != nullptr ? p.alpha * __ldg(p.alpha_ptr) : p.alpha;
+    // peer epilogue: this call's epoch is the next one (the signal kernel advances it later)
+    int out_par = 0;
+    if constexpr (EPI == kEpiPeer)
+      out_par = static_cast<int>((*reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) + 1u) &
+                                 1u);
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -353,7 +364,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (EPI == kEpiPeer) {
             const int owner = row / p.comm_rows;
             __nv_bfloat16* dst =
-                p.peer_out[owner] +
+                p.peer_out[out_par][owner] +
                 static_cast<int64_t>(p.comm_rank * p.comm_rows + row - owner * p.comm_rows) *
                     p.ldc +
                 col;
@@ -726,16 +737,18 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
 }
 
 // AG -> GEMM: C[M, N] = epilogue(A_gathered . B^T), A_gathered = concat over TP ranks of
-// the [R, K] shards at `shard_ptrs[r]` (row pitch `lda`; rank r's shard is ready once
-// its slot in this rank's flag array `flags_ptr` reaches `epoch`). With `xfull`, the
+// the [R, K] shards at `shard_ptrs[r]` / `shard_ptrs_odd[r]` for an even / odd epoch (row
+// pitch `lda`); the epoch is read from `epoch_ptr` (already advanced by this call's
+// signal), and rank r's shard is ready once its slot in `flags_ptr` reaches it. With `xfull`, the
 // gathered A is also written to that local [M, K] tensor. Epilogues: bf16 (dgrad of a
 // row-parallel layer, `b_mn`), RoPE (QKV) or SwiGLU (gate|up).
-void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda, at::Tensor b,
-                bool b_mn, at::Tensor c, int64_t epi, c10::optional<at::Tensor> xfull,
+void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
+                std::vector<int64_t> shard_ptrs_odd, int64_t lda, at::Tensor b, bool b_mn,
+                at::Tensor c, int64_t epi, c10::optional<at::Tensor> xfull,
                 c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
                 c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
                 int64_t head_dim, int64_t rope_cols, int64_t pos_div, int64_t rank,
-                int64_t flags_ptr, int64_t epoch, at::Tensor status,
+                int64_t flags_ptr, int64_t epoch_ptr, at::Tensor status,
                 c10::optional<at::Tensor> rope_cs) {
   check_operand(a_local, "A shard");
   check_operand(b, "B");
@@ -749,7 +762,10 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda
   TORCH_CHECK(K == Kb, "gemm_tc_ag: K mismatch");
   TORCH_CHECK(c.dim() == 2 && c.stride(1) == 1 && c.size(0) == M && c.scalar_type() == at::kBFloat16,
               "gemm_tc_ag: bad C");
+  TORCH_CHECK(shard_ptrs_odd.size() == shard_ptrs.size());
   for (auto ptr : shard_ptrs) TORCH_CHECK(ptr % 16 == 0, "shard pointers must be 16-byte aligned");
+  for (auto ptr : shard_ptrs_odd) TORCH_CHECK(ptr % 16 == 0, "shard pointers must be 16-byte aligned");
+  TORCH_CHECK(epoch_ptr % 4 == 0 && epoch_ptr != 0);
   const int64_t N = c.size(1);
   GemmParams p{};
   p.M = static_cast<int>(M);
@@ -763,7 +779,7 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda
   p.comm_rank = static_cast<int>(rank);
   p.comm_size = tp;
   p.flags = reinterpret_cast<const uint32_t*>(flags_ptr);
-  p.epoch = static_cast<uint32_t>(epoch);
+  p.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch_ptr);
   p.m_rotate = static_cast<int>(rank * (R / kBM));
   p.splits = 1;
   int bn = choose_bn(p.M, p.N, epi);
@@ -797,8 +813,10 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda
   const at::cuda::CUDAGuard guard(a_local.device());
   ensure_current_context(a_local.device().index());
   CommMaps cm{};
-  for (int r = 0; r < tp; ++r)
-    cm.a[r] = make_tmap_2d(reinterpret_cast<const void*>(shard_ptrs[r]), R, K, lda, kBM);
+  for (int r = 0; r < tp; ++r) {
+    cm.a[0][r] = make_tmap_2d(reinterpret_cast<const void*>(shard_ptrs[r]), R, K, lda, kBM);
+    cm.a[1][r] = make_tmap_2d(reinterpret_cast<const void*>(shard_ptrs_odd[r]), R, K, lda, kBM);
+  }
   if (xfull.has_value()) {
     check_operand(*xfull, "xfull");
     TORCH_CHECK(xfull->size(0) == M && xfull->size(1) == K);
@@ -810,7 +828,7 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda
                         : make_tmap_2d(b.data_ptr(), b_rows, K, b.stride(0),
                                        epi == kEpiSwiGLU ? bn / 2 : bn);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  const CUtensorMap& ta = cm.a[rank];
+  const CUtensorMap& ta = cm.a[0][rank];
   if (epi == kEpiSwiGLU)
     launch<256, false, false, kEpiSwiGLU, true>(ta, tb, p, stream, 0, &cm);
   else if (epi == kEpiRoPE)
@@ -822,11 +840,13 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs, int64_t lda
 }
 
 // GEMM -> RS: partial C = A . B^T for all M rows; row r's bf16 partial goes to rank
-// (r / rows_per_rank)'s staging buffer `staging_ptrs[owner]`, laid out [tp][rows][N]
-// with this rank's slot `rank`. The owner reduces the slots with rs_reduce.
+// (r / rows_per_rank)'s staging buffer (`staging_ptrs` / `staging_ptrs_odd` by the parity
+// of the upcoming epoch, *epoch_ptr + 1), laid out [tp][rows][N] with this rank's slot
+// `rank`. The owner reduces the slots with rs_reduce after the signal.
 void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
-                std::vector<int64_t> staging_ptrs, int64_t rows_per_rank, int64_t n_out,
-                int64_t rank, at::Tensor status) {
+                std::vector<int64_t> staging_ptrs, std::vector<int64_t> staging_ptrs_odd,
+                int64_t rows_per_rank, int64_t n_out, int64_t rank, int64_t epoch_ptr,
+                at::Tensor status) {
   check_operand(a, "A");
   check_operand(b, "B");
   const int tp = static_cast<int>(staging_ptrs.size());
@@ -836,7 +856,10 @@ void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
   TORCH_CHECK(K == (b_mn ? b.size(0) : b.size(1)), "gemm_tc_rs: K mismatch");
   TORCH_CHECK(M == rows_per_rank * tp, "gemm_tc_rs: M must equal tp * rows_per_rank");
   TORCH_CHECK((n_out * 2) % 16 == 0, "gemm_tc_rs: N must be a multiple of 8");
+  TORCH_CHECK(staging_ptrs_odd.size() == staging_ptrs.size());
   for (auto ptr : staging_ptrs) TORCH_CHECK(ptr % 16 == 0, "staging must be 16-byte aligned");
+  for (auto ptr : staging_ptrs_odd) TORCH_CHECK(ptr % 16 == 0, "staging must be 16-byte aligned");
+  TORCH_CHECK(epoch_ptr % 4 == 0 && epoch_ptr != 0);
   GemmParams p{};
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(n_out);
@@ -848,8 +871,11 @@ void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
   p.comm_rank = static_cast<int>(rank);
   p.comm_size = tp;
   p.splits = 1;
-  for (int r = 0; r < tp; ++r)
-    p.peer_out[r] = reinterpret_cast<__nv_bfloat16*>(staging_ptrs[r]);
+  p.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch_ptr);
+  for (int r = 0; r < tp; ++r) {
+    p.peer_out[0][r] = reinterpret_cast<__nv_bfloat16*>(staging_ptrs[r]);
+    p.peer_out[1][r] = reinterpret_cast<__nv_bfloat16*>(staging_ptrs_odd[r]);
+  }
   const int bn = choose_bn(p.M, p.N, kEpiPeer);
   p.num_m_tiles = static_cast<int>((M + kBM - 1) / kBM);
   p.num_n_tiles = static_cast<int>((n_out + bn - 1) / bn);

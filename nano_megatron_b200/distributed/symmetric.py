@@ -8,11 +8,13 @@ over NVLink (P2P through NVSwitch). Buffer layout (identical on all ranks):
     [ reduce-scatter staging: 2 parities x TP x rows x cols bf16 ]
     [ all-gather shards:       2 parities x rows x cols bf16      ]
 
-A channel's epoch counter advances once per collective call on every rank
-(all ranks issue the same calls in the same order); parity = epoch & 1 selects
-the data half, so call k+1 never overwrites data call k may still be reading
-(a rank only reaches call k+2 after every peer has signalled call k+1, which it
-does after finishing call k). ``emulated`` builds TP workspaces inside one
+A channel's epoch counter lives in device memory (one int per channel, local to
+the rank) and is advanced by the signal kernel once per collective call on every
+rank (all ranks issue the same calls in the same order); no launch carries the
+epoch as an argument, so a step's fused collectives can be captured in a CUDA
+graph. Parity = epoch & 1 selects the data half, so call k+1 never overwrites
+data call k may still be reading (a rank only reaches call k+2 after every peer
+has signalled call k+1, which it does after finishing call k). ``emulated`` builds TP workspaces inside one
 process on one GPU -- every "peer" buffer is local -- so the fused kernels'
 indexing and reductions can be checked without several GPUs; there the calls
 of the emulated ranks are issued phase by phase so no kernel ever waits for a
@@ -38,7 +40,7 @@ class SymmetricWorkspace:
         self.device = device
         self.rs_bytes, self.ag_bytes = rs_bytes, ag_bytes
         self._opened = opened         # peer mappings to close
-        self.epoch = [0] * 16
+        self.epochs = torch.zeros(16, dtype=torch.int32, device=device)  # device counters
         from nano_megatron_b200.ops._ext import status_word
 
         self.status = status_word(device)
@@ -93,9 +95,9 @@ class SymmetricWorkspace:
         self._opened = []
 
     # ------------------------------------------------------------------ addressing
-    def next_epoch(self, channel: int) -> int:
-        self.epoch[channel] = (self.epoch[channel] + 1) & 0x7FFFFFFF or 1
-        return self.epoch[channel]
+    def epoch_ptr(self, channel: int) -> int:
+        """Device address of this rank's epoch counter for ``channel``."""
+        return self.epochs.data_ptr() + 4 * channel
 
     def flags(self, rank: int, channel: int) -> int:
         return self.ptrs[rank] + channel * MAX_TP * 4
@@ -103,20 +105,17 @@ class SymmetricWorkspace:
     def signal_targets(self, channel: int) -> list[int]:
         return [self.flags(d, channel) + self.rank * 4 for d in range(self.size)]
 
-    def rs_staging(self, rank: int, epoch: int) -> int:
-        return self.ptrs[rank] + FLAG_BYTES + (epoch & 1) * self.rs_bytes
+    def rs_staging(self, rank: int, parity: int) -> int:
+        return self.ptrs[rank] + FLAG_BYTES + (parity & 1) * self.rs_bytes
 
-    def ag_shard(self, rank: int, epoch: int) -> int:
-        return self.ptrs[rank] + FLAG_BYTES + 2 * self.rs_bytes + (epoch & 1) * self.ag_bytes
+    def ag_shard(self, rank: int, parity: int) -> int:
+        return self.ptrs[rank] + FLAG_BYTES + 2 * self.rs_bytes + (parity & 1) * self.ag_bytes
 
-    def ag_shard_tensor(self, epoch: int, rows: int, cols: int) -> torch.Tensor:
-        """This rank's shard slot as a [rows, cols] bf16 tensor view."""
+    def check_ag(self, rows: int, cols: int) -> None:
         need = rows * cols * 2
         if need > self.ag_bytes:
             raise ValueError(f"all-gather shard needs {need} bytes; workspace has "
                              f"{self.ag_bytes}")
-        off = FLAG_BYTES + 2 * self.rs_bytes + (epoch & 1) * self.ag_bytes
-        return self.owner[off:off + need].view(torch.bfloat16).view(rows, cols)
 
     def check_rs(self, rows: int, cols: int) -> None:
         need = self.size * rows * cols * 2

@@ -28,46 +28,46 @@ EPI = {"bf16": 0, "rope": 3, "swiglu": 2}
 
 
 def rs_issue(ws, a: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,
-             n_out: int | None = None) -> tuple[int, int, int]:
-    """GEMM with the peer epilogue + signal. Returns (epoch, rows_per_rank, n_out)."""
+             n_out: int | None = None) -> tuple[int, int]:
+    """GEMM with the peer epilogue + signal. Returns (rows_per_rank, n_out)."""
     M = a.shape[0]
     if M % ws.size:
         raise ValueError(f"rows {M} not divisible by TP size {ws.size}")
     rows = M // ws.size
     n = n_out if n_out is not None else (b.shape[1] if b_mn else b.shape[0])
     ws.check_rs(rows, n)
-    epoch = ws.next_epoch(CH_RS)
-    lib().gemm_tc_rs(a, False, b, b_mn, [ws.rs_staging(r, epoch) for r in range(ws.size)], rows,
-                     n, ws.rank, ws.status)
-    lib().peer_signal(ws.signal_targets(CH_RS), epoch)
-    return epoch, rows, n
+    lib().gemm_tc_rs(a, False, b, b_mn, [ws.rs_staging(r, 0) for r in range(ws.size)],
+                     [ws.rs_staging(r, 1) for r in range(ws.size)], rows, n, ws.rank,
+                     ws.epoch_ptr(CH_RS), ws.status)
+    lib().peer_signal(ws.signal_targets(CH_RS), ws.epoch_ptr(CH_RS))
+    return rows, n
 
 
-def rs_finish(ws, epoch: int, out: torch.Tensor, residual: torch.Tensor | None = None) -> None:
-    lib().rs_reduce(ws.rs_staging(ws.rank, epoch), ws.size, out, residual, ws.flags(ws.rank, CH_RS),
-                    epoch, ws.status)
+def rs_finish(ws, out: torch.Tensor, residual: torch.Tensor | None = None) -> None:
+    lib().rs_reduce(ws.rs_staging(ws.rank, 0), ws.rs_staging(ws.rank, 1), ws.size, out, residual,
+                    ws.flags(ws.rank, CH_RS), ws.epoch_ptr(CH_RS), ws.status)
 
 
 def gemm_reduce_scatter(ws, a: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,
                         residual: torch.Tensor | None = None,
                         out: torch.Tensor | None = None) -> torch.Tensor:
-    epoch, rows, n = rs_issue(ws, a, b, b_mn=b_mn)
+    rows, n = rs_issue(ws, a, b, b_mn=b_mn)
     if out is None:
         out = torch.empty(rows, n, device=a.device, dtype=torch.bfloat16)
-    rs_finish(ws, epoch, out, residual)
+    rs_finish(ws, out, residual)
     return out
 
 
-def ag_issue(ws, x_local: torch.Tensor, channel: int = CH_AG) -> int:
+def ag_issue(ws, x_local: torch.Tensor, channel: int = CH_AG) -> None:
     """Publish this rank's shard into its symmetric slot and signal every rank."""
-    epoch = ws.next_epoch(channel)
     R, K = x_local.shape
-    ws.ag_shard_tensor(epoch, R, K).copy_(x_local)
-    lib().peer_signal(ws.signal_targets(channel), epoch)
-    return epoch
+    ws.check_ag(R, K)
+    lib().ag_publish(x_local, ws.ag_shard(ws.rank, 0), ws.ag_shard(ws.rank, 1),
+                     ws.epoch_ptr(channel))
+    lib().peer_signal(ws.signal_targets(channel), ws.epoch_ptr(channel))
 
 
-def ag_finish(ws, epoch: int, x_local: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
+def ag_finish(ws, x_local: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
               b_mn: bool = False, epi: str = "bf16", xfull: torch.Tensor | None = None,
               aux: torch.Tensor | None = None, swiglu_up_row: int = 0,
               positions: torch.Tensor | None = None, inv_freq: torch.Tensor | None = None,
@@ -79,10 +79,11 @@ def ag_finish(ws, epoch: int, x_local: torch.Tensor, b: torch.Tensor, out: torch
         from .gemm import rope_table
 
         table = rope_table(positions, inv_freq)
-    lib().gemm_tc_ag(x_local, [ws.ag_shard(r, epoch) for r in range(ws.size)], K, b, b_mn, out,
-                     EPI[epi], xfull, aux, swiglu_up_row, positions, inv_freq, head_dim,
-                     rope_cols, pos_div, ws.rank, ws.flags(ws.rank, channel), epoch, ws.status,
-                     table)
+    lib().gemm_tc_ag(x_local, [ws.ag_shard(r, 0) for r in range(ws.size)],
+                     [ws.ag_shard(r, 1) for r in range(ws.size)], K, b, b_mn, out, EPI[epi],
+                     xfull, aux, swiglu_up_row, positions, inv_freq, head_dim, rope_cols,
+                     pos_div, ws.rank, ws.flags(ws.rank, channel), ws.epoch_ptr(channel),
+                     ws.status, table)
 
 
 def allgather_gemm(ws, x_local: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,
@@ -95,6 +96,6 @@ def allgather_gemm(ws, x_local: torch.Tensor, b: torch.Tensor, *, b_mn: bool = F
     out = torch.empty(M, n, device=x_local.device, dtype=torch.bfloat16)
     xfull = torch.empty(M, K, device=x_local.device, dtype=torch.bfloat16) \
         if store_gathered else None
-    epoch = ag_issue(ws, x_local)
-    ag_finish(ws, epoch, x_local, b, out, b_mn=b_mn, epi=epi, xfull=xfull, **kw)
+    ag_issue(ws, x_local)
+    ag_finish(ws, x_local, b, out, b_mn=b_mn, epi=epi, xfull=xfull, **kw)
     return out, xfull

@@ -14,9 +14,11 @@ with the host.
 Capture protocol: one eager warm-up microbatch on a side stream (lazy kernel
 attributes, cached positions, workspaces), then capture, then the gradient
 buffers are zeroed again because warm-up accumulated into them. Used by the
-no-pipeline schedule when ``kernels.cuda_graphs`` is on, the model has no
-tensor-parallel NVLink workspace (its flag epochs are per-call arguments), and
-the data-parallel strategy does no per-microbatch communication.
+no-pipeline schedule when ``kernels.cuda_graphs`` is on and the data-parallel
+strategy does no per-microbatch communication. Tensor-parallel layers are
+captured too: their NCCL collectives are graph-capturable, and the fused NVLink
+collectives keep their flag epochs in device memory, so every replay advances
+them like an eager call would.
 """
 
 from __future__ import annotations
@@ -85,8 +87,6 @@ def graph_key(mb: dict) -> tuple:
 
 
 def graphs_supported(config, model, data_parallel, device: torch.device) -> bool:
-    from nano_megatron_b200.models.gpt.model import GPTModel
-
     if device.type != "cuda" or not bool(getattr(config.kernels, "cuda_graphs", True)):
         return False
     if not getattr(data_parallel, "graph_safe_microbatches", False):
@@ -95,7 +95,4 @@ def graphs_supported(config, model, data_parallel, device: torch.device) -> bool
         return False
     if str(getattr(config.activation_checkpoint, "mode", "none")) != "none":
         return False
-    for m in model.modules():
-        if isinstance(m, GPTModel) and getattr(m, "tp_workspace", None) is not None:
-            return False
     return True

@@ -43,10 +43,11 @@ def test_gemm_reduce_scatter(tp, b_mn):
         w = [torch.randn(N, K, device=DEV).bfloat16() for _ in range(tp)]
         res = [torch.randn(R, N, device=DEV).bfloat16() for _ in range(tp)]
         bstore = [x.t().contiguous() if b_mn else x for x in w]
-        issued = [CG.rs_issue(ws[r], a[r], bstore[r], b_mn=b_mn) for r in range(tp)]
+        for r in range(tp):
+            CG.rs_issue(ws[r], a[r], bstore[r], b_mn=b_mn)
         outs = [torch.empty(R, N, device=DEV, dtype=torch.bfloat16) for _ in range(tp)]
         for r in range(tp):
-            CG.rs_finish(ws[r], issued[r][0], outs[r], res[r])
+            CG.rs_finish(ws[r], outs[r], res[r])
         _ok()
         full = sum(a[r].float() @ w[r].float().t() for r in range(tp))
         for r in range(tp):
@@ -62,12 +63,13 @@ def test_allgather_gemm_bf16_and_gathered_copy(tp):
     for it in range(3):
         x = [torch.randn(R, K, device=DEV).bfloat16() for _ in range(tp)]
         w = torch.randn(N, K, device=DEV).bfloat16()
-        epochs = [CG.ag_issue(ws[r], x[r]) for r in range(tp)]
+        for r in range(tp):
+            CG.ag_issue(ws[r], x[r])
         outs, xf = [], []
         for r in range(tp):
             o = torch.empty(R * tp, N, device=DEV, dtype=torch.bfloat16)
             g = torch.empty(R * tp, K, device=DEV, dtype=torch.bfloat16)
-            CG.ag_finish(ws[r], epochs[r], x[r], w, o, xfull=g)
+            CG.ag_finish(ws[r], x[r], w, o, xfull=g)
             outs.append(o)
             xf.append(g)
         _ok()
@@ -84,11 +86,12 @@ def test_allgather_gemm_dgrad_layout():
     ws = SymmetricWorkspace.emulated(tp, rs_bytes=2 * MB, ag_bytes=8 * MB, device=DEV)
     dy = [torch.randn(R, K, device=DEV).bfloat16() for _ in range(tp)]
     w = torch.randn(K, n_local, device=DEV).bfloat16()       # weight [out=K, in_local]
-    epochs = [CG.ag_issue(ws[r], dy[r]) for r in range(tp)]
+    for r in range(tp):
+        CG.ag_issue(ws[r], dy[r])
     outs = []
     for r in range(tp):
         o = torch.empty(R * tp, n_local, device=DEV, dtype=torch.bfloat16)
-        CG.ag_finish(ws[r], epochs[r], dy[r], w, o, b_mn=True)
+        CG.ag_finish(ws[r], dy[r], w, o, b_mn=True)
         outs.append(o)
     _ok()
     ref = torch.cat(dy).float() @ w.float()
@@ -108,21 +111,23 @@ def test_allgather_gemm_rope_and_swiglu_match_local_kernels():
     pos = torch.arange(R * tp // B, device=DEV, dtype=torch.int32)
     inv = 1.0 / (10000 ** (torch.arange(0, D, 2, device=DEV).float() / D))
     ref = F.qkv_rope_linear(xcat, wqkv, pos, inv, D, (hq + hkv) * D, pos_div=B)
-    epochs = [CG.ag_issue(ws[r], x[r]) for r in range(tp)]
+    for r in range(tp):
+        CG.ag_issue(ws[r], x[r])
     for r in range(tp):
         o = torch.empty(R * tp, wqkv.shape[0], device=DEV, dtype=torch.bfloat16)
-        CG.ag_finish(ws[r], epochs[r], x[r], wqkv, o, epi="rope", positions=pos, inv_freq=inv,
+        CG.ag_finish(ws[r], x[r], wqkv, o, epi="rope", positions=pos, inv_freq=inv,
                      head_dim=D, rope_cols=(hq + hkv) * D, pos_div=B)
         _ok()
         assert _rel(o, ref) < 1e-3
     ffn = 768
     wgu = (torch.randn(2 * ffn, H, device=DEV) * 0.05).bfloat16()
     h_ref, gu_ref = F.swiglu_linear(xcat, wgu, ffn)
-    epochs = [CG.ag_issue(ws[r], x[r]) for r in range(tp)]
+    for r in range(tp):
+        CG.ag_issue(ws[r], x[r])
     for r in range(tp):
         h = torch.empty(R * tp, ffn, device=DEV, dtype=torch.bfloat16)
         gu = torch.empty(R * tp, 2 * ffn, device=DEV, dtype=torch.bfloat16)
-        CG.ag_finish(ws[r], epochs[r], x[r], wgu, h, epi="swiglu", aux=gu, swiglu_up_row=ffn)
+        CG.ag_finish(ws[r], x[r], wgu, h, epi="swiglu", aux=gu, swiglu_up_row=ffn)
         _ok()
         assert _rel(h, h_ref) < 1e-3 and _rel(gu, gu_ref) < 1e-3
 
@@ -134,9 +139,9 @@ def test_missing_peer_times_out_with_status():
     ws = SymmetricWorkspace.emulated(tp, rs_bytes=2 * MB, ag_bytes=2 * MB, device=DEV)
     x = torch.randn(R, K, device=DEV).bfloat16()
     w = torch.randn(N, K, device=DEV).bfloat16()
-    epoch = CG.ag_issue(ws[0], x)          # rank 1 never publishes this epoch
+    CG.ag_issue(ws[0], x)                  # rank 1 never publishes this epoch
     o = torch.empty(R * tp, N, device=DEV, dtype=torch.bfloat16)
-    CG.ag_finish(ws[0], epoch, x, w, o)
+    CG.ag_finish(ws[0], x, w, o)
     torch.cuda.synchronize()
     st = status_word(DEV)
     assert int(st.item()) == 0x301

@@ -1,8 +1,9 @@
-"""TP2 + sequence parallelism on two GPUs: fused NVLink collectives vs NCCL collectives.
+"""TP2 + sequence parallelism on two GPUs: fused NVLink collectives vs NCCL collectives,
+eager and replayed from per-microbatch CUDA graphs.
 
-Same weights, same batch: the training-step loss and the merged weight
-gradients with ``kernels.fused_tp_comm`` on must match the run with it off
-(bf16 tolerance). Child processes, one per GPU, bounded by timeouts.
+Same weights, same batch: the training-step loss and the weight gradients with
+``kernels.fused_tp_comm`` on (eager, and captured + replayed) must match the
+eager NCCL run (bf16 tolerance). Child processes, one per GPU, bounded by timeouts.
 """
 
 import os
@@ -15,7 +16,7 @@ pytestmark = pytest.mark.gpu
 WORLD = 2
 
 
-def _cfg(fused: bool):
+def _cfg(fused: bool, graphs: bool = False):
     from nano_megatron_b200.config import config_from_dict
 
     return config_from_dict({
@@ -25,7 +26,7 @@ def _cfg(fused: bool):
         "model": {"layers": 2, "hidden_size": 256, "ffn_hidden_size": 512, "heads": 4,
                   "kv_heads": 2, "seq_length": 256, "vocab_size": 512},
         "precision": {"params": "bfloat16", "compute": "bfloat16", "grad_reduce": "float32"},
-        "kernels": {"backend": "b200", "fused_tp_comm": fused},
+        "kernels": {"backend": "b200", "fused_tp_comm": fused, "cuda_graphs": graphs},
         "training": {"micro_batch_size": 2, "gradient_accumulation_steps": 2, "seed": 7},
         "optimizer": {"lr": 1e-3}})
 
@@ -45,22 +46,24 @@ def _worker(rank, world, port, out_dir, errq):
         batch = {"input_ids": ids[:, :-1].contiguous(), "labels": ids[:, 1:].contiguous()}
         runtime = DistributedRuntime(_cfg(True).distributed).initialize()
         results = {}
-        for fused in (False, True):
-            cfg = _cfg(fused)
+        for fused, graphs in ((False, False), (True, False), (True, True)):
+            cfg = _cfg(fused, graphs)
             comps = build_training_components(cfg, runtime)
             assert (getattr(comps.model.model, "tp_workspace", None) is not None) == fused
             tr = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
                          data_parallel=comps.data_parallel, rng=comps.rng)
-            micro = tr._prepare_batch(batch)
-            comps.data_parallel.zero_grad()
-            acc = tr.schedule.forward_backward(micro)
-            comps.data_parallel.finalize_gradients()
+            assert getattr(tr.schedule, "use_graphs", False) == graphs
             from nano_megatron_b200.training.metrics import aggregate_loss_metrics
 
+            for rep in range(2):      # graphs: capture on the first pass, replay on the second
+                micro = tr._prepare_batch(batch)
+                comps.data_parallel.zero_grad()
+                acc = tr.schedule.forward_backward(micro)
+                comps.data_parallel.finalize_gradients()
             s, c = aggregate_loss_metrics(acc, comps.parallel, runtime.device)
             grads = {n: p.main_grad.detach().float().cpu().clone()
                      for n, p in comps.model.named_parameters()}
-            results[fused] = (float(s / c), grads)
+            results[(fused, graphs)] = (float(s / c), grads)
         from nano_megatron_b200.ops._ext import check_status
 
         check_status(runtime.device)
@@ -96,9 +99,11 @@ def test_fused_tp_matches_nccl_tp(tmp_path):
     assert not alive and all(p.exitcode == 0 for p in procs)
     for r in range(WORLD):
         res = torch.load(tmp_path / f"r{r}.pt")
-        (l0, g0), (l1, g1) = res[False], res[True]
-        assert abs(l0 - l1) < 2e-2 * abs(l0), (l0, l1)
-        for n in g0:
-            a, b = g0[n], g1[n]
-            rel = ((a - b).norm() / (a.norm() + 1e-12)).item()
-            assert rel < 5e-2, (r, n, rel)
+        l0, g0 = res[(False, False)]
+        for key in ((True, False), (True, True)):
+            l1, g1 = res[key]
+            assert abs(l0 - l1) < 2e-2 * abs(l0), (key, l0, l1)
+            for n in g0:
+                a, b = g0[n], g1[n]
+                rel = ((a - b).norm() / (a.norm() + 1e-12)).item()
+                assert rel < 5e-2, (key, r, n, rel)
