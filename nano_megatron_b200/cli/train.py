@@ -96,9 +96,14 @@ def run(config_path: Path, *, overrides: Sequence[str] = (), resume: Path | None
             log(f"checkpoint run directory: {run_dir}")
         ckpt = CheckpointManager(config=config.checkpoint, parallel=comps.parallel,
                                  run_config=config)
+        from nano_megatron_b200.distributed.health import PeerHealth
+
+        health = PeerHealth.from_default_group() if runtime.world_size > 1 else None
+        if health is not None:
+            health.start()
         trainer = Trainer(config=config, model=comps.model, parallel=comps.parallel,
                           data_parallel=comps.data_parallel, checkpoint=ckpt, rng=comps.rng,
-                          metrics_path=run_dir / "metrics.jsonl",
+                          health=health, metrics_path=run_dir / "metrics.jsonl",
                           resume_metrics_path=None if resume is None
                           else Path(resume).parent / "metrics.jsonl")
         try:
@@ -120,6 +125,8 @@ def run(config_path: Path, *, overrides: Sequence[str] = (), resume: Path | None
         finally:
             trainer.close()
             ckpt.close()
+            if health is not None:
+                health.stop()
         if runtime.is_primary:
             log(f"finished step={state.step} samples={state.consumed_samples} "
                 f"tokens={state.consumed_tokens}")

@@ -120,7 +120,7 @@ def _move_to_device(batch, device):
 class Trainer:
     def __init__(self, *, config, model, parallel, data_parallel, checkpoint=None,
                  data_iterator=None, metrics_path=None, resume_metrics_path=None, rng=None,
-                 device=None) -> None:
+                 device=None, health=None) -> None:
         self.config = config
         self.model = model
         self.parallel = parallel
@@ -128,6 +128,7 @@ class Trainer:
         self.checkpoint = checkpoint
         self.data_iterator = data_iterator
         self.rng = rng
+        self.health = health            # PeerHealth: host-side failure detection, optional
         self.state = TrainerState()
         self.device = device or next(model.parameters()).device
         data_parallel.configure_precision(config.precision)
@@ -287,9 +288,26 @@ class Trainer:
         device_ms = 0.0
         first_step = self.state.step
         self._last_saved = None
+        health = getattr(self, "health", None)
         while self.state.step < target:
-            batch = next(self.data_iterator) if self.batch_router.is_source else None
-            out, ms = self.timed_train_step(batch)
+            if health is not None:
+                health.check()          # stop between steps if a peer failed
+            data = getattr(self, "_data", None)
+            saved = data.state_dict() if self.batch_router.is_source and \
+                callable(getattr(data, "state_dict", None)) else None
+            try:
+                batch = next(self.data_iterator) if self.batch_router.is_source else None
+                out, ms = self.timed_train_step(batch)
+            except BaseException as error:
+                # Leave the data position at the last completed step (as the reference
+                # does) so a checkpoint taken by the caller resumes exactly, and tell the
+                # other ranks before they launch their next step.
+                if saved is not None:
+                    data.load_state_dict(saved)
+                    self.data_iterator = iter(data)
+                if health is not None:
+                    health.report_failure(error)
+                raise
             self._record_data_state()
             device_ms += ms
             pending.append(out)
