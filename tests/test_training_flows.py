@@ -1,0 +1,174 @@
+"""Training flows (CPU): W&B replay on resume with a fake wandb module, CLI resume under
+ZeRO-2 + full activation checkpointing + offloads, async save while training continues,
+and a data-parallel expansion keeping the new replica's RNG with a warning.
+Reference counterparts: tests/integration/test_cli_resume.py:58-151,
+tests/integration/test_wandb_training_flow.py, tests/unit/test_wandb_logger.py:12-41,
+tests/distributed_cpu/test_checkpoint_rank_local.py:435, 605-700.
+"""
+
+from __future__ import annotations
+
+import json
+import warnings
+from pathlib import Path
+
+import pytest
+import torch
+import yaml
+
+from dist_utils import run_ranks
+
+
+class _FakeRun:
+    def __init__(self, **kw):
+        self.kw = kw
+        self.id = kw.get("id", "run-x")
+        self.logged: list = []
+        self.summary = {}
+        self.finished = False
+
+    def log(self, payload):
+        self.logged.append(dict(payload))
+
+    def finish(self):
+        self.finished = True
+
+
+class _FakeWandb:
+    def __init__(self):
+        self.runs: list = []
+        self.defined: list = []
+
+    def init(self, **kw):
+        run = _FakeRun(**kw)
+        run.summary = type("S", (dict,), {"update": dict.update})()
+        self.runs.append(run)
+        return run
+
+    def define_metric(self, *a, **kw):
+        self.defined.append((a, kw))
+
+
+def _base_cfg(tmp: Path, **over) -> dict:
+    from nano_megatron_b200.config import TrainConfig
+    from nano_megatron_b200.config.loader import config_to_dict
+
+    d = config_to_dict(TrainConfig())
+    d["distributed"].update(backend="gloo", device="cpu")
+    d["model"].update(layers=2, hidden_size=32, ffn_hidden_size=64, heads=4, kv_heads=2,
+                      seq_length=16, vocab_size=128)
+    d["precision"].update(params="float32", compute="float32")
+    d["training"].update(micro_batch_size=2, gradient_accumulation_steps=2, max_steps=4,
+                         log_interval=1, seed=5)
+    d["optimizer"].update(lr=1e-2)
+    d["checkpoint"].update(directory=str(tmp / "runs"), save_interval=2, keep_last=4)
+    for k, v in over.items():
+        d[k].update(v)
+    return d
+
+
+def test_wandb_replay_and_fork_on_resume(tmp_path, monkeypatch):
+    from nano_megatron_b200.cli import train as trcli
+    from nano_megatron_b200.training import wandb_logger
+
+    fake = _FakeWandb()
+    monkeypatch.setattr(wandb_logger.importlib, "import_module",
+                        lambda name: fake if name == "wandb" else __import__(name))
+    cfg = tmp_path / "c.yaml"
+    cfg.write_text(yaml.safe_dump(_base_cfg(tmp_path, wandb={"enabled": True,
+                                                             "mode": "offline"})))
+    trcli.run(cfg, max_steps=2, log=lambda *_: None)
+    first = fake.runs[0]
+    assert [p["trainer/step"] for p in first.logged] == [1, 2] and first.finished
+    run1 = next((tmp_path / "runs").iterdir())
+    trcli.run(cfg, resume=run1 / "step_00000002", max_steps=4, log=lambda *_: None)
+    second = fake.runs[1]
+    assert first.kw["resume"] == "allow" and second.kw["resume"] == "never"
+    assert second.id != first.id
+    steps = [p["trainer/step"] for p in second.logged]
+    assert steps == [1, 2, 3, 4]                       # replayed prefix, then new steps
+    assert second.summary.get("wandb/forked_from_step") == 2
+
+
+def test_cli_resume_zero2_full_checkpointing_offload_is_exact(tmp_path):
+    """4 steps in one go == 2 steps, then resume for 2 more (same losses)."""
+    from nano_megatron_b200.cli import train as trcli
+    from nano_megatron_b200.training.metric_history import read_metric_history
+
+    over = dict(data_parallel={"mode": "zero2"},
+                activation_checkpoint={"mode": "full", "offload_saved_tensors": True},
+                offload={"optimizer_state": True})
+    cfg_a = tmp_path / "a.yaml"
+    cfg_a.write_text(yaml.safe_dump(_base_cfg(tmp_path / "a", **over)))
+    trcli.run(cfg_a, max_steps=4, log=lambda *_: None)
+    run_a = next((tmp_path / "a" / "runs").iterdir())
+    full = [r.metrics["loss"] for r in read_metric_history(run_a / "metrics.jsonl")]
+    cfg_b = tmp_path / "b.yaml"
+    cfg_b.write_text(yaml.safe_dump(_base_cfg(tmp_path / "b", **over)))
+    trcli.run(cfg_b, max_steps=2, log=lambda *_: None)
+    run_b1 = next((tmp_path / "b" / "runs").iterdir())
+    trcli.run(cfg_b, resume=run_b1 / "step_00000002", max_steps=4, log=lambda *_: None)
+    run_b2 = sorted((tmp_path / "b" / "runs").iterdir())[-1]
+    resumed = [r.metrics["loss"] for r in read_metric_history(run_b2 / "metrics.jsonl")]
+    assert len(full) == len(resumed) == 4
+    for a, b in zip(full, resumed):
+        assert abs(a - b) < 1e-6 * abs(a), (full, resumed)
+
+
+def test_async_save_lets_training_continue_before_flush(tmp_path):
+    from nano_megatron_b200.checkpoint import CheckpointManager
+    from nano_megatron_b200.config import config_from_dict
+    from nano_megatron_b200.distributed import DistributedRuntime
+    from nano_megatron_b200.training import Trainer
+    from nano_megatron_b200.training.engine import build_training_components
+
+    d = _base_cfg(tmp_path, checkpoint={"async_save": True})
+    cfg = config_from_dict(d)
+    comps = build_training_components(cfg, DistributedRuntime(cfg.distributed).initialize())
+    ck = CheckpointManager(config=cfg.checkpoint, parallel=comps.parallel, run_config=cfg)
+    tr = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
+                 data_parallel=comps.data_parallel, checkpoint=ck, rng=comps.rng)
+    ids = torch.randint(0, 128, (4, 17))
+    batch = {"input_ids": ids[:, :-1], "labels": ids[:, 1:]}
+    tr.train_step(batch)
+    saved = {k: v.clone() for k, v in comps.model.state_dict().items()}
+    path = tr.save_checkpoint()
+    tr.train_step(batch)                                # training continues meanwhile
+    tr.flush()
+    assert (path / ".complete").is_file()
+    state = torch.load(path / "model.pt")
+    for k, v in saved.items():
+        torch.testing.assert_close(state[k], v, rtol=0, atol=0)   # snapshot, not later values
+
+
+def _expand_save(rank, world, root):
+    from nano_megatron_b200.checkpoint import CheckpointManager
+    from nano_megatron_b200.config import config_from_dict
+    from nano_megatron_b200.distributed import DistributedRuntime
+    from nano_megatron_b200.training import Trainer
+    from nano_megatron_b200.training.engine import build_training_components
+
+    d = _base_cfg(Path(root), parallel={"data": world})
+    d["checkpoint"]["directory"] = str(Path(root) / "ck")
+    cfg = config_from_dict(d)
+    comps = build_training_components(cfg, DistributedRuntime(cfg.distributed).initialize())
+    ck = CheckpointManager(config=cfg.checkpoint, parallel=comps.parallel, run_config=cfg)
+    tr = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
+                 data_parallel=comps.data_parallel, checkpoint=ck, rng=comps.rng)
+    if world == 1:
+        ids = torch.randint(0, 128, (4, 17))
+        tr.train_step({"input_ids": ids[:, :-1], "labels": ids[:, 1:]})
+        tr.save_checkpoint()
+        return
+    latest = ck.latest()
+    with warnings.catch_warnings(record=True) as caught:
+        warnings.simplefilter("always")
+        tr.load_checkpoint(latest)
+    new_replica = comps.parallel.coordinate.dp == 1
+    assert any("new data-parallel replica" in str(w.message) for w in caught) == new_replica
+
+
+@pytest.mark.distributed
+def test_dp_expansion_keeps_new_replica_rng_with_warning(tmp_path):
+    run_ranks(1, _expand_save, str(tmp_path))
+    run_ranks(2, _expand_save, str(tmp_path))
