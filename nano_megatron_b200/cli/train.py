@@ -34,6 +34,10 @@ def parser() -> argparse.ArgumentParser:
                    help="override a dotted configuration key; may be repeated")
     p.add_argument("--resume", type=Path, help="checkpoint directory to restore")
     p.add_argument("--max-steps", type=int, help="override only this invocation's stop step")
+    p.add_argument("--profile-dir", type=Path,
+                   help="write a torch.profiler Chrome trace per rank for --profile-steps")
+    p.add_argument("--profile-steps", default="2:4", metavar="START:STOP",
+                   help="completed-step window to profile (default 2:4)")
     return p
 
 
@@ -82,7 +86,8 @@ def load_run_tokenizer(config):
 
 
 def run(config_path: Path, *, overrides: Sequence[str] = (), resume: Path | None = None,
-        max_steps: int | None = None, log=print):
+        max_steps: int | None = None, log=print, profile_dir: Path | None = None,
+        profile_steps: str = "2:4"):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     config = load_config(config_path, overrides=overrides, world_size=world)
     validate_config(config, world_size=world)
@@ -106,6 +111,11 @@ def run(config_path: Path, *, overrides: Sequence[str] = (), resume: Path | None
                           health=health, metrics_path=run_dir / "metrics.jsonl",
                           resume_metrics_path=None if resume is None
                           else Path(resume).parent / "metrics.jsonl")
+        if profile_dir is not None:
+            from nano_megatron_b200.utils.profiling import StepProfiler
+
+            a, b = (int(x) for x in profile_steps.split(":"))
+            trainer.profiler = StepProfiler(profile_dir, a, b, rank=runtime.rank)
         try:
             if resume is not None:
                 trainer.load_checkpoint(resume)
@@ -123,6 +133,8 @@ def run(config_path: Path, *, overrides: Sequence[str] = (), resume: Path | None
                     config, comps.parallel, tokenizer=tokenizer))
             state = trainer.fit(max_steps=max_steps, log=log)
         finally:
+            if trainer.profiler is not None:
+                trainer.profiler.close()
             trainer.close()
             ckpt.close()
             if health is not None:
@@ -135,7 +147,8 @@ def run(config_path: Path, *, overrides: Sequence[str] = (), resume: Path | None
 
 def main(argv: Sequence[str] | None = None) -> None:
     a = parser().parse_args(argv)
-    run(a.config, overrides=a.overrides, resume=a.resume, max_steps=a.max_steps)
+    run(a.config, overrides=a.overrides, resume=a.resume, max_steps=a.max_steps,
+        profile_dir=a.profile_dir, profile_steps=a.profile_steps)
 
 
 if __name__ == "__main__":

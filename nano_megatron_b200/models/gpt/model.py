@@ -28,6 +28,7 @@ from nano_megatron_b200.nn.activation_checkpoint import activation_checkpoint
 from nano_megatron_b200.nn.dropout import make_dropout
 from nano_megatron_b200.nn.norms import RMSNorm
 from nano_megatron_b200.nn.rotary import rope_inv_freq
+from nano_megatron_b200.utils.profiling import nvtx_range
 from nano_megatron_b200.tensor_parallel.embedding import VocabParallelEmbedding
 from nano_megatron_b200.tensor_parallel.layers import (
     ColumnParallelLinear,
@@ -285,14 +286,16 @@ class GPTModel(nn.Module):
         if inv_freq.device != device:
             self.rope_inv_freq = inv_freq = inv_freq.to(device)
         for layer in self.layers:
-            if self._checkpoint_layer(layer):
-                h = activation_checkpoint(
-                    lambda x, lyr=layer: lyr(x, attn_spec=attn_spec, mlp_spec=mlp_spec, mb=mb,
-                                             inv_freq=inv_freq),
-                    h, offload_saved_tensors=bool(getattr(self.activation_checkpoint_config,
-                                                          "offload_saved_tensors", False)))
-            else:
-                h = layer(h, attn_spec=attn_spec, mlp_spec=mlp_spec, mb=mb, inv_freq=inv_freq)
+            with nvtx_range(f"layer {layer.layer_index}"):
+                if self._checkpoint_layer(layer):
+                    h = activation_checkpoint(
+                        lambda x, lyr=layer: lyr(x, attn_spec=attn_spec, mlp_spec=mlp_spec,
+                                                 mb=mb, inv_freq=inv_freq),
+                        h, offload_saved_tensors=bool(getattr(
+                            self.activation_checkpoint_config, "offload_saved_tensors", False)))
+                else:
+                    h = layer(h, attn_spec=attn_spec, mlp_spec=mlp_spec, mb=mb,
+                              inv_freq=inv_freq)
         if self.lm_head is None:
             return GPTOutput(logits=None, loss=None, hidden_states=h)
         if labels is not None:

@@ -19,6 +19,8 @@ import os
 
 import torch
 
+from nano_megatron_b200.utils.profiling import nvtx_range
+
 from ..p2p import P2PCommunicator
 from .base import LossAccumulator, batch_labels, extract_loss
 from .plans import build_1f1b_plan, build_gpipe_plan, build_interleaved_plan, validate_plan
@@ -108,10 +110,12 @@ class PipelineScheduleExecutor:
             # blocked setting up the matching NCCL connection. Sends stay
             # asynchronous, which is what overlaps transfers with compute.
             pending = None
-            if a.kind == "F":
-                self._forward(a, buf, microbatches, m, acc, records, forward_only, last_b, plan)
-            else:
-                self._backward(a, buf, records, is_last=(i == last_b.get(a.chunk)))
+            with nvtx_range(f"{a.kind} c{a.chunk} mb{a.microbatch}"):
+                if a.kind == "F":
+                    self._forward(a, buf, microbatches, m, acc, records, forward_only, last_b,
+                                  plan)
+                else:
+                    self._backward(a, buf, records, is_last=(i == last_b.get(a.chunk)))
             # keep at most a couple of sends in flight
             self.p2p.drain_sends(keep=4)
         self.p2p.drain_sends(keep=0)

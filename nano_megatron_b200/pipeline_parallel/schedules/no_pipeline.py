@@ -4,6 +4,8 @@ from __future__ import annotations
 
 import torch
 
+from nano_megatron_b200.utils.profiling import nvtx_range
+
 from .base import LossAccumulator, batch_labels, extract_loss
 
 
@@ -42,7 +44,8 @@ class NoPipelineSchedule:
                 with dp.microbatch_context(is_last_microbatch=True):
                     dp.backward(loss)
                 continue
-            acc.add(self._graphs[key].run(mb).clone(), batch_labels(mb))
+            with nvtx_range(f"graph mb {i}"):
+                acc.add(self._graphs[key].run(mb).clone(), batch_labels(mb))
 
     def forward_backward(self, microbatches, *, forward_only: bool = False
                          ) -> LossAccumulator:
@@ -55,11 +58,12 @@ class NoPipelineSchedule:
         for i, mb in enumerate(microbatches):
             last = i == m - 1
             if forward_only:
-                with torch.no_grad():
+                with torch.no_grad(), nvtx_range(f"eval mb {i}"):
                     extract_loss(self.stage(None, mb), mb, m, acc)
                 continue
-            with dp.forward_microbatch_context(synchronize_gradients=last):
+            with dp.forward_microbatch_context(synchronize_gradients=last), \
+                    nvtx_range(f"fwd mb {i}"):
                 loss = extract_loss(self.stage(None, mb), mb, m, acc)
-            with dp.microbatch_context(is_last_microbatch=last):
+            with dp.microbatch_context(is_last_microbatch=last), nvtx_range(f"bwd mb {i}"):
                 dp.backward(loss)
         return acc

@@ -50,8 +50,13 @@ class GraphedMicrobatch:
             self.static[k].copy_(mb[k], non_blocking=True)
 
     def _step(self) -> torch.Tensor:
-        out = self.stage(None, self.static)
-        (out / self.m).backward()
+        # A captured microbatch is never the gradient-synchronising one: outside these
+        # contexts a strategy's backward hooks (the overlap reducer) would launch
+        # reductions that the graph would then replay on every microbatch.
+        with self.dp.forward_microbatch_context(synchronize_gradients=False):
+            out = self.stage(None, self.static)
+        with self.dp.microbatch_context(is_last_microbatch=False):
+            (out / self.m).backward()
         return out.detach()
 
     def capture(self, mb: dict) -> None:

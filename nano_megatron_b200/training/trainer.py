@@ -23,6 +23,7 @@ import torch
 import torch.distributed as dist
 
 from nano_megatron_b200.parallel.group_plan import GroupKey
+from nano_megatron_b200.utils.profiling import nvtx_range
 from nano_megatron_b200.utils.timing import DeviceStepTimer, max_over_ranks
 
 from .batch_router import BatchRouter
@@ -129,6 +130,7 @@ class Trainer:
         self.data_iterator = data_iterator
         self.rng = rng
         self.health = health            # PeerHealth: host-side failure detection, optional
+        self.profiler = None            # utils.profiling.StepProfiler, optional
         self.state = TrainerState()
         self.device = device or next(model.parameters()).device
         data_parallel.configure_precision(config.precision)
@@ -189,6 +191,10 @@ class Trainer:
 
     def train_step(self, batch) -> dict[str, Any]:
         """One optimizer update. Returns device tensors (``loss``, ``grad_norm``...)."""
+        with nvtx_range(f"step {self.state.step}"):
+            return self._train_step(batch)
+
+    def _train_step(self, batch) -> dict[str, Any]:
         self.model.train()
         micro = self._prepare_batch(batch)
         dp = self.data_parallel
@@ -289,9 +295,12 @@ class Trainer:
         first_step = self.state.step
         self._last_saved = None
         health = getattr(self, "health", None)
+        profiler = getattr(self, "profiler", None)
         while self.state.step < target:
             if health is not None:
                 health.check()          # stop between steps if a peer failed
+            if profiler is not None:
+                profiler.before_step(self.state.step)
             data = getattr(self, "_data", None)
             saved = data.state_dict() if self.batch_router.is_source and \
                 callable(getattr(data, "state_dict", None)) else None
@@ -309,6 +318,8 @@ class Trainer:
                     health.report_failure(error)
                 raise
             self._record_data_state()
+            if profiler is not None:
+                profiler.after_step(self.state.step)
             device_ms += ms
             pending.append(out)
             if self.state.step % interval == 0 or self.state.step == target:

@@ -105,3 +105,26 @@ def test_train_resume_export_generate(tmp_path, capsys):
     assert len(g["generated_token_ids"]) <= 5 and g["text"].startswith("a tiny")
     with pytest.raises(SystemExit):
         gcli.main(["--model", str(tmp_path / "art")])
+
+
+def test_train_cli_writes_profiler_trace(tmp_path):
+    import yaml
+
+    from nano_megatron_b200.cli import train as trcli
+    from nano_megatron_b200.config import TrainConfig
+    from nano_megatron_b200.config.loader import config_to_dict
+
+    d = config_to_dict(TrainConfig())
+    d["distributed"].update(backend="gloo", device="cpu")
+    d["model"].update(layers=1, hidden_size=32, ffn_hidden_size=64, heads=4, seq_length=16,
+                      vocab_size=64)
+    d["precision"].update(params="float32", compute="float32")
+    d["training"].update(micro_batch_size=2, gradient_accumulation_steps=1, max_steps=4)
+    d["checkpoint"].update(directory=str(tmp_path / "runs"), save_final=False)
+    cfg = tmp_path / "c.yaml"
+    cfg.write_text(yaml.safe_dump(d))
+    trcli.main(["--config", str(cfg), "--profile-dir", str(tmp_path / "prof"),
+                "--profile-steps", "1:3"])
+    trace = json.loads((tmp_path / "prof" / "trace_rank0000.json").read_text())
+    names = {e.get("name", "") for e in trace.get("traceEvents", [])}
+    assert any("step" in n for n in names) or len(names) > 10
