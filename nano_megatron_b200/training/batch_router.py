@@ -65,7 +65,10 @@ class BatchRouter:
         out = {}
         for k, shape, dt in header:
             dtype = getattr(torch, dt.replace("torch.", ""))
-            t = batch[k].to(dev) if self.is_source else torch.empty(shape, dtype=dtype, device=dev)
+            # contiguous: loaders hand out views (input_ids / labels slice one [B, S+1]
+            # buffer) and a collective sends the tensor's storage as laid out
+            t = batch[k].to(dev).contiguous() if self.is_source else \
+                torch.empty(shape, dtype=dtype, device=dev)
             dist.broadcast(t, src=src, group=g.process_group)
             out[k] = t
         return out

@@ -206,6 +206,7 @@ class Trainer:
         dp.finalize_gradients()
         clip = self.config.optimizer.clip_grad_norm
         grad_norm = dp.clip_grad_norm(clip)
+        lr_used = dp.learning_rate      # the rate this update applies (the one to log)
         dp.optimizer_step()
         self.state.step += 1
         self.lr_scheduler.set_completed_steps(self.state.step)
@@ -217,7 +218,7 @@ class Trainer:
         self.state.consumed_tokens += gbs * self.config.model.seq_length
         loss_sum, count = aggregate_loss_metrics(acc, self.parallel, self.device)
         return {"loss_sum": loss_sum, "token_count": count, "grad_norm": grad_norm,
-                "learning_rate": dp.learning_rate}
+                "learning_rate": lr_used}
 
     @torch.no_grad()
     def evaluate_step(self, batch) -> tuple[torch.Tensor, torch.Tensor]:

@@ -161,3 +161,117 @@ def test_config_defaults_match(ref):
     ours["kernels"].pop("fused_tp_comm")
     ours["context_parallel"].pop("load_balance")
     assert ours == theirs
+
+
+def test_training_curve_matches_reference_cli(ref, tmp_path):
+    """Same YAML through the reference CLI (subprocess) and ours: identical per-step loss,
+    gradient norm and learning rate from the same seed (same init, same data order)."""
+    import json
+    import os
+    import subprocess
+
+    import yaml
+
+    from nano_megatron_b200.cli import train as trcli
+
+    d = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
+                        "gpt_single_cpu.yaml").read_text())
+    d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
+                      vocab_size=256, seq_length=32)
+    d["training"]["max_steps"] = 4
+    d["optimizer"]["clip_grad_norm"] = 1.0
+
+    def write(name):
+        d["checkpoint"]["directory"] = str(tmp_path / name)
+        p = tmp_path / f"{name}.yaml"
+        p.write_text(yaml.safe_dump(d))
+        return p
+
+    ref_cfg, our_cfg = write("ref"), write("ours")
+    env = dict(os.environ, PYTHONPATH=str(REF))
+    code = ("import sys; from pathlib import Path; from nano_megatron.cli.train import run; "
+            "run(Path(sys.argv[1]), overrides=[], resume=None, max_steps=None)")
+    r = subprocess.run([sys.executable, "-c", code, str(ref_cfg)], env=env,
+                       capture_output=True, text=True, timeout=600, cwd=tmp_path)
+    assert r.returncode == 0, r.stderr[-3000:]
+    trcli.run(our_cfg, log=lambda *_: None)
+
+    def curve(name):
+        run_dir = next((tmp_path / name).iterdir())
+        recs = [json.loads(x) for x in (run_dir / "metrics.jsonl").read_text().splitlines()
+                if x.strip()]
+        return [(x["step"], x["metrics"]["loss"], x["metrics"]["grad_norm"],
+                 x["metrics"]["learning_rate"]) for x in recs if x["prefix"] == "train"]
+
+    theirs, ours = curve("ref"), curve("ours")
+    assert [s for s, *_ in theirs] == [s for s, *_ in ours] == [1, 2, 3, 4]
+    for (s, l1, g1, lr1), (_, l2, g2, lr2) in zip(theirs, ours):
+        assert l2 == pytest.approx(l1, rel=2e-6), (s, theirs, ours)
+        assert g2 == pytest.approx(g1, rel=1e-5), (s, theirs, ours)
+        assert lr2 == pytest.approx(lr1, rel=1e-12), (s, theirs, ours)
+
+
+def _our_cli_rank(rank, world, cfg_path):
+    from nano_megatron_b200.cli import train as trcli
+
+    trcli.run(Path(cfg_path), log=lambda *_: None)
+
+
+LAYOUTS = {
+    "tp2_sp": {"tensor": 2, "data": 1, "sequence_parallel": True},
+    "pp2_1f1b": {"pipeline": 2, "data": 1},
+    "dp2": {"data": 2},
+}
+
+
+@pytest.mark.distributed
+@pytest.mark.parametrize("layout", list(LAYOUTS))
+def test_multirank_training_curve_matches_reference(ref, tmp_path, layout):
+    import json
+    import os
+    import random
+    import subprocess
+
+    import yaml
+
+    from dist_utils import run_ranks
+
+    d = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
+                        "gpt_single_cpu.yaml").read_text())
+    d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
+                      vocab_size=256, seq_length=32)
+    d["parallel"].update(LAYOUTS[layout])
+    if layout == "pp2_1f1b":
+        d["pipeline"].update(schedule="1f1b")
+    d["training"].update(max_steps=3, micro_batch_size=2, gradient_accumulation_steps=2)
+    d["optimizer"]["clip_grad_norm"] = 1.0
+
+    def write(name):
+        d["checkpoint"]["directory"] = str(tmp_path / name)
+        p = tmp_path / f"{name}.yaml"
+        p.write_text(yaml.safe_dump(d))
+        return p
+
+    ref_cfg, our_cfg = write("ref"), write("ours")
+    env = dict(os.environ, PYTHONPATH=str(REF), OMP_NUM_THREADS="1")
+    port = random.randint(30000, 45000)
+    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                        "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+                        "--master-port", str(port), "-m", "nano_megatron.cli.train",
+                        "--config", str(ref_cfg)],
+                       env=env, capture_output=True, text=True, timeout=900, cwd=tmp_path)
+    assert r.returncode == 0, r.stderr[-3000:]
+    run_ranks(2, _our_cli_rank, str(our_cfg))
+
+    def curve(name):
+        run_dir = next((tmp_path / name).iterdir())
+        recs = [json.loads(x) for x in (run_dir / "metrics.jsonl").read_text().splitlines()
+                if x.strip()]
+        return [(x["step"], x["metrics"]["loss"], x["metrics"]["grad_norm"])
+                for x in recs if x["prefix"] == "train"]
+
+    theirs, ours = curve("ref"), curve("ours")
+    assert len(theirs) == len(ours) == 3
+    for (s, l1, g1), (_, l2, g2) in zip(theirs, ours):
+        assert l2 == pytest.approx(l1, rel=1e-5), (layout, s, theirs, ours)
+        assert g2 == pytest.approx(g1, rel=1e-4), (layout, s, theirs, ours)
