@@ -340,6 +340,10 @@ class CheckpointManager:
         elif manifest.storage_backend == "torch.save":
             model_state = _torch_load(path / "model.pt")
             dp_state = _torch_load(path / "data_parallel.pt")
+        elif manifest.storage_backend == "torch.distributed.checkpoint":
+            # single-process checkpoints written by the reference (DCP directory "dcp/")
+            model_state = _read_dcp_model(path / "dcp")
+            dp_state = _torch_load(path / "data_parallel.pt")
         else:
             raise ValueError(f"unsupported checkpoint backend {manifest.storage_backend!r}")
         if not isinstance(model_state, Mapping) or not isinstance(dp_state, Mapping):
@@ -464,6 +468,26 @@ def portable_run_config(run_config):
     if isinstance(d.get("kernels"), dict) and d["kernels"].get("backend") == "b200":
         d["kernels"]["backend"] = "torch"
     return d
+
+
+def _read_dcp_model(directory: Path) -> dict:
+    """Model state of a ``torch.distributed.checkpoint`` directory saved as {"model": ...},
+    read into CPU tensors allocated from the checkpoint's own metadata (no process group
+    needed; every rank may read it)."""
+    import torch.distributed.checkpoint as dcp
+
+    meta = dcp.FileSystemReader(str(directory)).read_metadata()
+    target: dict = {}
+    for fqn, md in meta.state_dict_metadata.items():
+        if not fqn.startswith("model."):
+            continue
+        props = getattr(md, "properties", None)
+        if props is None or not hasattr(md, "size"):
+            continue
+        target[fqn[len("model."):]] = torch.empty(tuple(md.size), dtype=props.dtype)
+    state = {"model": target}
+    dcp.load(state, checkpoint_id=str(directory), no_dist=True)
+    return state["model"]
 
 
 def _write_payloads(payloads) -> None:

@@ -275,3 +275,119 @@ def test_multirank_training_curve_matches_reference(ref, tmp_path, layout):
     for (s, l1, g1), (_, l2, g2) in zip(theirs, ours):
         assert l2 == pytest.approx(l1, rel=1e-5), (layout, s, theirs, ours)
         assert g2 == pytest.approx(g1, rel=1e-4), (layout, s, theirs, ours)
+
+
+def _ref_cli(cfg: Path, tmp: Path, *extra: str, nproc: int = 1) -> None:
+    import os
+    import random
+    import subprocess
+
+    env = dict(os.environ, PYTHONPATH=str(REF), OMP_NUM_THREADS="1")
+    if nproc == 1:
+        cmd = [sys.executable, "-m", "nano_megatron.cli.train", "--config", str(cfg), *extra]
+    else:
+        cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node",
+               str(nproc), "--master-addr", "127.0.0.1", "--master-port",
+               str(random.randint(30000, 45000)), "-m", "nano_megatron.cli.train", "--config",
+               str(cfg), *extra]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=900, cwd=tmp)
+    assert r.returncode == 0, r.stderr[-3000:]
+
+
+def _curve(run_dir: Path):
+    import json
+
+    recs = [json.loads(x) for x in (run_dir / "metrics.jsonl").read_text().splitlines()
+            if x.strip()]
+    return {x["step"]: x["metrics"]["loss"] for x in recs if x["prefix"] == "train"}
+
+
+def _our_resume_rank(rank, world, cfg, ckpt):
+    from nano_megatron_b200.cli import train as trcli
+
+    trcli.run(Path(cfg), resume=Path(ckpt), max_steps=4, log=lambda *_: None)
+
+
+@pytest.mark.distributed
+@pytest.mark.parametrize("world", [1, 2])
+def test_resume_from_reference_checkpoint(ref, tmp_path, world):
+    """The reference trains 2 steps and checkpoints (single process: DCP; 2 ranks DP2:
+    rank-local torch.save); our framework resumes that checkpoint and its steps 3-4
+    reproduce the losses of the reference's uninterrupted 4-step run."""
+    import yaml
+
+    from dist_utils import run_ranks
+
+    d = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
+                        "gpt_single_cpu.yaml").read_text())
+    d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
+                      vocab_size=256, seq_length=32)
+    d["parallel"]["data"] = world
+    d["training"].update(max_steps=4, gradient_accumulation_steps=2 // world)
+    d["checkpoint"].update(save_interval=2, keep_last=4)
+
+    def write(name):
+        d["checkpoint"]["directory"] = str(tmp_path / name)
+        p = tmp_path / f"{name}.yaml"
+        p.write_text(yaml.safe_dump(d))
+        return p
+
+    full_cfg, part_cfg, ours_cfg = write("full"), write("part"), write("ours")
+    _ref_cli(full_cfg, tmp_path, nproc=world)
+    _ref_cli(part_cfg, tmp_path, "--max-steps", "2", nproc=world)
+    ref_full = _curve(next((tmp_path / "full").iterdir()))
+    ckpt = next((tmp_path / "part").iterdir()) / "step_00000002"
+    assert (ckpt / ".complete").is_file()
+    if world == 1:
+        from nano_megatron_b200.cli import train as trcli
+
+        trcli.run(ours_cfg, resume=ckpt, max_steps=4, log=lambda *_: None)
+    else:
+        run_ranks(world, _our_resume_rank, str(ours_cfg), str(ckpt))
+    ours = _curve(sorted((tmp_path / "ours").iterdir())[-1])
+    assert sorted(ours) == [1, 2, 3, 4]                   # replayed prefix + resumed steps
+    for step in (3, 4):
+        assert ours[step] == pytest.approx(ref_full[step], rel=2e-6), (step, ours, ref_full)
+
+
+def _our_train_rank(rank, world, cfg, steps):
+    from nano_megatron_b200.cli import train as trcli
+
+    trcli.run(Path(cfg), max_steps=steps, log=lambda *_: None)
+
+
+@pytest.mark.distributed
+@pytest.mark.parametrize("world", [1, 2])
+def test_reference_resumes_our_checkpoint(ref, tmp_path, world):
+    """We train 2 steps and checkpoint; the reference's own CLI resumes that checkpoint and
+    its steps 3-4 reproduce the losses of our uninterrupted 4-step run."""
+    import yaml
+
+    from dist_utils import run_ranks
+
+    d = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
+                        "gpt_single_cpu.yaml").read_text())
+    d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
+                      vocab_size=256, seq_length=32)
+    d["parallel"]["data"] = world
+    d["training"].update(max_steps=4, gradient_accumulation_steps=2 // world)
+    d["checkpoint"].update(save_interval=2, keep_last=4)
+
+    def write(name):
+        d["checkpoint"]["directory"] = str(tmp_path / name)
+        p = tmp_path / f"{name}.yaml"
+        p.write_text(yaml.safe_dump(d))
+        return p
+
+    full_cfg, part_cfg, ref_cfg = write("full"), write("part"), write("ref")
+    for cfg, steps in ((full_cfg, 4), (part_cfg, 2)):
+        if world == 1:
+            _our_train_rank(0, 1, str(cfg), steps)
+        else:
+            run_ranks(world, _our_train_rank, str(cfg), steps)
+    ours_full = _curve(next((tmp_path / "full").iterdir()))
+    ckpt = next((tmp_path / "part").iterdir()) / "step_00000002"
+    _ref_cli(ref_cfg, tmp_path, "--resume", str(ckpt), "--max-steps", "4", nproc=world)
+    theirs = _curve(sorted((tmp_path / "ref").iterdir())[-1])
+    for step in (3, 4):
+        assert theirs[step] == pytest.approx(ours_full[step], rel=2e-6), (step, theirs, ours_full)
