@@ -1,14 +1,18 @@
 """Headline benchmark: device-timed training tokens/s of the 311M GPT.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--config 311m|1p3b-cp|1p3b-zero1|1p3b-zero2|1p3b-zero3|8b]
     torchrun --nproc-per-node N bench.py --gpus N ...        (N > 1)
 
-Config (the reference's headline 311M config): 24 layers, hidden 1024, 16 MHA
-heads of 64, SwiGLU 2736, vocab 8192 (310,821,888 parameters), seq 512, global
+Default config (the reference's headline 311M config): 24 layers, hidden 1024, 16
+MHA heads of 64, SwiGLU 2736, vocab 8192 (310,821,888 parameters), seq 512, global
 batch 256, micro-batch 8, bf16, AdamW lr 3e-4 cosine, clip 1.0, DDP bucketed
 all-reduce. Layout by GPU count: 1 -> TP1, 2 -> TP2+SP, 4 -> TP2xPP2+SP (1F1B,
 P2P overlap), 8 -> TP2xPP2xDP2+SP. Data: synthetic uniform-random token ids;
-random-init weights.
+random-init weights. ``--config`` selects the other benchmark configs of the
+project (1.3B ring-CP at 32k tokens, 1.3B ZeRO-1/2/3, the 8B shape under
+TP4xPP2 interleaved 1F1B with full activation checkpointing); ``WORKLOADS``
+lists their layouts per GPU count. All use a fixed global batch (strong scaling).
 
 ``value`` is whole-job tokens/s from CUDA events around exactly K train steps
 (barrier + synchronize on both sides, max over ranks). ``e2e`` repeats the K
@@ -29,34 +33,121 @@ import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-MODEL = {"layers": 24, "hidden_size": 1024, "ffn_hidden_size": 2736, "heads": 16,
-         "kv_heads": 16, "seq_length": 512, "vocab_size": 8192, "dropout": 0.0,
-         "tie_embeddings": True}
-GLOBAL_BATCH = 256
-MICRO_BATCH = 8
-LAYOUTS = {1: (1, 1, 1), 2: (2, 1, 1), 4: (2, 2, 1), 8: (2, 2, 2)}  # (tp, pp, dp)
+METRIC = "tokens/sec (device-timed, max over ranks) for {} at 1/2/4/8 B200"
+_L1P3B = {"layers": 24, "hidden_size": 2048, "ffn_hidden_size": 5504, "heads": 16,
+          "kv_heads": 4, "vocab_size": 8192, "dropout": 0.0, "tie_embeddings": True}
+
+
+def _zero(mode: str) -> dict:
+    return {
+        "title": "1.3B DP8 " + mode.upper(),
+        "describe": f"GPT-1.3B (24L, H2048, 16 q / 4 kv heads of 128, F5504, V8192), {mode}",
+        "model": dict(_L1P3B, seq_length=2048), "global_batch": 128, "micro_batch": 4,
+        "layouts": {n: {"data": n} for n in (1, 2, 4, 8)},
+        "sections": {"data_parallel": {"mode": mode, "overlap_grad_reduce": True}},
+        # the reference keeps fp32 masters under FSDP2 only with fp32 parameters
+        "reference_sections": {"precision": {"params": "float32", "compute": "bfloat16"}}
+        if mode == "zero3" else {},
+    }
+
+
+# The BASELINE configs. ``layouts`` maps GPU count -> parallel sizes; the global batch is
+# fixed across GPU counts (strong scaling), so gradient accumulation = global / (mb * dp).
+WORKLOADS = {
+    "311m": {
+        "title": "311M TP2xPP2xDP2",
+        "describe": "GPT-311M (24L, H1024, 16 heads, F2736, V8192, tied)",
+        "model": {"layers": 24, "hidden_size": 1024, "ffn_hidden_size": 2736, "heads": 16,
+                  "kv_heads": 16, "seq_length": 512, "vocab_size": 8192, "dropout": 0.0,
+                  "tie_embeddings": True},
+        "global_batch": 256, "micro_batch": 8,
+        "layouts": {1: {}, 2: {"tensor": 2}, 4: {"tensor": 2, "pipeline": 2},
+                    8: {"tensor": 2, "pipeline": 2, "data": 2}},
+        "sections": {"pipeline": {"schedule": "1f1b", "overlap_p2p": True},
+                     "data_parallel": {"mode": "ddp", "overlap_grad_reduce": True}},
+    },
+    "1p3b-cp": {
+        "title": "1.3B TP2xCP4 seq 32768",
+        "describe": "GPT-1.3B (24L, H2048, 16 q / 4 kv heads of 128, F5504, V8192), "
+                    "ring CP with load-balanced chunks",
+        "model": dict(_L1P3B, seq_length=32768), "global_batch": 8, "micro_batch": 1,
+        "layouts": {1: {}, 2: {"context": 2}, 4: {"tensor": 2, "context": 2},
+                    8: {"tensor": 2, "context": 4}},
+        "sections": {"context_parallel": {"backend": "ring", "load_balance": True},
+                     "data_parallel": {"mode": "ddp", "overlap_grad_reduce": True}},
+        # the reference has no load-balanced chunking (contiguous CP shards)
+        "reference_sections": {"context_parallel": {"backend": "ring"}},
+    },
+    "1p3b-zero1": _zero("zero1"),
+    "1p3b-zero2": _zero("zero2"),
+    "1p3b-zero3": _zero("zero3"),
+    "8b": {
+        "title": "8B-shape TP4xPP2 interleaved",
+        "describe": "Llama-style 8B shape (32L, H4096, 32 q / 8 kv heads of 128, F14336, "
+                    "V32768, untied, rope 5e5), full activation checkpointing",
+        "model": {"layers": 32, "hidden_size": 4096, "ffn_hidden_size": 14336, "heads": 32,
+                  "kv_heads": 8, "seq_length": 4096, "vocab_size": 32768, "dropout": 0.0,
+                  "rope_theta": 500000.0, "tie_embeddings": False},
+        "global_batch": 64, "micro_batch": 1,
+        # 8B with fp32 masters and Adam moments does not fit one 180 GB GPU
+        "layouts": {2: {"tensor": 2}, 4: {"tensor": 4},
+                    8: {"tensor": 4, "pipeline": 2, "virtual": 2}},
+        "sections": {"activation_checkpoint": {"mode": "full"},
+                     "data_parallel": {"mode": "ddp", "overlap_grad_reduce": True}},
+    },
+}
 BASELINE_PUBLISHED = None  # the reference publishes no throughput number
 
 
-def make_config_dict(n_gpus: int, steps: int) -> dict:
-    tp, pp, dp = LAYOUTS[n_gpus]
-    gas = GLOBAL_BATCH // (MICRO_BATCH * dp)
-    return {
+def layout_of(workload: str, n_gpus: int) -> dict:
+    w = WORKLOADS[workload]
+    if n_gpus not in w["layouts"]:
+        raise SystemExit(f"--config {workload} runs on {sorted(w['layouts'])} GPUs, "
+                         f"not {n_gpus}")
+    lay = {"tensor": 1, "pipeline": 1, "context": 1, "data": 1, "virtual": 1}
+    lay.update(w["layouts"][n_gpus])
+    return lay
+
+
+def layout_name(lay: dict) -> str:
+    parts = [f"{n}{lay[k]}" for n, k in (("tp", "tensor"), ("cp", "context"),
+                                          ("pp", "pipeline"), ("dp", "data")) if lay[k] > 1]
+    if lay["virtual"] > 1:
+        parts.append(f"v{lay['virtual']}")
+    return "".join(parts) or "tp1"
+
+
+def make_config_dict(n_gpus: int, steps: int, workload: str = "311m", *,
+                     reference: bool = False) -> dict:
+    w = WORKLOADS[workload]
+    lay = layout_of(workload, n_gpus)
+    tp, pp, dp = lay["tensor"], lay["pipeline"], lay["data"]
+    gas = w["global_batch"] // (w["micro_batch"] * dp)
+    horizon = max(10488, steps + 100)
+    d = {
         "distributed": {"backend": "nccl", "device": "cuda", "timeout_minutes": 10},
-        "parallel": {"tensor": tp, "pipeline": pp, "context": 1, "expert": 1, "data": dp,
-                     "order": ["tp", "cp", "ep", "dp", "pp"], "sequence_parallel": tp > 1},
-        "model": dict(MODEL),
+        "parallel": {"tensor": tp, "pipeline": pp, "context": lay["context"], "expert": 1,
+                     "data": dp, "order": ["tp", "cp", "ep", "dp", "pp"],
+                     "sequence_parallel": tp > 1},
+        "model": dict(w["model"]),
         "precision": {"params": "bfloat16", "compute": "bfloat16", "grad_reduce": "float32"},
-        "data_parallel": {"mode": "ddp", "bucket_bytes": 268435456,
-                          "overlap_grad_reduce": True},
+        "data_parallel": {"mode": "ddp", "bucket_bytes": 268435456, "overlap_grad_reduce": True},
         "pipeline": {"schedule": "1f1b", "overlap_p2p": True},
         "optimizer": {"lr": 3e-4, "betas": [0.9, 0.95], "eps": 1e-8, "weight_decay": 0.1,
                       "clip_grad_norm": 1.0},
-        "lr_scheduler": {"schedule": "cosine", "warmup_steps": 0,
-                         "decay_steps": max(10488, steps + 100), "min_lr": 3e-5},
-        "training": {"micro_batch_size": MICRO_BATCH, "gradient_accumulation_steps": gas,
-                     "max_steps": max(10488, steps + 100), "seed": 1234, "log_interval": 10},
+        "lr_scheduler": {"schedule": "cosine", "warmup_steps": 0, "decay_steps": horizon,
+                         "min_lr": 3e-5},
+        "training": {"micro_batch_size": w["micro_batch"], "gradient_accumulation_steps": gas,
+                     "max_steps": horizon, "seed": 1234, "log_interval": 10},
     }
+    sections = dict(w.get("sections", {}))
+    if reference:
+        sections.update(w.get("reference_sections", {}))
+    for k, v in sections.items():
+        d.setdefault(k, {}).update(v)
+    if lay["virtual"] > 1:
+        d["pipeline"].update(schedule="interleaved_1f1b", virtual_stages_per_rank=lay["virtual"])
+    return d
 
 
 # ---------------------------------------------------------------------- clocks
@@ -195,7 +286,7 @@ def run_ours(args, rank, world, local):
     from nano_megatron_b200.training import Trainer
     from nano_megatron_b200.training.engine import build_training_components
 
-    d = make_config_dict(args.gpus, args.steps + args.warmup)
+    d = make_config_dict(args.gpus, args.steps + args.warmup, args.config)
     d["kernels"] = {"backend": "b200", "fused_tp_comm": not args.no_fused_tp,
                     "cuda_graphs": not args.no_cuda_graphs}
     cfg = config_from_dict(d)
@@ -204,9 +295,9 @@ def run_ours(args, rank, world, local):
     device = runtime.device
     trainer = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
                       data_parallel=comps.data_parallel, rng=comps.rng, device=device)
-    dp = comps.parallel.dp.size
-    rows = GLOBAL_BATCH // dp
-    batches = synthetic_batches(4, rows, MODEL["seq_length"], MODEL["vocab_size"],
+    w = WORKLOADS[args.config]
+    rows = w["global_batch"] // comps.parallel.dp.size
+    batches = synthetic_batches(4, rows, w["model"]["seq_length"], w["model"]["vocab_size"],
                                 seed=1234 + comps.parallel.coordinate.dp)
     src = trainer.batch_router.is_source
     lib = _ext.lib()
@@ -236,7 +327,7 @@ def run_reference(args, rank, world, local):
     from nano_megatron.parallel import ParallelContext, ParallelRNG, ParameterDomainRegistry, RNGStream
     from nano_megatron.training import Trainer
 
-    d = make_config_dict(args.gpus, args.steps + args.warmup)
+    d = make_config_dict(args.gpus, args.steps + args.warmup, args.config, reference=True)
     d["wandb"] = {"enabled": False}
     cfg = config_from_dict(d)
     runtime = DistributedRuntime(cfg.distributed).initialize()
@@ -248,7 +339,12 @@ def run_reference(args, rank, world, local):
     builder = GPTModelBuilder(DenseGPTComponents(cp_attention=cp_attention),
                               parameter_domains=ParameterDomainRegistry(),
                               activation_checkpoint_config=cfg.activation_checkpoint)
-    built = builder.build_stage(cfg.model, parallel, kernels, rng=rng)
+    if cfg.pipeline.virtual_stages_per_rank > 1:
+        built = builder.build_pipeline(cfg.model, parallel, kernels,
+                                       virtual_stages_per_rank=cfg.pipeline.virtual_stages_per_rank,
+                                       rng=rng)
+    else:
+        built = builder.build_stage(cfg.model, parallel, kernels, rng=rng)
     dtype = {"bfloat16": torch.bfloat16, "float32": torch.float32}[cfg.precision.params.value]
     model = built.model.to(device=runtime.device, dtype=dtype)
     strategy = build_data_parallel_strategy(cfg.data_parallel, cfg.offload, parallel,
@@ -256,8 +352,9 @@ def run_reference(args, rank, world, local):
     trainer = Trainer(config=cfg, model=model, parallel=parallel, data_parallel=strategy,
                       rng=rng)
     device = runtime.device
-    rows = GLOBAL_BATCH // parallel.dp.size
-    batches = synthetic_batches(4, rows, MODEL["seq_length"], MODEL["vocab_size"],
+    w = WORKLOADS[args.config]
+    rows = w["global_batch"] // parallel.dp.size
+    batches = synthetic_batches(4, rows, w["model"]["seq_length"], w["model"]["vocab_size"],
                                 seed=1234 + parallel.coordinate.dp)
     src = trainer.batch_router.is_source
     with ClockSampler(local) as clocks:
@@ -274,25 +371,26 @@ def unavailable(why: str) -> int:
 
 
 def finish(args, rank, world, dev_ms, e2e_ms, e2e_wall_ms, clocks, launches, *, impl, runtime):
-    tokens_per_step = GLOBAL_BATCH * MODEL["seq_length"]
+    w = WORKLOADS[args.config]
+    seq, gb = w["model"]["seq_length"], w["global_batch"]
+    tokens_per_step = gb * seq
     value = tokens_per_step * args.steps / (dev_ms / 1000.0)
     e2e_value = tokens_per_step * args.steps / (e2e_ms / 1000.0)
-    tp, pp, dp = LAYOUTS[args.gpus]
-    layout = "".join(f"{n}{s}" for n, s in (("tp", tp), ("pp", pp), ("dp", dp)) if s > 1) or "tp1"
+    lay = layout_of(args.config, args.gpus)
     line = {
-        "metric": "tokens/sec (device-timed, max over ranks) for 311M TP2xPP2xDP2 at 1/2/4/8 B200",
+        "metric": METRIC.format(w["title"]),
         "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dev_ms / args.steps, "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None if BASELINE_PUBLISHED is None else value / BASELINE_PUBLISHED,
         "dtype": "bf16", "data": "synthetic uniform-random token ids, random-init weights",
-        "config": {"model": "GPT-311M (24L, H1024, 16 heads, F2736, V8192, tied)",
-                   "global_batch": GLOBAL_BATCH, "seq_len": MODEL["seq_length"],
-                   "micro_batch": MICRO_BATCH, "parallelism": layout,
-                   "l2": "no flush: weights (622 MB) and activations exceed the 126 MB L2"},
+        "config": {"model": w["describe"], "name": args.config,
+                   "global_batch": gb, "seq_len": seq,
+                   "micro_batch": w["micro_batch"], "parallelism": layout_name(lay),
+                   "l2": "no flush: weights (>= 622 MB) and activations exceed the 126 MB L2"},
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "wall_ms_per_step": e2e_wall_ms / args.steps,
-                "h2d_bytes_per_step": 2 * (GLOBAL_BATCH // dp) * MODEL["seq_length"] * 8,
+                "h2d_bytes_per_step": 2 * (gb // lay["data"]) * seq * 8,
                 "d2h_bytes_per_step": 8},
         "impl": impl,
     }
@@ -310,7 +408,9 @@ def finish(args, rank, world, dev_ms, e2e_ms, e2e_wall_ms, clocks, launches, *, 
 
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    ap.add_argument("--gpus", type=int, default=1, choices=sorted(LAYOUTS))
+    ap.add_argument("--gpus", type=int, default=1, choices=[1, 2, 4, 8])
+    ap.add_argument("--config", default="311m", choices=sorted(WORKLOADS),
+                    help="benchmark workload (default: the headline 311M config)")
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
@@ -322,6 +422,7 @@ def main() -> int:
                          "CUDA graph per microbatch")
     args = ap.parse_args()
     rank, world, local = dist_env()
+    layout_of(args.config, args.gpus)
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch with torchrun")
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")

@@ -4,7 +4,9 @@ The reference pickles each batch and broadcasts it as a Python object every
 step (src/nano_megatron/training/batch_router.py:30-121). Here the source
 moves the token tensors to the device once and broadcasts them as tensors over
 the batch-replica communicator (NCCL over NVLink), then every rank slices its
-context-parallel part (contiguous or zigzag).
+context-parallel part (contiguous or zigzag). The key/shape/dtype header is sent
+once: batches keep one layout for the life of the router (the source raises
+before sending a batch of another layout).
 """
 
 from __future__ import annotations
@@ -56,12 +58,19 @@ class BatchRouter:
             header = [(k, tuple(batch[k].shape), str(batch[k].dtype)) for k in keys]
         else:
             header = None
-        box = [header]
-        dist.broadcast_object_list(box, src=src, group=g.process_group) \
-            if self._shape_cache.get("header") is None else None
-        if self._shape_cache.get("header") is None:
-            self._shape_cache["header"] = box[0]
-        header = self._shape_cache["header"]
+        cached = self._shape_cache.get("header")
+        if cached is None:
+            # The key / shape / dtype header crosses once; later steps send tensors only,
+            # so the peers never wait on the host for the source.
+            box = [header]
+            dist.broadcast_object_list(box, src=src, group=g.process_group)
+            self._shape_cache["header"] = cached = box[0]
+        elif self.is_source and header != cached:
+            # The peers post receives of the cached shapes; sending others would mismatch.
+            raise ValueError(f"batch layout changed after the first step: {header} != "
+                             f"{cached}; the peers of a batch-replica group need batches of "
+                             "one fixed shape")
+        header = cached
         out = {}
         for k, shape, dt in header:
             dtype = getattr(torch, dt.replace("torch.", ""))

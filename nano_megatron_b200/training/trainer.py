@@ -24,7 +24,7 @@ import torch.distributed as dist
 
 from nano_megatron_b200.parallel.group_plan import GroupKey
 from nano_megatron_b200.utils.profiling import nvtx_range
-from nano_megatron_b200.utils.timing import DeviceStepTimer, max_over_ranks
+from nano_megatron_b200.utils.timing import DeviceStepTimer, StepPhaseTimer, summarize_phases
 
 from .batch_router import BatchRouter
 from .lr_scheduler import LearningRateScheduler
@@ -145,6 +145,7 @@ class Trainer:
                                                   data_parallel=data_parallel,
                                                   max_steps=config.training.max_steps)
         self.timer = DeviceStepTimer(self.device)
+        self.phases = StepPhaseTimer(self.device)
         self.last_step_ms: float | None = None
         self.metrics_path = metrics_path
         self.resume_metrics_path = resume_metrics_path
@@ -200,14 +201,18 @@ class Trainer:
         dp = self.data_parallel
         dp.zero_grad()
         acc = self.schedule.forward_backward(micro, forward_only=False)
+        self.phases.mark("forward_backward")
         sync = getattr(self.model, "synchronize_tied_embedding_gradients", None)
         if callable(sync):
             sync()
         dp.finalize_gradients()
+        self.phases.mark("grad_sync")
         clip = self.config.optimizer.clip_grad_norm
         grad_norm = dp.clip_grad_norm(clip)
+        self.phases.mark("clip")
         lr_used = dp.learning_rate      # the rate this update applies (the one to log)
         dp.optimizer_step()
+        self.phases.mark("optimizer")
         self.state.step += 1
         self.lr_scheduler.set_completed_steps(self.state.step)
         self.state.lr_scheduler = self.lr_scheduler.state_dict()
@@ -291,8 +296,8 @@ class Trainer:
         target = max_steps if max_steps is not None else self.config.training.max_steps
         interval = self.config.training.log_interval
         pending: list = []
+        marks: list = []
         t0 = time.perf_counter()
-        device_ms = 0.0
         first_step = self.state.step
         self._last_saved = None
         health = getattr(self, "health", None)
@@ -307,7 +312,9 @@ class Trainer:
                 callable(getattr(data, "state_dict", None)) else None
             try:
                 batch = next(self.data_iterator) if self.batch_router.is_source else None
-                out, ms = self.timed_train_step(batch)
+                self.phases.begin()
+                out = self.train_step(batch)
+                step_marks = self.phases.end()
             except BaseException as error:
                 # Leave the data position at the last completed step (as the reference
                 # does) so a checkpoint taken by the caller resumes exactly, and tell the
@@ -321,11 +328,11 @@ class Trainer:
             self._record_data_state()
             if profiler is not None:
                 profiler.after_step(self.state.step)
-            device_ms += ms
+            marks.append(step_marks)
             pending.append(out)
             if self.state.step % interval == 0 or self.state.step == target:
-                self._log(pending, time.perf_counter() - t0, device_ms, log)
-                pending, device_ms, t0 = [], 0.0, time.perf_counter()
+                self._log(pending, time.perf_counter() - t0, marks, log)
+                pending, marks, t0 = [], [], time.perf_counter()
             self._after_step(log)
         ck = self.config.checkpoint
         if self.checkpoint is not None and ck.save_final and self.state.step > first_step and \
@@ -378,7 +385,10 @@ class Trainer:
                                             "checkpoint/best_validation_step": self.state.step})
         return metrics
 
-    def _log(self, pending, host_s, device_ms, log) -> None:
+    def _log(self, pending, host_s, marks, log) -> None:
+        """One log record for the steps in ``pending``. Device times come from the steps'
+        phase marks (CUDA events), max over ranks per phase; ``time_<phase>_ms`` are
+        per-step averages."""
         loss_sum = sum(float(p["loss_sum"]) for p in pending)
         count = sum(float(p["token_count"]) for p in pending)
         loss = loss_sum / max(count, 1.0)
@@ -388,13 +398,17 @@ class Trainer:
             self.config.training.gradient_accumulation_steps * \
             self.parallel.dp.size * self.parallel.ep.size
         tokens = n * gbs * self.config.model.seq_length
-        dev_max = max_over_ranks(device_ms, self.device)
+        phases = summarize_phases(marks, self.device)
+        dev_max = phases["step"]
         metrics = {"step": self.state.step, "loss": loss,
                    "perplexity": math.exp(min(loss, 50.0)), "token_count": count,
                    "grad_norm": gn, "learning_rate": pending[-1]["learning_rate"],
                    "samples_per_second": n * gbs / max(host_s, 1e-9),
                    "tokens_per_second": tokens / max(host_s, 1e-9),
                    "tokens_per_second_device": tokens / max(dev_max / 1000.0, 1e-9)}
+        for k, v in phases.items():
+            metrics[f"time_{k}_ms"] = v / n
+        self.last_step_ms = phases["step"] / n
         if self.device.type == "cuda":
             gib = 1024 ** 3
             metrics.update({

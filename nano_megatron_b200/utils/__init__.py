@@ -1,5 +1,5 @@
 """Small shared utilities (device timing, NVTX ranges)."""
 
-from .timing import DeviceStepTimer, max_over_ranks
+from .timing import DeviceStepTimer, StepPhaseTimer, max_over_ranks, summarize_phases
 
-__all__ = ["DeviceStepTimer", "max_over_ranks"]
+__all__ = ["DeviceStepTimer", "StepPhaseTimer", "max_over_ranks", "summarize_phases"]

@@ -8,7 +8,7 @@
   ``[start, stop)`` and writes one Chrome trace per rank into a directory.
 
 The reference has neither (profiling lives only in its GPU tests); device-timed
-tokens/s per step comes from ``utils.timing.DeviceStepTimer``.
+tokens/s and per-phase step times come from ``utils.timing.StepPhaseTimer``.
 """
 
 from __future__ import annotations

@@ -391,3 +391,39 @@ def test_reference_resumes_our_checkpoint(ref, tmp_path, world):
     theirs = _curve(sorted((tmp_path / "ref").iterdir())[-1])
     for step in (3, 4):
         assert theirs[step] == pytest.approx(ours_full[step], rel=2e-6), (step, theirs, ours_full)
+
+
+def _bench_module():
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location("nmb_bench", Path(__file__).parents[1] /
+                                                  "bench.py")
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def test_bench_workloads_validate_in_both_frameworks(ref):
+    """Every benchmark config (each GPU count) is a valid run config for both arms."""
+    from nano_megatron_b200.config import config_from_dict
+    from nano_megatron_b200.config.validation import validate_config
+
+    from nano_megatron.config import config_from_dict as ref_from_dict
+    from nano_megatron.config.validation import validate_config as ref_validate
+
+    bench = _bench_module()
+    for name, w in bench.WORKLOADS.items():
+        for n in w["layouts"]:
+            ours = config_from_dict(bench.make_config_dict(n, 8, name))
+            res = validate_config(ours, world_size=n)
+            assert not getattr(res, "errors", ()), (name, n, res)
+            d = bench.make_config_dict(n, 8, name, reference=True)
+            d["wandb"] = {"enabled": False}
+            theirs = ref_from_dict(d)
+            ref_res = ref_validate(theirs, world_size=n)
+            assert not getattr(ref_res, "errors", ()), (name, n, ref_res)
+            lay = bench.layout_of(name, n)
+            size = lay["tensor"] * lay["pipeline"] * lay["context"] * lay["data"]
+            assert size == n, (name, n, lay)
+            mb, gas = ours.training.micro_batch_size, ours.training.gradient_accumulation_steps
+            assert mb * gas * lay["data"] == w["global_batch"], (name, n)

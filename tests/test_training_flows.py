@@ -1,6 +1,8 @@
 """Training flows (CPU): W&B replay on resume with a fake wandb module, CLI resume under
 ZeRO-2 + full activation checkpointing + offloads, async save while training continues,
-and a data-parallel expansion keeping the new replica's RNG with a warning.
+a data-parallel expansion keeping the new replica's RNG with a warning, bitwise
+reproducibility of multi-rank training (with dropout) across reruns, and the per-phase
+step times in the fit log.
 Reference counterparts: tests/integration/test_cli_resume.py:58-151,
 tests/integration/test_wandb_training_flow.py, tests/unit/test_wandb_logger.py:12-41,
 tests/distributed_cpu/test_checkpoint_rank_local.py:435, 605-700.
@@ -172,3 +174,110 @@ def _expand_save(rank, world, root):
 def test_dp_expansion_keeps_new_replica_rng_with_warning(tmp_path):
     run_ranks(1, _expand_save, str(tmp_path))
     run_ranks(2, _expand_save, str(tmp_path))
+
+
+def _repro_rank(rank, world, layout):
+    """Train the same 3 steps twice from scratch on this rank; everything must be bitwise equal."""
+    from nano_megatron_b200.config import config_from_dict
+    from nano_megatron_b200.distributed import DistributedRuntime
+    from nano_megatron_b200.training import Trainer
+    from nano_megatron_b200.training.engine import build_training_components
+
+    runs = []
+    for _trial in range(2):
+        d = _base_cfg(Path("."), **layout)
+        d["model"]["dropout"] = 0.1                     # exercises the keyed dropout streams
+        d["checkpoint"]["save_interval"] = 0
+        cfg = config_from_dict(d)
+        comps = build_training_components(cfg, DistributedRuntime(cfg.distributed).initialize())
+        tr = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
+                     data_parallel=comps.data_parallel, rng=comps.rng)
+        gen = torch.Generator().manual_seed(11)
+        rows = 4 * 2 // comps.parallel.dp.size
+        losses = []
+        for _ in range(3):
+            ids = torch.randint(0, 128, (rows, 17), generator=gen)
+            out = tr.train_step({"input_ids": ids[:, :-1], "labels": ids[:, 1:]})
+            losses.append((float(out["loss_sum"]), float(out["token_count"])))
+        with comps.data_parallel.full_parameters():
+            params = {k: v.detach().clone() for k, v in comps.model.state_dict().items()}
+        runs.append((losses, params))
+    (la, pa), (lb, pb) = runs
+    assert la == lb, (la, lb)
+    assert pa.keys() == pb.keys()
+    for k in pa:
+        assert torch.equal(pa[k], pb[k]), k
+
+
+@pytest.mark.distributed
+@pytest.mark.parametrize("layout", [
+    {"parallel": {"tensor": 2, "sequence_parallel": True}},
+    {"parallel": {"data": 2}, "data_parallel": {"mode": "zero2", "overlap_grad_reduce": True}},
+], ids=["tp2_sp", "dp2_zero2_overlap"])
+def test_training_is_bitwise_reproducible_gloo(layout):
+    run_ranks(2, _repro_rank, layout)
+
+
+def _phase_rank(rank, world):
+    from nano_megatron_b200.config import config_from_dict
+    from nano_megatron_b200.distributed import DistributedRuntime
+    from nano_megatron_b200.training import Trainer
+    from nano_megatron_b200.training.engine import build_training_components
+
+    d = _base_cfg(Path("."), parallel={"data": world})
+    d["training"]["log_interval"] = 2
+    d["checkpoint"]["save_interval"] = 0
+    d["checkpoint"]["save_final"] = False
+    cfg = config_from_dict(d)
+    comps = build_training_components(cfg, DistributedRuntime(cfg.distributed).initialize())
+    tr = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
+                 data_parallel=comps.data_parallel, rng=comps.rng)
+
+    def batches():
+        g = torch.Generator().manual_seed(rank)
+        while True:
+            ids = torch.randint(0, 128, (4, 17), generator=g)
+            yield {"input_ids": ids[:, :-1], "labels": ids[:, 1:]}
+
+    tr.bind_data_iterator(batches())
+    lines = []
+    tr.fit(max_steps=4, log=lines.append)
+    m = tr.last_metrics
+    phases = [m[f"time_{p}_ms"] for p in ("forward_backward", "grad_sync", "clip", "optimizer")]
+    assert all(v > 0 for v in phases), m
+    # Each phase is a max over ranks, so their sum bounds the slowest rank's step from above.
+    assert m["time_step_ms"] <= sum(phases) * (1 + 1e-9) + 1e-6, m
+    assert m["time_forward_backward_ms"] > m["time_clip_ms"]
+    assert m["tokens_per_second_device"] > 0
+    if rank == 0:
+        assert len(lines) == 2 and "time_optimizer_ms=" in lines[-1]
+
+
+@pytest.mark.distributed
+def test_fit_logs_per_phase_device_times_gloo():
+    run_ranks(2, _phase_rank)
+
+
+def _router_rank(rank, world):
+    from nano_megatron_b200.config import config_from_dict
+    from nano_megatron_b200.distributed import DistributedRuntime
+    from nano_megatron_b200.training.batch_router import BatchRouter
+    from nano_megatron_b200.training.engine import build_training_components
+
+    d = _base_cfg(Path("."), parallel={"tensor": world})
+    cfg = config_from_dict(d)
+    comps = build_training_components(cfg, DistributedRuntime(cfg.distributed).initialize())
+    router = BatchRouter(comps.parallel)
+    ids = torch.arange(4 * 17).view(4, 17)
+    batch = {"input_ids": ids[:, :-1], "labels": ids[:, 1:]}
+    for _ in range(2):
+        out = router.route(batch if router.is_source else None)
+        assert torch.equal(out["input_ids"], ids[:, :-1]) and torch.equal(out["labels"], ids[:, 1:])
+    if router.is_source:   # a new layout fails on the source before anything is sent
+        with pytest.raises(ValueError, match="layout changed"):
+            router.route({"input_ids": ids[:2, :-1], "labels": ids[:2, 1:]})
+
+
+@pytest.mark.distributed
+def test_batch_router_sends_header_once_and_rejects_layout_change_gloo():
+    run_ranks(2, _router_rank)
