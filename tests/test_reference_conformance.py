@@ -218,9 +218,22 @@ def _our_cli_rank(rank, world, cfg_path):
 
 
 LAYOUTS = {
-    "tp2_sp": {"tensor": 2, "data": 1, "sequence_parallel": True},
-    "pp2_1f1b": {"pipeline": 2, "data": 1},
-    "dp2": {"data": 2},
+    "tp2_sp": {"parallel": {"tensor": 2, "data": 1, "sequence_parallel": True}},
+    "tp2": {"parallel": {"tensor": 2, "data": 1}},
+    "pp2_1f1b": {"parallel": {"pipeline": 2, "data": 1}, "pipeline": {"schedule": "1f1b"}},
+    "pp2_gpipe": {"parallel": {"pipeline": 2, "data": 1}, "pipeline": {"schedule": "gpipe"}},
+    "pp2_interleaved": {"parallel": {"pipeline": 2, "data": 1}, "model": {"layers": 4},
+                        "pipeline": {"schedule": "interleaved_1f1b",
+                                     "virtual_stages_per_rank": 2}},
+    "cp2_ring": {"parallel": {"context": 2, "data": 1},
+                 "context_parallel": {"backend": "ring"}},
+    "cp2_all_gather": {"parallel": {"context": 2, "data": 1},
+                       "context_parallel": {"backend": "all_gather"}},
+    "dp2": {"parallel": {"data": 2}},
+    "dp2_overlap": {"parallel": {"data": 2}, "data_parallel": {"overlap_grad_reduce": True}},
+    "dp2_zero1": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero1"}},
+    "dp2_zero2": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero2"}},
+    "dp2_zero3": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero3"}},
 }
 
 
@@ -240,9 +253,8 @@ def test_multirank_training_curve_matches_reference(ref, tmp_path, layout):
                         "gpt_single_cpu.yaml").read_text())
     d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
                       vocab_size=256, seq_length=32)
-    d["parallel"].update(LAYOUTS[layout])
-    if layout == "pp2_1f1b":
-        d["pipeline"].update(schedule="1f1b")
+    for section, values in LAYOUTS[layout].items():
+        d[section].update(values)
     d["training"].update(max_steps=3, micro_batch_size=2, gradient_accumulation_steps=2)
     d["optimizer"]["clip_grad_norm"] = 1.0
 
