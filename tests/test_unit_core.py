@@ -3,6 +3,7 @@
 from __future__ import annotations
 
 import math
+from pathlib import Path
 
 import pytest
 import torch
@@ -229,3 +230,22 @@ def test_split_microbatches():
     assert len(parts) == 3 and parts[1]["input_ids"][0, 0] == 8 and parts[2]["meta"] == 3
     with pytest.raises(ValueError):
         split_microbatches(b, 4)
+
+
+@pytest.mark.parametrize("path", sorted((Path(__file__).parents[1] / "examples" /
+                                         "configs").glob("*.yaml")), ids=lambda p: p.stem)
+def test_example_configs_load_and_validate(path, monkeypatch):
+    """Every shipped example config loads strictly and passes validation at its own world
+    size, without configuration warnings."""
+    import warnings
+
+    import yaml
+
+    from nano_megatron_b200.config.loader import load_config
+
+    par = yaml.safe_load(path.read_text())["parallel"]
+    world = par["tensor"] * par["pipeline"] * par["context"] * par["expert"] * (par["data"] or 1)
+    monkeypatch.setenv("WORLD_SIZE", str(world))
+    with warnings.catch_warnings():
+        warnings.simplefilter("error")
+        load_config(path)
