@@ -23,9 +23,11 @@ class _CPBase:
     def local_positions(self, seq_local: int, rank: int, size: int) -> torch.Tensor:
         return local_positions(seq_local, rank, size, self.load_balance)
 
-    def q_chunks(self, seq_local: int):
-        """(row start, rows, absolute position offset) of each local query chunk."""
-        size, rank = self.group.size, self.group.rank
+    def q_chunks(self, seq_local: int, rank: int | None = None):
+        """(row start, rows, absolute position offset) of each query chunk of ``rank``
+        (default: this rank)."""
+        size = self.group.size
+        rank = self.group.rank if rank is None else rank
         if not self.load_balance:
             return [(0, seq_local, rank * seq_local)]
         c = seq_local // 2
@@ -120,12 +122,23 @@ def _merge(o_acc, lse_acc, o_new, lse_new):
 
 
 class RingContextParallelAttention(_CPBase):
-    """K/V rotate around the CP ring; partial outputs merged by LSE; masked blocks skipped."""
+    """K/V rotate around the CP ring; partial outputs merged by LSE; masked blocks skipped.
 
-    def _ring_pairs(self, rank_src: int, Sq: int, Sk: int):
-        """(q start, q rows, q offset, k start, k rows, k offset) sub-blocks vs a source rank."""
+    Each step starts the next K/V rotation (P2P on the communicator's stream) before
+    computing on the current block and waits for it only afterwards, so the transfer
+    overlaps the flash-attention blocks. In the backward pass the dK/dV partial computed
+    for a source rank's K/V is sent straight back to that rank (fp32) as soon as it is
+    complete, instead of travelling the ring with an accumulator; the owner adds the
+    partials in step order. Fully masked (causal) source blocks send nothing. The reference
+    rotates K/V with blocking exchanges and carries a 4-tensor fp32 accumulator stack once
+    around the ring (src/nano_megatron/context_parallel/ring.py:82-101, 169-250).
+    """
+
+    def _ring_pairs(self, rank_src: int, Sq: int, Sk: int, rank_q: int | None = None):
+        """(q start, q rows, q offset, k start, k rows, k offset) sub-blocks of rank
+        ``rank_q``'s queries (default: this rank) against the keys of ``rank_src``."""
         size = self.group.size
-        qs = self.q_chunks(Sq)
+        qs = self.q_chunks(Sq, rank_q)
         if not self.load_balance:
             ks = [(0, Sk, rank_src * Sk)]
         else:
@@ -140,16 +153,27 @@ class RingContextParallelAttention(_CPBase):
                 out.append((qstart, qrows, qoff, kstart, krows, koff))
         return out
 
-    def _rotate(self, t: torch.Tensor) -> torch.Tensor:
+    def _exchange(self, send: torch.Tensor | None, to: int, recv: torch.Tensor | None,
+                  frm: int) -> list:
+        """Start a send to / receive from group-local ranks; returns the pending works."""
         g = self.group
-        nxt = g.ranks[(g.rank + 1) % g.size]
-        prv = g.ranks[(g.rank - 1) % g.size]
+        ops = []
+        if send is not None:
+            ops.append(dist.P2POp(dist.isend, send, g.ranks[to], group=g.process_group))
+        if recv is not None:
+            ops.append(dist.P2POp(dist.irecv, recv, g.ranks[frm], group=g.process_group))
+        return dist.batch_isend_irecv(ops) if ops else []
+
+    def _start_rotate(self, t: torch.Tensor):
+        """Send ``t`` to the next rank of the ring and receive the previous rank's block."""
+        g = self.group
         recv = torch.empty_like(t)
-        ops = [dist.P2POp(dist.isend, t, nxt, group=g.process_group),
-               dist.P2POp(dist.irecv, recv, prv, group=g.process_group)]
-        for w in dist.batch_isend_irecv(ops):
+        return recv, self._exchange(t, (g.rank + 1) % g.size, recv, (g.rank - 1) % g.size)
+
+    @staticmethod
+    def _wait(works) -> None:
+        for w in works:
             w.wait()
-        return recv
 
     def forward(self, q, k, v, o, mb):
         B, Sq, Hq, D = q.shape
@@ -161,13 +185,14 @@ class RingContextParallelAttention(_CPBase):
         cur = kv
         for step in range(g.size):
             src = (g.rank - step) % g.size
-            nxt = self._rotate(cur) if step + 1 < g.size else None
+            nxt, works = self._start_rotate(cur) if step + 1 < g.size else (None, [])
             view = cur.view(-1, B, 2, hkv, D)
             kb, vb = view[:, :, 0].transpose(0, 1), view[:, :, 1].transpose(0, 1)
             for qs, qr, qo, ks, kr, ko in self._ring_pairs(src, Sq, kb.shape[1]):
                 on, ln = F.attention_fwd(q[:, qs:qs + qr], kb[:, ks:ks + kr], vb[:, ks:ks + kr],
                                          causal=True, q_offset=qo, k_offset=ko)
                 _merge(o_acc[:, qs:qs + qr], lse_acc[:, :, qs:qs + qr], on, ln)
+            self._wait(works)
             if nxt is not None:
                 cur = nxt
         o.transpose(0, 1).copy_(o_acc.to(o.dtype))
@@ -178,16 +203,22 @@ class RingContextParallelAttention(_CPBase):
         hkv = k.shape[2]
         g = self.group
         kv = _kv_rows(q, k, v).contiguous()
-        dkv = torch.zeros(kv.shape, dtype=torch.float32, device=q.device)
+        Sk = kv.shape[0]
+        own = torch.zeros(kv.shape, dtype=torch.float32, device=q.device)
         dq_acc = torch.zeros(B, Sq, Hq, D, dtype=torch.float32, device=q.device)
         o_bs = o.transpose(0, 1)
-        cur, cur_d = kv, dkv
+        cur = kv
+        returns, incoming = [], []          # pending dK/dV partial exchanges
         for step in range(g.size):
             src = (g.rank - step) % g.size
+            nxt, works = self._start_rotate(cur) if step + 1 < g.size else (None, [])
             view = cur.view(-1, B, 2, hkv, D)
             kb, vb = view[:, :, 0].transpose(0, 1), view[:, :, 1].transpose(0, 1)
-            dview = cur_d.view(-1, B, 2, hkv, D)
-            for qs, qr, qo, ks, kr, ko in self._ring_pairs(src, Sq, kb.shape[1]):
+            pairs = self._ring_pairs(src, Sq, Sk)
+            part = own if step == 0 else \
+                (torch.zeros(kv.shape, dtype=torch.float32, device=q.device) if pairs else None)
+            dview = part.view(-1, B, 2, hkv, D) if part is not None else None
+            for qs, qr, qo, ks, kr, ko in pairs:
                 dqc = torch.empty(B, qr, Hq, D, device=q.device, dtype=q.dtype)
                 dkc = torch.empty(B, kr, hkv, D, device=q.device, dtype=q.dtype)
                 dvc = torch.empty_like(dkc)
@@ -198,11 +229,23 @@ class RingContextParallelAttention(_CPBase):
                 dq_acc[:, qs:qs + qr] += dqc.float()
                 dview[ks:ks + kr, :, 0] += dkc.transpose(0, 1).float()
                 dview[ks:ks + kr, :, 1] += dvc.transpose(0, 1).float()
-            # K/V and their gradient accumulators travel on together; after size
-            # rotations each accumulator is back on the rank that owns its K/V.
-            cur = self._rotate(cur) if step + 1 < g.size else cur
-            cur_d = self._rotate(cur_d)
+            if step > 0:
+                # Return this partial to the owner of the K/V just used, and receive the
+                # partial that rank (rank + step) computed for this rank's K/V, if any.
+                frm = (g.rank + step) % g.size
+                recv = torch.empty(kv.shape, dtype=torch.float32, device=q.device) \
+                    if self._ring_pairs(g.rank, Sq, Sk, rank_q=frm) else None
+                returns.append((part, self._exchange(part, src, recv, frm)))
+                if recv is not None:
+                    incoming.append(recv)
+            self._wait(works)
+            if nxt is not None:
+                cur = nxt
+        for _part, works in returns:
+            self._wait(works)
+        for recv in incoming:           # step order: deterministic summation
+            own += recv
         dq.copy_(dq_acc.to(dq.dtype))
-        lv = cur_d.view(-1, B, 2, hkv, D)
+        lv = own.view(-1, B, 2, hkv, D)
         dk.copy_(lv[:, :, 0].transpose(0, 1))
         dv.copy_(lv[:, :, 1].transpose(0, 1))

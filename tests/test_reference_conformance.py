@@ -229,6 +229,8 @@ LAYOUTS = {
                  "context_parallel": {"backend": "ring"}},
     "cp2_all_gather": {"parallel": {"context": 2, "data": 1},
                        "context_parallel": {"backend": "all_gather"}},
+    "cp4_ring": {"parallel": {"context": 4, "data": 1},
+                 "context_parallel": {"backend": "ring"}},
     "dp2": {"parallel": {"data": 2}},
     "dp2_overlap": {"parallel": {"data": 2}, "data_parallel": {"overlap_grad_reduce": True}},
     "dp2_zero1": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero1"}},
@@ -265,15 +267,17 @@ def test_multirank_training_curve_matches_reference(ref, tmp_path, layout):
         return p
 
     ref_cfg, our_cfg = write("ref"), write("ours")
+    par = d["parallel"]
+    world = par["tensor"] * par["pipeline"] * par["context"] * (par["data"] or 1)
     env = dict(os.environ, PYTHONPATH=str(REF), OMP_NUM_THREADS="1")
     port = random.randint(30000, 45000)
     r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-                        "--nproc-per-node", "2", "--master-addr", "127.0.0.1",
+                        "--nproc-per-node", str(world), "--master-addr", "127.0.0.1",
                         "--master-port", str(port), "-m", "nano_megatron.cli.train",
                         "--config", str(ref_cfg)],
                        env=env, capture_output=True, text=True, timeout=900, cwd=tmp_path)
     assert r.returncode == 0, r.stderr[-3000:]
-    run_ranks(2, _our_cli_rank, str(our_cfg))
+    run_ranks(world, _our_cli_rank, str(our_cfg))
 
     def curve(name):
         run_dir = next((tmp_path / name).iterdir())
