@@ -1,9 +1,10 @@
 """Kernel microbenchmarks: CUDA-event timing of each sm_100a kernel vs its library baseline.
 
-    python -m nano_megatron_b200.ops.bench_kernels [--case all|gemm|attn|norm] [--iters N]
+    python -m nano_megatron_b200.ops.bench_kernels [--case all|gemm|attn|mem] [--iters N]
 
-Prints one JSON object of achieved TFLOP/s (GEMM, attention) or GB/s (memory-bound
-kernels). Also the small, self-contained workload used for ncu captures
+Prints one JSON object of achieved TFLOP/s (GEMM, attention) or GB/s and the fraction of
+the measured copy bandwidth (memory-bound kernels: RMSNorm, SwiGLU backward, attention
+backward prep / dQ conversion, embedding, AdamW). Also the small, self-contained workload used for ncu captures
 (``--case gemm_profile`` / ``attn_profile`` run a few launches of one kernel).
 """
 
@@ -97,14 +98,73 @@ def attn_cases(iters: int) -> dict:
     return res
 
 
-def norm_cases(iters: int) -> dict:
-    x = torch.randn(32768, 1024, device="cuda").bfloat16()
-    w = torch.ones(1024, device="cuda").bfloat16()
+def _hbm_peak_gbs() -> float | None:
+    """The measured copy bandwidth of this pool (``MEASURED_PEAKS.json`` at the repo root)."""
+    import os
+
+    path = os.path.join(os.path.dirname(__file__), "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"])
+    except (OSError, KeyError, ValueError):
+        return None
+
+
+def mem_cases(iters: int) -> dict:
+    """Memory-bound kernels at 311M-layer widths with 65536 rows (every operand set exceeds
+    the 126 MB L2): GB/s of the algorithmic bytes and the fraction of the measured copy
+    bandwidth. Bytes count each operand read or written once."""
+    rows, h, ffn, heads, d = 65536, 1024, 2736, 16, 64
+    dev = "cuda"
+    x = torch.randn(rows, h, device=dev).bfloat16()
+    w = torch.ones(h, device=dev).bfloat16()
+    dy = torch.randn_like(x)
+    dres = torch.randn_like(x)
     y = torch.empty_like(x)
-    r = torch.empty(32768, device="cuda")
-    nbytes = 2 * x.numel() * 2
-    return {"rmsnorm_fwd_GBps": nbytes / _time(lambda: lib().rmsnorm_fwd(x, w, y, r, 1e-5),
-                                               iters) / 1e6}
+    rstd = torch.empty(rows, device=dev)
+    dwg = torch.zeros(h, device=dev)
+    n = x.numel()
+    cases = {
+        "rmsnorm_fwd": (4 * n + 4 * rows, lambda: lib().rmsnorm_fwd(x, w, y, rstd, 1e-5)),
+        "rmsnorm_bwd_res": (8 * n + 4 * rows,
+                            lambda: lib().rmsnorm_bwd(x, w, dy, rstd, y, dwg, dres)),
+    }
+    gu = torch.randn(rows // 2, 2 * ffn, device=dev).bfloat16()
+    dh = torch.randn(rows // 2, ffn, device=dev).bfloat16()
+    gout = torch.empty_like(gu)
+    cases["swiglu_bwd"] = (10 * (rows // 2) * ffn, lambda: lib().swiglu_bwd(gu, dh, gout))
+    b, s = rows // 512, 512
+    o = torch.randn(b, s, heads, d, device=dev).bfloat16()
+    do = torch.randn_like(o)
+    delta = torch.empty(b * heads * s, device=dev)
+    dq_acc = torch.empty(o.numel(), device=dev)
+    dq = torch.empty_like(o)
+    cases["attn_bwd_prep"] = (8 * o.numel() + 4 * delta.numel(),
+                              lambda: lib().flash_attn_bwd_prep(o, do, delta, dq_acc))
+    cases["attn_dq_convert"] = (6 * o.numel(),
+                                lambda: lib().flash_attn_bwd_dq_convert(dq_acc, dq, None, None))
+    ids = torch.randint(0, 8192, (rows,), device=dev)
+    table = torch.randn(8192, h, device=dev).bfloat16()
+    emb = torch.empty(rows, h, device=dev, dtype=torch.bfloat16)
+    tgrad = torch.zeros(8192, h, device=dev)
+    cases["embedding_fwd"] = (8 * rows + 4 * n, lambda: lib().embedding_fwd(ids, table, 0, emb))
+    cases["embedding_bwd"] = (8 * rows + 2 * n + 8 * n,
+                              lambda: lib().embedding_bwd(ids, dy, tgrad, 0))
+    numel = 80 * 1024 * 1024
+    p32 = torch.zeros(numel, device=dev)
+    g32 = torch.randn(numel, device=dev)
+    m32, v32 = torch.zeros_like(p32), torch.zeros_like(p32)
+    plow = torch.empty(numel, device=dev, dtype=torch.bfloat16)
+    cases["adamw"] = (30 * numel, lambda: lib().adamw_step(p32, g32, m32, v32, plow, 1e-4, 0.9,
+                                                           0.95, 1e-8, 0.1, 1, None, None))
+    peak = _hbm_peak_gbs()
+    res = {}
+    for name, (nbytes, fn) in cases.items():
+        gbs = nbytes / _time(fn, iters) / 1e6
+        res[f"{name}_GBps"] = gbs
+        if peak:
+            res[f"{name}_frac_of_measured_hbm"] = gbs / peak
+    return res
 
 
 def main() -> None:
@@ -134,9 +194,9 @@ def main() -> None:
         out.update(gemm_cases(a.iters))
     if a.case in ("all", "attn"):
         out.update(attn_cases(a.iters))
-    if a.case in ("all", "norm"):
-        out.update(norm_cases(a.iters))
-    print(json.dumps({k: round(v, 1) for k, v in out.items()}, indent=1))
+    if a.case in ("all", "mem", "norm"):
+        out.update(mem_cases(a.iters))
+    print(json.dumps({k: round(v, 3 if "frac" in k else 1) for k, v in out.items()}, indent=1))
 
 
 if __name__ == "__main__":
