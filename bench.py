@@ -51,11 +51,11 @@ def _zero(mode: str) -> dict:
     }
 
 
-# The BASELINE configs. ``layouts`` maps GPU count -> parallel sizes; the global batch is
+# The benchmark configs. ``layouts`` maps GPU count -> parallel sizes; the global batch is
 # fixed across GPU counts (strong scaling), so gradient accumulation = global / (mb * dp).
 WORKLOADS = {
     "311m": {
-        "title": "311M TP2xPP2xDP2",
+        "title": "311M TP2\u00d7PP2\u00d7DP2",   # the headline metric's name, verbatim
         "describe": "GPT-311M (24L, H1024, 16 heads, F2736, V8192, tied)",
         "model": {"layers": 24, "hidden_size": 1024, "ffn_hidden_size": 2736, "heads": 16,
                   "kv_heads": 16, "seq_length": 512, "vocab_size": 8192, "dropout": 0.0,

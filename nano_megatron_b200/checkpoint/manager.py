@@ -23,6 +23,7 @@ from __future__ import annotations
 
 import contextlib
 import copy
+import dataclasses
 import json
 import math
 import os
@@ -42,6 +43,8 @@ from .manifest import (
     make_manifest,
     validate_topology,
 )
+from .fsdp2_format import (SHARD_INFO_FILE, from_fsdp2_state, load_dcp, load_dcp_model,
+                           save_dcp, to_fsdp2_state, zero3_state_dir)
 from .mapping import ShardedState
 
 BEST_VALIDATION_FILE = "best_validation.json"
@@ -199,7 +202,22 @@ class CheckpointManager:
         dp_state = data_parallel.state_dict()
         payloads: list[tuple[Any, Path]] = []
         c = self.parallel.coordinate
-        if _world() == 1:
+        if mode == "zero3":
+            # The reference's ZeRO-3 layout: one DCP directory per (tp, pp) coordinate with
+            # the model and a per-parameter AdamW state; plus our shard description (layer
+            # ranges, TP shard metadata) for export.
+            backend = "fsdp2_dcp"
+            metadata, local_shard = {}, None
+            if c.dp == 0 and c.cp == 0:
+                b1, b2, eps, wd = data_parallel._opt_hparams()
+                nested = to_fsdp2_state(sharded.state, dp_state, data_parallel.buffers.buckets,
+                                        betas=(b1, b2), eps=eps, weight_decay=wd)
+                d = zero3_state_dir(target, c.tp, c.pp)
+                info = dataclasses.replace(self._local_shard(canon, sharded),
+                                           state_file=str(d.relative_to(target)))
+                payloads.append((_DCPPayload(nested), d))
+                payloads.append((_JSONPayload(info.to_dict()), d / SHARD_INFO_FILE))
+        elif _world() == 1:
             backend = "torch.save"
             payloads.append((sharded.state, target / "model.pt"))
             payloads.append((dict(dp_state), target / "data_parallel.pt"))
@@ -340,9 +358,14 @@ class CheckpointManager:
         elif manifest.storage_backend == "torch.save":
             model_state = _torch_load(path / "model.pt")
             dp_state = _torch_load(path / "data_parallel.pt")
+        elif manifest.storage_backend == "fsdp2_dcp":
+            c = self.parallel.coordinate
+            nested = load_dcp(zero3_state_dir(path, c.tp, c.pp))
+            model_state = nested["model"]
+            dp_state = from_fsdp2_state(nested, data_parallel.buffers.buckets, mode=mode)
         elif manifest.storage_backend == "torch.distributed.checkpoint":
             # single-process checkpoints written by the reference (DCP directory "dcp/")
-            model_state = _read_dcp_model(path / "dcp")
+            model_state = load_dcp_model(path / "dcp")
             dp_state = _torch_load(path / "data_parallel.pt")
         else:
             raise ValueError(f"unsupported checkpoint backend {manifest.storage_backend!r}")
@@ -470,29 +493,26 @@ def portable_run_config(run_config):
     return d
 
 
-def _read_dcp_model(directory: Path) -> dict:
-    """Model state of a ``torch.distributed.checkpoint`` directory saved as {"model": ...},
-    read into CPU tensors allocated from the checkpoint's own metadata (no process group
-    needed; every rank may read it)."""
-    import torch.distributed.checkpoint as dcp
+@dataclass
+class _DCPPayload:
+    """A nested state written as a single-writer torch.distributed.checkpoint directory."""
+    state: dict
 
-    meta = dcp.FileSystemReader(str(directory)).read_metadata()
-    target: dict = {}
-    for fqn, md in meta.state_dict_metadata.items():
-        if not fqn.startswith("model."):
-            continue
-        props = getattr(md, "properties", None)
-        if props is None or not hasattr(md, "size"):
-            continue
-        target[fqn[len("model."):]] = torch.empty(tuple(md.size), dtype=props.dtype)
-    state = {"model": target}
-    dcp.load(state, checkpoint_id=str(directory), no_dist=True)
-    return state["model"]
+
+@dataclass
+class _JSONPayload:
+    value: Any
 
 
 def _write_payloads(payloads) -> None:
     for obj, path in payloads:
-        _torch_save(obj, path)
+        if isinstance(obj, _DCPPayload):
+            save_dcp(obj.state, path)
+        elif isinstance(obj, _JSONPayload):
+            path.parent.mkdir(parents=True, exist_ok=True)
+            path.write_text(json.dumps(obj.value, indent=1, sort_keys=True))
+        else:
+            _torch_save(obj, path)
 
 
 def _param_dtype(run_config) -> torch.dtype | None:

@@ -22,6 +22,8 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 
 namespace nmb {
@@ -29,7 +31,11 @@ namespace fabw {
 
 constexpr int kBN = 128;  // keys per CTA
 constexpr int kBM = 128;  // queries per step
-constexpr int kThreads = 192;
+// Threads: warp 0 loads (TMA), warp 1 issues the MMAs, then SH groups of four
+// softmax warps. With SH = 2 the two groups split the 128 query columns of each
+// step (and the dQ / dK-dV drains) in halves: warp w reads TMEM lane quarter w % 4.
+template <int SH>
+constexpr int threads_for() { return 64 + 128 * SH; }
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
@@ -117,8 +123,8 @@ __device__ __forceinline__ void store_row_sw128(uint8_t* tile, int row, const ui
   }
 }
 
-template <int D>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int D, int SH>
+__global__ void __launch_bounds__(threads_for<SH>(), 1)
     flash_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV,
@@ -141,9 +147,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* qdo_full = bars + 1;   // [QS]
   uint64_t* qdo_empty = bars + 3;  // [QS]
   uint64_t* sdp_full = bars + 5;   // S^T and dP^T in TMEM
-  uint64_t* pds_full = bars + 6;   // P^T and dS^T in smem (4 warp arrivals)
+  uint64_t* pds_full = bars + 6;   // P^T and dS^T in smem (4 * SH warp arrivals)
   uint64_t* mm_done = bars + 7;    // dV/dK/dQ MMAs of a step complete
-  uint64_t* dq_free = bars + 8;    // dQ drained from TMEM (4 warp arrivals)
+  uint64_t* dq_free = bars + 8;    // dQ drained from TMEM (4 * SH warp arrivals)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -160,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int total_steps = steps_per_head * group;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 9; ++i) mbar_init(&bars[i], (i == 6 || i == 8) ? 4 : 1);
+    for (int i = 0; i < 9; ++i) mbar_init(&bars[i], (i == 6 || i == 8) ? 4 * SH : 1);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&tmQ);
@@ -260,7 +266,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ---------------------------------------------------------------- softmax / dQ / epilogue
+    static_assert(SH == 1 || SH == 2, "one or two softmax warp groups");
     const int quarter = warp & 3;
+    const int half = SH == 1 ? 0 : (warp - 2) >> 2;   // softmax warp group: 0 .. SH-1
     const int lane = threadIdx.x & 31;
     const int row = quarter * 32 + lane;  // TMEM lane: key row (S^T, dP^T, dV, dK) / query row (dQ)
     const uint32_t lo = static_cast<uint32_t>(quarter * 32) << 16;
@@ -270,14 +278,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < total_steps; ++t) {
       const int h = kvh * group + t / steps_per_head;
       const int m0 = (m_begin + t % steps_per_head) * kBM;
-      // lse / delta of this query block (read by all 128 threads, one each)
-      {
+      // lse / delta of this query block (read by the first group's 128 threads, one each)
+      if (half == 0) {
         const int64_t base = (static_cast<int64_t>(b) * p.Hq + h) * p.Sq;
         const int q = m0 + row;
         sLse[row] = q < p.Sq ? p.lse[base + q] : INFINITY;
         sDelta[row] = q < p.Sq ? p.delta[base + q] : 0.f;
       }
-      asm volatile("bar.sync 1, 128;" ::: "memory");
+      asm volatile("bar.sync 1, %0;" ::"n"(128 * SH) : "memory");
       if (ok) ok = mbar_wait(sdp_full, t & 1, p.status, kStatusAttnTimeout, abort_flag);
       ok = __all_sync(0xffffffffu, ok);  // keep TMEM ops warp-uniform
       if (!ok) continue;  // keep joining the named barrier until the loop ends
@@ -291,9 +299,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool diag = p.causal && (p.k_offset + n0 + kBN - 1 > p.q_offset + m0);
       const bool tail = (m0 + kBM > p.Sq) || (n0 + kBN > p.Sk);
       // One 32-query chunk at a time: exponentiate, form dS, and store both bf16 chunks
-      // straight into the swizzled P^T / dS^T tiles (keeps register pressure low).
+      // straight into the swizzled P^T / dS^T tiles (keeps register pressure low). Each
+      // softmax group takes its share of the chunks.
+      constexpr int kChunks = kBM / 32 / SH;
 #pragma unroll 1
-      for (int c = 0; c < kBM / 32; ++c) {
+      for (int c = half * kChunks; c < (half + 1) * kChunks; ++c) {
         uint32_t sr[32], dr[32];
         tmem_ld_32x32b_x32(tmem + lo + C::kColS + c * 32, sr);
         tmem_ld_32x32b_x32(tmem + lo + C::kColDP + c * 32, dr);
@@ -329,8 +339,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int q = m0 + row;
       float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Sq + q) * p.Hq + h) * D;
+      constexpr int kDqChunks = D / 32 / SH;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = half * kDqChunks; c < (half + 1) * kDqChunks; ++c) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(tmem + lo + C::kColDQ + c * 32, r);
         tmem_wait_ld();
@@ -346,7 +357,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
     }
-    // ---- epilogue: dK (scaled, inverse RoPE) and dV for this thread's key row
+    // ---- epilogue: dK (scaled, inverse RoPE) and dV for this thread's key row; with two
+    // softmax groups the first writes dK and the second dV
     if (ok) {
       const bool have = total_steps > 0;
       if (have) tc_fence_after();
@@ -360,7 +372,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                              static_cast<int64_t>(kvh) * D;
         const float pos = p.k_pos != nullptr ? static_cast<float>(__ldg(p.k_pos + krc)) : 0.f;
 #pragma unroll
-        for (int c = 0; c < D / 64; ++c) {
+        for (int c = 0; c < (SH == 1 || half == 0 ? D / 64 : 0); ++c) {
           uint32_t a[32], bb[32];
           float x1[32], x2[32];
           if (have) {
@@ -395,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
 #pragma unroll
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < (SH == 1 || half == 1 ? D / 32 : 0); ++c) {
           uint32_t r[32];
           if (have) {
             tmem_ld_32x32b_x32(tmem + lo + C::kColDV + c * 32, r);
@@ -457,6 +469,32 @@ static CUtensorMap make_map(const at::Tensor& t) {
 using namespace nmb;
 using namespace nmb::fabw;
 
+// Softmax warp groups per CTA: 1 (default) or 2 (NMB_ATTN_BWD_SOFTMAX_GROUPS=2).
+static int softmax_groups() {
+  static const int n = [] {
+    const char* e = std::getenv("NMB_ATTN_BWD_SOFTMAX_GROUPS");
+    return e != nullptr && std::atoi(e) == 2 ? 2 : 1;
+  }();
+  return n;
+}
+
+int64_t attn_bwd_softmax_groups() { return softmax_groups(); }
+
+template <int D, int SH>
+static void launch_bwd(dim3 grid, cudaStream_t stream, const CUtensorMap& mq,
+                       const CUtensorMap& mk, const CUtensorMap& mv, const CUtensorMap& mdo,
+                       const Params& p) {
+  static bool set = false;
+  if (!set) {
+    C10_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_tc_kernel<D, SH>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        Cfg<D>::kSmem));
+    set = true;
+  }
+  flash_bwd_tc_kernel<D, SH><<<grid, threads_for<SH>(), Cfg<D>::kSmem, stream>>>(mq, mk, mv,
+                                                                                 mdo, p);
+}
+
 // dK / dV of the causal attention (tcgen05). `delta` (rowsum(dO*O)) and the
 // zeroed fp32 `dq_acc` must be prepared by the caller (flash_attn_bwd_prep).
 void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor dout,
@@ -504,23 +542,15 @@ void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor d
   TORCH_CHECK(static_cast<int64_t>(p.Hkv) * p.B < (1ll << 31) && (p.Sk + kBN - 1) / kBN < 65536);
   dim3 grid(p.Hkv * p.B, (p.Sk + kBN - 1) / kBN, 1);
   if (D == 64) {
-    static bool set = false;
-    if (!set) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_tc_kernel<64>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          Cfg<64>::kSmem));
-      set = true;
-    }
-    flash_bwd_tc_kernel<64><<<grid, kThreads, Cfg<64>::kSmem, stream>>>(mq, mk, mv, mdo, p);
+    if (softmax_groups() == 2)
+      launch_bwd<64, 2>(grid, stream, mq, mk, mv, mdo, p);
+    else
+      launch_bwd<64, 1>(grid, stream, mq, mk, mv, mdo, p);
   } else {
-    static bool set = false;
-    if (!set) {
-      C10_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_tc_kernel<128>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          Cfg<128>::kSmem));
-      set = true;
-    }
-    flash_bwd_tc_kernel<128><<<grid, kThreads, Cfg<128>::kSmem, stream>>>(mq, mk, mv, mdo, p);
+    if (softmax_groups() == 2)
+      launch_bwd<128, 2>(grid, stream, mq, mk, mv, mdo, p);
+    else
+      launch_bwd<128, 1>(grid, stream, mq, mk, mv, mdo, p);
   }
   NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -22,6 +22,7 @@ void flash_attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, a
 void flash_attn_bwd_prep(at::Tensor o, at::Tensor dout, at::Tensor delta, at::Tensor dq_acc);
 void flash_attn_bwd_dq_convert(at::Tensor dq_acc, at::Tensor dq, c10::optional<at::Tensor> q_pos,
                                c10::optional<at::Tensor> inv_freq);
+int64_t attn_bwd_softmax_groups();
 void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor dout,
                           at::Tensor lse, at::Tensor delta, at::Tensor dq_acc, at::Tensor dk,
                           at::Tensor dv, double softmax_scale, bool causal, int64_t q_offset,
@@ -82,6 +83,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_bwd_prep", &flash_attn_bwd_prep);
   m.def("flash_attn_bwd_dq_convert", &flash_attn_bwd_dq_convert);
   m.def("flash_attn_bwd_tc_kv", &flash_attn_bwd_tc_kv, "tcgen05/TMEM attention backward (dK, dV, dQ acc)");
+  m.def("attn_bwd_softmax_groups", &attn_bwd_softmax_groups,
+        "softmax warp groups of the attention backward (NMB_ATTN_BWD_SOFTMAX_GROUPS)");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
   m.def("rmsnorm_bwd", &rmsnorm_bwd);
   m.def("swiglu_fwd", &swiglu_fwd);

@@ -23,9 +23,22 @@ namespace nmb {
 // Driver-API calls such as cuTensorMapEncodeTiled crash in a thread that has no
 // current context yet (e.g. an autograd worker whose first CUDA call is ours,
 // since device guards skip cudaSetDevice when the index already matches).
+// The driver entry point is resolved through the runtime, so the library does not link
+// against libcuda and imports on machines without a GPU driver.
 inline void ensure_current_context(int device) {
+  using GetCurrentFn = CUresult (*)(CUcontext*);
+  static const GetCurrentFn get_current = [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &fn, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      fn = nullptr;
+    return reinterpret_cast<GetCurrentFn>(fn);
+  }();
   CUcontext ctx = nullptr;
-  if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS || ctx == nullptr) cudaSetDevice(device);
+  if (get_current == nullptr || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+    cudaSetDevice(device);
 }
 
 // ---------------------------------------------------------------- status word

@@ -521,7 +521,7 @@ class FlatShardZeROStrategy(DataParallelStrategy):
                 t = sh[k].to(self.buffers.device) if sh[k].device != self.buffers.device \
                     else sh[k]
                 entry[key] = self._gather_shard(b, t)[:b.numel].clone()
-            buckets[b.index] = entry
+            buckets[str(b.index)] = entry      # string keys, as the reference's loader reads
         return {"mode": self.mode, "step": self.step_count, "learning_rate": self._lr,
                 "buckets": buckets}
 

@@ -321,13 +321,15 @@ def merge_checkpoint_model(checkpoint: Path, manifest: CheckpointManifest,
                                              "entries")
             asm.add(_global_key(k, None), t, manifest.tensor_metadata[k])
         return asm.finish(cfg)
-    if manifest.storage_backend != "rank_local_torch.save":
+    if manifest.storage_backend not in ("rank_local_torch.save", "fsdp2_dcp"):
         raise InferenceArtifactError(f"checkpoint backend {manifest.storage_backend!r} cannot "
                                      "be exported; supported backends are "
-                                     "rank_local_torch.save and torch.save")
+                                     "rank_local_torch.save, fsdp2_dcp and torch.save")
     if manifest.parallel_sizes.get("ep", 1) != 1:
         raise InferenceArtifactError("checkpoint export currently requires EP=1")
     tp, pp = manifest.parallel_sizes["tp"], manifest.parallel_sizes["pp"]
+    if manifest.storage_backend == "fsdp2_dcp":
+        return _merge_zero3(checkpoint, manifest, cfg, tp, pp, asm)
     shards = [s for s in manifest.rank_local_shards if s.ep == 0]
     coords = {(s.tp, s.pp) for s in shards}
     if len(shards) != tp * pp or coords != {(t, p) for t in range(tp) for p in range(pp)}:
@@ -347,6 +349,34 @@ def merge_checkpoint_model(checkpoint: Path, manifest: CheckpointManifest,
                 raise InferenceArtifactError(f"rank-local model state must contain string Tensor "
                                              f"entries: {path}")
             asm.add(_global_key(k, ranges), t, s.tensor_metadata[k])
+    return asm.finish(cfg)
+
+
+def _merge_zero3(checkpoint: Path, manifest: CheckpointManifest, cfg: GPTConfig, tp: int,
+                 pp: int, asm) -> dict[str, torch.Tensor]:
+    """ZeRO-3 checkpoints: one DCP directory per (tp, pp) coordinate; the shard description
+    written beside it gives the TP shard metadata and layer ranges."""
+    from nano_megatron_b200.checkpoint.fsdp2_format import (SHARD_INFO_FILE, load_dcp_model,
+                                                           zero3_state_dir)
+    from nano_megatron_b200.checkpoint.manifest import RankLocalShard
+
+    for p_ in range(pp):
+        for t_ in range(tp):
+            d = zero3_state_dir(checkpoint, t_, p_)
+            info_path = d / SHARD_INFO_FILE
+            if not info_path.is_file():
+                raise InferenceArtifactError(
+                    f"ZeRO-3 checkpoint directory {d} has no {SHARD_INFO_FILE} shard description "
+                    "(written by this framework); cannot place its tensors")
+            shard = RankLocalShard.from_dict(json.loads(info_path.read_text()))
+            model = load_dcp_model(d)
+            if set(model) != set(shard.tensor_metadata):
+                raise InferenceArtifactError(f"ZeRO-3 model keys do not match the shard "
+                                             f"description: {d}")
+            ranges = _shard_ranges(shard) if pp > 1 or manifest.virtual_stages_per_rank > 1 \
+                else None
+            for k, t in model.items():
+                asm.add(_global_key(k, ranges), t, shard.tensor_metadata[k])
     return asm.finish(cfg)
 
 

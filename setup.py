@@ -27,7 +27,8 @@ def extension() -> CUDAExtension:
         sources=sources,
         include_dirs=[str(CSRC)],
         extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": NVCC_FLAGS},
-        libraries=["cuda"],
+        # no libcuda link: driver entry points are resolved through the runtime, so the
+        # library also imports (for the build check) on hosts without a GPU driver
     )
 
 

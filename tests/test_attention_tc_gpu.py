@@ -1,6 +1,9 @@
 """tcgen05 attention backward (dK/dV/dQ) against fp32 autograd of the reference formula."""
 
 import math
+import os
+import subprocess
+import sys
 
 import pytest
 import torch
@@ -47,6 +50,10 @@ def test_tc_backward_matches_fp32(d, hq, hkv, s, b):
     dv = dqkv[:, :, hq + hkv:].transpose(0, 1)
     F.attention_bwd(q, k, v, o, do, lse, dq, dk, dv, causal=True)
     torch.cuda.synchronize()
+    from nano_megatron_b200.ops._ext import lib
+
+    assert lib().attn_bwd_softmax_groups() == \
+        (2 if os.environ.get("NMB_ATTN_BWD_SOFTMAX_GROUPS") == "2" else 1)
     assert _rel(dv, vr.grad) < 2e-2
     assert _rel(dk, kr.grad) < 2e-2
     assert _rel(dq, qr.grad) < 2e-2
@@ -72,3 +79,15 @@ def test_tc_backward_inverse_rope_matches_cpu_formula():
         outs.append((dq.cpu(), dk.cpu(), dv.cpu()))
     for a, c in zip(*outs):
         assert _rel(a, c) < 2e-2
+
+
+def test_two_softmax_warp_groups_variant():
+    """The backward with two softmax warp groups per CTA (each takes half of the query
+    columns and of the dQ / dK-dV drains) passes the same checks, in a fresh process."""
+    if os.environ.get("NMB_ATTN_BWD_SOFTMAX_GROUPS") == "2":
+        pytest.skip("already running the variant")
+    env = dict(os.environ, NMB_ATTN_BWD_SOFTMAX_GROUPS="2")
+    r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-q", "-m", "gpu",
+                        "-p", "no:cacheprovider", "-k", "matches_fp32 or inverse_rope"],
+                       env=env, capture_output=True, text=True, timeout=900)
+    assert r.returncode == 0, r.stdout[-4000:] + r.stderr[-2000:]

@@ -37,10 +37,11 @@ def _tokenizer(root: Path):
     return ByteLevelBPETokenizer.load(d), d
 
 
-def _cfg(root: Path, vocab: int, *, tp=1, pp=1, dp=1):
+def _cfg(root: Path, vocab: int, *, tp=1, pp=1, dp=1, mode="ddp"):
     from nano_megatron_b200.config import config_from_dict
 
     return config_from_dict({
+        "data_parallel": {"mode": mode},
         "model": {"layers": 4, "hidden_size": 64, "ffn_hidden_size": 128, "heads": 4,
                   "kv_heads": 2, "seq_length": 64, "vocab_size": vocab},
         "parallel": {"tensor": tp, "pipeline": pp, "context": 1, "expert": 1, "data": dp,
@@ -156,3 +157,41 @@ def test_tp2_pp2_checkpoint_exports_global_weights(tmp_path):
         ref = torch.load(tmp_path / "ref_art" / "model.pt")
         for k, v in full.items():
             torch.testing.assert_close(ref[k], v, rtol=0, atol=0)
+
+
+def _zero3_save(rank, world, root, weights_path):
+    root = Path(root)
+    tok, _ = _tokenizer(root)
+    cfg = _cfg(root, tok.vocab_size, tp=2, dp=2, mode="zero3")
+    from nano_megatron_b200.checkpoint import CheckpointManager
+    from nano_megatron_b200.distributed import DistributedRuntime
+    from nano_megatron_b200.training import Trainer
+    from nano_megatron_b200.training.engine import build_training_components
+
+    comps = build_training_components(cfg, DistributedRuntime(cfg.distributed).initialize())
+    ck = CheckpointManager(config=cfg.checkpoint, parallel=comps.parallel, run_config=cfg)
+    tr = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
+                 data_parallel=comps.data_parallel, checkpoint=ck, rng=comps.rng)
+    with comps.data_parallel.full_parameters():
+        _load_global(comps, torch.load(weights_path))
+    comps.data_parallel.load_model_parameters()
+    tr.save_checkpoint()
+
+
+@pytest.mark.distributed
+def test_zero3_tp2_checkpoint_exports_global_weights(tmp_path):
+    """A TP2 x DP2 ZeRO-3 checkpoint (FSDP2 DCP layout) exports to the global weights."""
+    from nano_megatron_b200.checkpoint.manifest import CheckpointManifest
+    from nano_megatron_b200.inference import export_checkpoint
+
+    tok, _ = _tokenizer(tmp_path)
+    comps, _ = _train_and_save(_cfg(tmp_path, tok.vocab_size))
+    full = {k.removeprefix("model."): v.clone() for k, v in comps.model.state_dict().items()}
+    wp = tmp_path / "full.pt"
+    torch.save(full, wp)
+    run_ranks(4, _zero3_save, str(tmp_path), str(wp))
+    ck = sorted((tmp_path / "ck").glob("step_*"))[-1]
+    assert CheckpointManifest.read(ck / "manifest.json").storage_backend == "fsdp2_dcp"
+    art = export_checkpoint(ck, tmp_path / "artifact_zero3")
+    for k, v in full.items():
+        torch.testing.assert_close(art.state_dict[k], v, rtol=0, atol=0)

@@ -136,6 +136,13 @@ LAYOUTS = {
     "pp2_interleaved": ({"parallel": {"pipeline": 2},
                          "pipeline": {"schedule": "interleaved_1f1b",
                                       "virtual_stages_per_rank": 2}}, 2),
+    "pp2_1f1b_dynamic": ({"parallel": {"pipeline": 2},
+                          "pipeline": {"schedule": "1f1b", "overlap_p2p": True,
+                                       "dynamic_activation_shapes": True}}, 2),
+    "pp2_interleaved_dynamic": ({"parallel": {"pipeline": 2},
+                                 "pipeline": {"schedule": "interleaved_1f1b",
+                                              "virtual_stages_per_rank": 2,
+                                              "dynamic_activation_shapes": True}}, 2),
     "dp2_ddp": ({"parallel": {"data": 2}}, 2),
     "dp2_zero1": ({"parallel": {"data": 2}, "dp_mode": "zero1"}, 2),
     "dp2_zero2": ({"parallel": {"data": 2}, "dp_mode": "zero2"}, 2),

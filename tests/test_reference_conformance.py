@@ -225,6 +225,9 @@ LAYOUTS = {
     "pp2_interleaved": {"parallel": {"pipeline": 2, "data": 1}, "model": {"layers": 4},
                         "pipeline": {"schedule": "interleaved_1f1b",
                                      "virtual_stages_per_rank": 2}},
+    "pp2_1f1b_dynamic": {"parallel": {"pipeline": 2, "data": 1},
+                         "pipeline": {"schedule": "1f1b", "overlap_p2p": True,
+                                      "dynamic_activation_shapes": True}},
     "cp2_ring": {"parallel": {"context": 2, "data": 1},
                  "context_parallel": {"backend": "ring"}},
     "cp2_all_gather": {"parallel": {"context": 2, "data": 1},
@@ -318,6 +321,33 @@ def _curve(run_dir: Path):
     return {x["step"]: x["metrics"]["loss"] for x in recs if x["prefix"] == "train"}
 
 
+RESUME_CASES = {
+    "single": (1, {}),
+    "dp2": (2, {"parallel": {"data": 2}}),
+    "dp2_zero1": (2, {"parallel": {"data": 2}, "data_parallel": {"mode": "zero1"}}),
+    "dp2_zero2": (2, {"parallel": {"data": 2}, "data_parallel": {"mode": "zero2"}}),
+    "dp2_zero3": (2, {"parallel": {"data": 2}, "data_parallel": {"mode": "zero3"}}),
+    "tp2_sp": (2, {"parallel": {"tensor": 2, "data": 1, "sequence_parallel": True}}),
+    "pp2": (2, {"parallel": {"pipeline": 2, "data": 1}}),
+}
+
+
+def _resume_cfg(case: str) -> tuple[int, dict]:
+    import yaml
+
+    world, over = RESUME_CASES[case]
+    d = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
+                        "gpt_single_cpu.yaml").read_text())
+    d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
+                      vocab_size=256, seq_length=32)
+    dp = over.get("parallel", {}).get("data", 1)
+    d["training"].update(max_steps=4, gradient_accumulation_steps=2 // dp)
+    d["checkpoint"].update(save_interval=2, keep_last=4)
+    for section, values in over.items():
+        d[section].update(values)
+    return world, d
+
+
 def _our_resume_rank(rank, world, cfg, ckpt):
     from nano_megatron_b200.cli import train as trcli
 
@@ -325,22 +355,16 @@ def _our_resume_rank(rank, world, cfg, ckpt):
 
 
 @pytest.mark.distributed
-@pytest.mark.parametrize("world", [1, 2])
-def test_resume_from_reference_checkpoint(ref, tmp_path, world):
-    """The reference trains 2 steps and checkpoints (single process: DCP; 2 ranks DP2:
-    rank-local torch.save); our framework resumes that checkpoint and its steps 3-4
-    reproduce the losses of the reference's uninterrupted 4-step run."""
+@pytest.mark.parametrize("case", list(RESUME_CASES))
+def test_resume_from_reference_checkpoint(ref, tmp_path, case):
+    """The reference trains 2 steps and checkpoints (single process: DCP; several ranks:
+    rank-local torch.save; ZeRO-3: FSDP2 DCP); our framework resumes that checkpoint and
+    its steps 3-4 reproduce the losses of the reference's uninterrupted 4-step run."""
     import yaml
 
     from dist_utils import run_ranks
 
-    d = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
-                        "gpt_single_cpu.yaml").read_text())
-    d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
-                      vocab_size=256, seq_length=32)
-    d["parallel"]["data"] = world
-    d["training"].update(max_steps=4, gradient_accumulation_steps=2 // world)
-    d["checkpoint"].update(save_interval=2, keep_last=4)
+    world, d = _resume_cfg(case)
 
     def write(name):
         d["checkpoint"]["directory"] = str(tmp_path / name)
@@ -373,21 +397,15 @@ def _our_train_rank(rank, world, cfg, steps):
 
 
 @pytest.mark.distributed
-@pytest.mark.parametrize("world", [1, 2])
-def test_reference_resumes_our_checkpoint(ref, tmp_path, world):
+@pytest.mark.parametrize("case", list(RESUME_CASES))
+def test_reference_resumes_our_checkpoint(ref, tmp_path, case):
     """We train 2 steps and checkpoint; the reference's own CLI resumes that checkpoint and
     its steps 3-4 reproduce the losses of our uninterrupted 4-step run."""
     import yaml
 
     from dist_utils import run_ranks
 
-    d = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
-                        "gpt_single_cpu.yaml").read_text())
-    d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
-                      vocab_size=256, seq_length=32)
-    d["parallel"]["data"] = world
-    d["training"].update(max_steps=4, gradient_accumulation_steps=2 // world)
-    d["checkpoint"].update(save_interval=2, keep_last=4)
+    world, d = _resume_cfg(case)
 
     def write(name):
         d["checkpoint"]["directory"] = str(tmp_path / name)
@@ -443,3 +461,79 @@ def test_bench_workloads_validate_in_both_frameworks(ref):
             assert size == n, (name, n, lay)
             mb, gas = ours.training.micro_batch_size, ours.training.gradient_accumulation_steps
             assert mb * gas * lay["data"] == w["global_batch"], (name, n)
+
+
+@pytest.mark.distributed
+def test_export_and_generation_interchange_with_reference(ref, tmp_path):
+    """A TP2 checkpoint trained by the reference's CLI (with our tokenizer artifact and a
+    text corpus) exports to bit-identical weights through both exporters, and both
+    frameworks' generators sample the same tokens from the same artifact and seed (ours
+    with and without its K/V cache)."""
+    import json
+    import os
+    import subprocess
+
+    import yaml
+
+    from nano_megatron_b200.inference import export_checkpoint, generate_from_artifact
+    from nano_megatron_b200.tokenizer import ByteBPETrainingConfig, ByteLevelBPETokenizer
+
+    texts = ["once upon a time a small fox found a shiny stone by the river. "
+             "the fox showed the stone to a bird and they both smiled."] * 30
+    (tmp_path / "train.jsonl").write_text("".join(json.dumps({"text": t}) + "\n"
+                                                  for t in texts))
+    tok = ByteLevelBPETokenizer.train(texts, ByteBPETrainingConfig(vocab_size=300))
+    tok.save(tmp_path / "tok")
+    d = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
+                        "gpt_single_cpu.yaml").read_text())
+    d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
+                      vocab_size=tok.vocab_size, seq_length=32)
+    d["parallel"].update(tensor=2, data=1)
+    d["training"].update(max_steps=2)
+    d["checkpoint"].update(directory=str(tmp_path / "ck"), save_interval=2)
+    d["data"].update(text_path=str(tmp_path / "train.jsonl"),
+                     tokenizer={"path": str(tmp_path / "tok")})
+    cfg = tmp_path / "ref.yaml"
+    cfg.write_text(yaml.safe_dump(d))
+    _ref_cli(cfg, tmp_path, nproc=2)
+    ckpt = next((tmp_path / "ck").iterdir()) / "step_00000002"
+
+    env = dict(os.environ, PYTHONPATH=str(REF), OMP_NUM_THREADS="1")
+
+    def ref_cli(*args):
+        r = subprocess.run([sys.executable, *args], env=env, capture_output=True, text=True,
+                           timeout=600, cwd=tmp_path)
+        assert r.returncode == 0, r.stderr[-3000:]
+        return r.stdout
+
+    ref_cli("-m", "nano_megatron.cli.export", "--checkpoint", str(ckpt), "--output",
+            str(tmp_path / "art_ref"))
+    ours = export_checkpoint(ckpt, tmp_path / "art_ours")
+    theirs = torch_load(tmp_path / "art_ref" / "model.pt")
+    assert set(theirs) == set(ours.state_dict)
+    for k, v in theirs.items():
+        assert torch_equal(v, ours.state_dict[k]), k
+
+    kw = dict(max_new_tokens=12, temperature=0.8, top_k=20, top_p=0.95, seed=7)
+    out = json.loads(ref_cli("-m", "nano_megatron.cli.generate", "--model",
+                             str(tmp_path / "art_ref"), "--prompt", "once upon a time",
+                             "--device", "cpu", "--max-new-tokens", "12", "--temperature",
+                             "0.8", "--top-k", "20", "--top-p", "0.95", "--seed", "7",
+                             "--json").strip().splitlines()[-1])
+    for cache in (True, False):
+        mine = generate_from_artifact(tmp_path / "art_ref", "once upon a time", device="cpu",
+                                      use_kv_cache=cache, **kw)
+        assert list(mine.generated_token_ids) == out["generated_token_ids"], (cache, out)
+        assert mine.text == out["text"]
+
+
+def torch_load(path):
+    import torch
+
+    return torch.load(path, map_location="cpu", weights_only=True)
+
+
+def torch_equal(a, b) -> bool:
+    import torch
+
+    return a.dtype == b.dtype and torch.equal(a, b)
