@@ -152,29 +152,68 @@ def make_config_dict(n_gpus: int, steps: int, workload: str = "311m", *,
 
 # ---------------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples nvidia-smi SM clocks and throttle reasons during the timed region."""
+    """Samples SM clocks, power and clock-event reasons of one GPU during the timed region.
 
+    Reads NVML in-process (read-only queries) every ``interval_s``; when NVML is not
+    importable it runs ``nvidia-smi`` instead. The GPU is addressed by UUID, so the sample
+    comes from the device this rank computes on even when CUDA_VISIBLE_DEVICES renumbers
+    devices."""
+
+    REASON_BITS = {"hw_slowdown": "nvmlClocksEventReasonHwSlowdown",
+                   "hw_thermal_slowdown": "nvmlClocksEventReasonHwThermalSlowdown",
+                   "sw_thermal_slowdown": "nvmlClocksEventReasonSwThermalSlowdown",
+                   "sw_power_cap": "nvmlClocksEventReasonSwPowerCap"}
     QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int) -> None:
-        self.gpu = gpu_index
-        self.rows: list[list[str]] = []
+    def __init__(self, device_uuid: str, *, interval_s: float = 0.2, nvml=None) -> None:
+        self.uuid = device_uuid if device_uuid.startswith("GPU-") else f"GPU-{device_uuid}"
+        self.interval_s = interval_s
+        self.samples: list[tuple[float, float, set]] = []   # (sm MHz, max MHz, reasons)
         self._stop = threading.Event()
         self._thread = threading.Thread(target=self._run, daemon=True)
+        self._read = self._nvml_reader(nvml) or self._smi_read
+
+    @classmethod
+    def for_device(cls, device) -> "ClockSampler":
+        import torch
+
+        return cls(str(torch.cuda.get_device_properties(device).uuid))
+
+    def _nvml_reader(self, nvml):
+        try:
+            if nvml is None:
+                import pynvml as nvml
+            nvml.nvmlInit()
+            h = nvml.nvmlDeviceGetHandleByUUID(self.uuid)
+        except Exception:  # noqa: BLE001 - no NVML: fall back to nvidia-smi
+            return None
+        bits = {name: getattr(nvml, attr) for name, attr in self.REASON_BITS.items()}
+
+        def read():
+            sm = float(nvml.nvmlDeviceGetClockInfo(h, nvml.NVML_CLOCK_SM))
+            mx = float(nvml.nvmlDeviceGetMaxClockInfo(h, nvml.NVML_CLOCK_SM))
+            mask = int(nvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+            return sm, mx, {n for n, b in bits.items() if mask & b}
+        return read
+
+    def _smi_read(self):
+        out = subprocess.run(["nvidia-smi", "-i", self.uuid, f"--query-gpu={self.QUERY}",
+                              "--format=csv,noheader,nounits"],
+                             capture_output=True, text=True, timeout=5).stdout
+        r = [c.strip() for c in out.strip().splitlines()[0].split(",")]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        return float(r[1]), float(r[2]), {n for n, v in zip(names, r[5:9])
+                                          if v.lower() == "active"}
 
     def _run(self) -> None:
         while not self._stop.is_set():
             try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.gpu),
-                                      f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits"],
-                                     capture_output=True, text=True, timeout=5).stdout
-                for line in out.strip().splitlines():
-                    self.rows.append([c.strip() for c in line.split(",")])
-            except Exception:  # noqa: BLE001
+                self.samples.append(self._read())
+            except Exception:  # noqa: BLE001 - a failed sample is skipped
                 pass
-            self._stop.wait(0.2)
+            self._stop.wait(self.interval_s)
 
     def __enter__(self):
         self._thread.start()
@@ -185,18 +224,11 @@ class ClockSampler:
         self._thread.join(timeout=10)
 
     def summary(self) -> dict:
-        sm = sorted(float(r[1]) for r in self.rows if len(r) > 8 and r[1].replace(".", "").isdigit())
-        mx = [float(r[2]) for r in self.rows if len(r) > 8 and r[2].replace(".", "").isdigit()]
-        reasons = set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for r in self.rows:
-            if len(r) > 8:
-                for name, val in zip(names, r[5:9]):
-                    if val.strip().lower() == "active":
-                        reasons.add(name)
+        sm = sorted(x[0] for x in self.samples)
+        reasons = set().union(*(x[2] for x in self.samples)) if self.samples else set()
         return {"sm_mhz": sm[len(sm) // 2] if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons),
-                "samples": len(self.rows)}
+                "sm_max_mhz": max(x[1] for x in self.samples) if self.samples else None,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
 
 
 # ---------------------------------------------------------------------- common
@@ -301,7 +333,7 @@ def run_ours(args, rank, world, local):
                                 seed=1234 + comps.parallel.coordinate.dp)
     src = trainer.batch_router.is_source
     lib = _ext.lib()
-    with ClockSampler(local) as clocks:
+    with ClockSampler.for_device(device) as clocks:
         dev_ms, _, launches = run_timed(trainer, batches, args.steps, args.warmup, device, src,
                                         e2e=False, lib=lib)
     e2e_ms, e2e_wall, _ = run_timed(trainer, batches, args.steps, 0, device, src, e2e=True)
@@ -357,7 +389,7 @@ def run_reference(args, rank, world, local):
     batches = synthetic_batches(4, rows, w["model"]["seq_length"], w["model"]["vocab_size"],
                                 seed=1234 + parallel.coordinate.dp)
     src = trainer.batch_router.is_source
-    with ClockSampler(local) as clocks:
+    with ClockSampler.for_device(device) as clocks:
         dev_ms, _, _ = run_timed(trainer, batches, args.steps, args.warmup, device, src, e2e=False)
     e2e_ms, e2e_wall, _ = run_timed(trainer, batches, args.steps, 0, device, src, e2e=True)
     return finish(args, rank, world, dev_ms, e2e_ms, e2e_wall, clocks.summary(), None,

@@ -249,3 +249,53 @@ def test_example_configs_load_and_validate(path, monkeypatch):
     with warnings.catch_warnings():
         warnings.simplefilter("error")
         load_config(path)
+
+
+def test_validate_nccl_cli_helpers(monkeypatch):
+    from nano_megatron_b200.distributed import validate_nccl as v
+
+    for k in ("RANK", "LOCAL_RANK", "WORLD_SIZE"):
+        monkeypatch.delenv(k, raising=False)
+    a = v.parser().parse_args([])
+    assert (a.collective_mib, a.all_gather_mib, a.p2p_mib, a.warmup, a.iterations) == \
+        (256, 32, 256, 5, 20)
+    with pytest.raises(ValueError):
+        v._pos("iterations", 0)
+    # 1 GiB in 1 ms = 1073.7 GB/s; all-reduce bus factor 2(n-1)/n at n = 8
+    assert v._gbs(1 << 30, 1.0) == pytest.approx(1073.741824)
+    assert v._gbs(1 << 30, 1.0, 2 * 7 / 8) == pytest.approx(1073.741824 * 1.75)
+    with pytest.raises(KeyError):
+        v.main([])          # needs the torchrun environment (RANK / LOCAL_RANK / WORLD_SIZE)
+
+
+def test_bench_clock_sampler_reads_nvml_by_uuid():
+    """The benchmark's clock sampler (fake NVML): device addressed by UUID, reasons decoded
+    from the clock-event bitmask, median SM clock reported."""
+    import importlib.util
+    import time
+    from types import SimpleNamespace
+
+    spec = importlib.util.spec_from_file_location("nmb_bench_clocks",
+                                                  Path(__file__).parents[1] / "bench.py")
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    seen = {}
+    clocks = iter([1965, 1500, 1965, 1800] * 100)
+
+    def by_uuid(u):
+        seen["uuid"] = u
+        return "handle"
+
+    fake = SimpleNamespace(
+        NVML_CLOCK_SM=0, nvmlInit=lambda: None, nvmlDeviceGetHandleByUUID=by_uuid,
+        nvmlDeviceGetClockInfo=lambda h, c: next(clocks),
+        nvmlDeviceGetMaxClockInfo=lambda h, c: 1965,
+        nvmlDeviceGetCurrentClocksEventReasons=lambda h: 0x4,
+        nvmlClocksEventReasonHwSlowdown=0x8, nvmlClocksEventReasonHwThermalSlowdown=0x40,
+        nvmlClocksEventReasonSwThermalSlowdown=0x20, nvmlClocksEventReasonSwPowerCap=0x4)
+    with bench.ClockSampler("1234-abcd", interval_s=0.01, nvml=fake) as s:
+        time.sleep(0.2)
+    out = s.summary()
+    assert seen["uuid"] == "GPU-1234-abcd"
+    assert out["samples"] >= 4 and out["sm_max_mhz"] == 1965
+    assert out["sm_mhz"] in (1800, 1965) and out["reasons"] == ["sw_power_cap"]
