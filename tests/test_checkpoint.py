@@ -172,3 +172,47 @@ def tmp_path_step(root):
 @pytest.mark.distributed
 def test_write_failure_is_collective_gloo(tmp_path):
     run_ranks(2, _failing_save, str(tmp_path))
+
+
+def test_fsdp2_layout_round_trip_of_zero_bucket_state():
+    """Flat ZeRO bucket state -> the reference's per-parameter FSDP2 layout -> back."""
+    from types import SimpleNamespace
+
+    from nano_megatron_b200.checkpoint.fsdp2_format import from_fsdp2_state, to_fsdp2_state
+
+    shapes = {"model.embedding.weight": (6, 4), "model.layers.0.input_norm.weight": (4,),
+              "model.final_norm.weight": (4,)}
+    names = list(shapes)
+    sizes = [int(torch.tensor(shapes[n]).prod()) for n in names]
+
+    def bucket(index, members):
+        slices, cur = [], 0
+        for n in members:
+            k = sizes[names.index(n)]
+            slices.append(SimpleNamespace(name=n, start=cur, end=cur + k))
+            cur += k
+        return SimpleNamespace(index=index, slices=slices, numel=cur,
+                               metadata=lambda m=members, c=cur: {"parameter_names": list(m),
+                                                                  "numel": c})
+
+    buckets = [bucket(0, names[:2]), bucket(1, names[2:])]
+    g = torch.Generator().manual_seed(0)
+    model = {n: torch.randn(shapes[n], generator=g) for n in names}
+    model["model.lm_head.weight"] = model["model.embedding.weight"]       # tied view
+    dp = {"mode": "zero3", "step": 7, "learning_rate": 1e-3, "buckets": {}}
+    for b in buckets:
+        dp["buckets"][str(b.index)] = {
+            "metadata": b.metadata(),
+            "master_parameter": torch.cat([model[s.name].reshape(-1) for s in b.slices]),
+            "exp_avg": torch.randn(b.numel, generator=g),
+            "exp_avg_sq": torch.rand(b.numel, generator=g)}
+    nested = to_fsdp2_state(model, dp, buckets, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    group = nested["optimizer"]["param_groups"][0]
+    assert group["params"] == names and group["lr"] == 1e-3 and group["betas"] == (0.9, 0.95)
+    assert set(nested["optimizer"]["state"]) == set(names)         # the tied head once
+    assert float(nested["optimizer"]["state"][names[0]]["step"]) == 7.0
+    back = from_fsdp2_state(nested, buckets)
+    assert back["step"] == 7 and back["learning_rate"] == 1e-3
+    for k, entry in dp["buckets"].items():
+        for key in ("master_parameter", "exp_avg", "exp_avg_sq"):
+            assert torch.equal(back["buckets"][k][key], entry[key]), (k, key)
