@@ -53,3 +53,45 @@ def run_ranks(world: int, fn, *args, timeout: float = 300.0) -> None:
         bad = [p.exitcode for p in procs if p.exitcode != 0]
         if bad:
             raise AssertionError(f"rank exit codes {bad}")
+
+
+def _gpu_entry(rank, world, port, fn, args, errq):
+    os.environ.update({"RANK": str(rank), "WORLD_SIZE": str(world), "LOCAL_RANK": str(rank),
+                       "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(port),
+                       "NCCL_NVLS_ENABLE": "0"})
+    try:
+        fn(rank, world, *args)
+    except Exception:  # noqa: BLE001
+        errq.put((rank, traceback.format_exc()))
+        raise
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def run_gpu_ranks(world: int, fn, *args, timeout: float = 300.0) -> None:
+    """Run ``fn(rank, world, *args)`` as one process per GPU (rank r on cuda:r) with the
+    torchrun environment set (NCCL rendezvous on 127.0.0.1, NVLS off); ``fn`` initialises
+    its own process group. Re-raises the first failure; kills ranks that outlive
+    ``timeout``."""
+    import random
+
+    ctx = mp.get_context("spawn")
+    errq = ctx.SimpleQueue()
+    port = random.randint(20000, 40000)
+    procs = [ctx.Process(target=_gpu_entry, args=(r, world, port, fn, args, errq))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    if not errq.empty():
+        raise AssertionError("rank %d failed:\n%s" % errq.get())
+    if alive:
+        raise AssertionError(f"{len(alive)} rank(s) timed out")
+    bad = [p.exitcode for p in procs if p.exitcode != 0]
+    if bad:
+        raise AssertionError(f"rank exit codes {bad}")
