@@ -537,3 +537,70 @@ def torch_equal(a, b) -> bool:
     import torch
 
     return a.dtype == b.dtype and torch.equal(a, b)
+
+
+def test_tokenizer_cli_pipeline_matches_reference(ref, tmp_path):
+    """split -> train -> preprocess (pt and mmap) -> inspect through both frameworks' CLIs
+    on the same JSONL: identical split files, tokenizer artifacts, corpora and encodings."""
+    import hashlib
+    import json
+    import os
+    import random
+    import subprocess
+
+    rnd = random.Random(5)
+    words = ["the", "cat", "sat", "on", "a", "mat", "little", "dog", "ran", "far", "home",
+             "sun", "was", "warm", "and", "bright", "they", "played", "all", "day"]
+    docs = [" ".join(rnd.choice(words) for _ in range(rnd.randint(5, 40))) + "."
+            for _ in range(400)]
+    src = tmp_path / "docs.jsonl"
+    src.write_text("".join(json.dumps({"text": t}) + "\n" for t in docs))
+
+    def cli(pkg, root, *args):
+        out = tmp_path / root
+        env = dict(os.environ, PYTHONPATH=str(REF) if pkg == "nano_megatron"
+                   else str(Path(__file__).parents[1]), OMP_NUM_THREADS="1")
+        r = subprocess.run([sys.executable, "-m", f"{pkg}.cli.tokenizer", *args], env=env,
+                           capture_output=True, text=True, timeout=600, cwd=tmp_path)
+        assert r.returncode == 0, (pkg, args, r.stderr[-3000:])
+        return r.stdout, out
+
+    def digest(p: Path) -> str:
+        return hashlib.sha256(p.read_bytes()).hexdigest()
+
+    runs = {}
+    for pkg, tag in (("nano_megatron", "ref"), ("nano_megatron_b200", "ours")):
+        d = tmp_path / tag
+        d.mkdir()
+        cli(pkg, tag, "split", "--input", str(src), "--train-output", str(d / "train.jsonl"),
+            "--validation-output", str(d / "val.jsonl"), "--validation-fraction", "0.2")
+        cli(pkg, tag, "train", "--input", str(d / "train.jsonl"), "--output", str(d / "tok"),
+            "--vocab-size", "400", "--min-frequency", "2")
+        cli(pkg, tag, "preprocess", "--input", str(d / "train.jsonl"), "--output",
+            str(d / "train.pt"), "--tokenizer", str(d / "tok"))
+        cli(pkg, tag, "preprocess", "--input", str(d / "val.jsonl"), "--output",
+            str(d / "val.mmap"), "--tokenizer", str(d / "tok"), "--format", "mmap")
+        out, _ = cli(pkg, tag, "inspect", "--tokenizer", str(d / "tok"), "--text",
+                     "the little cat ran home", "--add-bos", "--add-eos")
+        runs[tag] = (d, json.loads(out.strip().splitlines()[-1]))
+    (dr, ir), (do, io) = runs["ref"], runs["ours"]
+    for name in ("train.jsonl", "val.jsonl", "tok/tokenizer.json"):
+        assert digest(dr / name) == digest(do / name), name
+    mr = json.loads((dr / "tok" / "metadata.json").read_text())
+    mo = json.loads((do / "tok" / "metadata.json").read_text())
+    assert mr["fingerprint"] == mo["fingerprint"]
+    assert ir == io                                   # ids, tokens, decoded text, specials
+    import torch
+
+    tr = torch.load(dr / "train.pt", weights_only=False)
+    to = torch.load(do / "train.pt", weights_only=False)
+    for key in ("tokens", "document_offsets"):
+        assert torch.equal(torch.as_tensor(tr[key]), torch.as_tensor(to[key])), key
+    assert tr["fingerprint"] == to["fingerprint"]
+    assert tr["tokenizer_fingerprint"] == to["tokenizer_fingerprint"] == mr["fingerprint"]
+    for name in ("tokens.bin", "document_offsets.bin"):
+        assert digest(dr / "val.mmap" / name) == digest(do / "val.mmap" / name), name
+    m1 = json.loads((dr / "val.mmap" / "metadata.json").read_text())
+    m2 = json.loads((do / "val.mmap" / "metadata.json").read_text())
+    assert {k: v for k, v in m1.items() if "path" not in k} == \
+        {k: v for k, v in m2.items() if "path" not in k}
