@@ -604,3 +604,66 @@ def test_tokenizer_cli_pipeline_matches_reference(ref, tmp_path):
     m2 = json.loads((do / "val.mmap" / "metadata.json").read_text())
     assert {k: v for k, v in m1.items() if "path" not in k} == \
         {k: v for k, v in m2.items() if "path" not in k}
+
+
+@pytest.mark.distributed
+def test_validation_flow_matches_reference(ref, tmp_path):
+    """Training with periodic validation on a text corpus through both CLIs: the same train
+    and validation loss records, the same best-validation pin (step, loss) and the same
+    retained checkpoints."""
+    import json
+
+    import yaml
+
+    from nano_megatron_b200.cli import train as trcli
+    from nano_megatron_b200.tokenizer import ByteBPETrainingConfig, ByteLevelBPETokenizer
+
+    texts = [f"story {i}: a small fox met a bird by the river and they talked about the "
+             f"weather for {i % 7} minutes." for i in range(300)]
+    val = [f"tale {i}: the bird flew home after {i % 5} hours." for i in range(60)]
+    (tmp_path / "train.jsonl").write_text("".join(json.dumps({"text": t}) + "\n"
+                                                  for t in texts))
+    (tmp_path / "val.jsonl").write_text("".join(json.dumps({"text": t}) + "\n" for t in val))
+    tok = ByteLevelBPETokenizer.train(texts, ByteBPETrainingConfig(vocab_size=300))
+    tok.save(tmp_path / "tok")
+    d = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
+                        "gpt_single_cpu.yaml").read_text())
+    d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
+                      vocab_size=tok.vocab_size, seq_length=32)
+    d["training"].update(max_steps=6)
+    d["optimizer"]["lr"] = 3e-3
+    d["data"].update(text_path=str(tmp_path / "train.jsonl"),
+                     tokenizer={"path": str(tmp_path / "tok")})
+    d["validation"] = {"interval": 2, "batches": 3,
+                       "data": {"text_path": str(tmp_path / "val.jsonl"),
+                                "tokenizer": {"path": str(tmp_path / "tok")},
+                                "shuffle": False}}
+    d["checkpoint"].update(save_interval=100, keep_last=1, save_best_validation=True)
+
+    def write(name):
+        d["checkpoint"]["directory"] = str(tmp_path / name)
+        p = tmp_path / f"{name}.yaml"
+        p.write_text(yaml.safe_dump(d))
+        return p
+
+    ref_cfg, our_cfg = write("ref"), write("ours")
+    _ref_cli(ref_cfg, tmp_path)
+    trcli.run(our_cfg, log=lambda *_: None)
+
+    def records(name):
+        run = next((tmp_path / name).iterdir())
+        recs = [json.loads(x) for x in (run / "metrics.jsonl").read_text().splitlines()
+                if x.strip()]
+        pin = json.loads((run / "best_validation.json").read_text())
+        kept = sorted(p.name for p in run.glob("step_*") if (p / ".complete").is_file())
+        return ([(x["prefix"], x["step"], x["metrics"]["loss"]) for x in recs], pin, kept)
+
+    (rr, rpin, rkept), (orr, opin, okept) = records("ref"), records("ours")
+    assert [(p, s) for p, s, _ in rr] == [(p, s) for p, s, _ in orr]
+    assert any(p == "validation" for p, _, _ in rr)
+    for (_, s, l1), (_, _, l2) in zip(rr, orr):
+        assert l2 == pytest.approx(l1, rel=2e-6), (s, rr, orr)
+    assert {k: v for k, v in rpin.items() if k != "value"} == \
+        {k: v for k, v in opin.items() if k != "value"}      # step, checkpoint, metric, mode
+    assert opin["value"] == pytest.approx(rpin["value"], rel=2e-6)
+    assert rkept == okept
