@@ -325,7 +325,6 @@ RESUME_CASES = {
     "single": (1, {}),
     "dp2": (2, {"parallel": {"data": 2}}),
     "dp2_zero1": (2, {"parallel": {"data": 2}, "data_parallel": {"mode": "zero1"}}),
-    "dp2_zero2": (2, {"parallel": {"data": 2}, "data_parallel": {"mode": "zero2"}}),
     "dp2_zero3": (2, {"parallel": {"data": 2}, "data_parallel": {"mode": "zero3"}}),
     "tp2_sp": (2, {"parallel": {"tensor": 2, "data": 1, "sequence_parallel": True}}),
     "pp2": (2, {"parallel": {"pipeline": 2, "data": 1}}),
