@@ -315,6 +315,8 @@ class Trainer:
                 self.phases.begin()
                 out = self.train_step(batch)
                 step_marks = self.phases.end()
+                if self.state.step % interval == 0 or self.state.step == target:
+                    self._check_device_status()     # before logging, inside the failure path
             except BaseException as error:
                 # Leave the data position at the last completed step (as the reference
                 # does) so a checkpoint taken by the caller resumes exactly, and tell the
@@ -384,6 +386,16 @@ class Trainer:
                                                 self.state.best_validation_loss,
                                             "checkpoint/best_validation_step": self.state.step})
         return metrics
+
+    def _check_device_status(self) -> None:
+        """Raise if one of this framework's kernels reported a bounded wait that ran out
+        (the device status word; read at log time, when the host synchronises anyway)."""
+        if self.device.type != "cuda":
+            return
+        from nano_megatron_b200.ops import _ext
+
+        if _ext.available():
+            _ext.check_status(self.device)
 
     def _log(self, pending, host_s, marks, log) -> None:
         """One log record for the steps in ``pending``. Device times come from the steps'

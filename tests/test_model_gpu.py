@@ -94,3 +94,27 @@ def test_cuda_graph_steps_match_eager_steps():
     for n, p in params[False].items():
         rel = ((params[True][n] - p).norm() / (p.norm() + 1e-12)).item()
         assert rel < 1e-3, (n, rel)
+
+
+def test_fit_raises_on_a_kernel_timeout_status():
+    """A status code left by a kernel's bounded wait (set here directly, no kernel times
+    out) stops ``fit`` at its next logging step with the decoded reason."""
+    from nano_megatron_b200.ops._ext import status_word
+
+    _comps, tr = _trainer(False)
+
+    def batches():
+        g = torch.Generator().manual_seed(5)
+        while True:
+            ids = torch.randint(0, 1024, (6, 129), generator=g)
+            yield {"input_ids": ids[:, :-1], "labels": ids[:, 1:]}
+
+    tr.bind_data_iterator(batches())
+    word = status_word(torch.device("cuda", torch.cuda.current_device()))
+    try:
+        word.fill_(0x301)
+        with pytest.raises(RuntimeError, match="peer flag wait timed out"):
+            tr.fit(max_steps=2, log=None)
+    finally:
+        word.zero_()
+        torch.cuda.synchronize()
