@@ -118,3 +118,26 @@ def test_fit_raises_on_a_kernel_timeout_status():
     finally:
         word.zero_()
         torch.cuda.synchronize()
+
+
+def test_forward_is_bitwise_reproducible_and_backward_to_fp32_rounding():
+    """Race check: the same step twice from the same state. The forward has no atomics,
+    so its loss is bitwise equal; gradients (fp32 atomics in split-K, attention dQ, norm
+    and embedding backward) agree to fp32 summation-order rounding."""
+    comps, tr = _trainer(False)
+    ids = torch.randint(0, 1024, (6, 129), generator=torch.Generator().manual_seed(8))
+    micro = tr._prepare_batch({"input_ids": ids[:, :-1], "labels": ids[:, 1:]})
+    dp = comps.data_parallel
+    runs = []
+    for _ in range(2):
+        dp.zero_grad()
+        acc = tr.schedule.forward_backward(micro)
+        dp.finalize_gradients()
+        torch.cuda.synchronize()
+        runs.append((acc.loss_sum.detach().clone(),
+                     {n: p.main_grad.detach().clone() for n, p in comps.model.named_parameters()}))
+    (l0, g0), (l1, g1) = runs
+    assert torch.equal(l0, l1), (l0, l1)
+    for n, a in g0.items():
+        b = g1[n]
+        assert torch.allclose(a, b, rtol=1e-5, atol=1e-6 * float(a.abs().max())), n
