@@ -666,3 +666,59 @@ def test_validation_flow_matches_reference(ref, tmp_path):
         {k: v for k, v in opin.items() if k != "value"}      # step, checkpoint, metric, mode
     assert opin["value"] == pytest.approx(rpin["value"], rel=2e-6)
     assert rkept == okept
+
+
+def test_tinystories_sample_and_corpus_match_reference(ref, tmp_path):
+    """Same pinned-source stand-in through both frameworks: identical bottom-k selection,
+    identical sample JSONL, identical train/validation mmap corpora."""
+    import hashlib
+    import json
+
+    from nano_megatron import tokenizer as ref_tok
+    from nano_megatron.data import tinystories as rts
+    from nano_megatron.data import tinystories_corpus as rtc
+
+    from nano_megatron_b200.data import tinystories as ots
+    from nano_megatron_b200.data import tinystories_corpus as otc
+    from nano_megatron_b200.tokenizer import ByteBPETrainingConfig, ByteLevelBPETokenizer
+
+    stories = [f"Once upon a time {i} a fox met {i % 9} birds by the river." for i in range(300)]
+    train = tmp_path / "train.txt"
+    train.write_bytes(b"".join(s.encode() + b"\n<|endoftext|>\n" for s in stories))
+    val = tmp_path / "valid.txt"
+    val.write_bytes(b"<|endoftext|>".join(f"A short tale {i}.".encode() for i in range(40)))
+
+    def verify(mod, p):
+        return mod.verify_file(p, expected_size=p.stat().st_size,
+                               expected_sha256=hashlib.sha256(p.read_bytes()).hexdigest())
+
+    ours = ots.select_story_indices(train, sample_size=50, seed=7, expected_source_records=300)
+    theirs = rts.select_story_indices(train, sample_size=50, seed=7,
+                                      expected_source_records=300)
+    assert ours == theirs
+    for mod, tag in ((ots, "ours"), (rts, "ref")):
+        mod.create_exact_sample(train, tmp_path / f"{tag}.jsonl", tmp_path / f"{tag}.json",
+                                source_verification=verify(mod, train), sample_size=50, seed=7,
+                                expected_source_records=300)
+    assert (tmp_path / "ours.jsonl").read_bytes() == (tmp_path / "ref.jsonl").read_bytes()
+    mo = json.loads((tmp_path / "ours.json").read_text())
+    mr = json.loads((tmp_path / "ref.json").read_text())
+    assert mo["artifact"]["sha256"] == mr["artifact"]["sha256"]
+
+    ByteLevelBPETokenizer.train(stories, ByteBPETrainingConfig(vocab_size=300)).save(
+        tmp_path / "tok")
+    vocab = ref_tok.ByteLevelBPETokenizer.load(tmp_path / "tok").vocab_size
+    for mod, vmod, tag in ((otc, ots, "ours"), (rtc, rts, "ref")):
+        mod.build_tinystories_corpus(train, val, tmp_path / "tok", tmp_path / f"corpus_{tag}",
+                                     train_verification=verify(vmod, train),
+                                     validation_verification=verify(vmod, val),
+                                     expected_train_stories=300,
+                                     expected_validation_stories=40,
+                                     expected_vocab_size=vocab)
+    splits = sorted(p.name for p in (tmp_path / "corpus_ref").iterdir() if p.is_dir())
+    assert splits == ["train.mmap", "validation.mmap"]
+    for split in splits:
+        for f in ("tokens.bin", "document_offsets.bin"):
+            a = (tmp_path / "corpus_ref" / split / f).read_bytes()
+            b = (tmp_path / "corpus_ours" / split / f).read_bytes()
+            assert a == b, (split, f)
