@@ -722,3 +722,47 @@ def test_tinystories_sample_and_corpus_match_reference(ref, tmp_path):
             a = (tmp_path / "corpus_ref" / split / f).read_bytes()
             b = (tmp_path / "corpus_ours" / split / f).read_bytes()
             assert a == b, (split, f)
+
+
+OVERRIDES = [
+    ["training.max_steps=7", "optimizer.lr=2e-4", "model.dropout=0.0",
+     "parallel.order=[\"tp\",\"cp\",\"ep\",\"dp\",\"pp\"]", "optimizer.betas=[0.8, 0.9]",
+     "data.path=null", "checkpoint.directory=runs/x", "wandb.tags=['a', 'b']",
+     "activation_checkpoint.mode=selective", "lr_scheduler.decay_steps=100"],
+    ["model.kv_heads=2", "training.seed=99", "precision.compute=bfloat16",
+     "data_parallel.bucket_bytes=4096", "pipeline.schedule=gpipe", "wandb.mode=disabled"],
+]
+
+
+@pytest.mark.parametrize("overrides", OVERRIDES, ids=["mixed", "types"])
+def test_config_overrides_parse_like_the_reference(ref, overrides, monkeypatch):
+    """``--set key=value`` strings (JSON, Python literals, bare strings) give the same
+    configuration in both loaders."""
+    import dataclasses
+    import enum
+
+    from nano_megatron.config.loader import load_config as ref_load
+
+    from nano_megatron_b200.config.loader import load_config
+
+    monkeypatch.delenv("WORLD_SIZE", raising=False)
+    path = Path(__file__).parents[1] / "examples" / "configs" / "gpt_single_cpu.yaml"
+    ours = load_config(path, overrides=overrides, emit_warnings=False)
+    theirs = ref_load(path, overrides=overrides, emit_warnings=False)
+
+    def plain(v):
+        if dataclasses.is_dataclass(v):
+            return {f.name: plain(getattr(v, f.name)) for f in dataclasses.fields(v)}
+        if isinstance(v, enum.Enum):
+            return v.value
+        if isinstance(v, (list, tuple)):
+            return [plain(x) for x in v]
+        if isinstance(v, Path):
+            return str(v)
+        return v
+
+    a, b = plain(ours), plain(theirs)
+    a["kernels"].pop("cuda_graphs", None)
+    a["kernels"].pop("fused_tp_comm", None)
+    a["context_parallel"].pop("load_balance", None)
+    assert a == b
