@@ -766,3 +766,68 @@ def test_config_overrides_parse_like_the_reference(ref, overrides, monkeypatch):
     a["kernels"].pop("fused_tp_comm", None)
     a["context_parallel"].pop("load_balance", None)
     assert a == b
+
+
+VALIDATION_CASES = [
+    ({"lr_scheduler": {"warmup_steps": 50, "decay_steps": 10}}, 1),
+    ({"lr_scheduler": {"min_lr": 1.0}}, 1),
+    ({"precision": {"compute": "float32", "params": "bfloat16"}}, 1),
+    ({"parallel": {"tensor": 3}}, 3),
+    ({"parallel": {"tensor": 8}, "model": {"heads": 4}}, 8),
+    ({"parallel": {"context": 3}}, 3),
+    ({"parallel": {"tensor": 2, "context": 2, "sequence_parallel": True},
+      "model": {"seq_length": 36}}, 4),
+    ({"parallel": {"pipeline": 4}, "model": {"layers": 2}}, 4),
+    ({"pipeline": {"schedule": "interleaved_1f1b", "virtual_stages_per_rank": 2}}, 1),
+    ({"parallel": {"pipeline": 2}, "pipeline": {"schedule": "interleaved_1f1b",
+                                                "virtual_stages_per_rank": 1}}, 2),
+    ({"parallel": {"pipeline": 2}, "model": {"layers": 4},
+      "training": {"gradient_accumulation_steps": 3},
+      "pipeline": {"schedule": "interleaved_1f1b", "virtual_stages_per_rank": 2}}, 2),
+    ({"pipeline": {"virtual_stages_per_rank": 2}}, 1),
+    ({"validation": {"interval": 5}}, 1),
+    ({"parallel": {"context": 2}, "model": {"dropout": 0.1}}, 2),
+    ({"offload": {"optimizer_state": True}}, 1),
+    ({"offload": {"zero3_params_and_grads": True}}, 1),
+    ({"data_parallel": {"mode": "zero3", "overlap_grad_reduce": True},
+      "parallel": {"data": 2}}, 2),
+    ({"pipeline": {"overlap_p2p": True}}, 1),
+    ({"parallel": {"sequence_parallel": True}}, 1),
+    ({"parallel": {"data": 2}}, 3),
+    ({"parallel": {"pipeline": 2}, "model": {"layers": 4},
+      "training": {"gradient_accumulation_steps": 2},
+      "pipeline": {"schedule": "interleaved_1f1b", "virtual_stages_per_rank": 2}}, 2),
+    ({"activation_checkpoint": {"mode": "selective", "selective_ops": []}}, 1),
+]
+
+
+@pytest.mark.parametrize("case", range(len(VALIDATION_CASES)))
+def test_config_validation_agrees_with_reference(ref, case):
+    """Cross-block validation: both frameworks accept or reject the same configurations and
+    both warn (or stay silent) on the same ones."""
+    import yaml
+
+    from nano_megatron.config import config_from_dict as ref_from_dict
+    from nano_megatron.config.validation import validate_config as ref_validate
+
+    from nano_megatron_b200.config import config_from_dict
+    from nano_megatron_b200.config.validation import validate_config
+
+    over, world = VALIDATION_CASES[case]
+    base = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
+                           "gpt_single_cpu.yaml").read_text())
+    base["parallel"]["data"] = None
+    for section, values in over.items():
+        base[section].update(values)
+
+    def outcome(from_dict, validate):
+        import copy
+
+        try:
+            res = validate(from_dict(copy.deepcopy(base)), world_size=world)
+        except Exception as error:  # noqa: BLE001 - rejected at construction or validation
+            return ("error", type(error).__name__ != "")
+        return ("ok", bool(getattr(res, "warnings", ())))
+
+    assert outcome(config_from_dict, validate_config) == outcome(ref_from_dict, ref_validate), \
+        over
