@@ -8,9 +8,9 @@ send the peer needs first: no deadlock regardless of how the schedule
 interleaves F and B (the reference colours sources over three communicators for
 the same purpose, src/nano_megatron/pipeline_parallel/p2p.py:84-149).
 
-Sends are asynchronous; the tensor is kept alive until the send completes.
-Receives can be posted early (``post_recv``) and waited on right before the
-compute that needs them, so transfers overlap compute (``overlap_p2p``).
+Sends are asynchronous; the tensor is kept alive until the send completes, and
+the executor decides how many stay in flight (``overlap_p2p``). Receives are
+posted by the executor right before the action that consumes them.
 Shapes are static (``[S_local(/TP), B, H]``) or, with dynamic shapes, each
 payload is preceded by an int64 header carrying (version, ndim, dims...).
 """

@@ -5,9 +5,12 @@ the previous *logical* stage (pp_rank - 1 of the same chunk, or the last rank's
 previous chunk when wrapping around under interleaving), runs the stage and
 sends its output to the next logical stage; a backward receives the output
 gradient from the next logical stage (the last logical stage starts from its
-loss), runs autograd and sends the input gradient back. Sends are
-asynchronous (a bounded number stay in flight, overlapping the next compute);
-receives are posted right before the action that needs them. Semantics follow the
+loss), runs autograd and sends the input gradient back. Sends are always
+asynchronous (up to four stay in flight, overlapping the next actions' compute):
+completing each send before the next action would deadlock interleaved plans, in
+which a peer may first need a transfer this rank issues later, so ``overlap_p2p``
+is accepted for configuration compatibility and sends overlap either way.
+Receives are posted right before the action that needs them. Semantics follow the
 reference executor (src/nano_megatron/pipeline_parallel/schedules/executor.py:
 270-587): loss scaled by 1/M, the last backward of each chunk marked as the
 gradient-synchronising one, tied-embedding hooks around the step.
@@ -91,33 +94,27 @@ class PipelineScheduleExecutor:
         records: dict = {}
         last_b = {c: max(i for i, a in enumerate(plan) if a.kind == "B" and a.chunk == c)
                   for c in range(self.chunks)} if not forward_only else {}
-        pending = None  # (action index, (work, buffer)) of a pre-posted receive
+        in_flight = 4
         for i, a in enumerate(plan):
             if _DEBUG:
                 print(f"[pp rank {self.parallel.rank} stage {self.rank}] {a}", flush=True)
-            if self._needs_recv(a):
-                if pending is not None and pending[0] == i:
-                    work, buf = pending[1]
-                else:
-                    work, buf = self._post(a)
-                work.wait()
-            else:
-                buf = None
             # Receives are posted right before the action that consumes them, never
             # ahead of compute: a receive kernel left spinning on the GPU while this
             # host blocks on an implicit device synchronisation (first-use kernel
             # loading, allocator growth) can deadlock against a peer that is itself
             # blocked setting up the matching NCCL connection. Sends stay
             # asynchronous, which is what overlaps transfers with compute.
-            pending = None
+            buf = None
+            if self._needs_recv(a):
+                work, buf = self._post(a)
+                work.wait()
             with nvtx_range(f"{a.kind} c{a.chunk} mb{a.microbatch}"):
                 if a.kind == "F":
                     self._forward(a, buf, microbatches, m, acc, records, forward_only, last_b,
                                   plan)
                 else:
                     self._backward(a, buf, records, is_last=(i == last_b.get(a.chunk)))
-            # keep at most a couple of sends in flight
-            self.p2p.drain_sends(keep=4)
+            self.p2p.drain_sends(keep=in_flight)
         self.p2p.drain_sends(keep=0)
         return acc
 
