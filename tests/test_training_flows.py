@@ -281,3 +281,96 @@ def _router_rank(rank, world):
 @pytest.mark.distributed
 def test_batch_router_sends_header_once_and_rejects_layout_change_gloo():
     run_ranks(2, _router_rank)
+
+
+def _overlap_rank(rank, world):
+    """Record the strategy's bucket all-reduces around one training step."""
+    from nano_megatron_b200.config import config_from_dict
+    from nano_megatron_b200.data_parallel import strategies
+    from nano_megatron_b200.distributed import DistributedRuntime
+    from nano_megatron_b200.training import Trainer
+    from nano_megatron_b200.training.engine import build_training_components
+
+    d = _base_cfg(Path("."), parallel={"data": world},
+                  data_parallel={"mode": "ddp", "overlap_grad_reduce": True,
+                                 "bucket_bytes": 1 << 12})
+    d["model"]["layers"] = 4
+    d["training"]["gradient_accumulation_steps"] = 3
+    cfg = config_from_dict(d)
+    comps = build_training_components(cfg, DistributedRuntime(cfg.distributed).initialize())
+    tr = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
+                 data_parallel=comps.data_parallel, rng=comps.rng)
+    dp = comps.data_parallel
+    buckets = {b.grad_data.data_ptr(): b for b in dp.buffers.buckets}
+    events = []
+    state = {"finalizing": False}
+    real = strategies.dist
+
+    class _Work:
+        def __init__(self, inner, idx):
+            self.inner, self.idx, self.waits = inner, idx, 0
+
+        def wait(self):
+            self.waits += 1
+            events.append(("wait", self.idx, state["finalizing"]))
+            return self.inner.wait()
+
+    class _Dist:
+        def __getattr__(self, name):
+            return getattr(real, name)
+
+        def all_reduce(self, t, *a, async_op=False, **kw):
+            b = buckets.get(t.data_ptr())
+            out = real.all_reduce(t, *a, async_op=async_op, **kw)
+            if b is None:
+                return out
+            events.append(("async" if async_op else "sync", b.index, state["finalizing"]))
+            if async_op:
+                w = _Work(out, b.index)
+                works.append(w)
+                return w
+            return out
+
+    works = []
+    strategies.dist = _Dist()
+    finalize = dp.finalize_gradients
+
+    def tracked():
+        state["finalizing"] = True
+        try:
+            finalize()
+        finally:
+            state["finalizing"] = False
+
+    dp.finalize_gradients = tracked
+    try:
+        ids = torch.randint(0, 128, (6, 17), generator=torch.Generator().manual_seed(rank))
+        tr.train_step({"input_ids": ids[:, :-1], "labels": ids[:, 1:]})
+    finally:
+        strategies.dist = real
+    from nano_megatron_b200.data_parallel.zero3 import unit_of_name
+
+    names = {id(p): n for n, p in dp._named}
+    outer = {b.index for b in dp.buffers.buckets if b.defer_until_finalize or
+             unit_of_name(names[id(b.slices[0].parameter)]) == "outer"}
+    layer_buckets = {b.index for b in dp.buffers.buckets} - outer
+    launched = [i for kind, i, fin in events if kind == "async"]
+    # every layer bucket starts exactly once, inside the last microbatch's backward
+    assert sorted(launched) == sorted(layer_buckets) and layer_buckets, \
+        (events, layer_buckets, outer)
+    assert all(not fin for kind, _, fin in events if kind == "async")
+    # layer by layer in the backward's order (last layer first)
+    unit = {b.index: unit_of_name(names[id(b.slices[0].parameter)]) for b in dp.buffers.buckets}
+    layers = [unit[i][2] for i in launched]
+    assert layers == sorted(layers, reverse=True) and layers[0] > layers[-1]
+    # finalize waits on each in-flight reduction exactly once, then reduces the outer
+    # (embedding / final norm / head, and any tied) buckets synchronously
+    assert all(w.waits == 1 for w in works)
+    assert all(fin for kind, _, fin in events if kind == "wait")
+    assert {i for kind, i, fin in events if kind == "sync"} == outer and outer
+    assert all(fin for kind, _, fin in events if kind == "sync")
+
+
+@pytest.mark.distributed
+def test_overlap_reducer_starts_buckets_during_backward_and_waits_once_gloo():
+    run_ranks(2, _overlap_rank)
