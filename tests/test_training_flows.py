@@ -2,8 +2,9 @@
 ZeRO-2 + full activation checkpointing + offloads, async save while training continues,
 a data-parallel expansion keeping the new replica's RNG with a warning, bitwise
 reproducibility of multi-rank training (with dropout) across reruns, and the per-phase
-step times in the fit log.
+step times in the fit log, and the overlapped DDP reducer's launch / wait order.
 Reference counterparts: tests/integration/test_cli_resume.py:58-151,
+tests/unit/test_data_parallel_buckets.py:55-282 (delayed all-reduce works),
 tests/integration/test_wandb_training_flow.py, tests/unit/test_wandb_logger.py:12-41,
 tests/distributed_cpu/test_checkpoint_rank_local.py:435, 605-700.
 """
