@@ -2,9 +2,11 @@
 
 Counting rule of the reference (src/nano_megatron/data_parallel/_common.py:123-224):
 a parameter contributes to the global norm once — TP-replicated parameters
-only on TP rank 0, tied embedding copies only on their source rank — then the
-squared norm is summed over TP x EP and PP (and over the replica group when the
-gradient is sharded, ZeRO). The norm and the clip coefficient
+only on TP rank 0, tied embedding copies only on their source rank, dense
+(expert-replicated) parameters only on EP rank 0 — then the squared norm is summed
+over TP x EP and PP (and, first, over the replica group when the gradient is
+sharded, ZeRO; there the dense part is dropped on EP ranks other than 0 after that
+sum, src/nano_megatron/data_parallel/_zero.py:137-151). The norm and the clip coefficient
 ``min(1, max_norm / (norm + 1e-6))`` stay on the device: nothing here
 synchronises with the host.
 """
@@ -29,11 +31,24 @@ def counts_toward_norm(slice_, parallel) -> bool:
     return True
 
 
+def is_dense(bucket) -> bool:
+    d = getattr(bucket, "domain", "dense")
+    return str(getattr(d, "value", d)) == "dense"
+
+
+def dense_counted_here(parallel) -> bool:
+    """Dense parameters are replicated over EP: only EP rank 0 counts them."""
+    ep = getattr(parallel, "ep", None) if parallel is not None else None
+    return ep is None or ep.size == 1 or ep.rank == 0
+
+
 def norm_ranges(buffers, parallel) -> list[tuple[int, int]]:
-    """Merged [start, end) ranges of the flat gradient buffer that count toward the norm."""
+    """Merged [start, end) ranges of the flat (unsharded) gradient buffer that count toward
+    the norm."""
     ranges: list[list[int]] = []
+    dense_here = dense_counted_here(parallel)
     for bucket, s in buffers.slices():
-        if not counts_toward_norm(s, parallel):
+        if not counts_toward_norm(s, parallel) or (is_dense(bucket) and not dense_here):
             continue
         a, b = bucket.offset + s.start, bucket.offset + s.end
         if ranges and ranges[-1][1] >= a - 8:

@@ -458,21 +458,24 @@ class FlatShardZeROStrategy(DataParallelStrategy):
 
     def clip_grad_norm(self, max_norm: float | None) -> torch.Tensor:
         dev = self.buffers.device
-        sq = torch.zeros(1, dtype=torch.float32, device=dev)
-        from .common import counts_toward_norm
+        sq = torch.zeros(2, dtype=torch.float32, device=dev)   # [dense, expert] shard sums
+        from .common import counts_toward_norm, dense_counted_here, is_dense
 
         for b, sh in zip(self.buffers.buckets, self.shards):
             lo = b.rank * b.shard_numel
             hi = lo + b.shard_numel
+            slot = 0 if is_dense(b) else 1
             for s in b.slices:
                 a, e = max(s.start, lo), min(s.end, hi)
                 if a >= e or not counts_toward_norm(s, self.parallel):
                     continue
-                sq += F.sumsq(sh["grad"][a - lo:e - lo])
+                sq[slot] += F.sumsq(sh["grad"][a - lo:e - lo])
         g = self.replica_group
         if g is not None and g.size > 1:
             dist.all_reduce(sq, group=g.process_group)
-        sq = reduce_model_parallel(sq, self.parallel)
+        if not dense_counted_here(self.parallel):
+            sq[0] = 0.0          # the EP replicas of the dense parameters count once
+        sq = reduce_model_parallel(sq.sum().reshape(1), self.parallel)
         norm = sq.sqrt() / self.replica_size
         coef = clip_coefficient(norm, max_norm)
         self._grad_scale = (coef / self.replica_size).reshape(1).to(torch.float32)

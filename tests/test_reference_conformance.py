@@ -239,6 +239,8 @@ LAYOUTS = {
     "dp2_zero1": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero1"}},
     "dp2_zero2": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero2"}},
     "dp2_zero3": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero3"}},
+    "ep2": {"parallel": {"expert": 2, "data": 1}},
+    "ep2_zero2": {"parallel": {"expert": 2, "data": 1}, "data_parallel": {"mode": "zero2"}},
 }
 
 
@@ -271,7 +273,8 @@ def test_multirank_training_curve_matches_reference(ref, tmp_path, layout):
 
     ref_cfg, our_cfg = write("ref"), write("ours")
     par = d["parallel"]
-    world = par["tensor"] * par["pipeline"] * par["context"] * (par["data"] or 1)
+    world = par["tensor"] * par["pipeline"] * par["context"] * par.get("expert", 1) * \
+        (par["data"] or 1)
     env = dict(os.environ, PYTHONPATH=str(REF), OMP_NUM_THREADS="1")
     port = random.randint(30000, 45000)
     r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
