@@ -239,6 +239,13 @@ LAYOUTS = {
     "dp2_zero1": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero1"}},
     "dp2_zero2": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero2"}},
     "dp2_zero3": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero3"}},
+    "tp2_pp2_sp": {"parallel": {"tensor": 2, "pipeline": 2, "data": 1,
+                                "sequence_parallel": True}, "pipeline": {"schedule": "1f1b"}},
+    "tp2_cp2_sp_ring": {"parallel": {"tensor": 2, "context": 2, "data": 1,
+                                     "sequence_parallel": True},
+                        "context_parallel": {"backend": "ring"}},
+    "pp2_dp2_zero1": {"parallel": {"pipeline": 2, "data": 2},
+                      "data_parallel": {"mode": "zero1"}},
     "ep2": {"parallel": {"expert": 2, "data": 1}},
     "ep2_zero2": {"parallel": {"expert": 2, "data": 1}, "data_parallel": {"mode": "zero2"}},
 }
