@@ -1,10 +1,13 @@
 """Topology-stable dropout.
 
 Masks are drawn from a generator seeded by the ParallelRNG ACTIVATION stream
-keyed by (layer, microbatch, global token offset, op), so a token's mask does
-not depend on how the batch is sharded or recomputed (the same keying as the
-reference, src/nano_megatron/nn/dropout.py:14-70). p = 0 (the default) is a
-no-op and allocates nothing.
+keyed by (layer, microbatch, global token offset of the local shard, op) -- the
+keying of the reference, src/nano_megatron/nn/dropout.py:14-70 -- so a mask is
+reproduced exactly by a rerun and by activation-checkpoint recomputation. The draw
+itself (CPU generator or the Philox kernel on CUDA, over this framework's
+sequence-major tensors) differs from the reference's, so with p > 0 the two
+frameworks' losses agree statistically, not bit for bit. p = 0 (the default, and
+every benchmark configuration) is a no-op and allocates nothing.
 """
 
 from __future__ import annotations

@@ -246,6 +246,10 @@ LAYOUTS = {
                         "context_parallel": {"backend": "ring"}},
     "pp2_dp2_zero1": {"parallel": {"pipeline": 2, "data": 2},
                       "data_parallel": {"mode": "zero1"}},
+    "tp2_sp_ac_full": {"parallel": {"tensor": 2, "data": 1, "sequence_parallel": True},
+                       "activation_checkpoint": {"mode": "full"}},
+    "pp2_ac_selective": {"parallel": {"pipeline": 2, "data": 1},
+                         "activation_checkpoint": {"mode": "selective"}},
     "ep2": {"parallel": {"expert": 2, "data": 1}},
     "ep2_zero2": {"parallel": {"expert": 2, "data": 1}, "data_parallel": {"mode": "zero2"}},
 }
