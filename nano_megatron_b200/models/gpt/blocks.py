@@ -191,21 +191,29 @@ class AttentionBlockFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, h, w_norm, w_q, w_k, w_v, w_out, b_out, spec: AttnSpec, mb: MicrobatchInfo,
-                inv_freq, dropout_fn):
+                inv_freq, dropout_fn, b_qkv=None):
+        """``b_qkv``: the (q, k, v) column-parallel biases when the model has biases; they
+        are added before the rotary embedding, as in the reference's attention."""
         H = spec.hidden
         h2 = h.reshape(-1, H)
         xn, rstd = F.rmsnorm(h2, w_norm, spec.eps)
         w_qkv = fused_rows([w_q, w_k, w_v])
         D, hq, hkv = spec.head_dim, spec.heads, spec.kv_heads
-        fused = spec.tp.fused(xn) and D in (64, 128)
+        fused = spec.tp.fused(xn) and D in (64, 128) and b_qkv is None
         if fused:
             qkv, xg = CG.allgather_gemm(spec.tp.workspace, xn, w_qkv, epi="rope",
                                         positions=mb.positions, inv_freq=inv_freq, head_dim=D,
                                         rope_cols=(hq + hkv) * D, pos_div=mb.batch)
-        else:
+        elif b_qkv is None:
             xg = spec.tp.gather(xn)
             qkv = F.qkv_rope_linear(xg, w_qkv, mb.positions, inv_freq, D, (hq + hkv) * D,
                                     pos_div=mb.batch)
+        else:
+            xg = spec.tp.gather(xn)
+            qkv = F.linear(xg, w_qkv)
+            qkv += torch.cat([b.detach() for b in b_qkv]).to(qkv.dtype)
+            F.rope_(qkv, (hq + hkv) * D, D, mb.positions, inv_freq, inverse=False,
+                    pos_div=mb.batch)
         q, k, v = _split_qkv(qkv, mb.seq, mb.batch, hq, hkv, D)
         o = torch.empty(mb.seq, mb.batch, hq, D, device=h.device, dtype=qkv.dtype)
         lse = spec.core.forward(q, k, v, o, mb)
@@ -224,6 +232,7 @@ class AttentionBlockFn(torch.autograd.Function):
             out = h2 + y
         ctx.spec, ctx.mb, ctx.inv_freq = spec, mb, inv_freq
         ctx.params = (w_norm, w_q, w_k, w_v, w_out, b_out)
+        ctx.b_qkv = b_qkv
         ctx.dropout_fn = dropout_fn
         ctx.save_for_backward(h2, rstd, xg, qkv, o, lse)
         return out.view(h.shape)
@@ -257,6 +266,10 @@ class AttentionBlockFn(torch.autograd.Function):
         if not getattr(spec.core, "applies_inverse_rope", True):
             F.rope_(dqkv, (hq + hkv) * D, D, mb.positions, ctx.inv_freq, inverse=True,
                     pos_div=mb.batch)
+        if ctx.b_qkv is not None:
+            gb = FusedGrad(list(ctx.b_qkv))
+            F.bias_grad(dqkv, gb.target)
+            gb.flush()
         w_qkv = fused_rows([w_q, w_k, w_v])
         if fused:
             dxn = CG.gemm_reduce_scatter(spec.tp.workspace, dqkv, w_qkv, b_mn=True)
@@ -266,7 +279,8 @@ class AttentionBlockFn(torch.autograd.Function):
         F.linear_wgrad(dqkv, xg, g.target)
         g.flush()
         dh_in = F.rmsnorm_bwd(h2, w_norm.detach(), dxn, rstd, main_grad_of(w_norm), dres=dh)
-        return (dh_in.view(dout.shape), None, None, None, None, None, None, None, None, None, None)
+        return (dh_in.view(dout.shape), None, None, None, None, None, None, None, None, None, None,
+                None)
 
 
 @dataclass
@@ -281,20 +295,28 @@ class MLPBlockFn(torch.autograd.Function):
     """h_out = h + down(silu(gate(norm(h))) * up(norm(h))) with TP/SP collectives."""
 
     @staticmethod
-    def forward(ctx, h, w_norm, w_gate, w_up, w_down, b_down, spec: MLPSpec, dropout_fn):
+    def forward(ctx, h, w_norm, w_gate, w_up, w_down, b_down, spec: MLPSpec, dropout_fn,
+                b_gu=None):
+        """``b_gu``: the (gate, up) column-parallel biases when the model has biases; they
+        are added before the SwiGLU activation."""
         H = spec.hidden
         h2 = h.reshape(-1, H)
         xn, rstd = F.rmsnorm(h2, w_norm, spec.eps)
         w_gu = fused_rows([w_gate, w_up])
-        fused = spec.tp.fused(xn) and spec.ffn % 128 == 0
+        fused = spec.tp.fused(xn) and spec.ffn % 128 == 0 and b_gu is None
         if fused:
             gu = torch.empty(xn.shape[0] * spec.tp.size, 2 * spec.ffn, device=xn.device,
                              dtype=xn.dtype)
             hmid, xg = CG.allgather_gemm(spec.tp.workspace, xn, w_gu, epi="swiglu",
                                          n_out=spec.ffn, aux=gu, swiglu_up_row=spec.ffn)
-        else:
+        elif b_gu is None:
             xg = spec.tp.gather(xn)
             hmid, gu = F.swiglu_linear(xg, w_gu, spec.ffn)
+        else:
+            xg = spec.tp.gather(xn)
+            gu = F.linear(xg, w_gu)
+            gu += torch.cat([b.detach() for b in b_gu]).to(gu.dtype)
+            hmid = F.swiglu_act(gu, spec.ffn)
         fuse_residual = spec.tp.size == 1 and b_down is None and dropout_fn is None
         if fuse_residual:
             out = F.linear(hmid, w_down.detach(), residual=h2)
@@ -309,6 +331,7 @@ class MLPBlockFn(torch.autograd.Function):
             out = h2 + y
         ctx.spec = spec
         ctx.params = (w_norm, w_gate, w_up, w_down, b_down)
+        ctx.b_gu = b_gu
         ctx.dropout_fn = dropout_fn
         ctx.save_for_backward(h2, rstd, xg, gu, hmid)
         return out.view(h.shape)
@@ -333,6 +356,10 @@ class MLPBlockFn(torch.autograd.Function):
         F.linear_wgrad(dyg, hmid, main_grad_of(w_down))
         dgu = F.swiglu_bwd(gu, dmid, inplace=True)
         del dmid
+        if ctx.b_gu is not None:
+            gb = FusedGrad(list(ctx.b_gu))
+            F.bias_grad(dgu, gb.target)
+            gb.flush()
         w_gu = fused_rows([w_gate, w_up])
         if fused:
             dxn = CG.gemm_reduce_scatter(spec.tp.workspace, dgu, w_gu, b_mn=True)
@@ -342,7 +369,7 @@ class MLPBlockFn(torch.autograd.Function):
         F.linear_wgrad(dgu, xg, g.target)
         g.flush()
         dh_in = F.rmsnorm_bwd(h2, w_norm.detach(), dxn, rstd, main_grad_of(w_norm), dres=dh)
-        return dh_in.view(dout.shape), None, None, None, None, None, None, None
+        return dh_in.view(dout.shape), None, None, None, None, None, None, None, None
 
 
 class EmbeddingFn(torch.autograd.Function):

@@ -141,16 +141,20 @@ class GPTLayer(nn.Module):
                               layer=self.layer_index, microbatch=mb.microbatch_index,
                               global_token_offset=token_offset, op="mlp_residual")
 
+        m = self.mlp
+        b_qkv = (a.q_proj.bias, a.k_proj.bias, a.v_proj.bias) \
+            if a.q_proj.bias is not None else None
+        b_gu = (m.gate_proj.bias, m.up_proj.bias) if m.gate_proj.bias is not None else None
+
         def attn(x):
             return B.AttentionBlockFn.apply(
                 x, self.input_norm.weight, a.q_proj.weight, a.k_proj.weight, a.v_proj.weight,
-                a.out_proj.weight, a.out_proj.bias, attn_spec, mb, inv_freq, drop_a)
+                a.out_proj.weight, a.out_proj.bias, attn_spec, mb, inv_freq, drop_a, b_qkv)
 
         def mlp(x):
-            m = self.mlp
             return B.MLPBlockFn.apply(x, self.post_attention_norm.weight, m.gate_proj.weight,
                                       m.up_proj.weight, m.down_proj.weight, m.down_proj.bias,
-                                      mlp_spec, drop_m)
+                                      mlp_spec, drop_m, b_gu)
 
         off = bool(getattr(self.checkpoint_config, "offload_saved_tensors", False))
         h = activation_checkpoint(attn, h, offload_saved_tensors=off) \

@@ -74,6 +74,17 @@ def swiglu_linear(x: torch.Tensor, w_gate_up: torch.Tensor, ffn: int):
     return torch.nn.functional.silu(g) * u, gu
 
 
+def swiglu_act(gu: torch.Tensor, ffn: int) -> torch.Tensor:
+    """``silu(g) * u`` of a ``[rows, 2*ffn] = [g | u]`` tensor (the elementwise part of
+    ``swiglu_linear``, for projections whose output needs a bias first)."""
+    if _cuda(gu):
+        h = torch.empty(gu.shape[0], ffn, device=gu.device, dtype=gu.dtype)
+        lib().swiglu_fwd(gu, h)
+        return h
+    g, u = gu[:, :ffn], gu[:, ffn:]
+    return torch.nn.functional.silu(g) * u
+
+
 def swiglu_bwd(gu: torch.Tensor, dh: torch.Tensor, inplace: bool = True) -> torch.Tensor:
     """d[g|u] from the saved ``gu`` and the upstream ``dh`` (overwrites ``gu`` on CUDA)."""
     ffn = dh.shape[1]

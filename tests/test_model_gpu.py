@@ -22,7 +22,8 @@ def _build(device: str, **model):
 
 @pytest.mark.parametrize("model", [dict(), dict(heads=2, kv_heads=1, hidden_size=256),
                                    dict(hidden_size=512, heads=4, kv_heads=2,
-                                        ffn_hidden_size=1368)])
+                                        ffn_hidden_size=1368),
+                                   dict(bias=True)])
 def test_cuda_model_matches_cpu_fp32(model):
     torch.manual_seed(0)
     cpu = _build("cpu", **model)

@@ -250,6 +250,16 @@ LAYOUTS = {
                        "activation_checkpoint": {"mode": "full"}},
     "pp2_ac_selective": {"parallel": {"pipeline": 2, "data": 1},
                          "activation_checkpoint": {"mode": "selective"}},
+    "dp2_zero2_offload": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero2"},
+                          "offload": {"optimizer_state": True, "activations": True},
+                          "activation_checkpoint": {"mode": "full",
+                                                    "offload_saved_tensors": True}},
+    "pp2_untied": {"parallel": {"pipeline": 2, "data": 1},
+                   "model": {"tie_embeddings": False}},
+    "tp2_sp_bias": {"parallel": {"tensor": 2, "data": 1, "sequence_parallel": True},
+                    "model": {"bias": True}},
+    "dp2_bias": {"parallel": {"data": 2}, "model": {"bias": True}},
+    "tp2_bias": {"parallel": {"tensor": 2, "data": 1}, "model": {"bias": True}},
     "ep2": {"parallel": {"expert": 2, "data": 1}},
     "ep2_zero2": {"parallel": {"expert": 2, "data": 1}, "data_parallel": {"mode": "zero2"}},
 }
