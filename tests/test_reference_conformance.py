@@ -260,6 +260,7 @@ LAYOUTS = {
                     "model": {"bias": True}},
     "dp2_bias": {"parallel": {"data": 2}, "model": {"bias": True}},
     "tp2_bias": {"parallel": {"tensor": 2, "data": 1}, "model": {"bias": True}},
+    "tp2_padded_vocab": {"parallel": {"tensor": 2, "data": 1}, "model": {"vocab_size": 255}},
     "ep2": {"parallel": {"expert": 2, "data": 1}},
     "ep2_zero2": {"parallel": {"expert": 2, "data": 1}, "data_parallel": {"mode": "zero2"}},
 }
