@@ -204,12 +204,36 @@ class DataParallelStrategy:
 
     def _wait_inflight(self) -> set:
         done = set()
-        for idx, work in getattr(self, "_inflight", {}).items():
+        for idx, (work, low) in getattr(self, "_inflight", {}).items():
             work.wait()
+            if low is not None:
+                self.buffers.buckets[idx].grad_data.copy_(low)
             done.add(idx)
         if hasattr(self, "_inflight"):
             self._inflight.clear()
         return done
+
+    def _reduce_dtype(self) -> torch.dtype | None:
+        """``precision.grad_reduce`` when it differs from the fp32 gradient buffers: the
+        replica sum then runs on a copy in that dtype (as the reference packs its buckets
+        in it), halving the bytes on the wire for bf16."""
+        d = self.grad_reduce_dtype
+        return d if d is not None and d != self.buffers.grad_dtype else None
+
+    def _all_reduce_bucket(self, b, *, async_op: bool = False):
+        """Sum bucket ``b``'s gradients over the replica group. Returns (work, low) when
+        asynchronous, where ``low`` is the reduced-precision copy to copy back after the
+        wait (None when the buffer itself is reduced)."""
+        g = self.replica_group
+        dt = self._reduce_dtype()
+        target = b.grad_data if dt is None else b.grad_data.to(dt)
+        work = dist.all_reduce(target, group=g.process_group, async_op=async_op)
+        low = None if dt is None else target
+        if async_op:
+            return work, low
+        if low is not None:
+            b.grad_data.copy_(low)
+        return None
 
     def _reduce_buckets(self, skip: set = frozenset()) -> None:
         g = self.replica_group
@@ -217,7 +241,7 @@ class DataParallelStrategy:
             return
         for b in self.buffers.buckets:
             if b.index not in skip:
-                dist.all_reduce(b.grad_data, group=g.process_group)
+                self._all_reduce_bucket(b)
 
     # ------------------------------------------------------------------ overlap reducer
     def _overlap_active(self) -> bool:
@@ -248,8 +272,7 @@ class DataParallelStrategy:
         def launch(key):
             for b in by_unit.get(key, ()):
                 if b.index not in self._inflight:
-                    self._inflight[b.index] = dist.all_reduce(b.grad_data, group=g.process_group,
-                                                              async_op=True)
+                    self._inflight[b.index] = self._all_reduce_bucket(b, async_op=True)
 
         for mod in model.modules():
             if not isinstance(mod, GPTLayer):
@@ -446,8 +469,15 @@ class FlatShardZeROStrategy(DataParallelStrategy):
             if g is None or g.size == 1:
                 sh["grad"].copy_(full)
                 continue
+            dt = self._reduce_dtype()
+            if dt is not None:
+                full = full.to(dt)
             if self.reduce_scatter and full.is_cuda:
-                dist.reduce_scatter_tensor(sh["grad"], full, group=g.process_group)
+                out = sh["grad"] if dt is None else torch.empty(sh["grad"].shape, dtype=dt,
+                                                                 device=full.device)
+                dist.reduce_scatter_tensor(out, full, group=g.process_group)
+                if dt is not None:
+                    sh["grad"].copy_(out)
             else:
                 dist.all_reduce(full, group=g.process_group)
                 sh["grad"].copy_(b.shard_view(full))

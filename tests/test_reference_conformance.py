@@ -261,6 +261,9 @@ LAYOUTS = {
     "dp2_bias": {"parallel": {"data": 2}, "model": {"bias": True}},
     "tp2_bias": {"parallel": {"tensor": 2, "data": 1}, "model": {"bias": True}},
     "tp2_padded_vocab": {"parallel": {"tensor": 2, "data": 1}, "model": {"vocab_size": 255}},
+    "dp2_bf16_reduce": {"parallel": {"data": 2}, "precision": {"grad_reduce": "bfloat16"}},
+    "dp2_zero2_bf16_reduce": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero2"},
+                              "precision": {"grad_reduce": "bfloat16"}},
     "ep2": {"parallel": {"expert": 2, "data": 1}},
     "ep2_zero2": {"parallel": {"expert": 2, "data": 1}, "data_parallel": {"mode": "zero2"}},
 }

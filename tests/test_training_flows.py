@@ -375,3 +375,39 @@ def _overlap_rank(rank, world):
 @pytest.mark.distributed
 def test_overlap_reducer_starts_buckets_during_backward_and_waits_once_gloo():
     run_ranks(2, _overlap_rank)
+
+
+def _bf16_reduce_rank(rank, world, mode):
+    from nano_megatron_b200.config import config_from_dict
+    from nano_megatron_b200.distributed import DistributedRuntime
+    from nano_megatron_b200.training import Trainer
+    from nano_megatron_b200.training.engine import build_training_components
+
+    out = {}
+    for reduce in ("float32", "bfloat16"):
+        d = _base_cfg(Path("."), parallel={"data": world}, data_parallel={"mode": mode},
+                      precision={"grad_reduce": reduce})
+        cfg = config_from_dict(d)
+        comps = build_training_components(cfg, DistributedRuntime(cfg.distributed).initialize())
+        tr = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
+                     data_parallel=comps.data_parallel, rng=comps.rng)
+        dp = comps.data_parallel
+        ids = torch.randint(0, 128, (4, 17), generator=torch.Generator().manual_seed(rank))
+        micro = tr._prepare_batch({"input_ids": ids[:, :-1], "labels": ids[:, 1:]})
+        dp.zero_grad()
+        tr.schedule.forward_backward(micro)
+        dp.finalize_gradients()
+        reduced = torch.cat([sh["grad"] for sh in dp.shards]) if hasattr(dp, "shards") \
+            else dp.buffers.grad_flat
+        out[reduce] = reduced.clone()
+    lo, hi = out["bfloat16"], out["float32"]
+    # summed in bf16: every reduced value is a bf16 number; the fp32 sum generally is not
+    assert torch.equal(lo, lo.to(torch.bfloat16).float())
+    assert not torch.equal(hi, hi.to(torch.bfloat16).float())
+    assert ((lo - hi).norm() / hi.norm()).item() < 1e-2
+
+
+@pytest.mark.distributed
+@pytest.mark.parametrize("mode", ["ddp", "zero2"])
+def test_grad_reduce_dtype_is_the_wire_precision_gloo(mode):
+    run_ranks(2, _bf16_reduce_rank, mode)
