@@ -302,13 +302,22 @@ def test_multirank_training_curve_matches_reference(ref, tmp_path, layout):
         (par["data"] or 1)
     env = dict(os.environ, PYTHONPATH=str(REF), OMP_NUM_THREADS="1")
     port = random.randint(30000, 45000)
-    r = subprocess.run([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-                        "--nproc-per-node", str(world), "--master-addr", "127.0.0.1",
-                        "--master-port", str(port), "-m", "nano_megatron.cli.train",
-                        "--config", str(ref_cfg)],
-                       env=env, capture_output=True, text=True, timeout=900, cwd=tmp_path)
-    assert r.returncode == 0, r.stderr[-3000:]
-    run_ranks(world, _our_cli_rank, str(our_cfg))
+    # the two frameworks train concurrently (independent processes and rendezvous)
+    proc = subprocess.Popen([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+                             "--nproc-per-node", str(world), "--master-addr", "127.0.0.1",
+                             "--master-port", str(port), "-m", "nano_megatron.cli.train",
+                             "--config", str(ref_cfg)],
+                            env=env, stdout=subprocess.PIPE, stderr=subprocess.PIPE,
+                            text=True, cwd=tmp_path)
+    try:
+        run_ranks(world, _our_cli_rank, str(our_cfg))
+    finally:
+        try:
+            _, err = proc.communicate(timeout=900)
+        except subprocess.TimeoutExpired:
+            proc.terminate()            # torchrun stops its own workers on SIGTERM
+            _, err = proc.communicate(timeout=60)
+    assert proc.returncode == 0, err[-3000:]
 
     def curve(name):
         run_dir = next((tmp_path / name).iterdir())
@@ -324,7 +333,8 @@ def test_multirank_training_curve_matches_reference(ref, tmp_path, layout):
         assert g2 == pytest.approx(g1, rel=1e-4), (layout, s, theirs, ours)
 
 
-def _ref_cli(cfg: Path, tmp: Path, *extra: str, nproc: int = 1) -> None:
+def _ref_cli_start(cfg: Path, tmp: Path, *extra: str, nproc: int = 1):
+    """Start the reference's training CLI (torchrun for several ranks) in the background."""
     import os
     import random
     import subprocess
@@ -337,8 +347,23 @@ def _ref_cli(cfg: Path, tmp: Path, *extra: str, nproc: int = 1) -> None:
                str(nproc), "--master-addr", "127.0.0.1", "--master-port",
                str(random.randint(30000, 45000)), "-m", "nano_megatron.cli.train", "--config",
                str(cfg), *extra]
-    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=900, cwd=tmp)
-    assert r.returncode == 0, r.stderr[-3000:]
+    return subprocess.Popen(cmd, env=env, stdout=subprocess.PIPE, stderr=subprocess.PIPE,
+                            text=True, cwd=tmp)
+
+
+def _ref_cli_wait(proc) -> None:
+    import subprocess
+
+    try:
+        _, err = proc.communicate(timeout=900)
+    except subprocess.TimeoutExpired:
+        proc.terminate()                # torchrun stops its own workers on SIGTERM
+        _, err = proc.communicate(timeout=60)
+    assert proc.returncode == 0, err[-3000:]
+
+
+def _ref_cli(cfg: Path, tmp: Path, *extra: str, nproc: int = 1) -> None:
+    _ref_cli_wait(_ref_cli_start(cfg, tmp, *extra, nproc=nproc))
 
 
 def _curve(run_dir: Path):
@@ -400,8 +425,10 @@ def test_resume_from_reference_checkpoint(ref, tmp_path, case):
         return p
 
     full_cfg, part_cfg, ours_cfg = write("full"), write("part"), write("ours")
-    _ref_cli(full_cfg, tmp_path, nproc=world)
-    _ref_cli(part_cfg, tmp_path, "--max-steps", "2", nproc=world)
+    runs = [_ref_cli_start(full_cfg, tmp_path, nproc=world),
+            _ref_cli_start(part_cfg, tmp_path, "--max-steps", "2", nproc=world)]
+    for proc in runs:                   # the two reference runs are independent
+        _ref_cli_wait(proc)
     ref_full = _curve(next((tmp_path / "full").iterdir()))
     ckpt = next((tmp_path / "part").iterdir()) / "step_00000002"
     assert (ckpt / ".complete").is_file()
