@@ -404,8 +404,11 @@ class Trainer:
         loss_sum = sum(float(p["loss_sum"]) for p in pending)
         count = sum(float(p["token_count"]) for p in pending)
         loss = loss_sum / max(count, 1.0)
-        gn = float(pending[-1]["grad_norm"])
         n = len(pending)
+        # like the reference's metric store: the loss is token-weighted over the interval,
+        # every other per-step metric (gradient norm, learning rate) is the interval mean
+        gn = sum(float(p["grad_norm"]) for p in pending) / n
+        lr = sum(float(p["learning_rate"]) for p in pending) / n
         gbs = self.config.training.micro_batch_size * \
             self.config.training.gradient_accumulation_steps * \
             self.parallel.dp.size * self.parallel.ep.size
@@ -414,7 +417,7 @@ class Trainer:
         dev_max = phases["step"]
         metrics = {"step": self.state.step, "loss": loss,
                    "perplexity": math.exp(min(loss, 50.0)), "token_count": count,
-                   "grad_norm": gn, "learning_rate": pending[-1]["learning_rate"],
+                   "grad_norm": gn, "learning_rate": lr,
                    "samples_per_second": n * gbs / max(host_s, 1e-9),
                    "tokens_per_second": tokens / max(host_s, 1e-9),
                    "tokens_per_second_device": tokens / max(dev_max / 1000.0, 1e-9)}

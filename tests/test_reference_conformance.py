@@ -163,9 +163,12 @@ def test_config_defaults_match(ref):
     assert ours == theirs
 
 
-def test_training_curve_matches_reference_cli(ref, tmp_path):
+@pytest.mark.parametrize("interval", [1, 2], ids=["log_every_step", "log_every_2"])
+def test_training_curve_matches_reference_cli(ref, tmp_path, interval):
     """Same YAML through the reference CLI (subprocess) and ours: identical per-step loss,
-    gradient norm and learning rate from the same seed (same init, same data order)."""
+    gradient norm and learning rate from the same seed (same init, same data order); with
+    ``log_interval`` 2 each record aggregates two steps (token-weighted loss, last norm and
+    learning rate) the same way."""
     import json
     import os
     import subprocess
@@ -179,6 +182,7 @@ def test_training_curve_matches_reference_cli(ref, tmp_path):
     d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
                       vocab_size=256, seq_length=32)
     d["training"]["max_steps"] = 4
+    d["training"]["log_interval"] = interval
     d["optimizer"]["clip_grad_norm"] = 1.0
 
     def write(name):
@@ -204,7 +208,7 @@ def test_training_curve_matches_reference_cli(ref, tmp_path):
                  x["metrics"]["learning_rate"]) for x in recs if x["prefix"] == "train"]
 
     theirs, ours = curve("ref"), curve("ours")
-    assert [s for s, *_ in theirs] == [s for s, *_ in ours] == [1, 2, 3, 4]
+    assert [s for s, *_ in theirs] == [s for s, *_ in ours] == list(range(interval, 5, interval))
     for (s, l1, g1, lr1), (_, l2, g2, lr2) in zip(theirs, ours):
         assert l2 == pytest.approx(l1, rel=2e-6), (s, theirs, ours)
         assert g2 == pytest.approx(g1, rel=1e-5), (s, theirs, ours)
