@@ -890,3 +890,57 @@ def test_config_validation_agrees_with_reference(ref, case):
 
     assert outcome(config_from_dict, validate_config) == outcome(ref_from_dict, ref_validate), \
         over
+
+
+def test_generation_settings_match_reference(ref, tmp_path):
+    """One artifact, several sampling settings (greedy, top-k, nucleus, no BOS, long
+    continuation): both frameworks' generators return the same tokens and stop reason."""
+    import json
+    import os
+    import subprocess
+
+    import yaml
+
+    from nano_megatron_b200.cli import train as trcli
+    from nano_megatron_b200.inference import export_checkpoint, generate_from_artifact
+    from nano_megatron_b200.tokenizer import ByteBPETrainingConfig, ByteLevelBPETokenizer
+
+    texts = [f"the little fox {i} ran to the river and found a stone." for i in range(200)]
+    (tmp_path / "train.jsonl").write_text("".join(json.dumps({"text": t}) + "\n"
+                                                  for t in texts))
+    tok = ByteLevelBPETokenizer.train(texts, ByteBPETrainingConfig(vocab_size=300))
+    tok.save(tmp_path / "tok")
+    d = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
+                        "gpt_single_cpu.yaml").read_text())
+    d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
+                      vocab_size=tok.vocab_size, seq_length=32)
+    d["training"]["max_steps"] = 6
+    d["optimizer"]["lr"] = 3e-3
+    d["checkpoint"].update(directory=str(tmp_path / "ck"), save_interval=6)
+    d["data"].update(text_path=str(tmp_path / "train.jsonl"),
+                     tokenizer={"path": str(tmp_path / "tok")})
+    cfg = tmp_path / "cfg.yaml"
+    cfg.write_text(yaml.safe_dump(d))
+    trcli.run(cfg, log=lambda *_: None)
+    ckpt = next((tmp_path / "ck").iterdir()) / "step_00000006"
+    export_checkpoint(ckpt, tmp_path / "art")
+    env = dict(os.environ, PYTHONPATH=str(REF), OMP_NUM_THREADS="1")
+    settings = [
+        dict(temperature=0.0, top_p=1.0, top_k=0, seed=1, add_bos=True, max_new_tokens=20),
+        dict(temperature=1.0, top_p=1.0, top_k=1, seed=2, add_bos=True, max_new_tokens=12),
+        dict(temperature=0.7, top_p=0.5, top_k=0, seed=3, add_bos=False, max_new_tokens=12),
+        dict(temperature=1.3, top_p=0.9, top_k=40, seed=4, add_bos=True, max_new_tokens=28),
+    ]
+    for kw in settings:
+        args = ["--model", str(tmp_path / "art"), "--prompt", "the little fox", "--device",
+                "cpu", "--temperature", str(kw["temperature"]), "--top-p", str(kw["top_p"]),
+                "--top-k", str(kw["top_k"]), "--seed", str(kw["seed"]), "--max-new-tokens",
+                str(kw["max_new_tokens"]), "--json",
+                "--add-bos" if kw["add_bos"] else "--no-add-bos"]
+        r = subprocess.run([sys.executable, "-m", "nano_megatron.cli.generate", *args], env=env,
+                           capture_output=True, text=True, timeout=300, cwd=tmp_path)
+        assert r.returncode == 0, r.stderr[-2000:]
+        theirs = json.loads(r.stdout.strip().splitlines()[-1])
+        mine = generate_from_artifact(tmp_path / "art", "the little fox", device="cpu", **kw)
+        assert list(mine.generated_token_ids) == theirs["generated_token_ids"], (kw, theirs)
+        assert mine.stop_reason == theirs["stop_reason"] and mine.text == theirs["text"], kw
