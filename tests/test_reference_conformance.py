@@ -944,3 +944,70 @@ def test_generation_settings_match_reference(ref, tmp_path):
         mine = generate_from_artifact(tmp_path / "art", "the little fox", device="cpu", **kw)
         assert list(mine.generated_token_ids) == theirs["generated_token_ids"], (kw, theirs)
         assert mine.stop_reason == theirs["stop_reason"] and mine.text == theirs["text"], kw
+
+
+@pytest.mark.distributed
+def test_mmap_corpus_training_matches_reference(ref, tmp_path):
+    """Training on an mmap token corpus with shuffling over two data-parallel ranks: the
+    sampler order, window slicing and loss / gradient-norm curves equal the reference's."""
+    import json
+    import os
+    import random
+    import subprocess
+
+    import yaml
+
+    from dist_utils import run_ranks
+
+    from nano_megatron_b200.tokenizer import ByteBPETrainingConfig, ByteLevelBPETokenizer
+
+    rnd = random.Random(3)
+    words = "the a fox bird river stone sun ran flew sat under over big small".split()
+    texts = [" ".join(rnd.choice(words) for _ in range(rnd.randint(8, 60)))
+             for _ in range(300)]
+    (tmp_path / "docs.jsonl").write_text("".join(json.dumps({"text": t}) + "\n"
+                                                 for t in texts))
+    ByteLevelBPETokenizer.train(texts, ByteBPETrainingConfig(vocab_size=300)).save(
+        tmp_path / "tok")
+    env = dict(os.environ, PYTHONPATH=str(Path(__file__).parents[1]), OMP_NUM_THREADS="1")
+    r = subprocess.run([sys.executable, "-m", "nano_megatron_b200.cli.tokenizer", "preprocess",
+                        "--input", str(tmp_path / "docs.jsonl"), "--output",
+                        str(tmp_path / "corpus.mmap"), "--tokenizer", str(tmp_path / "tok"),
+                        "--format", "mmap"], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    vocab = json.loads((tmp_path / "tok" / "metadata.json").read_text())["vocab_size"]
+    d = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
+                        "gpt_single_cpu.yaml").read_text())
+    d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
+                      vocab_size=vocab, seq_length=32)
+    d["parallel"]["data"] = 2
+    d["training"].update(max_steps=4)
+    d["data"].update(mmap_path=str(tmp_path / "corpus.mmap"),
+                     tokenizer={"path": str(tmp_path / "tok")}, shuffle=True)
+
+    def write(name):
+        d["checkpoint"]["directory"] = str(tmp_path / name)
+        p = tmp_path / f"{name}.yaml"
+        p.write_text(yaml.safe_dump(d))
+        return p
+
+    ref_cfg, our_cfg = write("ref"), write("ours")
+    proc = _ref_cli_start(ref_cfg, tmp_path, nproc=2)
+    try:
+        run_ranks(2, _our_cli_rank, str(our_cfg))
+    finally:
+        _ref_cli_wait(proc)
+
+    def curve(name):
+        run = next((tmp_path / name).iterdir())
+        recs = [json.loads(x) for x in (run / "metrics.jsonl").read_text().splitlines()
+                if x.strip()]
+        return [(x["step"], x["metrics"]["loss"], x["metrics"]["grad_norm"])
+                for x in recs if x["prefix"] == "train"]
+
+    theirs, ours = curve("ref"), curve("ours")
+    assert [s for s, *_ in theirs] == [s for s, *_ in ours] == [1, 2, 3, 4]
+    for (s, l1, g1), (_, l2, g2) in zip(theirs, ours):
+        assert l2 == pytest.approx(l1, rel=1e-5), (s, theirs, ours)
+        assert g2 == pytest.approx(g1, rel=1e-4), (s, theirs, ours)
