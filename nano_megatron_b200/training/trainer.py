@@ -357,13 +357,23 @@ class Trainer:
                 self.save_checkpoint()
 
     def run_validation(self, log=print) -> dict[str, float]:
+        """Evaluate ``validation.batches`` batches. Only batch-replica source ranks hold a
+        validation loader; the others take part in every batch's routing and schedule with
+        ``None``, so the source's batch count is shared with them first."""
         batches = []
-        it = iter(self.validation_data)
-        for _ in range(self.config.validation.batches):
-            try:
-                batches.append(next(it))
-            except StopIteration:
-                break
+        if self.batch_router.is_source:
+            it = iter(self.validation_data)
+            for _ in range(self.config.validation.batches):
+                try:
+                    batches.append(next(it))
+                except StopIteration:
+                    break
+        g = self.batch_router.group
+        if g is not None and g.size > 1:
+            box = [len(batches) if self.batch_router.is_source else None]
+            dist.broadcast_object_list(box, src=g.ranks[0], group=g.process_group)
+            if not self.batch_router.is_source:
+                batches = [None] * int(box[0])
         metrics = self.evaluate(batches)
         if self.parallel.rank == 0 and log is not None:
             log("validation " + " ".join(f"{k}={v:.6g}" for k, v in metrics.items()))

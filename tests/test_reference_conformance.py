@@ -664,11 +664,21 @@ def test_tokenizer_cli_pipeline_matches_reference(ref, tmp_path):
         {k: v for k, v in m2.items() if "path" not in k}
 
 
+VALIDATION_LAYOUTS = {
+    "single": (1, {}),
+    "pp2": (2, {"parallel": {"pipeline": 2, "data": 1}}),
+    "cp2_ring": (2, {"parallel": {"context": 2, "data": 1},
+                     "context_parallel": {"backend": "ring"}}),
+    "tp2_sp": (2, {"parallel": {"tensor": 2, "data": 1, "sequence_parallel": True}}),
+}
+
+
 @pytest.mark.distributed
-def test_validation_flow_matches_reference(ref, tmp_path):
-    """Training with periodic validation on a text corpus through both CLIs: the same train
-    and validation loss records, the same best-validation pin (step, loss) and the same
-    retained checkpoints."""
+@pytest.mark.parametrize("layout", list(VALIDATION_LAYOUTS))
+def test_validation_flow_matches_reference(ref, tmp_path, layout):
+    """Training with periodic validation on a text corpus through both CLIs (one rank, or
+    two under PP / CP / TP: the forward-only schedules): the same train and validation loss
+    records, the same best-validation pin (step, loss) and the same retained checkpoints."""
     import json
 
     import yaml
@@ -697,6 +707,9 @@ def test_validation_flow_matches_reference(ref, tmp_path):
                                 "tokenizer": {"path": str(tmp_path / "tok")},
                                 "shuffle": False}}
     d["checkpoint"].update(save_interval=100, keep_last=1, save_best_validation=True)
+    world, over = VALIDATION_LAYOUTS[layout]
+    for section, values in over.items():
+        d[section].update(values)
 
     def write(name):
         d["checkpoint"]["directory"] = str(tmp_path / name)
@@ -705,8 +718,16 @@ def test_validation_flow_matches_reference(ref, tmp_path):
         return p
 
     ref_cfg, our_cfg = write("ref"), write("ours")
-    _ref_cli(ref_cfg, tmp_path)
-    trcli.run(our_cfg, log=lambda *_: None)
+    proc = _ref_cli_start(ref_cfg, tmp_path, nproc=world)
+    try:
+        if world == 1:
+            trcli.run(our_cfg, log=lambda *_: None)
+        else:
+            from dist_utils import run_ranks
+
+            run_ranks(world, _our_cli_rank, str(our_cfg))
+    finally:
+        _ref_cli_wait(proc)
 
     def records(name):
         run = next((tmp_path / name).iterdir())
