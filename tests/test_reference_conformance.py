@@ -1032,3 +1032,43 @@ def test_mmap_corpus_training_matches_reference(ref, tmp_path):
     for (s, l1, g1), (_, l2, g2) in zip(theirs, ours):
         assert l2 == pytest.approx(l1, rel=1e-5), (s, theirs, ours)
         assert g2 == pytest.approx(g1, rel=1e-4), (s, theirs, ours)
+
+
+@pytest.mark.distributed
+@pytest.mark.parametrize("mode", ["ddp", "zero1"])
+def test_dp_reshard_resume_matches_reference(ref, tmp_path, mode):
+    """A DP2 checkpoint written by the reference, resumed on ONE rank by the reference and by
+    this framework (data-parallel resharding: global sample offset, sharded optimizer
+    state): both continue with the same losses."""
+    import yaml
+
+    d = yaml.safe_load((Path(__file__).parents[1] / "examples" / "configs" /
+                        "gpt_single_cpu.yaml").read_text())
+    d["model"].update(layers=2, hidden_size=64, ffn_hidden_size=128, heads=4, kv_heads=2,
+                      vocab_size=256, seq_length=32)
+    d["data_parallel"]["mode"] = mode
+    d["checkpoint"].update(save_interval=2, keep_last=4)
+
+    def write(name, dp, gas):
+        d["parallel"]["data"] = dp
+        d["training"].update(max_steps=4, gradient_accumulation_steps=gas)
+        d["checkpoint"]["directory"] = str(tmp_path / name)
+        p = tmp_path / f"{name}.yaml"
+        p.write_text(yaml.safe_dump(d))
+        return p
+
+    part = write("part", 2, 1)
+    _ref_cli(part, tmp_path, "--max-steps", "2", nproc=2)
+    ckpt = next((tmp_path / "part").iterdir()) / "step_00000002"
+    ref_cfg, our_cfg = write("ref", 1, 2), write("ours", 1, 2)   # same global batch on 1 rank
+    proc = _ref_cli_start(ref_cfg, tmp_path, "--resume", str(ckpt), "--max-steps", "4")
+    try:
+        from nano_megatron_b200.cli import train as trcli
+
+        trcli.run(our_cfg, resume=ckpt, max_steps=4, log=lambda *_: None)
+    finally:
+        _ref_cli_wait(proc)
+    theirs = _curve(sorted((tmp_path / "ref").iterdir())[-1])
+    ours = _curve(sorted((tmp_path / "ours").iterdir())[-1])
+    for step in (3, 4):
+        assert ours[step] == pytest.approx(theirs[step], rel=2e-6), (step, ours, theirs)
