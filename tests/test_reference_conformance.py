@@ -385,6 +385,9 @@ RESUME_CASES = {
     "dp2_zero3": (2, {"parallel": {"data": 2}, "data_parallel": {"mode": "zero3"}}),
     "tp2_sp": (2, {"parallel": {"tensor": 2, "data": 1, "sequence_parallel": True}}),
     "pp2": (2, {"parallel": {"pipeline": 2, "data": 1}}),
+    "pp2_interleaved": (2, {"parallel": {"pipeline": 2, "data": 1}, "model": {"layers": 4},
+                            "pipeline": {"schedule": "interleaved_1f1b",
+                                         "virtual_stages_per_rank": 2}}),
 }
 
 
