@@ -268,6 +268,10 @@ LAYOUTS = {
     "dp2_bf16_reduce": {"parallel": {"data": 2}, "precision": {"grad_reduce": "bfloat16"}},
     "dp2_zero2_bf16_reduce": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero2"},
                               "precision": {"grad_reduce": "bfloat16"}},
+    "dp2_weight_decay": {"parallel": {"data": 2},
+                         "optimizer": {"weight_decay": 0.1, "lr": 1e-2}},
+    "dp2_zero2_weight_decay": {"parallel": {"data": 2}, "data_parallel": {"mode": "zero2"},
+                               "optimizer": {"weight_decay": 0.1, "lr": 1e-2}},
     "ep2": {"parallel": {"expert": 2, "data": 1}},
     "ep2_zero2": {"parallel": {"expert": 2, "data": 1}, "data_parallel": {"mode": "zero2"}},
 }
