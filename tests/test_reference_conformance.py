@@ -666,7 +666,11 @@ def test_tokenizer_cli_pipeline_matches_reference(ref, tmp_path):
             str(d / "val.mmap"), "--tokenizer", str(d / "tok"), "--format", "mmap")
         out, _ = cli(pkg, tag, "inspect", "--tokenizer", str(d / "tok"), "--text",
                      "the little cat ran home", "--add-bos", "--add-eos")
-        runs[tag] = (d, json.loads(out.strip().splitlines()[-1]))
+        # special-token-looking text stays text (encode_special_tokens)
+        out2, _ = cli(pkg, tag, "inspect", "--tokenizer", str(d / "tok"), "--text",
+                      "<|bos|> the cat <|endoftext|> sat <|pad|>")
+        runs[tag] = (d, (json.loads(out.strip().splitlines()[-1]),
+                         json.loads(out2.strip().splitlines()[-1])))
     (dr, ir), (do, io) = runs["ref"], runs["ours"]
     for name in ("train.jsonl", "val.jsonl", "tok/tokenizer.json"):
         assert digest(dr / name) == digest(do / name), name
