@@ -157,6 +157,8 @@ LAYOUTS = {
     "cp4_ring": ({"parallel": {"context": 4}, "cp": {"backend": "ring"}}, 4),
     "cp4_ring_zigzag": ({"parallel": {"context": 4},
                          "cp": {"backend": "ring", "load_balance": True}}, 4),
+    "tp2_cp2_sp_allgather": ({"parallel": {"tensor": 2, "context": 2, "sequence_parallel": True},
+                              "cp": {"backend": "all_gather"}}, 4),
     "tp2_cp2_sp_ring": ({"parallel": {"tensor": 2, "context": 2, "sequence_parallel": True},
                          "cp": {"backend": "ring"}}, 4),
     "pp2_dp2_zero2": ({"parallel": {"pipeline": 2, "data": 2}, "dp_mode": "zero2"}, 4),

@@ -282,6 +282,10 @@ LAYOUTS = {
                       "context_parallel": {"backend": "ring"},
                       "data_parallel": {"mode": "zero1"}},
     "pp2_ep2": {"parallel": {"pipeline": 2, "expert": 2, "data": 1}},
+    "pp2_dp2_interleaved_zero1": {"parallel": {"pipeline": 2, "data": 2},
+                                  "model": {"layers": 4}, "data_parallel": {"mode": "zero1"},
+                                  "pipeline": {"schedule": "interleaved_1f1b",
+                                               "virtual_stages_per_rank": 2}},
     "ep2": {"parallel": {"expert": 2, "data": 1}},
     "ep2_zero2": {"parallel": {"expert": 2, "data": 1}, "data_parallel": {"mode": "zero2"}},
 }
