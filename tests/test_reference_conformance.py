@@ -286,6 +286,9 @@ LAYOUTS = {
                                   "model": {"layers": 4}, "data_parallel": {"mode": "zero1"},
                                   "pipeline": {"schedule": "interleaved_1f1b",
                                                "virtual_stages_per_rank": 2}},
+    "dp2_mqa_rope_theta": {"parallel": {"data": 2},
+                           "model": {"kv_heads": 1, "rope_theta": 500000.0,
+                                     "norm_epsilon": 1e-6}},
     "ep2": {"parallel": {"expert": 2, "data": 1}},
     "ep2_zero2": {"parallel": {"expert": 2, "data": 1}, "data_parallel": {"mode": "zero2"}},
 }
