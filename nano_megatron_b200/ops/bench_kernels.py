@@ -1,10 +1,12 @@
 """Kernel microbenchmarks: CUDA-event timing of each sm_100a kernel vs its library baseline.
 
-    python -m nano_megatron_b200.ops.bench_kernels [--case all|gemm|attn|mem] [--iters N]
+    python -m nano_megatron_b200.ops.bench_kernels [--case all|gemm|gemm_tiles|attn|mem] [--iters N]
 
 Prints one JSON object of achieved TFLOP/s (GEMM, attention) or GB/s and the fraction of
 the measured copy bandwidth (memory-bound kernels: RMSNorm, SwiGLU backward, attention
-backward prep / dQ conversion, embedding, AdamW). Also the small, self-contained workload used for ncu captures
+backward prep / dQ conversion, embedding, AdamW). ``--case gemm_tiles`` sweeps the GEMM
+tile width (``block_n`` 128 and 256) on the 311M model's shapes, the data behind the tile
+choice in ``choose_bn`` (csrc/gemm_tcgen05.cu). Also the small, self-contained workload used for ncu captures
 (``--case gemm_profile`` / ``attn_profile`` run a few launches of one kernel).
 """
 
@@ -64,6 +66,35 @@ def gemm_cases(iters: int) -> dict:
             iters) / 1e9
         res[f"cublas_wgrad_{m}x{n}x{k}"] = fl / _time(
             lambda: torch.matmul(dy.t(), x, out=cb), iters) / 1e9
+    return res
+
+
+def gemm_tile_cases(iters: int) -> dict:
+    """TFLOP/s of forward, data-gradient and weight-gradient GEMMs at both tile widths."""
+    res = {}
+    for m, n, k in [(4096, 3072, 1024), (4096, 1024, 1024), (4096, 1024, 2736),
+                    (4096, 5472, 1024), (4096, 8192, 1024)]:
+        a = torch.randn(m, k, device="cuda").bfloat16()
+        b = torch.randn(n, k, device="cuda").bfloat16()
+        bt = b.t().contiguous()
+        c = torch.empty(m, n, device="cuda", dtype=torch.bfloat16)
+        fl = 2 * m * n * k
+        for bn in (128, 256):
+            res[f"fwd_bn{bn}_{m}x{n}x{k}"] = fl / _time(
+                lambda: G.gemm(a, b, c, block_n=bn), iters) / 1e9
+            res[f"dgrad_bn{bn}_{m}x{n}x{k}"] = fl / _time(
+                lambda: G.gemm(a, bt, c, b_mn=True, block_n=bn), iters) / 1e9
+        res[f"cublas_{m}x{n}x{k}"] = fl / _time(lambda: torch.matmul(a, b.t(), out=c), iters) / 1e9
+    for m, n, k in [(1024, 1024, 4096), (3072, 1024, 4096), (5472, 1024, 4096),
+                    (1024, 2736, 4096)]:
+        dy = torch.randn(k, m, device="cuda").bfloat16()
+        x = torch.randn(k, n, device="cuda").bfloat16()
+        cf = torch.zeros(m, n, device="cuda")
+        fl = 2 * m * n * k
+        for bn in (128, 256):
+            res[f"wgrad_bn{bn}_{m}x{n}x{k}"] = fl / _time(
+                lambda: G.gemm(dy, x, cf, a_mn=True, b_mn=True, epilogue=G.EPI_F32_ACC,
+                               beta=1.0, block_n=bn), iters) / 1e9
     return res
 
 
@@ -192,6 +223,8 @@ def main() -> None:
     out = {}
     if a.case in ("all", "gemm"):
         out.update(gemm_cases(a.iters))
+    if a.case == "gemm_tiles":
+        out.update(gemm_tile_cases(a.iters))
     if a.case in ("all", "attn"):
         out.update(attn_cases(a.iters))
     if a.case in ("all", "mem", "norm"):
