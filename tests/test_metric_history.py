@@ -1,6 +1,6 @@
 """The versioned ``metrics.jsonl`` timeline: encoding, resume replay and damaged files.
 
-Mirrors the reference's metric-history unit tests (tests/unit/test_metric_history.py:24-160):
+Mirrors the reference's metric-history unit tests (tests/unit/test_metric_history.py:24-152):
 non-finite metrics round-trip through strict JSON; a resumed run copies exactly the
 checkpoint's prefix of the previous timeline and continues its sequence numbers; a missing
 previous timeline warns and starts empty; a timeline that disagrees with the checkpoint is
