@@ -88,3 +88,27 @@ def test_cp_slice_rejects_a_sequence_that_does_not_divide():
     with pytest.raises(ValueError, match="2\\*CP"):
         shard_batch_for_context_parallel(_batch(6), 0, 2, load_balance=True)
     assert shard_batch_for_context_parallel(_batch(6), 0, 1) is not None
+
+
+def test_interval_metrics_weight_loss_by_tokens_and_average_the_rest():
+    """The reference's metric-store contract (tests/unit/test_metrics.py:30-54): the logged
+    loss is sum(loss_sum) / sum(token_count) over the interval, perplexity its exponent,
+    other metrics the interval mean; one process keeps the additive totals."""
+    import math
+    from types import SimpleNamespace
+
+    from nano_megatron_b200.training.metrics import (MetricStore, aggregate_loss_metrics,
+                                                     loss_and_perplexity)
+
+    loss, ppl = loss_and_perplexity(4.0 + 9.0, 2.0 + 3.0)
+    assert loss == pytest.approx(2.6) and ppl == pytest.approx(math.exp(2.6))
+    assert loss_and_perplexity(1e4, 1.0)[1] == pytest.approx(math.exp(50.0))   # clamped
+    store = MetricStore()
+    for lr in (0.3, 0.1):
+        store.add("lr", lr)
+    assert store.mean("lr") == pytest.approx(0.2) and math.isnan(store.mean("absent"))
+    store.clear()
+    assert math.isnan(store.mean("lr"))
+    acc = SimpleNamespace(loss_sum=torch.tensor(12.0), token_count=torch.tensor(6.0))
+    s, n = aggregate_loss_metrics(acc, None, torch.device("cpu"))
+    assert (float(s), float(n)) == (12.0, 6.0) and s.dtype == torch.float64
