@@ -224,6 +224,18 @@ def test_lr_schedule_warmup_and_cosine():
         s2.load_state_dict(st, expected_completed_steps=3)
 
 
+def test_constant_schedule_keeps_warmup_but_skips_decay():
+    """Reference: tests/unit/test_lr_scheduler.py:45-51."""
+    cfg = config_from_dict({"lr_scheduler": {"schedule": "constant", "warmup_steps": 4,
+                                             "min_lr": 1e-5},
+                            "optimizer": {"lr": 2e-3}, "training": {"max_steps": 10}})
+    dp = type("DP", (), {"set_learning_rate": lambda self, lr: None})()
+    s = LearningRateScheduler(config=cfg.lr_scheduler, optimizer_config=cfg.optimizer,
+                              data_parallel=dp, max_steps=10)
+    assert [s.rate_at(k) for k in range(4)] == pytest.approx([5e-4, 1e-3, 1.5e-3, 2e-3])
+    assert [s.rate_at(k) for k in (4, 9, 10, 50)] == pytest.approx([2e-3] * 4)
+
+
 def test_split_microbatches():
     b = {"input_ids": torch.arange(24).view(6, 4), "labels": torch.zeros(6, 4), "meta": 3}
     parts = split_microbatches(b, 2)
