@@ -236,6 +236,18 @@ def test_constant_schedule_keeps_warmup_but_skips_decay():
     assert [s.rate_at(k) for k in (4, 9, 10, 50)] == pytest.approx([2e-3] * 4)
 
 
+@pytest.mark.parametrize("field", ["cp_sharded", "sp_sharded", "tp_hidden_sharded"])
+def test_tensor_layout_flags_are_strict_booleans(field):
+    """Reference: tests/unit/test_parallel_layout.py:6-26."""
+    from nano_megatron_b200.parallel.layout import TensorLayout
+
+    assert TensorLayout(cp_sharded=True, sp_sharded=True, tp_hidden_sharded=True
+                        ).sequence_dim == 1
+    flags = {"cp_sharded": False, "sp_sharded": False, "tp_hidden_sharded": False, field: 1}
+    with pytest.raises(TypeError, match=field):
+        TensorLayout(**flags)
+
+
 def test_split_microbatches():
     b = {"input_ids": torch.arange(24).view(6, 4), "labels": torch.zeros(6, 4), "meta": 3}
     parts = split_microbatches(b, 2)
