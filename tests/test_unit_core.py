@@ -248,6 +248,41 @@ def test_tensor_layout_flags_are_strict_booleans(field):
         TensorLayout(**flags)
 
 
+def test_parameter_domain_registry_is_identity_keyed_and_strict():
+    """Reference: tests/unit/test_topology_domains.py:13-73 (distinct default replica
+    groups; identity-based idempotent registration; conflicts rejected; module registration
+    and completeness validation)."""
+    from nano_megatron_b200.parallel.domains import (ParameterDomain,
+                                                     ParameterDomainRegistry,
+                                                     default_replica_group)
+    from nano_megatron_b200.parallel.group_plan import GroupKey
+
+    assert default_replica_group("dense") == GroupKey.DENSE_REPLICA
+    assert default_replica_group(ParameterDomain.EXPERT) == GroupKey.EXPERT_REPLICA
+    with pytest.raises(ValueError):
+        ParameterDomain.parse("shared")
+    reg = ParameterDomainRegistry()
+    w = torch.nn.Parameter(torch.zeros(4, 2))
+    twin = torch.nn.Parameter(torch.zeros(4, 2))       # equal values, another identity
+    first = reg.register(w, tensor_sharded=True, tensor_shard_dim=0, name="w")
+    assert reg.register(w, tensor_sharded=True, tensor_shard_dim=0) == first   # idempotent
+    assert w in reg and twin not in reg and len(reg) == 1 and reg.name(w) == "w"
+    with pytest.raises(ValueError, match="already registered"):
+        reg.register(w, domain="expert", tensor_sharded=True, tensor_shard_dim=0)
+    with pytest.raises(ValueError, match="rename"):
+        reg.register(w, tensor_sharded=True, tensor_shard_dim=0, name="other")
+    with pytest.raises(ValueError):
+        reg.register(twin, tensor_shard_dim=1)          # a shard dim needs tensor_sharded
+    mod = torch.nn.Linear(2, 3)
+    reg.register_module(mod, domain="expert", prefix="moe.")
+    assert reg.domain(mod.weight) == ParameterDomain.EXPERT
+    assert reg.replica_group(mod.bias) == GroupKey.EXPERT_REPLICA
+    assert reg.name(mod.bias) == "moe.bias"
+    reg.validate_complete([w, mod.weight, mod.bias])
+    with pytest.raises(ValueError, match="no registered domain"):
+        reg.validate_complete([w, twin])
+
+
 def test_split_microbatches():
     b = {"input_ids": torch.arange(24).view(6, 4), "labels": torch.zeros(6, 4), "meta": 3}
     parts = split_microbatches(b, 2)
