@@ -283,6 +283,48 @@ def test_parameter_domain_registry_is_identity_keyed_and_strict():
         reg.validate_complete([w, twin])
 
 
+def test_flat_buffers_round_trip_pad_and_cut_buckets():
+    """Reference: tests/unit/test_data_parallel_buckets.py:21-44 (flat bucket round trip
+    and padding); also the bucket cut at ``bucket_bytes``, per-domain buckets and unit
+    boundaries."""
+    from types import SimpleNamespace
+
+    from nano_megatron_b200.data_parallel.buffers import FlatBuffers
+    from nano_megatron_b200.parallel.domains import ParameterDomainRegistry
+
+    torch.manual_seed(0)
+    ps = [torch.nn.Parameter(torch.randn(n)) for n in (5, 7, 3, 4)]
+    orig = [p.detach().clone() for p in ps]
+    reg = ParameterDomainRegistry()
+    for i, p in enumerate(ps):
+        reg.register(p, domain="expert" if i == 3 else "dense", name=f"p{i}")
+    par = SimpleNamespace(group=lambda key: SimpleNamespace(size=3, rank=1))
+    fb = FlatBuffers([(f"layers.{i // 2}.p{i}", p) for i, p in enumerate(ps)], domains=reg,
+                     parallel=par, bucket_bytes=12 * 4, param_dtype=torch.float32,
+                     grad_dtype=torch.float32, device=torch.device("cpu"))
+    # dense: p0 + p1 = 12 elements fit one bucket, p2 opens the next; expert: its own
+    assert [[s.name for s in b.slices] for b in fb.buckets] == \
+        [["layers.0.p0", "layers.0.p1"], ["layers.1.p2"], ["layers.1.p3"]]
+    assert [str(getattr(b.domain, "value", b.domain)) for b in fb.buckets] == \
+        ["dense", "dense", "expert"]
+    for p, o in zip(ps, orig):                      # values survive; params view the buffer
+        assert torch.equal(p.detach(), o)
+        assert p.data.untyped_storage().data_ptr() == fb.param_flat.untyped_storage().data_ptr()
+        p.main_grad.fill_(1.0)
+    assert fb.grad_flat.sum().item() == sum(p.numel() for p in ps)
+    for b in fb.buckets:                            # equal shards over the replica group
+        assert b.padded_numel % 3 == 0 and b.padded_numel >= b.numel
+        assert b.shard_view(b.grad_data).numel() == b.shard_numel
+        assert b.storage_numel >= b.padded_numel
+    fb.zero_grad()
+    assert fb.grad_flat.abs().sum().item() == 0
+    cut = FlatBuffers([(f"layers.{i}.p", torch.nn.Parameter(torch.ones(2))) for i in range(3)],
+                      domains=None, parallel=None, bucket_bytes=1 << 20,
+                      param_dtype=torch.float32, grad_dtype=torch.float32,
+                      device=torch.device("cpu"), unit_key=lambda n: n.split(".")[1])
+    assert len(cut.buckets) == 3                    # never straddles a sharding unit
+
+
 def test_split_microbatches():
     b = {"input_ids": torch.arange(24).view(6, 4), "labels": torch.zeros(6, 4), "meta": 3}
     parts = split_microbatches(b, 2)
