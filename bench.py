@@ -125,7 +125,7 @@ def make_config_dict(n_gpus: int, steps: int, workload: str = "311m", *,
     gas = w["global_batch"] // (w["micro_batch"] * dp)
     horizon = max(10488, steps + 100)
     d = {
-        "distributed": {"backend": "nccl", "device": "cuda", "timeout_minutes": 10},
+        "distributed": {"backend": "nccl", "device": "cuda", "timeout_minutes": 5},
         "parallel": {"tensor": tp, "pipeline": pp, "context": lay["context"], "expert": 1,
                      "data": dp, "order": ["tp", "cp", "ep", "dp", "pp"],
                      "sequence_parallel": tp > 1},
@@ -333,13 +333,49 @@ def run_ours(args, rank, world, local):
                                 seed=1234 + comps.parallel.coordinate.dp)
     src = trainer.batch_router.is_source
     lib = _ext.lib()
-    with ClockSampler.for_device(device) as clocks:
-        dev_ms, _, launches = run_timed(trainer, batches, args.steps, args.warmup, device, src,
-                                        e2e=False, lib=lib)
-    e2e_ms, e2e_wall, _ = run_timed(trainer, batches, args.steps, 0, device, src, e2e=True)
-    _ext.check_status(device)
-    return finish(args, rank, world, dev_ms, e2e_ms, e2e_wall, clocks.summary(), launches,
-                  impl="ours", runtime=runtime)
+    try:
+        with ClockSampler.for_device(device) as clocks:
+            dev_ms, _, launches = run_timed(trainer, batches, args.steps, args.warmup, device,
+                                            src, e2e=False, lib=lib)
+        e2e_ms, e2e_wall, _ = run_timed(trainer, batches, args.steps, 0, device, src, e2e=True)
+        _ext.check_status(device)
+        report(args, rank, dev_ms, e2e_ms, e2e_wall, clocks.summary(), launches, impl="ours")
+        if args.breakdown:
+            kernel_breakdown(trainer, batches, device, src, args.breakdown, rank)
+    finally:
+        # graphs (holding NCCL work) -> TP barrier -> unmap peers -> barrier -> free own
+        # buffer -> subgroups -> default group; see distributed/shutdown.py
+        comps.close(trainer)
+    return 0
+
+
+def kernel_breakdown(trainer, batches, device, is_source, out_dir: str, rank: int) -> None:
+    """Diagnostic, after the timed steps: one more train step under ``torch.profiler``;
+    writes this rank's device time per kernel name (sorted, with shares of the step's
+    kernel time) to ``out_dir/kernels_rank<r>.json``. Profiler times are for shares only,
+    never for the reported throughput."""
+    import torch
+
+    os.makedirs(out_dir, exist_ok=True)
+    barrier_sync(device)
+    acts = [torch.profiler.ProfilerActivity.CPU, torch.profiler.ProfilerActivity.CUDA]
+    with torch.profiler.profile(activities=acts) as prof:
+        trainer.train_step(batches[0] if is_source else None)
+        torch.cuda.synchronize(device)
+    totals: dict = {}
+    for ev in prof.events():
+        if ev.device_type == torch.autograd.DeviceType.CUDA:
+            t = totals.setdefault(ev.name, [0.0, 0])
+            t[0] += ev.device_time_total if hasattr(ev, "device_time_total") else ev.cuda_time
+            t[1] += 1
+    rows = sorted(((n, us, c) for n, (us, c) in totals.items()), key=lambda r: -r[1])
+    total = sum(r[1] for r in rows) or 1.0
+    out = {"rank": rank, "kernel_us_total": total,
+           "kernels": [{"name": n[:160], "us": round(us, 1), "launches": c,
+                        "share": round(us / total, 4)} for n, us, c in rows]}
+    with open(os.path.join(out_dir, f"kernels_rank{rank}.json"), "w") as f:
+        json.dump(out, f, indent=1)
+    barrier_sync(device)
 
 
 # ---------------------------------------------------------------------- reference arm
@@ -389,11 +425,22 @@ def run_reference(args, rank, world, local):
     batches = synthetic_batches(4, rows, w["model"]["seq_length"], w["model"]["vocab_size"],
                                 seed=1234 + parallel.coordinate.dp)
     src = trainer.batch_router.is_source
-    with ClockSampler.for_device(device) as clocks:
-        dev_ms, _, _ = run_timed(trainer, batches, args.steps, args.warmup, device, src, e2e=False)
-    e2e_ms, e2e_wall, _ = run_timed(trainer, batches, args.steps, 0, device, src, e2e=True)
-    return finish(args, rank, world, dev_ms, e2e_ms, e2e_wall, clocks.summary(), None,
-                  impl="reference", runtime=runtime)
+    try:
+        with ClockSampler.for_device(device) as clocks:
+            dev_ms, _, _ = run_timed(trainer, batches, args.steps, args.warmup, device, src,
+                                     e2e=False)
+        e2e_ms, e2e_wall, _ = run_timed(trainer, batches, args.steps, 0, device, src, e2e=True)
+        report(args, rank, dev_ms, e2e_ms, e2e_wall, clocks.summary(), None, impl="reference")
+    finally:
+        import torch.distributed as dist
+
+        torch.cuda.synchronize(device)
+        del trainer
+        if dist.is_available() and dist.is_initialized():
+            dist.barrier(device_ids=[device.index])
+        parallel.close()
+        runtime.close()
+    return 0
 
 
 def unavailable(why: str) -> int:
@@ -402,7 +449,7 @@ def unavailable(why: str) -> int:
     return 0
 
 
-def finish(args, rank, world, dev_ms, e2e_ms, e2e_wall_ms, clocks, launches, *, impl, runtime):
+def report(args, rank, dev_ms, e2e_ms, e2e_wall_ms, clocks, launches, *, impl):
     w = WORKLOADS[args.config]
     seq, gb = w["model"]["seq_length"], w["global_batch"]
     tokens_per_step = gb * seq
@@ -430,12 +477,6 @@ def finish(args, rank, world, dev_ms, e2e_ms, e2e_wall_ms, clocks, launches, *, 
         line["gpu_launches"] = launches
     if rank == 0:
         print(json.dumps(line), flush=True)
-    import torch.distributed as dist
-
-    if dist.is_available() and dist.is_initialized():
-        dist.barrier()
-    runtime.close()
-    return 0
 
 
 def main() -> int:
@@ -452,6 +493,9 @@ def main() -> int:
     ap.add_argument("--no-cuda-graphs", action="store_true",
                     help="diagnostic: launch every kernel from Python instead of replaying one "
                          "CUDA graph per microbatch")
+    ap.add_argument("--breakdown", default=None, metavar="DIR",
+                    help="diagnostic: after timing, profile one more step and write per-kernel "
+                         "device times per rank to DIR")
     args = ap.parse_args()
     rank, world, local = dist_env()
     layout_of(args.config, args.gpus)

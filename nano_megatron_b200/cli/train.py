@@ -139,6 +139,7 @@ def run(config_path: Path, *, overrides: Sequence[str] = (), resume: Path | None
             ckpt.close()
             if health is not None:
                 health.stop()
+            comps.close(trainer)    # graphs, peer memory, subgroups, default group, in order
         if runtime.is_primary:
             log(f"finished step={state.step} samples={state.consumed_samples} "
                 f"tokens={state.consumed_tokens}")

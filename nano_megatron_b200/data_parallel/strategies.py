@@ -213,6 +213,14 @@ class DataParallelStrategy:
             self._inflight.clear()
         return done
 
+    def release_pending_work(self) -> None:
+        """Wait for and drop every asynchronous reduction still referenced (shutdown)."""
+        for work, _low in getattr(self, "_inflight", {}).values():
+            work.wait()
+        if hasattr(self, "_inflight"):
+            self._inflight.clear()
+        self._pending = []
+
     def _reduce_dtype(self) -> torch.dtype | None:
         """``precision.grad_reduce`` when it differs from the fp32 gradient buffers: the
         replica sum then runs on a copy in that dtype (as the reference packs its buckets

@@ -88,11 +88,22 @@ class SymmetricWorkspace:
                     ag_bytes=ag_bytes, opened=[]) for r in range(size)]
 
     def close(self) -> None:
+        """Unmap every peer buffer (``cudaIpcCloseMemHandle``). Call only after every peer
+        has finished the kernels that store into this rank's view of it (a TP barrier)."""
+        if not self._opened:
+            return
         from nano_megatron_b200.ops._ext import lib
 
-        for p in self._opened:
+        opened, self._opened = self._opened, []
+        for p in opened:
             lib().symm_close(p, self.device.index)
-        self._opened = []
+        self.ptrs = [p if r == self.rank else 0 for r, p in enumerate(self.ptrs)]
+
+    def release(self) -> None:
+        """Free this rank's own buffer. Call only after every peer has unmapped it."""
+        self.close()
+        self.owner = None
+        self.ptrs = []
 
     # ------------------------------------------------------------------ addressing
     def epoch_ptr(self, channel: int) -> int:

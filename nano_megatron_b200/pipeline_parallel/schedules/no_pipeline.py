@@ -47,6 +47,11 @@ class NoPipelineSchedule:
             with nvtx_range(f"graph mb {i}"):
                 acc.add(self._graphs[key].run(mb).clone(), batch_labels(mb))
 
+    def release_graphs(self) -> None:
+        graphs, self._graphs = self._graphs, {}
+        for g in graphs.values():
+            g.release()
+
     def forward_backward(self, microbatches, *, forward_only: bool = False
                          ) -> LossAccumulator:
         acc = LossAccumulator()

@@ -77,6 +77,12 @@ class GraphedMicrobatch:
         self.graph = g
         self.dp.zero_grad()                  # drop the warm-up's gradient contribution
 
+    def release(self) -> None:
+        """Free the graph and its static buffers (the graph's memory pool goes with it)."""
+        self.graph = None
+        self.out = None
+        self.static = {}
+
     def run(self, mb: dict) -> torch.Tensor:
         from nano_megatron_b200.ops._ext import lib
 

@@ -29,6 +29,18 @@ class TrainingComponents:
     model: torch.nn.Module
     built: object
     data_parallel: object
+    tp_workspace: object = None
+
+    def close(self, trainer=None, *, keep_runtime: bool = False) -> None:
+        """Ordered teardown: graphs, peer mappings, own buffer, subgroups and (unless
+        ``keep_runtime``) the default group
+        (:func:`nano_megatron_b200.distributed.shutdown.shutdown`)."""
+        from nano_megatron_b200.distributed.shutdown import shutdown
+
+        ws, self.tp_workspace = self.tp_workspace, None
+        shutdown(trainer=trainer, model=self.model, workspace=ws, parallel=self.parallel,
+                 runtime=None if keep_runtime else self.runtime,
+                 device=getattr(self.runtime, "device", None))
 
 
 def build_model(config, parallel, rng, *, device):
@@ -58,5 +70,5 @@ def build_training_components(config, runtime) -> TrainingComponents:
     strategy.configure_precision(config.precision)
     from nano_megatron_b200.tensor_parallel.fused import attach_tp_workspace
 
-    attach_tp_workspace(model, config, parallel, torch.device(runtime.device))
-    return TrainingComponents(runtime, parallel, rng, model, built, strategy)
+    ws = attach_tp_workspace(model, config, parallel, torch.device(runtime.device))
+    return TrainingComponents(runtime, parallel, rng, model, built, strategy, ws)

@@ -478,6 +478,17 @@ class Trainer:
         if self.checkpoint is not None and hasattr(self.checkpoint, "flush"):
             self.checkpoint.flush()
 
+    def release_graphs(self) -> None:
+        """Drop every captured CUDA graph (and the device work handles of the data-parallel
+        strategy). Graphs that captured NCCL collectives must be gone before the process
+        groups are destroyed."""
+        release = getattr(self.schedule, "release_graphs", None)
+        if callable(release):
+            release()
+        drop = getattr(self.data_parallel, "release_pending_work", None)
+        if callable(drop):
+            drop()
+
     def close(self) -> None:
         try:
             self.flush()

@@ -60,7 +60,9 @@ def _worker(rank, world, port, errq):
         torch.cuda.synchronize()
         assert int(status_word(dev).item()) == 0
         dist.barrier(device_ids=[rank])
-        ws.close()
+        ws.close()                        # unmap peers once nobody stores into them
+        dist.barrier(device_ids=[rank])
+        ws.release()                      # free the own buffer once no peer maps it
         dist.destroy_process_group()
     except Exception:  # noqa: BLE001
         errq.put((rank, traceback.format_exc()))

@@ -64,6 +64,7 @@ def _worker(rank, world, port, out_dir, errq):
             grads = {n: p.main_grad.detach().float().cpu().clone()
                      for n, p in comps.model.named_parameters()}
             results[(fused, graphs)] = (float(s / c), grads)
+            comps.close(tr, keep_runtime=True)    # graphs, peer memory, subgroups
         from nano_megatron_b200.ops._ext import check_status
 
         check_status(runtime.device)

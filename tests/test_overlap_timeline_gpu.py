@@ -77,7 +77,7 @@ def _worker(rank, world, port, out_dir, errq):
             torch.cuda.synchronize()
         path = os.path.join(out_dir, f"trace{rank}.json")
         prof.export_chrome_trace(path)
-        runtime.close()
+        comps.close(tr)
     except Exception:  # noqa: BLE001
         errq.put((rank, traceback.format_exc()))
         raise

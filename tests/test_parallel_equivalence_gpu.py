@@ -101,7 +101,7 @@ def _step(cfg, out_path, full_path=None):
     check_status(rt.device)
     torch.save({"loss": float(s / n), "grads": grads, "tp_rank": tp.rank, "tp": tp.size,
                 "dp_rank": c.dp}, out_path)
-    rt.close()
+    comps.close(tr)
 
 
 def _single_rank(rank, world, out_dir):
