@@ -117,12 +117,25 @@ def layout_name(lay: dict) -> str:
     return "".join(parts) or "tp1"
 
 
+def micro_batch_of(workload: str, n_gpus: int, override: int | None = None) -> int:
+    """Micro-batch size: ``override`` if given, else the workload's value for this GPU
+    count (an int, or a mapping GPU count -> int). The global batch never changes."""
+    if override:
+        return int(override)
+    mb = WORKLOADS[workload]["micro_batch"]
+    return int(mb[n_gpus]) if isinstance(mb, dict) else int(mb)
+
+
 def make_config_dict(n_gpus: int, steps: int, workload: str = "311m", *,
-                     reference: bool = False) -> dict:
+                     reference: bool = False, micro_batch: int | None = None) -> dict:
     w = WORKLOADS[workload]
     lay = layout_of(workload, n_gpus)
     tp, pp, dp = lay["tensor"], lay["pipeline"], lay["data"]
-    gas = w["global_batch"] // (w["micro_batch"] * dp)
+    mb = micro_batch_of(workload, n_gpus, micro_batch)
+    if w["global_batch"] % (mb * dp):
+        raise SystemExit(f"global batch {w['global_batch']} is not a multiple of micro-batch "
+                         f"{mb} x DP {dp}")
+    gas = w["global_batch"] // (mb * dp)
     horizon = max(10488, steps + 100)
     d = {
         "distributed": {"backend": "nccl", "device": "cuda", "timeout_minutes": 5},
@@ -137,7 +150,7 @@ def make_config_dict(n_gpus: int, steps: int, workload: str = "311m", *,
                       "clip_grad_norm": 1.0},
         "lr_scheduler": {"schedule": "cosine", "warmup_steps": 0, "decay_steps": horizon,
                          "min_lr": 3e-5},
-        "training": {"micro_batch_size": w["micro_batch"], "gradient_accumulation_steps": gas,
+        "training": {"micro_batch_size": mb, "gradient_accumulation_steps": gas,
                      "max_steps": horizon, "seed": 1234, "log_interval": 10},
     }
     sections = dict(w.get("sections", {}))
@@ -318,7 +331,8 @@ def run_ours(args, rank, world, local):
     from nano_megatron_b200.training import Trainer
     from nano_megatron_b200.training.engine import build_training_components
 
-    d = make_config_dict(args.gpus, args.steps + args.warmup, args.config)
+    d = make_config_dict(args.gpus, args.steps + args.warmup, args.config,
+                         micro_batch=args.micro_batch)
     d["kernels"] = {"backend": "b200", "fused_tp_comm": not args.no_fused_tp,
                     "cuda_graphs": not args.no_cuda_graphs}
     cfg = config_from_dict(d)
@@ -395,7 +409,8 @@ def run_reference(args, rank, world, local):
     from nano_megatron.parallel import ParallelContext, ParallelRNG, ParameterDomainRegistry, RNGStream
     from nano_megatron.training import Trainer
 
-    d = make_config_dict(args.gpus, args.steps + args.warmup, args.config, reference=True)
+    d = make_config_dict(args.gpus, args.steps + args.warmup, args.config, reference=True,
+                         micro_batch=args.micro_batch)
     d["wandb"] = {"enabled": False}
     cfg = config_from_dict(d)
     runtime = DistributedRuntime(cfg.distributed).initialize()
@@ -465,7 +480,8 @@ def report(args, rank, dev_ms, e2e_ms, e2e_wall_ms, clocks, launches, *, impl):
         "dtype": "bf16", "data": "synthetic uniform-random token ids, random-init weights",
         "config": {"model": w["describe"], "name": args.config,
                    "global_batch": gb, "seq_len": seq,
-                   "micro_batch": w["micro_batch"], "parallelism": layout_name(lay),
+                   "micro_batch": micro_batch_of(args.config, args.gpus, args.micro_batch),
+                   "parallelism": layout_name(lay),
                    "l2": "no flush: weights (>= 622 MB) and activations exceed the 126 MB L2"},
         "clocks": clocks,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "wall_ms_per_step": e2e_wall_ms / args.steps,
@@ -493,6 +509,8 @@ def main() -> int:
     ap.add_argument("--no-cuda-graphs", action="store_true",
                     help="diagnostic: launch every kernel from Python instead of replaying one "
                          "CUDA graph per microbatch")
+    ap.add_argument("--micro-batch", type=int, default=None,
+                    help="override the workload's micro-batch size (global batch unchanged)")
     ap.add_argument("--breakdown", default=None, metavar="DIR",
                     help="diagnostic: after timing, profile one more step and write per-kernel "
                          "device times per rank to DIR")

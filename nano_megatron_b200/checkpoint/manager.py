@@ -471,6 +471,7 @@ class CheckpointManager:
 # They are left out of the manifest's run_config while at the default, so that the
 # reference's own config loader (which rejects unknown fields) can read the manifest.
 _EXTENSION_FIELDS = {("kernels", "cuda_graphs"): True, ("kernels", "fused_tp_comm"): True,
+                     ("kernels", "fused_dp_comm"): True, ("kernels", "fused_cp_comm"): True,
                      ("context_parallel", "load_balance"): False}
 
 

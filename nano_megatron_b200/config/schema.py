@@ -249,11 +249,19 @@ class KernelConfig:
     # Sequence-parallel TP collectives fused into the GEMMs over NVLink symmetric memory
     # (AG->GEMM, GEMM->RS); off = NCCL all-gather / reduce-scatter around plain GEMMs.
     fused_tp_comm: bool = True
+    # Data-parallel gradient reduction fused with the sharded AdamW update and the bf16
+    # parameter all-gather over NVLink peer memory (DDP, ZeRO-1/2); off = NCCL collectives.
+    fused_dp_comm: bool = True
+    # Context-parallel ring attention pulling the next K/V block straight from its owner's
+    # memory (peer loads) instead of NCCL send/recv.
+    fused_cp_comm: bool = True
 
     def __post_init__(self) -> None:
         _set(self, "backend", _enum("kernels.backend", KernelBackend, self.backend))
         _bool("kernels.cuda_graphs", self.cuda_graphs)
         _bool("kernels.fused_tp_comm", self.fused_tp_comm)
+        _bool("kernels.fused_dp_comm", self.fused_dp_comm)
+        _bool("kernels.fused_cp_comm", self.fused_cp_comm)
 
 
 @dataclass(frozen=True, slots=True)

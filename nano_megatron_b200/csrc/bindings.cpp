@@ -53,7 +53,7 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
                 c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
                 int64_t head_dim, int64_t rope_cols, int64_t pos_div, int64_t rank,
                 int64_t flags_ptr, int64_t epoch_ptr, at::Tensor status,
-                c10::optional<at::Tensor> rope_cs);
+                c10::optional<at::Tensor> rope_cs, c10::optional<at::Tensor> gather_ready);
 void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
                 std::vector<int64_t> staging_ptrs, std::vector<int64_t> staging_ptrs_odd,
                 int64_t rows_per_rank, int64_t n_out, int64_t rank, int64_t epoch_ptr,
@@ -66,6 +66,16 @@ void ag_publish(at::Tensor x, int64_t even_ptr, int64_t odd_ptr, int64_t epoch_p
 void rs_reduce(int64_t staging_even, int64_t staging_odd, int64_t tp, at::Tensor out,
                c10::optional<at::Tensor> residual, int64_t flags_ptr, int64_t epoch_ptr,
                at::Tensor status);
+int64_t replica_reduce_blocks(int64_t len, int64_t device);
+void replica_reduce(std::vector<int64_t> grad_ptrs, int64_t self, int64_t off, int64_t len,
+                    at::Tensor segments, at::Tensor partials, int64_t flags_ptr,
+                    int64_t epoch_ptr, at::Tensor status);
+void replica_adamw_gather(std::vector<int64_t> grad_ptrs, std::vector<int64_t> param_ptrs,
+                          int64_t self, int64_t off, int64_t len, at::Tensor master,
+                          at::Tensor exp_avg, at::Tensor exp_avg_sq, double lr, double beta1,
+                          double beta2, double eps, double wd, int64_t step,
+                          c10::optional<at::Tensor> grad_scale, c10::optional<at::Tensor> lr_t);
+void replica_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, at::Tensor status);
 void scale_inplace(at::Tensor x, double s);
 void dropout_apply(at::Tensor x, at::Tensor y, double p, int64_t seed);
 
@@ -105,7 +115,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("aux"), py::arg("swiglu_up_row"), py::arg("positions"), py::arg("inv_freq"),
         py::arg("head_dim"), py::arg("rope_cols"), py::arg("pos_div"), py::arg("rank"),
         py::arg("flags_ptr"), py::arg("epoch_ptr"), py::arg("status"),
-        py::arg("rope_cs") = py::none());
+        py::arg("rope_cs") = py::none(), py::arg("gather_ready") = py::none());
   m.def("gemm_tc_rs", &gemm_tc_rs, "GEMM->RS: partial tiles stored into the owner's staging");
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
@@ -113,6 +123,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_signal", &peer_signal);
   m.def("ag_publish", &ag_publish);
   m.def("rs_reduce", &rs_reduce);
+  m.def("replica_reduce_blocks", &replica_reduce_blocks);
+  m.def("replica_reduce", &replica_reduce,
+        "DP: sum this rank's shard over all replicas' gradient buffers (peer loads) in place, "
+        "with per-block partial squared norms");
+  m.def("replica_adamw_gather", &replica_adamw_gather,
+        "DP: AdamW over this rank's shard, bf16 result stored into every replica's parameters");
+  m.def("replica_wait", &replica_wait, "DP: bounded wait for every replica's flag");
   m.def("launch_count", []() { return nmb::launch_counter().load(); },
         "number of kernel launches issued by this library so far (graph replays included)");
   m.def("record_graph_launches", [](int64_t n) { nmb::launch_counter() += n; },

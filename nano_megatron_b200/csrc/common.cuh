@@ -51,6 +51,8 @@ enum StatusCode : int {
   kStatusAttnTimeout = 0x201,
   kStatusPeerFlagTimeout = 0x301,
   kStatusPeerBarrierTimeout = 0x302,
+  kStatusReplicaFlagTimeout = 0x401,
+  kStatusCpFlagTimeout = 0x501,
 };
 
 // Wall-clock budget for any single wait, in nanoseconds (2 s). Pipeline waits
@@ -59,6 +61,11 @@ constexpr unsigned long long kWaitBudgetNs = 2000000000ull;
 // Budget for waits on another GPU's flag (1 s): shorter than the in-kernel pipeline
 // waits, so when a peer is missing the peer wait is the one that reports.
 constexpr unsigned long long kPeerWaitBudgetNs = 1000000000ull;
+// Iteration caps: a second, clock-independent bound on every spin loop. Each is well
+// above what the wall-clock budget allows (a try_wait or an NVLink load takes tens of ns
+// or more per round), so in practice the time budget trips first.
+constexpr uint32_t kMbarMaxIters = 1u << 28;
+constexpr uint32_t kPeerMaxIters = 1u << 25;
 
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
   unsigned long long t;
@@ -132,7 +139,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* s
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 0u) {
       if (abort_flag != nullptr && *abort_flag) return false;
-      if (globaltimer_ns() - start > kWaitBudgetNs) {
+      if (globaltimer_ns() - start > kWaitBudgetNs || it >= kMbarMaxIters) {
         record_status(status, code);
         if (abort_flag != nullptr) *abort_flag = 1;
         return false;
@@ -172,6 +179,11 @@ __device__ __forceinline__ void tma_store_commit() {
 }
 
 // Wait until every committed bulk store has finished *reading* its shared-memory source.
+// Wait until every committed bulk store of this thread has been performed (written).
+__device__ __forceinline__ void tma_store_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
 __device__ __forceinline__ void tma_store_wait_read() {
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
 }
@@ -197,6 +209,17 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
 
 __device__ __forceinline__ void fence_sc_sys() { asm volatile("fence.sc.sys;" ::: "memory"); }
 
+// Device-scope flag pair (producer and consumer on this GPU, e.g. two CTAs of one kernel).
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Bounded wait until *flag has reached `epoch` (wrap-safe compare). Returns false after
 // recording `code` when the budget runs out or another role aborted.
 __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch, int* status,
@@ -207,7 +230,7 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch, 
     if (static_cast<int32_t>(ld_acquire_sys(flag) - epoch) >= 0) return true;
     if ((it & 63u) == 0u) {
       if (abort_flag != nullptr && *abort_flag) return false;
-      if (globaltimer_ns() - start > kPeerWaitBudgetNs) {
+      if (globaltimer_ns() - start > kPeerWaitBudgetNs || it >= kPeerMaxIters) {
         record_status(status, code);
         if (abort_flag != nullptr) *abort_flag = 1;
         return false;

@@ -35,9 +35,17 @@
 // rank r's [comm_rows, K] shard living in r's symmetric buffer. The producer
 // TMA-loads each tile from its owner's shard (a peer pointer mapped into this
 // process; plain TMA, no multicast) after a bounded wait on the owner's "shard
-// ready" flag, starting with this rank's own rows. For n-tile 0 the MMA warp also
-// TMA-stores the staged A tile into a local [M, K] buffer, materialising the
-// gathered input that the backward pass needs without a separate all-gather.
+// ready" flag. For n-tile 0 the MMA warp also TMA-stores the staged A tile into a
+// local [M, K] buffer (materialising the gathered input the backward pass needs without
+// a separate all-gather) and, once those stores are written, publishes a per-m-tile flag.
+// Tiles are ordered so every remote row crosses NVLink once: first n-tile 0 of the
+// peers' m-tiles, then all tiles of this rank's own rows, then the remaining n-tiles of
+// the peers' rows, which read A from the local copy (a brief poll of the m-tile flag;
+// a tile that finds it unset reads from the peer instead, so no new wait is introduced).
+//
+// The peer epilogue stages each 32 x 64 bf16 block of a warp in shared memory and writes
+// it to the owner as 128-byte row segments (8 lanes per row), not as one 16-byte piece
+// per row and lane: full-line writes over NVLink.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -81,6 +89,7 @@ struct GemmParams {
   __nv_bfloat16* peer_out[2][kMaxTP];   // peer epilogue: [parity][rank] staging bases
   int splits;                           // split-K factor (kEpiF32Acc with beta = 1 only)
   const float2* rope_cs;                // kEpiRoPE: (cos, sin) table [seq_len][head_dim / 2]
+  uint32_t* gather_ready;               // gather: per m-tile "rows staged in xfull" = epoch
 };
 
 // Per-rank tensor maps of the gathered A operand and of the local gathered copy.
@@ -106,6 +115,18 @@ struct GemmCfg {
   static constexpr int kTmemCols = 2 * BN;  // double-buffered accumulator
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
+
+// Peer epilogue staging: per epilogue warp 32 rows x 64 bf16 (+16 B pad per row, so the
+// row-wise writes and the segment-wise reads are both free of bank conflicts).
+constexpr int kPeerRowBytes = 64 * 2 + 16;
+constexpr int kPeerStageBytes = 4 * 32 * kPeerRowBytes;
+// How long a gather tile polls for the local copy of its rows before reading the peer.
+constexpr unsigned long long kLocalCopyPollNs = 20000ull;
+
+template <int BN, int EPI>
+constexpr int gemm_smem_bytes() {
+  return GemmCfg<BN>::kSmemBytes + (EPI == kEpiPeer ? kPeerStageBytes : 0);
+}
 
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 
@@ -135,13 +156,46 @@ __device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, int col, in
 template <bool GATHER>
 __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& m0, int& nt,
                                             int& ks) {
+  if constexpr (GATHER) {
+    // remote m-tiles x n-tile 0 | own m-tiles x all n-tiles | remote m-tiles x n-tiles >= 1
+    const int own = p.comm_rows / kBM;
+    const int rem = p.num_m_tiles - own;
+    const int own0 = p.comm_rank * own;
+    ks = 0;
+    if (t < rem) {
+      m0 = ((own0 + own + t) % p.num_m_tiles) * kBM;
+      nt = 0;
+      return;
+    }
+    t -= rem;
+    if (t < own * p.num_n_tiles) {
+      m0 = (own0 + t % own) * kBM;
+      nt = t / own;
+      return;
+    }
+    t -= own * p.num_n_tiles;
+    m0 = ((own0 + own + t % rem) % p.num_m_tiles) * kBM;
+    nt = 1 + t / rem;
+    return;
+  }
   const int per_split = p.num_m_tiles * p.num_n_tiles;
   ks = t / per_split;
   t -= ks * per_split;
-  int mt = t % p.num_m_tiles;
-  if constexpr (GATHER) mt = (mt + p.m_rotate) % p.num_m_tiles;
+  const int mt = t % p.num_m_tiles;
   m0 = mt * kBM;
   nt = t / p.num_m_tiles;
+}
+
+// Brief, bounded poll of a gather m-tile's local-copy flag; false = not there (yet).
+__device__ __forceinline__ bool poll_local_copy(const uint32_t* flag, uint32_t epoch) {
+  if (ld_acquire_gpu(flag) == epoch) return true;
+  const unsigned long long start = globaltimer_ns();
+  for (uint32_t it = 0; it < 4096u; ++it) {
+    __nanosleep(32);
+    if (ld_acquire_gpu(flag) == epoch) return true;
+    if (globaltimer_ns() - start > kLocalCopyPollNs) break;
+  }
+  return false;
 }
 
 __device__ __forceinline__ void split_range(const GemmParams& p, int num_kb, int ks, int& kb0,
@@ -176,6 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty_bar = tfull_bar + 2;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* peer_stage = smem + S * Cfg::kStageBytes + 256;   // kEpiPeer only
 
   const int warp = threadIdx.x / 32;
   const int num_tiles = p.num_m_tiles * p.num_n_tiles * p.splits;
@@ -219,9 +274,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         tile_coords<GATHER>(t, p, m0, nt, ks);
         split_range(p, num_kb, ks, kb0, kb1);
         int owner = 0;
+        bool from_local = false;
         if constexpr (GATHER) {
           owner = m0 / p.comm_rows;
-          if (!((ready >> owner) & 1u)) {
+          if (owner != p.comm_rank && nt > 0 && p.store_gathered && p.gather_ready != nullptr) {
+            from_local = poll_local_copy(p.gather_ready + m0 / kBM, epoch);
+            if (from_local) fence_proxy_async_global();
+          }
+          if (!from_local && !((ready >> owner) & 1u)) {
             if (!wait_flag(p.flags + owner, epoch, p.status, kStatusPeerFlagTimeout,
                            abort_flag)) {
               ok = false;
@@ -242,7 +302,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint8_t* sb = smem_b + stage * Cfg::kBBytes;
           const int k0 = kb * kBK;
           if constexpr (GATHER) {
-            tma_load_2d(sa, &cm.a[par][owner], &full_bar[stage], k0, m0 - owner * p.comm_rows);
+            if (from_local)
+              tma_load_2d(sa, &cm.xfull, &full_bar[stage], k0, m0);
+            else
+              tma_load_2d(sa, &cm.a[par][owner], &full_bar[stage], k0, m0 - owner * p.comm_rows);
           } else if constexpr (!A_MN) {
             tma_load_2d(sa, &tmA, &full_bar[stage], k0, m0);
           } else {
@@ -275,6 +338,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
+      uint32_t gepoch = 0;
+      if constexpr (GATHER) gepoch = *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr);
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
@@ -323,6 +388,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (!ok) break;
         umma_commit(&tfull_bar[acc]);
+        if (store_a && p.gather_ready != nullptr) {
+          // the tile's rows are in xfull once the bulk stores are written: publish them
+          tma_store_wait_all();
+          fence_proxy_async_global();
+          st_release_gpu(p.gather_ready + m0 / kBM, gepoch);
+        }
       }
     }
   } else {
@@ -349,7 +420,51 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
 
-      if constexpr (EPI == kEpiBF16 || EPI == kEpiF32Acc || EPI == kEpiPeer) {
+      if constexpr (EPI == kEpiPeer) {
+        // every row of a 128-row tile has the same owner (rows per rank % 128 == 0)
+        const int owner = m0 / p.comm_rows;
+        __nv_bfloat16* base = p.peer_out[out_par][owner] +
+                              static_cast<int64_t>(p.comm_rank * p.comm_rows - owner * p.comm_rows) *
+                                  p.ldc;
+        uint8_t* wst = peer_stage + quarter * 32 * kPeerRowBytes;
+        const int n0 = nt * BN;
+#pragma unroll 1
+        for (int c2 = 0; c2 < BN / 64; ++c2) {
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(tbase + (2 * c2 + h) * 32, r);
+            tmem_wait_ld();
+            uint4* d = reinterpret_cast<uint4*>(wst + lane * kPeerRowBytes + h * 64);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint4 w;
+              w.x = pack_bf16x2(__uint_as_float(r[8 * q + 0]) * alpha,
+                                __uint_as_float(r[8 * q + 1]) * alpha);
+              w.y = pack_bf16x2(__uint_as_float(r[8 * q + 2]) * alpha,
+                                __uint_as_float(r[8 * q + 3]) * alpha);
+              w.z = pack_bf16x2(__uint_as_float(r[8 * q + 4]) * alpha,
+                                __uint_as_float(r[8 * q + 5]) * alpha);
+              w.w = pack_bf16x2(__uint_as_float(r[8 * q + 6]) * alpha,
+                                __uint_as_float(r[8 * q + 7]) * alpha);
+              d[q] = w;
+            }
+          }
+          __syncwarp();
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const int rr = i * 4 + (lane >> 3);
+            const int grow = m0 + quarter * 32 + rr;
+            const int gcol = n0 + c2 * 64 + (lane & 7) * 8;
+            if (grow < p.M && gcol < p.N) {
+              const uint4 v = *reinterpret_cast<const uint4*>(wst + rr * kPeerRowBytes +
+                                                              (lane & 7) * 16);
+              *reinterpret_cast<uint4*>(base + static_cast<int64_t>(grow) * p.ldc + gcol) = v;
+            }
+          }
+          __syncwarp();
+        }
+      } else if constexpr (EPI == kEpiBF16 || EPI == kEpiF32Acc) {
         const int n0 = nt * BN;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
@@ -361,15 +476,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           float v[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
-          if constexpr (EPI == kEpiPeer) {
-            const int owner = row / p.comm_rows;
-            __nv_bfloat16* dst =
-                p.peer_out[out_par][owner] +
-                static_cast<int64_t>(p.comm_rank * p.comm_rows + row - owner * p.comm_rows) *
-                    p.ldc +
-                col;
-            store_row32_bf16(dst, col, p.N, v);
-          } else if constexpr (EPI == kEpiBF16) {
+          if constexpr (EPI == kEpiBF16) {
             if (p.R != nullptr) {
               const __nv_bfloat16* rr = p.R + static_cast<int64_t>(row) * p.ldr + col;
 #pragma unroll
@@ -556,19 +663,20 @@ static int num_sms() {
 template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER = false>
 static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
                    cudaStream_t stream, int max_ctas, const CommMaps* cmp = nullptr) {
-  using Cfg = GemmCfg<BN>;
+  constexpr int smem_bytes = gemm_smem_bytes<BN, EPI>();
+  static_assert(smem_bytes <= 227 * 1024, "GEMM shared memory exceeds the per-CTA limit");
   auto kern = gemm_tcgen05_kernel<BN, A_MN, B_MN, EPI, GATHER>;
   static CommMaps empty_maps{};
   const CommMaps& cm = cmp != nullptr ? *cmp : empty_maps;
   static bool attr_set = false;
   if (!attr_set) {
     C10_CUDA_CHECK(
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::kSmemBytes));
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes));
     attr_set = true;
   }
   const int tiles = p.num_m_tiles * p.num_n_tiles * p.splits;
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
-  kern<<<grid, kThreads, Cfg::kSmemBytes, stream>>>(ta, tb, cm, p); NMB_LAUNCHED(1);
+  kern<<<grid, kThreads, smem_bytes, stream>>>(ta, tb, cm, p); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -749,7 +857,7 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
                 c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
                 int64_t head_dim, int64_t rope_cols, int64_t pos_div, int64_t rank,
                 int64_t flags_ptr, int64_t epoch_ptr, at::Tensor status,
-                c10::optional<at::Tensor> rope_cs) {
+                c10::optional<at::Tensor> rope_cs, c10::optional<at::Tensor> gather_ready) {
   check_operand(a_local, "A shard");
   check_operand(b, "B");
   const int tp = static_cast<int>(shard_ptrs.size());
@@ -822,6 +930,12 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
     TORCH_CHECK(xfull->size(0) == M && xfull->size(1) == K);
     cm.xfull = make_tmap_2d(xfull->data_ptr(), M, K, xfull->stride(0), kBM);
     p.store_gathered = 1;
+    if (gather_ready.has_value()) {
+      TORCH_CHECK(gather_ready->is_cuda() && gather_ready->scalar_type() == at::kInt &&
+                      gather_ready->is_contiguous() && gather_ready->numel() >= M / kBM,
+                  "gemm_tc_ag: gather_ready must hold one int32 per 128-row tile");
+      p.gather_ready = reinterpret_cast<uint32_t*>(gather_ready->data_ptr<int>());
+    }
   }
   const int64_t b_rows = b_mn ? b.size(1) : b.size(0);
   CUtensorMap tb = b_mn ? make_tmap_2d(b.data_ptr(), K, b_rows, b.stride(0), kBK)
@@ -855,6 +969,7 @@ void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
   const int64_t K = a_mn ? a.size(0) : a.size(1);
   TORCH_CHECK(K == (b_mn ? b.size(0) : b.size(1)), "gemm_tc_rs: K mismatch");
   TORCH_CHECK(M == rows_per_rank * tp, "gemm_tc_rs: M must equal tp * rows_per_rank");
+  TORCH_CHECK(rows_per_rank % kBM == 0, "gemm_tc_rs: rows per rank must be a multiple of 128");
   TORCH_CHECK((n_out * 2) % 16 == 0, "gemm_tc_rs: N must be a multiple of 8");
   TORCH_CHECK(staging_ptrs_odd.size() == staging_ptrs.size());
   for (auto ptr : staging_ptrs) TORCH_CHECK(ptr % 16 == 0, "staging must be 16-byte aligned");

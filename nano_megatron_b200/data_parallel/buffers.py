@@ -88,9 +88,11 @@ class FlatBuffers:
 
     def __init__(self, named_params: list[tuple[str, nn.Parameter]], *, domains, parallel,
                  bucket_bytes: int, param_dtype: torch.dtype, grad_dtype: torch.dtype,
-                 device: torch.device, unit_key=None) -> None:
+                 device: torch.device, unit_key=None, allocate=None) -> None:
         """``unit_key(name)``: optional; a new bucket also starts whenever it changes, so
-        buckets never straddle two sharding units (ZeRO-3 gathers one unit at a time)."""
+        buckets never straddle two sharding units (ZeRO-3 gathers one unit at a time).
+        ``allocate(numel, param_dtype, grad_dtype) -> (param_flat, grad_flat)``: optional
+        zeroed storage (e.g. peer-mapped memory); default fresh device tensors."""
         self.param_dtype = param_dtype
         self.grad_dtype = grad_dtype
         self.device = device
@@ -136,8 +138,11 @@ class FlatBuffers:
             self.buckets.append(bucket)
             total += padded
         self.numel = total
-        self.param_flat = torch.zeros(total, dtype=param_dtype, device=device)
-        self.grad_flat = torch.zeros(total, dtype=grad_dtype, device=device)
+        if allocate is not None:
+            self.param_flat, self.grad_flat = allocate(total, param_dtype, grad_dtype)
+        else:
+            self.param_flat = torch.zeros(total, dtype=param_dtype, device=device)
+            self.grad_flat = torch.zeros(total, dtype=grad_dtype, device=device)
         for b in self.buckets:
             b.param_data = self.param_flat[b.offset:b.offset + b.storage_numel]
             b.grad_data = self.grad_flat[b.offset:b.offset + b.storage_numel]

@@ -52,6 +52,10 @@ class DataParallelStrategy:
     # True when forward/backward of a microbatch issues no collective and no host sync, so
     # it can be captured in a CUDA graph (gradients are reduced in finalize_gradients).
     graph_safe_microbatches = False
+    # kernels.fused_dp_comm: reduce / update / gather over NVLink peer memory when the
+    # replica group allows it (see replica_comm.fused_replica_supported)
+    fused_replica_enabled = False
+    replica = None
 
     def __init__(self, *, config=None, offload=None, parallel=None, parameter_domains=None) -> None:
         self.config = config
@@ -75,6 +79,9 @@ class DataParallelStrategy:
         self._comm_stream = None
 
     # ------------------------------------------------------------------ contract
+    def configure_kernels(self, kernels) -> None:
+        self.fused_replica_enabled = bool(getattr(kernels, "fused_dp_comm", True))
+
     def configure_precision(self, precision) -> None:
         self.param_dtype = _torch_dtype(precision.params)
         self.compute_dtype = _torch_dtype(precision.compute)
@@ -121,14 +128,32 @@ class DataParallelStrategy:
         self._broadcast_from_replica_root(named)
         bucket_bytes = int(getattr(self.config, "bucket_bytes", 256 * 1024 * 1024))
         grad_dtype = torch.float64 if model_dtype == torch.float64 else torch.float32
+        from .replica_comm import ReplicaComm, fused_replica_supported
+
+        allocate = None
+        self.replica = None
+        if fused_replica_supported(self, device)[0]:
+            def allocate(total, pdt, gdt):
+                self.replica = ReplicaComm.create(self.replica_group, total, pdt, gdt, device)
+                return self.replica.flat_tensors(total, pdt, gdt)
         self.buffers = FlatBuffers(named, domains=self.parameter_domains, parallel=self.parallel,
                                    bucket_bytes=bucket_bytes, param_dtype=model_dtype,
                                    grad_dtype=grad_dtype, device=device,
-                                   unit_key=self._bucket_unit_key())
+                                   unit_key=self._bucket_unit_key(), allocate=allocate)
+        if self.replica is not None and any(b.group is not self.replica_group and
+                                            getattr(b.group, "ranks", None) !=
+                                            self.replica_group.ranks
+                                            for b in self.buffers.buckets):
+            raise RuntimeError("fused replica path needs every bucket on the dense replica "
+                               "group")
         self._named = named
         self._ranges = norm_ranges(self.buffers, self.parallel)
         self._sp_slices = [(b, s) for b, s in self.buffers.slices() if s.sequence_parallel_grad]
         self._init_optimizer_state()
+        if self.replica is not None:
+            from .common import counts_toward_norm
+
+            self.replica.prepare(self.buffers, lambda s: counts_toward_norm(s, self.parallel))
         self._lr = float(getattr(optimizer_config, "lr", 3e-4))
         self._lr_t = torch.tensor([self._lr], dtype=torch.float32, device=device)
         self._model = model
@@ -195,6 +220,8 @@ class DataParallelStrategy:
             off += n
 
     def finalize_gradients(self) -> None:
+        if self.replica is not None:
+            return self._fused_finalize()
         # Overlapped bucket reductions finish first: the sequence-parallel norm-gradient
         # sum over TP below rewrites some of the same gradient memory (the two sums commute).
         early = self._wait_inflight()
@@ -305,6 +332,8 @@ class DataParallelStrategy:
 
     def clip_grad_norm(self, max_norm: float | None) -> torch.Tensor:
         """Global gradient norm of the *averaged* gradients (device tensor)."""
+        if self.replica is not None:
+            return self._fused_clip(max_norm)
         flat, ranges = self._grad_view_for_norm()
         sq = local_sumsq(flat, ranges).reshape(1).to(torch.float32)
         sq = self._reduce_norm_over_shards(sq)
@@ -316,6 +345,57 @@ class DataParallelStrategy:
 
     def _reduce_norm_over_shards(self, sq):
         return sq
+
+    # ------------------------------------------------------------------ fused replica path
+    def _fused_finalize(self) -> None:
+        """signal(GRAD), then every bucket's shard summed over the replicas in place, with
+        partial squared norms (replica_comm / csrc/dp_comm.cu)."""
+        from .replica_comm import CH_GRAD
+
+        self._reduce_sequence_parallel_grads()
+        self.replica.signal(CH_GRAD)
+        self._replica_partials = [(b, self.replica.reduce(b, lambda x: x.offset))
+                                  for b in self.buffers.buckets]
+        self._reduced = True
+
+    def _fused_clip(self, max_norm):
+        from .common import dense_counted_here, is_dense
+
+        dev = self.buffers.device
+        dense = [p for b, p in self._replica_partials if is_dense(b)]
+        expert = [p for b, p in self._replica_partials if not is_dense(b)]
+        parts = [torch.cat(x).sum().reshape(1) if x else torch.zeros(1, device=dev)
+                 for x in (dense, expert)]
+        sq = torch.cat(parts)
+        dist.all_reduce(sq, group=self.replica_group.process_group)
+        if not dense_counted_here(self.parallel):
+            sq[0] = 0.0          # the EP replicas of the dense parameters count once
+        sq = reduce_model_parallel(sq.sum().reshape(1), self.parallel)
+        norm = sq.sqrt() / self.replica_size
+        coef = clip_coefficient(norm, max_norm)
+        self._grad_scale = (coef / self.replica_size).reshape(1).to(torch.float32)
+        return norm.reshape(())
+
+    def _fused_optimizer_step(self) -> None:
+        """AdamW over this rank's shard of every bucket with the bf16 result stored into
+        every replica's parameters, then a bounded wait until all replicas have done so."""
+        from .replica_comm import CH_PARAM
+
+        if not self._reduced:
+            self.finalize_gradients()
+        self.step_count += 1
+        b1, b2, eps, wd = self._opt_hparams()
+        scale = self._scale()
+        for b in self.buffers.buckets:
+            master, m, v = self._shard_state(b)
+            self.replica.adamw_gather(b, lambda x: x.offset, master, m, v, lr=self._lr,
+                                      betas=(b1, b2), eps=eps, wd=wd, step=self.step_count,
+                                      grad_scale=scale, lr_t=self._lr_t)
+        self.replica.signal(CH_PARAM)
+        self.replica.wait(CH_PARAM)
+
+    def _shard_state(self, b):
+        raise NotImplementedError
 
     # ------------------------------------------------------------------ optimizer
     def _opt_hparams(self):
@@ -363,12 +443,29 @@ class DDPStrategy(DataParallelStrategy):
 
     def setup(self, model, optimizer_config, parameter_domains=None):
         super().setup(model, optimizer_config, parameter_domains)
-        if self._overlap_active():
+        if self._overlap_active() and self.replica is None:
             self._register_overlap_hooks(model)
         return model
 
     def eager_last_microbatch(self) -> bool:
-        return self._overlap_active()
+        return self._overlap_active() and self.replica is None
+
+    def _shard_state(self, b):
+        lo = b.offset + b.rank * b.shard_numel
+        hi = lo + b.shard_numel
+        return self.master[lo:hi], self.exp_avg[lo:hi], self.exp_avg_sq[lo:hi]
+
+    def gather_replicated_state(self) -> None:
+        """Fused replica path: each rank updated only its own shards of the fp32 master and
+        moments; copy every shard from its owner so the full state is current here."""
+        if self.replica is None:
+            return
+        g = self.replica_group
+        for b in self.buffers.buckets:
+            for t in (self.master, self.exp_avg, self.exp_avg_sq):
+                full = t[b.offset:b.offset + b.padded_numel]
+                mine = full[b.rank * b.shard_numel:(b.rank + 1) * b.shard_numel].clone()
+                dist.all_gather_into_tensor(full, mine, group=g.process_group)
 
     def _init_optimizer_state(self) -> None:
         buf = self.buffers
@@ -380,6 +477,8 @@ class DDPStrategy(DataParallelStrategy):
         self.exp_avg_sq = torch.zeros_like(self.master)
 
     def optimizer_step(self) -> None:
+        if self.replica is not None:
+            return self._fused_optimizer_step()
         if not self._reduced:
             self.finalize_gradients()
         self.step_count += 1
@@ -393,6 +492,7 @@ class DDPStrategy(DataParallelStrategy):
 
     def state_dict(self) -> dict:
         """torch.optim.AdamW-shaped state (one entry per unique parameter) + fp32 masters."""
+        self.gather_replicated_state()
         b1, b2, eps, wd = self._opt_hparams()
         state, ids = {}, []
         for i, (b, s) in enumerate(self.buffers.slices()):
@@ -494,7 +594,13 @@ class FlatShardZeROStrategy(DataParallelStrategy):
         # squared norm over this rank's shard of each bucket (counting rule per slice)
         return None, None
 
+    def _shard_state(self, b):
+        sh = self.shards[b.index]
+        return sh["master"], sh["exp_avg"], sh["exp_avg_sq"]
+
     def clip_grad_norm(self, max_norm: float | None) -> torch.Tensor:
+        if self.replica is not None:
+            return self._fused_clip(max_norm)
         dev = self.buffers.device
         sq = torch.zeros(2, dtype=torch.float32, device=dev)   # [dense, expert] shard sums
         from .common import counts_toward_norm, dense_counted_here, is_dense
@@ -520,6 +626,8 @@ class FlatShardZeROStrategy(DataParallelStrategy):
         return norm.reshape(())
 
     def optimizer_step(self) -> None:
+        if self.replica is not None:
+            return self._fused_optimizer_step()
         if not self._reduced:
             self.finalize_gradients()
         self.step_count += 1

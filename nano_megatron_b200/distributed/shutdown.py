@@ -67,10 +67,25 @@ def _detach_workspace(model, workspace) -> None:
             m.tp_workspace = None
 
 
+def _group_barrier(group, device) -> None:
+    import torch.distributed as dist
+
+    if group is None or getattr(group, "size", 1) <= 1 or not dist.is_initialized():
+        return
+    pg = getattr(group, "process_group", None)
+    if device is not None and getattr(device, "type", None) == "cuda":
+        dist.barrier(group=pg, device_ids=[device.index])
+    else:
+        dist.barrier(group=pg)
+
+
 def shutdown(*, trainer=None, model=None, workspace=None, parallel=None, runtime=None,
-             device=None, record: Callable[[str], Any] | None = None) -> None:
+             device=None, heaps=(), record: Callable[[str], Any] | None = None) -> None:
     """Release everything in the documented order; see the module docstring.
 
+    ``heaps``: further peer-mapped allocations as (heap, group) pairs (e.g. the
+    data-parallel replica buffers); each is unmapped after a barrier over its group and
+    freed after a second one, like the TP workspace.
     ``record`` (optional) is called with each step name as it runs, for tests.
     """
     if model is None and trainer is not None:
@@ -97,6 +112,14 @@ def shutdown(*, trainer=None, model=None, workspace=None, parallel=None, runtime
         step("tp_barrier_before_free", lambda: _tp_barrier(parallel, device))
         step("free_own_buffer", lambda: (_detach_workspace(model, workspace),
                                          workspace.release()))
+    for heap, group in heaps:
+        if heap is None:
+            continue
+        step("tp_barrier_before_unmap", lambda g=group: _group_barrier(g, device))
+        step("unmap_peers", heap.close)
+        step("synchronize", lambda: _synchronize(device))
+        step("tp_barrier_before_free", lambda g=group: _group_barrier(g, device))
+        step("free_own_buffer", heap.release)
     if parallel is not None:
         step("close_subgroups", parallel.close)
     if runtime is not None:

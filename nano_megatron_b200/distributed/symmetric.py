@@ -29,6 +29,7 @@ import torch.distributed as dist
 FLAG_BYTES = 4096
 MAX_TP = 8
 CH_RS, CH_AG, CH_AG_BWD = 0, 1, 2
+GATHER_READY_TILES = 4096          # 128-row tiles of a gathered operand (512K rows)
 
 
 class SymmetricWorkspace:
@@ -41,6 +42,10 @@ class SymmetricWorkspace:
         self.rs_bytes, self.ag_bytes = rs_bytes, ag_bytes
         self._opened = opened         # peer mappings to close
         self.epochs = torch.zeros(16, dtype=torch.int32, device=device)  # device counters
+        # per channel and 128-row tile: epoch at which the gathered rows sit in the local
+        # copy (written and read by the AG->GEMM kernel on this GPU only)
+        self.gather_ready = torch.zeros(16, GATHER_READY_TILES, dtype=torch.int32,
+                                        device=device)
         from nano_megatron_b200.ops._ext import status_word
 
         self.status = status_word(device)
@@ -137,3 +142,100 @@ class SymmetricWorkspace:
 
 def _align(n: int, a: int = 1 << 21) -> int:
     return max(a, (int(n) + a - 1) // a * a)
+
+
+class SymmetricHeap:
+    """One IPC-exported device allocation per rank of a group, mapped by every peer and cut
+    into named regions at identical offsets on every rank (16-byte aligned). Used by the
+    data-parallel replica path for the flat gradient / parameter buffers and their flags.
+
+    ``ptr(rank, name)`` is the device address of ``name`` in ``rank``'s allocation as seen
+    from this process; ``local(name, dtype)`` is a tensor view of this rank's region. The
+    epoch counters (one per flag channel) are local device memory. Teardown is
+    ``close()`` (unmap peers; after a barrier) then ``release()`` (free; after another)."""
+
+    def __init__(self, *, rank: int, size: int, ptrs: list[int], owner, device,
+                 offsets: dict[str, tuple[int, int]], opened: list[int]) -> None:
+        self.rank, self.size = rank, size
+        self.ptrs, self.owner, self.device = ptrs, owner, device
+        self.offsets = offsets
+        self._opened = opened
+        self.epochs = torch.zeros(16, dtype=torch.int32, device=device)
+        from nano_megatron_b200.ops._ext import status_word
+
+        self.status = status_word(device)
+
+    @staticmethod
+    def layout(regions: dict[str, int]) -> tuple[dict[str, tuple[int, int]], int]:
+        offsets, cur = {}, 0
+        for name, nbytes in regions.items():
+            offsets[name] = (cur, int(nbytes))
+            cur += -(-int(nbytes) // 256) * 256
+        return offsets, max(cur, 256)
+
+    @classmethod
+    def create(cls, group, regions: dict[str, int], device) -> "SymmetricHeap":
+        """Collective over ``group`` (rank, size, process_group)."""
+        from nano_megatron_b200.ops._ext import lib
+
+        if group.size > MAX_TP:
+            raise ValueError(f"symmetric heap supports at most {MAX_TP} ranks")
+        offsets, total = cls.layout(regions)
+        dev = torch.device(device)
+        buf, handle = lib().symm_alloc(total, dev.index)
+        handles: list = [None] * group.size
+        dist.all_gather_object(handles, bytes(handle), group=group.process_group)
+        ptrs, opened = [], []
+        for r, h in enumerate(handles):
+            if r == group.rank:
+                ptrs.append(buf.data_ptr())
+            else:
+                p = lib().symm_open(h, dev.index)
+                opened.append(p)
+                ptrs.append(p)
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=group.process_group, device_ids=[dev.index])
+        return cls(rank=group.rank, size=group.size, ptrs=ptrs, owner=buf, device=dev,
+                   offsets=offsets, opened=opened)
+
+    @classmethod
+    def emulated(cls, size: int, regions: dict[str, int], device) -> list["SymmetricHeap"]:
+        """``size`` heaps in one process on one GPU (every "peer" is local memory)."""
+        offsets, total = cls.layout(regions)
+        dev = torch.device(device)
+        bufs = [torch.zeros(total, dtype=torch.uint8, device=dev) for _ in range(size)]
+        ptrs = [b.data_ptr() for b in bufs]
+        return [cls(rank=r, size=size, ptrs=ptrs, owner=bufs[r], device=dev, offsets=offsets,
+                    opened=[]) for r in range(size)]
+
+    def ptr(self, rank: int, name: str) -> int:
+        return self.ptrs[rank] + self.offsets[name][0]
+
+    def local(self, name: str, dtype: torch.dtype) -> torch.Tensor:
+        off, nbytes = self.offsets[name]
+        return self.owner[off:off + nbytes].view(dtype)
+
+    def epoch_ptr(self, channel: int) -> int:
+        return self.epochs.data_ptr() + 4 * channel
+
+    def flag_slots(self, rank: int, channel: int) -> int:
+        """Address of ``rank``'s flag array for ``channel`` (one uint32 per source rank)."""
+        return self.ptr(rank, "flags") + channel * MAX_TP * 4
+
+    def signal_targets(self, channel: int) -> list[int]:
+        return [self.flag_slots(d, channel) + self.rank * 4 for d in range(self.size)]
+
+    def close(self) -> None:
+        if not self._opened:
+            return
+        from nano_megatron_b200.ops._ext import lib
+
+        opened, self._opened = self._opened, []
+        for p in opened:
+            lib().symm_close(p, self.device.index)
+        self.ptrs = [p if r == self.rank else 0 for r, p in enumerate(self.ptrs)]
+
+    def release(self) -> None:
+        self.close()
+        self.owner = None
+        self.ptrs = []

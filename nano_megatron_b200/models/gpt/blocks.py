@@ -303,7 +303,9 @@ class MLPBlockFn(torch.autograd.Function):
         h2 = h.reshape(-1, H)
         xn, rstd = F.rmsnorm(h2, w_norm, spec.eps)
         w_gu = fused_rows([w_gate, w_up])
-        fused = spec.tp.fused(xn) and spec.ffn % 128 == 0 and b_gu is None
+        # any local FFN width with 16-byte rows: the SwiGLU epilogue predicates the last
+        # (partial) tile, e.g. 1368 = 2736 / TP2 for the 311M model
+        fused = spec.tp.fused(xn) and spec.ffn % 8 == 0 and b_gu is None
         if fused:
             gu = torch.empty(xn.shape[0] * spec.tp.size, 2 * spec.ffn, device=xn.device,
                              dtype=xn.dtype)
@@ -347,7 +349,7 @@ class MLPBlockFn(torch.autograd.Function):
             dy = ctx.dropout_fn.backward(dy)
         if b_down is not None:
             F.bias_grad(dy, main_grad_of(b_down))
-        fused = spec.tp.fused(dy) and spec.ffn % 128 == 0
+        fused = spec.tp.fused(dy) and spec.ffn % 8 == 0
         if fused:
             dmid, dyg = CG.allgather_gemm(spec.tp.workspace, dy, w_down.detach(), b_mn=True)
         else:

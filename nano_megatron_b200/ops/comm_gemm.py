@@ -79,11 +79,13 @@ def ag_finish(ws, x_local: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
         from .gemm import rope_table
 
         table = rope_table(positions, inv_freq)
+    ready = ws.gather_ready[channel] if out.shape[0] // 128 <= ws.gather_ready.shape[1] \
+        else None
     lib().gemm_tc_ag(x_local, [ws.ag_shard(r, 0) for r in range(ws.size)],
                      [ws.ag_shard(r, 1) for r in range(ws.size)], K, b, b_mn, out, EPI[epi],
                      xfull, aux, swiglu_up_row, positions, inv_freq, head_dim, rope_cols,
                      pos_div, ws.rank, ws.flags(ws.rank, channel), ws.epoch_ptr(channel),
-                     ws.status, table)
+                     ws.status, table, ready)
 
 
 def allgather_gemm(ws, x_local: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,

@@ -38,9 +38,14 @@ class TrainingComponents:
         from nano_megatron_b200.distributed.shutdown import shutdown
 
         ws, self.tp_workspace = self.tp_workspace, None
+        dp = self.data_parallel
+        replica = getattr(dp, "replica", None)
+        heaps = [(replica, dp.replica_group)] if replica is not None else []
+        if replica is not None:
+            dp.replica = None
         shutdown(trainer=trainer, model=self.model, workspace=ws, parallel=self.parallel,
                  runtime=None if keep_runtime else self.runtime,
-                 device=getattr(self.runtime, "device", None))
+                 device=getattr(self.runtime, "device", None), heaps=heaps)
 
 
 def build_model(config, parallel, rng, *, device):

@@ -134,6 +134,9 @@ class Trainer:
         self.state = TrainerState()
         self.device = device or next(model.parameters()).device
         data_parallel.configure_precision(config.precision)
+        configure_kernels = getattr(data_parallel, "configure_kernels", None)
+        if callable(configure_kernels):
+            configure_kernels(config.kernels)
         self.prepare_pipeline_stage()
         data_parallel.setup(model, config.optimizer, getattr(data_parallel, "parameter_domains",
                                                              None))

@@ -33,10 +33,12 @@ def _ok():
 
 @pytest.mark.parametrize("tp", [2, 4])
 @pytest.mark.parametrize("b_mn", [False, True])
-def test_gemm_reduce_scatter(tp, b_mn):
+@pytest.mark.parametrize("K", [512, 1368])
+def test_gemm_reduce_scatter(tp, b_mn, K):
+    """K = 1368: the down projection's reduction width at TP2 (a partial last K block)."""
     torch.manual_seed(tp)
     ws = SymmetricWorkspace.emulated(tp, rs_bytes=16 * MB, ag_bytes=8 * MB, device=DEV)
-    R, K, N = 256, 512, 384
+    R, N = 256, 384
     M = R * tp
     for it in range(3):  # exercises both parities and epoch advance
         a = [torch.randn(M, K, device=DEV).bfloat16() for _ in range(tp)]
@@ -80,9 +82,11 @@ def test_allgather_gemm_bf16_and_gathered_copy(tp):
             assert _rel(outs[r], ref) < 1e-2, (it, r)
 
 
-def test_allgather_gemm_dgrad_layout():
-    """dgrad of a row-parallel layer: A = dy (gathered), B = W stored [N_local, K] (MN-major)."""
-    tp, R, n_local, K = 2, 384, 512, 1024
+@pytest.mark.parametrize("n_local", [512, 1368])
+def test_allgather_gemm_dgrad_layout(n_local):
+    """dgrad of a row-parallel layer: A = dy (gathered), B = W stored [N_local, K] (MN-major);
+    1368 = the 311M model's local FFN width at TP2 (a partial last output tile)."""
+    tp, R, K = 2, 384, 1024
     ws = SymmetricWorkspace.emulated(tp, rs_bytes=2 * MB, ag_bytes=8 * MB, device=DEV)
     dy = [torch.randn(R, K, device=DEV).bfloat16() for _ in range(tp)]
     w = torch.randn(K, n_local, device=DEV).bfloat16()       # weight [out=K, in_local]
@@ -99,7 +103,10 @@ def test_allgather_gemm_dgrad_layout():
         assert _rel(o, ref) < 1e-2
 
 
-def test_allgather_gemm_rope_and_swiglu_match_local_kernels():
+@pytest.mark.parametrize("ffn", [768, 344, 1368])
+def test_allgather_gemm_rope_and_swiglu_match_local_kernels(ffn):
+    """``ffn`` = the local SwiGLU width; 344 and 1368 (F = 688 / 2736 at TP2) are not
+    multiples of the 128-column output tile."""
     tp, R, H, D = 2, 256, 512, 64
     hq, hkv = 8, 4
     ws = SymmetricWorkspace.emulated(tp, rs_bytes=2 * MB, ag_bytes=8 * MB, device=DEV)
@@ -119,7 +126,6 @@ def test_allgather_gemm_rope_and_swiglu_match_local_kernels():
                      head_dim=D, rope_cols=(hq + hkv) * D, pos_div=B)
         _ok()
         assert _rel(o, ref) < 1e-3
-    ffn = 768
     wgu = (torch.randn(2 * ffn, H, device=DEV) * 0.05).bfloat16()
     h_ref, gu_ref = F.swiglu_linear(xcat, wgu, ffn)
     for r in range(tp):

@@ -16,14 +16,14 @@ pytestmark = pytest.mark.gpu
 WORLD = 2
 
 
-def _cfg(fused: bool, graphs: bool = False):
+def _cfg(fused: bool, graphs: bool = False, ffn: int = 512):
     from nano_megatron_b200.config import config_from_dict
 
     return config_from_dict({
         "distributed": {"backend": "nccl", "device": "cuda", "timeout_minutes": 2},
         "parallel": {"tensor": 2, "pipeline": 1, "context": 1, "expert": 1, "data": 1,
                      "sequence_parallel": True},
-        "model": {"layers": 2, "hidden_size": 256, "ffn_hidden_size": 512, "heads": 4,
+        "model": {"layers": 2, "hidden_size": 256, "ffn_hidden_size": ffn, "heads": 4,
                   "kv_heads": 2, "seq_length": 256, "vocab_size": 512},
         "precision": {"params": "bfloat16", "compute": "bfloat16", "grad_reduce": "float32"},
         "kernels": {"backend": "b200", "fused_tp_comm": fused, "cuda_graphs": graphs},
@@ -46,8 +46,10 @@ def _worker(rank, world, port, out_dir, errq):
         batch = {"input_ids": ids[:, :-1].contiguous(), "labels": ids[:, 1:].contiguous()}
         runtime = DistributedRuntime(_cfg(True).distributed).initialize()
         results = {}
-        for fused, graphs in ((False, False), (True, False), (True, True)):
-            cfg = _cfg(fused, graphs)
+        # ffn 688: local width 344 at TP2, not a multiple of the 128-column GEMM tile
+        for fused, graphs, ffn in ((False, False, 512), (True, False, 512), (True, True, 512),
+                                   (False, False, 688), (True, True, 688)):
+            cfg = _cfg(fused, graphs, ffn)
             comps = build_training_components(cfg, runtime)
             assert (getattr(comps.model.model, "tp_workspace", None) is not None) == fused
             tr = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
@@ -63,7 +65,7 @@ def _worker(rank, world, port, out_dir, errq):
             s, c = aggregate_loss_metrics(acc, comps.parallel, runtime.device)
             grads = {n: p.main_grad.detach().float().cpu().clone()
                      for n, p in comps.model.named_parameters()}
-            results[(fused, graphs)] = (float(s / c), grads)
+            results[(fused, graphs, ffn)] = (float(s / c), grads)
             comps.close(tr, keep_runtime=True)    # graphs, peer memory, subgroups
         from nano_megatron_b200.ops._ext import check_status
 
@@ -100,8 +102,10 @@ def test_fused_tp_matches_nccl_tp(tmp_path):
     assert not alive and all(p.exitcode == 0 for p in procs)
     for r in range(WORLD):
         res = torch.load(tmp_path / f"r{r}.pt")
-        l0, g0 = res[(False, False)]
-        for key in ((True, False), (True, True)):
+        for key, base in (((True, False, 512), (False, False, 512)),
+                          ((True, True, 512), (False, False, 512)),
+                          ((True, True, 688), (False, False, 688))):
+            l0, g0 = res[base]
             l1, g1 = res[key]
             assert abs(l0 - l1) < 2e-2 * abs(l0), (key, l0, l1)
             for n in g0:

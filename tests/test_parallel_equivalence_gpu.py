@@ -53,6 +53,21 @@ def _batch():
     return {"input_ids": ids[:, :-1], "labels": ids[:, 1:]}
 
 
+def _gather_reduced_shards(dp) -> None:
+    """ZeRO-2/3 reduce-scatter: the replica-summed gradient exists only as each owner's
+    shard. Put the full sum back into every rank's ``main_grad`` (all-gather of the shards)
+    so all strategies are compared on the same quantity."""
+    import torch.distributed as dist
+
+    shards = getattr(dp, "shards", None)
+    g = dp.replica_group
+    if not shards or not getattr(dp, "reduce_scatter", False) or g is None or g.size == 1:
+        return
+    for b, sh in zip(dp.buffers.buckets, shards):
+        dist.all_gather_into_tensor(b.grad_data[:b.padded_numel], sh["grad"],
+                                    group=g.process_group)
+
+
 def _step(cfg, out_path, full_path=None):
     """One forward/backward of the global batch; saves loss and merged-ready gradients."""
     from nano_megatron_b200.distributed import DistributedRuntime
@@ -89,6 +104,7 @@ def _step(cfg, out_path, full_path=None):
     acc = tr.schedule.forward_backward(micro)
     comps.model.synchronize_tied_embedding_gradients()
     dp.finalize_gradients()
+    _gather_reduced_shards(dp)
     s, n = aggregate_loss_metrics(acc, comps.parallel, rt.device)
     grads, seen = {}, set()
     for name, p in comps.model.named_parameters():

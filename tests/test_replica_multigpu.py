@@ -1,0 +1,93 @@
+"""DDP, ZeRO-1 and ZeRO-2 on two GPUs: the fused replica path (peer-memory reduction +
+sharded AdamW + parameter all-gather, ``kernels.fused_dp_comm``) against the NCCL path.
+
+Same weights, same batches: three optimizer steps with the fused path must give the same
+per-step loss and gradient norm and the same parameters as the NCCL collectives (fp32
+reduction on both sides, so the difference is summation order only), and the DDP state
+gathered for a checkpoint must equal the NCCL run's replicated state. Child processes,
+one per GPU, NVLS off, bounded by timeouts.
+"""
+
+from __future__ import annotations
+
+import os
+
+import pytest
+import torch
+
+from dist_utils import run_gpu_ranks
+
+pytestmark = pytest.mark.gpu
+
+WORLD = 2
+
+
+def _cfg(mode: str, fused: bool):
+    from nano_megatron_b200.config import config_from_dict
+
+    return config_from_dict({
+        "distributed": {"backend": "nccl", "device": "cuda", "timeout_minutes": 2},
+        "parallel": {"data": WORLD},
+        "model": {"layers": 2, "hidden_size": 256, "ffn_hidden_size": 688, "heads": 4,
+                  "kv_heads": 2, "seq_length": 128, "vocab_size": 1000},
+        "precision": {"params": "bfloat16", "compute": "bfloat16", "grad_reduce": "float32"},
+        "kernels": {"backend": "b200", "fused_dp_comm": fused, "cuda_graphs": True},
+        "data_parallel": {"mode": mode, "bucket_bytes": 1 << 20},
+        "training": {"micro_batch_size": 2, "gradient_accumulation_steps": 2, "seed": 11},
+        "optimizer": {"lr": 1e-3, "clip_grad_norm": 0.5}})
+
+
+def _rank(rank, world, mode, out_dir):
+    from nano_megatron_b200.distributed import DistributedRuntime
+    from nano_megatron_b200.ops._ext import check_status
+    from nano_megatron_b200.training import Trainer
+    from nano_megatron_b200.training.engine import build_training_components
+
+    runtime = DistributedRuntime(_cfg(mode, True).distributed).initialize()
+    out = {}
+    for fused in (False, True):
+        cfg = _cfg(mode, fused)
+        comps = build_training_components(cfg, runtime)
+        tr = Trainer(config=cfg, model=comps.model, parallel=comps.parallel,
+                     data_parallel=comps.data_parallel, rng=comps.rng)
+        assert (comps.data_parallel.replica is not None) == fused, "fused path not taken"
+        g = torch.Generator().manual_seed(100 + rank)
+        losses, norms = [], []
+        for _ in range(3):
+            ids = torch.randint(0, 1000, (4, 129), generator=g)
+            r = tr.train_step({"input_ids": ids[:, :-1], "labels": ids[:, 1:]})
+            losses.append(float(r["loss_sum"] / r["token_count"]))
+            norms.append(float(r["grad_norm"]))
+        params = {n: p.detach().float().cpu().clone()
+                  for n, p in comps.model.named_parameters()}
+        state = comps.data_parallel.state_dict() if mode == "ddp" else None
+        check_status(runtime.device)
+        out[fused] = {"loss": losses, "norm": norms, "params": params, "state": state}
+        comps.close(tr, keep_runtime=True)
+    torch.save(out, os.path.join(out_dir, f"r{rank}.pt"))
+    runtime.close()
+
+
+@pytest.mark.parametrize("mode", ["ddp", "zero1", "zero2"])
+def test_fused_replica_matches_nccl(mode, tmp_path):
+    if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
+        pytest.skip(f"needs {WORLD} GPUs")
+    run_gpu_ranks(WORLD, _rank, mode, str(tmp_path), timeout=300)
+    for r in range(WORLD):
+        res = torch.load(tmp_path / f"r{r}.pt")
+        a, b = res[False], res[True]
+        for x, y in zip(a["loss"], b["loss"]):
+            assert abs(x - y) <= 2e-3 * abs(x), (mode, a["loss"], b["loss"])
+        for x, y in zip(a["norm"], b["norm"]):
+            assert abs(x - y) <= 1e-3 * abs(x), (mode, a["norm"], b["norm"])
+        for n, p in a["params"].items():
+            q = b["params"][n]
+            rel = ((p - q).norm() / (p.norm() + 1e-12)).item()
+            assert rel < 5e-3, (mode, n, rel)
+        if mode == "ddp":
+            sa, sb = a["state"]["optimizer"]["state"], b["state"]["optimizer"]["state"]
+            for i in sa:
+                for k in ("exp_avg", "exp_avg_sq", "master_param"):
+                    x, y = sa[i][k].float(), sb[i][k].float()
+                    rel = ((x - y).norm() / (x.norm() + 1e-12)).item()
+                    assert rel < 5e-3, (i, k, rel)
