@@ -772,12 +772,25 @@ static int noalloc_launch(const BwdParams& p, cudaStream_t stream) {
   if (cudaFuncSetAttribute(flash_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            smem) != cudaSuccess)
     return NMB_NOALLOC_LAUNCH_FAILED;
+  // An error left pending by some earlier, unrelated call is not this call's failure:
+  // clear it first, so the check after each launch below sees only our own launches.
+  (void)cudaGetLastError();
   dim3 grid((p.Sk + 63) / 64, p.Hkv, p.B);
+  // pre: delta = rowsum(dO * O) and dq_acc = 0; the main kernel adds into dq_acc; dq:
+  // dq = bf16(dq_acc). With no keys (Sk == 0) the main kernel has nothing to do and dq
+  // comes out as zeros.
   flash_bwd_pre_kernel<D><<<(rows + 7) / 8, 256, 0, stream>>>(p);
-  flash_bwd_kernel<D><<<grid, 128, smem, stream>>>(p);
+  if (cudaGetLastError() != cudaSuccess) return NMB_NOALLOC_LAUNCH_FAILED;
+  int launched = 1;
+  if (p.Sk > 0) {
+    flash_bwd_kernel<D><<<grid, 128, smem, stream>>>(p);
+    if (cudaGetLastError() != cudaSuccess) return NMB_NOALLOC_LAUNCH_FAILED;
+    ++launched;
+  }
   flash_bwd_dq_kernel<D><<<(pairs + 255) / 256, 256, 0, stream>>>(p);
-  NMB_LAUNCHED(3);
-  return cudaGetLastError() == cudaSuccess ? NMB_NOALLOC_OK : NMB_NOALLOC_LAUNCH_FAILED;
+  if (cudaGetLastError() != cudaSuccess) return NMB_NOALLOC_LAUNCH_FAILED;
+  NMB_LAUNCHED(launched + 1);
+  return NMB_NOALLOC_OK;
 }
 
 }  // namespace attn

@@ -24,6 +24,10 @@
 //  * All calls share the one scratch array: calls that can overlap on the GPU
 //    (different streams without ordering) race and corrupt each other. The
 //    kernels clear the parts that must start at zero on every call.
+//  * seq_k == 0 (no keys) is valid: dq is written as zeros and dk/dv are empty.
+//  * A CUDA error that an earlier, unrelated call left pending is cleared before the
+//    launches (cudaGetLastError), so NMB_NOALLOC_LAUNCH_FAILED reports only a failure
+//    of this call's own kernel launches.
 //  * Layout: q/o/dout/dq are contiguous [B, Sq, Hq, D]; k/v/dk/dv contiguous
 //    [B, Sk, Hkv, D]; lse is [B, Hq, Sq] fp32 (base-2 log-sum-exp from the
 //    forward); bf16 tensors, D = 64 or 128, Hq a multiple of Hkv.

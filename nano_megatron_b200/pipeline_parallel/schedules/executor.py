@@ -80,8 +80,13 @@ class PipelineScheduleExecutor:
         prev_pp = self.rank - 1  # previous logical stage lives on pp_rank-1 (mod PP)
         next_pp = self.rank + 1
         if a.kind == "F":
-            return self.p2p.post_recv_activation(self.activation_shape, prev_pp)
-        return self.p2p.post_recv_grad(self.activation_shape, next_pp)
+            return self.p2p.post_recv_activation(self.activation_shape, prev_pp,
+                                                 a.microbatch, a.chunk)
+        return self.p2p.post_recv_grad(self.activation_shape, next_pp, a.microbatch, a.chunk)
+
+    def _consumer_chunk(self, chunk: int, step: int) -> int:
+        """Chunk (virtual stage) of the logical stage ``step`` (+1 / -1) away."""
+        return (self._logical(chunk) + step) // self.pp
 
     # run ------------------------------------------------------------------
     def forward_backward(self, microbatches, *, forward_only: bool = False) -> LossAccumulator:
@@ -135,7 +140,8 @@ class PipelineScheduleExecutor:
         if self._is_last(a.chunk):
             out = extract_loss(out, mb, m, acc)
         else:
-            self.p2p.send_activation(out, self.rank + 1)
+            self.p2p.send_activation(out, self.rank + 1, a.microbatch,
+                                     self._consumer_chunk(a.chunk, +1))
         if not forward_only:
             records[(a.microbatch, a.chunk)] = (inp, out)
 
@@ -149,7 +155,8 @@ class PipelineScheduleExecutor:
                 torch.autograd.backward(out, grad)
         if inp is not None and not self._is_first(a.chunk):
             g = inp.grad if inp.grad is not None else torch.zeros_like(inp)
-            self.p2p.send_grad(g, self.rank - 1)
+            self.p2p.send_grad(g, self.rank - 1, a.microbatch,
+                               self._consumer_chunk(a.chunk, -1))
 
 
 def build_pipeline_schedule(config, model, parallel, data_parallel):

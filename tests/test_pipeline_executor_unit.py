@@ -42,17 +42,17 @@ class _Recorder:
         self.ops.append((kind, dst))
         self.in_flight.append(_Work(self.ops, kind))
 
-    def send_activation(self, t, dst):
+    def send_activation(self, t, dst, microbatch=0, chunk=0):
         self._send("send_act", t, dst)
 
-    def send_grad(self, t, dst):
+    def send_grad(self, t, dst, microbatch=0, chunk=0):
         self._send("send_grad", t, dst)
 
-    def post_recv_activation(self, shape, src):
+    def post_recv_activation(self, shape, src, microbatch=0, chunk=0):
         self.ops.append(("recv_act", src))
         return _Work(self.ops, "recv"), torch.ones(shape)
 
-    def post_recv_grad(self, shape, src):
+    def post_recv_grad(self, shape, src, microbatch=0, chunk=0):
         self.ops.append(("recv_grad", src))
         return _Work(self.ops, "recv"), torch.ones(shape)
 

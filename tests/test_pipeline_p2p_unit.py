@@ -82,20 +82,42 @@ def test_static_shapes_use_one_batched_op_per_transfer_on_the_right_channel(monk
 
 
 def test_dynamic_shapes_send_a_validated_header_first(monkeypatch):
-    hdr = torch.zeros(p2p_mod.HEADER_LEN, dtype=torch.int64)
-    hdr[0], hdr[1], hdr[2:5] = p2p_mod.HEADER_VERSION, 3, torch.tensor([5, 2, 8])
+    hdr = torch.tensor(p2p_mod.encode_header(p2p_mod.KIND_ACTIVATION, 3, 1, (5, 2, 8)))
     c, calls = _comm(monkeypatch, dynamic=True, header_for_recv=hdr)
-    c.send_activation(torch.ones(5, 2, 8, dtype=torch.bfloat16), 2)
+    c.send_activation(torch.ones(5, 2, 8, dtype=torch.bfloat16), 2, microbatch=3, chunk=1)
     assert calls[0][:3] == ("send", 12, "pp") and calls[0][3:] == ((p2p_mod.HEADER_LEN,),
                                                                     torch.int64)
     assert calls[1] == ("send", 12, "pp", (5, 2, 8), torch.bfloat16)
     sent_header = c._sends[0][1]
-    assert sent_header[:5].tolist() == [p2p_mod.HEADER_VERSION, 3, 5, 2, 8]
-    work, buf = c.post_recv_activation((99, 99, 99), 0)    # the header decides the shape
-    assert buf.shape == (5, 2, 8)
+    # version, kind, microbatch, consumer chunk, ndim, dims, unused dims -1
+    assert sent_header.tolist() == [p2p_mod.HEADER_VERSION, p2p_mod.KIND_ACTIVATION, 3, 1, 3,
+                                    5, 2, 8] + [-1] * (p2p_mod.MAX_DIMS - 3)
+    work, buf = c.post_recv_activation((99, 99, 99), 0, microbatch=3, chunk=1)
+    assert buf.shape == (5, 2, 8)                           # the header decides the shape
     assert calls[2][0] == "recv" and calls[2][4] == torch.int64 and calls[3][3] == (5, 2, 8)
     bad = hdr.clone()
     bad[0] = p2p_mod.HEADER_VERSION + 1
     c2, _ = _comm(monkeypatch, dynamic=True, header_for_recv=bad)
     with pytest.raises(RuntimeError, match="header version"):
-        c2.post_recv_grad((5, 2, 8), 2)
+        c2.post_recv_activation((5, 2, 8), 0, microbatch=3, chunk=1)
+
+
+@pytest.mark.parametrize("expect", [(p2p_mod.KIND_GRAD, 3, 1),       # wrong kind
+                                    (p2p_mod.KIND_ACTIVATION, 4, 1),  # wrong microbatch
+                                    (p2p_mod.KIND_ACTIVATION, 3, 0)])  # wrong chunk
+def test_misrouted_transfer_is_rejected(monkeypatch, expect):
+    hdr = torch.tensor(p2p_mod.encode_header(p2p_mod.KIND_ACTIVATION, 3, 1, (5, 2, 8)))
+    c, _ = _comm(monkeypatch, dynamic=True, header_for_recv=hdr)
+    kind, mb, chunk = expect
+    post = c.post_recv_grad if kind == p2p_mod.KIND_GRAD else c.post_recv_activation
+    with pytest.raises(RuntimeError, match="out of order"):
+        post((5, 2, 8), 0, microbatch=mb, chunk=chunk)
+
+
+def test_malformed_header_shape_is_rejected():
+    vals = p2p_mod.encode_header(p2p_mod.KIND_GRAD, 0, 0, (4, 4))
+    vals[7] = 9                       # a dim past ndim that is not -1
+    with pytest.raises(RuntimeError, match="malformed"):
+        p2p_mod.decode_header(vals, (p2p_mod.KIND_GRAD, 0, 0))
+    with pytest.raises(ValueError):
+        p2p_mod.encode_header(p2p_mod.KIND_GRAD, 0, 0, tuple(range(1, 10)))
