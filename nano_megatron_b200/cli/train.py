@@ -131,6 +131,7 @@ def run(config_path: Path, *, overrides: Sequence[str] = (), resume: Path | None
             if config.validation.interval > 0:
                 trainer.bind_validation_data(build_validation_dataloader(
                     config, comps.parallel, tokenizer=tokenizer))
+            primary = runtime.is_primary
             state = trainer.fit(max_steps=max_steps, log=log)
         finally:
             if trainer.profiler is not None:
@@ -140,7 +141,7 @@ def run(config_path: Path, *, overrides: Sequence[str] = (), resume: Path | None
             if health is not None:
                 health.stop()
             comps.close(trainer)    # graphs, peer memory, subgroups, default group, in order
-        if runtime.is_primary:
+        if primary:
             log(f"finished step={state.step} samples={state.consumed_samples} "
                 f"tokens={state.consumed_tokens}")
         return state

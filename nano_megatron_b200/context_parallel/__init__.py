@@ -20,7 +20,8 @@ holds chunks r and 2*CP-1-r of 2*CP equal chunks) so causal work is balanced.
 
 from __future__ import annotations
 
-from .attention import AllGatherContextParallelAttention, RingContextParallelAttention
+from .attention import (AllGatherContextParallelAttention, PeerRingContextParallelAttention,
+                        RingContextParallelAttention)
 from .utils import local_positions, shard_sequence, unshard_sequence
 
 
@@ -32,10 +33,13 @@ def build_context_parallel_attention(config, parallel):
     if backend == "all_gather":
         return AllGatherContextParallelAttention(parallel.cp, load_balance=balance)
     if backend == "ring":
-        return RingContextParallelAttention(parallel.cp, load_balance=balance)
+        # the peer-memory transport is attached later (attach_cp_heap) when the layout
+        # allows it; until then (and on CPU) this core runs the NCCL ring
+        return PeerRingContextParallelAttention(parallel.cp, load_balance=balance)
     raise ValueError(f"unknown context-parallel backend {backend!r}")
 
 
-__all__ = ["AllGatherContextParallelAttention", "RingContextParallelAttention",
+__all__ = ["AllGatherContextParallelAttention", "PeerRingContextParallelAttention",
+           "RingContextParallelAttention",
            "build_context_parallel_attention", "local_positions", "shard_sequence",
            "unshard_sequence"]

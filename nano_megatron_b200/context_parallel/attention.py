@@ -249,3 +249,154 @@ class RingContextParallelAttention(_CPBase):
         lv = own.view(-1, B, 2, hkv, D)
         dk.copy_(lv[:, :, 0].transpose(0, 1))
         dv.copy_(lv[:, :, 1].transpose(0, 1))
+
+
+CH_KV, CH_DKV = 0, 1
+
+
+class PeerRingContextParallelAttention(RingContextParallelAttention):
+    """Ring attention whose K/V blocks travel through NVLink peer memory.
+
+    Every rank publishes the layer's K/V block into its :class:`SymmetricHeap` slot for
+    that layer (one copy, then a signal). Ring step ``i`` computes on block ``i`` with the
+    flash kernels while their pull warp copies block ``i + 1`` from its owner's slot into
+    a local double buffer (plain peer loads; the kernels' TMA loads then read only this
+    GPU's memory). The owner is read directly, not relayed around the ring: NVSwitch gives
+    every pair full bandwidth. In the backward pass the blocks are pulled again from the
+    same slots, and each fp32 dK/dV partial for another rank's keys is stored into that
+    rank's return slot by peer stores; after a signal the owner adds the partials of the
+    ranks whose queries see its keys (the causal layout tells which) to its own. Falls back
+    to the NCCL ring when no heap is attached (CPU, or a layout the heap does not cover).
+    The reference rotates K/V with blocking send/receive pairs
+    (src/nano_megatron/context_parallel/ring.py:82-101, 161, 247).
+    """
+
+    heap = None
+    layer_slots: dict = {}
+    kv_numel = 0
+
+    def attach(self, heap, layer_slots: dict, kv_numel: int, device) -> None:
+        self.heap = heap
+        self.layer_slots = dict(layer_slots)
+        self.kv_numel = int(kv_numel)
+        self._bufs = [torch.empty(kv_numel, dtype=torch.bfloat16, device=device)
+                      for _ in range(2)]
+        self._dkv_numel = kv_numel
+
+    def detach(self) -> None:
+        self.heap = None
+        self._bufs = []
+
+    # ------------------------------------------------------------------ addressing
+    def _slot_ptr(self, rank: int, layer: int) -> int:
+        return self.heap.ptr(rank, "kv") + self.layer_slots[layer] * self.kv_numel * 2
+
+    def _slot_view(self, layer: int) -> torch.Tensor:
+        kv = self.heap.local("kv", torch.bfloat16)
+        off = self.layer_slots[layer] * self.kv_numel
+        return kv[off:off + self.kv_numel]
+
+    def _ret_ptr(self, owner: int, parity: int, src: int) -> int:
+        n = self.heap.size
+        return self.heap.ptr(owner, "dkv") + ((parity & 1) * n + src) * self._dkv_numel * 4
+
+    def _pull(self, src: int, layer: int, step_next: int):
+        if step_next >= self.heap.size:
+            return None
+        h = self.heap
+        return (self._slot_ptr(src, layer), self._bufs[step_next % 2],
+                h.flag_slots(h.rank, CH_KV) + src * 4, h.epoch_ptr(CH_KV))
+
+    def _usable(self, q, mb) -> bool:
+        return self.heap is not None and q.is_cuda and \
+            mb.extra.get("layer") in self.layer_slots
+
+    def _block(self, step: int, own: torch.Tensor) -> torch.Tensor:
+        return own if step == 0 else self._bufs[step % 2]
+
+    # ------------------------------------------------------------------ forward
+    def forward(self, q, k, v, o, mb):
+        if not self._usable(q, mb):
+            return super().forward(q, k, v, o, mb)
+        from nano_megatron_b200.ops._ext import lib
+
+        layer = mb.extra["layer"]
+        B, Sq, Hq, D = q.shape
+        hkv = k.shape[2]
+        g, h = self.group, self.heap
+        own = self._slot_view(layer)
+        own.view(-1, B, 2 * hkv * D).copy_(_kv_rows(q, k, v))     # publish this layer's K/V
+        lib().peer_signal(h.signal_targets(CH_KV), h.epoch_ptr(CH_KV))
+        o_acc = torch.zeros(B, Sq, Hq, D, device=q.device, dtype=torch.float32)
+        lse_acc = torch.full((B, Hq, Sq), float("-inf"), device=q.device, dtype=torch.float32)
+        for step in range(g.size):
+            src = (g.rank - step) % g.size
+            pull = self._pull((g.rank - step - 1) % g.size, layer, step + 1)
+            view = self._block(step, own).view(-1, B, 2, hkv, D)
+            kb, vb = view[:, :, 0].transpose(0, 1), view[:, :, 1].transpose(0, 1)
+            pairs = self._ring_pairs(src, Sq, kb.shape[1])
+            if not pairs and pull is not None:
+                lib().cp_pull(pull[0], pull[1], pull[2], pull[3], h.status)
+            for i, (qs, qr, qo, ks, kr, ko) in enumerate(pairs):
+                on, ln = F.attention_fwd(q[:, qs:qs + qr], kb[:, ks:ks + kr], vb[:, ks:ks + kr],
+                                         causal=True, q_offset=qo, k_offset=ko,
+                                         pull=pull if i == 0 else None)
+                _merge(o_acc[:, qs:qs + qr], lse_acc[:, :, qs:qs + qr], on, ln)
+        o.transpose(0, 1).copy_(o_acc.to(o.dtype))
+        return lse_acc
+
+    # ------------------------------------------------------------------ backward
+    def backward(self, q, k, v, o, do, lse, dq, dk, dv, mb, inv_freq):
+        if not self._usable(q, mb):
+            return super().backward(q, k, v, o, do, lse, dq, dk, dv, mb, inv_freq)
+        from nano_megatron_b200.ops._ext import lib
+
+        layer = mb.extra["layer"]
+        B, Sq, Hq, D = q.shape
+        hkv = k.shape[2]
+        g, h = self.group, self.heap
+        own = self._slot_view(layer)            # still this layer's K/V (published in forward)
+        Sk = own.numel() // (B * 2 * hkv * D)
+        mine = torch.zeros(Sk, B, 2 * hkv * D, dtype=torch.float32, device=q.device)
+        dq_acc = torch.zeros(B, Sq, Hq, D, dtype=torch.float32, device=q.device)
+        o_bs = o.transpose(0, 1)
+        mask = 0
+        for step in range(g.size):
+            src = (g.rank - step) % g.size
+            pull = self._pull((g.rank - step - 1) % g.size, layer, step + 1)
+            view = self._block(step, own).view(-1, B, 2, hkv, D)
+            kb, vb = view[:, :, 0].transpose(0, 1), view[:, :, 1].transpose(0, 1)
+            pairs = self._ring_pairs(src, Sq, Sk)
+            if not pairs and pull is not None:
+                lib().cp_pull(pull[0], pull[1], pull[2], pull[3], h.status)
+            part = mine if step == 0 else \
+                (torch.zeros(Sk, B, 2 * hkv * D, dtype=torch.float32, device=q.device)
+                 if pairs else None)
+            dview = part.view(-1, B, 2, hkv, D) if part is not None else None
+            for i, (qs, qr, qo, ks, kr, ko) in enumerate(pairs):
+                dqc = torch.empty(B, qr, Hq, D, device=q.device, dtype=q.dtype)
+                dkc = torch.empty(B, kr, hkv, D, device=q.device, dtype=q.dtype)
+                dvc = torch.empty_like(dkc)
+                F.attention_bwd(q[:, qs:qs + qr], kb[:, ks:ks + kr], vb[:, ks:ks + kr],
+                                o_bs[:, qs:qs + qr], do[:, qs:qs + qr],
+                                lse[:, :, qs:qs + qr].contiguous(), dqc, dkc, dvc, causal=True,
+                                q_offset=qo, k_offset=ko, pull=pull if i == 0 else None)
+                dq_acc[:, qs:qs + qr] += dqc.float()
+                dview[ks:ks + kr, :, 0] += dkc.transpose(0, 1).float()
+                dview[ks:ks + kr, :, 1] += dvc.transpose(0, 1).float()
+            if step > 0 and part is not None:
+                # return the partial to the owner of these keys: peer stores into its slot
+                lib().cp_push(part.view(-1), self._ret_ptr(src, 0, g.rank),
+                              self._ret_ptr(src, 1, g.rank), h.epoch_ptr(CH_DKV))
+            # which ranks' queries see this rank's keys (they send partials back)
+            frm = (g.rank + step) % g.size
+            if step > 0 and self._ring_pairs(g.rank, Sq, Sk, rank_q=frm):
+                mask |= 1 << frm
+        lib().peer_signal(h.signal_targets(CH_DKV), h.epoch_ptr(CH_DKV))
+        lib().cp_reduce(mine.view(-1), [self._ret_ptr(h.rank, 0, s) for s in range(g.size)],
+                        [self._ret_ptr(h.rank, 1, s) for s in range(g.size)], mask,
+                        h.flag_slots(h.rank, CH_DKV), h.epoch_ptr(CH_DKV), h.status)
+        dq.copy_(dq_acc.to(dq.dtype))
+        lv = mine.view(-1, B, 2, hkv, D)
+        dk.copy_(lv[:, :, 0].transpose(0, 1))
+        dv.copy_(lv[:, :, 1].transpose(0, 1))

@@ -12,7 +12,10 @@
 //               softmax in base 2, rescales its O row in TMEM when the running
 //               max grows, writes P (bf16) to shared memory in the UMMA
 //               K-major 128-byte-swizzled layout and signals the MMA warp;
-//               at the end it normalises O and stores O and the base-2 LSE.
+//               at the end it normalises O and stores O and the base-2 LSE;
+//   warp 6    : ring pull (context parallelism) — copies this CTA's slice of the
+//               next ring step's K/V block from the owner GPU's memory into a local
+//               buffer while the other warps compute (idle otherwise).
 // Q/K/V are read through 4-D TMA maps (d, head, seq, batch) over the strided
 // views of the fused QKV buffer; P is the A operand (K-major) and V the B
 // operand (MN-major) of the second product. Causal key blocks above the
@@ -31,7 +34,8 @@ namespace fatc {
 
 constexpr int kBM = 128;
 constexpr int kBN = 128;
-constexpr int kThreads = 192;
+constexpr int kThreads = 224;      // 6 compute warps + 1 pull warp
+constexpr int kPullWarp = 6;
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
@@ -54,6 +58,7 @@ struct Params {
   int causal;
   float scale_log2;
   int* status;
+  PullDesc pull;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -213,6 +218,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (ok) do_pv(nblk - 1);
     }
+  } else if (warp == kPullWarp) {
+    pull_slice(p.pull, threadIdx.x & 31, 32);
   } else {
     // ---------------------------------------------------------------- softmax
     const int quarter = warp & 3;
@@ -383,10 +390,30 @@ static CUtensorMap make_map(const at::Tensor& t, int rows) {
 using namespace nmb;
 using namespace nmb::fatc;
 
+// Ring-pull descriptor from host arguments (pull_src == 0: no pull).
+PullDesc make_pull(int64_t src, const c10::optional<at::Tensor>& dst, int64_t flag, int64_t epoch,
+                   int* status) {
+  PullDesc d{};
+  if (src == 0) return d;
+  TORCH_CHECK(dst.has_value() && dst->is_cuda() && dst->is_contiguous() &&
+                  dst->nbytes() % 16 == 0 && reinterpret_cast<uintptr_t>(dst->data_ptr()) % 16 == 0,
+              "ring pull: destination must be a contiguous, 16-byte multiple CUDA buffer");
+  TORCH_CHECK(src % 16 == 0 && flag % 4 == 0 && flag != 0 && epoch % 4 == 0 && epoch != 0,
+              "ring pull: bad source / flag / epoch address");
+  d.src = reinterpret_cast<const uint4*>(src);
+  d.dst = reinterpret_cast<uint4*>(dst->data_ptr());
+  d.vec16 = static_cast<long long>(dst->nbytes() / 16);
+  d.flag = reinterpret_cast<const uint32_t*>(flag);
+  d.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch);
+  d.status = status;
+  return d;
+}
+
 // Same contract as flash_attn_fwd; runs the tcgen05 kernel.
 void flash_attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
                        double softmax_scale, bool causal, int64_t q_offset, int64_t k_offset,
-                       at::Tensor status) {
+                       at::Tensor status, int64_t pull_src, c10::optional<at::Tensor> pull_dst,
+                       int64_t pull_flag, int64_t pull_epoch) {
   const int64_t D = q.size(3);
   TORCH_CHECK(D == 64 || D == 128, "flash_attn_fwd_tc: head_dim must be 64 or 128");
   for (const at::Tensor* t : {&q, &k, &v, &o}) {
@@ -411,6 +438,7 @@ void flash_attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, a
   p.causal = causal ? 1 : 0;
   p.scale_log2 = static_cast<float>(softmax_scale) * kLog2e;
   p.status = status.data_ptr<int>();
+  p.pull = make_pull(pull_src, pull_dst, pull_flag, pull_epoch, p.status);
   if (p.B == 0 || p.Sq == 0) return;
   const at::cuda::CUDAGuard guard(q.device());
   ensure_current_context(q.device().index());

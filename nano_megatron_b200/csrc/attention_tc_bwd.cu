@@ -34,8 +34,11 @@ constexpr int kBM = 128;  // queries per step
 // Threads: warp 0 loads (TMA), warp 1 issues the MMAs, then SH groups of four
 // softmax warps. With SH = 2 the two groups split the 128 query columns of each
 // step (and the dQ / dK-dV drains) in halves: warp w reads TMEM lane quarter w % 4.
+// The last warp pulls the next ring step's K/V block (context parallelism; idle otherwise).
 template <int SH>
-constexpr int threads_for() { return 64 + 128 * SH; }
+constexpr int threads_for() { return 64 + 128 * SH + 32; }
+template <int SH>
+constexpr int pull_warp() { return 2 + 4 * SH; }
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int D>
@@ -70,6 +73,7 @@ struct Params {
   const int* k_pos;
   const float* inv_freq;
   int* status;
+  PullDesc pull;
 };
 
 __device__ __forceinline__ float ex2(float x) {
@@ -264,6 +268,8 @@ __global__ void __launch_bounds__(threads_for<SH>(), 1)
         umma_commit(&qdo_empty[st]);
       }
     }
+  } else if (warp == pull_warp<SH>()) {
+    pull_slice(p.pull, threadIdx.x & 31, 32);
   } else {
     // ---------------------------------------------------------------- softmax / dQ / epilogue
     static_assert(SH == 1 || SH == 2, "one or two softmax warp groups");
@@ -469,6 +475,9 @@ static CUtensorMap make_map(const at::Tensor& t) {
 using namespace nmb;
 using namespace nmb::fabw;
 
+PullDesc make_pull(int64_t src, const c10::optional<at::Tensor>& dst, int64_t flag, int64_t epoch,
+                   int* status);   // attention_tc.cu
+
 // Softmax warp groups per CTA: 1 (default) or 2 (NMB_ATTN_BWD_SOFTMAX_GROUPS=2).
 static int softmax_groups() {
   static const int n = [] {
@@ -501,7 +510,9 @@ void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor d
                           at::Tensor lse, at::Tensor delta, at::Tensor dq_acc, at::Tensor dk,
                           at::Tensor dv, double softmax_scale, bool causal, int64_t q_offset,
                           int64_t k_offset, c10::optional<at::Tensor> k_pos,
-                          c10::optional<at::Tensor> inv_freq, at::Tensor status) {
+                          c10::optional<at::Tensor> inv_freq, at::Tensor status,
+                          int64_t pull_src, c10::optional<at::Tensor> pull_dst,
+                          int64_t pull_flag, int64_t pull_epoch) {
   const int64_t D = q.size(3);
   TORCH_CHECK(D == 64 || D == 128, "flash_attn_bwd_tc: head_dim must be 64 or 128");
   for (const at::Tensor* t : {&q, &k, &v, &dout, &dk, &dv}) {
@@ -534,6 +545,7 @@ void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor d
   p.inv_freq = inv_freq.has_value() ? inv_freq->data_ptr<float>() : nullptr;
   TORCH_CHECK(p.k_pos == nullptr || p.inv_freq != nullptr);
   p.status = status.data_ptr<int>();
+  p.pull = make_pull(pull_src, pull_dst, pull_flag, pull_epoch, p.status);
   if (p.B == 0 || p.Sk == 0) return;
   const at::cuda::CUDAGuard guard(q.device());
   ensure_current_context(q.device().index());

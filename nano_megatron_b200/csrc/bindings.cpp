@@ -18,7 +18,8 @@ void flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::
                     c10::optional<at::Tensor> k_pos, c10::optional<at::Tensor> inv_freq);
 void flash_attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
                        double softmax_scale, bool causal, int64_t q_offset, int64_t k_offset,
-                       at::Tensor status);
+                       at::Tensor status, int64_t pull_src, c10::optional<at::Tensor> pull_dst,
+                       int64_t pull_flag, int64_t pull_epoch);
 void flash_attn_bwd_prep(at::Tensor o, at::Tensor dout, at::Tensor delta, at::Tensor dq_acc);
 void flash_attn_bwd_dq_convert(at::Tensor dq_acc, at::Tensor dq, c10::optional<at::Tensor> q_pos,
                                c10::optional<at::Tensor> inv_freq);
@@ -27,7 +28,9 @@ void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor d
                           at::Tensor lse, at::Tensor delta, at::Tensor dq_acc, at::Tensor dk,
                           at::Tensor dv, double softmax_scale, bool causal, int64_t q_offset,
                           int64_t k_offset, c10::optional<at::Tensor> k_pos,
-                          c10::optional<at::Tensor> inv_freq, at::Tensor status);
+                          c10::optional<at::Tensor> inv_freq, at::Tensor status,
+                          int64_t pull_src, c10::optional<at::Tensor> pull_dst,
+                          int64_t pull_flag, int64_t pull_epoch);
 void rmsnorm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps);
 void rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, at::Tensor rstd, at::Tensor dx,
                  c10::optional<at::Tensor> dw, c10::optional<at::Tensor> dres);
@@ -57,7 +60,22 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
 void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
                 std::vector<int64_t> staging_ptrs, std::vector<int64_t> staging_ptrs_odd,
                 int64_t rows_per_rank, int64_t n_out, int64_t rank, int64_t epoch_ptr,
-                at::Tensor status);
+                at::Tensor status, c10::optional<at::Tensor> alpha_t);
+void tp_embedding_scatter(at::Tensor ids, at::Tensor w, int64_t vstart, int64_t rows_per_rank,
+                          std::vector<int64_t> slots_even, std::vector<int64_t> slots_odd,
+                          int64_t epoch_ptr);
+void tp_embedding_collect(int64_t slot_even, int64_t slot_odd, at::Tensor out, int64_t tp,
+                          int64_t flags_ptr, int64_t epoch_ptr, at::Tensor status);
+void tp_embedding_bwd_gather(at::Tensor ids, std::vector<int64_t> slots_even,
+                             std::vector<int64_t> slots_odd, int64_t rows_per_rank, int64_t H,
+                             at::Tensor grad, int64_t vstart, int64_t flags_ptr,
+                             int64_t epoch_ptr, at::Tensor status);
+void tp_ce_stats_scatter(at::Tensor logits, at::Tensor labels, int64_t vstart, int64_t rank,
+                         std::vector<int64_t> slots_even, std::vector<int64_t> slots_odd,
+                         int64_t epoch_ptr);
+void tp_ce_finish_gather(at::Tensor logits, at::Tensor labels, int64_t vstart, int64_t stats_even,
+                         int64_t stats_odd, int64_t tp, at::Tensor loss_row, bool write_grad,
+                         int64_t flags_ptr, int64_t epoch_ptr, at::Tensor status);
 std::tuple<at::Tensor, pybind11::bytes> symm_alloc(int64_t bytes, int64_t device);
 int64_t symm_open(pybind11::bytes handle, int64_t device);
 void symm_close(int64_t ptr, int64_t device);
@@ -76,6 +94,10 @@ void replica_adamw_gather(std::vector<int64_t> grad_ptrs, std::vector<int64_t> p
                           double beta2, double eps, double wd, int64_t step,
                           c10::optional<at::Tensor> grad_scale, c10::optional<at::Tensor> lr_t);
 void replica_wait(int64_t flags_ptr, int64_t n, int64_t epoch_ptr, at::Tensor status);
+void cp_pull(int64_t src, at::Tensor dst, int64_t flag_ptr, int64_t epoch_ptr, at::Tensor status);
+void cp_push(at::Tensor src, int64_t dst_even, int64_t dst_odd, int64_t epoch_ptr);
+void cp_reduce(at::Tensor acc, std::vector<int64_t> slots_even, std::vector<int64_t> slots_odd,
+               int64_t mask, int64_t flags_ptr, int64_t epoch_ptr, at::Tensor status);
 void scale_inplace(at::Tensor x, double s);
 void dropout_apply(at::Tensor x, at::Tensor y, double p, int64_t seed);
 
@@ -89,10 +111,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("max_ctas"), py::arg("rope_cs") = py::none());
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
-  m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc, "tcgen05/TMEM causal flash attention forward");
+  m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc,
+        "tcgen05/TMEM causal flash attention forward (optionally pulling the next ring block)",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o"), py::arg("lse"),
+        py::arg("softmax_scale"), py::arg("causal"), py::arg("q_offset"), py::arg("k_offset"),
+        py::arg("status"), py::arg("pull_src") = 0, py::arg("pull_dst") = py::none(),
+        py::arg("pull_flag") = 0, py::arg("pull_epoch") = 0);
   m.def("flash_attn_bwd_prep", &flash_attn_bwd_prep);
   m.def("flash_attn_bwd_dq_convert", &flash_attn_bwd_dq_convert);
-  m.def("flash_attn_bwd_tc_kv", &flash_attn_bwd_tc_kv, "tcgen05/TMEM attention backward (dK, dV, dQ acc)");
+  m.def("flash_attn_bwd_tc_kv", &flash_attn_bwd_tc_kv,
+        "tcgen05/TMEM attention backward (dK, dV, dQ acc; optionally pulling the next ring block)",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("dout"), py::arg("lse"),
+        py::arg("delta"), py::arg("dq_acc"), py::arg("dk"), py::arg("dv"),
+        py::arg("softmax_scale"), py::arg("causal"), py::arg("q_offset"), py::arg("k_offset"),
+        py::arg("k_pos"), py::arg("inv_freq"), py::arg("status"), py::arg("pull_src") = 0,
+        py::arg("pull_dst") = py::none(), py::arg("pull_flag") = 0, py::arg("pull_epoch") = 0);
   m.def("attn_bwd_softmax_groups", &attn_bwd_softmax_groups,
         "softmax warp groups of the attention backward (NMB_ATTN_BWD_SOFTMAX_GROUPS)");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
@@ -116,7 +149,21 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("head_dim"), py::arg("rope_cols"), py::arg("pos_div"), py::arg("rank"),
         py::arg("flags_ptr"), py::arg("epoch_ptr"), py::arg("status"),
         py::arg("rope_cs") = py::none(), py::arg("gather_ready") = py::none());
-  m.def("gemm_tc_rs", &gemm_tc_rs, "GEMM->RS: partial tiles stored into the owner's staging");
+  m.def("gemm_tc_rs", &gemm_tc_rs, "GEMM->RS: partial tiles stored into the owner's staging",
+        py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"), py::arg("staging_ptrs"),
+        py::arg("staging_ptrs_odd"), py::arg("rows_per_rank"), py::arg("n_out"),
+        py::arg("rank"), py::arg("epoch_ptr"), py::arg("status"),
+        py::arg("alpha_t") = py::none());
+  m.def("tp_embedding_scatter", &tp_embedding_scatter,
+        "TP embedding: rows of this vocabulary shard stored into the sequence owners' slots");
+  m.def("tp_embedding_collect", &tp_embedding_collect,
+        "TP embedding: wait for every rank, copy this rank's slot out");
+  m.def("tp_embedding_bwd_gather", &tp_embedding_bwd_gather,
+        "TP embedding backward: dY rows of this vocabulary shard read from the owners' slots");
+  m.def("tp_ce_stats_scatter", &tp_ce_stats_scatter,
+        "TP cross-entropy: per-row shard statistics stored into every rank's slot");
+  m.def("tp_ce_finish_gather", &tp_ce_finish_gather,
+        "TP cross-entropy: merge every rank's statistics, loss and in-place gradient");
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
@@ -130,6 +177,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("replica_adamw_gather", &replica_adamw_gather,
         "DP: AdamW over this rank's shard, bf16 result stored into every replica's parameters");
   m.def("replica_wait", &replica_wait, "DP: bounded wait for every replica's flag");
+  m.def("cp_pull", &cp_pull, "CP ring: pull a peer's published block into local memory");
+  m.def("cp_push", &cp_push, "CP ring: store a dK/dV partial into its owner's return slot");
+  m.def("cp_reduce", &cp_reduce, "CP ring: add the returned partials once every rank signalled");
   m.def("launch_count", []() { return nmb::launch_counter().load(); },
         "number of kernel launches issued by this library so far (graph replays included)");
   m.def("record_graph_launches", [](int64_t n) { nmb::launch_counter() += n; },

@@ -240,6 +240,36 @@ __device__ __forceinline__ bool wait_flag(const uint32_t* flag, uint32_t epoch, 
   }
 }
 
+// ------------------------------------------------------------ ring pull (peer -> local)
+// A kernel computing on block i of a ring can bring block i+1 into local memory while it
+// runs: each CTA copies its slice of `vec16` 16-byte words from `src` (another GPU's
+// memory, mapped here) to `dst` (this GPU) with plain loads and stores, after a bounded
+// wait until the owner's publish flag reaches the expected epoch. The next kernel on the
+// stream reads `dst` (kernel boundary = ordering); the TMA loads of that kernel therefore
+// read only this GPU's memory.
+struct PullDesc {
+  const uint4* src;            // nullptr: nothing to pull
+  uint4* dst;
+  long long vec16;
+  const uint32_t* flag;        // owner's publish flag (a slot in this rank's flag array)
+  const uint32_t* epoch_ptr;   // device counter holding the epoch to wait for
+  int* status;
+};
+
+__device__ __forceinline__ void pull_slice(const PullDesc& d, int tid, int nthreads) {
+  if (d.src == nullptr) return;
+  const uint32_t e = *reinterpret_cast<const volatile uint32_t*>(d.epoch_ptr);
+  if (!wait_flag(d.flag, e, d.status, kStatusCpFlagTimeout, nullptr)) return;
+  const long long ncta = static_cast<long long>(gridDim.x) * gridDim.y * gridDim.z;
+  const long long cta =
+      blockIdx.x + static_cast<long long>(gridDim.x) * (blockIdx.y + static_cast<long long>(
+                                                                         gridDim.y) * blockIdx.z);
+  const long long per = (d.vec16 + ncta - 1) / ncta;
+  const long long lo = cta * per;
+  const long long hi = lo + per < d.vec16 ? lo + per : d.vec16;
+  for (long long i = lo + tid; i < hi; i += nthreads) d.dst[i] = __ldcg(d.src + i);
+}
+
 // ------------------------------------------------------------------ tcgen05
 __device__ __forceinline__ void tmem_alloc(uint32_t* smem_result, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(

@@ -960,7 +960,7 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
 void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
                 std::vector<int64_t> staging_ptrs, std::vector<int64_t> staging_ptrs_odd,
                 int64_t rows_per_rank, int64_t n_out, int64_t rank, int64_t epoch_ptr,
-                at::Tensor status) {
+                at::Tensor status, c10::optional<at::Tensor> alpha_t) {
   check_operand(a, "A");
   check_operand(b, "B");
   const int tp = static_cast<int>(staging_ptrs.size());
@@ -987,6 +987,11 @@ void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
   p.comm_size = tp;
   p.splits = 1;
   p.epoch_ptr = reinterpret_cast<const uint32_t*>(epoch_ptr);
+  if (alpha_t.has_value()) {
+    TORCH_CHECK(alpha_t->is_cuda() && alpha_t->scalar_type() == at::kFloat,
+                "gemm_tc_rs: alpha must be an fp32 device scalar");
+    p.alpha_ptr = alpha_t->data_ptr<float>();
+  }
   for (int r = 0; r < tp; ++r) {
     p.peer_out[0][r] = reinterpret_cast<__nv_bfloat16*>(staging_ptrs[r]);
     p.peer_out[1][r] = reinterpret_cast<__nv_bfloat16*>(staging_ptrs_odd[r]);

@@ -7,6 +7,8 @@ over NVLink (P2P through NVSwitch). Buffer layout (identical on all ranks):
     [ flags: 16 channels x 8 source slots x uint32 | pad to 4 KiB ]
     [ reduce-scatter staging: 2 parities x TP x rows x cols bf16 ]
     [ all-gather shards:       2 parities x rows x cols bf16      ]
+    [ embedding rows:          2 parities x rows x hidden bf16    ]  (optional)
+    [ cross-entropy stats:     2 parities x TP x tokens x 3 fp32  ]  (optional)
 
 A channel's epoch counter lives in device memory (one int per channel, local to
 the rank) and is advanced by the signal kernel once per collective call on every
@@ -28,18 +30,20 @@ import torch.distributed as dist
 
 FLAG_BYTES = 4096
 MAX_TP = 8
-CH_RS, CH_AG, CH_AG_BWD = 0, 1, 2
+CH_RS, CH_AG, CH_AG_BWD, CH_EMB, CH_CE = 0, 1, 2, 3, 4
 GATHER_READY_TILES = 4096          # 128-row tiles of a gathered operand (512K rows)
 
 
 class SymmetricWorkspace:
     def __init__(self, *, rank: int, size: int, ptrs: list[int], owner: torch.Tensor,
-                 device: torch.device, rs_bytes: int, ag_bytes: int, opened: list[int]) -> None:
+                 device: torch.device, rs_bytes: int, ag_bytes: int, opened: list[int],
+                 emb_bytes: int = 0, ce_bytes: int = 0) -> None:
         self.rank, self.size = rank, size
         self.ptrs = ptrs              # base address of every rank's buffer, mapped here
         self.owner = owner            # keeps this rank's allocation alive
         self.device = device
         self.rs_bytes, self.ag_bytes = rs_bytes, ag_bytes
+        self.emb_bytes, self.ce_bytes = emb_bytes, ce_bytes
         self._opened = opened         # peer mappings to close
         self.epochs = torch.zeros(16, dtype=torch.int32, device=device)  # device counters
         # per channel and 128-row tile: epoch at which the gathered rows sit in the local
@@ -52,20 +56,22 @@ class SymmetricWorkspace:
 
     # ------------------------------------------------------------------ construction
     @staticmethod
-    def total_bytes(rs_bytes: int, ag_bytes: int) -> int:
-        return FLAG_BYTES + 2 * rs_bytes + 2 * ag_bytes
+    def total_bytes(rs_bytes: int, ag_bytes: int, emb_bytes: int = 0, ce_bytes: int = 0) -> int:
+        return FLAG_BYTES + 2 * (rs_bytes + ag_bytes + emb_bytes + ce_bytes)
 
     @classmethod
-    def create(cls, group, *, rs_bytes: int, ag_bytes: int, device: torch.device
-               ) -> "SymmetricWorkspace":
+    def create(cls, group, *, rs_bytes: int, ag_bytes: int, device: torch.device,
+               emb_bytes: int = 0, ce_bytes: int = 0) -> "SymmetricWorkspace":
         """Collective over ``group`` (a ParallelGroup with an NCCL process group)."""
         from nano_megatron_b200.ops._ext import lib
 
         if group.size > MAX_TP:
             raise ValueError(f"symmetric workspace supports at most {MAX_TP} ranks")
         rs_bytes, ag_bytes = _align(rs_bytes), _align(ag_bytes)
+        emb_bytes, ce_bytes = _align(emb_bytes, 4096, 0), _align(ce_bytes, 4096, 0)
         dev = torch.device(device)
-        buf, handle = lib().symm_alloc(cls.total_bytes(rs_bytes, ag_bytes), dev.index)
+        buf, handle = lib().symm_alloc(cls.total_bytes(rs_bytes, ag_bytes, emb_bytes, ce_bytes),
+                                       dev.index)
         handles: list = [None] * group.size
         dist.all_gather_object(handles, bytes(handle), group=group.process_group)
         ptrs, opened = [], []
@@ -79,18 +85,21 @@ class SymmetricWorkspace:
         torch.cuda.synchronize(dev)
         dist.barrier(group=group.process_group, device_ids=[dev.index])
         return cls(rank=group.rank, size=group.size, ptrs=ptrs, owner=buf, device=dev,
-                   rs_bytes=rs_bytes, ag_bytes=ag_bytes, opened=opened)
+                   rs_bytes=rs_bytes, ag_bytes=ag_bytes, opened=opened, emb_bytes=emb_bytes,
+                   ce_bytes=ce_bytes)
 
     @classmethod
-    def emulated(cls, size: int, *, rs_bytes: int, ag_bytes: int, device: torch.device
-                 ) -> list["SymmetricWorkspace"]:
+    def emulated(cls, size: int, *, rs_bytes: int, ag_bytes: int, device: torch.device,
+                 emb_bytes: int = 0, ce_bytes: int = 0) -> list["SymmetricWorkspace"]:
         rs_bytes, ag_bytes = _align(rs_bytes), _align(ag_bytes)
+        emb_bytes, ce_bytes = _align(emb_bytes, 4096, 0), _align(ce_bytes, 4096, 0)
         dev = torch.device(device)
-        bufs = [torch.zeros(cls.total_bytes(rs_bytes, ag_bytes), dtype=torch.uint8, device=dev)
-                for _ in range(size)]
+        bufs = [torch.zeros(cls.total_bytes(rs_bytes, ag_bytes, emb_bytes, ce_bytes),
+                            dtype=torch.uint8, device=dev) for _ in range(size)]
         ptrs = [b.data_ptr() for b in bufs]
         return [cls(rank=r, size=size, ptrs=ptrs, owner=bufs[r], device=dev, rs_bytes=rs_bytes,
-                    ag_bytes=ag_bytes, opened=[]) for r in range(size)]
+                    ag_bytes=ag_bytes, opened=[], emb_bytes=emb_bytes, ce_bytes=ce_bytes)
+                for r in range(size)]
 
     def close(self) -> None:
         """Unmap every peer buffer (``cudaIpcCloseMemHandle``). Call only after every peer
@@ -127,6 +136,24 @@ class SymmetricWorkspace:
     def ag_shard(self, rank: int, parity: int) -> int:
         return self.ptrs[rank] + FLAG_BYTES + 2 * self.rs_bytes + (parity & 1) * self.ag_bytes
 
+    def emb_slot(self, rank: int, parity: int) -> int:
+        return self.ptrs[rank] + FLAG_BYTES + 2 * (self.rs_bytes + self.ag_bytes) + \
+            (parity & 1) * self.emb_bytes
+
+    def ce_slot(self, rank: int, parity: int) -> int:
+        return self.ptrs[rank] + FLAG_BYTES + 2 * (self.rs_bytes + self.ag_bytes +
+                                                   self.emb_bytes) + (parity & 1) * self.ce_bytes
+
+    def check_emb(self, rows: int, hidden: int) -> None:
+        if rows * hidden * 2 > self.emb_bytes:
+            raise ValueError(f"embedding slot needs {rows * hidden * 2} bytes; workspace has "
+                             f"{self.emb_bytes}")
+
+    def check_ce(self, tokens: int) -> None:
+        if self.size * tokens * 12 > self.ce_bytes:
+            raise ValueError(f"cross-entropy statistics need {self.size * tokens * 12} bytes; "
+                             f"workspace has {self.ce_bytes}")
+
     def check_ag(self, rows: int, cols: int) -> None:
         need = rows * cols * 2
         if need > self.ag_bytes:
@@ -140,8 +167,9 @@ class SymmetricWorkspace:
                              f"{self.rs_bytes}")
 
 
-def _align(n: int, a: int = 1 << 21) -> int:
-    return max(a, (int(n) + a - 1) // a * a)
+def _align(n: int, a: int = 1 << 21, minimum: int | None = None) -> int:
+    up = (int(n) + a - 1) // a * a
+    return max(a if minimum is None else minimum, up)
 
 
 class SymmetricHeap:

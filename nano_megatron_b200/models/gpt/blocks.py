@@ -110,8 +110,11 @@ class TPInfo:
 
     def fused(self, x: torch.Tensor) -> bool:
         """Use the fused AG->GEMM / GEMM->RS kernels for this local row block."""
+        return x.is_cuda and self.fused_rows(x.shape[0])
+
+    def fused_rows(self, rows: int) -> bool:
         return (self.workspace is not None and self.sequence_parallel and self.size > 1 and
-                x.is_cuda and x.shape[0] % 128 == 0)
+                rows % 128 == 0)
 
     def gather(self, x):
         return all_gather_dim0(x, self.group) if self.sequence_parallel and self.size > 1 else x
@@ -231,6 +234,7 @@ class AttentionBlockFn(torch.autograd.Function):
                 y = dropout_fn(y)
             out = h2 + y
         ctx.spec, ctx.mb, ctx.inv_freq = spec, mb, inv_freq
+        ctx.layer = mb.extra.get("layer")
         ctx.params = (w_norm, w_q, w_k, w_v, w_out, b_out)
         ctx.b_qkv = b_qkv
         ctx.dropout_fn = dropout_fn
@@ -261,6 +265,7 @@ class AttentionBlockFn(torch.autograd.Function):
         dqkv = torch.empty_like(qkv)
         dq, dk, dv = _split_qkv(dqkv, mb.seq, mb.batch, hq, hkv, D)
         do = d_ctx.view(mb.seq, mb.batch, hq, D).transpose(0, 1)
+        mb.extra["layer"] = ctx.layer
         spec.core.backward(q, k, v, o, do, lse, dq, dk, dv, mb, ctx.inv_freq)
         del d_ctx
         if not getattr(spec.core, "applies_inverse_rope", True):
@@ -375,21 +380,35 @@ class MLPBlockFn(torch.autograd.Function):
 
 
 class EmbeddingFn(torch.autograd.Function):
-    """Vocab-parallel lookup of sequence-major ids, summed over TP (RS under SP)."""
+    """Vocab-parallel lookup of sequence-major ids, summed over TP (RS under SP).
+
+    With the fused TP workspace the reduce-scatter is a selection done by the lookup
+    itself (each rank stores only the rows of its vocabulary shard into the sequence
+    owner's slot) and the backward reads the dY rows of its shard straight from their
+    owners (:func:`nano_megatron_b200.ops.comm_gemm.embedding_lookup_scatter`)."""
 
     @staticmethod
     def forward(ctx, ids, weight, vstart: int, tp: TPInfo):
-        out = F.embedding(ids, weight.detach(), vstart)
-        out = tp.reduce_out(out)
-        ctx.vstart, ctx.tp, ctx.weight = vstart, tp, weight
+        fused = tp.fused_rows(ids.numel() // max(tp.size, 1)) and weight.shape[1] % 8 == 0
+        if fused:
+            out = CG.embedding_lookup_scatter(tp.workspace, ids, weight.detach(), vstart)
+        else:
+            out = F.embedding(ids, weight.detach(), vstart)
+            out = tp.reduce_out(out)
+        ctx.vstart, ctx.tp, ctx.weight, ctx.fused = vstart, tp, weight, fused
         ctx.save_for_backward(ids)
         return out
 
     @staticmethod
     def backward(ctx, dy):
         (ids,) = ctx.saved_tensors
-        dyg = ctx.tp.gather(dy.reshape(-1, dy.shape[-1]).contiguous())
-        F.embedding_bwd(ids, dyg, main_grad_of(ctx.weight), ctx.vstart)
+        dy2 = dy.reshape(-1, dy.shape[-1]).contiguous()
+        if ctx.fused:
+            CG.embedding_backward_gather(ctx.tp.workspace, ids, dy2, main_grad_of(ctx.weight),
+                                         ctx.vstart)
+        else:
+            dyg = ctx.tp.gather(dy2)
+            F.embedding_bwd(ids, dyg, main_grad_of(ctx.weight), ctx.vstart)
         return None, None, None, None
 
 
@@ -404,13 +423,20 @@ class HeadLossFn(torch.autograd.Function):
         H = h.shape[-1]
         h2 = h.reshape(-1, H)
         xn, rstd = F.rmsnorm(h2, w_norm.detach(), eps)
-        xg = tp.gather(xn)
-        logits = F.linear(xg, w_lm.detach())
-        rows = vocab_parallel_ce_rows(logits, labels, tp.group if tp.size > 1 else None,
-                                      write_grad=True)
+        fused = tp.fused(xn) and w_lm.shape[0] % 8 == 0
+        if fused:
+            # AG -> LM-head GEMM, then the row statistics exchanged by peer stores + flag
+            logits, xg = CG.allgather_gemm(tp.workspace, xn, w_lm.detach())
+            rows = CG.vocab_parallel_ce_rows(tp.workspace, logits, labels,
+                                             tp.workspace.rank * w_lm.shape[0], write_grad=True)
+        else:
+            xg = tp.gather(xn)
+            logits = F.linear(xg, w_lm.detach())
+            rows = vocab_parallel_ce_rows(logits, labels, tp.group if tp.size > 1 else None,
+                                          write_grad=True)
         count = (labels >= 0).sum().to(rows.dtype)
         loss = rows.sum() / count.clamp_min(1.0)
-        ctx.tp, ctx.eps, ctx.params = tp, eps, (w_norm, w_lm)
+        ctx.tp, ctx.eps, ctx.params, ctx.fused = tp, eps, (w_norm, w_lm), fused
         ctx.hshape = h.shape
         ctx.save_for_backward(h2, rstd, xg, logits, count)
         return loss
@@ -422,8 +448,12 @@ class HeadLossFn(torch.autograd.Function):
         alpha = (g.to(torch.float32) / count.clamp_min(1.0).to(torch.float32)).reshape(1)
         if not dlogits.is_cuda:
             alpha = alpha.to(dlogits.dtype) if dlogits.dtype == torch.float64 else alpha
-        dxg = F.linear_dgrad(dlogits, w_lm.detach(), alpha_t=alpha)
+        if ctx.fused:
+            dxn = CG.gemm_reduce_scatter(ctx.tp.workspace, dlogits, w_lm.detach(), b_mn=True,
+                                         alpha_t=alpha)
+        else:
+            dxg = F.linear_dgrad(dlogits, w_lm.detach(), alpha_t=alpha)
+            dxn = ctx.tp.reduce_in_grad(dxg)
         F.linear_wgrad(dlogits, xg, main_grad_of(w_lm), alpha_t=alpha)
-        dxn = ctx.tp.reduce_in_grad(dxg)
         dh = F.rmsnorm_bwd(h2, w_norm.detach(), dxn, rstd, main_grad_of(w_norm))
         return dh.view(ctx.hshape), None, None, None, None, None

@@ -147,6 +147,7 @@ class GPTLayer(nn.Module):
         b_gu = (m.gate_proj.bias, m.up_proj.bias) if m.gate_proj.bias is not None else None
 
         def attn(x):
+            mb.extra["layer"] = self.layer_index    # context parallelism keys its K/V slot
             return B.AttentionBlockFn.apply(
                 x, self.input_norm.weight, a.q_proj.weight, a.k_proj.weight, a.v_proj.weight,
                 a.out_proj.weight, a.out_proj.bias, attn_spec, mb, inv_freq, drop_a, b_qkv)

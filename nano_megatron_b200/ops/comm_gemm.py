@@ -20,7 +20,7 @@ from __future__ import annotations
 
 import torch
 
-from nano_megatron_b200.distributed.symmetric import CH_AG, CH_RS
+from nano_megatron_b200.distributed.symmetric import CH_AG, CH_CE, CH_EMB, CH_RS
 
 from ._ext import lib
 
@@ -28,8 +28,10 @@ EPI = {"bf16": 0, "rope": 3, "swiglu": 2}
 
 
 def rs_issue(ws, a: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,
-             n_out: int | None = None) -> tuple[int, int]:
-    """GEMM with the peer epilogue + signal. Returns (rows_per_rank, n_out)."""
+             n_out: int | None = None, alpha_t: torch.Tensor | None = None
+             ) -> tuple[int, int]:
+    """GEMM with the peer epilogue + signal. Returns (rows_per_rank, n_out). ``alpha_t``:
+    optional fp32 device scalar multiplying the product."""
     M = a.shape[0]
     if M % ws.size:
         raise ValueError(f"rows {M} not divisible by TP size {ws.size}")
@@ -38,7 +40,7 @@ def rs_issue(ws, a: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,
     ws.check_rs(rows, n)
     lib().gemm_tc_rs(a, False, b, b_mn, [ws.rs_staging(r, 0) for r in range(ws.size)],
                      [ws.rs_staging(r, 1) for r in range(ws.size)], rows, n, ws.rank,
-                     ws.epoch_ptr(CH_RS), ws.status)
+                     ws.epoch_ptr(CH_RS), ws.status, alpha_t)
     lib().peer_signal(ws.signal_targets(CH_RS), ws.epoch_ptr(CH_RS))
     return rows, n
 
@@ -50,8 +52,9 @@ def rs_finish(ws, out: torch.Tensor, residual: torch.Tensor | None = None) -> No
 
 def gemm_reduce_scatter(ws, a: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,
                         residual: torch.Tensor | None = None,
-                        out: torch.Tensor | None = None) -> torch.Tensor:
-    rows, n = rs_issue(ws, a, b, b_mn=b_mn)
+                        out: torch.Tensor | None = None,
+                        alpha_t: torch.Tensor | None = None) -> torch.Tensor:
+    rows, n = rs_issue(ws, a, b, b_mn=b_mn, alpha_t=alpha_t)
     if out is None:
         out = torch.empty(rows, n, device=a.device, dtype=torch.bfloat16)
     rs_finish(ws, out, residual)
@@ -101,3 +104,78 @@ def allgather_gemm(ws, x_local: torch.Tensor, b: torch.Tensor, *, b_mn: bool = F
     ag_issue(ws, x_local)
     ag_finish(ws, x_local, b, out, b_mn=b_mn, epi=epi, xfull=xfull, **kw)
     return out, xfull
+
+
+# ---------------------------------------------------------------- embedding (C3)
+def embedding_issue(ws, ids: torch.Tensor, weight: torch.Tensor, vstart: int) -> int:
+    """Store the rows of this vocabulary shard into the sequence owners' slots + signal.
+    ``ids``: every token of the TP group's block, sequence-major. Returns rows per rank."""
+    T = ids.numel()
+    if T % ws.size:
+        raise ValueError(f"{T} tokens not divisible by TP size {ws.size}")
+    R = T // ws.size
+    ws.check_emb(R, weight.shape[1])
+    lib().tp_embedding_scatter(ids, weight, vstart, R, [ws.emb_slot(r, 0) for r in range(ws.size)],
+                               [ws.emb_slot(r, 1) for r in range(ws.size)], ws.epoch_ptr(CH_EMB))
+    lib().peer_signal(ws.signal_targets(CH_EMB), ws.epoch_ptr(CH_EMB))
+    return R
+
+
+def embedding_finish(ws, out: torch.Tensor) -> None:
+    lib().tp_embedding_collect(ws.emb_slot(ws.rank, 0), ws.emb_slot(ws.rank, 1), out, ws.size,
+                               ws.flags(ws.rank, CH_EMB), ws.epoch_ptr(CH_EMB), ws.status)
+
+
+def embedding_lookup_scatter(ws, ids: torch.Tensor, weight: torch.Tensor,
+                             vstart: int) -> torch.Tensor:
+    """Vocabulary-parallel lookup fused with the sequence-parallel reduce-scatter: this
+    rank's [T / TP, H] rows of the embedding output."""
+    R = embedding_issue(ws, ids, weight, vstart)
+    out = torch.empty(R, weight.shape[1], device=weight.device, dtype=weight.dtype)
+    embedding_finish(ws, out)
+    return out
+
+
+def embedding_bwd_finish(ws, ids: torch.Tensor, dy_local: torch.Tensor, grad: torch.Tensor,
+                         vstart: int) -> None:
+    R, H = dy_local.shape
+    lib().tp_embedding_bwd_gather(ids, [ws.ag_shard(r, 0) for r in range(ws.size)],
+                                  [ws.ag_shard(r, 1) for r in range(ws.size)], R, H, grad,
+                                  vstart, ws.flags(ws.rank, CH_AG), ws.epoch_ptr(CH_AG),
+                                  ws.status)
+
+
+def embedding_backward_gather(ws, ids: torch.Tensor, dy_local: torch.Tensor,
+                              grad: torch.Tensor, vstart: int) -> None:
+    """Embedding backward fused with the sequence-parallel all-gather of dY: publish this
+    rank's dY rows, then add every token of this vocabulary shard into ``grad`` (fp32)
+    reading its dY row from the owning rank."""
+    ag_issue(ws, dy_local)
+    embedding_bwd_finish(ws, ids, dy_local, grad, vstart)
+
+
+# ---------------------------------------------------------------- cross-entropy (C6)
+def ce_issue(ws, logits: torch.Tensor, labels: torch.Tensor, vstart: int) -> None:
+    ws.check_ce(logits.shape[0])
+    lib().tp_ce_stats_scatter(logits, labels, vstart, ws.rank,
+                              [ws.ce_slot(r, 0) for r in range(ws.size)],
+                              [ws.ce_slot(r, 1) for r in range(ws.size)], ws.epoch_ptr(CH_CE))
+    lib().peer_signal(ws.signal_targets(CH_CE), ws.epoch_ptr(CH_CE))
+
+
+def ce_finish(ws, logits: torch.Tensor, labels: torch.Tensor, vstart: int,
+              write_grad: bool) -> torch.Tensor:
+    loss_row = torch.empty(logits.shape[0], device=logits.device, dtype=torch.float32)
+    lib().tp_ce_finish_gather(logits, labels, vstart, ws.ce_slot(ws.rank, 0),
+                              ws.ce_slot(ws.rank, 1), ws.size, loss_row, write_grad,
+                              ws.flags(ws.rank, CH_CE), ws.epoch_ptr(CH_CE), ws.status)
+    return loss_row
+
+
+def vocab_parallel_ce_rows(ws, logits: torch.Tensor, labels: torch.Tensor, vstart: int,
+                           write_grad: bool) -> torch.Tensor:
+    """Per-row loss of the vocabulary-parallel cross-entropy; the row statistics travel by
+    peer stores + flag instead of a collective. With ``write_grad`` the local logits are
+    overwritten by d loss_row / d logits."""
+    ce_issue(ws, logits, labels, vstart)
+    return ce_finish(ws, logits, labels, vstart, write_grad)

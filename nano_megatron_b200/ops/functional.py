@@ -266,17 +266,28 @@ def ce_finish(logits: torch.Tensor, labels: torch.Tensor, vstart: int, all_stats
 
 
 # ------------------------------------------------------------------ attention
+def _pull_args(pull) -> dict:
+    """``pull`` = (source address, destination tensor, flag address, epoch address): the
+    attention kernel copies that ring block from the owner GPU into the destination while
+    it computes (context parallelism); None = no pull."""
+    if pull is None:
+        return {}
+    src, dst, flag, epoch = pull
+    return {"pull_src": int(src), "pull_dst": dst, "pull_flag": int(flag),
+            "pull_epoch": int(epoch)}
+
+
 def flash_fwd(q, k, v, o, lse, scale: float, causal: bool, q_offset: int = 0,
-              k_offset: int = 0) -> None:
+              k_offset: int = 0, pull=None) -> None:
     """tcgen05/TMEM flash-attention forward into ``o`` ([B,S,H,D] view) and ``lse``."""
     from ._ext import status_word
 
     lib().flash_attn_fwd_tc(q, k, v, o, lse, scale, causal, q_offset, k_offset,
-                            status_word(q.device))
+                            status_word(q.device), **_pull_args(pull))
 
 
 def attention_fwd(q, k, v, *, causal: bool, q_offset: int = 0, k_offset: int = 0,
-                  softmax_scale: float | None = None):
+                  softmax_scale: float | None = None, pull=None):
     """q [B,Sq,Hq,D], k/v [B,Sk,Hkv,D] (strided views). Returns (o [B,Sq,Hq,D], lse).
 
     ``lse`` is base-2 (log2 of the softmax denominator of scaled scores)."""
@@ -285,7 +296,7 @@ def attention_fwd(q, k, v, *, causal: bool, q_offset: int = 0, k_offset: int = 0
     if _cuda(q):
         o = torch.empty(B, Sq, Hq, D, device=q.device, dtype=q.dtype)
         lse = torch.empty(B, Hq, Sq, device=q.device, dtype=torch.float32)
-        flash_fwd(q, k, v, o, lse, scale, causal, q_offset, k_offset)
+        flash_fwd(q, k, v, o, lse, scale, causal, q_offset, k_offset, pull=pull)
         return o, lse
     o, lse = _attn_math(q, k, v, causal, q_offset, k_offset, scale)
     return o.to(q.dtype), lse
@@ -311,7 +322,7 @@ def _attn_math(q, k, v, causal, q_offset, k_offset, scale):
 def attention_bwd(q, k, v, o, do, lse, dq, dk, dv, *, causal: bool, q_offset: int = 0,
                   k_offset: int = 0, softmax_scale: float | None = None,
                   q_pos: torch.Tensor | None = None, k_pos: torch.Tensor | None = None,
-                  inv_freq: torch.Tensor | None = None) -> None:
+                  inv_freq: torch.Tensor | None = None, pull=None) -> None:
     """Writes dq/dk/dv (strided views). With ``q_pos``/``k_pos`` the inverse RoPE
     is applied to dq/dk on the way out (gradients w.r.t. pre-rotation q/k)."""
     B, Sq, Hq, D = q.shape
@@ -324,7 +335,8 @@ def attention_bwd(q, k, v, o, do, lse, dq, dk, dv, *, causal: bool, q_offset: in
         L = lib()
         L.flash_attn_bwd_prep(o, do, delta, dq_acc)
         L.flash_attn_bwd_tc_kv(q, k, v, do, lse, delta, dq_acc, dk, dv, scale, causal,
-                               q_offset, k_offset, k_pos, inv_freq, status_word(q.device))
+                               q_offset, k_offset, k_pos, inv_freq, status_word(q.device),
+                               **_pull_args(pull))
         L.flash_attn_bwd_dq_convert(dq_acc, dq, q_pos, inv_freq)
         return
     # Explicit flash-attention backward using the given (global) log-sum-exp, so a

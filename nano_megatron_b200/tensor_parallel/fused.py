@@ -4,7 +4,9 @@ Created once per TP group (a collective over that group) when training on CUDA
 with TP > 1, sequence parallelism and ``kernels.fused_tp_comm``. Sizes follow
 from the config: each rank's local row block is R = micro_batch * S / (CP * TP)
 rows of the hidden size H; reduce-scatter staging holds TP slots of [R, H]
-(two parities), the all-gather slot one [R, H] shard (two parities).
+(two parities), the all-gather slot one [R, H] shard (two parities), the embedding
+slot [R, H] rows (two parities) and the cross-entropy slots TP x (TP * R) x 3 fp32
+row statistics (two parities).
 """
 
 from __future__ import annotations
@@ -32,8 +34,10 @@ def attach_tp_workspace(model: torch.nn.Module, config, parallel, device: torch.
     from nano_megatron_b200.models.gpt.model import GPTModel
 
     R, H = fused_tp_rows(config, parallel), int(config.model.hidden_size)
-    ws = SymmetricWorkspace.create(parallel.tp, rs_bytes=parallel.tp.size * R * H * 2,
-                                   ag_bytes=R * H * 2, device=device)
+    tp = parallel.tp.size
+    ws = SymmetricWorkspace.create(parallel.tp, rs_bytes=tp * R * H * 2, ag_bytes=R * H * 2,
+                                   emb_bytes=R * H * 2, ce_bytes=tp * (tp * R) * 12,
+                                   device=device)
     for m in model.modules():
         if isinstance(m, GPTModel):
             m.tp_workspace = ws

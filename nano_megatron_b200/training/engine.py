@@ -30,6 +30,7 @@ class TrainingComponents:
     built: object
     data_parallel: object
     tp_workspace: object = None
+    cp_heaps: list = None
 
     def close(self, trainer=None, *, keep_runtime: bool = False) -> None:
         """Ordered teardown: graphs, peer mappings, own buffer, subgroups and (unless
@@ -43,6 +44,14 @@ class TrainingComponents:
         heaps = [(replica, dp.replica_group)] if replica is not None else []
         if replica is not None:
             dp.replica = None
+        heaps += list(self.cp_heaps or [])
+        self.cp_heaps = []
+        from nano_megatron_b200.models.gpt.model import GPTModel
+
+        for m in self.model.modules():
+            core = getattr(m, "cp_attention", None) if isinstance(m, GPTModel) else None
+            if core is not None and hasattr(core, "detach"):
+                core.detach()
         shutdown(trainer=trainer, model=self.model, workspace=ws, parallel=self.parallel,
                  runtime=None if keep_runtime else self.runtime,
                  device=getattr(self.runtime, "device", None), heaps=heaps)
@@ -76,4 +85,13 @@ def build_training_components(config, runtime) -> TrainingComponents:
     from nano_megatron_b200.tensor_parallel.fused import attach_tp_workspace
 
     ws = attach_tp_workspace(model, config, parallel, torch.device(runtime.device))
-    return TrainingComponents(runtime, parallel, rng, model, built, strategy, ws)
+    from nano_megatron_b200.context_parallel.fused import attach_cp_heap
+    from nano_megatron_b200.models.gpt.model import GPTModel
+
+    cores = {id(m.cp_attention): m.cp_attention for m in model.modules()
+             if isinstance(m, GPTModel) and m.cp_attention is not None}
+    cp_heaps = [attach_cp_heap(model, config, parallel, core, torch.device(runtime.device))
+                for core in cores.values()]
+    comps = TrainingComponents(runtime, parallel, rng, model, built, strategy, ws)
+    comps.cp_heaps = [(h, parallel.cp) for h in cp_heaps if h is not None]
+    return comps

@@ -155,3 +155,77 @@ def test_missing_peer_times_out_with_status():
     y = torch.randn(64, 64, device=DEV) @ torch.randn(64, 64, device=DEV)  # context still fine
     torch.cuda.synchronize()
     assert torch.isfinite(y).all()
+
+
+def _aux_ws(tp, R, H):
+    return SymmetricWorkspace.emulated(tp, rs_bytes=2 * MB, ag_bytes=R * H * 2, device=DEV,
+                                       emb_bytes=R * H * 2, ce_bytes=tp * tp * R * 12)
+
+
+@pytest.mark.parametrize("tp", [2, 4])
+def test_embedding_lookup_scatter_matches_full_lookup(tp):
+    """Each rank stores only the rows of its vocabulary shard into the sequence owners'
+    slots; every rank's output equals a plain lookup of its own tokens."""
+    torch.manual_seed(20 + tp)
+    V, H, R = 512, 256, 128
+    Vl = V // tp
+    ws = _aux_ws(tp, R, H)
+    w = torch.randn(V, H, device=DEV).bfloat16()
+    for it in range(3):                    # parities and epoch advance
+        ids = torch.randint(0, V, (R * tp,), device=DEV)
+        for r in range(tp):
+            CG.embedding_issue(ws[r], ids, w[r * Vl:(r + 1) * Vl].contiguous(), r * Vl)
+        outs = [torch.empty(R, H, device=DEV, dtype=torch.bfloat16) for _ in range(tp)]
+        for r in range(tp):
+            CG.embedding_finish(ws[r], outs[r])
+        _ok()
+        for r in range(tp):
+            assert torch.equal(outs[r], w[ids[r * R:(r + 1) * R]]), (it, r)
+
+
+@pytest.mark.parametrize("tp", [2, 4])
+def test_embedding_backward_gather_matches_scatter_add(tp):
+    torch.manual_seed(30 + tp)
+    V, H, R = 512, 256, 128
+    Vl = V // tp
+    ws = _aux_ws(tp, R, H)
+    ids = torch.randint(0, V, (R * tp,), device=DEV)
+    dy = [torch.randn(R, H, device=DEV).bfloat16() for _ in range(tp)]
+    grads = [torch.zeros(Vl, H, device=DEV) for _ in range(tp)]
+    for r in range(tp):
+        CG.ag_issue(ws[r], dy[r])
+    for r in range(tp):
+        CG.embedding_bwd_finish(ws[r], ids, dy[r], grads[r], r * Vl)
+    _ok()
+    ref = torch.zeros(V, H, device=DEV).index_add_(0, ids, torch.cat(dy).float())
+    for r in range(tp):
+        torch.testing.assert_close(grads[r], ref[r * Vl:(r + 1) * Vl], rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("tp", [2, 4])
+def test_vocab_parallel_ce_by_peer_stores_matches_fp32(tp):
+    """Row statistics exchanged by peer stores + flag: loss rows and the in-place
+    softmax - onehot gradient equal fp32 cross-entropy over the full vocabulary."""
+    torch.manual_seed(40 + tp)
+    T, V = 256, 1024
+    Vl = V // tp
+    ws = _aux_ws(tp, T // tp, 64)
+    full = (torch.randn(T, V, device=DEV) * 3).bfloat16()
+    labels = torch.randint(0, V, (T,), device=DEV)
+    labels[::7] = -100
+    for it in range(2):
+        shards = [full[:, r * Vl:(r + 1) * Vl].contiguous() for r in range(tp)]
+        for r in range(tp):
+            CG.ce_issue(ws[r], shards[r], labels, r * Vl)
+        rows = [CG.ce_finish(ws[r], shards[r], labels, r * Vl, write_grad=True)
+                for r in range(tp)]
+        _ok()
+        ref = torch.nn.functional.cross_entropy(full.float(), labels, ignore_index=-100,
+                                                reduction="none")
+        valid = labels >= 0
+        onehot = torch.zeros(T, V, device=DEV)
+        onehot[valid, labels[valid]] = 1.0
+        gref = (full.float().softmax(-1) - onehot) * valid[:, None]
+        for r in range(tp):
+            torch.testing.assert_close(rows[r], ref, rtol=2e-3, atol=2e-3)
+            assert _rel(shards[r], gref[:, r * Vl:(r + 1) * Vl]) < 1e-2, (it, r)

@@ -158,7 +158,8 @@ def test_config_defaults_match(ref):
     theirs = config_to_dict(ref.TrainConfig())
     # fields this framework adds (documented, defaults preserve reference behaviour)
     ours["kernels"].pop("cuda_graphs")
-    ours["kernels"].pop("fused_tp_comm")
+    for extra in ("fused_tp_comm", "fused_dp_comm", "fused_cp_comm"):
+        ours["kernels"].pop(extra)
     ours["context_parallel"].pop("load_balance")
     assert ours == theirs
 
