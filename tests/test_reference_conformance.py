@@ -881,7 +881,8 @@ def test_config_overrides_parse_like_the_reference(ref, overrides, monkeypatch):
 
     a, b = plain(ours), plain(theirs)
     a["kernels"].pop("cuda_graphs", None)
-    a["kernels"].pop("fused_tp_comm", None)
+    for extra in ("fused_tp_comm", "fused_dp_comm", "fused_cp_comm"):
+        a["kernels"].pop(extra, None)
     a["context_parallel"].pop("load_balance", None)
     assert a == b
 
