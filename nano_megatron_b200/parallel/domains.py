@@ -1,8 +1,13 @@
-"""Parameter domains: which replica group reduces each parameter's gradient.
+"""Parameter domains: which replica group sums each parameter's gradient.
 
-Dense parameters reduce over DENSE_REPLICA (dp x ep x cp); expert parameters
-over EXPERT_REPLICA (dp x cp). Registration is by identity and never mutates
-the parameter. Reference: src/nano_megatron/parallel/domains.py:13-243.
+A parameter is either *dense* (identical on every data / expert / context replica: its
+gradient is summed over DENSE_REPLICA = dp x ep x cp) or *expert* (different per EP
+rank: summed over EXPERT_REPLICA = dp x cp). A :class:`ParameterPlacement` records the
+domain, the replica group and whether (and along which dim) the tensor is split over TP;
+the data-parallel buffers cut their buckets per domain and the checkpoint mapping uses the
+shard dim. The registry is keyed by object identity, holds a strong reference to each
+parameter and never modifies one. The public names and the two default groups are the
+reference's (src/nano_megatron/parallel/domains.py).
 """
 
 from __future__ import annotations
@@ -23,18 +28,19 @@ class ParameterDomain(StrEnum):
     def parse(cls, value: "ParameterDomain | str") -> "ParameterDomain":
         if isinstance(value, cls):
             return value
-        try:
-            return cls(str(value).strip().lower())
-        except ValueError as error:
-            raise ValueError(f"unknown parameter domain {value!r}") from error
+        known = {d.value: d for d in cls}
+        if isinstance(value, str) and value.strip().lower() in known:
+            return known[value.strip().lower()]
+        raise ValueError(f"{value!r} names no parameter domain (known: {', '.join(known)})")
 
 
-_DEFAULT_REPLICA = {ParameterDomain.DENSE: GroupKey.DENSE_REPLICA,
-                    ParameterDomain.EXPERT: GroupKey.EXPERT_REPLICA}
+_REPLICA_OF = {ParameterDomain.DENSE: GroupKey.DENSE_REPLICA,
+               ParameterDomain.EXPERT: GroupKey.EXPERT_REPLICA}
 
 
 def default_replica_group(domain: ParameterDomain | str) -> GroupKey:
-    return _DEFAULT_REPLICA[ParameterDomain.parse(domain)]
+    """The group a domain's gradients are summed over unless a placement says otherwise."""
+    return _REPLICA_OF[ParameterDomain.parse(domain)]
 
 
 @dataclass(frozen=True, slots=True)
@@ -47,108 +53,147 @@ class ParameterPlacement:
     def __post_init__(self) -> None:
         object.__setattr__(self, "domain", ParameterDomain.parse(self.domain))
         object.__setattr__(self, "replica_group", normalize_group_key(self.replica_group))
-        if not isinstance(self.tensor_sharded, bool):
-            raise TypeError("tensor_sharded must be a boolean")
-        d = self.tensor_shard_dim
-        if d is not None:
-            if isinstance(d, bool) or not isinstance(d, int) or d < 0:
-                raise ValueError("tensor_shard_dim must be a non-negative integer or null")
-            if not self.tensor_sharded:
-                raise ValueError("tensor_shard_dim requires tensor_sharded=True")
+        if type(self.tensor_sharded) is not bool:
+            raise TypeError(f"tensor_sharded is {self.tensor_sharded!r}, not a bool")
+        dim = self.tensor_shard_dim
+        if dim is None:
+            return
+        if type(dim) is not int or dim < 0:
+            raise ValueError(f"tensor_shard_dim {dim!r} is not a dimension index (int >= 0)")
+        if not self.tensor_sharded:
+            raise ValueError(f"tensor_shard_dim={dim} given for a tensor that is not "
+                             "sharded over TP (set tensor_sharded=True)")
 
     @classmethod
     def for_domain(cls, domain, *, tensor_sharded: bool = False,
                    replica_group: GroupKeyLike | None = None,
                    tensor_shard_dim: int | None = None) -> "ParameterPlacement":
         d = ParameterDomain.parse(domain)
-        return cls(d, tensor_sharded, _DEFAULT_REPLICA[d] if replica_group is None
-                   else replica_group, tensor_shard_dim)
+        group = _REPLICA_OF[d] if replica_group is None else replica_group
+        return cls(d, tensor_sharded, group, tensor_shard_dim)
+
+
+def _resolve(placement, domain, tensor_sharded, replica_group,
+             tensor_shard_dim) -> ParameterPlacement:
+    """One placement from ``register``'s arguments: an explicit placement object, or a
+    domain (positional or keyword, default dense) plus the placement fields."""
+    if isinstance(placement, ParameterPlacement):
+        extras = {"domain": domain is not None, "tensor_sharded": bool(tensor_sharded),
+                  "replica_group": replica_group is not None,
+                  "tensor_shard_dim": tensor_shard_dim is not None}
+        given = [k for k, v in extras.items() if v]
+        if given:
+            raise ValueError("an explicit ParameterPlacement already fixes " +
+                             ", ".join(given) + "; pass one or the other")
+        return placement
+    if placement is not None and domain is not None:
+        raise ValueError(f"domain given twice ({placement!r} positionally, {domain!r} by "
+                         "keyword)")
+    chosen = placement if placement is not None else domain
+    return ParameterPlacement.for_domain(
+        ParameterDomain.DENSE if chosen is None else chosen, tensor_sharded=tensor_sharded,
+        replica_group=replica_group, tensor_shard_dim=tensor_shard_dim)
+
+
+class _Entry:
+    __slots__ = ("param", "placement", "name")
+
+    def __init__(self, param, placement, name) -> None:
+        self.param, self.placement, self.name = param, placement, name
 
 
 class ParameterDomainRegistry:
-    def __init__(self) -> None:
-        self._entries: dict[int, list] = {}  # id -> [param, placement, name]
+    """Placement of every model parameter, looked up by identity."""
 
+    def __init__(self) -> None:
+        self._by_id: dict[int, _Entry] = {}
+
+    def _find(self, parameter: Any) -> _Entry | None:
+        e = self._by_id.get(id(parameter))
+        return e if e is not None and e.param is parameter else None
+
+    def _need(self, parameter: Any) -> _Entry:
+        e = self._find(parameter)
+        if e is None:
+            raise KeyError(f"parameter of shape {tuple(getattr(parameter, 'shape', ()))} has "
+                           "no placement in this registry")
+        return e
+
+    # ------------------------------------------------------------------ registration
     def register(self, parameter: Any, placement=None, *, domain=None, tensor_sharded=False,
                  replica_group=None, tensor_shard_dim=None, name: str | None = None
                  ) -> ParameterPlacement:
+        """Record a parameter's placement. Registering it again is a no-op if the
+        placement agrees (a name may be added later, not changed); a different placement
+        is an error: one tensor has one gradient reduction."""
         if parameter is None:
-            raise TypeError("cannot register None as a parameter")
-        if isinstance(placement, ParameterPlacement):
-            if domain is not None or tensor_sharded or replica_group is not None \
-                    or tensor_shard_dim is not None:
-                raise ValueError("domain/tensor_sharded/replica_group cannot accompany an "
-                                 "explicit placement")
-            resolved = placement
-        else:
-            if placement is not None and domain is not None:
-                raise ValueError("parameter domain was supplied both positionally and by keyword")
-            resolved = ParameterPlacement.for_domain(
-                domain or placement or ParameterDomain.DENSE, tensor_sharded=tensor_sharded,
-                replica_group=replica_group, tensor_shard_dim=tensor_shard_dim)
-        entry = self._entries.get(id(parameter))
-        if entry is not None:
-            if entry[0] is not parameter:
-                raise RuntimeError("parameter identity collision in domain registry")
-            if entry[1] != resolved:
-                raise ValueError(f"parameter is already registered with {entry[1]}, "
-                                 f"cannot use {resolved}")
-            if name is not None and entry[2] not in (None, name):
-                raise ValueError(f"parameter is already registered as {entry[2]!r}, "
-                                 f"cannot rename to {name!r}")
-            entry[2] = entry[2] or name
-            return entry[1]
-        self._entries[id(parameter)] = [parameter, resolved, name]
-        return resolved
+            raise TypeError("register() got None instead of a parameter")
+        want = _resolve(placement, domain, tensor_sharded, replica_group, tensor_shard_dim)
+        old = self._by_id.get(id(parameter))
+        if old is None:
+            self._by_id[id(parameter)] = _Entry(parameter, want, name)
+            return want
+        if old.param is not parameter:     # only if an entry outlived its object's id
+            raise RuntimeError("stale registry entry shares this parameter's id")
+        label = old.name or name or "parameter"
+        if old.placement != want:
+            raise ValueError(f"{label} is already registered as {old.placement}; "
+                             f"refusing {want}")
+        if name is not None and old.name is not None and old.name != name:
+            raise ValueError(f"cannot rename {old.name!r} to {name!r}")
+        if old.name is None:
+            old.name = name
+        return old.placement
 
     def register_module(self, module: Any, placement=None, *, prefix: str = "", **kwargs
                         ) -> None:
+        """Register every parameter of ``module`` under ``prefix + its dotted name``."""
         for pname, p in module.named_parameters():
-            self.register(p, placement, name=f"{prefix}{pname}", **kwargs)
+            self.register(p, placement, name=prefix + pname, **kwargs)
 
     def unregister(self, parameter: Any) -> None:
-        self._entries.pop(id(parameter), None)
+        if self._find(parameter) is not None:
+            del self._by_id[id(parameter)]
 
-    def _entry(self, parameter: Any) -> list:
-        entry = self._entries.get(id(parameter))
-        if entry is None or entry[0] is not parameter:
-            raise KeyError("parameter is not registered in the domain registry")
-        return entry
-
+    # ------------------------------------------------------------------ queries
     def placement(self, parameter: Any) -> ParameterPlacement:
-        return self._entry(parameter)[1]
+        return self._need(parameter).placement
 
     def get(self, parameter: Any, default: Any = None):
-        entry = self._entries.get(id(parameter))
-        return default if entry is None or entry[0] is not parameter else entry[1]
+        e = self._find(parameter)
+        return default if e is None else e.placement
 
     def domain(self, parameter: Any) -> ParameterDomain:
-        return self.placement(parameter).domain
+        return self._need(parameter).placement.domain
 
     def replica_group(self, parameter: Any) -> GroupKeyLike:
-        return self.placement(parameter).replica_group
+        return self._need(parameter).placement.replica_group
 
     def name(self, parameter: Any) -> str | None:
-        return self._entry(parameter)[2]
+        return self._need(parameter).name
 
     def parameters(self, domain=None) -> tuple[Any, ...]:
-        d = None if domain is None else ParameterDomain.parse(domain)
-        return tuple(e[0] for e in self._entries.values() if d is None or e[1].domain is d)
+        keep = None if domain is None else ParameterDomain.parse(domain)
+        return tuple(e.param for e in self._by_id.values()
+                     if keep is None or e.placement.domain is keep)
 
     def grouped_parameters(self) -> dict[ParameterDomain, tuple[Any, ...]]:
-        return {d: self.parameters(d) for d in ParameterDomain if self.parameters(d)}
+        out: dict[ParameterDomain, list] = {}
+        for e in self._by_id.values():
+            out.setdefault(e.placement.domain, []).append(e.param)
+        return {d: tuple(out[d]) for d in ParameterDomain if d in out}
 
     def items(self) -> Iterator[tuple[Any, ParameterPlacement]]:
-        return ((e[0], e[1]) for e in self._entries.values())
+        return iter([(e.param, e.placement) for e in self._by_id.values()])
 
     def validate_complete(self, parameters: Iterable[Any]) -> None:
-        missing = [p for p in parameters if id(p) not in self._entries]
-        if missing:
-            raise ValueError(f"{len(missing)} parameter(s) have no registered domain")
+        """Every given parameter must have a placement (the DP buffers need one each)."""
+        count = sum(1 for p in parameters if self._find(p) is None)
+        if count:
+            raise ValueError(f"{count} parameter(s) have no registered domain")
 
     def __contains__(self, parameter: object) -> bool:
-        e = self._entries.get(id(parameter))
-        return e is not None and e[0] is parameter
+        return self._find(parameter) is not None
 
     def __len__(self) -> int:
-        return len(self._entries)
+        return len(self._by_id)
