@@ -43,76 +43,89 @@ class GenerationResult:
     stop_reason: str
 
     def to_dict(self) -> dict[str, object]:
-        return {"completion": self.completion, "generated_token_ids":
-                list(self.generated_token_ids), "prompt": self.prompt,
-                "stop_reason": self.stop_reason, "text": self.text,
-                "token_ids": list(self.token_ids)}
+        """JSON form (the CLI's output line): every field, keys sorted, tuples as lists."""
+        out = {}
+        for name in sorted(self.__slots__):
+            v = getattr(self, name)
+            out[name] = list(v) if isinstance(v, tuple) else v
+        return out
 
 
 def resolve_device(value) -> torch.device:
-    if isinstance(value, torch.device):
-        dev = value
-    elif value == "auto":
-        dev = torch.device("cuda" if torch.cuda.is_available() else "cpu")
-    else:
-        try:
-            dev = torch.device(value)
-        except (TypeError, RuntimeError) as e:
-            raise ValueError(f"invalid generation device {value!r}: {e}") from e
-    if dev.type == "cuda" and not torch.cuda.is_available():
-        raise RuntimeError("CUDA generation was requested but CUDA is unavailable")
+    """``"auto"`` (CUDA when present), a device string or a ``torch.device``; only CPU and
+    CUDA are accepted, and CUDA only where it exists."""
+    if value == "auto":
+        value = "cuda" if torch.cuda.is_available() else "cpu"
+    try:
+        dev = value if isinstance(value, torch.device) else torch.device(value)
+    except (TypeError, RuntimeError) as e:
+        raise ValueError(f"cannot parse generation device {value!r} ({e})") from e
     if dev.type not in ("cpu", "cuda"):
-        raise ValueError(f"generation device must be CPU or CUDA, got {dev}")
+        raise ValueError(f"generation runs on cpu or cuda, not {dev.type}")
+    if dev.type == "cuda" and not torch.cuda.is_available():
+        raise RuntimeError(f"device {dev} requested, but this process sees no CUDA device")
     return dev
 
 
 def resolve_dtype(value: str, *, artifact: InferenceArtifact, device: torch.device):
+    """``"auto"``: fp32 on CPU, the artifact's weight dtype on CUDA; else a named dtype
+    (fp16 only on CUDA)."""
     if value == "auto":
-        return torch.float32 if device.type == "cpu" else artifact.weight_dtype
-    if value not in _DTYPES:
-        raise ValueError(f"generation dtype must be auto or one of {sorted(_DTYPES)}")
-    if device.type == "cpu" and value == "float16":
-        raise ValueError("float16 generation is not supported on CPU; use float32 or bfloat16")
-    return _DTYPES[value]
+        return artifact.weight_dtype if device.type == "cuda" else torch.float32
+    dt = _DTYPES.get(value)
+    if dt is None:
+        raise ValueError(f"generation dtype {value!r}: use auto, " + ", ".join(sorted(_DTYPES)))
+    if dt is torch.float16 and device.type == "cpu":
+        raise ValueError("float16 generation needs CUDA; on CPU use float32 or bfloat16")
+    return dt
 
 
 def load_model_for_generation(artifact_path, *, device="auto", dtype: str = "auto"):
-    """Load a validated artifact into one ordinary, non-distributed GPT model."""
+    """Artifact -> one single-device ``GPTModel`` in eval mode on ``device``."""
     from nano_megatron_b200.models.gpt.model import GPTModel
 
     artifact = load_inference_artifact(artifact_path)
     dev = resolve_device(device)
-    dt = resolve_dtype(dtype, artifact=artifact, device=dev)
     model = GPTModel(artifact.model_config, parallel=local_parallel())
-    model.to(dtype=dt)
+    model.to(dtype=resolve_dtype(dtype, artifact=artifact, device=dev))
     model.load_state_dict(artifact.state_dict, strict=True)
-    model.to(device=dev)
-    model.eval()
-    if artifact.model_config.tie_embeddings and \
-            model.embedding.weight is not model.lm_head.weight:
-        raise RuntimeError("loaded GPT model did not preserve tied embedding identity")
+    model.to(device=dev).eval()
+    tied = artifact.model_config.tie_embeddings
+    if tied and model.lm_head.weight is not model.embedding.weight:
+        raise RuntimeError("tied artifact loaded with separate embedding and LM-head tensors")
     return artifact, model, dev
 
 
 def sample_next_token(logits: torch.Tensor, *, temperature: float, top_p: float, top_k: int,
                       generator: torch.Generator) -> int:
-    scores = logits.detach().float().cpu()
+    """Next token id from one row of logits.
+
+    Temperature 0 is greedy. Otherwise the scores are divided by the temperature, all but
+    the ``top_k`` best are masked (k = 0: no cut), then the nucleus cut keeps, in
+    descending order, every token whose preceding probability mass is at most ``top_p``,
+    and one token is drawn from the softmax with ``generator``. These are the reference's
+    steps in its order (src/nano_megatron/inference/generation.py:120-148): the same
+    seed then picks the same tokens from the same logits.
+    """
+    z = logits.detach().to(device="cpu", dtype=torch.float32)
     if temperature == 0.0:
-        return int(scores.argmax().item())
-    scores.div_(temperature)
+        return int(torch.argmax(z))
+    z = z / temperature
+    neg = float("-inf")
     if top_k:
-        kth = torch.topk(scores, min(top_k, scores.numel())).values[-1]
-        scores.masked_fill_(scores < kth, float("-inf"))
+        floor = z.topk(min(top_k, z.numel())).values[-1]
+        z = torch.where(z < floor, torch.full_like(z, neg), z)
     if top_p < 1.0:
-        s_sorted, order = torch.sort(scores, descending=True)
-        p_sorted = torch.softmax(s_sorted, dim=-1)
-        drop = torch.cumsum(p_sorted, dim=-1) - p_sorted > top_p
-        s_sorted.masked_fill_(drop, float("-inf"))
-        scores = torch.full_like(scores, float("-inf")).scatter_(0, order, s_sorted)
-    probs = torch.softmax(scores, dim=-1)
-    if not torch.isfinite(probs).all() or float(probs.sum()) <= 0.0:
-        raise RuntimeError("sampling produced an invalid probability distribution")
-    return int(torch.multinomial(probs, 1, generator=generator).item())
+        ranked, order = z.sort(descending=True)
+        p = ranked.softmax(-1)
+        mass_before = p.cumsum(-1) - p
+        ranked = ranked.masked_fill(mass_before > top_p, neg)
+        z = torch.full_like(z, neg).scatter(0, order, ranked)
+    probs = z.softmax(-1)
+    if not bool(torch.isfinite(probs).all()) or float(probs.sum()) <= 0.0:
+        raise RuntimeError("no token left to sample: the filtered distribution is empty or "
+                           "not finite")
+    return int(torch.multinomial(probs, 1, generator=generator))
 
 
 class KVCacheDecoder:
@@ -204,29 +217,36 @@ class KVCacheDecoder:
         return self._lin(y, m.lm_head.weight)[0, :m.original_vocab_size]
 
 
+def _real(v) -> bool:
+    return isinstance(v, (int, float)) and not isinstance(v, bool)
+
+
+def _whole(v) -> bool:
+    return isinstance(v, int) and not isinstance(v, bool)
+
+
 def _check_args(prompt, max_new_tokens, temperature, top_p, top_k, seed, add_bos) -> None:
-    if not isinstance(prompt, str):
-        raise TypeError("prompt must be a string")
-    if isinstance(max_new_tokens, bool) or not isinstance(max_new_tokens, int):
-        raise TypeError("max_new_tokens must be an integer")
-    if max_new_tokens < 1:
-        raise ValueError("max_new_tokens must be positive")
-    if isinstance(temperature, bool) or not isinstance(temperature, (int, float)):
-        raise TypeError("temperature must be a number")
-    if not math.isfinite(float(temperature)) or temperature < 0.0:
-        raise ValueError("temperature must be finite and non-negative")
-    if isinstance(top_p, bool) or not isinstance(top_p, (int, float)):
-        raise TypeError("top_p must be a number")
-    if not 0.0 < float(top_p) <= 1.0:
-        raise ValueError("top_p must be in (0, 1]")
-    if isinstance(top_k, bool) or not isinstance(top_k, int):
-        raise TypeError("top_k must be an integer")
-    if top_k < 0:
-        raise ValueError("top_k must be non-negative")
-    if isinstance(seed, bool) or not isinstance(seed, int) or seed < 0:
-        raise ValueError("seed must be a non-negative integer")
-    if not isinstance(add_bos, bool):
-        raise TypeError("add_bos must be a boolean")
+    """Argument checks of ``generate_text``: TypeError for a wrong kind, ValueError for a
+    value out of range."""
+    kinds = [("prompt", prompt, lambda v: isinstance(v, str), "text"),
+             ("max_new_tokens", max_new_tokens, _whole, "an int"),
+             ("temperature", temperature, _real, "a number"),
+             ("top_p", top_p, _real, "a number"),
+             ("top_k", top_k, _whole, "an int"),
+             ("add_bos", add_bos, lambda v: isinstance(v, bool), "a bool")]
+    for name, value, ok, want in kinds:
+        if not ok(value):
+            raise TypeError(f"{name} must be {want}, got {value!r}")
+    ranges = [("max_new_tokens", max_new_tokens >= 1, ">= 1"),
+              ("temperature", math.isfinite(float(temperature)) and temperature >= 0.0,
+               "finite and >= 0"),
+              ("top_p", 0.0 < float(top_p) <= 1.0, "in (0, 1]"),
+              ("top_k", top_k >= 0, ">= 0")]
+    for name, ok, want in ranges:
+        if not ok:
+            raise ValueError(f"{name} must be {want}")
+    if not _whole(seed) or seed < 0:
+        raise ValueError(f"seed must be an int >= 0, got {seed!r}")
 
 
 def generate_text(artifact: InferenceArtifact, model, prompt: str, *, device: torch.device,
@@ -237,11 +257,11 @@ def generate_text(artifact: InferenceArtifact, model, prompt: str, *, device: to
     tok = artifact.tokenizer
     prompt_ids = tok.encode(prompt, add_bos=add_bos, add_eos=False)
     if not prompt_ids:
-        raise ValueError("prompt produces no tokens; enable BOS or provide non-empty text")
+        raise ValueError("the prompt encodes to zero tokens: give some text or add_bos=True")
     limit = artifact.model_config.seq_length
     if len(prompt_ids) + max_new_tokens > limit:
-        raise ValueError("prompt plus requested generation exceeds model sequence length: "
-                         f"{len(prompt_ids)} + {max_new_tokens} > {limit}")
+        raise ValueError(f"{len(prompt_ids)} prompt tokens + {max_new_tokens} new tokens "
+                         f"exceeds model sequence length {limit}")
     ids, new = list(prompt_ids), []
     gen = torch.Generator(device="cpu").manual_seed(seed)
     stop = "length"

@@ -1,17 +1,30 @@
-"""Tokenizer protocol, special tokens and training configuration.
+"""What the training stack needs from a tokenizer, and the byte-BPE training settings.
 
-Same contract as the reference (src/nano_megatron/tokenizer/base.py:21-157):
-four control-form special tokens (``<|name|>``) in the fixed order unk, bos,
-eos, pad (ids 0..3 for freshly trained artifacts).
+The model only sees integer ids, so a tokenizer is anything with the small interface of
+:class:`TextTokenizer` (no torch involved; usable in plain preprocessing scripts).
+
+Special tokens have four roles: unknown, begin-of-sequence, end-of-text and padding. Their
+text must look like a control token, ``<|name|>`` with an ASCII name, so it can never be
+produced by ordinary text through the byte-level alphabet; they are handed to the BPE
+trainer in the order unk, bos, eos, pad, which gives them ids 0..3 in a freshly trained
+vocabulary. The default strings, that order and the control form are the reference's
+(src/nano_megatron/tokenizer/base.py), so artifacts trained by either framework load in
+the other.
 """
 
 from __future__ import annotations
 
 import re
-from dataclasses import dataclass, field
+from dataclasses import astuple, dataclass, field, fields
 from typing import Protocol, Sequence
 
 CONTROL_TOKEN = re.compile(r"^<\|[A-Za-z0-9_.:-]+\|>$")
+
+
+def _byte_alphabet() -> set[str]:
+    from tokenizers.pre_tokenizers import ByteLevel
+
+    return set(ByteLevel.alphabet())
 
 
 class TextTokenizer(Protocol):
@@ -38,30 +51,37 @@ class SpecialTokens:
     pad: str = "<|pad|>"
 
     def __post_init__(self) -> None:
-        from tokenizers.pre_tokenizers import ByteLevel
-
-        values = self.as_dict()
-        for role, tok in values.items():
-            if not isinstance(tok, str):
-                raise TypeError(f"special token {role!r} must be a string")
-            if tok == "":
-                raise ValueError(f"special token {role!r} cannot be empty")
-            if CONTROL_TOKEN.fullmatch(tok) is None:
-                raise ValueError(f"special token {role!r} must use the reserved control form "
-                                 "'<|name|>' with an ASCII name")
-        if len(set(values.values())) != len(values):
-            raise ValueError("unk, bos, eos and pad special tokens must be unique")
-        alphabet = set(ByteLevel.alphabet())
-        clash = [r for r, t in values.items() if t in alphabet]
-        if clash:
-            raise ValueError("special tokens must not overlap single-symbol byte-level alphabet "
-                             "entries: " + ", ".join(clash))
+        roles = self.as_dict()
+        for role, text in roles.items():
+            if not isinstance(text, str):
+                raise TypeError(f"{role} token is a {type(text).__name__}, not text")
+            if not CONTROL_TOKEN.fullmatch(text):
+                raise ValueError(f"{role} token {text!r} is not of the form '<|name|>' "
+                                 "(name: letters, digits, '_', '.', ':', '-')")
+        seen: dict[str, str] = {}
+        for role, text in roles.items():
+            if text in seen:
+                raise ValueError(f"{role} and {seen[text]} tokens are both {text!r}")
+            seen[text] = role
+        in_alphabet = sorted(r for r, t in roles.items() if t in _byte_alphabet())
+        if in_alphabet:
+            raise ValueError("special tokens collide with byte-level alphabet symbols: " +
+                             ", ".join(in_alphabet))
 
     def as_dict(self) -> dict[str, str]:
-        return {"unk": self.unk, "bos": self.bos, "eos": self.eos, "pad": self.pad}
+        """role -> text, in id order (unk, bos, eos, pad)."""
+        return {f.name: getattr(self, f.name) for f in fields(self)}
 
     def ordered(self) -> tuple[str, str, str, str]:
-        return self.unk, self.bos, self.eos, self.pad
+        """The texts in the order the BPE trainer receives them (ids 0..3)."""
+        return astuple(self)
+
+
+def _count_field(name: str, value) -> None:
+    if type(value) is not int:
+        raise TypeError(f"{name} must be an int, got {value!r}")
+    if value <= 0:
+        raise ValueError(f"{name} must be >= 1, got {value}")
 
 
 @dataclass(frozen=True, slots=True)
@@ -72,19 +92,16 @@ class ByteBPETrainingConfig:
     show_progress: bool = False
 
     def __post_init__(self) -> None:
-        from tokenizers.pre_tokenizers import ByteLevel
-
-        for name in ("vocab_size", "min_frequency"):
-            v = getattr(self, name)
-            if isinstance(v, bool) or not isinstance(v, int):
-                raise TypeError(f"{name} must be an integer")
-            if v < 1:
-                raise ValueError(f"{name} must be positive")
+        _count_field("vocab_size", self.vocab_size)
+        _count_field("min_frequency", self.min_frequency)
         if not isinstance(self.special_tokens, SpecialTokens):
-            raise TypeError("special_tokens must be a SpecialTokens instance")
-        if not isinstance(self.show_progress, bool):
-            raise TypeError("show_progress must be a boolean")
-        need = len(set(ByteLevel.alphabet()) | set(self.special_tokens.ordered()))
-        if self.vocab_size < need:
-            raise ValueError(f"vocab_size must be at least {need} to keep every byte and special "
-                             "token")
+            raise TypeError(f"special_tokens is a {type(self.special_tokens).__name__}, "
+                            "expected SpecialTokens")
+        if type(self.show_progress) is not bool:
+            raise TypeError(f"show_progress must be a bool, got {self.show_progress!r}")
+        # every one of the 256 byte symbols stays in the vocabulary (unseen bytes must
+        # still encode), plus the special tokens
+        floor = len(_byte_alphabet() | set(self.special_tokens.ordered()))
+        if self.vocab_size < floor:
+            raise ValueError(f"vocab_size={self.vocab_size} cannot hold the byte alphabet and "
+                             f"the special tokens ({floor} entries)")
