@@ -1,13 +1,24 @@
-"""Pinned TinyStories sources: verified resumable download, story splitting, exact sampling.
+"""TinyStories, pinned: download with resume and verification, story splitting, and the
+deterministic 500k-story training sample.
 
-The pinned revisions, byte sizes, sha256 digests and record counts identify the
-upstream files (same pins as the reference,
-src/nano_megatron/data/tinystories.py:17-43). Downloads try each mirror in
-turn, resume a ``.part`` file with an HTTP Range request, verify size and
-digest, and publish by rename. The 500k sample keeps the ``k`` stories with the
-smallest blake2b-128 score of ``"<algorithm>\\0<seed>\\0<index>"`` (a bottom-k
-selection in bounded memory, order preserved), so every builder picks the same
-stories.
+Sources. Each upstream file is pinned by revision, byte size, SHA-256 and story count
+(:data:`TRAIN`, :data:`VALIDATION`); a download tries each mirror in turn, resumes a
+``<name>.part`` file with an HTTP ``Range`` request, hashes while it writes, and appears
+under its final name (a rename) only once size and digest match.
+
+Stories. The raw files are stories separated by ``<|endoftext|>``; a story is the text
+between two separators with surrounding whitespace removed, and blank stories are
+skipped (the pinned train file has 230 of them).
+
+Sample. The training sample keeps the ``k`` stories with the smallest score
+``blake2b-128("<algorithm>\\0<seed>\\0<story index>")`` (read as a big-endian integer),
+written in their original order. Any builder that hashes the same way picks the same
+stories, in one pass and with memory for ``k`` entries only. A metadata JSON next to the
+JSONL sample records the selection, the source and the sample's own digest; a sample whose
+metadata does not verify is rebuilt by nobody silently.
+
+The pins, URLs, the score recipe and the metadata layout are the reference's
+(src/nano_megatron/data/tinystories.py), so both frameworks build byte-identical samples.
 """
 
 from __future__ import annotations
@@ -25,32 +36,53 @@ from urllib.request import Request, urlopen
 
 TINYSTORIES_CANONICAL_REVISION = "f54c09fd23315a6f9c86f9dc80f725de7d8f9c64"
 TINYSTORIES_MIRROR_REVISION = "d71d0182cc67962186d395b75b2c180340904e00"
-TINYSTORIES_TRAIN_BYTES = 1_924_281_556
-TINYSTORIES_TRAIN_SHA256 = "c5cf5e22ff13614e830afbe61a99fbcbe8bcb7dd72252b989fa1117a368d401f"
-TINYSTORIES_TRAIN_RECORDS = 2_119_719
-TINYSTORIES_EMPTY_RECORDS = 230
-TINYSTORIES_TRAIN_STORIES = TINYSTORIES_TRAIN_RECORDS - TINYSTORIES_EMPTY_RECORDS
-TINYSTORIES_SAMPLE_STORIES = 500_000
-TINYSTORIES_SAMPLE_SEED = 1234
 TINYSTORIES_DELIMITER = b"<|endoftext|>"
-TINYSTORIES_VALIDATION_BYTES = 19_447_282
-TINYSTORIES_VALIDATION_SHA256 = "94e431816c4cce81ff71e4408ff8d3bda9a42e8d2663986697c3954288cb38b4"
-TINYSTORIES_VALIDATION_STORIES = 21_990
 
 
-def _urls(filename: str) -> tuple[str, str]:
-    return ("https://www.modelscope.cn/api/v1/datasets/AI-ModelScope/TinyStories/repo?"
+def _mirrors(filename: str) -> tuple[str, str]:
+    """ModelScope mirror first, the Hugging Face original second."""
+    return (f"https://www.modelscope.cn/api/v1/datasets/AI-ModelScope/TinyStories/repo?"
             f"Revision={TINYSTORIES_MIRROR_REVISION}&FilePath={filename}",
-            "https://huggingface.co/datasets/roneneldan/TinyStories/resolve/"
+            f"https://huggingface.co/datasets/roneneldan/TinyStories/resolve/"
             f"{TINYSTORIES_CANONICAL_REVISION}/{filename}?download=true")
 
 
-TINYSTORIES_TRAIN_URLS = _urls("TinyStories-train.txt")
-TINYSTORIES_VALIDATION_URLS = _urls("TinyStories-valid.txt")
+@dataclass(frozen=True)
+class PinnedFile:
+    filename: str
+    size: int
+    sha256: str
+    stories: int              # non-empty stories
+
+    @property
+    def urls(self) -> tuple[str, str]:
+        return _mirrors(self.filename)
+
+
+TRAIN = PinnedFile("TinyStories-train.txt", 1_924_281_556,
+                   "c5cf5e22ff13614e830afbe61a99fbcbe8bcb7dd72252b989fa1117a368d401f",
+                   2_119_719 - 230)
+VALIDATION = PinnedFile("TinyStories-valid.txt", 19_447_282,
+                        "94e431816c4cce81ff71e4408ff8d3bda9a42e8d2663986697c3954288cb38b4",
+                        21_990)
+
+TINYSTORIES_TRAIN_BYTES = TRAIN.size
+TINYSTORIES_TRAIN_SHA256 = TRAIN.sha256
+TINYSTORIES_TRAIN_RECORDS = 2_119_719           # separator-delimited records, blanks included
+TINYSTORIES_EMPTY_RECORDS = 230
+TINYSTORIES_TRAIN_STORIES = TRAIN.stories
+TINYSTORIES_TRAIN_URLS = TRAIN.urls
+TINYSTORIES_VALIDATION_BYTES = VALIDATION.size
+TINYSTORIES_VALIDATION_SHA256 = VALIDATION.sha256
+TINYSTORIES_VALIDATION_STORIES = VALIDATION.stories
+TINYSTORIES_VALIDATION_URLS = VALIDATION.urls
+TINYSTORIES_SAMPLE_STORIES = 500_000
+TINYSTORIES_SAMPLE_SEED = 1234
 
 SAMPLE_FORMAT = "nano-megatron-tinystories-sample"
 SAMPLE_VERSION = 1
 SELECTION_ALGORITHM = "blake2b-index-bottom-k-v1"
+_CHUNK = 8 << 20
 
 ProgressCallback = Callable[[int, int], None]
 
@@ -62,244 +94,281 @@ class FileVerification:
     sha256: str
 
 
-def _pos(name: str, v) -> int:
+# ---------------------------------------------------------------------- small checks
+def _int_at_least(name: str, v, low: int) -> int:
     if isinstance(v, bool) or not isinstance(v, int):
-        raise TypeError(f"{name} must be an integer")
-    if v < 1:
-        raise ValueError(f"{name} must be positive")
+        raise TypeError(f"{name} must be an int, got {v!r}")
+    if v < low:
+        raise ValueError(f"{name} must be >= {low}, got {v}")
     return v
 
 
-def _nonneg(name: str, v) -> int:
-    if isinstance(v, bool) or not isinstance(v, int):
-        raise TypeError(f"{name} must be an integer")
-    if v < 0:
-        raise ValueError(f"{name} must be non-negative")
-    return v
-
-
-def _sha(v) -> str:
-    if not isinstance(v, str) or len(v) != 64:
-        raise ValueError("expected_sha256 must be a 64-character hexadecimal digest")
-    try:
-        bytes.fromhex(v)
-    except ValueError as e:
-        raise ValueError("expected_sha256 must be hexadecimal") from e
+def _digest(v) -> str:
+    ok = isinstance(v, str) and len(v) == 64 and all(c in "0123456789abcdefABCDEF" for c in v)
+    if not ok:
+        raise ValueError(f"{v!r} is not a SHA-256 hex digest (64 hex characters)")
     return v.lower()
 
 
-def sha256_file(path, *, chunk_size: int = 8 << 20) -> str:
-    _pos("chunk_size", chunk_size)
+def sha256_file(path, *, chunk_size: int = _CHUNK) -> str:
+    _int_at_least("chunk_size", chunk_size, 1)
     h = hashlib.sha256()
     with Path(path).open("rb") as f:
-        for block in iter(lambda: f.read(chunk_size), b""):
+        while block := f.read(chunk_size):
             h.update(block)
     return h.hexdigest()
 
 
 def verify_file(path, *, expected_size: int, expected_sha256: str) -> FileVerification:
+    """Size and SHA-256 of ``path`` against the pins (size first: it is free)."""
     p = Path(path)
-    size, want = _pos("expected_size", expected_size), _sha(expected_sha256)
+    size = _int_at_least("expected_size", expected_size, 1)
+    want = _digest(expected_sha256)
     if not p.is_file():
-        raise FileNotFoundError(f"expected file does not exist: {p}")
-    if p.stat().st_size != size:
-        raise ValueError(f"file size does not match pinned source: {p}: {p.stat().st_size} != "
-                         f"{size}")
+        raise FileNotFoundError(f"{p} does not exist")
+    have = p.stat().st_size
+    if have != size:
+        raise ValueError(f"{p} is {have} bytes; the pinned source is {size}")
     got = sha256_file(p)
     if got != want:
-        raise ValueError(f"file SHA256 does not match pinned source: {p}: {got} != {want}")
+        raise ValueError(f"{p} has SHA-256 {got}; the pinned source has {want}")
     return FileVerification(p.resolve(), size, got)
 
 
-def _status(resp) -> int:
-    s = getattr(resp, "status", None)
-    if s is None:
-        s = resp.getcode()
-    if isinstance(s, bool) or not isinstance(s, int):
-        raise RuntimeError(f"download response returned invalid HTTP status {s!r}")
-    return s
+# ---------------------------------------------------------------------- download
+class _Transfer:
+    """One attempt at one URL: continue ``<dest>.part`` and publish it when complete."""
 
+    def __init__(self, dest: Path, size: int, sha: str, chunk: int, opener, progress) -> None:
+        self.dest, self.part = dest, dest.with_name(dest.name + ".part")
+        self.size, self.sha, self.chunk = size, sha, chunk
+        self.opener, self.progress = opener, progress
 
-def _fetch(url: str, dest: Path, *, size: int, sha: str, chunk: int, opener,
-           progress) -> FileVerification:
-    part = dest.with_name(dest.name + ".part")
-    have = part.stat().st_size if part.exists() else 0
-    if have > size:
-        raise ValueError(f"partial download is larger than the pinned source: {part}: {have} > "
-                         f"{size}")
-    if have == size:
-        try:
-            v = verify_file(part, expected_size=size, expected_sha256=sha)
-        except ValueError:
-            part.unlink()
-            raise
-        part.replace(dest)
-        return FileVerification(dest.resolve(), v.size_bytes, v.sha256)
-    headers = {"User-Agent": "nano-megatron-tinystories/1"}
-    if have:
-        headers["Range"] = f"bytes={have}-"
-    h = hashlib.sha256()
-    if have:
-        with part.open("rb") as f:
-            for block in iter(lambda: f.read(chunk), b""):
+    def _publish(self, digest: str) -> FileVerification:
+        self.part.replace(self.dest)
+        return FileVerification(self.dest.resolve(), self.size, digest)
+
+    def _hash_of_part(self) -> "hashlib._Hash":
+        h = hashlib.sha256()
+        with self.part.open("rb") as f:
+            while block := f.read(self.chunk):
                 h.update(block)
-    with opener(Request(url, headers=headers)) as resp:
-        st = _status(resp)
-        append = have > 0 and st == 206
-        if append:
-            cr = resp.headers.get("Content-Range", "")
-            if not cr.startswith(f"bytes {have}-"):
-                raise RuntimeError("download server returned an incompatible Content-Range for "
-                                   f"resume: {cr!r}")
-        elif st in (200, 206):
-            have, h = 0, hashlib.sha256()       # server ignored Range: restart the .part file
-        else:
-            raise RuntimeError(f"download server returned HTTP status {st} for {url}")
-        got = have
-        with part.open("ab" if append else "wb") as f:
-            if progress is not None:
-                progress(got, size)
-            for block in iter(lambda: resp.read(chunk), b""):
+        return h
+
+    def run(self, url: str) -> FileVerification:
+        start = self.part.stat().st_size if self.part.exists() else 0
+        if start > self.size:
+            raise ValueError(f"{self.part} holds {start} bytes, more than the pinned "
+                             f"{self.size}")
+        if start == self.size:                       # finished earlier, never published
+            try:
+                v = verify_file(self.part, expected_size=self.size, expected_sha256=self.sha)
+            except ValueError:
+                self.part.unlink()
+                raise
+            return self._publish(v.sha256)
+        headers = {"User-Agent": "nano-megatron-tinystories/1"}
+        if start:
+            headers["Range"] = f"bytes={start}-"
+        with self.opener(Request(url, headers=headers)) as resp:
+            status = getattr(resp, "status", None)
+            status = resp.getcode() if status is None else status
+            if isinstance(status, bool) or not isinstance(status, int):
+                raise RuntimeError(f"{url}: unusable HTTP status {status!r}")
+            if status not in (200, 206):
+                raise RuntimeError(f"{url}: HTTP status {status}")
+            resumed = start > 0 and status == 206
+            if resumed:
+                span = resp.headers.get("Content-Range", "")
+                if not span.startswith(f"bytes {start}-"):
+                    raise RuntimeError(f"{url}: asked to resume at byte {start}, server sent "
+                                       f"Content-Range {span!r}")
+                h = self._hash_of_part()
+            else:                                     # full body (Range ignored or no .part)
+                start, h = 0, hashlib.sha256()
+            got = self._stream(resp, h, start, append=resumed)
+        if got != self.size:
+            raise EOFError(f"{url}: stream ended at byte {got} of {self.size}; run again to "
+                           f"resume {self.part}")
+        digest = h.hexdigest()
+        if digest != self.sha:
+            self.part.unlink(missing_ok=True)
+            raise ValueError(f"{url}: downloaded file has SHA-256 {digest}, pinned {self.sha}")
+        return self._publish(digest)
+
+    def _stream(self, resp, h, got: int, *, append: bool) -> int:
+        with self.part.open("ab" if append else "wb") as f:
+            if self.progress is not None:
+                self.progress(got, self.size)
+            while block := resp.read(self.chunk):
+                got += len(block)
+                if got > self.size:
+                    f.close()
+                    self.part.unlink(missing_ok=True)
+                    raise ValueError(f"server sent more than the pinned {self.size} bytes")
                 f.write(block)
                 h.update(block)
-                got += len(block)
-                if got > size:
-                    f.close()
-                    part.unlink(missing_ok=True)
-                    raise ValueError(f"download exceeded pinned source size: {got} > {size}")
-                if progress is not None:
-                    progress(got, size)
+                if self.progress is not None:
+                    self.progress(got, self.size)
             f.flush()
             os.fsync(f.fileno())
-    if got != size:
-        raise EOFError(f"download ended before the pinned source size: {got} != {size}; rerun to "
-                       f"resume {part}")
-    if h.hexdigest() != sha:
-        part.unlink(missing_ok=True)
-        raise ValueError("downloaded TinyStories source failed SHA256 verification: "
-                         f"{h.hexdigest()} != {sha}")
-    part.replace(dest)
-    return FileVerification(dest.resolve(), got, h.hexdigest())
+        return got
 
 
 def download_pinned_file(destination, *, urls: Sequence[str] = TINYSTORIES_TRAIN_URLS,
                          expected_size: int = TINYSTORIES_TRAIN_BYTES,
                          expected_sha256: str = TINYSTORIES_TRAIN_SHA256,
-                         chunk_size: int = 8 << 20, retries: int = 3, opener=urlopen,
+                         chunk_size: int = _CHUNK, retries: int = 3, opener=urlopen,
                          progress: ProgressCallback | None = None) -> FileVerification:
-    """Mirror fallback + Range resume + verification + atomic publish."""
+    """Verified copy of a pinned file at ``destination`` (an existing file is verified,
+    not fetched again). Up to ``retries`` rounds over ``urls``; every failure is named in
+    the final error."""
     dest = Path(destination)
-    size, sha = _pos("expected_size", expected_size), _sha(expected_sha256)
-    chunk, tries = _pos("chunk_size", chunk_size), _pos("retries", retries)
+    size = _int_at_least("expected_size", expected_size, 1)
+    sha = _digest(expected_sha256)
+    chunk = _int_at_least("chunk_size", chunk_size, 1)
+    rounds = _int_at_least("retries", retries, 1)
     urls = tuple(urls)
-    if not urls or any(not isinstance(u, str) or not u for u in urls):
-        raise ValueError("urls must contain at least one non-empty URL")
+    if not urls or not all(isinstance(u, str) and u for u in urls):
+        raise ValueError("urls must be one or more non-empty strings")
     if dest.exists():
         return verify_file(dest, expected_size=size, expected_sha256=sha)
     dest.parent.mkdir(parents=True, exist_ok=True)
-    failures = []
-    for attempt in range(1, tries + 1):
+    transfer = _Transfer(dest, size, sha, chunk, opener, progress)
+    errors = []
+    for r in range(rounds):
         for url in urls:
             try:
-                return _fetch(url, dest, size=size, sha=sha, chunk=chunk, opener=opener,
-                              progress=progress)
+                return transfer.run(url)
             except (EOFError, OSError, RuntimeError, ValueError) as e:
-                failures.append(f"attempt {attempt} {url}: {type(e).__name__}: {e}")
-    raise RuntimeError("could not download pinned TinyStories source: " + "; ".join(failures))
+                errors.append(f"[round {r + 1}] {url}: {type(e).__name__}: {e}")
+    raise RuntimeError("download failed on every mirror: " + " | ".join(errors))
 
 
+# ---------------------------------------------------------------------- stories
 def _story_bytes(path, *, delimiter: bytes = TINYSTORIES_DELIMITER,
-                 chunk_size: int = 8 << 20) -> Iterator[bytes]:
+                 chunk_size: int = _CHUNK) -> Iterator[bytes]:
+    """Stripped, non-blank byte strings between separators, streamed in chunks."""
     if not isinstance(delimiter, bytes) or not delimiter:
-        raise ValueError("delimiter must be non-empty bytes")
-    _pos("chunk_size", chunk_size)
-    tail = b""
+        raise ValueError("the story delimiter must be non-empty bytes")
+    _int_at_least("chunk_size", chunk_size, 1)
+    buf = bytearray()
     with Path(path).open("rb") as f:
-        for block in iter(lambda: f.read(chunk_size), b""):
-            pieces = (tail + block).split(delimiter)
-            tail = pieces.pop()
-            for p in pieces:
-                p = p.strip()
-                if p:
-                    yield p
-    tail = tail.strip()
-    if tail:
-        yield tail
+        while block := f.read(chunk_size):
+            buf += block
+            begin = 0
+            while (cut := buf.find(delimiter, begin)) >= 0:
+                story = bytes(buf[begin:cut]).strip()
+                if story:
+                    yield story
+                begin = cut + len(delimiter)
+            del buf[:begin]
+    last = bytes(buf).strip()
+    if last:
+        yield last
 
 
 def iter_delimited_stories(path, *, delimiter: bytes = TINYSTORIES_DELIMITER,
-                           chunk_size: int = 8 << 20) -> Iterator[str]:
-    for s in _story_bytes(path, delimiter=delimiter, chunk_size=chunk_size):
-        yield s.decode("utf-8")
+                           chunk_size: int = _CHUNK) -> Iterator[str]:
+    return (s.decode("utf-8") for s in _story_bytes(path, delimiter=delimiter,
+                                                    chunk_size=chunk_size))
 
 
 def selection_score(seed: int, index: int) -> int:
-    msg = f"{SELECTION_ALGORITHM}\0{seed}\0{index}".encode("ascii")
-    return int.from_bytes(hashlib.blake2b(msg, digest_size=16).digest(), "big")
+    key = f"{SELECTION_ALGORITHM}\0{seed}\0{index}".encode("ascii")
+    return int.from_bytes(hashlib.blake2b(key, digest_size=16).digest(), "big")
 
 
 def select_story_indices(source, *, sample_size: int, seed: int,
                          expected_source_records: int | None,
                          progress: ProgressCallback | None = None) -> tuple[frozenset, int]:
-    k, seed = _pos("sample_size", sample_size), _nonneg("seed", seed)
+    """Indices of the ``sample_size`` lowest-scoring stories, and the story count."""
+    k = _int_at_least("sample_size", sample_size, 1)
+    seed = _int_at_least("seed", seed, 0)
     if expected_source_records is not None:
-        _pos("expected_source_records", expected_source_records)
+        _int_at_least("expected_source_records", expected_source_records, 1)
         if k > expected_source_records:
-            raise ValueError("sample_size cannot exceed expected_source_records")
-    heap: list[tuple[int, int]] = []     # max-heap on (score, index) via negation
-    total = 0
-    for i, _ in enumerate(_story_bytes(source)):
-        item = (-selection_score(seed, i), -i)
-        if len(heap) < k:
-            heapq.heappush(heap, item)
-        elif item > heap[0]:
-            heapq.heapreplace(heap, item)
-        total = i + 1
-        if progress is not None and total % 100_000 == 0:
-            progress(total, expected_source_records or k)
-    if total < k:
-        raise ValueError(f"source contains only {total} stories; cannot select {k}")
-    if expected_source_records is not None and total != expected_source_records:
-        raise ValueError(f"TinyStories source record count changed: {total} != "
+            raise ValueError(f"cannot sample {k} of {expected_source_records} stories")
+    count = 0
+    total_hint = expected_source_records or k
+
+    def scored():
+        nonlocal count
+        for i, _ in enumerate(_story_bytes(source)):
+            count = i + 1
+            if progress is not None and count % 100_000 == 0:
+                progress(count, total_hint)
+            yield selection_score(seed, i), i
+
+    best = heapq.nsmallest(k, scored())          # keeps a k-entry heap while streaming
+    if count < k:
+        raise ValueError(f"{source} has {count} stories, fewer than the {k} requested")
+    if expected_source_records is not None and count != expected_source_records:
+        raise ValueError(f"{source} has {count} stories; the pinned source has "
                          f"{expected_source_records}")
     if progress is not None:
-        progress(total, expected_source_records or k)
-    return frozenset(-ni for _, ni in heap), total
+        progress(count, total_hint)
+    return frozenset(i for _, i in best), count
 
 
-def _json(path: Path) -> dict:
+# ---------------------------------------------------------------------- the sample
+def _read_json_object(path: Path) -> dict:
     try:
-        v = json.loads(path.read_text(encoding="utf-8"))
+        obj = json.loads(path.read_text(encoding="utf-8"))
     except (OSError, json.JSONDecodeError) as e:
-        raise ValueError(f"could not read TinyStories metadata {path}: {e}") from e
-    if not isinstance(v, dict):
-        raise ValueError(f"TinyStories metadata must contain a JSON object: {path}")
-    return v
+        raise ValueError(f"unreadable sample metadata {path}: {e}") from e
+    if not isinstance(obj, dict):
+        raise ValueError(f"sample metadata {path} is not a JSON object")
+    return obj
 
 
 def validate_sample_artifact(sample_path, metadata_path, *, sample_size: int, seed: int,
                              expected_source_records: int, expected_source_sha256: str) -> dict:
-    sample, mfile = Path(sample_path), Path(metadata_path)
-    if not sample.is_file() or not mfile.is_file():
-        raise FileNotFoundError("TinyStories sample requires both JSONL and metadata files")
-    meta = _json(mfile)
-    sel, src, art = meta.get("selection"), meta.get("source"), meta.get("artifact")
-    if meta.get("format") != SAMPLE_FORMAT or meta.get("version") != SAMPLE_VERSION:
-        raise ValueError("TinyStories sample metadata format/version is unsupported")
-    if not all(isinstance(x, dict) for x in (sel, src, art)):
-        raise ValueError("TinyStories sample metadata sections are invalid")
+    """Check an existing sample against its metadata and the requested selection."""
+    sample, mpath = Path(sample_path), Path(metadata_path)
+    if not (sample.is_file() and mpath.is_file()):
+        raise FileNotFoundError(f"a sample is the pair {sample} + {mpath}; one is missing")
+    meta = _read_json_object(mpath)
+    if (meta.get("format"), meta.get("version")) != (SAMPLE_FORMAT, SAMPLE_VERSION):
+        raise ValueError(f"{mpath}: format/version {meta.get('format')!r}/"
+                         f"{meta.get('version')!r} is not {SAMPLE_FORMAT!r}/{SAMPLE_VERSION}")
+    parts = {k: meta.get(k) for k in ("selection", "source", "artifact")}
+    bad = [k for k, v in parts.items() if not isinstance(v, dict)]
+    if bad:
+        raise ValueError(f"{mpath}: sections {bad} are not objects")
     want = {"algorithm": SELECTION_ALGORITHM, "records": sample_size, "seed": seed,
             "source_records": expected_source_records}
-    if sel != want:
-        raise ValueError(f"TinyStories sample selection metadata does not match: {sel!r} != "
-                         f"{want!r}")
-    if src.get("sha256") != _sha(expected_source_sha256):
-        raise ValueError("TinyStories sample was built from a different source digest")
-    if art.get("records") != sample_size or art.get("size_bytes") != sample.stat().st_size:
-        raise ValueError("TinyStories sample artifact count/size metadata does not match")
+    if parts["selection"] != want:
+        raise ValueError(f"{mpath}: selection {parts['selection']!r} differs from the "
+                         f"requested {want!r}")
+    if parts["source"].get("sha256") != _digest(expected_source_sha256):
+        raise ValueError(f"{mpath}: sample was drawn from another source file")
+    art = parts["artifact"]
+    if (art.get("records"), art.get("size_bytes")) != (sample_size, sample.stat().st_size):
+        raise ValueError(f"{mpath}: the sample's story count or byte size changed")
     if art.get("sha256") != sha256_file(sample):
-        raise ValueError("TinyStories sample JSONL failed SHA256 verification")
+        raise ValueError(f"{sample}: content does not match the SHA-256 in {mpath}")
     return meta
+
+
+def _sample_metadata(out: Path, src: Path, v: FileVerification, *, written: int,
+                     digest: str, size: int, sample_size: int, seed: int,
+                     total: int) -> dict[str, Any]:
+    pinned = v.sha256 == TINYSTORIES_TRAIN_SHA256
+    return {
+        "artifact": {"format": "jsonl", "path": str(out), "records": written, "sha256": digest,
+                     "size_bytes": size, "text_key": "text"},
+        "format": SAMPLE_FORMAT,
+        "selection": {"algorithm": SELECTION_ALGORITHM, "records": sample_size, "seed": seed,
+                      "source_records": total},
+        "source": {"canonical_revision": TINYSTORIES_CANONICAL_REVISION,
+                   "empty_records_excluded": TINYSTORIES_EMPTY_RECORDS if pinned else None,
+                   "mirror_revision": TINYSTORIES_MIRROR_REVISION, "non_empty_stories": total,
+                   "path": str(src),
+                   "records_including_empty": TINYSTORIES_TRAIN_RECORDS if pinned else None,
+                   "sha256": v.sha256, "size_bytes": v.size_bytes,
+                   "story_delimiter": TINYSTORIES_DELIMITER.decode("ascii")},
+        "version": SAMPLE_VERSION}
 
 
 def create_exact_sample(source_path, sample_path, metadata_path, *,
@@ -308,96 +377,79 @@ def create_exact_sample(source_path, sample_path, metadata_path, *,
                         seed: int = TINYSTORIES_SAMPLE_SEED,
                         expected_source_records: int = TINYSTORIES_TRAIN_STORIES,
                         progress: ProgressCallback | None = None) -> dict[str, Any]:
-    """Create (or validate and reuse) the deterministic JSONL sample."""
-    src = Path(source_path).resolve()
-    out = Path(sample_path).resolve()
-    mfile = Path(metadata_path).resolve()
+    """Write the sample JSONL + metadata (two passes over the source: select, then write),
+    or verify and reuse an existing pair. Both files appear by rename, sample first."""
+    src, out, mpath = (Path(p).resolve() for p in (source_path, sample_path, metadata_path))
     if src != source_verification.path.resolve():
-        raise ValueError("source_verification does not describe source_path")
+        raise ValueError(f"the verification is for {source_verification.path}, not {src}")
     if not src.is_file() or src.stat().st_size != source_verification.size_bytes:
-        raise ValueError("source_path size changed after source verification")
-    if out == mfile or src in (out, mfile):
-        raise ValueError("source, sample, and metadata paths must be distinct")
-    if out.exists() or mfile.exists():
-        if not out.is_file() or not mfile.is_file():
-            raise FileExistsError("refusing to replace an incomplete TinyStories sample "
-                                  f"artifact; remove both {out} and {mfile} to rebuild")
-        meta = validate_sample_artifact(out, mfile, sample_size=sample_size, seed=seed,
+        raise ValueError(f"{src} changed since it was verified")
+    if len({src, out, mpath}) != 3:
+        raise ValueError("source, sample and metadata must be three different paths")
+    if out.exists() or mpath.exists():
+        if not (out.is_file() and mpath.is_file()):
+            raise FileExistsError(f"half a sample exists ({out}, {mpath}); delete both to "
+                                  "rebuild it")
+        meta = validate_sample_artifact(out, mpath, sample_size=sample_size, seed=seed,
                                         expected_source_records=expected_source_records,
                                         expected_source_sha256=source_verification.sha256)
-        return {**meta, "reused": True}
-    out.parent.mkdir(parents=True, exist_ok=True)
-    mfile.parent.mkdir(parents=True, exist_ok=True)
-    chosen, total = select_story_indices(src, sample_size=sample_size, seed=seed,
-                                         expected_source_records=expected_source_records,
-                                         progress=progress)
+        return dict(meta, reused=True)
+    for d in {out.parent, mpath.parent}:
+        d.mkdir(parents=True, exist_ok=True)
+    keep, total = select_story_indices(src, sample_size=sample_size, seed=seed,
+                                       expected_source_records=expected_source_records,
+                                       progress=progress)
     tag = uuid.uuid4().hex
-    otmp = out.with_name(f".{out.name}.{tag}.tmp")
-    mtmp = mfile.with_name(f".{mfile.name}.{tag}.tmp")
+    out_tmp = out.with_name(f".{out.name}.{tag}.tmp")
+    meta_tmp = mpath.with_name(f".{mpath.name}.{tag}.tmp")
     h = hashlib.sha256()
-    written = records = 0
-    published = False
+    written = seen = 0
+    sample_published = False
     try:
-        with otmp.open("xb") as f:
+        with out_tmp.open("xb") as f:
             for i, story in enumerate(_story_bytes(src)):
-                records = i + 1
-                if i not in chosen:
-                    continue
-                line = (json.dumps({"text": story.decode("utf-8")}, ensure_ascii=False,
-                                   separators=(",", ":")) + "\n").encode("utf-8")
-                f.write(line)
-                h.update(line)
-                written += 1
-                if progress is not None and written % 100_000 == 0:
-                    progress(written, sample_size)
+                seen = i + 1
+                if i in keep:
+                    row = json.dumps({"text": story.decode("utf-8")}, ensure_ascii=False,
+                                     separators=(",", ":")).encode("utf-8") + b"\n"
+                    f.write(row)
+                    h.update(row)
+                    written += 1
+                    if progress is not None and written % 100_000 == 0:
+                        progress(written, sample_size)
             f.flush()
             os.fsync(f.fileno())
         if written != sample_size:
-            raise RuntimeError(f"sample writer emitted {written} stories, expected {sample_size}")
-        if records != expected_source_records:
-            raise RuntimeError("TinyStories source record count changed between sample passes: "
-                               f"{records} != {expected_source_records}")
+            raise RuntimeError(f"wrote {written} stories instead of {sample_size}")
+        if seen != expected_source_records:
+            raise RuntimeError(f"{src} changed between the two passes ({seen} stories, "
+                               f"expected {expected_source_records})")
         if progress is not None:
             progress(written, sample_size)
-        pinned = source_verification.sha256 == TINYSTORIES_TRAIN_SHA256
-        meta = {
-            "artifact": {"format": "jsonl", "path": str(out), "records": written,
-                         "sha256": h.hexdigest(), "size_bytes": otmp.stat().st_size,
-                         "text_key": "text"},
-            "format": SAMPLE_FORMAT,
-            "selection": {"algorithm": SELECTION_ALGORITHM, "records": sample_size, "seed": seed,
-                          "source_records": total},
-            "source": {"canonical_revision": TINYSTORIES_CANONICAL_REVISION,
-                       "empty_records_excluded": TINYSTORIES_EMPTY_RECORDS if pinned else None,
-                       "mirror_revision": TINYSTORIES_MIRROR_REVISION,
-                       "non_empty_stories": total, "path": str(src),
-                       "records_including_empty": TINYSTORIES_TRAIN_RECORDS if pinned else None,
-                       "sha256": source_verification.sha256,
-                       "size_bytes": source_verification.size_bytes,
-                       "story_delimiter": TINYSTORIES_DELIMITER.decode("ascii")},
-            "version": SAMPLE_VERSION}
-        mtmp.write_text(json.dumps(meta, ensure_ascii=False, indent=2, sort_keys=True) + "\n",
-                        encoding="utf-8")
-        otmp.replace(out)
-        published = True
-        mtmp.replace(mfile)
+        meta = _sample_metadata(out, src, source_verification, written=written,
+                                digest=h.hexdigest(), size=out_tmp.stat().st_size,
+                                sample_size=sample_size, seed=seed, total=total)
+        meta_tmp.write_text(json.dumps(meta, ensure_ascii=False, indent=2, sort_keys=True)
+                            + "\n", encoding="utf-8")
+        out_tmp.replace(out)
+        sample_published = True
+        meta_tmp.replace(mpath)
     except BaseException:
-        otmp.unlink(missing_ok=True)
-        mtmp.unlink(missing_ok=True)
-        if published:
-            out.unlink(missing_ok=True)
+        for p in (out_tmp, meta_tmp) + ((out,) if sample_published else ()):
+            p.unlink(missing_ok=True)
         raise
-    return {**meta, "reused": False}
+    return dict(meta, reused=False)
 
 
 def prepare_tinystories_500k(data_dir=Path("data/raw/tinystories"), *,
                              urls: Sequence[str] = TINYSTORIES_TRAIN_URLS,
                              progress: ProgressCallback | None = None) -> dict[str, Any]:
+    """Download the pinned train file into ``data_dir`` and build the 500k sample."""
     d = Path(data_dir)
-    src, sample, meta = d / "TinyStories-train.txt", d / "train_500k.jsonl", \
-        d / "train_500k.metadata.json"
+    src = d / TRAIN.filename
+    sample, mpath = d / "train_500k.jsonl", d / "train_500k.metadata.json"
     v = download_pinned_file(src, urls=urls, progress=progress)
-    m = create_exact_sample(src, sample, meta, source_verification=v, progress=progress)
-    return {"command": "prepare-tinystories-500k", "sample": m,
-            "sample_metadata": str(meta.resolve()), "sample_output": str(sample.resolve()),
+    meta = create_exact_sample(src, sample, mpath, source_verification=v, progress=progress)
+    return {"command": "prepare-tinystories-500k", "sample": meta,
+            "sample_metadata": str(mpath.resolve()), "sample_output": str(sample.resolve()),
             "source": {"path": str(v.path), "sha256": v.sha256, "size_bytes": v.size_bytes}}
