@@ -23,6 +23,15 @@ runs the sharded AdamW and refreshes its bf16 shard from the fp32 master. The
 reference wraps the whole stage (or each virtual chunk) in one FSDP2 unit
 instead (src/nano_megatron/data_parallel/zero3.py:152-165), which gathers
 every parameter of the stage at once.
+
+``offload.zero3_params_and_grads`` (the reference's FSDP2 ``CPUOffloadPolicy``,
+src/nano_megatron/data_parallel/zero3.py:77-80,139-142) keeps every sharded tensor in
+(pinned) host memory: the bf16 parameter shards, the reduced fp32 gradient shards, the
+fp32 masters and both Adam moments. A gather copies the shard to the device first (an
+asynchronous copy from pinned memory on the compute stream, which the all-gather then
+follows); after the reduce-scatter each gradient shard is copied to the host, and the
+AdamW update runs on the host. What stays on the device between uses is the flat fp32
+gradient accumulation buffer of the microbatches, as without offload.
 """
 
 from __future__ import annotations
@@ -67,6 +76,9 @@ class Zero3Strategy(Zero2Strategy):
             self._units.setdefault(key, []).append(b)
             b.shapes = [tuple(s.parameter.shape) for s in b.slices]
             b.bf16_shard = b.shard_view(b.param_data[:b.padded_numel]).clone()
+        self.host_shards = bool(self.offload_policy.zero3_params_and_grads)
+        if self.host_shards:
+            self._move_shards_to_host()
         self._empty = torch.empty(0, dtype=buf.param_dtype, device=buf.device)
         self._gathered: set = set()
         self._pending: dict = {}
@@ -79,6 +91,20 @@ class Zero3Strategy(Zero2Strategy):
         buf.param_flat = None
         self._register_hooks(model)
         return model
+
+    def _move_shards_to_host(self) -> None:
+        pin = bool(self.offload_policy.pin_memory) and torch.cuda.is_available()
+
+        def host(t: torch.Tensor) -> torch.Tensor:
+            out = torch.empty(t.shape, dtype=t.dtype, pin_memory=pin)
+            out.copy_(t)
+            return out
+
+        for b, sh in zip(self.buffers.buckets, self.shards):
+            b.bf16_shard = host(b.bf16_shard)
+            for k in ("master", "exp_avg", "exp_avg_sq"):
+                sh[k] = host(sh[k])
+            sh["host_grad"] = host(sh["grad"])
 
     def _layer_modules(self, model):
         from nano_megatron_b200.models.gpt.model import GPTLayer
@@ -138,11 +164,14 @@ class Zero3Strategy(Zero2Strategy):
     def _start_gather(self, b, async_op: bool):
         full = torch.empty(b.storage_numel, dtype=self.buffers.param_dtype,
                            device=self.buffers.device)
+        shard = b.bf16_shard
+        if shard.device != full.device:          # host-resident shard: stage it first
+            shard = shard.to(full.device, non_blocking=True)
         g = self.replica_group
         if g is None or g.size == 1:
-            full[:b.padded_numel].copy_(b.bf16_shard)
+            full[:b.padded_numel].copy_(shard)
             return full, None
-        work = dist.all_gather_into_tensor(full[:b.padded_numel], b.bf16_shard,
+        work = dist.all_gather_into_tensor(full[:b.padded_numel], shard,
                                            group=g.process_group, async_op=async_op)
         return full, work
 
@@ -216,7 +245,11 @@ class Zero3Strategy(Zero2Strategy):
 
         for b, sh in zip(self.buffers.buckets, self.shards):
             dev = sh["master"].device
-            grad = sh["grad"] if dev == sh["grad"].device else sh["grad"].to(dev)
+            if "host_grad" in sh:
+                sh["host_grad"].copy_(sh["grad"])          # the reduced shard, to the host
+                grad = sh["host_grad"]
+            else:
+                grad = sh["grad"] if dev == sh["grad"].device else sh["grad"].to(dev)
             sc = scale if scale is None or scale.device == dev else scale.to(dev)
             lr_t = self._lr_t if self._lr_t.device == dev else None
             F.adamw_(sh["master"], grad, sh["exp_avg"], sh["exp_avg_sq"], None, lr=self._lr,
