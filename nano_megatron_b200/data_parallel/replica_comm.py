@@ -87,6 +87,7 @@ class ReplicaComm:
         from nano_megatron_b200.ops._ext import lib
 
         dev = buffers.device
+        index = dev.index if dev.index is not None else torch.cuda.current_device()
         for b in buffers.buckets:
             lo = b.rank * b.shard_numel
             hi = lo + b.shard_numel
@@ -101,7 +102,7 @@ class ReplicaComm:
                     segs.append([a, e])
             flat = [x - lo for seg in segs for x in seg]
             self.segments[b.index] = torch.tensor(flat, dtype=torch.int64, device=dev)
-            blocks = int(lib().replica_reduce_blocks(b.shard_numel, dev.index))
+            blocks = int(lib().replica_reduce_blocks(b.shard_numel, index))
             self.partials[b.index] = torch.zeros(blocks, dtype=torch.float32, device=dev)
 
     # ------------------------------------------------------------------ step phases

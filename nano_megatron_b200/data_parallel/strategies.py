@@ -358,6 +358,25 @@ class DataParallelStrategy:
                                   for b in self.buffers.buckets]
         self._reduced = True
 
+    def materialize_reduced_gradients(self) -> None:
+        """After ``finalize_gradients``: make every rank's ``main_grad`` hold the whole
+        replica-summed gradient. The step itself needs only this rank's shard of each bucket
+        (the fused replica path sums shards in place; ZeRO-2/3 reduce-scatter), so this
+        all-gather exists for inspection and tests."""
+        g = self.replica_group
+        if g is None or g.size == 1 or not self._reduced or self.buffers is None:
+            return
+        shards = getattr(self, "shards", None)
+        for i, b in enumerate(self.buffers.buckets):
+            full = b.grad_data[:b.padded_numel]
+            if self.replica is not None:
+                mine = b.shard_view(full).clone()
+            elif shards and getattr(self, "reduce_scatter", False) and full.is_cuda:
+                mine = shards[i]["grad"]
+            else:
+                continue       # all-reduced: already whole
+            dist.all_gather_into_tensor(full, mine, group=g.process_group)
+
     def _fused_clip(self, max_norm):
         from .common import dense_counted_here, is_dense
 

@@ -69,7 +69,7 @@ class SymmetricWorkspace:
             raise ValueError(f"symmetric workspace supports at most {MAX_TP} ranks")
         rs_bytes, ag_bytes = _align(rs_bytes), _align(ag_bytes)
         emb_bytes, ce_bytes = _align(emb_bytes, 4096, 0), _align(ce_bytes, 4096, 0)
-        dev = torch.device(device)
+        dev = _indexed(device)
         buf, handle = lib().symm_alloc(cls.total_bytes(rs_bytes, ag_bytes, emb_bytes, ce_bytes),
                                        dev.index)
         handles: list = [None] * group.size
@@ -93,7 +93,7 @@ class SymmetricWorkspace:
                  emb_bytes: int = 0, ce_bytes: int = 0) -> list["SymmetricWorkspace"]:
         rs_bytes, ag_bytes = _align(rs_bytes), _align(ag_bytes)
         emb_bytes, ce_bytes = _align(emb_bytes, 4096, 0), _align(ce_bytes, 4096, 0)
-        dev = torch.device(device)
+        dev = _indexed(device)
         bufs = [torch.zeros(cls.total_bytes(rs_bytes, ag_bytes, emb_bytes, ce_bytes),
                             dtype=torch.uint8, device=dev) for _ in range(size)]
         ptrs = [b.data_ptr() for b in bufs]
@@ -167,6 +167,14 @@ class SymmetricWorkspace:
                              f"{self.rs_bytes}")
 
 
+def _indexed(device) -> torch.device:
+    """``device`` with an explicit CUDA index (``cuda`` alone means the current device)."""
+    dev = torch.device(device)
+    if dev.type == "cuda" and dev.index is None:
+        dev = torch.device("cuda", torch.cuda.current_device())
+    return dev
+
+
 def _align(n: int, a: int = 1 << 21, minimum: int | None = None) -> int:
     up = (int(n) + a - 1) // a * a
     return max(a if minimum is None else minimum, up)
@@ -209,7 +217,7 @@ class SymmetricHeap:
         if group.size > MAX_TP:
             raise ValueError(f"symmetric heap supports at most {MAX_TP} ranks")
         offsets, total = cls.layout(regions)
-        dev = torch.device(device)
+        dev = _indexed(device)
         buf, handle = lib().symm_alloc(total, dev.index)
         handles: list = [None] * group.size
         dist.all_gather_object(handles, bytes(handle), group=group.process_group)
@@ -230,7 +238,7 @@ class SymmetricHeap:
     def emulated(cls, size: int, regions: dict[str, int], device) -> list["SymmetricHeap"]:
         """``size`` heaps in one process on one GPU (every "peer" is local memory)."""
         offsets, total = cls.layout(regions)
-        dev = torch.device(device)
+        dev = _indexed(device)
         bufs = [torch.zeros(total, dtype=torch.uint8, device=dev) for _ in range(size)]
         ptrs = [b.data_ptr() for b in bufs]
         return [cls(rank=r, size=size, ptrs=ptrs, owner=bufs[r], device=dev, offsets=offsets,

@@ -6,7 +6,8 @@ loads its shard of the same weights on 2 (or 4) GPUs, runs the step on the same 
 batch, and its token-weighted loss and merged gradients must agree within bf16
 tolerance. Covers the NCCL paths the single-GPU tests cannot: pipeline P2P (1F1B and
 interleaved), context-parallel ring (zig-zag) and all-gather, the overlapped DDP
-reducer, ZeRO-1 and ZeRO-3. Child processes, one per GPU, NVLS off, bounded by timeouts.
+reducer, ZeRO-1, ZeRO-2 and ZeRO-3 (also with its shards offloaded to pinned host
+memory). Child processes, one per GPU, NVLS off, bounded by timeouts.
 """
 
 from __future__ import annotations
@@ -44,6 +45,7 @@ def _config(layout: dict):
                           "bucket_bytes": 1 << 18 if layout.get("dp_overlap") else 1 << 28},
         "pipeline": layout.get("pipeline", {}),
         "context_parallel": layout.get("cp", {}),
+        "offload": {"zero3_params_and_grads": bool(layout.get("offload"))},
         "optimizer": {"lr": 1e-3, "clip_grad_norm": None}})
 
 
@@ -51,21 +53,6 @@ def _batch():
     g = torch.Generator().manual_seed(99)
     ids = torch.randint(0, MODEL["vocab_size"], (GB, MODEL["seq_length"] + 1), generator=g)
     return {"input_ids": ids[:, :-1], "labels": ids[:, 1:]}
-
-
-def _gather_reduced_shards(dp) -> None:
-    """ZeRO-2/3 reduce-scatter: the replica-summed gradient exists only as each owner's
-    shard. Put the full sum back into every rank's ``main_grad`` (all-gather of the shards)
-    so all strategies are compared on the same quantity."""
-    import torch.distributed as dist
-
-    shards = getattr(dp, "shards", None)
-    g = dp.replica_group
-    if not shards or not getattr(dp, "reduce_scatter", False) or g is None or g.size == 1:
-        return
-    for b, sh in zip(dp.buffers.buckets, shards):
-        dist.all_gather_into_tensor(b.grad_data[:b.padded_numel], sh["grad"],
-                                    group=g.process_group)
 
 
 def _step(cfg, out_path, full_path=None):
@@ -104,7 +91,7 @@ def _step(cfg, out_path, full_path=None):
     acc = tr.schedule.forward_backward(micro)
     comps.model.synchronize_tied_embedding_gradients()
     dp.finalize_gradients()
-    _gather_reduced_shards(dp)
+    dp.materialize_reduced_gradients()
     s, n = aggregate_loss_metrics(acc, comps.parallel, rt.device)
     grads, seen = {}, set()
     for name, p in comps.model.named_parameters():
@@ -140,7 +127,9 @@ LAYOUTS = {
     "cp2_all_gather": ({"parallel": {"context": 2}, "cp": {"backend": "all_gather"}}, 2),
     "dp2_ddp_overlap": ({"parallel": {"data": 2}, "dp_overlap": True}, 2),
     "dp2_zero1": ({"parallel": {"data": 2}, "dp_mode": "zero1"}, 2),
+    "dp2_zero2": ({"parallel": {"data": 2}, "dp_mode": "zero2"}, 2),
     "dp2_zero3": ({"parallel": {"data": 2}, "dp_mode": "zero3"}, 2),
+    "dp2_zero3_offload": ({"parallel": {"data": 2}, "dp_mode": "zero3", "offload": True}, 2),
     "tp2_pp2_sp": ({"parallel": {"tensor": 2, "pipeline": 2, "sequence_parallel": True}}, 4),
     "tp2_cp2_sp_ring": ({"parallel": {"tensor": 2, "context": 2, "sequence_parallel": True},
                          "cp": {"backend": "ring", "load_balance": True}}, 4),
