@@ -466,8 +466,28 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else if constexpr (EPI == kEpiBF16 || EPI == kEpiF32Acc) {
         const int n0 = nt * BN;
+        // Residual (kEpiBF16): each thread reads its own row, 32 columns = 64 bytes per
+        // chunk, as four 16-byte loads issued one chunk ahead of their use, so the global
+        // latency overlaps the TMEM drain of the previous chunk.
+        const bool res_vec = EPI == kEpiBF16 && p.R != nullptr && row_ok &&
+                             (p.ldr % 8) == 0 && (reinterpret_cast<uintptr_t>(p.R) & 15u) == 0;
+        const uint4* res_row =
+            res_vec ? reinterpret_cast<const uint4*>(p.R + static_cast<int64_t>(row) * p.ldr + n0)
+                    : nullptr;
+        uint4 res_next[4];
+        if (res_vec && n0 + 32 <= p.N) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) res_next[q] = __ldg(res_row + q);
+        }
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
+          uint4 res_cur[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) res_cur[q] = res_next[q];
+          if (res_vec && c + 1 < BN / 32 && n0 + (c + 2) * 32 <= p.N) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) res_next[q] = __ldg(res_row + (c + 1) * 4 + q);
+          }
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + c * 32, r);
           tmem_wait_ld();
@@ -477,7 +497,17 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * alpha;
           if constexpr (EPI == kEpiBF16) {
-            if (p.R != nullptr) {
+            if (res_vec && col + 32 <= p.N) {
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const uint32_t w[4] = {res_cur[q].x, res_cur[q].y, res_cur[q].z, res_cur[q].w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  v[q * 8 + 2 * e] += bf16_lo(w[e]);
+                  v[q * 8 + 2 * e + 1] += bf16_hi(w[e]);
+                }
+              }
+            } else if (p.R != nullptr) {
               const __nv_bfloat16* rr = p.R + static_cast<int64_t>(row) * p.ldr + col;
 #pragma unroll
               for (int j = 0; j < 32; ++j)
