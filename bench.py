@@ -60,7 +60,9 @@ WORKLOADS = {
         "model": {"layers": 24, "hidden_size": 1024, "ffn_hidden_size": 2736, "heads": 16,
                   "kv_heads": 16, "seq_length": 512, "vocab_size": 8192, "dropout": 0.0,
                   "tie_embeddings": True},
-        "global_batch": 256, "micro_batch": 8,
+        # micro-batch per GPU count (both arms): the largest that measured fastest at that
+        # layout on B200 (fewer, larger GEMMs; PP keeps >= 16 microbatches in flight)
+        "global_batch": 256, "micro_batch": {1: 32, 2: 64, 4: 16, 8: 16},
         "layouts": {1: {}, 2: {"tensor": 2}, 4: {"tensor": 2, "pipeline": 2},
                     8: {"tensor": 2, "pipeline": 2, "data": 2}},
         "sections": {"pipeline": {"schedule": "1f1b", "overlap_p2p": True},

@@ -311,28 +311,44 @@ struct BwdParams {
   const float* inv_freq;
 };
 
-// delta = rowsum(dO * O); also zero the fp32 dQ accumulator.
+// delta = rowsum(dO * O); also zero the fp32 dQ accumulator. D / 8 threads per row, each
+// with one 16-byte piece of O and dO; rows are ordered (b, h, s), which is the layout of
+// delta, so a row's index is its delta index and a warp's delta stores are contiguous.
+// The row's threads are consecutive lanes of one warp (D / 8 divides 32).
 template <int D>
-__global__ void flash_bwd_pre_kernel(const BwdParams p) {
-  const int row = blockIdx.x * 8 + threadIdx.x / 32;  // one warp per (b, s, h)
-  const int lane = threadIdx.x & 31;
-  const int total = p.B * p.Sq * p.Hq;
-  if (row >= total) return;
-  const int h = row % p.Hq;
-  const int s = (row / p.Hq) % p.Sq;
-  const int b = row / (p.Hq * p.Sq);
-  const __nv_bfloat16* orow = p.o + b * p.o_batch + static_cast<int64_t>(s) * p.o_row + h * D;
-  const __nv_bfloat16* drow = p.dout + b * p.do_batch + static_cast<int64_t>(s) * p.do_row + h * D;
+__global__ void __launch_bounds__(256) flash_bwd_pre_kernel(const BwdParams p) {
+  constexpr int TPR = D / 8;
+  const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t row = gt / TPR;
+  const int part = static_cast<int>(gt % TPR);
+  const bool ok = row < static_cast<int64_t>(p.B) * p.Hq * p.Sq;
   float acc = 0.f;
-  for (int d = lane * 2; d < D; d += 64) {
-    const uint32_t ov = *reinterpret_cast<const uint32_t*>(orow + d);
-    const uint32_t dv = *reinterpret_cast<const uint32_t*>(drow + d);
-    acc += bf16_lo(ov) * bf16_lo(dv) + bf16_hi(ov) * bf16_hi(dv);
+  if (ok) {
+    const int s = static_cast<int>(row % p.Sq);
+    const int h = static_cast<int>((row / p.Sq) % p.Hq);
+    const int b = static_cast<int>(row / (static_cast<int64_t>(p.Sq) * p.Hq));
+    const uint4 ov = __ldg(reinterpret_cast<const uint4*>(
+        p.o + b * p.o_batch + static_cast<int64_t>(s) * p.o_row + h * D + part * 8));
+    const uint4 dv = __ldg(reinterpret_cast<const uint4*>(
+        p.dout + b * p.do_batch + static_cast<int64_t>(s) * p.do_row + h * D + part * 8));
+    const uint32_t ow[4] = {ov.x, ov.y, ov.z, ov.w}, dw[4] = {dv.x, dv.y, dv.z, dv.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+      acc += bf16_lo(ow[e]) * bf16_lo(dw[e]) + bf16_hi(ow[e]) * bf16_hi(dw[e]);
+    float4* dqa = reinterpret_cast<float4*>(
+        p.dq_acc + ((static_cast<int64_t>(b) * p.Sq + s) * p.Hq + h) * D + part * 8);
+    dqa[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+    dqa[1] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  acc = warp_sum(acc);
-  if (lane == 0) p.delta[(static_cast<int64_t>(b) * p.Hq + h) * p.Sq + s] = acc;
-  float* dqa = p.dq_acc + ((static_cast<int64_t>(b) * p.Sq + s) * p.Hq + h) * D;
-  for (int d = lane; d < D; d += 32) dqa[d] = 0.f;
+#pragma unroll
+  for (int off = TPR / 2; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (ok && part == 0) p.delta[row] = acc;
+}
+
+template <int D>
+static void launch_bwd_pre(const BwdParams& p, cudaStream_t stream) {
+  const int64_t threads = static_cast<int64_t>(p.B) * p.Hq * p.Sq * (D / 8);
+  flash_bwd_pre_kernel<D><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(p);
 }
 
 __device__ __forceinline__ void red_add_v2(float* addr, float a, float b) {
@@ -555,22 +571,63 @@ __global__ void __launch_bounds__(128) flash_bwd_kernel(const BwdParams p) {
 }
 
 // dq_acc (fp32) -> dq (bf16) with optional inverse RoPE. One thread per pair.
+// dq = bf16(dq_acc), with the inverse rotate-half RoPE when positions are given. A thread
+// takes 8 rotation pairs (columns c..c+7 and c+D/2..c+D/2+7) of up to 4 heads of one
+// (b, s) row: the angles depend only on the position and the pair, so each thread
+// evaluates 8 sincosf and reuses them across its heads. 16-byte loads and stores.
+constexpr int kDqHeadsPerThread = 4;
+
 template <int D>
-__global__ void flash_bwd_dq_kernel(const BwdParams p) {
-  const int64_t idx = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t total = static_cast<int64_t>(p.B) * p.Sq * p.Hq * (D / 2);
-  if (idx >= total) return;
-  const int c = idx % (D / 2);
-  const int h = (idx / (D / 2)) % p.Hq;
-  const int s = (idx / ((D / 2) * p.Hq)) % p.Sq;
-  const int b = idx / (static_cast<int64_t>(D / 2) * p.Hq * p.Sq);
-  const float* src = p.dq_acc + ((static_cast<int64_t>(b) * p.Sq + s) * p.Hq + h) * D;
-  float x1 = src[c], x2 = src[c + D / 2];
-  if (p.q_pos != nullptr)
-    inv_rope_pair(x1, x2, static_cast<float>(__ldg(p.q_pos + s)) * __ldg(p.inv_freq + c));
-  __nv_bfloat16* dst = p.dq + b * p.dq_batch + static_cast<int64_t>(s) * p.dq_row + h * D;
-  dst[c] = __float2bfloat16_rn(x1);
-  dst[c + D / 2] = __float2bfloat16_rn(x2);
+__global__ void __launch_bounds__(256) flash_bwd_dq_kernel(const BwdParams p) {
+  constexpr int CH = D / 16;  // 8-pair chunks per head
+  const int hgroups = (p.Hq + kDqHeadsPerThread - 1) / kDqHeadsPerThread;
+  const int64_t gt = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (gt >= static_cast<int64_t>(p.B) * p.Sq * hgroups * CH) return;
+  const int j = static_cast<int>(gt % CH);
+  const int hg = static_cast<int>((gt / CH) % hgroups);
+  const int64_t bs = gt / (static_cast<int64_t>(CH) * hgroups);
+  const int s = static_cast<int>(bs % p.Sq);
+  const int b = static_cast<int>(bs / p.Sq);
+  const bool rope = p.q_pos != nullptr;
+  float cs[8], sn[8];
+  if (rope) {
+    const float pos = static_cast<float>(__ldg(p.q_pos + s));
+#pragma unroll
+    for (int e = 0; e < 8; ++e) sincosf(pos * __ldg(p.inv_freq + j * 8 + e), &sn[e], &cs[e]);
+  }
+  const int h0 = hg * kDqHeadsPerThread, h1 = min(p.Hq, h0 + kDqHeadsPerThread);
+  const float* src = p.dq_acc + bs * p.Hq * D + j * 8;
+  __nv_bfloat16* dst = p.dq + b * p.dq_batch + static_cast<int64_t>(s) * p.dq_row + j * 8;
+#pragma unroll 2
+  for (int h = h0; h < h1; ++h) {
+    const float4* a4 = reinterpret_cast<const float4*>(src + h * D);
+    const float4* b4 = reinterpret_cast<const float4*>(src + h * D + D / 2);
+    const float4 a0 = a4[0], a1 = a4[1], b0 = b4[0], b1 = b4[1];
+    float x1[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+    float x2[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    if (rope) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float u = x1[e] * cs[e] + x2[e] * sn[e];
+        const float w = x2[e] * cs[e] - x1[e] * sn[e];
+        x1[e] = u;
+        x2[e] = w;
+      }
+    }
+    *reinterpret_cast<uint4*>(dst + h * D) =
+        make_uint4(pack_bf16x2(x1[0], x1[1]), pack_bf16x2(x1[2], x1[3]),
+                   pack_bf16x2(x1[4], x1[5]), pack_bf16x2(x1[6], x1[7]));
+    *reinterpret_cast<uint4*>(dst + h * D + D / 2) =
+        make_uint4(pack_bf16x2(x2[0], x2[1]), pack_bf16x2(x2[2], x2[3]),
+                   pack_bf16x2(x2[4], x2[5]), pack_bf16x2(x2[6], x2[7]));
+  }
+}
+
+template <int D>
+static void launch_bwd_dq(const BwdParams& p, cudaStream_t stream) {
+  const int64_t threads = static_cast<int64_t>(p.B) * p.Sq *
+                          ((p.Hq + kDqHeadsPerThread - 1) / kDqHeadsPerThread) * (D / 16);
+  flash_bwd_dq_kernel<D><<<static_cast<unsigned>((threads + 255) / 256), 256, 0, stream>>>(p);
 }
 
 }  // namespace attn
@@ -706,23 +763,21 @@ void flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::
   if (p.B == 0 || p.Sq == 0) return;
   const at::cuda::CUDAGuard guard(q.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  const int rows = p.B * p.Sq * p.Hq;
   dim3 grid((p.Sk + 63) / 64, p.Hkv, p.B);
-  const int64_t pairs = static_cast<int64_t>(rows) * (D / 2);
   if (D == 64) {
-    flash_bwd_pre_kernel<64><<<(rows + 7) / 8, 256, 0, stream>>>(p); NMB_LAUNCHED(1);
+    launch_bwd_pre<64>(p, stream); NMB_LAUNCHED(1);
     const int smem = (4 * 64 * 64 + 64 * 64) * 2 + 2 * 64 * 4;
     auto kern = flash_bwd_kernel<64>;
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     kern<<<grid, 128, smem, stream>>>(p); NMB_LAUNCHED(1);
-    flash_bwd_dq_kernel<64><<<(pairs + 255) / 256, 256, 0, stream>>>(p); NMB_LAUNCHED(1);
+    launch_bwd_dq<64>(p, stream); NMB_LAUNCHED(1);
   } else {
-    flash_bwd_pre_kernel<128><<<(rows + 7) / 8, 256, 0, stream>>>(p); NMB_LAUNCHED(1);
+    launch_bwd_pre<128>(p, stream); NMB_LAUNCHED(1);
     const int smem = (4 * 64 * 128 + 64 * 64) * 2 + 2 * 64 * 4;
     auto kern = flash_bwd_kernel<128>;
     C10_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     kern<<<grid, 128, smem, stream>>>(p); NMB_LAUNCHED(1);
-    flash_bwd_dq_kernel<128><<<(pairs + 255) / 256, 256, 0, stream>>>(p); NMB_LAUNCHED(1);
+    launch_bwd_dq<128>(p, stream); NMB_LAUNCHED(1);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -766,8 +821,6 @@ static float* noalloc_scratch_for_current_device(int* err) {
 
 template <int D>
 static int noalloc_launch(const BwdParams& p, cudaStream_t stream) {
-  const int rows = p.B * p.Sq * p.Hq;
-  const int64_t pairs = static_cast<int64_t>(rows) * (D / 2);
   const int smem = (4 * 64 * D + 64 * 64) * 2 + 2 * 64 * 4;
   if (cudaFuncSetAttribute(flash_bwd_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            smem) != cudaSuccess)
@@ -779,7 +832,7 @@ static int noalloc_launch(const BwdParams& p, cudaStream_t stream) {
   // pre: delta = rowsum(dO * O) and dq_acc = 0; the main kernel adds into dq_acc; dq:
   // dq = bf16(dq_acc). With no keys (Sk == 0) the main kernel has nothing to do and dq
   // comes out as zeros.
-  flash_bwd_pre_kernel<D><<<(rows + 7) / 8, 256, 0, stream>>>(p);
+  launch_bwd_pre<D>(p, stream);
   if (cudaGetLastError() != cudaSuccess) return NMB_NOALLOC_LAUNCH_FAILED;
   int launched = 1;
   if (p.Sk > 0) {
@@ -787,7 +840,7 @@ static int noalloc_launch(const BwdParams& p, cudaStream_t stream) {
     if (cudaGetLastError() != cudaSuccess) return NMB_NOALLOC_LAUNCH_FAILED;
     ++launched;
   }
-  flash_bwd_dq_kernel<D><<<(pairs + 255) / 256, 256, 0, stream>>>(p);
+  launch_bwd_dq<D>(p, stream);
   if (cudaGetLastError() != cudaSuccess) return NMB_NOALLOC_LAUNCH_FAILED;
   NMB_LAUNCHED(launched + 1);
   return NMB_NOALLOC_OK;
@@ -896,11 +949,10 @@ void flash_attn_bwd_prep(at::Tensor o, at::Tensor dout, at::Tensor delta, at::Te
   if (p.B == 0 || p.Sq == 0) return;
   const at::cuda::CUDAGuard guard(o.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  const int rows = p.B * p.Sq * p.Hq;
   if (D == 64)
-    flash_bwd_pre_kernel<64><<<(rows + 7) / 8, 256, 0, stream>>>(p);
+    launch_bwd_pre<64>(p, stream);
   else
-    flash_bwd_pre_kernel<128><<<(rows + 7) / 8, 256, 0, stream>>>(p);
+    launch_bwd_pre<128>(p, stream);
   NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -924,11 +976,10 @@ void flash_attn_bwd_dq_convert(at::Tensor dq_acc, at::Tensor dq, c10::optional<a
   if (p.B == 0 || p.Sq == 0) return;
   const at::cuda::CUDAGuard guard(dq.device());
   cudaStream_t stream = at::cuda::getCurrentCUDAStream();
-  const int64_t pairs = static_cast<int64_t>(p.B) * p.Sq * p.Hq * (D / 2);
   if (D == 64)
-    flash_bwd_dq_kernel<64><<<(pairs + 255) / 256, 256, 0, stream>>>(p);
+    launch_bwd_dq<64>(p, stream);
   else
-    flash_bwd_dq_kernel<128><<<(pairs + 255) / 256, 256, 0, stream>>>(p);
+    launch_bwd_dq<128>(p, stream);
   NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

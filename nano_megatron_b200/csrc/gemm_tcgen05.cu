@@ -103,7 +103,13 @@ struct CommMaps {
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;                // one 128-byte swizzle row of bf16
-constexpr int kThreads = 192;
+// Epilogue warps: two per TMEM lane quarter (each drains half of the tile's columns), so
+// two warps per SM sub-partition overlap their TMEM loads, global loads and math; the peer
+// epilogue keeps one per quarter (its shared staging area is per quarter).
+template <int EPI>
+__host__ __device__ constexpr int epi_warps() { return EPI == 4 /*kEpiPeer*/ ? 4 : 8; }
+template <int EPI>
+__host__ __device__ constexpr int gemm_threads() { return 64 + 32 * epi_warps<EPI>(); }
 constexpr int kUmmaK = 16;
 
 template <int BN>
@@ -128,7 +134,9 @@ constexpr int gemm_smem_bytes() {
   return GemmCfg<BN>::kSmemBytes + (EPI == kEpiPeer ? kPeerStageBytes : 0);
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// silu(x) = x / (1 + e^-x) with the fast reciprocal-based division (the result is
+// rounded to bf16); for x < -87, e^-x is +inf and the quotient is -0, the limit.
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // Store 32 fp32 values as bf16 to row pointer `dst` (cols [col, col+32)), predicated on N.
 __device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, int col, int ncols,
@@ -213,7 +221,7 @@ __device__ __forceinline__ void red_add_v4(float* out, float a, float b, float c
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI, bool GATHER>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CommMaps cm, const GemmParams p) {
@@ -243,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull_bar[a], 1);
-      mbar_init(&tempty_bar[a], 4);  // one arrive per epilogue warp
+      mbar_init(&tempty_bar[a], epi_warps<EPI>());  // one arrive per epilogue warp
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -399,6 +407,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ------------------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    // column share of this warp: part `ew` of `kParts` equal parts of the tile
+    constexpr int kParts = epi_warps<EPI>() / 4;
+    const int ew = (warp - 2) / 4;
     const int lane = threadIdx.x & 31;
     const float alpha = p.alpha_ptr != nullptr ? p.alpha * __ldg(p.alpha_ptr) : p.alpha;
     // peer epilogue: this call's epoch is the next one (the signal kernel advances it later)
@@ -466,6 +477,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else if constexpr (EPI == kEpiBF16 || EPI == kEpiF32Acc) {
         const int n0 = nt * BN;
+        constexpr int kChunks = BN / 32 / kParts;   // 32-column chunks of this warp
+        const int c_begin = ew * kChunks, c_end = c_begin + kChunks;
         // Residual (kEpiBF16): each thread reads its own row, 32 columns = 64 bytes per
         // chunk, as four 16-byte loads issued one chunk ahead of their use, so the global
         // latency overlaps the TMEM drain of the previous chunk.
@@ -475,16 +488,16 @@ __global__ void __launch_bounds__(kThreads, 1)
             res_vec ? reinterpret_cast<const uint4*>(p.R + static_cast<int64_t>(row) * p.ldr + n0)
                     : nullptr;
         uint4 res_next[4];
-        if (res_vec && n0 + 32 <= p.N) {
+        if (res_vec && n0 + (c_begin + 1) * 32 <= p.N) {
 #pragma unroll
-          for (int q = 0; q < 4; ++q) res_next[q] = __ldg(res_row + q);
+          for (int q = 0; q < 4; ++q) res_next[q] = __ldg(res_row + c_begin * 4 + q);
         }
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = c_begin; c < c_end; ++c) {
           uint4 res_cur[4];
 #pragma unroll
           for (int q = 0; q < 4; ++q) res_cur[q] = res_next[q];
-          if (res_vec && c + 1 < BN / 32 && n0 + (c + 2) * 32 <= p.N) {
+          if (res_vec && c + 1 < c_end && n0 + (c + 2) * 32 <= p.N) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) res_next[q] = __ldg(res_row + (c + 1) * 4 + q);
           }
@@ -549,8 +562,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else if constexpr (EPI == kEpiSwiGLU) {
         const int n0h = nt * (BN / 2);
+        constexpr int kChunks = BN / 64 / kParts;   // 32-column gate/up chunk pairs
 #pragma unroll 1
-        for (int c = 0; c < BN / 64; ++c) {
+        for (int c = ew * kChunks; c < (ew + 1) * kChunks; ++c) {
           uint32_t g[32], u[32];
           tmem_ld_32x32b_x32(tbase + c * 32, g);
           tmem_ld_32x32b_x32(tbase + BN / 2 + c * 32, u);
@@ -581,10 +595,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int chunks_per_head = D / 32;
         const int slot = row_ok ? (row / p.pos_div) % p.seq_len : 0;
         const int pos = row_ok ? __ldg(p.positions + slot) : 0;
+        // (head, half-chunk) pairs of the tile, dealt round-robin to the kParts warps
+        const int pairs = (BN / D) * half_chunks;
 #pragma unroll 1
-        for (int h = 0; h < BN / D; ++h) {
-#pragma unroll 1
-          for (int j = 0; j < half_chunks; ++j) {
+        for (int i = ew; i < pairs; i += kParts) {
+          {
+            const int h = i / half_chunks, j = i % half_chunks;
             const int c_lo = h * chunks_per_head + j;
             const int c_hi = c_lo + half_chunks;
             uint32_t lo[32], hi[32];
@@ -706,7 +722,7 @@ static void launch(const CUtensorMap& ta, const CUtensorMap& tb, GemmParams& p,
   }
   const int tiles = p.num_m_tiles * p.num_n_tiles * p.splits;
   int grid = std::min(tiles, max_ctas > 0 ? max_ctas : num_sms());
-  kern<<<grid, kThreads, smem_bytes, stream>>>(ta, tb, cm, p); NMB_LAUNCHED(1);
+  kern<<<grid, gemm_threads<EPI>(), smem_bytes, stream>>>(ta, tb, cm, p); NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

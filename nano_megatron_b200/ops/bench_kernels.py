@@ -1,13 +1,15 @@
 """Kernel microbenchmarks: CUDA-event timing of each sm_100a kernel vs its library baseline.
 
-    python -m nano_megatron_b200.ops.bench_kernels [--case all|gemm|gemm_tiles|attn|mem] [--iters N]
+    python -m nano_megatron_b200.ops.bench_kernels [--case all|gemm|gemm_tiles|gemm_layer|attn|mem] [--iters N]
 
 Prints one JSON object of achieved TFLOP/s (GEMM, attention) or GB/s and the fraction of
 the measured copy bandwidth (memory-bound kernels: RMSNorm, SwiGLU backward, attention
 backward prep / dQ conversion, embedding, AdamW). ``--case gemm_tiles`` sweeps the GEMM
 tile width (``block_n`` 128 and 256) on the 311M model's shapes, the data behind the tile
-choice in ``choose_bn`` (csrc/gemm_tcgen05.cu). Also the small, self-contained workload used for ncu captures
-(``--case gemm_profile`` / ``attn_profile`` run a few launches of one kernel).
+choice in ``choose_bn`` (csrc/gemm_tcgen05.cu); ``--case gemm_layer`` times the layer's
+GEMMs with their fused epilogues (RoPE, SwiGLU, residual) against the plain product. Also the small, self-contained workload used for ncu captures
+(``--case gemm_profile`` / ``gemm_epi_profile:<swiglu|rope|residual>`` / ``attn_profile[:d128]``
+run a few launches of one kernel).
 """
 
 from __future__ import annotations
@@ -96,6 +98,67 @@ def gemm_tile_cases(iters: int) -> dict:
                 lambda: G.gemm(dy, x, cf, a_mn=True, b_mn=True, epilogue=G.EPI_F32_ACC,
                                beta=1.0, block_n=bn), iters) / 1e9
     return res
+
+
+def gemm_layer_cases(iters: int, m: int = 8192) -> dict:
+    """TFLOP/s of the 311M layer's GEMMs with the epilogues the model runs (RoPE on the
+    QKV projection, SwiGLU on gate/up, residual add on the output and down projections),
+    next to the plain product and cuBLAS at the same shape (``m`` tokens per call)."""
+    res = {}
+    hid, ffn, seq, hd = 1024, 2736, 512, 64
+    x = torch.randn(m, hid, device="cuda").bfloat16()
+    pos = torch.arange(seq, device="cuda", dtype=torch.int32)
+    inv_freq = 1.0 / (10000.0 ** (torch.arange(0, hd, 2, device="cuda").float() / hd))
+    w_qkv = torch.randn(3 * hid, hid, device="cuda").bfloat16()
+    qkv = torch.empty(m, 3 * hid, device="cuda", dtype=torch.bfloat16)
+    fl = 2 * m * 3 * hid * hid
+    res["qkv_rope"] = fl / _time(lambda: G.qkv_rope_fwd(x, w_qkv, pos, inv_freq, hd, 2 * hid,
+                                                         out=qkv), iters) / 1e9
+    res["qkv_plain"] = fl / _time(lambda: G.gemm(x, w_qkv, qkv), iters) / 1e9
+    res["qkv_cublas"] = fl / _time(lambda: torch.matmul(x, w_qkv.t(), out=qkv), iters) / 1e9
+    w_gu = torch.randn(2 * ffn, hid, device="cuda").bfloat16()
+    h = torch.empty(m, ffn, device="cuda", dtype=torch.bfloat16)
+    gu = torch.empty(m, 2 * ffn, device="cuda", dtype=torch.bfloat16)
+    fl = 2 * m * 2 * ffn * hid
+    res["gate_up_swiglu"] = fl / _time(lambda: G.swiglu_fwd(x, w_gu, ffn, out=h, gate_up=gu),
+                                       iters) / 1e9
+    res["gate_up_plain"] = fl / _time(lambda: G.gemm(x, w_gu, gu), iters) / 1e9
+    res["gate_up_cublas"] = fl / _time(lambda: torch.matmul(x, w_gu.t(), out=gu), iters) / 1e9
+    for name, k in (("out_proj", hid), ("down_proj", ffn)):
+        a = torch.randn(m, k, device="cuda").bfloat16()
+        w = torch.randn(hid, k, device="cuda").bfloat16()
+        r = torch.randn(m, hid, device="cuda").bfloat16()
+        y = torch.empty(m, hid, device="cuda", dtype=torch.bfloat16)
+        fl = 2 * m * hid * k
+        res[f"{name}_residual"] = fl / _time(lambda: G.gemm(a, w, y, residual=r), iters) / 1e9
+        res[f"{name}_plain"] = fl / _time(lambda: G.gemm(a, w, y), iters) / 1e9
+        res[f"{name}_cublas"] = fl / _time(lambda: torch.matmul(a, w.t(), out=y), iters) / 1e9
+    return res
+
+
+def gemm_epilogue_profile(epi: str) -> None:
+    """Three launches of one fused-epilogue GEMM of the 311M layer (M=8192), for ncu."""
+    m, hid, ffn = 8192, 1024, 2736
+    x = torch.randn(m, hid, device="cuda").bfloat16()
+    if epi == "swiglu":
+        w = torch.randn(2 * ffn, hid, device="cuda").bfloat16()
+        h = torch.empty(m, ffn, device="cuda", dtype=torch.bfloat16)
+        gu = torch.empty(m, 2 * ffn, device="cuda", dtype=torch.bfloat16)
+        fn = lambda: G.swiglu_fwd(x, w, ffn, out=h, gate_up=gu)  # noqa: E731
+    elif epi == "rope":
+        pos = torch.arange(512, device="cuda", dtype=torch.int32)
+        inv = 1.0 / (10000.0 ** (torch.arange(0, 64, 2, device="cuda").float() / 64))
+        w = torch.randn(3 * hid, hid, device="cuda").bfloat16()
+        y = torch.empty(m, 3 * hid, device="cuda", dtype=torch.bfloat16)
+        fn = lambda: G.qkv_rope_fwd(x, w, pos, inv, 64, 2 * hid, out=y)  # noqa: E731
+    else:  # residual: the output projection
+        w = torch.randn(hid, hid, device="cuda").bfloat16()
+        r = torch.randn(m, hid, device="cuda").bfloat16()
+        y = torch.empty(m, hid, device="cuda", dtype=torch.bfloat16)
+        fn = lambda: G.gemm(x, w, y, residual=r)  # noqa: E731
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
 
 
 def attn_cases(iters: int) -> dict:
@@ -211,13 +274,20 @@ def main() -> None:
             G.gemm(x, w, c)
         torch.cuda.synchronize()
         return
-    if a.case == "attn_profile":
-        b, s, h, d = 8, 512, 16, 64
-        qkv = torch.randn(b, s, 3 * h, d, device="cuda").bfloat16()
+    if a.case.startswith("gemm_epi_profile"):  # gemm_epi_profile:swiglu|rope|residual
+        gemm_epilogue_profile(a.case.split(":", 1)[1] if ":" in a.case else "swiglu")
+        return
+    if a.case.startswith("attn_profile"):  # attn_profile[:d128] -> fwd + bwd, 3 launches
+        b, s, h, hkv, d = (1, 8192, 8, 2, 128) if a.case.endswith("d128") else (16, 512, 16, 16, 64)
+        qkv = torch.randn(b, s, h + 2 * hkv, d, device="cuda").bfloat16()
+        q, k, v = qkv[:, :, :h], qkv[:, :, h:h + hkv], qkv[:, :, h + hkv:]
         o = torch.empty(b, s, h, d, device="cuda", dtype=torch.bfloat16)
         lse = torch.empty(b, h, s, device="cuda")
+        dqkv = torch.empty_like(qkv)
         for _ in range(3):
-            F.flash_fwd(qkv[:, :, :h], qkv[:, :, h:2 * h], qkv[:, :, 2 * h:], o, lse, 0.125, True)
+            F.flash_fwd(q, k, v, o, lse, d ** -0.5, True)
+            F.attention_bwd(q, k, v, o, o, lse, dqkv[:, :, :h], dqkv[:, :, h:h + hkv],
+                            dqkv[:, :, h + hkv:], causal=True)
         torch.cuda.synchronize()
         return
     out = {}
@@ -225,6 +295,8 @@ def main() -> None:
         out.update(gemm_cases(a.iters))
     if a.case == "gemm_tiles":
         out.update(gemm_tile_cases(a.iters))
+    if a.case in ("all", "gemm_layer"):
+        out.update(gemm_layer_cases(a.iters))
     if a.case in ("all", "attn"):
         out.update(attn_cases(a.iters))
     if a.case in ("all", "mem", "norm"):
