@@ -20,7 +20,8 @@ holds chunks r and 2*CP-1-r of 2*CP equal chunks) so causal work is balanced.
 
 from __future__ import annotations
 
-from .attention import (AllGatherContextParallelAttention, PeerRingContextParallelAttention,
+from .attention import (AllGatherContextParallelAttention,
+                        PeerAllGatherContextParallelAttention, PeerRingContextParallelAttention,
                         RingContextParallelAttention)
 from .utils import local_positions, shard_sequence, unshard_sequence
 
@@ -31,7 +32,9 @@ def build_context_parallel_attention(config, parallel):
     backend = str(getattr(config.backend, "value", config.backend))
     balance = bool(getattr(config, "load_balance", False))
     if backend == "all_gather":
-        return AllGatherContextParallelAttention(parallel.cp, load_balance=balance)
+        # the peer-memory gather / reduce-scatter is attached later (attach_cp_heap) when the
+        # layout allows it; until then (and on CPU) this core runs the NCCL all-gather
+        return PeerAllGatherContextParallelAttention(parallel.cp, load_balance=balance)
     if backend == "ring":
         # the peer-memory transport is attached later (attach_cp_heap) when the layout
         # allows it; until then (and on CPU) this core runs the NCCL ring
@@ -39,7 +42,8 @@ def build_context_parallel_attention(config, parallel):
     raise ValueError(f"unknown context-parallel backend {backend!r}")
 
 
-__all__ = ["AllGatherContextParallelAttention", "PeerRingContextParallelAttention",
+__all__ = ["AllGatherContextParallelAttention", "PeerAllGatherContextParallelAttention",
+           "PeerRingContextParallelAttention",
            "RingContextParallelAttention",
            "build_context_parallel_attention", "local_positions", "shard_sequence",
            "unshard_sequence"]

@@ -400,3 +400,115 @@ class PeerRingContextParallelAttention(RingContextParallelAttention):
         lv = mine.view(-1, B, 2, hkv, D)
         dk.copy_(lv[:, :, 0].transpose(0, 1))
         dv.copy_(lv[:, :, 1].transpose(0, 1))
+
+
+class PeerAllGatherContextParallelAttention(PeerRingContextParallelAttention):
+    """All-gather context parallelism whose K/V gather and dK/dV reduce-scatter go through
+    NVLink peer memory instead of NCCL collectives.
+
+    Forward: every rank publishes the layer's K/V block into its heap slot and signals;
+    each peer's block is then pulled (plain peer loads after a bounded wait on the owner's
+    flag) straight into its place in the global-order K/V buffer -- the zig-zag halves of
+    a load-balanced layout land at their global chunk positions, so no reordering pass is
+    needed -- and the flash kernels run each local query chunk against the full K/V, as
+    in :class:`AllGatherContextParallelAttention`. The gathered buffer is kept for the
+    backward pass. Backward: dK/dV over the full K/V are accumulated in fp32; each owner's
+    rows are stored into its return slot by peer stores, and after one signal every rank
+    adds the partials of all peers to its own rows (the reduce-scatter).
+    Reference: src/nano_megatron/context_parallel/all_gather.py:38-113 (NCCL all-gather of
+    K/V, reduce-scatter of their gradients). Falls back to the NCCL all-gather without a
+    heap.
+    """
+
+    _gather = AllGatherContextParallelAttention._gather
+
+    def _chunk_rows(self, rank: int, S: int):
+        """(local row start, rows, global row start) of ``rank``'s K/V block pieces."""
+        if not self.load_balance:
+            return [(0, S, rank * S)]
+        c = S // 2
+        a, b = chunk_ids(rank, self.group.size, True)
+        return [(0, c, a * c), (c, c, b * c)]
+
+    def forward(self, q, k, v, o, mb):
+        if not self._usable(q, mb):
+            return AllGatherContextParallelAttention.forward(self, q, k, v, o, mb)
+        from nano_megatron_b200.ops._ext import lib
+
+        layer = mb.extra["layer"]
+        B, Sq, Hq, D = q.shape
+        hkv = k.shape[2]
+        g, h = self.group, self.heap
+        S = k.shape[1]
+        row = B * 2 * hkv * D                                  # elements per sequence row
+        own = self._slot_view(layer)
+        own.view(-1, B, 2 * hkv * D).copy_(_kv_rows(q, k, v))  # publish this layer's K/V
+        lib().peer_signal(h.signal_targets(CH_KV), h.epoch_ptr(CH_KV))
+        full = torch.empty(g.size * S, B, 2 * hkv * D, device=q.device, dtype=q.dtype)
+        flat = full.view(-1)
+        for r in range(g.size):
+            for lo, rows, glo in self._chunk_rows(r, S):
+                dst = flat[glo * row:(glo + rows) * row]
+                if r == g.rank:
+                    dst.copy_(own[lo * row:(lo + rows) * row])
+                else:
+                    lib().cp_pull(self._slot_ptr(r, layer) + lo * row * 2, dst,
+                                  h.flag_slots(h.rank, CH_KV) + r * 4, h.epoch_ptr(CH_KV),
+                                  h.status)
+        kvf = full.view(g.size * S, B, 2, hkv, D)
+        kf, vf = kvf[:, :, 0].transpose(0, 1), kvf[:, :, 1].transpose(0, 1)
+        o_bs = o.transpose(0, 1)
+        lse = torch.empty(B, Hq, Sq, device=q.device, dtype=torch.float32)
+        for start, rows, off in self.q_chunks(Sq):
+            oc, lc = F.attention_fwd(q[:, start:start + rows], kf, vf, causal=True,
+                                     q_offset=off, k_offset=0)
+            o_bs[:, start:start + rows].copy_(oc)
+            lse[:, :, start:start + rows].copy_(lc)
+        mb.extra["cp_kv_full"] = full
+        return lse
+
+    def backward(self, q, k, v, o, do, lse, dq, dk, dv, mb, inv_freq):
+        if not self._usable(q, mb) or "cp_kv_full" not in mb.extra:
+            return AllGatherContextParallelAttention.backward(self, q, k, v, o, do, lse, dq, dk,
+                                                              dv, mb, inv_freq)
+        from nano_megatron_b200.ops._ext import lib
+
+        full = mb.extra.pop("cp_kv_full")
+        B, S, hkv, D = k.shape
+        Hq = q.shape[2]
+        g, h = self.group, self.heap
+        row = B * 2 * hkv * D
+        kvf = full.view(-1, B, 2, hkv, D)
+        kf, vf = kvf[:, :, 0].transpose(0, 1), kvf[:, :, 1].transpose(0, 1)
+        Stot = kf.shape[1]
+        dfull = torch.zeros(Stot, B, 2 * hkv * D, dtype=torch.float32, device=q.device)
+        dview = dfull.view(Stot, B, 2, hkv, D)
+        o_bs = o.transpose(0, 1)
+        for start, rows, off in self.q_chunks(q.shape[1]):
+            dkc = torch.empty(B, Stot, hkv, D, device=q.device, dtype=q.dtype)
+            dvc = torch.empty_like(dkc)
+            F.attention_bwd(q[:, start:start + rows], kf, vf, o_bs[:, start:start + rows],
+                            do[:, start:start + rows], lse[:, :, start:start + rows].contiguous(),
+                            dq[:, start:start + rows], dkc, dvc, causal=True, q_offset=off,
+                            k_offset=0)
+            dview[:, :, 0] += dkc.transpose(0, 1).float()
+            dview[:, :, 1] += dvc.transpose(0, 1).float()
+        dflat = dfull.view(-1)
+        mine = torch.empty(S * row, dtype=torch.float32, device=q.device)
+        for r in range(g.size):
+            for lo, rows, glo in self._chunk_rows(r, S):
+                part = dflat[glo * row:(glo + rows) * row]
+                if r == g.rank:
+                    mine[lo * row:(lo + rows) * row].copy_(part)
+                else:   # peer stores into r's return slot for this source rank
+                    lib().cp_push(part, self._ret_ptr(r, 0, g.rank) + lo * row * 4,
+                                  self._ret_ptr(r, 1, g.rank) + lo * row * 4,
+                                  h.epoch_ptr(CH_DKV))
+        lib().peer_signal(h.signal_targets(CH_DKV), h.epoch_ptr(CH_DKV))
+        mask = sum(1 << r for r in range(g.size) if r != g.rank)
+        lib().cp_reduce(mine, [self._ret_ptr(h.rank, 0, s) for s in range(g.size)],
+                        [self._ret_ptr(h.rank, 1, s) for s in range(g.size)], mask,
+                        h.flag_slots(h.rank, CH_DKV), h.epoch_ptr(CH_DKV), h.status)
+        lv = mine.view(S, B, 2, hkv, D)
+        dk.copy_(lv[:, :, 0].transpose(0, 1))
+        dv.copy_(lv[:, :, 1].transpose(0, 1))

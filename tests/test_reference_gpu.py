@@ -117,6 +117,12 @@ def test_bf16_loss_curve_matches_reference():
         pytest.skip("reference implementation not installed")
     ours, theirs = _run("ours"), _run("reference")
     assert len(ours) == len(theirs) == STEPS
+    out = os.environ.get("NMB_PARITY_OUT")
+    if out:   # keep the two curves for the record (a summary is committed under profiles/)
+        with open(out, "w") as f:
+            json.dump({"ours": ours, "reference": theirs,
+                       "max_rel_diff": max(abs(a - b) / abs(b) for a, b in zip(ours, theirs))},
+                      f)
     # identical initial weights and data: the first loss agrees to bf16 rounding, later
     # steps within bf16 training noise (the reference updates bf16 parameters in place,
     # this framework keeps fp32 masters)
