@@ -125,8 +125,9 @@ def test_bf16_loss_curve_matches_reference():
                       f)
     # identical initial weights and data: the first loss agrees to bf16 rounding, later
     # steps within bf16 training noise (the reference updates bf16 parameters in place,
-    # this framework keeps fp32 masters)
+    # this framework keeps fp32 masters). Measured on B200 over these 8 steps: at most
+    # 0.17 % apart, so 1 % leaves a 6x margin.
     assert ours[0] == pytest.approx(theirs[0], rel=5e-3), (ours, theirs)
     for a, b in zip(ours, theirs):
-        assert a == pytest.approx(b, rel=5e-2), (ours, theirs)
+        assert a == pytest.approx(b, rel=1e-2), (ours, theirs)
     assert ours[-1] < ours[0] - 0.3 and theirs[-1] < theirs[0] - 0.3, (ours, theirs)
