@@ -72,9 +72,29 @@ struct Params {
   float scale_log2, scale;
   const int* k_pos;
   const float* inv_freq;
+  const float2* k_cs;   // optional (cos, sin)(k_pos[row] * inv_freq[i]) table [Sk][D/2]
+  // optional phase trace: kTraceSlots %globaltimer stamps per CTA (see kTrace* below)
+  unsigned long long* trace;
   int* status;
   PullDesc pull;
 };
+
+// Phase trace layout per CTA (nanoseconds, %globaltimer): [0] entry, [1] set-up done,
+// [2] end of the dK/dV epilogue; softmax thread, for the first kTraceSteps steps t:
+// [3 + 6t + e] e = 0 step start, 1 S/dP ready, 2 P/dS tiles free, 3 P/dS written,
+// 4 dV/dK/dQ done, 5 dQ drained; MMA thread: [3 + 6 kTraceSteps + 2t + e] e = 0 Q/dO
+// landed, 1 P/dS ready. Written only when Params::trace is set (a diagnostic run).
+// [3 + 8 kTraceSteps + e]: inside step 0's first P/dS chunk, e = 0 TMEM loads landed,
+// 1 values computed, 2 tiles stored; e = 3 all chunks done.
+constexpr int kTraceSteps = 5;
+constexpr int kTraceChunk = 3 + 8 * kTraceSteps;
+constexpr int kTraceSlots = kTraceChunk + 4;
+
+__device__ __forceinline__ void trace_stamp(const Params& p, int slot) {
+  if (p.trace != nullptr)
+    p.trace[(blockIdx.x + static_cast<long long>(gridDim.x) * blockIdx.y) * kTraceSlots + slot] =
+        globaltimer_ns();
+}
 
 __device__ __forceinline__ float ex2(float x) {
   float y;
@@ -169,6 +189,7 @@ __global__ void __launch_bounds__(threads_for<SH>(), 1)
   const int steps_per_head = max(0, num_mb - m_begin);
   const int total_steps = steps_per_head * group;
 
+  if (threadIdx.x == 64) trace_stamp(p, 0);
   if (threadIdx.x == 0) {
     for (int i = 0; i < 9; ++i) mbar_init(&bars[i], (i == 6 || i == 8) ? 4 * SH : 1);
     *abort_flag = 0;
@@ -186,6 +207,7 @@ __global__ void __launch_bounds__(threads_for<SH>(), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 64) trace_stamp(p, 1);
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
@@ -226,6 +248,7 @@ __global__ void __launch_bounds__(threads_for<SH>(), 1)
         const uint32_t aQ = smem_u32(sQ0 + st * C::kTile), aDO = smem_u32(sDO0 + st * C::kTile);
         ok = mbar_wait(&qdo_full[st], static_cast<uint32_t>(t / QS) & 1u, p.status,
                        kStatusAttnTimeout, abort_flag);
+        if (t < kTraceSteps) trace_stamp(p, 3 + 6 * kTraceSteps + 2 * t);
         // Unpipelined: S^T shares TMEM with the previous step's dQ, which must be drained.
         if (ok && !C::kPipe && t > 0)
           ok = mbar_wait(dq_free, (t - 1) & 1, p.status, kStatusAttnTimeout, abort_flag);
@@ -242,6 +265,7 @@ __global__ void __launch_bounds__(threads_for<SH>(), 1)
         }
         umma_commit(sdp_full);
         ok = mbar_wait(pds_full, t & 1, p.status, kStatusAttnTimeout, abort_flag);
+        if (t < kTraceSteps) trace_stamp(p, 3 + 6 * kTraceSteps + 2 * t + 1);
         // Pipelined: the previous dQ (own columns) must be drained before this step's dQ.
         if (ok && C::kPipe && t > 0)
           ok = mbar_wait(dq_free, (t - 1) & 1, p.status, kStatusAttnTimeout, abort_flag);
@@ -281,18 +305,31 @@ __global__ void __launch_bounds__(threads_for<SH>(), 1)
     const int krow = n0 + row;
     const int kpos = p.k_offset + krow;
     bool ok = true;
+    // lse / delta of a step's query block: the first group's 128 threads read one value
+    // each, one step ahead (issued before this step's dQ drain, so the global latency is
+    // off the critical path), and publish them in shared memory at the step's start
+    float lse_next = INFINITY, delta_next = 0.f;
+    auto fetch_ld = [&](int t) {
+      if (half != 0 || t >= total_steps) return;
+      const int h = kvh * group + t / steps_per_head;
+      const int q = (m_begin + t % steps_per_head) * kBM + row;
+      const int64_t base = (static_cast<int64_t>(b) * p.Hq + h) * p.Sq;
+      lse_next = q < p.Sq ? __ldg(p.lse + base + q) : INFINITY;
+      delta_next = q < p.Sq ? __ldg(p.delta + base + q) : 0.f;
+    };
+    fetch_ld(0);
     for (int t = 0; t < total_steps; ++t) {
       const int h = kvh * group + t / steps_per_head;
       const int m0 = (m_begin + t % steps_per_head) * kBM;
-      // lse / delta of this query block (read by the first group's 128 threads, one each)
       if (half == 0) {
-        const int64_t base = (static_cast<int64_t>(b) * p.Hq + h) * p.Sq;
-        const int q = m0 + row;
-        sLse[row] = q < p.Sq ? p.lse[base + q] : INFINITY;
-        sDelta[row] = q < p.Sq ? p.delta[base + q] : 0.f;
+        sLse[row] = lse_next;
+        sDelta[row] = delta_next;
       }
       asm volatile("bar.sync 1, %0;" ::"n"(128 * SH) : "memory");
+      const bool tr = threadIdx.x == 64 && t < kTraceSteps;
+      if (tr) trace_stamp(p, 3 + 6 * t);
       if (ok) ok = mbar_wait(sdp_full, t & 1, p.status, kStatusAttnTimeout, abort_flag);
+      if (tr) trace_stamp(p, 3 + 6 * t + 1);
       ok = __all_sync(0xffffffffu, ok);  // keep TMEM ops warp-uniform
       if (!ok) continue;  // keep joining the named barrier until the loop ends
       tc_fence_after();
@@ -302,6 +339,7 @@ __global__ void __launch_bounds__(threads_for<SH>(), 1)
         ok = __all_sync(0xffffffffu, ok);  // keep TMEM ops warp-uniform
       if (!ok) continue;  // keep joining the named barrier until the loop ends
       }
+      if (tr) trace_stamp(p, 3 + 6 * t + 2);
       const bool diag = p.causal && (p.k_offset + n0 + kBN - 1 > p.q_offset + m0);
       const bool tail = (m0 + kBM > p.Sq) || (n0 + kBN > p.Sk);
       // One 32-query chunk at a time: exponentiate, form dS, and store both bf16 chunks
@@ -313,35 +351,73 @@ __global__ void __launch_bounds__(threads_for<SH>(), 1)
         uint32_t sr[32], dr[32];
         tmem_ld_32x32b_x32(tmem + lo + C::kColS + c * 32, sr);
         tmem_ld_32x32b_x32(tmem + lo + C::kColDP + c * 32, dr);
+        // The chunk's 32 query statistics (the same for every thread), read as 16-byte
+        // shared loads while the TMEM loads are in flight: one load latency per chunk
+        // instead of one per element (per-element reads of these values, interleaved
+        // with the tile stores, serialised the phase on load latency).
+        float lq[32], dl[32];
+        {
+          const float4* l4 = reinterpret_cast<const float4*>(sLse + c * 32);
+          const float4* d4 = reinterpret_cast<const float4*>(sDelta + c * 32);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const float4 a = l4[i], bq = d4[i];
+            lq[4 * i] = a.x;
+            lq[4 * i + 1] = a.y;
+            lq[4 * i + 2] = a.z;
+            lq[4 * i + 3] = a.w;
+            dl[4 * i] = bq.x;
+            dl[4 * i + 1] = bq.y;
+            dl[4 * i + 2] = bq.z;
+            dl[4 * i + 3] = bq.w;
+          }
+        }
         tmem_wait_ld();
+        const bool trc = tr && t == 0 && c == half * kChunks;
+        if (trc) trace_stamp(p, kTraceChunk);
         uint32_t ppk[16], dpk[16];
+        // Visible query columns of this key row within the chunk: [vis_lo, vis_hi)
+        // (all 32 outside diagonal / tail blocks); masked entries get P = 0 by a select.
+        int vis_lo = 0, vis_hi = 32;
+        if (diag || tail) {
+          const int q0 = m0 + c * 32;
+          vis_hi = krow < p.Sk ? min(32, p.Sq - q0) : 0;
+          if (p.causal) vis_lo = max(0, kpos - p.q_offset - q0);
+        }
+        // Stage by stage over the 32 elements (all exponent arguments, then all
+        // exponentials, then dS), so the 32 independent MUFU operations are in flight
+        // together instead of one dependency chain per element.
+        float pr[32], ds[32];
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pr[e] = fmaf(__uint_as_float(sr[e]), p.scale_log2, -lq[e]);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pr[e] = ex2(pr[e]);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pr[e] = (e >= vis_lo && e < vis_hi) ? pr[e] : 0.f;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) ds[e] = pr[e] * (__uint_as_float(dr[e]) - dl[e]);
 #pragma unroll
         for (int e = 0; e < 32; e += 2) {
-          float pv[2], dsv[2];
-#pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int qc = c * 32 + e + u;
-            float pr = ex2(__uint_as_float(sr[e + u]) * p.scale_log2 - sLse[qc]);
-            if ((diag || tail) &&
-                (m0 + qc >= p.Sq || krow >= p.Sk || (p.causal && kpos > p.q_offset + m0 + qc)))
-              pr = 0.f;
-            pv[u] = pr;
-            dsv[u] = pr * (__uint_as_float(dr[e + u]) - sDelta[qc]);
-          }
-          ppk[e / 2] = pack_bf16x2(pv[0], pv[1]);
-          dpk[e / 2] = pack_bf16x2(dsv[0], dsv[1]);
+          ppk[e / 2] = pack_bf16x2(pr[e], pr[e + 1]);
+          dpk[e / 2] = pack_bf16x2(ds[e], ds[e + 1]);
         }
+        if (trc) trace_stamp(p, kTraceChunk + 1);
         store_chunk_sw128(sP, row, c, ppk);
         store_chunk_sw128(sDS, row, c, dpk);
+        if (trc) trace_stamp(p, kTraceChunk + 2);
       }
+      if (tr && t == 0) trace_stamp(p, kTraceChunk + 3);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(pds_full);
+      if (tr) trace_stamp(p, 3 + 6 * t + 3);
+      fetch_ld(t + 1);
       // drain dQ (thread = query row m0 + row)
       ok = mbar_wait(mm_done, t & 1, p.status, kStatusAttnTimeout, abort_flag);
       ok = __all_sync(0xffffffffu, ok);  // keep TMEM ops warp-uniform
       if (!ok) continue;  // keep joining the named barrier until the loop ends
+      if (tr) trace_stamp(p, 3 + 6 * t + 4);
       tc_fence_after();
       const int q = m0 + row;
       float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Sq + q) * p.Hq + h) * D;
@@ -362,6 +438,7 @@ __global__ void __launch_bounds__(threads_for<SH>(), 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
+      if (tr) trace_stamp(p, 3 + 6 * t + 5);
     }
     // ---- epilogue: dK (scaled, inverse RoPE) and dV for this thread's key row; with two
     // softmax groups the first writes dK and the second dV
@@ -391,7 +468,22 @@ __global__ void __launch_bounds__(threads_for<SH>(), 1)
             x1[e] = have ? __uint_as_float(a[e]) * p.scale : 0.f;
             x2[e] = have ? __uint_as_float(bb[e]) * p.scale : 0.f;
           }
-          if (p.k_pos != nullptr) {
+          if (p.k_cs != nullptr) {
+            const float4* cs4 = reinterpret_cast<const float4*>(
+                p.k_cs + static_cast<int64_t>(krc) * (D / 2) + c * 32);
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float4 t4 = __ldg(cs4 + e / 2);   // (cos_e, sin_e, cos_e+1, sin_e+1)
+              float u = x1[e] * t4.x + x2[e] * t4.y;
+              float w = x2[e] * t4.x - x1[e] * t4.y;
+              x1[e] = u;
+              x2[e] = w;
+              u = x1[e + 1] * t4.z + x2[e + 1] * t4.w;
+              w = x2[e + 1] * t4.z - x1[e + 1] * t4.w;
+              x1[e + 1] = u;
+              x2[e + 1] = w;
+            }
+          } else if (p.k_pos != nullptr) {
 #pragma unroll
             for (int e = 0; e < 32; ++e) {
               float sn, cs;
@@ -432,6 +524,7 @@ __global__ void __launch_bounds__(threads_for<SH>(), 1)
       }
     }
   }
+  if (threadIdx.x == 64) trace_stamp(p, 2);
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
@@ -478,16 +571,19 @@ using namespace nmb::fabw;
 PullDesc make_pull(int64_t src, const c10::optional<at::Tensor>& dst, int64_t flag, int64_t epoch,
                    int* status);   // attention_tc.cu
 
-// Softmax warp groups per CTA: 1 (default) or 2 (NMB_ATTN_BWD_SOFTMAX_GROUPS=2).
+// Softmax warp groups per CTA: 2 (default; the P/dS phase is the longest of a step, and
+// two groups halve it: +2.8 % on the 1-GPU 311M step) or 1 (NMB_ATTN_BWD_SOFTMAX_GROUPS=1).
 static int softmax_groups() {
   static const int n = [] {
     const char* e = std::getenv("NMB_ATTN_BWD_SOFTMAX_GROUPS");
-    return e != nullptr && std::atoi(e) == 2 ? 2 : 1;
+    return e != nullptr && std::atoi(e) == 1 ? 1 : 2;
   }();
   return n;
 }
 
 int64_t attn_bwd_softmax_groups() { return softmax_groups(); }
+
+int64_t attn_bwd_trace_slots() { return kTraceSlots; }
 
 template <int D, int SH>
 static void launch_bwd(dim3 grid, cudaStream_t stream, const CUtensorMap& mq,
@@ -512,7 +608,8 @@ void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor d
                           int64_t k_offset, c10::optional<at::Tensor> k_pos,
                           c10::optional<at::Tensor> inv_freq, at::Tensor status,
                           int64_t pull_src, c10::optional<at::Tensor> pull_dst,
-                          int64_t pull_flag, int64_t pull_epoch) {
+                          int64_t pull_flag, int64_t pull_epoch,
+                          c10::optional<at::Tensor> k_cs, c10::optional<at::Tensor> trace) {
   const int64_t D = q.size(3);
   TORCH_CHECK(D == 64 || D == 128, "flash_attn_bwd_tc: head_dim must be 64 or 128");
   for (const at::Tensor* t : {&q, &k, &v, &dout, &dk, &dv}) {
@@ -544,6 +641,21 @@ void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor d
   p.k_pos = k_pos.has_value() ? k_pos->data_ptr<int>() : nullptr;
   p.inv_freq = inv_freq.has_value() ? inv_freq->data_ptr<float>() : nullptr;
   TORCH_CHECK(p.k_pos == nullptr || p.inv_freq != nullptr);
+  p.k_cs = nullptr;
+  p.trace = nullptr;
+  if (trace.has_value()) {
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->is_contiguous() &&
+                    trace->numel() >= static_cast<int64_t>(k.size(2)) * q.size(0) *
+                                          ((k.size(1) + kBN - 1) / kBN) * kTraceSlots,
+                "flash_attn_bwd_tc: trace must be an int64 buffer of grid x ", kTraceSlots);
+    p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
+  if (k_cs.has_value() && p.k_pos != nullptr) {
+    TORCH_CHECK(k_cs->is_cuda() && k_cs->scalar_type() == at::kFloat && k_cs->is_contiguous() &&
+                    k_cs->numel() >= k.size(1) * D,
+                "flash_attn_bwd_tc: k_cs must be a contiguous fp32 [Sk, D/2, 2] table");
+    p.k_cs = reinterpret_cast<const float2*>(k_cs->data_ptr<float>());
+  }
   p.status = status.data_ptr<int>();
   p.pull = make_pull(pull_src, pull_dst, pull_flag, pull_epoch, p.status);
   if (p.B == 0 || p.Sk == 0) return;

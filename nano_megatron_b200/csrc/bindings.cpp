@@ -24,13 +24,15 @@ void flash_attn_bwd_prep(at::Tensor o, at::Tensor dout, at::Tensor delta, at::Te
 void flash_attn_bwd_dq_convert(at::Tensor dq_acc, at::Tensor dq, c10::optional<at::Tensor> q_pos,
                                c10::optional<at::Tensor> inv_freq);
 int64_t attn_bwd_softmax_groups();
+int64_t attn_bwd_trace_slots();
 void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor dout,
                           at::Tensor lse, at::Tensor delta, at::Tensor dq_acc, at::Tensor dk,
                           at::Tensor dv, double softmax_scale, bool causal, int64_t q_offset,
                           int64_t k_offset, c10::optional<at::Tensor> k_pos,
                           c10::optional<at::Tensor> inv_freq, at::Tensor status,
                           int64_t pull_src, c10::optional<at::Tensor> pull_dst,
-                          int64_t pull_flag, int64_t pull_epoch);
+                          int64_t pull_flag, int64_t pull_epoch, c10::optional<at::Tensor> k_cs,
+                          c10::optional<at::Tensor> trace);
 void rmsnorm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps);
 void rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, at::Tensor rstd, at::Tensor dx,
                  c10::optional<at::Tensor> dw, c10::optional<at::Tensor> dres);
@@ -60,7 +62,9 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
 void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
                 std::vector<int64_t> staging_ptrs, std::vector<int64_t> staging_ptrs_odd,
                 int64_t rows_per_rank, int64_t n_out, int64_t rank, int64_t epoch_ptr,
-                at::Tensor status, c10::optional<at::Tensor> alpha_t);
+                at::Tensor status, c10::optional<at::Tensor> alpha_t,
+                c10::optional<at::Tensor> out, c10::optional<at::Tensor> residual,
+                std::vector<int64_t> tile_flag_ptrs);
 void tp_embedding_scatter(at::Tensor ids, at::Tensor w, int64_t vstart, int64_t rows_per_rank,
                           std::vector<int64_t> slots_even, std::vector<int64_t> slots_odd,
                           int64_t epoch_ptr);
@@ -125,7 +129,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("delta"), py::arg("dq_acc"), py::arg("dk"), py::arg("dv"),
         py::arg("softmax_scale"), py::arg("causal"), py::arg("q_offset"), py::arg("k_offset"),
         py::arg("k_pos"), py::arg("inv_freq"), py::arg("status"), py::arg("pull_src") = 0,
-        py::arg("pull_dst") = py::none(), py::arg("pull_flag") = 0, py::arg("pull_epoch") = 0);
+        py::arg("pull_dst") = py::none(), py::arg("pull_flag") = 0, py::arg("pull_epoch") = 0,
+        py::arg("k_cs") = py::none(), py::arg("trace") = py::none());
+  m.def("attn_bwd_trace_slots", &attn_bwd_trace_slots,
+        "timestamps per CTA written by the attention backward's optional phase trace");
   m.def("attn_bwd_softmax_groups", &attn_bwd_softmax_groups,
         "softmax warp groups of the attention backward (NMB_ATTN_BWD_SOFTMAX_GROUPS)");
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
@@ -153,7 +160,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"), py::arg("staging_ptrs"),
         py::arg("staging_ptrs_odd"), py::arg("rows_per_rank"), py::arg("n_out"),
         py::arg("rank"), py::arg("epoch_ptr"), py::arg("status"),
-        py::arg("alpha_t") = py::none());
+        py::arg("alpha_t") = py::none(), py::arg("out") = py::none(),
+        py::arg("residual") = py::none(), py::arg("tile_flag_ptrs") = std::vector<int64_t>());
   m.def("tp_embedding_scatter", &tp_embedding_scatter,
         "TP embedding: rows of this vocabulary shard stored into the sequence owners' slots");
   m.def("tp_embedding_collect", &tp_embedding_collect,

@@ -28,8 +28,13 @@
 //   kEpiPeer   : GEMM -> reduce-scatter. Output row r belongs to TP rank
 //                r / comm_rows; the bf16 partial tile is stored straight into that
 //                rank's symmetric staging buffer (slot = this rank) over NVLink, so
-//                the transfer overlaps the remaining tiles; a flag-gated reduce
-//                kernel on the owner sums the slots (comm_ops.cu).
+//                the transfer overlaps the remaining tiles. With the reduction in the
+//                kernel (rs_inplace), the other ranks' rows are computed first, each of
+//                their tiles followed by a per-tile flag in the owner's memory; this
+//                rank's own rows come last, and their epilogue waits (bounded) for the
+//                peers' tile flags and writes out = acc + the peers' partials + residual,
+//                so the own partial never leaves the SM and no second pass runs. Without
+//                it a flag-gated reduce kernel on the owner sums the slots (comm_ops.cu).
 //
 // Gathered A (template GATHER, AG -> GEMM): A's rows are split over the TP ranks,
 // rank r's [comm_rows, K] shard living in r's symmetric buffer. The producer
@@ -58,6 +63,10 @@ namespace nmb {
 enum EpiKind : int { kEpiBF16 = 0, kEpiF32Acc = 1, kEpiSwiGLU = 2, kEpiRoPE = 3, kEpiPeer = 4 };
 
 constexpr int kMaxTP = 8;
+// Per-tile flags of the in-kernel GEMM -> reduce-scatter: every rank's buffer holds
+// [TP senders][kRsTileFlags] epochs (a tile's index counts the owner's 128-row tiles x the
+// N tiles), written by the sender after the tile's partial has been stored.
+constexpr int kRsTileFlags = 16384;
 
 struct GemmParams {
   int M, N, K;               // N = output columns (for SwiGLU: F, the gate/up width)
@@ -89,7 +98,13 @@ struct GemmParams {
   __nv_bfloat16* peer_out[2][kMaxTP];   // peer epilogue: [parity][rank] staging bases
   int splits;                           // split-K factor (kEpiF32Acc with beta = 1 only)
   const float2* rope_cs;                // kEpiRoPE: (cos, sin) table [seq_len][head_dim / 2]
+  const uint32_t* rope_cs16;            // kEpiRoPE: the same table as packed bf16 (cos | sin)
   uint32_t* gather_ready;               // gather: per m-tile "rows staged in xfull" = epoch
+  // GEMM -> reduce-scatter with the reduction in the epilogue (kEpiPeer, rs_inplace = 1)
+  uint32_t* tile_flags[kMaxTP];         // per owner rank: its [TP][kRsTileFlags] flag array
+  __nv_bfloat16* own_out;               // this rank's reduced rows [comm_rows, N]
+  int64_t ld_own;
+  int rs_inplace;
 };
 
 // Per-rank tensor maps of the gathered A operand and of the local gathered copy.
@@ -104,17 +119,17 @@ struct CommMaps {
 constexpr int kBM = 128;
 constexpr int kBK = 64;                // one 128-byte swizzle row of bf16
 // Epilogue warps: two per TMEM lane quarter (each drains half of the tile's columns), so
-// two warps per SM sub-partition overlap their TMEM loads, global loads and math; the peer
-// epilogue keeps one per quarter (its shared staging area is per quarter).
+// two warps per SM sub-partition overlap their TMEM loads, global loads and math.
 template <int EPI>
-__host__ __device__ constexpr int epi_warps() { return EPI == 4 /*kEpiPeer*/ ? 4 : 8; }
+__host__ __device__ constexpr int epi_warps() { return 8; }
 template <int EPI>
 __host__ __device__ constexpr int gemm_threads() { return 64 + 32 * epi_warps<EPI>(); }
 constexpr int kUmmaK = 16;
 
-template <int BN>
+template <int BN, int EPI>
 struct GemmCfg {
-  static constexpr int kStages = BN == 256 ? 4 : 6;
+  // the peer epilogue's per-warp staging area (36 KB) takes one stage
+  static constexpr int kStages = (BN == 256 ? 4 : 6) - (EPI == kEpiPeer ? 1 : 0);
   static constexpr int kABytes = kBM * kBK * 2;
   static constexpr int kBBytes = BN * kBK * 2;
   static constexpr int kStageBytes = kABytes + kBBytes;
@@ -125,18 +140,28 @@ struct GemmCfg {
 // Peer epilogue staging: per epilogue warp 32 rows x 64 bf16 (+16 B pad per row, so the
 // row-wise writes and the segment-wise reads are both free of bank conflicts).
 constexpr int kPeerRowBytes = 64 * 2 + 16;
-constexpr int kPeerStageBytes = 4 * 32 * kPeerRowBytes;
+constexpr int kPeerStageBytes = 8 * 32 * kPeerRowBytes;
 // How long a gather tile polls for the local copy of its rows before reading the peer.
 constexpr unsigned long long kLocalCopyPollNs = 20000ull;
 
 template <int BN, int EPI>
 constexpr int gemm_smem_bytes() {
-  return GemmCfg<BN>::kSmemBytes + (EPI == kEpiPeer ? kPeerStageBytes : 0);
+  return GemmCfg<BN, EPI>::kSmemBytes + (EPI == kEpiPeer ? kPeerStageBytes : 0);
 }
 
 // silu(x) = x / (1 + e^-x) with the fast reciprocal-based division (the result is
 // rounded to bf16); for x < -87, e^-x is +inf and the quotient is -0, the limit.
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+// v[0..8) += the 8 bf16 values of a 16-byte word.
+__device__ __forceinline__ void add_bf16x8(float* v, const uint4 w) {
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+  for (int e = 0; e < 4; ++e) {
+    v[2 * e] += bf16_lo(u[e]);
+    v[2 * e + 1] += bf16_hi(u[e]);
+  }
+}
 
 // Store 32 fp32 values as bf16 to row pointer `dst` (cols [col, col+32)), predicated on N.
 __device__ __forceinline__ void store_row32_bf16(__nv_bfloat16* dst, int col, int ncols,
@@ -194,6 +219,30 @@ __device__ __forceinline__ void tile_coords(int t, const GemmParams& p, int& m0,
   nt = t / p.num_m_tiles;
 }
 
+// Work item t -> tile, per epilogue kind. The in-kernel GEMM -> reduce-scatter orders the
+// other ranks' rows first (their partials travel while this rank computes the rest) and
+// this rank's own rows last (their epilogue waits for the peers' partials).
+template <int EPI, bool GATHER>
+__device__ __forceinline__ void work_coords(int t, const GemmParams& p, int& m0, int& nt,
+                                            int& ks) {
+  if constexpr (EPI == kEpiPeer) {
+    if (p.rs_inplace) {
+      const int own = p.comm_rows / kBM, rem = p.num_m_tiles - own, own0 = p.comm_rank * own;
+      ks = 0;
+      if (t < rem * p.num_n_tiles) {
+        m0 = ((own0 + own + t % rem) % p.num_m_tiles) * kBM;
+        nt = t / rem;
+        return;
+      }
+      t -= rem * p.num_n_tiles;
+      m0 = (own0 + t % own) * kBM;
+      nt = t / own;
+      return;
+    }
+  }
+  tile_coords<GATHER>(t, p, m0, nt, ks);
+}
+
 // Brief, bounded poll of a gather m-tile's local-copy flag; false = not there (yet).
 __device__ __forceinline__ bool poll_local_copy(const uint32_t* flag, uint32_t epoch) {
   if (ld_acquire_gpu(flag) == epoch) return true;
@@ -225,7 +274,7 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
     gemm_tcgen05_kernel(const __grid_constant__ CUtensorMap tmA,
                         const __grid_constant__ CUtensorMap tmB,
                         const __grid_constant__ CommMaps cm, const GemmParams p) {
-  using Cfg = GemmCfg<BN>;
+  using Cfg = GemmCfg<BN, EPI>;
   constexpr int S = Cfg::kStages;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -279,7 +328,7 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
       const int par = static_cast<int>(epoch & 1u);
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int m0, nt, ks, kb0, kb1;
-        tile_coords<GATHER>(t, p, m0, nt, ks);
+        work_coords<EPI, GATHER>(t, p, m0, nt, ks);
         split_range(p, num_kb, ks, kb0, kb1);
         int owner = 0;
         bool from_local = false;
@@ -359,7 +408,7 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + acc * BN;
         int m0 = 0, nt = 0, ks = 0, kb0 = 0, kb1 = 0;
-        tile_coords<GATHER>(t, p, m0, nt, ks);
+        work_coords<EPI, GATHER>(t, p, m0, nt, ks);
         split_range(p, num_kb, ks, kb0, kb1);
         const bool store_a = GATHER && p.store_gathered && nt == 0;
         for (int kb = kb0; kb < kb1; ++kb) {
@@ -414,9 +463,11 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
     const float alpha = p.alpha_ptr != nullptr ? p.alpha * __ldg(p.alpha_ptr) : p.alpha;
     // peer epilogue: this call's epoch is the next one (the signal kernel advances it later)
     int out_par = 0;
-    if constexpr (EPI == kEpiPeer)
-      out_par = static_cast<int>((*reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) + 1u) &
-                                 1u);
+    uint32_t out_epoch = 0;
+    if constexpr (EPI == kEpiPeer) {
+      out_epoch = *reinterpret_cast<const volatile uint32_t*>(p.epoch_ptr) + 1u;
+      out_par = static_cast<int>(out_epoch & 1u);
+    }
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -426,7 +477,7 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
         break;
       tc_fence_after();
       int m0, nt, ks;
-      tile_coords<GATHER>(t, p, m0, nt, ks);
+      work_coords<EPI, GATHER>(t, p, m0, nt, ks);
       const int row = m0 + quarter * 32 + lane;
       const bool row_ok = row < p.M;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN;
@@ -434,13 +485,78 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
       if constexpr (EPI == kEpiPeer) {
         // every row of a 128-row tile has the same owner (rows per rank % 128 == 0)
         const int owner = m0 / p.comm_rows;
+        const int n0 = nt * BN;
+        const int tile_local = ((m0 - owner * p.comm_rows) / kBM) * p.num_n_tiles + nt;
+        if (p.rs_inplace && owner == p.comm_rank) {
+          // own rows: every peer's partial of this tile must have landed (bounded wait on
+          // the per-tile flags it wrote after its stores), then out = acc + partials (+ res)
+          bool landed = true;
+          for (int src = 0; src < p.comm_size && landed; ++src)
+            if (src != p.comm_rank)
+              landed = wait_flag(p.tile_flags[p.comm_rank] + src * kRsTileFlags + tile_local,
+                                 out_epoch, p.status, kStatusPeerFlagTimeout, abort_flag);
+          if (landed) {
+            const int lrow = row - p.comm_rank * p.comm_rows;
+            const __nv_bfloat16* stg = p.peer_out[out_par][p.comm_rank];  // [TP][rows][ldc]
+            constexpr int kChunks = BN / 32 / kParts;
+#pragma unroll 1
+            for (int c = ew * kChunks; c < (ew + 1) * kChunks; ++c) {
+              const int col = n0 + c * 32;
+              uint32_t r[32];
+              tmem_ld_32x32b_x32(tbase + c * 32, r);
+              float v[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) v[j] = 0.f;
+              const bool vec = col + 32 <= p.N;
+              // the residual and the peers' partials load while the TMEM load is in flight
+              if (vec) {
+                if (p.R != nullptr) {
+                  const uint4* rr = reinterpret_cast<const uint4*>(
+                      p.R + static_cast<int64_t>(lrow) * p.ldr + col);
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) add_bf16x8(v + 8 * q, __ldg(rr + q));
+                }
+                for (int src = 0; src < p.comm_size; ++src) {
+                  if (src == p.comm_rank) continue;
+                  const uint4* sp = reinterpret_cast<const uint4*>(
+                      stg + (static_cast<int64_t>(src) * p.comm_rows + lrow) * p.ldc + col);
+#pragma unroll
+                  for (int q = 0; q < 4; ++q) add_bf16x8(v + 8 * q, __ldcg(sp + q));
+                }
+              }
+              tmem_wait_ld();
+              if (col >= p.N) continue;
+              __nv_bfloat16* orow = p.own_out + static_cast<int64_t>(lrow) * p.ld_own;
+              if (vec) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) v[j] += __uint_as_float(r[j]) * alpha;
+                store_row32_bf16(orow + col, col, p.N, v);
+              } else {
+                for (int j = 0; j < 32 && col + j < p.N; ++j) {
+                  float x = __uint_as_float(r[j]) * alpha;
+                  if (p.R != nullptr)
+                    x += __bfloat162float(p.R[static_cast<int64_t>(lrow) * p.ldr + col + j]);
+                  for (int src = 0; src < p.comm_size; ++src)
+                    if (src != p.comm_rank)
+                      x += __bfloat162float(
+                          stg[(static_cast<int64_t>(src) * p.comm_rows + lrow) * p.ldc + col + j]);
+                  orow[col + j] = __float2bfloat16_rn(x);
+                }
+              }
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+          continue;
+        }
         __nv_bfloat16* base = p.peer_out[out_par][owner] +
                               static_cast<int64_t>(p.comm_rank * p.comm_rows - owner * p.comm_rows) *
                                   p.ldc;
-        uint8_t* wst = peer_stage + quarter * 32 * kPeerRowBytes;
-        const int n0 = nt * BN;
+        uint8_t* wst = peer_stage + (warp - 2) * 32 * kPeerRowBytes;
+        constexpr int kC2 = BN / 64 / kParts;   // 64-column blocks of this warp
 #pragma unroll 1
-        for (int c2 = 0; c2 < BN / 64; ++c2) {
+        for (int c2 = ew * kC2; c2 < (ew + 1) * kC2; ++c2) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
             uint32_t r[32];
@@ -474,6 +590,13 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
             }
           }
           __syncwarp();
+        }
+        if (p.rs_inplace) {
+          // the owner may read this tile once every epilogue warp's stores are visible
+          asm volatile("bar.sync 2, %0;" ::"n"(32 * epi_warps<EPI>()) : "memory");
+          if (threadIdx.x == 64)   // release at system scope: cumulative over the barrier
+            st_release_sys(p.tile_flags[owner] + p.comm_rank * kRsTileFlags + tile_local,
+                           out_epoch);
         }
       } else if constexpr (EPI == kEpiBF16 || EPI == kEpiF32Acc) {
         const int n0 = nt * BN;
@@ -597,6 +720,10 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
         const int pos = row_ok ? __ldg(p.positions + slot) : 0;
         // (head, half-chunk) pairs of the tile, dealt round-robin to the kParts warps
         const int pairs = (BN / D) * half_chunks;
+        // bf16 (cos, sin) of this row's position for the current half-chunk, loaded once
+        // and reused by every head of the tile that rotates with the same frequencies
+        uint32_t cs16[32];
+        int cs16_j = -1;
 #pragma unroll 1
         for (int i = ew; i < pairs; i += kParts) {
           {
@@ -617,7 +744,28 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
               b[e] = __uint_as_float(hi[e]) * alpha;
             }
             if (col_lo < p.rope_cols) {
-              if (p.rope_cs != nullptr) {  // precomputed (cos, sin) of this row's slot
+              if (p.rope_cs16 != nullptr) {
+                if (j != cs16_j) {
+                  const uint4* t4 = reinterpret_cast<const uint4*>(
+                      p.rope_cs16 + static_cast<int64_t>(slot) * (D / 2) + j * 32);
+#pragma unroll
+                  for (int q = 0; q < 8; ++q) {
+                    const uint4 w = __ldg(t4 + q);
+                    cs16[4 * q] = w.x;
+                    cs16[4 * q + 1] = w.y;
+                    cs16[4 * q + 2] = w.z;
+                    cs16[4 * q + 3] = w.w;
+                  }
+                  cs16_j = j;
+                }
+#pragma unroll
+                for (int e = 0; e < 32; ++e) {
+                  const float cs = bf16_lo(cs16[e]), sn = bf16_hi(cs16[e]);
+                  const float x1 = a[e], x2 = b[e];
+                  a[e] = x1 * cs - x2 * sn;
+                  b[e] = x2 * cs + x1 * sn;
+                }
+              } else if (p.rope_cs != nullptr) {  // precomputed (cos, sin) of this row's slot
                 const float4* cs4 = reinterpret_cast<const float4*>(
                     p.rope_cs + static_cast<int64_t>(slot) * (D / 2) + j * 32);
 #pragma unroll
@@ -842,10 +990,14 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
     p.rope_cols = static_cast<int>(rope_cols);
     TORCH_CHECK(rope_cols % head_dim == 0 && N % head_dim == 0);
     if (rope_cs.has_value()) {
-      TORCH_CHECK(rope_cs->scalar_type() == at::kFloat && rope_cs->is_contiguous() &&
+      TORCH_CHECK((rope_cs->scalar_type() == at::kFloat ||
+                   rope_cs->scalar_type() == at::kBFloat16) && rope_cs->is_contiguous() &&
                       rope_cs->numel() == positions->numel() * head_dim,
-                  "rope table must be fp32 [seq_len, head_dim/2, 2]");
-      p.rope_cs = reinterpret_cast<const float2*>(rope_cs->data_ptr<float>());
+                  "rope table must be fp32 or bf16 [seq_len, head_dim/2, 2]");
+      if (rope_cs->scalar_type() == at::kBFloat16)
+        p.rope_cs16 = reinterpret_cast<const uint32_t*>(rope_cs->data_ptr());
+      else
+        p.rope_cs = reinterpret_cast<const float2*>(rope_cs->data_ptr<float>());
     }
   }
   if (epi == kEpiF32Acc && beta == 1.0) {
@@ -953,9 +1105,13 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
     p.head_dim = static_cast<int>(head_dim);
     p.rope_cols = static_cast<int>(rope_cols);
     if (rope_cs.has_value()) {
-      TORCH_CHECK(rope_cs->scalar_type() == at::kFloat && rope_cs->is_contiguous() &&
+      TORCH_CHECK((rope_cs->scalar_type() == at::kFloat ||
+                   rope_cs->scalar_type() == at::kBFloat16) && rope_cs->is_contiguous() &&
                   rope_cs->numel() == positions->numel() * head_dim);
-      p.rope_cs = reinterpret_cast<const float2*>(rope_cs->data_ptr<float>());
+      if (rope_cs->scalar_type() == at::kBFloat16)
+        p.rope_cs16 = reinterpret_cast<const uint32_t*>(rope_cs->data_ptr());
+      else
+        p.rope_cs = reinterpret_cast<const float2*>(rope_cs->data_ptr<float>());
     }
   } else {
     TORCH_CHECK(epi == kEpiBF16, "gemm_tc_ag: epilogue must be bf16, RoPE or SwiGLU");
@@ -1006,7 +1162,9 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
 void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
                 std::vector<int64_t> staging_ptrs, std::vector<int64_t> staging_ptrs_odd,
                 int64_t rows_per_rank, int64_t n_out, int64_t rank, int64_t epoch_ptr,
-                at::Tensor status, c10::optional<at::Tensor> alpha_t) {
+                at::Tensor status, c10::optional<at::Tensor> alpha_t,
+                c10::optional<at::Tensor> out, c10::optional<at::Tensor> residual,
+                std::vector<int64_t> tile_flag_ptrs) {
   check_operand(a, "A");
   check_operand(b, "B");
   const int tp = static_cast<int>(staging_ptrs.size());
@@ -1045,6 +1203,34 @@ void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
   const int bn = choose_bn(p.M, p.N, kEpiPeer);
   p.num_m_tiles = static_cast<int>((M + kBM - 1) / kBM);
   p.num_n_tiles = static_cast<int>((n_out + bn - 1) / bn);
+  if (out.has_value()) {
+    // reduction in the epilogue: this rank's rows land in `out` (+ residual)
+    TORCH_CHECK(static_cast<int>(tile_flag_ptrs.size()) == tp,
+                "gemm_tc_rs: one tile-flag array per rank");
+    TORCH_CHECK(out->is_cuda() && out->scalar_type() == at::kBFloat16 && out->dim() == 2 &&
+                    out->size(0) == rows_per_rank && out->size(1) == n_out &&
+                    out->stride(1) == 1 && out->stride(0) % 8 == 0 &&
+                    reinterpret_cast<uintptr_t>(out->data_ptr()) % 16 == 0,
+                "gemm_tc_rs: out must be a [rows_per_rank, N] bf16 matrix, 16-byte rows");
+    TORCH_CHECK((rows_per_rank / kBM) * p.num_n_tiles <= kRsTileFlags,
+                "gemm_tc_rs: more tiles than the flag array holds");
+    p.rs_inplace = 1;
+    p.own_out = reinterpret_cast<__nv_bfloat16*>(out->data_ptr());
+    p.ld_own = out->stride(0);
+    for (int r = 0; r < tp; ++r) {
+      TORCH_CHECK(tile_flag_ptrs[r] % 16 == 0 && tile_flag_ptrs[r] != 0);
+      p.tile_flags[r] = reinterpret_cast<uint32_t*>(tile_flag_ptrs[r]);
+    }
+    if (residual.has_value()) {
+      TORCH_CHECK(residual->scalar_type() == at::kBFloat16 && residual->dim() == 2 &&
+                      residual->size(0) == rows_per_rank && residual->size(1) == n_out &&
+                      residual->stride(1) == 1 && residual->stride(0) % 8 == 0 &&
+                      reinterpret_cast<uintptr_t>(residual->data_ptr()) % 16 == 0,
+                  "gemm_tc_rs: residual must match out");
+      p.R = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+      p.ldr = residual->stride(0);
+    }
+  }
   if (M == 0 || n_out == 0) return;
   const at::cuda::CUDAGuard guard(a.device());
   ensure_current_context(a.device().index());

@@ -5,6 +5,7 @@ opens every peer's handle, so all ranks can load and store every rank's buffer
 over NVLink (P2P through NVSwitch). Buffer layout (identical on all ranks):
 
     [ flags: 16 channels x 8 source slots x uint32 | pad to 4 KiB ]
+    [ reduce-scatter tile flags: 8 source slots x 16384 tiles x uint32 ]
     [ reduce-scatter staging: 2 parities x TP x rows x cols bf16 ]
     [ all-gather shards:       2 parities x rows x cols bf16      ]
     [ embedding rows:          2 parities x rows x hidden bf16    ]  (optional)
@@ -30,6 +31,8 @@ import torch.distributed as dist
 
 FLAG_BYTES = 4096
 MAX_TP = 8
+RS_TILE_FLAGS = 16384              # per source rank; must equal kRsTileFlags (gemm_tcgen05.cu)
+TILE_FLAG_BYTES = MAX_TP * RS_TILE_FLAGS * 4
 CH_RS, CH_AG, CH_AG_BWD, CH_EMB, CH_CE = 0, 1, 2, 3, 4
 GATHER_READY_TILES = 4096          # 128-row tiles of a gathered operand (512K rows)
 
@@ -45,6 +48,10 @@ class SymmetricWorkspace:
         self.rs_bytes, self.ag_bytes = rs_bytes, ag_bytes
         self.emb_bytes, self.ce_bytes = emb_bytes, ce_bytes
         self._opened = opened         # peer mappings to close
+        # one process emulating every rank: kernels of the emulated ranks run one after
+        # another, so no kernel may wait inside for another rank's kernel (the
+        # reduce-scatter then reduces in a second pass instead of in its epilogue)
+        self.emulated = False
         self.epochs = torch.zeros(16, dtype=torch.int32, device=device)  # device counters
         # per channel and 128-row tile: epoch at which the gathered rows sit in the local
         # copy (written and read by the AG->GEMM kernel on this GPU only)
@@ -57,7 +64,7 @@ class SymmetricWorkspace:
     # ------------------------------------------------------------------ construction
     @staticmethod
     def total_bytes(rs_bytes: int, ag_bytes: int, emb_bytes: int = 0, ce_bytes: int = 0) -> int:
-        return FLAG_BYTES + 2 * (rs_bytes + ag_bytes + emb_bytes + ce_bytes)
+        return FLAG_BYTES + TILE_FLAG_BYTES + 2 * (rs_bytes + ag_bytes + emb_bytes + ce_bytes)
 
     @classmethod
     def create(cls, group, *, rs_bytes: int, ag_bytes: int, device: torch.device,
@@ -97,9 +104,12 @@ class SymmetricWorkspace:
         bufs = [torch.zeros(cls.total_bytes(rs_bytes, ag_bytes, emb_bytes, ce_bytes),
                             dtype=torch.uint8, device=dev) for _ in range(size)]
         ptrs = [b.data_ptr() for b in bufs]
-        return [cls(rank=r, size=size, ptrs=ptrs, owner=bufs[r], device=dev, rs_bytes=rs_bytes,
-                    ag_bytes=ag_bytes, opened=[], emb_bytes=emb_bytes, ce_bytes=ce_bytes)
-                for r in range(size)]
+        out = [cls(rank=r, size=size, ptrs=ptrs, owner=bufs[r], device=dev, rs_bytes=rs_bytes,
+                   ag_bytes=ag_bytes, opened=[], emb_bytes=emb_bytes, ce_bytes=ce_bytes)
+               for r in range(size)]
+        for ws in out:
+            ws.emulated = True
+        return out
 
     def close(self) -> None:
         """Unmap every peer buffer (``cudaIpcCloseMemHandle``). Call only after every peer
@@ -130,19 +140,27 @@ class SymmetricWorkspace:
     def signal_targets(self, channel: int) -> list[int]:
         return [self.flags(d, channel) + self.rank * 4 for d in range(self.size)]
 
+    def rs_tile_flags(self, rank: int) -> int:
+        """Base of ``rank``'s [source rank][tile] flag array of the in-kernel GEMM ->
+        reduce-scatter."""
+        return self.ptrs[rank] + FLAG_BYTES
+
+    def _data(self, rank: int) -> int:
+        return self.ptrs[rank] + FLAG_BYTES + TILE_FLAG_BYTES
+
     def rs_staging(self, rank: int, parity: int) -> int:
-        return self.ptrs[rank] + FLAG_BYTES + (parity & 1) * self.rs_bytes
+        return self._data(rank) + (parity & 1) * self.rs_bytes
 
     def ag_shard(self, rank: int, parity: int) -> int:
-        return self.ptrs[rank] + FLAG_BYTES + 2 * self.rs_bytes + (parity & 1) * self.ag_bytes
+        return self._data(rank) + 2 * self.rs_bytes + (parity & 1) * self.ag_bytes
 
     def emb_slot(self, rank: int, parity: int) -> int:
-        return self.ptrs[rank] + FLAG_BYTES + 2 * (self.rs_bytes + self.ag_bytes) + \
+        return self._data(rank) + 2 * (self.rs_bytes + self.ag_bytes) + \
             (parity & 1) * self.emb_bytes
 
     def ce_slot(self, rank: int, parity: int) -> int:
-        return self.ptrs[rank] + FLAG_BYTES + 2 * (self.rs_bytes + self.ag_bytes +
-                                                   self.emb_bytes) + (parity & 1) * self.ce_bytes
+        return self._data(rank) + 2 * (self.rs_bytes + self.ag_bytes + self.emb_bytes) + \
+            (parity & 1) * self.ce_bytes
 
     def check_emb(self, rows: int, hidden: int) -> None:
         if rows * hidden * 2 > self.emb_bytes:

@@ -15,8 +15,9 @@ collective + the same local kernels) is timed beside it.
 Cases (shapes of the 311M model under TP2 with a 64-sequence micro-batch, and of its
 8-GPU data-parallel replica group):
 * ``tp_rs``  GEMM -> reduce-scatter (out_proj forward, sequence parallel): peer-store
-  epilogue + flag-gated reduce (``ops.comm_gemm.gemm_reduce_scatter``) vs GEMM +
-  ``reduce_scatter_tensor``.
+  epilogue + flag-gated reduce kernel on the owner (``ops.comm_gemm.gemm_reduce_scatter``),
+  and the opt-in variant that reduces this rank's rows in the GEMM's own epilogue, vs
+  GEMM + ``reduce_scatter_tensor``.
 * ``tp_ag``  all-gather -> GEMM (QKV forward): gathered-A GEMM reading peer shards
   (``ops.comm_gemm.allgather_gemm``) vs ``all_gather_into_tensor`` + GEMM.
 * ``replica`` DDP / ZeRO-1/2 step: replica reduce of this rank's fp32 gradient shard
@@ -117,7 +118,17 @@ def case_tp(grp, dev, iters: int, rows_total: int = 32768, hidden: int = 1024) -
         flops = 2.0 * rows_total * hidden * k_out
         link = (n - 1) / n * rows_total * hidden * 2.0
         out.append(_line("tp_rs_out_proj", fused, base, flops, link,
-                         shape=f"{rows_total}x{hidden}x{k_out}", tp=n))
+                         shape=f"{rows_total}x{hidden}x{k_out}", tp=n,
+                         reduction="second kernel on the owner"))
+        saved, CG.RS_IN_KERNEL = CG.RS_IN_KERNEL, True   # the opt-in variant
+        try:
+            t2 = _timed(lambda: CG.gemm_reduce_scatter(ws, a, w, residual=res, out=y), iters,
+                        dev)
+        finally:
+            CG.RS_IN_KERNEL = saved
+        out.append(_line("tp_rs_out_proj_in_kernel", t2, base, flops, link,
+                         shape=f"{rows_total}x{hidden}x{k_out}", tp=n,
+                         reduction="in the GEMM epilogue (NMB_RS_IN_KERNEL=1)"))
         # --- all-gather -> GEMM (QKV): x_local [rows, hidden] x w [n_qkv, hidden]
         x = torch.randn(rows, hidden, device=dev, generator=g).bfloat16()
         wq = (torch.randn(n_qkv, hidden, device=dev, generator=g) * 0.05).bfloat16()

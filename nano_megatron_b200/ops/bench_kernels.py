@@ -6,7 +6,8 @@ Prints one JSON object of achieved TFLOP/s (GEMM, attention) or GB/s and the fra
 the measured copy bandwidth (memory-bound kernels: RMSNorm, SwiGLU backward, attention
 backward prep / dQ conversion, embedding, AdamW). ``--case gemm_tiles`` sweeps the GEMM
 tile width (``block_n`` 128 and 256) on the 311M model's shapes, the data behind the tile
-choice in ``choose_bn`` (csrc/gemm_tcgen05.cu); ``--case gemm_layer`` times the layer's
+choice in ``choose_bn`` (csrc/gemm_tcgen05.cu); ``--case attn_trace[:d128]`` prints the attention backward's in-kernel phase
+times; ``--case gemm_layer`` times the layer's
 GEMMs with their fused epilogues (RoPE, SwiGLU, residual) against the plain product. Also the small, self-contained workload used for ncu captures
 (``--case gemm_profile`` / ``gemm_epi_profile:<swiglu|rope|residual>`` / ``attn_profile[:d128]``
 run a few launches of one kernel).
@@ -112,8 +113,9 @@ def gemm_layer_cases(iters: int, m: int = 8192) -> dict:
     w_qkv = torch.randn(3 * hid, hid, device="cuda").bfloat16()
     qkv = torch.empty(m, 3 * hid, device="cuda", dtype=torch.bfloat16)
     fl = 2 * m * 3 * hid * hid
+    # rows are sequence-major (row = s * batch + b), as the model lays out a micro-batch
     res["qkv_rope"] = fl / _time(lambda: G.qkv_rope_fwd(x, w_qkv, pos, inv_freq, hd, 2 * hid,
-                                                         out=qkv), iters) / 1e9
+                                                         pos_div=m // seq, out=qkv), iters) / 1e9
     res["qkv_plain"] = fl / _time(lambda: G.gemm(x, w_qkv, qkv), iters) / 1e9
     res["qkv_cublas"] = fl / _time(lambda: torch.matmul(x, w_qkv.t(), out=qkv), iters) / 1e9
     w_gu = torch.randn(2 * ffn, hid, device="cuda").bfloat16()
@@ -150,7 +152,8 @@ def gemm_epilogue_profile(epi: str) -> None:
         inv = 1.0 / (10000.0 ** (torch.arange(0, 64, 2, device="cuda").float() / 64))
         w = torch.randn(3 * hid, hid, device="cuda").bfloat16()
         y = torch.empty(m, 3 * hid, device="cuda", dtype=torch.bfloat16)
-        fn = lambda: G.qkv_rope_fwd(x, w, pos, inv, 64, 2 * hid, out=y)  # noqa: E731
+        fn = lambda: G.qkv_rope_fwd(x, w, pos, inv, 64, 2 * hid, pos_div=m // 512,  # noqa: E731
+                                    out=y)
     else:  # residual: the output projection
         w = torch.randn(hid, hid, device="cuda").bfloat16()
         r = torch.randn(m, hid, device="cuda").bfloat16()
@@ -190,6 +193,81 @@ def attn_cases(iters: int) -> dict:
             lambda: torch.nn.functional.scaled_dot_product_attention(
                 qt, kt, vt, is_causal=True, enable_gqa=True), iters) / 1e9
     return res
+
+
+def attn_bwd_trace(b: int = 16, s: int = 512, h: int = 16, hkv: int = 16, d: int = 64) -> dict:
+    """Phase timing of the tcgen05 attention backward from its in-kernel %globaltimer trace
+    (one launch, after warm-up): mean microseconds per CTA phase and per step phase."""
+    from ._ext import status_word
+
+    L = lib()
+    qkv = torch.randn(b, s, h + 2 * hkv, d, device="cuda").bfloat16()
+    q, k, v = qkv[:, :, :h], qkv[:, :, h:h + hkv], qkv[:, :, h + hkv:]
+    o = torch.empty(b, s, h, d, device="cuda", dtype=torch.bfloat16)
+    lse = torch.empty(b, h, s, device="cuda")
+    F.flash_fwd(q, k, v, o, lse, d ** -0.5, True)
+    dqkv = torch.empty_like(qkv)
+    delta = torch.empty(b * h * s, device="cuda")
+    acc = torch.empty(b * s * h * d, device="cuda")
+    slots = int(L.attn_bwd_trace_slots())
+    ctas = hkv * b * ((s + 127) // 128)
+    trace = torch.zeros(ctas * slots, dtype=torch.int64, device="cuda")
+
+    def run(tr):
+        L.flash_attn_bwd_prep(o, o, delta, acc)
+        L.flash_attn_bwd_tc_kv(q, k, v, o, lse, delta, acc, dqkv[:, :, h:h + hkv],
+                               dqkv[:, :, h + hkv:], d ** -0.5, True, 0, 0, None, None,
+                               status_word(q.device), trace=tr)
+    for _ in range(3):
+        run(None)
+    run(trace)
+    torch.cuda.synchronize()
+    t = trace.view(ctas, slots).cpu().double() / 1000.0   # microseconds
+    steps = (slots - 3) // 8
+    t0 = t[:, 0].min()
+    res = {"ctas": ctas, "span_us": float(t[:, 2].max() - t0),
+           "cta_us_mean": float((t[:, 2] - t[:, 0]).mean()),
+           "setup_us_mean": float((t[:, 1] - t[:, 0]).mean())}
+    names = ["sdp_wait", "pds_free_wait", "softmax", "mm_done_wait", "dq_drain"]
+    for j, n in enumerate(names):
+        col_a, col_b = 3 + j, 4 + j
+        vals = []
+        for st in range(steps):
+            a, bb = t[:, col_a + 6 * st], t[:, col_b + 6 * st]
+            ok = (a > 0) & (bb > 0)
+            vals.append((bb - a)[ok])
+        cat = torch.cat(vals)
+        res[f"{n}_us_mean"] = float(cat.mean()) if cat.numel() else None
+    gaps = []
+    for st in range(steps - 1):
+        a, bb = t[:, 3 + 6 * st + 5], t[:, 3 + 6 * (st + 1)]
+        ok = (a > 0) & (bb > 0)
+        gaps.append((bb - a)[ok])
+    cat = torch.cat(gaps)
+    res["next_step_gap_us_mean"] = float(cat.mean()) if cat.numel() else None
+    last = []
+    for i in range(ctas):
+        fs = [t[i, 3 + 6 * st + 5] for st in range(steps) if t[i, 3 + 6 * st + 5] > 0]
+        if fs:
+            last.append(float(t[i, 2] - fs[-1]))
+    res["epilogue_us_mean"] = sum(last) / max(1, len(last))
+    mq = 3 + 6 * steps
+    lag = [(t[:, mq + 2 * st] - t[:, 3 + 6 * st])[(t[:, mq + 2 * st] > 0) & (t[:, 3 + 6 * st] > 0)]
+           for st in range(steps)]
+    cat = torch.cat(lag)
+    res["qdo_landed_minus_step_start_us_mean"] = float(cat.mean()) if cat.numel() else None
+    first = t[:, 3]
+    res["first_step_start_after_entry_us_mean"] = float((first - t[:, 0])[first > 0].mean())
+    ck = 3 + 8 * steps                       # step 0, first chunk: loads, math, stores
+    pds0 = t[:, 3 + 2]                       # step 0: P/dS tiles free (chunk loop start)
+    for j, n in enumerate(["chunk0_tmem_ld", "chunk0_math", "chunk0_store"]):
+        a = pds0 if j == 0 else t[:, ck + j - 1]
+        bq = t[:, ck + j]
+        ok = (a > 0) & (bq > 0)
+        res[f"{n}_us_mean"] = float((bq - a)[ok].mean()) if ok.any() else None
+    ok = (t[:, ck + 3] > 0) & (pds0 > 0)
+    res["step0_all_chunks_us_mean"] = float((t[:, ck + 3] - pds0)[ok].mean()) if ok.any() else None
+    return {k: (round(v, 3) if isinstance(v, float) else v) for k, v in res.items()}
 
 
 def _hbm_peak_gbs() -> float | None:
@@ -273,6 +351,10 @@ def main() -> None:
         for _ in range(3):
             G.gemm(x, w, c)
         torch.cuda.synchronize()
+        return
+    if a.case.startswith("attn_trace"):   # attn_trace[:d128]
+        cfg = (1, 8192, 8, 2, 128) if a.case.endswith("d128") else (16, 512, 16, 16, 64)
+        print(json.dumps(attn_bwd_trace(*cfg), indent=1))
         return
     if a.case.startswith("gemm_epi_profile"):  # gemm_epi_profile:swiglu|rope|residual
         gemm_epilogue_profile(a.case.split(":", 1)[1] if ":" in a.case else "swiglu")

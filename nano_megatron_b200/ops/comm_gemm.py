@@ -18,6 +18,8 @@ emulated ranks phase by phase; the public functions run both.
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 from nano_megatron_b200.distributed.symmetric import CH_AG, CH_CE, CH_EMB, CH_RS
@@ -26,23 +28,37 @@ from ._ext import lib
 
 EPI = {"bf16": 0, "rope": 3, "swiglu": 2}
 
+# GEMM -> reduce-scatter with this rank's rows reduced in the GEMM's own epilogue (per-tile
+# flags) instead of a second kernel. Off by default: on 2 x B200 at the 311M out_proj shape
+# (32768 x 1024 x 512, TP2) it measured 122 us against 110 us for the two-pass path
+# (``python -m nano_megatron_b200.ops.bench_comm --case tp``); the per-tile release of the
+# peer tiles serialises the epilogue. NMB_RS_IN_KERNEL=1 selects it.
+RS_IN_KERNEL = os.environ.get("NMB_RS_IN_KERNEL", "0") == "1"
+
 
 def rs_issue(ws, a: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,
-             n_out: int | None = None, alpha_t: torch.Tensor | None = None
-             ) -> tuple[int, int]:
-    """GEMM with the peer epilogue + signal. Returns (rows_per_rank, n_out). ``alpha_t``:
-    optional fp32 device scalar multiplying the product."""
+             n_out: int | None = None, alpha_t: torch.Tensor | None = None,
+             out: torch.Tensor | None = None, residual: torch.Tensor | None = None
+             ) -> tuple[int, int, bool]:
+    """GEMM with the peer epilogue + signal. Returns (rows_per_rank, n_out, reduced).
+    ``alpha_t``: optional fp32 device scalar multiplying the product. With ``out`` (and a
+    real multi-GPU workspace) the kernel also reduces this rank's rows into ``out``
+    (+ ``residual``) in its epilogue and ``reduced`` is True; otherwise ``rs_finish``
+    does the reduction in a second kernel."""
     M = a.shape[0]
     if M % ws.size:
         raise ValueError(f"rows {M} not divisible by TP size {ws.size}")
     rows = M // ws.size
     n = n_out if n_out is not None else (b.shape[1] if b_mn else b.shape[0])
     ws.check_rs(rows, n)
+    inplace = out is not None and RS_IN_KERNEL and not getattr(ws, "emulated", False)
     lib().gemm_tc_rs(a, False, b, b_mn, [ws.rs_staging(r, 0) for r in range(ws.size)],
                      [ws.rs_staging(r, 1) for r in range(ws.size)], rows, n, ws.rank,
-                     ws.epoch_ptr(CH_RS), ws.status, alpha_t)
+                     ws.epoch_ptr(CH_RS), ws.status, alpha_t,
+                     out if inplace else None, residual if inplace else None,
+                     [ws.rs_tile_flags(r) for r in range(ws.size)] if inplace else [])
     lib().peer_signal(ws.signal_targets(CH_RS), ws.epoch_ptr(CH_RS))
-    return rows, n
+    return rows, n, inplace
 
 
 def rs_finish(ws, out: torch.Tensor, residual: torch.Tensor | None = None) -> None:
@@ -54,10 +70,15 @@ def gemm_reduce_scatter(ws, a: torch.Tensor, b: torch.Tensor, *, b_mn: bool = Fa
                         residual: torch.Tensor | None = None,
                         out: torch.Tensor | None = None,
                         alpha_t: torch.Tensor | None = None) -> torch.Tensor:
-    rows, n = rs_issue(ws, a, b, b_mn=b_mn, alpha_t=alpha_t)
+    M = a.shape[0]
+    n = b.shape[1] if b_mn else b.shape[0]
     if out is None:
-        out = torch.empty(rows, n, device=a.device, dtype=torch.bfloat16)
-    rs_finish(ws, out, residual)
+        out = torch.empty(M // ws.size, n, device=a.device, dtype=torch.bfloat16)
+    if residual is not None and (residual.stride(-1) != 1 or residual.stride(0) % 8):
+        residual = residual.contiguous()
+    _, _, reduced = rs_issue(ws, a, b, b_mn=b_mn, alpha_t=alpha_t, out=out, residual=residual)
+    if not reduced:
+        rs_finish(ws, out, residual)
     return out
 
 
@@ -81,7 +102,7 @@ def ag_finish(ws, x_local: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
     if epi == "rope":
         from .gemm import rope_table
 
-        table = rope_table(positions, inv_freq)
+        table = rope_table(positions, inv_freq, torch.bfloat16)
     ready = ws.gather_ready[channel] if out.shape[0] // 128 <= ws.gather_ready.shape[1] \
         else None
     lib().gemm_tc_ag(x_local, [ws.ag_shard(r, 0) for r in range(ws.size)],

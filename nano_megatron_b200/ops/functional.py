@@ -334,9 +334,14 @@ def attention_bwd(q, k, v, o, do, lse, dq, dk, dv, *, causal: bool, q_offset: in
 
         L = lib()
         L.flash_attn_bwd_prep(o, do, delta, dq_acc)
+        k_cs = None
+        if k_pos is not None and inv_freq is not None:
+            from .gemm import rope_table
+
+            k_cs = rope_table(k_pos, inv_freq)
         L.flash_attn_bwd_tc_kv(q, k, v, do, lse, delta, dq_acc, dk, dv, scale, causal,
                                q_offset, k_offset, k_pos, inv_freq, status_word(q.device),
-                               **_pull_args(pull))
+                               **_pull_args(pull), k_cs=k_cs)
         L.flash_attn_bwd_dq_convert(dq_acc, dq, q_pos, inv_freq)
         return
     # Explicit flash-attention backward using the given (global) log-sum-exp, so a

@@ -55,18 +55,23 @@ def gemm(
 _ROPE_TABLES: dict = {}
 
 
-def rope_table(positions: torch.Tensor, inv_freq: torch.Tensor) -> torch.Tensor:
-    """fp32 ``[len(positions), D/2, 2]`` table of (cos, sin)(position * inv_freq).
+def rope_table(positions: torch.Tensor, inv_freq: torch.Tensor,
+               dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    """``[len(positions), D/2, 2]`` table of (cos, sin)(position * inv_freq), computed in
+    fp32 and stored as ``dtype``. The QKV GEMM's RoPE epilogue reads it as bf16 (the
+    reference's rotary embedding also casts cos and sin to the compute dtype,
+    src/nano_megatron/nn/rotary.py:36); the attention backward's inverse rotation reads it
+    as fp32.
 
     Built once per positions tensor (the model caches those per sequence layout) and
     kept with a reference to it, so its address cannot be reused by another tensor
     while the entry lives."""
-    key = (positions.data_ptr(), positions.numel(), inv_freq.data_ptr(), positions.device)
+    key = (positions.data_ptr(), positions.numel(), inv_freq.data_ptr(), positions.device, dtype)
     hit = _ROPE_TABLES.get(key)
     if hit is not None:
         return hit[2]
     ang = positions.to(torch.float32)[:, None] * inv_freq.to(torch.float32)[None, :]
-    table = torch.stack([torch.cos(ang), torch.sin(ang)], dim=-1).contiguous()
+    table = torch.stack([torch.cos(ang), torch.sin(ang)], dim=-1).to(dtype).contiguous()
     if len(_ROPE_TABLES) >= 64:
         _ROPE_TABLES.pop(next(iter(_ROPE_TABLES)))
     _ROPE_TABLES[key] = (positions, inv_freq, table)
@@ -119,4 +124,4 @@ def qkv_rope_fwd(x: torch.Tensor, w_qkv: torch.Tensor, positions: torch.Tensor,
         out = torch.empty(x.shape[0], w_qkv.shape[0], device=x.device, dtype=torch.bfloat16)
     return gemm(x, w_qkv, out, epilogue=EPI_ROPE, positions=positions, inv_freq=inv_freq,
                 head_dim=head_dim, rope_cols=rope_cols, pos_div=pos_div,
-                rope_cs=rope_table(positions, inv_freq))
+                rope_cs=rope_table(positions, inv_freq, torch.bfloat16))

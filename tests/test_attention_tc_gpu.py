@@ -53,7 +53,7 @@ def test_tc_backward_matches_fp32(d, hq, hkv, s, b):
     from nano_megatron_b200.ops._ext import lib
 
     assert lib().attn_bwd_softmax_groups() == \
-        (2 if os.environ.get("NMB_ATTN_BWD_SOFTMAX_GROUPS") == "2" else 1)
+        (1 if os.environ.get("NMB_ATTN_BWD_SOFTMAX_GROUPS") == "1" else 2)
     assert _rel(dv, vr.grad) < 2e-2
     assert _rel(dk, kr.grad) < 2e-2
     assert _rel(dq, qr.grad) < 2e-2
@@ -81,12 +81,13 @@ def test_tc_backward_inverse_rope_matches_cpu_formula():
         assert _rel(a, c) < 2e-2
 
 
-def test_two_softmax_warp_groups_variant():
-    """The backward with two softmax warp groups per CTA (each takes half of the query
-    columns and of the dQ / dK-dV drains) passes the same checks, in a fresh process."""
-    if os.environ.get("NMB_ATTN_BWD_SOFTMAX_GROUPS") == "2":
+def test_one_softmax_warp_group_variant():
+    """The backward with one softmax warp group per CTA (the default has two, each taking
+    half of the query columns and of the dQ / dK-dV drains) passes the same checks, in a
+    fresh process."""
+    if os.environ.get("NMB_ATTN_BWD_SOFTMAX_GROUPS") == "1":
         pytest.skip("already running the variant")
-    env = dict(os.environ, NMB_ATTN_BWD_SOFTMAX_GROUPS="2")
+    env = dict(os.environ, NMB_ATTN_BWD_SOFTMAX_GROUPS="1")
     r = subprocess.run([sys.executable, "-m", "pytest", __file__, "-q", "-m", "gpu",
                         "-p", "no:cacheprovider", "-k", "matches_fp32 or inverse_rope"],
                        env=env, capture_output=True, text=True, timeout=900)

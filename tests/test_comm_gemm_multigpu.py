@@ -15,7 +15,7 @@ pytestmark = pytest.mark.gpu
 WORLD = 2
 
 
-def _worker(rank, world, port, errq):
+def _worker(rank, world, port, errq, rs_in_kernel=False):
     import traceback
     from datetime import timedelta
 
@@ -33,6 +33,7 @@ def _worker(rank, world, port, errq):
         from nano_megatron_b200.ops import comm_gemm as CG
         from nano_megatron_b200.ops._ext import status_word
 
+        CG.RS_IN_KERNEL = rs_in_kernel    # reduce-scatter reduced in the GEMM epilogue
         grp = SimpleNamespace(rank=rank, size=world, process_group=dist.group.WORLD)
         ws = SymmetricWorkspace.create(grp, rs_bytes=32 << 20, ag_bytes=16 << 20, device=dev)
         R, K, N = 1024, 1024, 1024
@@ -69,7 +70,8 @@ def _worker(rank, world, port, errq):
         raise
 
 
-def test_fused_tp_collectives_two_gpus():
+@pytest.mark.parametrize("rs_in_kernel", [False, True], ids=["rs_two_pass", "rs_in_kernel"])
+def test_fused_tp_collectives_two_gpus(rs_in_kernel):
     if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
     import random
@@ -79,7 +81,8 @@ def test_fused_tp_collectives_two_gpus():
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
     port = random.randint(20000, 40000)
-    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, errq)) for r in range(WORLD)]
+    procs = [ctx.Process(target=_worker, args=(r, WORLD, port, errq, rs_in_kernel))
+             for r in range(WORLD)]
     for p in procs:
         p.start()
     for p in procs:

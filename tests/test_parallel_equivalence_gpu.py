@@ -130,6 +130,7 @@ LAYOUTS = {
     "dp2_zero2": ({"parallel": {"data": 2}, "dp_mode": "zero2"}, 2),
     "dp2_zero3": ({"parallel": {"data": 2}, "dp_mode": "zero3"}, 2),
     "dp2_zero3_offload": ({"parallel": {"data": 2}, "dp_mode": "zero3", "offload": True}, 2),
+    "tp2_sp": ({"parallel": {"tensor": 2, "sequence_parallel": True}}, 2),
     "tp2_pp2_sp": ({"parallel": {"tensor": 2, "pipeline": 2, "sequence_parallel": True}}, 4),
     "tp2_cp2_sp_ring": ({"parallel": {"tensor": 2, "context": 2, "sequence_parallel": True},
                          "cp": {"backend": "ring", "load_balance": True}}, 4),
