@@ -233,15 +233,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = mbar_wait(s_full, j & 1, p.status, kStatusAttnTimeout, abort_flag);
       if (!ok) break;
       tc_fence_after();
+      // all four 32-column loads in flight together, one wait
+      uint32_t r[kBN];
+#pragma unroll
+      for (int c = 0; c < kBN / 32; ++c)
+        tmem_ld_32x32b_x32(tS + lane_off + c * 32, *reinterpret_cast<uint32_t(*)[32]>(r + c * 32));
+      tmem_wait_ld();
       float s[kBN];
 #pragma unroll
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tS + lane_off + c * 32, r);
-        tmem_wait_ld();
-#pragma unroll
-        for (int e = 0; e < 32; ++e) s[c * 32 + e] = __uint_as_float(r[e]) * p.scale_log2;
-      }
+      for (int e = 0; e < kBN; ++e) s[e] = __uint_as_float(r[e]) * p.scale_log2;
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(s_free);
@@ -249,11 +249,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool need_mask = (n0 + kBN > p.Sk) ||
                              (p.causal && p.k_offset + n0 + kBN - 1 > p.q_offset + m0);
       if (need_mask) {
+        // visible keys of this query row in the block: columns [0, vis), applied with a
+        // select per element (per-element compare-and-branch stalled the phase)
+        int vis = min(kBN, p.Sk - n0);
+        if (p.causal) vis = min(vis, qpos - p.k_offset - n0 + 1);
 #pragma unroll
-        for (int e = 0; e < kBN; ++e) {
-          const int kc = n0 + e;
-          if (kc >= p.Sk || (p.causal && p.k_offset + kc > qpos)) s[e] = -INFINITY;
-        }
+        for (int e = 0; e < kBN; ++e) s[e] = e < vis ? s[e] : -INFINITY;
       }
       float mx = -INFINITY;
 #pragma unroll
@@ -262,13 +263,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float corr = (m_run == -INFINITY) ? 0.f : ex2(m_run - m_new);
       float rs = 0.f;
       uint32_t pk[kBN / 2];
+      // a row with no visible key yet (m_new = -inf) has s = -inf everywhere: exponent
+      // reference 0 gives P = 0 without a per-element test
+      const float mref = m_new == -INFINITY ? 0.f : m_new;
+#pragma unroll
+      for (int e = 0; e < kBN; ++e) s[e] = ex2(s[e] - mref);
+      float rs4[4] = {0.f, 0.f, 0.f, 0.f};   // four partial sums: short dependency chains
 #pragma unroll
       for (int e = 0; e < kBN; e += 2) {
-        const float p0 = m_new == -INFINITY ? 0.f : ex2(s[e] - m_new);
-        const float p1 = m_new == -INFINITY ? 0.f : ex2(s[e + 1] - m_new);
-        rs += p0 + p1;
-        pk[e / 2] = pack_bf16x2(p0, p1);
+        rs4[(e / 2) & 3] += s[e] + s[e + 1];
+        pk[e / 2] = pack_bf16x2(s[e], s[e + 1]);
       }
+      rs = (rs4[0] + rs4[1]) + (rs4[2] + rs4[3]);
       l_run = l_run * corr + rs;
       // PV_{j-1} must be complete before P is overwritten or O is rescaled.
       if (j > 0) {
