@@ -90,4 +90,6 @@ def test_fused_replica_matches_nccl(mode, tmp_path):
                 for k in ("exp_avg", "exp_avg_sq", "master_param"):
                     x, y = sa[i][k].float(), sb[i][k].float()
                     rel = ((x - y).norm() / (x.norm() + 1e-12)).item()
-                    assert rel < 5e-3, (i, k, rel)
+                    # the second moment is quadratic in the gradient: twice its relative
+                    # error (the two runs' gradients differ by fp32 atomics order)
+                    assert rel < (1e-2 if k == "exp_avg_sq" else 5e-3), (i, k, rel)
