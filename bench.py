@@ -62,7 +62,7 @@ WORKLOADS = {
                   "tie_embeddings": True},
         # micro-batch per GPU count (both arms): the largest that measured fastest at that
         # layout on B200 (fewer, larger GEMMs; PP keeps >= 16 microbatches in flight)
-        "global_batch": 256, "micro_batch": {1: 32, 2: 64, 4: 32, 8: 16},
+        "global_batch": 256, "micro_batch": {1: 32, 2: 64, 4: 32, 8: 32},
         "layouts": {1: {}, 2: {"tensor": 2}, 4: {"tensor": 2, "pipeline": 2},
                     8: {"tensor": 2, "pipeline": 2, "data": 2}},
         "sections": {"pipeline": {"schedule": "1f1b", "overlap_p2p": True},
