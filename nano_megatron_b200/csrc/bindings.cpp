@@ -8,7 +8,8 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
              double beta, c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
              c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
              int64_t head_dim, int64_t rope_cols, int64_t pos_div, at::Tensor status,
-             int64_t bn_override, int64_t max_ctas, c10::optional<at::Tensor> rope_cs);
+             int64_t bn_override, int64_t max_ctas, c10::optional<at::Tensor> rope_cs,
+             c10::optional<at::Tensor> ce_part);
 void flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor lse,
                     double softmax_scale, bool causal, int64_t q_offset, int64_t k_offset);
 void flash_attn_bwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor o, at::Tensor dout,
@@ -58,7 +59,8 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
                 c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
                 int64_t head_dim, int64_t rope_cols, int64_t pos_div, int64_t rank,
                 int64_t flags_ptr, int64_t epoch_ptr, at::Tensor status,
-                c10::optional<at::Tensor> rope_cs, c10::optional<at::Tensor> gather_ready);
+                c10::optional<at::Tensor> rope_cs, c10::optional<at::Tensor> gather_ready,
+                c10::optional<at::Tensor> ce_part);
 void gemm_tc_rs(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn,
                 std::vector<int64_t> staging_ptrs, std::vector<int64_t> staging_ptrs_odd,
                 int64_t rows_per_rank, int64_t n_out, int64_t rank, int64_t epoch_ptr,
@@ -77,6 +79,11 @@ void tp_embedding_bwd_gather(at::Tensor ids, std::vector<int64_t> slots_even,
 void tp_ce_stats_scatter(at::Tensor logits, at::Tensor labels, int64_t vstart, int64_t rank,
                          std::vector<int64_t> slots_even, std::vector<int64_t> slots_odd,
                          int64_t epoch_ptr);
+void ce_from_parts(at::Tensor logits, at::Tensor labels, at::Tensor parts, int64_t nparts,
+                   at::Tensor loss_row, bool write_grad);
+void tp_ce_parts_scatter(at::Tensor logits, at::Tensor labels, int64_t vstart, at::Tensor parts,
+                         int64_t nparts, int64_t rank, std::vector<int64_t> slots_even,
+                         std::vector<int64_t> slots_odd, int64_t epoch_ptr);
 void tp_ce_finish_gather(at::Tensor logits, at::Tensor labels, int64_t vstart, int64_t stats_even,
                          int64_t stats_odd, int64_t tp, at::Tensor loss_row, bool write_grad,
                          int64_t flags_ptr, int64_t epoch_ptr, at::Tensor status);
@@ -112,7 +119,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("alpha_t"), py::arg("alpha"), py::arg("beta"), py::arg("aux"),
         py::arg("swiglu_up_row"), py::arg("positions"), py::arg("inv_freq"), py::arg("head_dim"),
         py::arg("rope_cols"), py::arg("pos_div"), py::arg("status"), py::arg("bn_override"),
-        py::arg("max_ctas"), py::arg("rope_cs") = py::none());
+        py::arg("max_ctas"), py::arg("rope_cs") = py::none(), py::arg("ce_part") = py::none());
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
   m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc,
@@ -155,7 +162,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("aux"), py::arg("swiglu_up_row"), py::arg("positions"), py::arg("inv_freq"),
         py::arg("head_dim"), py::arg("rope_cols"), py::arg("pos_div"), py::arg("rank"),
         py::arg("flags_ptr"), py::arg("epoch_ptr"), py::arg("status"),
-        py::arg("rope_cs") = py::none(), py::arg("gather_ready") = py::none());
+        py::arg("rope_cs") = py::none(), py::arg("gather_ready") = py::none(),
+        py::arg("ce_part") = py::none());
   m.def("gemm_tc_rs", &gemm_tc_rs, "GEMM->RS: partial tiles stored into the owner's staging",
         py::arg("a"), py::arg("a_mn"), py::arg("b"), py::arg("b_mn"), py::arg("staging_ptrs"),
         py::arg("staging_ptrs_odd"), py::arg("rows_per_rank"), py::arg("n_out"),
@@ -170,6 +178,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "TP embedding backward: dY rows of this vocabulary shard read from the owners' slots");
   m.def("tp_ce_stats_scatter", &tp_ce_stats_scatter,
         "TP cross-entropy: per-row shard statistics stored into every rank's slot");
+  m.def("ce_from_parts", &ce_from_parts,
+        "cross-entropy from the LM-head GEMM's per-tile (max, sum exp): row loss + in-place grad");
+  m.def("tp_ce_parts_scatter", &tp_ce_parts_scatter,
+        "vocab-parallel CE: per-tile statistics merged and stored into every TP rank's slot");
   m.def("tp_ce_finish_gather", &tp_ce_finish_gather,
         "TP cross-entropy: merge every rank's statistics, loss and in-place gradient");
   m.def("symm_alloc", &symm_alloc);

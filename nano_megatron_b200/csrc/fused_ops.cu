@@ -470,6 +470,75 @@ __global__ void __launch_bounds__(NT) ce_fused_kernel(__nv_bfloat16* logits, int
   }
 }
 
+// (max, sum exp) of a row from `n` partial pairs written by the LM-head GEMM epilogue,
+// merged by one warp.
+__device__ __forceinline__ void merge_parts_warp(const float2* __restrict__ parts, int n,
+                                                 float& m_out, float& s_out) {
+  const int lane = threadIdx.x & 31;
+  float m = -INFINITY, s = 0.f;
+  for (int i = lane; i < n; i += 32) {
+    const float2 q = parts[i];
+    const float nm = fmaxf(m, q.x);
+    if (nm != -INFINITY)
+      s = (m == -INFINITY ? 0.f : s * ex2f((m - nm) * kLog2eF)) +
+          (q.x == -INFINITY ? 0.f : q.y * ex2f((q.x - nm) * kLog2eF));
+    m = nm;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o);
+    const float os = __shfl_xor_sync(0xffffffffu, s, o);
+    const float nm = fmaxf(m, om);
+    if (nm != -INFINITY)
+      s = (m == -INFINITY ? 0.f : s * ex2f((m - nm) * kLog2eF)) +
+          (om == -INFINITY ? 0.f : os * ex2f((om - nm) * kLog2eF));
+    m = nm;
+  }
+  m_out = m;
+  s_out = s;
+}
+
+// Cross-entropy over the whole vocabulary from the LM-head GEMM's per-tile statistics:
+// row loss, and the logits overwritten by softmax - onehot. One pass over the logits (the
+// statistics pass ran inside the GEMM).
+template <int NT>
+__global__ void __launch_bounds__(NT) ce_parts_finish_kernel(
+    __nv_bfloat16* logits, int64_t ld, const int64_t* __restrict__ labels, int V, int T,
+    const float2* __restrict__ parts, int nparts, float* __restrict__ loss_row, int write_grad) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  __shared__ float s_lse;
+  __nv_bfloat16* row = logits + static_cast<int64_t>(t) * ld;
+  const int64_t lab = labels[t];
+  const bool valid = lab >= 0;
+  if (threadIdx.x < 32) {
+    float m, sx;
+    merge_parts_warp(parts + static_cast<int64_t>(t) * nparts, nparts, m, sx);
+    if (threadIdx.x == 0) {
+      const float lse = m + __log2f(sx) * kLn2F;
+      const float tgt = (valid && lab < V) ? __bfloat162float(row[lab]) : 0.f;
+      loss_row[t] = valid ? lse - tgt : 0.f;
+      s_lse = lse;
+    }
+  }
+  __syncthreads();
+  if (!write_grad) return;
+  const float lse = s_lse;
+  const int nvec = V / 8;
+  for (int c = threadIdx.x; c < nvec; c += NT) {
+    uint4* q = reinterpret_cast<uint4*>(row) + c;
+    float f[8];
+    unpack8(*q, f);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      float gval = valid ? ex2f((f[e] - lse) * kLog2eF) : 0.f;
+      if (valid && c * 8 + e == lab) gval -= 1.f;
+      f[e] = gval;
+    }
+    *q = pack8(f);
+  }
+}
+
 // ------------------------------------------------------------------ AdamW
 // Decoupled-weight-decay Adam over flat fp32 buffers (torch.optim.AdamW
 // semantics): p *= 1 - lr*wd; m = b1 m + (1-b1) g; v = b2 v + (1-b2) g^2;
@@ -755,6 +824,25 @@ void ce_fused(at::Tensor logits, at::Tensor labels, at::Tensor loss_row, bool wr
   ce_fused_kernel<256><<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
       labels.data_ptr<int64_t>(), V, T, loss_row.data_ptr<float>(), write_grad ? 1 : 0); NMB_LAUNCHED(1);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void ce_from_parts(at::Tensor logits, at::Tensor labels, at::Tensor parts, int64_t nparts,
+                   at::Tensor loss_row, bool write_grad) {
+  NMB_CHECK_BF16(logits);
+  const int T = logits.size(0), V = logits.size(1);
+  TORCH_CHECK(V % 8 == 0 && logits.stride(1) == 1 && logits.stride(0) % 8 == 0);
+  TORCH_CHECK(parts.is_cuda() && parts.scalar_type() == at::kFloat && parts.is_contiguous() &&
+                  parts.numel() >= static_cast<int64_t>(T) * nparts * 2 && nparts >= 1,
+              "ce_from_parts: parts must hold T x nparts (max, sum exp) pairs");
+  TORCH_CHECK(labels.is_cuda() && labels.scalar_type() == at::kLong && labels.numel() == T);
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(logits.device());
+  ce_parts_finish_kernel<256><<<T, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<__nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
+      labels.data_ptr<int64_t>(), V, T, reinterpret_cast<const float2*>(parts.data_ptr<float>()),
+      static_cast<int>(nparts), loss_row.data_ptr<float>(), write_grad ? 1 : 0);
+  NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -25,6 +25,10 @@
 //                columns; writes h = silu(g) * u and keeps [g | u] for backward
 //   kEpiRoPE   : rotate-half rotary embedding applied to the first `rope_cols`
 //                columns (q and k heads) of a fused QKV projection
+//   kEpiCEStats: LM head. Stores the bf16 logits and, per row, the (max, sum exp) of the
+//                rounded logits over each epilogue warp's half of the tile into `ce_part`
+//                ([M][n-tiles x 2] float2), so the cross-entropy needs no statistics pass
+//                over the logits (it merges the parts, then writes the gradient in place)
 //   kEpiPeer   : GEMM -> reduce-scatter. Output row r belongs to TP rank
 //                r / comm_rows; the bf16 partial tile is stored straight into that
 //                rank's symmetric staging buffer (slot = this rank) over NVLink, so
@@ -60,7 +64,11 @@
 
 namespace nmb {
 
-enum EpiKind : int { kEpiBF16 = 0, kEpiF32Acc = 1, kEpiSwiGLU = 2, kEpiRoPE = 3, kEpiPeer = 4 };
+enum EpiKind : int {
+  kEpiBF16 = 0, kEpiF32Acc = 1, kEpiSwiGLU = 2, kEpiRoPE = 3, kEpiPeer = 4, kEpiCEStats = 5
+};
+// LM head with cross-entropy statistics: each epilogue warp covers half of a 256-column tile
+constexpr int kCEPartsPerTile = 2;
 
 constexpr int kMaxTP = 8;
 // Per-tile flags of the in-kernel GEMM -> reduce-scatter: every rank's buffer holds
@@ -100,6 +108,7 @@ struct GemmParams {
   const float2* rope_cs;                // kEpiRoPE: (cos, sin) table [seq_len][head_dim / 2]
   const uint32_t* rope_cs16;            // kEpiRoPE: the same table as packed bf16 (cos | sin)
   uint32_t* gather_ready;               // gather: per m-tile "rows staged in xfull" = epoch
+  float2* ce_part;                      // kEpiCEStats: [M][num_n_tiles * kCEPartsPerTile]
   // GEMM -> reduce-scatter with the reduction in the epilogue (kEpiPeer, rs_inplace = 1)
   uint32_t* tile_flags[kMaxTP];         // per owner rank: its [TP][kRsTileFlags] flag array
   __nv_bfloat16* own_out;               // this rank's reduced rows [comm_rows, N]
@@ -152,6 +161,12 @@ constexpr int gemm_smem_bytes() {
 // silu(x) = x / (1 + e^-x) with the fast reciprocal-based division (the result is
 // rounded to bf16); for x < -87, e^-x is +inf and the quotient is -0, the limit.
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // v[0..8) += the 8 bf16 values of a 16-byte word.
 __device__ __forceinline__ void add_bf16x8(float* v, const uint4 w) {
@@ -711,6 +726,42 @@ __global__ void __launch_bounds__(gemm_threads<EPI>(), 1)
           store_row32_bf16(arow + col, col, p.N, gv);
           store_row32_bf16(arow + p.N + col, col, p.N, uv);
         }
+      } else if constexpr (EPI == kEpiCEStats) {
+        static_assert(kParts == kCEPartsPerTile, "one statistics part per epilogue warp half");
+        const int n0 = nt * BN;
+        constexpr int kChunks = BN / 32 / kParts;
+        constexpr float kLog2e = 1.4426950408889634f;
+        float m = -INFINITY, sx = 0.f;
+        __nv_bfloat16* crow =
+            reinterpret_cast<__nv_bfloat16*>(p.C) + static_cast<int64_t>(row) * p.ldc;
+#pragma unroll 1
+        for (int c = ew * kChunks; c < (ew + 1) * kChunks; ++c) {
+          const int col = n0 + c * 32;
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, r);
+          tmem_wait_ld();
+          if (!row_ok || col >= p.N) continue;
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j)   // the values the cross-entropy will read back
+            v[j] = __bfloat162float(__float2bfloat16_rn(__uint_as_float(r[j]) * alpha));
+          store_row32_bf16(crow + col, col, p.N, v);
+          const int nv = min(32, p.N - col);
+          float lm = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) lm = j < nv ? fmaxf(lm, v[j]) : lm;
+          const float nm = fmaxf(m, lm);
+          float part[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            part[j & 3] += j < nv ? ex2_approx((v[j] - nm) * kLog2e) : 0.f;
+          sx = (m == -INFINITY ? 0.f : sx * ex2_approx((m - nm) * kLog2e)) +
+               ((part[0] + part[1]) + (part[2] + part[3]));
+          m = nm;
+        }
+        if (row_ok)
+          p.ce_part[(static_cast<int64_t>(row) * p.num_n_tiles + nt) * kCEPartsPerTile + ew] =
+              make_float2(m, sx);
       } else {  // kEpiRoPE
         const int n0 = nt * BN;
         const int D = p.head_dim;
@@ -919,7 +970,7 @@ static int choose_splits(int tiles, int num_kb) {
 // fp32-accumulating weight-gradient GEMMs use 128 x 128 tiles plus split-K instead.
 static int choose_bn(int M, int N, int epi) {
   (void)M;
-  if (epi == kEpiSwiGLU) return 256;
+  if (epi == kEpiSwiGLU || epi == kEpiCEStats) return 256;
   if (epi == kEpiF32Acc) return 128;
   return N > 128 ? 256 : 128;
 }
@@ -937,7 +988,8 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
              double beta, c10::optional<at::Tensor> aux, int64_t swiglu_up_row,
              c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
              int64_t head_dim, int64_t rope_cols, int64_t pos_div, at::Tensor status,
-             int64_t bn_override, int64_t max_ctas, c10::optional<at::Tensor> rope_cs) {
+             int64_t bn_override, int64_t max_ctas, c10::optional<at::Tensor> rope_cs,
+             c10::optional<at::Tensor> ce_part) {
   check_operand(a, "A");
   check_operand(b, "B");
   const int64_t M = a_mn ? a.size(1) : a.size(0);
@@ -978,6 +1030,16 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
     p.ld_aux = aux->stride(0);
     p.swiglu_up_row = static_cast<int>(swiglu_up_row);
     bn = 256;
+  }
+  if (epi == kEpiCEStats) {
+    bn = 256;
+    const int64_t parts = ((N + bn - 1) / bn) * kCEPartsPerTile;
+    TORCH_CHECK(ce_part.has_value() && ce_part->is_cuda() &&
+                    ce_part->scalar_type() == at::kFloat && ce_part->is_contiguous() &&
+                    ce_part->numel() >= M * parts * 2,
+                "LM-head statistics epilogue needs an fp32 [M, n-tiles x 2, 2] buffer");
+    TORCH_CHECK(!a_mn && !b_mn, "LM-head statistics epilogue requires K-major operands");
+    p.ce_part = reinterpret_cast<float2*>(ce_part->data_ptr<float>());
   }
   if (epi == kEpiRoPE) {
     TORCH_CHECK(positions.has_value() && inv_freq.has_value(), "RoPE epilogue inputs missing");
@@ -1029,6 +1091,8 @@ void gemm_tc(at::Tensor a, bool a_mn, at::Tensor b, bool b_mn, at::Tensor c, int
   } else if (epi == kEpiRoPE) {
     TORCH_CHECK(!a_mn && !b_mn, "RoPE epilogue requires K-major operands");
     dispatch_bn<false, false, kEpiRoPE>(bn, ta, tb, p, stream, mc);
+  } else if (epi == kEpiCEStats) {
+    launch<256, false, false, kEpiCEStats>(ta, tb, p, stream, mc);
   } else if (epi == kEpiBF16) {
     if (!a_mn && !b_mn) dispatch_bn<false, false, kEpiBF16>(bn, ta, tb, p, stream, mc);
     else if (!a_mn && b_mn) dispatch_bn<false, true, kEpiBF16>(bn, ta, tb, p, stream, mc);
@@ -1055,7 +1119,8 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
                 c10::optional<at::Tensor> positions, c10::optional<at::Tensor> inv_freq,
                 int64_t head_dim, int64_t rope_cols, int64_t pos_div, int64_t rank,
                 int64_t flags_ptr, int64_t epoch_ptr, at::Tensor status,
-                c10::optional<at::Tensor> rope_cs, c10::optional<at::Tensor> gather_ready) {
+                c10::optional<at::Tensor> rope_cs, c10::optional<at::Tensor> gather_ready,
+                c10::optional<at::Tensor> ce_part) {
   check_operand(a_local, "A shard");
   check_operand(b, "B");
   const int tp = static_cast<int>(shard_ptrs.size());
@@ -1113,6 +1178,14 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
       else
         p.rope_cs = reinterpret_cast<const float2*>(rope_cs->data_ptr<float>());
     }
+  } else if (epi == kEpiCEStats) {
+    bn = 256;
+    const int64_t parts = ((N + bn - 1) / bn) * kCEPartsPerTile;
+    TORCH_CHECK(!b_mn && ce_part.has_value() && ce_part->is_cuda() &&
+                    ce_part->scalar_type() == at::kFloat && ce_part->is_contiguous() &&
+                    ce_part->numel() >= M * parts * 2,
+                "gemm_tc_ag: LM-head statistics need an fp32 [M, n-tiles x 2, 2] buffer");
+    p.ce_part = reinterpret_cast<float2*>(ce_part->data_ptr<float>());
   } else {
     TORCH_CHECK(epi == kEpiBF16, "gemm_tc_ag: epilogue must be bf16, RoPE or SwiGLU");
   }
@@ -1149,6 +1222,8 @@ void gemm_tc_ag(at::Tensor a_local, std::vector<int64_t> shard_ptrs,
     launch<256, false, false, kEpiSwiGLU, true>(ta, tb, p, stream, 0, &cm);
   else if (epi == kEpiRoPE)
     dispatch_bn<false, false, kEpiRoPE, true>(bn, ta, tb, p, stream, 0, &cm);
+  else if (epi == kEpiCEStats)
+    launch<256, false, false, kEpiCEStats, true>(ta, tb, p, stream, 0, &cm);
   else if (b_mn)
     dispatch_bn<false, true, kEpiBF16, true>(bn, ta, tb, p, stream, 0, &cm);
   else

@@ -224,6 +224,49 @@ __global__ void __launch_bounds__(NT) ce_stats_scatter_kernel(
   }
 }
 
+// Same as ce_stats_scatter_kernel, but the (max, sum exp) of the row come from the LM-head
+// GEMM epilogue's per-tile parts (merged by one warp per row) instead of a pass over the
+// logits; only the target logit is read back.
+__global__ void ce_parts_scatter_kernel(const __nv_bfloat16* __restrict__ logits, int64_t ld,
+                                        const int64_t* __restrict__ labels, int64_t vstart, int V,
+                                        int T, const float2* __restrict__ parts, int nparts,
+                                        int rank, int tp, AuxPtrs dst, const uint32_t* epoch_ptr) {
+  const int t = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (t >= T) return;   // warp-uniform
+  const int lane = threadIdx.x & 31;
+  float m = -INFINITY, sx = 0.f;
+  for (int i = lane; i < nparts; i += 32) {
+    const float2 q = parts[static_cast<int64_t>(t) * nparts + i];
+    const float nm = fmaxf(m, q.x);
+    if (nm != -INFINITY)
+      sx = (m == -INFINITY ? 0.f : sx * ex2_aux((m - nm) * kLog2eAux)) +
+           (q.x == -INFINITY ? 0.f : q.y * ex2_aux((q.x - nm) * kLog2eAux));
+    m = nm;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o);
+    const float os = __shfl_xor_sync(0xffffffffu, sx, o);
+    const float nm = fmaxf(m, om);
+    if (nm != -INFINITY)
+      sx = (m == -INFINITY ? 0.f : sx * ex2_aux((m - nm) * kLog2eAux)) +
+           (om == -INFINITY ? 0.f : os * ex2_aux((om - nm) * kLog2eAux));
+    m = nm;
+  }
+  if (lane < tp) {
+    const uint32_t e = read_epoch(epoch_ptr) + 1u;
+    const int64_t lab = labels[t];
+    const int64_t li = lab - vstart;
+    const float tgt = (lab >= 0 && li >= 0 && li < V)
+                          ? __bfloat162float(logits[static_cast<int64_t>(t) * ld + li]) : 0.f;
+    float* st = static_cast<float*>((e & 1u) ? dst.odd[lane] : dst.even[lane]) +
+                (static_cast<int64_t>(rank) * T + t) * 3;
+    st[0] = m;
+    st[1] = sx;
+    st[2] = tgt;
+  }
+}
+
 // One block per row: wait for every rank's statistics, merge them, write the row loss and
 // (optionally) overwrite the local logits with d loss_row / d logits.
 template <int NT>
@@ -390,6 +433,32 @@ void tp_ce_stats_scatter(at::Tensor logits, at::Tensor labels, int64_t vstart, i
       reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
       labels.data_ptr<int64_t>(), vstart, V, T, static_cast<int>(rank), tp, dst,
       reinterpret_cast<const uint32_t*>(epoch_ptr));
+  NMB_LAUNCHED(1);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void tp_ce_parts_scatter(at::Tensor logits, at::Tensor labels, int64_t vstart, at::Tensor parts,
+                         int64_t nparts, int64_t rank, std::vector<int64_t> slots_even,
+                         std::vector<int64_t> slots_odd, int64_t epoch_ptr) {
+  TORCH_CHECK(logits.is_cuda() && logits.scalar_type() == at::kBFloat16 && logits.dim() == 2 &&
+              logits.stride(1) == 1);
+  TORCH_CHECK(labels.is_cuda() && labels.scalar_type() == at::kLong && labels.is_contiguous() &&
+              labels.numel() == logits.size(0));
+  TORCH_CHECK(parts.is_cuda() && parts.scalar_type() == at::kFloat && parts.is_contiguous() &&
+                  parts.numel() >= logits.size(0) * nparts * 2 && nparts >= 1,
+              "tp_ce_parts_scatter: parts must hold T x nparts (max, sum exp) pairs");
+  const AuxPtrs dst = aux_ptrs(slots_even, slots_odd);
+  const int tp = static_cast<int>(slots_even.size());
+  TORCH_CHECK(rank >= 0 && rank < tp);
+  check_ptrs(4, epoch_ptr);
+  const int T = static_cast<int>(logits.size(0)), V = static_cast<int>(logits.size(1));
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(logits.device());
+  ce_parts_scatter_kernel<<<(T + 7) / 8, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(logits.data_ptr()), logits.stride(0),
+      labels.data_ptr<int64_t>(), vstart, V, T,
+      reinterpret_cast<const float2*>(parts.data_ptr<float>()), static_cast<int>(nparts),
+      static_cast<int>(rank), tp, dst, reinterpret_cast<const uint32_t*>(epoch_ptr));
   NMB_LAUNCHED(1);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

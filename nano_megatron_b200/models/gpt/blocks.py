@@ -425,15 +425,25 @@ class HeadLossFn(torch.autograd.Function):
         xn, rstd = F.rmsnorm(h2, w_norm.detach(), eps)
         fused = tp.fused(xn) and w_lm.shape[0] % 8 == 0
         if fused:
-            # AG -> LM-head GEMM, then the row statistics exchanged by peer stores + flag
-            logits, xg = CG.allgather_gemm(tp.workspace, xn, w_lm.detach())
+            # AG -> LM-head GEMM whose epilogue also writes each row's per-tile (max, sum exp),
+            # then the row statistics exchanged by peer stores + flag
+            from nano_megatron_b200.ops.gemm import ce_parts_per_row
+
+            parts = torch.empty(xn.shape[0] * tp.size, ce_parts_per_row(w_lm.shape[0]), 2,
+                                device=xn.device, dtype=torch.float32)
+            logits, xg = CG.allgather_gemm(tp.workspace, xn, w_lm.detach(), epi="ce_stats",
+                                           ce_part=parts)
             rows = CG.vocab_parallel_ce_rows(tp.workspace, logits, labels,
-                                             tp.workspace.rank * w_lm.shape[0], write_grad=True)
+                                             tp.workspace.rank * w_lm.shape[0], write_grad=True,
+                                             parts=parts)
+        elif tp.size == 1:
+            # LM head + cross-entropy: the GEMM epilogue writes the row statistics
+            xg = xn
+            logits, rows = F.linear_ce(xg, w_lm.detach(), labels, write_grad=True)
         else:
             xg = tp.gather(xn)
             logits = F.linear(xg, w_lm.detach())
-            rows = vocab_parallel_ce_rows(logits, labels, tp.group if tp.size > 1 else None,
-                                          write_grad=True)
+            rows = vocab_parallel_ce_rows(logits, labels, tp.group, write_grad=True)
         count = (labels >= 0).sum().to(rows.dtype)
         loss = rows.sum() / count.clamp_min(1.0)
         ctx.tp, ctx.eps, ctx.params, ctx.fused = tp, eps, (w_norm, w_lm), fused

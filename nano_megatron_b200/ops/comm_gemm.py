@@ -26,7 +26,7 @@ from nano_megatron_b200.distributed.symmetric import CH_AG, CH_CE, CH_EMB, CH_RS
 
 from ._ext import lib
 
-EPI = {"bf16": 0, "rope": 3, "swiglu": 2}
+EPI = {"bf16": 0, "rope": 3, "swiglu": 2, "ce_stats": 5}
 
 # GEMM -> reduce-scatter with this rank's rows reduced in the GEMM's own epilogue (per-tile
 # flags) instead of a second kernel. Off by default: on 2 x B200 at the 311M out_proj shape
@@ -96,7 +96,7 @@ def ag_finish(ws, x_local: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
               aux: torch.Tensor | None = None, swiglu_up_row: int = 0,
               positions: torch.Tensor | None = None, inv_freq: torch.Tensor | None = None,
               head_dim: int = 0, rope_cols: int = 0, pos_div: int = 1,
-              channel: int = CH_AG) -> None:
+              channel: int = CH_AG, ce_part: torch.Tensor | None = None) -> None:
     R, K = x_local.shape
     table = None
     if epi == "rope":
@@ -109,7 +109,7 @@ def ag_finish(ws, x_local: torch.Tensor, b: torch.Tensor, out: torch.Tensor, *,
                      [ws.ag_shard(r, 1) for r in range(ws.size)], K, b, b_mn, out, EPI[epi],
                      xfull, aux, swiglu_up_row, positions, inv_freq, head_dim, rope_cols,
                      pos_div, ws.rank, ws.flags(ws.rank, channel), ws.epoch_ptr(channel),
-                     ws.status, table, ready)
+                     ws.status, table, ready, ce_part)
 
 
 def allgather_gemm(ws, x_local: torch.Tensor, b: torch.Tensor, *, b_mn: bool = False,
@@ -176,11 +176,18 @@ def embedding_backward_gather(ws, ids: torch.Tensor, dy_local: torch.Tensor,
 
 
 # ---------------------------------------------------------------- cross-entropy (C6)
-def ce_issue(ws, logits: torch.Tensor, labels: torch.Tensor, vstart: int) -> None:
+def ce_issue(ws, logits: torch.Tensor, labels: torch.Tensor, vstart: int,
+             parts: torch.Tensor | None = None) -> None:
+    """Store this rank's per-row (max, sum exp, target logit) into every TP rank's slot +
+    signal. With ``parts`` (the LM-head GEMM epilogue's per-tile statistics) only the target
+    logits are read back from ``logits``."""
     ws.check_ce(logits.shape[0])
-    lib().tp_ce_stats_scatter(logits, labels, vstart, ws.rank,
-                              [ws.ce_slot(r, 0) for r in range(ws.size)],
-                              [ws.ce_slot(r, 1) for r in range(ws.size)], ws.epoch_ptr(CH_CE))
+    slots = ([ws.ce_slot(r, 0) for r in range(ws.size)], [ws.ce_slot(r, 1) for r in range(ws.size)])
+    if parts is not None:
+        lib().tp_ce_parts_scatter(logits, labels, vstart, parts, parts.shape[1], ws.rank, *slots,
+                                  ws.epoch_ptr(CH_CE))
+    else:
+        lib().tp_ce_stats_scatter(logits, labels, vstart, ws.rank, *slots, ws.epoch_ptr(CH_CE))
     lib().peer_signal(ws.signal_targets(CH_CE), ws.epoch_ptr(CH_CE))
 
 
@@ -194,9 +201,9 @@ def ce_finish(ws, logits: torch.Tensor, labels: torch.Tensor, vstart: int,
 
 
 def vocab_parallel_ce_rows(ws, logits: torch.Tensor, labels: torch.Tensor, vstart: int,
-                           write_grad: bool) -> torch.Tensor:
+                           write_grad: bool, parts: torch.Tensor | None = None) -> torch.Tensor:
     """Per-row loss of the vocabulary-parallel cross-entropy; the row statistics travel by
     peer stores + flag instead of a collective. With ``write_grad`` the local logits are
     overwritten by d loss_row / d logits."""
-    ce_issue(ws, logits, labels, vstart)
+    ce_issue(ws, logits, labels, vstart, parts)
     return ce_finish(ws, logits, labels, vstart, write_grad)

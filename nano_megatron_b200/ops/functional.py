@@ -221,6 +221,20 @@ def ce_local(logits: torch.Tensor, labels: torch.Tensor, write_grad: bool):
     return ce_finish(logits, labels, 0, ce_stats(logits, labels, 0).unsqueeze(0), write_grad)
 
 
+def linear_ce(x: torch.Tensor, w: torch.Tensor, labels: torch.Tensor, write_grad: bool):
+    """LM head + single-shard cross-entropy: returns (logits, per-row loss); with
+    ``write_grad`` the logits become ``softmax - onehot``. On CUDA the GEMM's epilogue
+    produces the row statistics, so the cross-entropy reads the logits once."""
+    if _cuda(x) and w.shape[0] % 8 == 0:
+        logits, parts = _g.lm_head_ce_stats(x, w)
+        loss_row = torch.empty(x.shape[0], device=x.device, dtype=torch.float32)
+        lib().ce_from_parts(logits, labels.contiguous(), parts, parts.shape[1], loss_row,
+                            write_grad)
+        return logits, loss_row
+    logits = linear(x, w)
+    return logits, ce_local(logits, labels, write_grad)
+
+
 def ce_stats(logits: torch.Tensor, labels: torch.Tensor, vstart: int) -> torch.Tensor:
     """Per-row (max, sum exp(x - max), target logit or 0) of this vocabulary shard."""
     if _cuda(logits):

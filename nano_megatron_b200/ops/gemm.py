@@ -18,7 +18,7 @@ import torch
 
 from ._ext import lib, status_word
 
-EPI_BF16, EPI_F32_ACC, EPI_SWIGLU, EPI_ROPE = 0, 1, 2, 3
+EPI_BF16, EPI_F32_ACC, EPI_SWIGLU, EPI_ROPE, EPI_CE_STATS = 0, 1, 2, 3, 5
 
 
 def gemm(
@@ -43,13 +43,32 @@ def gemm(
     block_n: int = 0,
     max_ctas: int = 0,
     rope_cs: torch.Tensor | None = None,
+    ce_part: torch.Tensor | None = None,
 ) -> torch.Tensor:
     lib().gemm_tc(
         a, a_mn, b, b_mn, out, epilogue, residual, alpha_t, float(alpha), float(beta), aux,
         int(swiglu_up_row), positions, inv_freq, int(head_dim), int(rope_cols), int(pos_div),
-        status_word(a.device), int(block_n), int(max_ctas), rope_cs,
+        status_word(a.device), int(block_n), int(max_ctas), rope_cs, ce_part,
     )
     return out
+
+
+def ce_parts_per_row(vocab: int) -> int:
+    """(max, sum exp) parts per row the LM-head statistics epilogue writes: two per
+    256-column tile."""
+    return (vocab + 255) // 256 * 2
+
+
+def lm_head_ce_stats(x: torch.Tensor, weight: torch.Tensor, *, out: torch.Tensor | None = None
+                     ) -> tuple[torch.Tensor, torch.Tensor]:
+    """``x @ weight.T`` (bf16 logits) and the per-row, per-tile (max, sum exp) of the
+    rounded logits, ``[M, ce_parts_per_row(V), 2]`` fp32, from the same GEMM's epilogue."""
+    m, v = x.shape[0], weight.shape[0]
+    if out is None:
+        out = torch.empty(m, v, device=x.device, dtype=torch.bfloat16)
+    parts = torch.empty(m, ce_parts_per_row(v), 2, device=x.device, dtype=torch.float32)
+    gemm(x, weight, out, epilogue=EPI_CE_STATS, ce_part=parts)
+    return out, parts
 
 
 _ROPE_TABLES: dict = {}

@@ -282,3 +282,32 @@ def test_philox_dropout_statistics_and_replay():
     assert torch.equal(g, y)                      # same mask from (seed, index)
     y2 = DropoutMask(p, seed=1235)(x)
     assert not torch.equal(y2 != 0, y != 0)
+
+
+@pytest.mark.parametrize("vocab", [8192, 1000])
+def test_lm_head_ce_statistics_epilogue_matches_fp32(vocab):
+    """LM head GEMM whose epilogue writes per-tile (max, sum exp), then the one-pass
+    cross-entropy: loss rows and the in-place softmax - onehot gradient against fp32 torch
+    (a vocabulary that is not a multiple of the 256-column tile covers the tail tile;
+    ignored rows carry label -100)."""
+    from nano_megatron_b200.ops import functional as F
+
+    torch.manual_seed(11)
+    m, h = 512, 256
+    x = torch.randn(m, h, device=DEV).bfloat16()
+    w = (torch.randn(vocab, h, device=DEV) * 0.1).bfloat16()
+    labels = torch.randint(0, vocab, (m,), device=DEV)
+    labels[::7] = -100
+    logits, rows = F.linear_ce(x, w, labels, write_grad=True)
+    torch.cuda.synchronize()
+    assert int(status_word(x.device).item()) == 0
+    ref_logits = x.float() @ w.float().t()
+    valid = labels >= 0
+    lse = torch.logsumexp(ref_logits, -1)
+    tgt = ref_logits.gather(1, labels.clamp_min(0)[:, None])[:, 0]
+    ref_rows = torch.where(valid, lse - tgt, torch.zeros_like(lse))
+    assert _rel(rows, ref_rows) < 1e-2
+    grad = torch.softmax(ref_logits, -1)
+    grad[torch.arange(m, device=DEV)[valid], labels[valid]] -= 1.0
+    grad[~valid] = 0.0
+    assert _rel(logits, grad) < 2e-2
