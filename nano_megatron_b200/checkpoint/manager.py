@@ -472,6 +472,7 @@ class CheckpointManager:
 # reference's own config loader (which rejects unknown fields) can read the manifest.
 _EXTENSION_FIELDS = {("kernels", "cuda_graphs"): True, ("kernels", "fused_tp_comm"): True,
                      ("kernels", "fused_dp_comm"): True, ("kernels", "fused_cp_comm"): True,
+                     ("kernels", "deterministic"): False,
                      ("context_parallel", "load_balance"): False}
 
 

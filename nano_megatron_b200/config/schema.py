@@ -8,6 +8,9 @@ YAML files load unchanged. Additions are strictly additive:
   sm_100a kernels on CUDA devices (``torch`` is kept as a compatible spelling).
 * ``kernels.cuda_graphs`` captures the per-microbatch forward/backward of
   static-shape runs in CUDA graphs.
+* ``kernels.fused_tp_comm`` / ``fused_dp_comm`` / ``fused_cp_comm`` select the
+  collectives fused over NVLink peer memory, and ``kernels.deterministic`` the
+  fixed-order (bitwise reproducible) backward reductions.
 * ``context_parallel.load_balance`` selects zigzag chunking (rank r holds
   sequence chunks r and 2*CP-1-r) instead of contiguous chunks.
 """
@@ -255,6 +258,10 @@ class KernelConfig:
     # Context-parallel ring attention pulling the next K/V block straight from its owner's
     # memory (peer loads) instead of NCCL send/recv.
     fused_cp_comm: bool = True
+    # Fixed-order reductions in every backward kernel that otherwise sums with fp32
+    # atomics (split-K weight gradients, attention dQ, RMSNorm dgamma, embedding backward):
+    # bitwise reproducible steps at some speed cost.
+    deterministic: bool = False
 
     def __post_init__(self) -> None:
         _set(self, "backend", _enum("kernels.backend", KernelBackend, self.backend))
@@ -262,6 +269,7 @@ class KernelConfig:
         _bool("kernels.fused_tp_comm", self.fused_tp_comm)
         _bool("kernels.fused_dp_comm", self.fused_dp_comm)
         _bool("kernels.fused_cp_comm", self.fused_cp_comm)
+        _bool("kernels.deterministic", self.deterministic)
 
 
 @dataclass(frozen=True, slots=True)

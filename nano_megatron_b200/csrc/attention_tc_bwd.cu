@@ -62,7 +62,11 @@ struct Cfg {
 struct Params {
   const float* lse;     // [B, Hq, Sq] base 2
   const float* delta;   // [B, Hq, Sq]
-  float* dq_acc;        // [B, Sq, Hq, D]
+  float* dq_acc;        // [B, Sq, Hq, D], or [key blocks][B, Sq, Hq, D] (dq_slot_stride)
+  // 0: dQ partials are added into dq_acc with fp32 atomics. > 0 (deterministic mode): key
+  // block nb stores its partial into slot nb (dq_acc + nb * dq_slot_stride, zeroed by the
+  // caller) with plain stores, and the caller sums the slots in order.
+  int64_t dq_slot_stride;
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
   int64_t dk_row, dk_batch, dv_row, dv_batch;
@@ -428,11 +432,20 @@ __global__ void __launch_bounds__(threads_for<SH>(), 1)
         tmem_ld_32x32b_x32(tmem + lo + C::kColDQ + c * 32, r);
         tmem_wait_ld();
         if (q < p.Sq) {
+          if (p.dq_slot_stride != 0) {
+            float4* sdst = reinterpret_cast<float4*>(dst + nb * p.dq_slot_stride + c * 32);
 #pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            red_add_v4(dst + c * 32 + e, __uint_as_float(r[e]) * p.scale,
-                       __uint_as_float(r[e + 1]) * p.scale, __uint_as_float(r[e + 2]) * p.scale,
-                       __uint_as_float(r[e + 3]) * p.scale);
+            for (int e = 0; e < 32; e += 4)
+              sdst[e / 4] = make_float4(
+                  __uint_as_float(r[e]) * p.scale, __uint_as_float(r[e + 1]) * p.scale,
+                  __uint_as_float(r[e + 2]) * p.scale, __uint_as_float(r[e + 3]) * p.scale);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; e += 4)
+              red_add_v4(dst + c * 32 + e, __uint_as_float(r[e]) * p.scale,
+                         __uint_as_float(r[e + 1]) * p.scale, __uint_as_float(r[e + 2]) * p.scale,
+                         __uint_as_float(r[e + 3]) * p.scale);
+          }
         }
       }
       tc_fence_before();
@@ -609,7 +622,8 @@ void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor d
                           c10::optional<at::Tensor> inv_freq, at::Tensor status,
                           int64_t pull_src, c10::optional<at::Tensor> pull_dst,
                           int64_t pull_flag, int64_t pull_epoch,
-                          c10::optional<at::Tensor> k_cs, c10::optional<at::Tensor> trace) {
+                          c10::optional<at::Tensor> k_cs, c10::optional<at::Tensor> trace,
+                          int64_t dq_slot_stride) {
   const int64_t D = q.size(3);
   TORCH_CHECK(D == 64 || D == 128, "flash_attn_bwd_tc: head_dim must be 64 or 128");
   for (const at::Tensor* t : {&q, &k, &v, &dout, &dk, &dv}) {
@@ -622,6 +636,18 @@ void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor d
   p.lse = lse.data_ptr<float>();
   p.delta = delta.data_ptr<float>();
   p.dq_acc = dq_acc.data_ptr<float>();
+  TORCH_CHECK(dq_acc.is_cuda() && dq_acc.scalar_type() == at::kFloat && dq_acc.is_contiguous() &&
+                  (reinterpret_cast<uintptr_t>(dq_acc.data_ptr()) & 15u) == 0,
+              "flash_attn_bwd_tc: dq_acc must be a contiguous, 16-byte aligned fp32 buffer");
+  {
+    const int64_t rows_d = q.size(0) * q.size(1) * q.size(2) * D;
+    const int64_t slots = dq_slot_stride > 0 ? (k.size(1) + kBN - 1) / kBN : 1;
+    TORCH_CHECK(dq_slot_stride == 0 || (dq_slot_stride >= rows_d && dq_slot_stride % 4 == 0),
+                "flash_attn_bwd_tc: dq_slot_stride must be 0 or >= B*Sq*Hq*D and a multiple of 4");
+    TORCH_CHECK(dq_acc.numel() >= (slots - 1) * dq_slot_stride + rows_d,
+                "flash_attn_bwd_tc: dq_acc too small for ", slots, " slots");
+  }
+  p.dq_slot_stride = dq_slot_stride;
   p.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
   p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
   p.dk_row = dk.stride(1);

@@ -33,7 +33,10 @@ void flash_attn_bwd_tc_kv(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor d
                           c10::optional<at::Tensor> inv_freq, at::Tensor status,
                           int64_t pull_src, c10::optional<at::Tensor> pull_dst,
                           int64_t pull_flag, int64_t pull_epoch, c10::optional<at::Tensor> k_cs,
-                          c10::optional<at::Tensor> trace);
+                          c10::optional<at::Tensor> trace, int64_t dq_slot_stride);
+void set_deterministic(bool on);
+bool get_deterministic();
+void slots_sum(at::Tensor slots, at::Tensor out, bool accumulate);
 void rmsnorm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps);
 void rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, at::Tensor rstd, at::Tensor dx,
                  c10::optional<at::Tensor> dw, c10::optional<at::Tensor> dres);
@@ -137,7 +140,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("softmax_scale"), py::arg("causal"), py::arg("q_offset"), py::arg("k_offset"),
         py::arg("k_pos"), py::arg("inv_freq"), py::arg("status"), py::arg("pull_src") = 0,
         py::arg("pull_dst") = py::none(), py::arg("pull_flag") = 0, py::arg("pull_epoch") = 0,
-        py::arg("k_cs") = py::none(), py::arg("trace") = py::none());
+        py::arg("k_cs") = py::none(), py::arg("trace") = py::none(),
+        py::arg("dq_slot_stride") = 0);
+  m.def("set_deterministic", &set_deterministic,
+        "process-wide deterministic kernel mode (fixed-order reductions instead of atomics)");
+  m.def("get_deterministic", &get_deterministic);
+  m.def("slots_sum", &slots_sum, "out (+)= sum over the leading dim of slots, in order",
+        py::arg("slots"), py::arg("out"), py::arg("accumulate"));
   m.def("attn_bwd_trace_slots", &attn_bwd_trace_slots,
         "timestamps per CTA written by the attention backward's optional phase trace");
   m.def("attn_bwd_softmax_groups", &attn_bwd_softmax_groups,

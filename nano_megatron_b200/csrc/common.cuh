@@ -413,4 +413,56 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+
+// ------------------------------------------------------- deterministic mode
+// Process-wide switch (default off). When on, every kernel of this library that would
+// sum fp32 partials with atomics, in an order the hardware schedule decides, sums them in
+// a fixed order instead: split-K weight gradients run unsplit, the attention backward
+// stores one dQ partial per key block and sums the blocks in order, and the RMSNorm
+// weight gradient and the embedding backward reduce rows in row / token order. Runs are
+// then bitwise reproducible for a fixed launch configuration. Defined in fused_ops.cu.
+bool deterministic_mode();
+
+// Deterministic scatter-add of bf16 rows into fp32 `grad` rows ([V, H], H % 8 == 0,
+// 16-byte aligned). `sorted_ids` holds the T token ids sorted stably and `order` their
+// token indices, so equal ids form runs in token order. One warp per run adds the run's
+// rows, in that order, to the run's grad row with plain loads and stores: no two warps
+// touch the same row, so the result does not depend on the schedule. Ids outside
+// [vstart, vstart + V) are skipped. `chunk_of(t, c)` returns the c-th 16-byte chunk
+// (8 bf16) of token t's row.
+template <class ChunkOf>
+__device__ __forceinline__ void add_sorted_runs(const int64_t* __restrict__ sorted_ids,
+                                                const int64_t* __restrict__ order, int T,
+                                                int64_t vstart, int64_t V, int H,
+                                                float* __restrict__ grad, ChunkOf chunk_of) {
+  const int lane = threadIdx.x & 31;
+  const int warps = blockDim.x / 32;
+  const int nvec = H / 8;
+  for (int p = blockIdx.x * warps + threadIdx.x / 32; p < T; p += gridDim.x * warps) {
+    const int64_t id = sorted_ids[p];
+    if (p > 0 && sorted_ids[p - 1] == id) continue;  // not the first token of its run
+    const int64_t local = id - vstart;
+    if (local < 0 || local >= V) continue;
+    int end = p + 1;
+    while (end < T && sorted_ids[end] == id) ++end;
+    float4* dst = reinterpret_cast<float4*>(grad + local * H);
+    for (int c = lane; c < nvec; c += 32) {
+      float4 a = dst[2 * c], b = dst[2 * c + 1];
+      for (int j = p; j < end; ++j) {
+        const uint4 v = chunk_of(order[j], c);
+        a.x += bf16_lo(v.x);
+        a.y += bf16_hi(v.x);
+        a.z += bf16_lo(v.y);
+        a.w += bf16_hi(v.y);
+        b.x += bf16_lo(v.z);
+        b.y += bf16_hi(v.z);
+        b.z += bf16_lo(v.w);
+        b.w += bf16_hi(v.w);
+      }
+      dst[2 * c] = a;
+      dst[2 * c + 1] = b;
+    }
+  }
+}
+
 }  // namespace nmb

@@ -304,6 +304,72 @@ __global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids,
   }
 }
 
+// ------------------------------------------------------------------ deterministic mode
+// Kernels used instead of the atomic reductions above while deterministic_mode() is on.
+struct StridedRows {
+  const __nv_bfloat16* base;
+  int64_t ld;
+  __device__ __forceinline__ uint4 operator()(int64_t t, int c) const {
+    return reinterpret_cast<const uint4*>(base + t * ld)[c];
+  }
+};
+
+// grad[id - vstart] += dy[t], tokens grouped by id and added in token order.
+__global__ void embedding_bwd_sorted_kernel(const int64_t* __restrict__ sorted_ids,
+                                            const int64_t* __restrict__ order,
+                                            const __nv_bfloat16* __restrict__ dy, int64_t lddy,
+                                            float* __restrict__ grad, int64_t V, int64_t vstart,
+                                            int T, int H) {
+  add_sorted_runs(sorted_ids, order, T, vstart, V, H, grad, StridedRows{dy, lddy});
+}
+
+// RMSNorm weight gradient, first pass: partial[chunk][c] = sum over the chunk's rows, in
+// row order, of dy[r][c] * bf16(x[r][c] * rstd[r]) (the product the fused backward
+// accumulates). One thread per column; slots_sum_kernel adds the chunks in order.
+__global__ void rmsnorm_dw_partial_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx,
+                                          const __nv_bfloat16* __restrict__ dy, int64_t lddy,
+                                          const float* __restrict__ rstd, int rows, int H,
+                                          int rows_per_chunk, float* __restrict__ partial) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  if (c >= H) return;
+  const int r0 = blockIdx.y * rows_per_chunk;
+  const int r1 = min(rows, r0 + rows_per_chunk);
+  float acc = 0.f;
+  for (int r = r0; r < r1; ++r) {
+    const float xh = __bfloat162float(x[static_cast<int64_t>(r) * ldx + c]) * rstd[r];
+    acc += __bfloat162float(dy[static_cast<int64_t>(r) * lddy + c]) * round_bf16(xh);
+  }
+  partial[static_cast<int64_t>(blockIdx.y) * H + c] = acc;
+}
+
+// out[i] = (accumulate ? out[i] : 0) + slots[0][i] + slots[1][i] + ... + slots[S-1][i],
+// summed in slot order. `vec`: n % 4 == 0 and both buffers 16-byte aligned.
+__global__ void slots_sum_kernel(const float* __restrict__ slots, int S, int64_t n,
+                                 float* __restrict__ out, int accumulate, int vec) {
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t first = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (vec) {
+    const int64_t n4 = n / 4;
+    for (int64_t i = first; i < n4; i += stride) {
+      float4 a = accumulate ? reinterpret_cast<const float4*>(out)[i] : make_float4(0, 0, 0, 0);
+      for (int sl = 0; sl < S; ++sl) {
+        const float4 v = reinterpret_cast<const float4*>(slots + sl * n)[i];
+        a.x += v.x;
+        a.y += v.y;
+        a.z += v.z;
+        a.w += v.w;
+      }
+      reinterpret_cast<float4*>(out)[i] = a;
+    }
+  } else {
+    for (int64_t i = first; i < n; i += stride) {
+      float a = accumulate ? out[i] : 0.f;
+      for (int sl = 0; sl < S; ++sl) a += slots[sl * n + i];
+      out[i] = a;
+    }
+  }
+}
+
 // ------------------------------------------------------------------ cross-entropy
 constexpr float kLog2eF = 1.4426950408889634f;
 constexpr float kLn2F = 0.6931471805599453f;
@@ -650,6 +716,33 @@ static int grid_for(int64_t work, int threads) {
 #define NMB_CHECK_BF16(t) \
   TORCH_CHECK((t).is_cuda() && (t).scalar_type() == at::kBFloat16, #t " must be CUDA bf16")
 
+namespace nmb {
+namespace {
+std::atomic<bool> g_deterministic{false};
+}  // namespace
+bool deterministic_mode() { return g_deterministic.load(std::memory_order_relaxed); }
+}  // namespace nmb
+
+void set_deterministic(bool on) { nmb::g_deterministic.store(on, std::memory_order_relaxed); }
+bool get_deterministic() { return nmb::deterministic_mode(); }
+
+// out (+)= sum over the leading dimension of `slots` ([S, out.numel()] fp32), in order.
+void slots_sum(at::Tensor slots, at::Tensor out, bool accumulate) {
+  TORCH_CHECK(slots.is_cuda() && slots.scalar_type() == at::kFloat && slots.is_contiguous());
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kFloat && out.is_contiguous());
+  const int64_t n = out.numel();
+  TORCH_CHECK(n > 0 && slots.numel() % n == 0, "slots_sum: slots must be [S, out.numel()]");
+  const int64_t S = slots.numel() / n;
+  TORCH_CHECK(S < (1ll << 31));
+  const at::cuda::CUDAGuard guard(out.device());
+  const bool vec = n % 4 == 0 && (reinterpret_cast<uintptr_t>(slots.data_ptr()) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15u) == 0;
+  slots_sum_kernel<<<grid_for(vec ? n / 4 : n, 256), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      slots.data_ptr<float>(), static_cast<int>(S), n, out.data_ptr<float>(),
+      accumulate ? 1 : 0, vec ? 1 : 0); NMB_LAUNCHED(1);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void rmsnorm_fwd(at::Tensor x, at::Tensor w, at::Tensor y, at::Tensor rstd, double eps) {
   NMB_CHECK_BF16(x);
   NMB_CHECK_BF16(w);
@@ -711,6 +804,9 @@ void rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, at::Tensor rstd, at:
     rsp = reinterpret_cast<const __nv_bfloat16*>(dres->data_ptr());
     ldr = dres->stride(-2);
   }
+  // Deterministic mode: the fused kernel skips dw; two fixed-order passes add it.
+  float* const dw_out = dwp;
+  if (deterministic_mode()) dwp = nullptr;
   switch (H / 256) {
     case 1: rmsnorm_bwd_kernel<1><<<blocks, threads, 0, s>>>(xp, ldx, wp, gp, lddy, rp, dxp, lddx, dwp, rsp, ldr, rows); NMB_LAUNCHED(1); break;
     case 2: rmsnorm_bwd_kernel<2><<<blocks, threads, 0, s>>>(xp, ldx, wp, gp, lddy, rp, dxp, lddx, dwp, rsp, ldr, rows); NMB_LAUNCHED(1); break;
@@ -720,6 +816,17 @@ void rmsnorm_bwd(at::Tensor x, at::Tensor w, at::Tensor dy, at::Tensor rstd, at:
     default: TORCH_CHECK(false, "rmsnorm_bwd: unsupported hidden size ", H);
   }
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+  if (dw_out != nullptr && dwp == nullptr && rows > 0) {
+    const int nchunks0 = std::min(rows, 4 * 148);
+    const int per = (rows + nchunks0 - 1) / nchunks0;
+    const int nchunks = (rows + per - 1) / per;
+    at::Tensor partial = at::empty({nchunks, H}, x.options().dtype(at::kFloat));
+    rmsnorm_dw_partial_kernel<<<dim3(static_cast<unsigned>((H + 255) / 256), nchunks), 256, 0,
+                                s>>>(xp, ldx, gp, lddy, rp, rows, static_cast<int>(H), per,
+                                     partial.data_ptr<float>()); NMB_LAUNCHED(1);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    slots_sum(partial, *dw, true);
+  }
 }
 
 void swiglu_fwd(at::Tensor gu, at::Tensor h) {
@@ -787,6 +894,18 @@ void embedding_bwd(at::Tensor ids, at::Tensor dy, at::Tensor grad, int64_t vstar
   TORCH_CHECK(H % 8 == 0);
   const at::cuda::CUDAGuard guard(dy.device());
   const int blocks = std::max(1, std::min((T + 7) / 8, 148 * 16));
+  if (deterministic_mode()) {
+    TORCH_CHECK(ids.scalar_type() == at::kLong && dy.stride(1) == 1 && dy.stride(0) % 8 == 0);
+    if (T == 0) return;
+    const auto sorted = at::sort(ids.reshape({-1}), /*stable=*/true, 0, false);
+    const at::Tensor sid = std::get<0>(sorted).contiguous(), ord = std::get<1>(sorted).contiguous();
+    embedding_bwd_sorted_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        sid.data_ptr<int64_t>(), ord.data_ptr<int64_t>(),
+        reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()), dy.stride(0),
+        grad.data_ptr<float>(), grad.size(0), vstart, T, H); NMB_LAUNCHED(1);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   embedding_bwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       ids.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(dy.data_ptr()),
       dy.stride(0), grad.data_ptr<float>(), grad.size(0), vstart, T, H); NMB_LAUNCHED(1);

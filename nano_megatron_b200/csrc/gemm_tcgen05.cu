@@ -946,8 +946,10 @@ static void dispatch_bn(int bn, const CUtensorMap& ta, const CUtensorMap& tb, Ge
 }
 
 // Split-K factor for an fp32-accumulating GEMM: the smallest split (<= 8, >= 4 K-blocks
-// each) that fills the SMs' waves clearly better than no split.
+// each) that fills the SMs' waves clearly better than no split. Deterministic mode runs
+// unsplit: each output tile then has one writer, which adds to C with plain stores.
 static int choose_splits(int tiles, int num_kb) {
+  if (deterministic_mode()) return 1;
   const int sms = num_sms();
   auto eff = [&](int s) {
     const int work = tiles * s;

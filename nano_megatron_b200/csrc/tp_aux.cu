@@ -140,6 +140,34 @@ __global__ void embedding_bwd_gather_kernel(const int64_t* __restrict__ ids, Aux
   }
 }
 
+// Deterministic variant (deterministic_mode()): tokens stably sorted by id, each run of
+// equal ids added in token order by one warp (add_sorted_runs), after the same flag wait.
+struct GatheredRows {
+  AuxPtrs src;
+  bool odd;
+  int R, H;
+  __device__ __forceinline__ uint4 operator()(int64_t t, int c) const {
+    const int owner = static_cast<int>(t / R);
+    const __nv_bfloat16* row =
+        static_cast<const __nv_bfloat16*>(odd ? src.odd[owner] : src.even[owner]) +
+        (t - static_cast<int64_t>(owner) * R) * H;
+    return __ldcg(reinterpret_cast<const uint4*>(row) + c);
+  }
+};
+
+__global__ void embedding_bwd_gather_sorted_kernel(const int64_t* __restrict__ sorted_ids,
+                                                   const int64_t* __restrict__ order,
+                                                   AuxPtrs src, float* __restrict__ grad,
+                                                   int64_t V, int64_t vstart, int T, int H,
+                                                   int R, const uint32_t* flags, int tp,
+                                                   const uint32_t* epoch_ptr, int* status) {
+  __shared__ int ok;
+  block_wait_flags(flags, tp, epoch_ptr, status, &ok);
+  if (!ok) return;
+  const bool odd = read_epoch(epoch_ptr) & 1u;
+  add_sorted_runs(sorted_ids, order, T, vstart, V, H, grad, GatheredRows{src, odd, R, H});
+}
+
 // ------------------------------------------------------------------ cross-entropy
 __device__ __forceinline__ float ex2_aux(float x) {
   float y;
@@ -406,6 +434,18 @@ void tp_embedding_bwd_gather(at::Tensor ids, std::vector<int64_t> slots_even,
   check_ptrs(flags_ptr, epoch_ptr);
   const at::cuda::CUDAGuard guard(grad.device());
   const int blocks = std::max(1, std::min((T + 7) / 8, 4096));
+  if (deterministic_mode()) {
+    const auto sorted = at::sort(ids, /*stable=*/true, 0, false);
+    const at::Tensor sid = std::get<0>(sorted).contiguous(), ord = std::get<1>(sorted).contiguous();
+    embedding_bwd_gather_sorted_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+        sid.data_ptr<int64_t>(), ord.data_ptr<int64_t>(), src, grad.data_ptr<float>(),
+        grad.size(0), vstart, T, static_cast<int>(H), static_cast<int>(rows_per_rank),
+        reinterpret_cast<const uint32_t*>(flags_ptr), static_cast<int>(slots_even.size()),
+        reinterpret_cast<const uint32_t*>(epoch_ptr), status.data_ptr<int>());
+    NMB_LAUNCHED(1);
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   embedding_bwd_gather_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
       ids.data_ptr<int64_t>(), src, grad.data_ptr<float>(), grad.size(0), vstart, T,
       static_cast<int>(H), static_cast<int>(rows_per_rank),

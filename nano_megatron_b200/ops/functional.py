@@ -342,10 +342,12 @@ def attention_bwd(q, k, v, o, do, lse, dq, dk, dv, *, causal: bool, q_offset: in
     B, Sq, Hq, D = q.shape
     scale = softmax_scale if softmax_scale is not None else 1.0 / math.sqrt(D)
     if _cuda(q):
-        delta = torch.empty(B * Hq * Sq, device=q.device, dtype=torch.float32)
-        dq_acc = torch.empty(B * Sq * Hq * D, device=q.device, dtype=torch.float32)
         from ._ext import status_word
+        from .deterministic import is_deterministic
 
+        n = B * Sq * Hq * D
+        delta = torch.empty(B * Hq * Sq, device=q.device, dtype=torch.float32)
+        dq_acc = torch.empty(n, device=q.device, dtype=torch.float32)
         L = lib()
         L.flash_attn_bwd_prep(o, do, delta, dq_acc)
         k_cs = None
@@ -353,9 +355,16 @@ def attention_bwd(q, k, v, o, do, lse, dq, dk, dv, *, causal: bool, q_offset: in
             from .gemm import rope_table
 
             k_cs = rope_table(k_pos, inv_freq)
-        L.flash_attn_bwd_tc_kv(q, k, v, do, lse, delta, dq_acc, dk, dv, scale, causal,
-                               q_offset, k_offset, k_pos, inv_freq, status_word(q.device),
-                               **_pull_args(pull), k_cs=k_cs)
+        # Deterministic mode: one zeroed dQ slot per 128-key block (blocks a causal mask
+        # skips stay zero), summed in key-block order into the zeroed accumulator.
+        slots = (torch.zeros((k.shape[1] + 127) // 128, n, device=q.device, dtype=torch.float32)
+                 if is_deterministic() else None)
+        L.flash_attn_bwd_tc_kv(q, k, v, do, lse, delta, dq_acc if slots is None else slots,
+                               dk, dv, scale, causal, q_offset, k_offset, k_pos, inv_freq,
+                               status_word(q.device), **_pull_args(pull), k_cs=k_cs,
+                               dq_slot_stride=0 if slots is None else n)
+        if slots is not None:
+            L.slots_sum(slots, dq_acc, True)
         L.flash_attn_bwd_dq_convert(dq_acc, dq, q_pos, inv_freq)
         return
     # Explicit flash-attention backward using the given (global) log-sum-exp, so a

@@ -76,6 +76,9 @@ def build_model(config, parallel, rng, *, device):
 
 
 def build_training_components(config, runtime) -> TrainingComponents:
+    from nano_megatron_b200.ops.deterministic import configure as configure_determinism
+
+    configure_determinism(getattr(config.kernels, "deterministic", False))
     parallel = ParallelContext.create(runtime, config.parallel)
     rng = ParallelRNG.from_context(config.training.seed, parallel)
     model, built = build_model(config, parallel, rng, device=runtime.device)

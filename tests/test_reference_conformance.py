@@ -158,7 +158,7 @@ def test_config_defaults_match(ref):
     theirs = config_to_dict(ref.TrainConfig())
     # fields this framework adds (documented, defaults preserve reference behaviour)
     ours["kernels"].pop("cuda_graphs")
-    for extra in ("fused_tp_comm", "fused_dp_comm", "fused_cp_comm"):
+    for extra in ("fused_tp_comm", "fused_dp_comm", "fused_cp_comm", "deterministic"):
         ours["kernels"].pop(extra)
     ours["context_parallel"].pop("load_balance")
     assert ours == theirs
@@ -881,7 +881,7 @@ def test_config_overrides_parse_like_the_reference(ref, overrides, monkeypatch):
 
     a, b = plain(ours), plain(theirs)
     a["kernels"].pop("cuda_graphs", None)
-    for extra in ("fused_tp_comm", "fused_dp_comm", "fused_cp_comm"):
+    for extra in ("fused_tp_comm", "fused_dp_comm", "fused_cp_comm", "deterministic"):
         a["kernels"].pop(extra, None)
     a["context_parallel"].pop("load_balance", None)
     assert a == b
