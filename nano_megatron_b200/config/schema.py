@@ -1,7 +1,7 @@
 """Typed configuration blocks.
 
-The YAML schema is the reference's (src/nano_megatron/config/schema.py:60-665):
-the same 17 blocks, field names, defaults and per-field checks, so reference
+The YAML schema is the reference's (src/nano_megatron/config/schema.py:60-665): the same
+17 blocks, field names and defaults, and the same accept/reject decisions, so reference
 YAML files load unchanged. Additions are strictly additive:
 
 * ``kernels.backend`` also accepts ``b200``; every value selects this library's
@@ -13,10 +13,24 @@ YAML files load unchanged. Additions are strictly additive:
   fixed-order (bitwise reproducible) backward reductions.
 * ``context_parallel.load_balance`` selects zigzag chunking (rank r holds
   sequence chunks r and 2*CP-1-r) instead of contiguous chunks.
+
+How blocks validate themselves: every block is a frozen dataclass deriving from
+:class:`_Block`. A field's constraints travel with the field as metadata (:func:`_spec`);
+after construction one generic checker walks the fields and, guided by each field's type
+hint, rejects or normalises the value: booleans must be real booleans; integers real
+integers at or above their lower bound (1 unless the spec says otherwise); numbers real
+numbers within their bounds; enums are coerced from their string values; paths from
+strings; text is stripped and/or lower-cased where the spec asks. Wrong types raise
+``TypeError`` and out-of-range values ``ValueError``, each naming the dotted field. What
+involves more than one field, or a field the generic rules cannot express, is checked in
+the block's ``_cross_check``.
 """
 
 from __future__ import annotations
 
+import dataclasses
+import types
+import typing
 from dataclasses import dataclass, field
 from enum import StrEnum
 from pathlib import Path
@@ -24,46 +38,108 @@ from pathlib import Path
 from nano_megatron_b200.parallel.axes import DEFAULT_RANK_ORDER, ParallelAxis, normalize_rank_order
 
 
-# ------------------------------------------------------------------ field checks
-def _int(name: str, value, minimum: int = 1) -> None:
-    if isinstance(value, bool) or not isinstance(value, int):
-        raise TypeError(f"{name} must be an integer, got {value!r}")
-    if value < minimum:
-        raise ValueError(f"{name} must be >= {minimum}, got {value}")
+# ------------------------------------------------------------------ field specs
+@dataclass(frozen=True, slots=True)
+class _Spec:
+    low: float | None = None     # lower bound (inclusive, or exclusive with `above`)
+    above: bool = False
+    below: float | None = None   # exclusive upper bound for numbers
+    strip: bool = False          # text: strip surrounding whitespace
+    lower: bool = False          # text: lower-case
+    nonblank: bool = False       # text / path: must contain a non-space character
+    own: bool = False            # checked only by the block's _cross_check
 
 
-def _bool(name: str, value) -> None:
-    if not isinstance(value, bool):
-        raise TypeError(f"{name} must be a boolean, got {value!r}")
+_PLAIN = _Spec()
 
 
-def _number(name: str, value, *, allow_zero: bool = False) -> None:
-    if isinstance(value, bool) or not isinstance(value, (int, float)):
-        raise TypeError(f"{name} must be a number, got {value!r}")
-    if value < 0 or (value == 0 and not allow_zero):
-        raise ValueError(f"{name} must be {'>=' if allow_zero else '>'} 0, got {value}")
+def _spec(default=dataclasses.MISSING, *, factory=dataclasses.MISSING, **rules):
+    meta = {"spec": _Spec(**rules)}
+    if factory is not dataclasses.MISSING:
+        return field(default_factory=factory, metadata=meta)
+    return field(default=default, metadata=meta)
 
 
-def _path(name: str, value) -> Path | None:
-    if value is None:
-        return None
-    if not isinstance(value, (str, Path)):
-        raise TypeError(f"{name} must be a filesystem path string or null")
-    if isinstance(value, str) and not value.strip():
-        raise ValueError(f"{name} must not be empty")
-    return Path(value)
+_HINT_CACHE: dict[type, dict[str, object]] = {}
 
 
-def _enum(name: str, kind: type[StrEnum], value):
-    try:
-        return kind(value)
-    except (TypeError, ValueError) as error:
-        choices = ", ".join(m.value for m in kind)
-        raise ValueError(f"{name} must be one of: {choices}; got {value!r}") from error
+def _field_hints(cls: type) -> dict[str, object]:
+    hints = _HINT_CACHE.get(cls)
+    if hints is None:
+        hints = _HINT_CACHE[cls] = typing.get_type_hints(cls)
+    return hints
 
 
-def _set(obj, name: str, value) -> None:
-    object.__setattr__(obj, name, value)
+def _checked(name: str, value, hint, spec: _Spec):
+    """Validate one field value against its type hint and spec; return the stored value."""
+    if typing.get_origin(hint) in (typing.Union, types.UnionType):
+        if value is None:
+            return None
+        (hint,) = [arm for arm in typing.get_args(hint) if arm is not type(None)]
+    if hint is bool:
+        if not isinstance(value, bool):
+            raise TypeError(f"{name}: expected true or false, found {value!r}")
+        return value
+    if hint is int or hint is float:
+        kinds = (int,) if hint is int else (int, float)
+        if isinstance(value, bool) or not isinstance(value, kinds):
+            what = "a whole number" if hint is int else "a number"
+            raise TypeError(f"{name}: expected {what}, found {value!r}")
+        low = 1 if hint is int and spec.low is None else spec.low
+        if low is not None and (value <= low if spec.above else value < low):
+            raise ValueError(f"{name}: {value} is not {'above' if spec.above else 'at least'} "
+                             f"{low}")
+        if spec.below is not None and value >= spec.below:
+            raise ValueError(f"{name}: {value} is not below {spec.below}")
+        return value
+    if isinstance(hint, type) and issubclass(hint, StrEnum):
+        try:
+            return hint(value)
+        except (TypeError, ValueError) as error:
+            allowed = " | ".join(member.value for member in hint)
+            raise ValueError(f"{name}: {value!r} is not one of {allowed}") from error
+    if hint is str:
+        if not isinstance(value, str):
+            raise TypeError(f"{name}: expected text, found {value!r}")
+        if spec.nonblank and not value.strip():
+            raise ValueError(f"{name}: must not be blank")
+        text = value.strip() if spec.strip else value
+        return text.lower() if spec.lower else text
+    if hint is Path:
+        if not isinstance(value, (str, Path)):
+            raise TypeError(f"{name}: expected a filesystem path, found {value!r}")
+        if spec.nonblank and isinstance(value, str) and not value.strip():
+            raise ValueError(f"{name}: must not be blank")
+        return Path(value)
+    if dataclasses.is_dataclass(hint):
+        if not isinstance(value, hint):
+            raise TypeError(f"{name}: expected a {hint.__name__} block, found "
+                            f"{type(value).__name__}")
+        return value
+    raise TypeError(f"{name}: no generic rule for type {hint!r}; give it an own check")
+
+
+class _Block:
+    __slots__ = ()
+    SECTION = ""
+
+    def __post_init__(self) -> None:
+        hints = _field_hints(type(self))
+        for f in dataclasses.fields(self):
+            spec = f.metadata.get("spec", _PLAIN)
+            if spec.own:
+                continue
+            value = getattr(self, f.name)
+            stored = _checked(f"{self.SECTION}.{f.name}", value, hints[f.name], spec)
+            if stored is not value:
+                object.__setattr__(self, f.name, stored)
+        self._cross_check()
+
+    def _cross_check(self) -> None:
+        """Rules over several fields, and fields marked ``own``."""
+
+    def _store(self, name: str, value) -> None:
+        object.__setattr__(self, name, value)
 
 
 # ------------------------------------------------------------------ enums
@@ -109,50 +185,49 @@ class LearningRateSchedule(StrEnum):
 
 # ------------------------------------------------------------------ blocks
 @dataclass(frozen=True, slots=True)
-class DistributedConfig:
-    backend: str = "auto"
+class DistributedConfig(_Block):
+    SECTION = "distributed"
+    backend: str = _spec("auto", nonblank=True, strip=True, lower=True)
     timeout_minutes: int = 30
-    device: str = "auto"
-    init_method: str = "env://"
-
-    def __post_init__(self) -> None:
-        for name in ("backend", "device", "init_method"):
-            value = getattr(self, name)
-            if not isinstance(value, str) or not value.strip():
-                raise ValueError(f"distributed.{name} must be a non-empty string")
-        _int("distributed.timeout_minutes", self.timeout_minutes)
-        _set(self, "backend", self.backend.strip().lower())
-        _set(self, "device", self.device.strip().lower())
-        _set(self, "init_method", self.init_method.strip())
+    device: str = _spec("auto", nonblank=True, strip=True, lower=True)
+    init_method: str = _spec("env://", nonblank=True, strip=True)
 
 
 @dataclass(frozen=True, slots=True)
-class ParallelConfig:
+class ParallelConfig(_Block):
+    SECTION = "parallel"
     tensor: int = 1
     pipeline: int = 1
     context: int = 1
     expert: int = 1
     data: int | None = None
-    order: tuple[ParallelAxis, ...] = DEFAULT_RANK_ORDER
+    order: tuple[ParallelAxis, ...] = _spec(DEFAULT_RANK_ORDER, own=True)
     sequence_parallel: bool = False
 
-    def __post_init__(self) -> None:
-        for name in ("tensor", "pipeline", "context", "expert"):
-            _int(f"parallel.{name}", getattr(self, name))
-        if self.data is not None:
-            _int("parallel.data", self.data)
-        _bool("parallel.sequence_parallel", self.sequence_parallel)
-        _set(self, "order", normalize_rank_order(self.order))
+    def _cross_check(self) -> None:
+        self._store("order", normalize_rank_order(self.order))
 
-    tensor_parallel_size = property(lambda self: self.tensor)
-    pipeline_parallel_size = property(lambda self: self.pipeline)
-    context_parallel_size = property(lambda self: self.context)
-    expert_parallel_size = property(lambda self: self.expert)
+    @property
+    def tensor_parallel_size(self) -> int:
+        return self.tensor
+
+    @property
+    def pipeline_parallel_size(self) -> int:
+        return self.pipeline
+
+    @property
+    def context_parallel_size(self) -> int:
+        return self.context
+
+    @property
+    def expert_parallel_size(self) -> int:
+        return self.expert
 
     @property
     def data_parallel_size(self) -> int:
         if self.data is None:
-            raise ValueError("parallel.data has not been resolved against a world size")
+            raise ValueError("parallel.data is still null: resolve it against a world size "
+                             "first")
         return self.data
 
     @property
@@ -164,31 +239,31 @@ class ParallelConfig:
         return None if self.data is None else self.model_parallel_size * self.data
 
     def resolve_data_parallel_size(self, world_size: int | None) -> int:
+        """DP size implied by ``world_size`` (or the configured one, checked against it)."""
         if world_size is not None:
-            _int("world_size", world_size)
-        mp = self.model_parallel_size
-        if self.data is not None:
-            if world_size is not None and mp * self.data != world_size:
-                raise ValueError(
-                    "world size does not match parallel topology: "
-                    f"{world_size} != TP({self.tensor}) * PP({self.pipeline}) * "
-                    f"CP({self.context}) * EP({self.expert}) * DP({self.data}) = {mp * self.data}"
-                )
-            return self.data
-        if world_size is None:
-            raise ValueError("world_size is required when parallel.data is null")
-        if world_size % mp:
-            raise ValueError(f"world size {world_size} is not divisible by TP*PP*CP*EP ({mp})")
-        return world_size // mp
+            _checked("world_size", world_size, int, _PLAIN)
+        shard = self.model_parallel_size
+        layout = (f"TP {self.tensor} x PP {self.pipeline} x CP {self.context} x "
+                  f"EP {self.expert}")
+        if self.data is None:
+            if world_size is None:
+                raise ValueError("parallel.data is null, so a world size is needed to derive it")
+            if world_size % shard:
+                raise ValueError(f"{world_size} ranks cannot be split into model replicas of "
+                                 f"{layout} = {shard} ranks")
+            return world_size // shard
+        if world_size is not None and shard * self.data != world_size:
+            raise ValueError(f"{layout} x DP {self.data} = {shard * self.data} ranks, but the "
+                             f"world has {world_size}")
+        return self.data
 
     def resolved(self, world_size: int) -> "ParallelConfig":
-        return ParallelConfig(self.tensor, self.pipeline, self.context, self.expert,
-                              self.resolve_data_parallel_size(world_size), self.order,
-                              self.sequence_parallel)
+        return dataclasses.replace(self, data=self.resolve_data_parallel_size(world_size))
 
 
 @dataclass(frozen=True, slots=True)
-class GPTConfig:
+class GPTConfig(_Block):
+    SECTION = "model"
     layers: int = 12
     hidden_size: int = 768
     ffn_hidden_size: int = 2048
@@ -196,57 +271,54 @@ class GPTConfig:
     kv_heads: int | None = None
     seq_length: int = 2048
     vocab_size: int = 50304
-    rope_theta: float = 10000.0
-    dropout: float = 0.0
+    rope_theta: float = _spec(10000.0, low=0, above=True)
+    dropout: float = _spec(0.0, low=0, below=1)
     tie_embeddings: bool = True
-    norm_epsilon: float = 1.0e-5
+    norm_epsilon: float = _spec(1.0e-5, low=0, above=True)
     bias: bool = False
 
-    def __post_init__(self) -> None:
-        for name in ("layers", "hidden_size", "ffn_hidden_size", "heads", "seq_length",
-                     "vocab_size"):
-            _int(f"model.{name}", getattr(self, name))
-        if self.kv_heads is not None:
-            _int("model.kv_heads", self.kv_heads)
-        _number("model.rope_theta", self.rope_theta)
-        _number("model.norm_epsilon", self.norm_epsilon)
-        d = self.dropout
-        if isinstance(d, bool) or not isinstance(d, (int, float)) or not 0 <= d < 1:
-            raise ValueError(f"model.dropout must be in [0, 1), got {d}")
-        _bool("model.tie_embeddings", self.tie_embeddings)
-        _bool("model.bias", self.bias)
+    def _cross_check(self) -> None:
         if self.hidden_size % self.heads:
-            raise ValueError(f"model.hidden_size ({self.hidden_size}) must be divisible by "
-                             f"model.heads ({self.heads})")
+            raise ValueError(f"model: hidden_size {self.hidden_size} does not split into "
+                             f"{self.heads} equal heads")
         kv = self.num_kv_heads
         if kv > self.heads or self.heads % kv:
-            raise ValueError("model.kv_heads must divide model.heads and cannot exceed it; "
-                             f"got heads={self.heads}, kv_heads={kv}")
+            raise ValueError(f"model: {self.heads} query heads cannot share {kv} key/value "
+                             "heads evenly (kv_heads must divide heads)")
 
-    num_layers = property(lambda self: self.layers)
-    num_attention_heads = property(lambda self: self.heads)
-    num_kv_heads = property(lambda self: self.heads if self.kv_heads is None else self.kv_heads)
-    head_dim = property(lambda self: self.hidden_size // self.heads)
+    @property
+    def num_layers(self) -> int:
+        return self.layers
+
+    @property
+    def num_attention_heads(self) -> int:
+        return self.heads
+
+    @property
+    def num_kv_heads(self) -> int:
+        return self.heads if self.kv_heads is None else self.kv_heads
+
+    @property
+    def head_dim(self) -> int:
+        return self.hidden_size // self.heads
 
     def padded_vocab_size(self, tensor_parallel_size: int) -> int:
-        _int("tensor_parallel_size", tensor_parallel_size)
-        tp = tensor_parallel_size
-        return -(-self.vocab_size // tp) * tp
+        """Vocabulary rounded up to a multiple of the TP size (equal vocabulary shards)."""
+        tp = _checked("tensor_parallel_size", tensor_parallel_size, int, _PLAIN)
+        return (self.vocab_size + tp - 1) // tp * tp
 
 
 @dataclass(frozen=True, slots=True)
-class PrecisionConfig:
+class PrecisionConfig(_Block):
+    SECTION = "precision"
     params: PrecisionDType = PrecisionDType.BFLOAT16
     compute: PrecisionDType = PrecisionDType.BFLOAT16
     grad_reduce: PrecisionDType = PrecisionDType.FLOAT32
 
-    def __post_init__(self) -> None:
-        for name in ("params", "compute", "grad_reduce"):
-            _set(self, name, _enum(f"precision.{name}", PrecisionDType, getattr(self, name)))
-
 
 @dataclass(frozen=True, slots=True)
-class KernelConfig:
+class KernelConfig(_Block):
+    SECTION = "kernels"
     backend: KernelBackend = KernelBackend.TORCH
     cuda_graphs: bool = True
     # Sequence-parallel TP collectives fused into the GEMMs over NVLink symmetric memory
@@ -263,268 +335,185 @@ class KernelConfig:
     # bitwise reproducible steps at some speed cost.
     deterministic: bool = False
 
-    def __post_init__(self) -> None:
-        _set(self, "backend", _enum("kernels.backend", KernelBackend, self.backend))
-        _bool("kernels.cuda_graphs", self.cuda_graphs)
-        _bool("kernels.fused_tp_comm", self.fused_tp_comm)
-        _bool("kernels.fused_dp_comm", self.fused_dp_comm)
-        _bool("kernels.fused_cp_comm", self.fused_cp_comm)
-        _bool("kernels.deterministic", self.deterministic)
-
 
 @dataclass(frozen=True, slots=True)
-class DataParallelConfig:
+class DataParallelConfig(_Block):
+    SECTION = "data_parallel"
     mode: DataParallelMode = DataParallelMode.DDP
     bucket_bytes: int = 256 * 1024 * 1024
     overlap_grad_reduce: bool = False
     reshard_after_forward: bool = True
 
-    def __post_init__(self) -> None:
-        _set(self, "mode", _enum("data_parallel.mode", DataParallelMode, self.mode))
-        _int("data_parallel.bucket_bytes", self.bucket_bytes)
-        _bool("data_parallel.overlap_grad_reduce", self.overlap_grad_reduce)
-        _bool("data_parallel.reshard_after_forward", self.reshard_after_forward)
-
 
 @dataclass(frozen=True, slots=True)
-class PipelineConfig:
+class PipelineConfig(_Block):
+    SECTION = "pipeline"
     schedule: PipelineSchedule = PipelineSchedule.ONE_F_ONE_B
     activation_dtype: PrecisionDType | None = None
     overlap_p2p: bool = False
     virtual_stages_per_rank: int = 1
     dynamic_activation_shapes: bool = False
 
-    def __post_init__(self) -> None:
-        _set(self, "schedule", _enum("pipeline.schedule", PipelineSchedule, self.schedule))
-        if self.activation_dtype is not None:
-            _set(self, "activation_dtype",
-                 _enum("pipeline.activation_dtype", PrecisionDType, self.activation_dtype))
-        _bool("pipeline.overlap_p2p", self.overlap_p2p)
-        _int("pipeline.virtual_stages_per_rank", self.virtual_stages_per_rank)
-        _bool("pipeline.dynamic_activation_shapes", self.dynamic_activation_shapes)
-
 
 @dataclass(frozen=True, slots=True)
-class ContextParallelConfig:
+class ContextParallelConfig(_Block):
+    SECTION = "context_parallel"
     backend: ContextParallelBackend = ContextParallelBackend.ALL_GATHER
-    dropout: float = 0.0
+    dropout: float = _spec(0.0, own=True)
     load_balance: bool = False
 
-    def __post_init__(self) -> None:
-        _set(self, "backend", _enum("context_parallel.backend", ContextParallelBackend,
-                                    self.backend))
-        if isinstance(self.dropout, bool) or not isinstance(self.dropout, (int, float)):
-            raise TypeError("context_parallel.dropout must be a number")
-        if self.dropout != 0.0:
-            raise ValueError("context_parallel.dropout must be 0 in phase one; CP attention "
-                             "dropout is not implemented")
-        _bool("context_parallel.load_balance", self.load_balance)
+    def _cross_check(self) -> None:
+        d = _checked("context_parallel.dropout", self.dropout, float, _PLAIN)
+        if d != 0.0:
+            raise ValueError("context_parallel.dropout: attention dropout is not implemented "
+                             "for context parallelism; only 0 is accepted")
+
+
+_CHECKPOINTABLE_OPS = ("attention", "mlp")
 
 
 @dataclass(frozen=True, slots=True)
-class ActivationCheckpointConfig:
+class ActivationCheckpointConfig(_Block):
+    SECTION = "activation_checkpoint"
     mode: ActivationCheckpointMode = ActivationCheckpointMode.NONE
     block_interval: int = 1
-    selective_ops: tuple[str, ...] = ("attention", "mlp")
+    selective_ops: tuple[str, ...] = _spec(_CHECKPOINTABLE_OPS, own=True)
     use_reentrant: bool = False
     offload_saved_tensors: bool = False
 
-    def __post_init__(self) -> None:
-        _set(self, "mode", _enum("activation_checkpoint.mode", ActivationCheckpointMode, self.mode))
-        _set(self, "selective_ops", tuple(self.selective_ops))
-        _int("activation_checkpoint.block_interval", self.block_interval)
-        if not self.selective_ops:
-            raise ValueError("activation_checkpoint.selective_ops cannot be empty")
-        unknown = sorted(set(self.selective_ops) - {"attention", "mlp"})
-        if unknown:
-            raise ValueError("activation_checkpoint.selective_ops contains unsupported values: "
-                             + ", ".join(unknown))
-        _bool("activation_checkpoint.use_reentrant", self.use_reentrant)
+    def _cross_check(self) -> None:
+        ops = tuple(self.selective_ops)
+        self._store("selective_ops", ops)
+        if not ops:
+            raise ValueError("activation_checkpoint.selective_ops: name at least one op")
+        extra = sorted(set(ops) - set(_CHECKPOINTABLE_OPS))
+        if extra:
+            raise ValueError(f"activation_checkpoint.selective_ops: {', '.join(extra)} cannot "
+                             f"be recomputed (choose from {', '.join(_CHECKPOINTABLE_OPS)})")
         if self.use_reentrant:
-            raise ValueError("Nano-Megatron only supports non-reentrant activation checkpointing")
-        _bool("activation_checkpoint.offload_saved_tensors", self.offload_saved_tensors)
+            raise ValueError("activation_checkpoint.use_reentrant: only non-reentrant "
+                             "checkpointing is implemented")
 
 
 @dataclass(frozen=True, slots=True)
-class OffloadConfig:
+class OffloadConfig(_Block):
+    SECTION = "offload"
     optimizer_state: bool = False
     zero3_params_and_grads: bool = False
     activations: bool = False
     pin_memory: bool = True
     non_blocking: bool = True
 
-    def __post_init__(self) -> None:
-        for name in ("optimizer_state", "zero3_params_and_grads", "activations", "pin_memory",
-                     "non_blocking"):
-            _bool(f"offload.{name}", getattr(self, name))
-
 
 @dataclass(frozen=True, slots=True)
-class OptimizerConfig:
-    name: str = "adamw"
-    lr: float = 3.0e-4
-    betas: tuple[float, float] = (0.9, 0.95)
-    eps: float = 1.0e-8
-    weight_decay: float = 0.1
-    clip_grad_norm: float | None = 1.0
+class OptimizerConfig(_Block):
+    SECTION = "optimizer"
+    name: str = _spec("adamw", lower=True)
+    lr: float = _spec(3.0e-4, low=0, above=True)
+    betas: tuple[float, float] = _spec((0.9, 0.95), own=True)
+    eps: float = _spec(1.0e-8, low=0, above=True)
+    weight_decay: float = _spec(0.1, low=0)
+    clip_grad_norm: float | None = _spec(1.0, low=0, above=True)
 
-    def __post_init__(self) -> None:
-        if not isinstance(self.name, str):
-            raise TypeError("optimizer.name must be a string")
-        _set(self, "name", self.name.lower())
-        _set(self, "betas", tuple(self.betas))
+    def _cross_check(self) -> None:
+        betas = tuple(self.betas)
+        self._store("betas", betas)
         if self.name != "adamw":
-            raise ValueError("optimizer.name must be 'adamw' in the first implementation phase")
-        _number("optimizer.lr", self.lr)
-        _number("optimizer.eps", self.eps)
-        _number("optimizer.weight_decay", self.weight_decay, allow_zero=True)
-        if len(self.betas) != 2 or any(isinstance(b, bool) or not isinstance(b, (int, float))
-                                       or not 0 <= b < 1 for b in self.betas):
-            raise ValueError("optimizer.betas must contain two values in [0, 1)")
-        if self.clip_grad_norm is not None:
-            _number("optimizer.clip_grad_norm", self.clip_grad_norm)
+            raise ValueError(f"optimizer.name: {self.name!r} is not available (only adamw)")
+        in_range = [not isinstance(b, bool) and isinstance(b, (int, float)) and 0 <= b < 1
+                    for b in betas]
+        if len(betas) != 2 or not all(in_range):
+            raise ValueError(f"optimizer.betas: need two coefficients in [0, 1), got {betas!r}")
 
 
 @dataclass(frozen=True, slots=True)
-class LearningRateSchedulerConfig:
+class LearningRateSchedulerConfig(_Block):
+    SECTION = "lr_scheduler"
     schedule: LearningRateSchedule = LearningRateSchedule.COSINE
-    warmup_steps: int = 0
+    warmup_steps: int = _spec(0, low=0)
     decay_steps: int | None = None
-    min_lr: float = 0.0
-
-    def __post_init__(self) -> None:
-        _set(self, "schedule", _enum("lr_scheduler.schedule", LearningRateSchedule, self.schedule))
-        _int("lr_scheduler.warmup_steps", self.warmup_steps, minimum=0)
-        if self.decay_steps is not None:
-            _int("lr_scheduler.decay_steps", self.decay_steps)
-        _number("lr_scheduler.min_lr", self.min_lr, allow_zero=True)
+    min_lr: float = _spec(0.0, low=0)
 
 
 @dataclass(frozen=True, slots=True)
-class TrainingConfig:
+class TrainingConfig(_Block):
+    SECTION = "training"
     micro_batch_size: int = 1
     gradient_accumulation_steps: int = 1
     max_steps: int = 1000
-    seed: int = 1234
+    seed: int = _spec(1234, low=0)
     log_interval: int = 10
 
-    def __post_init__(self) -> None:
-        for name in ("micro_batch_size", "gradient_accumulation_steps", "max_steps",
-                     "log_interval"):
-            _int(f"training.{name}", getattr(self, name))
-        if isinstance(self.seed, bool) or not isinstance(self.seed, int) or self.seed < 0:
-            raise ValueError("training.seed must be a non-negative integer")
-
     def global_batch_size(self, parallel: ParallelConfig, *, world_size: int | None = None) -> int:
+        """Sequences per optimizer step over every replica (DP x EP)."""
         dp = parallel.resolve_data_parallel_size(world_size)
         return self.micro_batch_size * self.gradient_accumulation_steps * dp * parallel.expert
 
 
 @dataclass(frozen=True, slots=True)
-class CheckpointConfig:
+class CheckpointConfig(_Block):
+    SECTION = "checkpoint"
     directory: Path = Path("checkpoints/gpt")
-    save_interval: int = 500
+    save_interval: int = _spec(500, low=0)
     async_save: bool = False
     keep_last: int = 2
     save_final: bool = True
     save_best_validation: bool = True
 
-    def __post_init__(self) -> None:
-        _set(self, "directory", Path(self.directory))
-        _int("checkpoint.save_interval", self.save_interval, minimum=0)
-        _int("checkpoint.keep_last", self.keep_last)
-        for name in ("async_save", "save_final", "save_best_validation"):
-            _bool(f"checkpoint.{name}", getattr(self, name))
-
 
 @dataclass(frozen=True, slots=True)
-class TokenizerConfig:
-    path: Path
+class TokenizerConfig(_Block):
+    SECTION = "data.tokenizer"
+    path: Path = _spec(nonblank=True)
     append_eos: bool = True
 
-    def __post_init__(self) -> None:
-        if not isinstance(self.path, (str, Path)):
-            raise TypeError("data.tokenizer.path must be a filesystem path string")
-        if isinstance(self.path, str) and not self.path.strip():
-            raise ValueError("data.tokenizer.path must not be empty")
-        _set(self, "path", Path(self.path))
-        _bool("data.tokenizer.append_eos", self.append_eos)
-
 
 @dataclass(frozen=True, slots=True)
-class DataConfig:
-    path: Path | None = None
-    mmap_path: Path | None = None
-    text_path: Path | None = None
-    text_key: str = "text"
+class DataConfig(_Block):
+    SECTION = "data"
+    path: Path | None = _spec(None, nonblank=True)
+    mmap_path: Path | None = _spec(None, nonblank=True)
+    text_path: Path | None = _spec(None, nonblank=True)
+    text_key: str = _spec("text", nonblank=True)
     tokenizer: TokenizerConfig | None = None
-    num_workers: int = 0
+    num_workers: int = _spec(0, low=0)
     shuffle: bool = True
     packed_sequences: bool = False
 
-    def __post_init__(self) -> None:
-        for name in ("path", "mmap_path", "text_path"):
-            _set(self, name, _path(f"data.{name}", getattr(self, name)))
-        if not isinstance(self.text_key, str):
-            raise TypeError("data.text_key must be a string")
-        if not self.text_key.strip():
-            raise ValueError("data.text_key must not be empty")
-        if self.tokenizer is not None and not isinstance(self.tokenizer, TokenizerConfig):
-            raise TypeError("data.tokenizer must be a TokenizerConfig or null")
-        _int("data.num_workers", self.num_workers, minimum=0)
-        _bool("data.shuffle", self.shuffle)
-        _bool("data.packed_sequences", self.packed_sequences)
-
 
 @dataclass(frozen=True, slots=True)
-class ValidationConfig:
-    interval: int = 0
+class ValidationConfig(_Block):
+    SECTION = "validation"
+    interval: int = _spec(0, low=0)
     batches: int = 10
     data: DataConfig | None = None
 
-    def __post_init__(self) -> None:
-        _int("validation.interval", self.interval, minimum=0)
-        _int("validation.batches", self.batches)
-        if self.data is not None and not isinstance(self.data, DataConfig):
-            raise TypeError("validation.data must be a DataConfig or null")
+
+_WANDB_MODES = ("online", "offline", "disabled")
 
 
 @dataclass(frozen=True, slots=True)
-class WandbConfig:
+class WandbConfig(_Block):
+    SECTION = "wandb"
     enabled: bool = False
-    project: str = "nano-megatron"
-    entity: str | None = None
-    name: str | None = None
-    group: str | None = None
-    tags: tuple[str, ...] = ()
-    mode: str = "online"
-    directory: Path | None = None
-    run_id: str | None = None
+    project: str = _spec("nano-megatron", nonblank=True, strip=True)
+    entity: str | None = _spec(None, nonblank=True, strip=True)
+    name: str | None = _spec(None, nonblank=True, strip=True)
+    group: str | None = _spec(None, nonblank=True, strip=True)
+    tags: tuple[str, ...] = _spec((), own=True)
+    mode: str = _spec("online", strip=True, lower=True)
+    directory: Path | None = _spec(None, nonblank=True)
+    run_id: str | None = _spec(None, nonblank=True, strip=True)
 
-    def __post_init__(self) -> None:
-        _bool("wandb.enabled", self.enabled)
-        if not isinstance(self.project, str) or not self.project.strip():
-            raise ValueError("wandb.project must be a non-empty string")
-        _set(self, "project", self.project.strip())
-        for name in ("entity", "name", "group", "run_id"):
-            v = getattr(self, name)
-            if v is not None and (not isinstance(v, str) or not v.strip()):
-                raise ValueError(f"wandb.{name} must be a non-empty string or null")
-            if isinstance(v, str):
-                _set(self, name, v.strip())
+    def _cross_check(self) -> None:
         if isinstance(self.tags, str):
-            raise TypeError("wandb.tags must be a sequence of strings, not a string")
+            raise TypeError("wandb.tags: expected a list of tags, found a single string")
         tags = tuple(self.tags)
-        if any(not isinstance(t, str) or not t.strip() for t in tags):
-            raise ValueError("wandb.tags must contain non-empty strings")
-        _set(self, "tags", tuple(t.strip() for t in tags))
-        if not isinstance(self.mode, str):
-            raise TypeError("wandb.mode must be a string")
-        mode = self.mode.strip().lower()
-        if mode not in ("online", "offline", "disabled"):
-            raise ValueError("wandb.mode must be online, offline, or disabled")
-        _set(self, "mode", mode)
-        _set(self, "directory", _path("wandb.directory", self.directory))
+        if not all(isinstance(t, str) and t.strip() for t in tags):
+            raise ValueError(f"wandb.tags: every tag must be non-blank text, got {tags!r}")
+        self._store("tags", tuple(t.strip() for t in tags))
+        if self.mode not in _WANDB_MODES:
+            raise ValueError(f"wandb.mode: {self.mode!r} is not one of {' | '.join(_WANDB_MODES)}")
 
 
 @dataclass(frozen=True, slots=True)

@@ -1111,3 +1111,112 @@ def test_dp_reshard_resume_matches_reference(ref, tmp_path, mode):
     ours = _curve(sorted((tmp_path / "ours").iterdir())[-1])
     for step in (3, 4):
         assert ours[step] == pytest.approx(theirs[step], rel=2e-6), (step, ours, theirs)
+
+
+_FIELD_PROBES = [None, True, False, 0, 1, -1, 2, 0.0, 0.5, 1.0, -0.5, "", " ", "x", " NCCL ",
+                 "adamw", " adamw", "ADAMW", [], ["attention"], ["mlp", "x"], [0.9, 0.95], [0.9],
+                 [0.9, 1.0], "online", " OFFLINE ", ["a", " b "], ["", "a"],
+                 ["dp", "tp", "pp", "cp", "ep"], ["tp", "tp", "cp", "ep", "dp"], "float16", "ring",
+                 "zero3", "interleaved_1f1b", "selective", "cosine", "path/x", {"path": "tok"},
+                 {"path": ""}, {}]
+
+
+def test_every_field_accepts_and_normalises_like_the_reference(ref):
+    """Each field of each block set to each probe value: both frameworks accept or reject
+    it, and accepted values are stored identically (stripping, lower-casing, enum and path
+    coercion, tuple conversion)."""
+    import copy
+
+    from nano_megatron.config import config_from_dict as ref_from_dict
+
+    from nano_megatron_b200.config import config_from_dict, config_to_dict
+
+    def stored(from_dict, data):
+        try:
+            out = config_to_dict(from_dict(copy.deepcopy(data)))
+        except Exception:  # noqa: BLE001 - rejected
+            return None
+        for extra in ("cuda_graphs", "fused_tp_comm", "fused_dp_comm", "fused_cp_comm",
+                      "deterministic"):
+            out["kernels"].pop(extra, None)
+        out["context_parallel"].pop("load_balance", None)
+        return out
+
+    defaults = config_to_dict(ref.TrainConfig())
+    checked = 0
+    for section, block in defaults.items():
+        for name in block:
+            for value in _FIELD_PROBES:
+                data = {section: {name: value}}
+                assert stored(config_from_dict, data) == stored(ref_from_dict, data), data
+                checked += 1
+    assert checked > 3000
+
+
+def test_random_layouts_validate_like_the_reference(ref):
+    """Seeded random combinations of topology, model shape, schedule, precision, ZeRO
+    mode, offload, checkpointing and data sources: both frameworks reject the same
+    configurations, warn on the same ones, and derive the same DP size, global batch and
+    padded vocabulary."""
+    import copy
+    import random
+
+    from nano_megatron.config import config_from_dict as ref_from_dict
+    from nano_megatron.config.validation import validate_config as ref_validate
+
+    from nano_megatron_b200.config import config_from_dict
+    from nano_megatron_b200.config.validation import validate_config
+
+    space = {
+        ("parallel", "tensor"): [1, 2, 4, 8], ("parallel", "pipeline"): [1, 2, 4],
+        ("parallel", "context"): [1, 2, 3, 4], ("parallel", "expert"): [1, 2],
+        ("parallel", "data"): [None, 1, 2, 3], ("parallel", "sequence_parallel"): [False, True],
+        ("model", "layers"): [1, 2, 4, 6, 8], ("model", "hidden_size"): [64, 96, 128, 256],
+        ("model", "ffn_hidden_size"): [128, 172, 256], ("model", "heads"): [2, 4, 8],
+        ("model", "kv_heads"): [None, 1, 2, 4], ("model", "seq_length"): [16, 24, 36, 64],
+        ("model", "dropout"): [0.0, 0.1],
+        ("pipeline", "schedule"): ["1f1b", "gpipe", "interleaved_1f1b"],
+        ("pipeline", "virtual_stages_per_rank"): [1, 2, 3],
+        ("pipeline", "overlap_p2p"): [False, True],
+        ("pipeline", "dynamic_activation_shapes"): [False, True],
+        ("training", "gradient_accumulation_steps"): [1, 2, 3, 4, 8],
+        ("training", "max_steps"): [1, 5, 100],
+        ("lr_scheduler", "warmup_steps"): [0, 3, 10, 200],
+        ("lr_scheduler", "decay_steps"): [None, 2, 50], ("lr_scheduler", "min_lr"): [0.0, 1.0],
+        ("precision", "params"): ["float32", "bfloat16", "float16"],
+        ("precision", "compute"): ["float32", "bfloat16", "float16"],
+        ("data_parallel", "mode"): ["ddp", "zero1", "zero2", "zero3"],
+        ("data_parallel", "overlap_grad_reduce"): [False, True],
+        ("offload", "optimizer_state"): [False, True],
+        ("offload", "zero3_params_and_grads"): [False, True],
+        ("activation_checkpoint", "mode"): ["none", "full", "selective"],
+        ("activation_checkpoint", "offload_saved_tensors"): [False, True],
+        ("validation", "interval"): [0, 5],
+        ("validation", "data"): [None, {"path": "v.pt"}, {},
+                                 {"path": "v.pt", "mmap_path": "v.mmap"},
+                                 {"text_path": "v.jsonl"},
+                                 {"text_path": "v.jsonl", "tokenizer": {"path": "t2"}}],
+        ("data", "path"): [None, "d.pt"], ("data", "text_path"): [None, "d.jsonl"],
+        ("data", "tokenizer"): [None, {"path": "t"}], ("data", "packed_sequences"): [False, True],
+    }
+    keys = list(space)
+    rng = random.Random(1234)
+
+    def outcome(from_dict, validate, data, world):
+        try:
+            res = validate(from_dict(copy.deepcopy(data)), world_size=world)
+        except Exception:  # noqa: BLE001 - rejected
+            return ("error",)
+        return ("ok", bool(res.warnings), res.data_parallel_size, res.global_batch_size,
+                res.padded_vocab_size)
+
+    seen = set()
+    for _ in range(1500):
+        data: dict = {}
+        for section, name in rng.sample(keys, rng.randint(1, 10)):
+            data.setdefault(section, {})[name] = copy.deepcopy(rng.choice(space[section, name]))
+        world = rng.choice([None, 1, 2, 4, 8, 16])
+        ours = outcome(config_from_dict, validate_config, data, world)
+        assert ours == outcome(ref_from_dict, ref_validate, data, world), (data, world)
+        seen.add(ours[:2])
+    assert {("error",), ("ok", False), ("ok", True)} <= seen
