@@ -13,12 +13,16 @@ from nano_megatron_b200.inference import export_checkpoint
 
 def parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__)
-    p.add_argument("--checkpoint", type=Path, required=True, help="completed step directory")
-    p.add_argument("--output", type=Path, required=True, help="new inference artifact directory")
-    p.add_argument("--config", type=Path, help="training YAML for checkpoints without a usable "
-                   "embedded run_config")
-    p.add_argument("--tokenizer", type=Path, help="tokenizer artifact override (otherwise read "
-                   "from the checkpoint config)")
+    p.add_argument("--checkpoint", type=Path, required=True,
+                   help="a finished step_NNNNNNNN directory of a training run (any TP/PP/"
+                        "interleaved/ZeRO-3 layout)")
+    p.add_argument("--output", type=Path, required=True,
+                   help="where to write the artifact; must not exist yet")
+    p.add_argument("--config", type=Path,
+                   help="YAML to describe the model when the checkpoint's manifest carries no "
+                        "readable run config")
+    p.add_argument("--tokenizer", type=Path,
+                   help="tokenizer artifact to bundle instead of the one the run config names")
     return p
 
 

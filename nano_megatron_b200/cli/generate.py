@@ -12,21 +12,31 @@ from nano_megatron_b200.inference import GenerationResult, generate_from_artifac
 
 def parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__)
-    p.add_argument("--model", type=Path, required=True, help="inference artifact directory")
-    p.add_argument("--prompt", required=True, help="text prompt")
-    p.add_argument("--device", default="auto", help="auto, cpu, cuda, or cuda:N")
+    p.add_argument("--model", type=Path, required=True,
+                   help="artifact directory written by nano-megatron-export")
+    p.add_argument("--prompt", required=True, help="text to continue")
+    p.add_argument("--device", default="auto",
+                   help="'auto' uses CUDA when it is available; or cpu, cuda, cuda:N")
     p.add_argument("--dtype", choices=("auto", "float32", "bfloat16", "float16"),
-                   default="auto")
-    p.add_argument("--max-new-tokens", type=int, default=128)
-    p.add_argument("--temperature", type=float, default=0.8)
-    p.add_argument("--top-p", type=float, default=0.95)
-    p.add_argument("--top-k", type=int, default=0)
-    p.add_argument("--seed", type=int, default=1234)
+                   default="auto",
+                   help="'auto' = fp32 on CPU, the artifact's weight dtype on CUDA")
+    p.add_argument("--max-new-tokens", type=int, default=128,
+                   help="stop after this many sampled tokens (or at EOS)")
+    p.add_argument("--temperature", type=float, default=0.8,
+                   help="softmax temperature; 0 decodes greedily")
+    p.add_argument("--top-p", type=float, default=0.95,
+                   help="nucleus sampling mass (1 keeps the whole distribution)")
+    p.add_argument("--top-k", type=int, default=0,
+                   help="sample among the k most likely tokens only (0 = no limit)")
+    p.add_argument("--seed", type=int, default=1234, help="sampling RNG seed")
     p.add_argument("--add-bos", action=argparse.BooleanOptionalAction, default=True,
-                   help="prepend the tokenizer BOS token (default: true)")
+                   help="start the prompt with the tokenizer's BOS id (on by default)")
     p.add_argument("--kv-cache", action=argparse.BooleanOptionalAction, default=True,
-                   help="decode incrementally with a K/V cache (default: true)")
-    p.add_argument("--json", action="store_true", help="emit structured generation output")
+                   help="reuse cached keys/values between decode steps (on by default; "
+                        "--no-kv-cache recomputes the whole prefix every step)")
+    p.add_argument("--json", action="store_true",
+                   help="print the whole result (prompt, completion, token ids, stop reason) "
+                        "as one JSON object instead of the text")
     return p
 
 

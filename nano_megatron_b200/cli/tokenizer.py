@@ -27,43 +27,50 @@ from nano_megatron_b200.tokenizer import (
 def parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     sub = p.add_subparsers(dest="command", required=True)
-    t = sub.add_parser("train", help="train a byte-level BPE artifact from JSONL")
+    t = sub.add_parser("train", help="learn a byte-level BPE vocabulary from JSONL documents")
     t.add_argument("--input", type=Path, action="append", required=True,
-                   help="input JSONL path; repeat to train on multiple files")
-    t.add_argument("--output", type=Path, required=True, help="artifact directory")
-    t.add_argument("--vocab-size", type=int, default=8192)
-    t.add_argument("--min-frequency", type=int, default=2)
-    t.add_argument("--text-key", default="text")
+                   help="JSONL file of documents (give the flag several times for several files)")
+    t.add_argument("--output", type=Path, required=True,
+                   help="directory for the tokenizer artifact")
+    t.add_argument("--vocab-size", type=int, default=8192,
+                   help="target vocabulary size, special tokens included")
+    t.add_argument("--min-frequency", type=int, default=2,
+                   help="ignore merges seen fewer times than this")
+    t.add_argument("--text-key", default="text", help="JSON field that holds the document text")
     d = SpecialTokens()
-    t.add_argument("--unk-token", default=d.unk)
-    t.add_argument("--bos-token", default=d.bos)
-    t.add_argument("--eos-token", default=d.eos)
-    t.add_argument("--pad-token", default=d.pad)
-    t.add_argument("--show-progress", action="store_true")
-    pp = sub.add_parser("preprocess", help="encode JSONL into a structured flat-token corpus")
-    pp.add_argument("--input", type=Path, required=True)
-    pp.add_argument("--output", type=Path, required=True)
-    pp.add_argument("--tokenizer", type=Path, required=True)
+    t.add_argument("--unk-token", default=d.unk, help="spelling of the unknown-token marker")
+    t.add_argument("--bos-token", default=d.bos, help="spelling of the begin-of-sequence marker")
+    t.add_argument("--eos-token", default=d.eos, help="spelling of the end-of-sequence marker")
+    t.add_argument("--pad-token", default=d.pad, help="spelling of the padding marker")
+    t.add_argument("--show-progress", action="store_true", help="print trainer progress")
+    pp = sub.add_parser("preprocess", help="tokenize JSONL documents into one flat token corpus")
+    pp.add_argument("--input", type=Path, required=True, help="JSONL file of documents")
+    pp.add_argument("--output", type=Path, required=True,
+                    help="corpus file (.pt) or directory (mmap) to create")
+    pp.add_argument("--tokenizer", type=Path, required=True, help="tokenizer artifact to encode with")
     pp.add_argument("--format", choices=("pt", "mmap"), default="pt",
-                    help="output storage format (default: pt)")
-    pp.add_argument("--text-key", default="text")
+                    help="'pt': one torch file; 'mmap': memory-mapped token array plus metadata")
+    pp.add_argument("--text-key", default="text", help="JSON field that holds the document text")
     pp.add_argument("--append-eos", action=argparse.BooleanOptionalAction, default=True,
-                    help="append exactly one EOS token after each document")
-    s = sub.add_parser("split", help="deterministically split JSONL documents into train and "
-                       "validation files")
-    s.add_argument("--input", type=Path, required=True)
-    s.add_argument("--train-output", type=Path, required=True)
-    s.add_argument("--validation-output", type=Path, required=True)
-    s.add_argument("--validation-fraction", type=float, default=0.1)
-    s.add_argument("--seed", type=int, default=1234)
-    s.add_argument("--text-key", default="text")
-    i = sub.add_parser("inspect", help="inspect a tokenizer encoding or mmap corpus metadata")
+                    help="end every document with one EOS id (on by default)")
+    s = sub.add_parser("split", help="divide JSONL documents into train and validation files by "
+                       "a seeded hash of their text")
+    s.add_argument("--input", type=Path, required=True, help="JSONL file of documents")
+    s.add_argument("--train-output", type=Path, required=True, help="JSONL file for training")
+    s.add_argument("--validation-output", type=Path, required=True,
+                   help="JSONL file for validation")
+    s.add_argument("--validation-fraction", type=float, default=0.1,
+                   help="expected share of documents routed to validation")
+    s.add_argument("--seed", type=int, default=1234, help="salt of the routing hash")
+    s.add_argument("--text-key", default="text", help="JSON field that holds the document text")
+    i = sub.add_parser("inspect", help="show how a tokenizer encodes text, or describe a mmap "
+                       "corpus")
     tgt = i.add_mutually_exclusive_group(required=True)
-    tgt.add_argument("--tokenizer", type=Path)
-    tgt.add_argument("--mmap", type=Path, help="mmap token-corpus artifact directory")
-    i.add_argument("--text")
-    i.add_argument("--add-bos", action="store_true")
-    i.add_argument("--add-eos", action="store_true")
+    tgt.add_argument("--tokenizer", type=Path, help="tokenizer artifact to describe")
+    tgt.add_argument("--mmap", type=Path, help="mmap corpus directory to describe")
+    i.add_argument("--text", help="text to encode with --tokenizer")
+    i.add_argument("--add-bos", action="store_true", help="prefix the encoding with BOS")
+    i.add_argument("--add-eos", action="store_true", help="end the encoding with EOS")
     return p
 
 

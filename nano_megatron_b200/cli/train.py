@@ -29,11 +29,17 @@ from nano_megatron_b200.training.engine import build_training_components
 
 def parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
-    p.add_argument("--config", type=Path, required=True, help="YAML training configuration")
+    p.add_argument("--config", type=Path, required=True,
+                   help="YAML file describing the run (model, parallel layout, data, "
+                        "optimizer, ...)")
     p.add_argument("--set", dest="overrides", action="append", default=[], metavar="KEY=VALUE",
-                   help="override a dotted configuration key; may be repeated")
-    p.add_argument("--resume", type=Path, help="checkpoint directory to restore")
-    p.add_argument("--max-steps", type=int, help="override only this invocation's stop step")
+                   help="section.field=value applied on top of the YAML; give it once per field")
+    p.add_argument("--resume", type=Path,
+                   help="step directory of an earlier run to continue from (weights, "
+                        "optimizer, data position, RNG)")
+    p.add_argument("--max-steps", type=int,
+                   help="stop at this step in this invocation, without changing the stored "
+                        "config")
     p.add_argument("--profile-dir", type=Path,
                    help="write a torch.profiler Chrome trace per rank for --profile-steps")
     p.add_argument("--profile-steps", default="2:4", metavar="START:STOP",
