@@ -110,6 +110,29 @@ class TrainerState:
         self.best_validation_checkpoint = bc
 
 
+def check_token_ranges(batch, vocab_size: int) -> None:
+    """Reject a batch whose token ids fall outside the vocabulary, on the host.
+
+    The fused kernels treat an id outside a rank's vocabulary shard as "another rank's
+    token" (a zero embedding row, no logit of its own), which is right for shards but
+    would silently train on garbage for an id outside the whole vocabulary, e.g. after a
+    tokenizer/model mismatch. Inputs must lie in [0, vocab_size); labels below 0 are
+    ignored positions and otherwise must lie below vocab_size. Only CPU tensors are checked
+    (before the copy to the device), so the check never synchronises with the GPU.
+    """
+    if not isinstance(batch, dict):
+        return
+    for key, allow_negative in (("input_ids", False), ("labels", True)):
+        t = batch.get(key)
+        if not isinstance(t, torch.Tensor) or t.is_cuda or t.numel() == 0:
+            continue
+        hi, lo = int(t.max()), int(t.min())
+        if hi >= vocab_size or (lo < 0 and not allow_negative):
+            bad = hi if hi >= vocab_size else lo
+            raise ValueError(f"batch[{key!r}] holds token id {bad}, outside the model's "
+                             f"vocabulary of {vocab_size} (model.vocab_size)")
+
+
 def _move_to_device(batch, device):
     if isinstance(batch, torch.Tensor):
         return batch.to(device, non_blocking=True)
@@ -182,6 +205,7 @@ class Trainer:
 
     # ------------------------------------------------------------------ steps
     def _prepare_batch(self, batch):
+        check_token_ranges(batch, self.config.model.vocab_size)
         batch = self.batch_router.route(batch)
         batch = _move_to_device(batch, self.device)
         micro = split_microbatches(batch, self.micro_batch_size)

@@ -112,3 +112,20 @@ def test_interval_metrics_weight_loss_by_tokens_and_average_the_rest():
     acc = SimpleNamespace(loss_sum=torch.tensor(12.0), token_count=torch.tensor(6.0))
     s, n = aggregate_loss_metrics(acc, None, torch.device("cpu"))
     assert (float(s), float(n)) == (12.0, 6.0) and s.dtype == torch.float64
+
+
+def test_token_ids_outside_the_vocabulary_are_rejected_on_the_host():
+    import torch
+
+    from nano_megatron_b200.training.trainer import check_token_ranges
+
+    ok = {"input_ids": torch.tensor([[0, 5, 9]]), "labels": torch.tensor([[5, 9, -100]])}
+    check_token_ranges(ok, 10)
+    check_token_ranges(None, 10)                       # non-source ranks carry no batch
+    check_token_ranges({"input_ids": torch.empty(0, dtype=torch.long)}, 10)
+    with pytest.raises(ValueError, match="token id 10"):
+        check_token_ranges({"input_ids": torch.tensor([[1, 10]])}, 10)
+    with pytest.raises(ValueError, match="token id -1"):
+        check_token_ranges({"input_ids": torch.tensor([[-1, 2]])}, 10)
+    with pytest.raises(ValueError, match="labels"):
+        check_token_ranges({"labels": torch.tensor([[3, 12]])}, 10)
