@@ -12,4 +12,14 @@ from .manifest import (
 )
 from .mapping import ShardedState, infer_shard_metadata, iter_tensors
 
-__all__ = [n for n in dir() if not n.startswith("_")]
+__all__ = [n for n in dir() if not n.startswith("_")] + ["TrainerState"]
+
+
+def __getattr__(name: str):
+    # TrainerState (what a checkpoint's trainer entry restores) lives with the trainer;
+    # imported on first use, since the trainer imports this package
+    if name == "TrainerState":
+        from nano_megatron_b200.training.trainer import TrainerState
+
+        return TrainerState
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

@@ -12,6 +12,9 @@ from .strategies import (
 )
 from .zero3 import Zero3Strategy
 
+# the reference's spellings of the ZeRO strategy classes
+ZeRO1Strategy, ZeRO2Strategy, ZeRO3Strategy = Zero1Strategy, Zero2Strategy, Zero3Strategy
+
 _STRATEGIES = {"ddp": DDPStrategy, "replicated": ReplicatedStrategy, "zero1": Zero1Strategy,
                "zero2": Zero2Strategy, "zero3": Zero3Strategy}
 

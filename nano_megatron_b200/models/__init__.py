@@ -1,1 +1,5 @@
-"""Model families."""
+"""Model families (the dense GPT in :mod:`.gpt`)."""
+
+from .gpt import GPTModel, GPTModelBuilder, GPTOutput
+
+__all__ = ["GPTModel", "GPTModelBuilder", "GPTOutput"]

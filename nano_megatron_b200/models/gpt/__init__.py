@@ -4,5 +4,6 @@ from .builder import BuiltGPTPipeline, BuiltGPTStage, GPTModelBuilder, GPTPipeli
 from .factory import DenseGPTComponents, GPTComponentFactory
 from .model import GPTAttention, GPTLayer, GPTMLP, GPTModel, GPTOutput
 from .tied_embeddings import TiedEmbeddingSynchronizer
+from nano_megatron_b200.pipeline_parallel.partition import LayerPartition
 
 __all__ = [n for n in dir() if not n.startswith("_")]

@@ -4,9 +4,9 @@ from .axes import DEFAULT_RANK_ORDER, PARALLEL_AXES, ParallelAxis, ParallelCoord
 from .context import ParallelContext
 from .domains import ParameterDomain, ParameterDomainRegistry, ParameterPlacement, default_replica_group
 from .group import LocalGroup, ParallelGroup, require_parallel_group
-from .group_plan import DEFAULT_GROUP_PLAN, GroupKey, GroupPlan, GroupSpec, PlannedGroup
+from .group_plan import DEFAULT_GROUP_PLAN, GroupKey, GroupKeyLike, GroupPlan, GroupSpec, PlannedGroup
 from .layout import TensorLayout
-from .registry import ParallelGroupRegistry
+from .registry import GroupRegistry, ParallelGroupRegistry
 from .rng import ParallelRNG, RNGStream
 from .topology import ParallelTopology
 

@@ -1,7 +1,14 @@
 """Pipeline schedules (GPipe, 1F1B, interleaved 1F1B) and the executor."""
 
 from .base import LossAccumulator, extract_loss
+from .executor import PipelineScheduleExecutor
 from .no_pipeline import NoPipelineSchedule
+from .plans import (
+    build_1f1b_plan,
+    build_gpipe_plan,
+    build_interleaved_plan,
+    build_interleaved_schedule_table,
+)
 
 
 def build_schedule(config, model, parallel, data_parallel):
@@ -17,4 +24,6 @@ def build_schedule(config, model, parallel, data_parallel):
     return build_pipeline_schedule(config, model, parallel, data_parallel)
 
 
-__all__ = ["LossAccumulator", "NoPipelineSchedule", "build_schedule", "extract_loss"]
+__all__ = ["LossAccumulator", "NoPipelineSchedule", "PipelineScheduleExecutor",
+           "build_1f1b_plan", "build_gpipe_plan", "build_interleaved_plan",
+           "build_interleaved_schedule_table", "build_schedule", "extract_loss"]

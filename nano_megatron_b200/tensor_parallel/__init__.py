@@ -9,6 +9,8 @@ from .comm import (
     reduce_from_tensor_parallel_region,
     reduce_scatter_dim0,
     reduce_scatter_to_sequence_parallel_region,
+    register_sequence_parallel_gradient_hooks,
+    scatter_to_sequence_parallel_region,
     scatter_to_tensor_parallel_region,
 )
 from .cross_entropy import VocabParallelCrossEntropy, vocab_parallel_ce_rows

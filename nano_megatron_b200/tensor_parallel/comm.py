@@ -178,3 +178,42 @@ def gather_from_sequence_parallel_region(x, group, *, sequence_dim: int = 0):
 def reduce_scatter_to_sequence_parallel_region(x, group, *, sequence_dim: int = 0):
     """Reduce-scatter along the sequence dimension; all-gather in backward."""
     return x if group.size == 1 else _SeqReduceScatter.apply(x, group, sequence_dim % x.dim())
+
+
+def scatter_to_sequence_parallel_region(x, group, *, sequence_dim: int = 0):
+    """Keep this rank's block of the sequence dimension (no reduction: the input is
+    replicated over the group); all-gather in backward."""
+    return x if group.size == 1 else _Scatter.apply(x, group, sequence_dim % x.dim())
+
+
+_SP_HOOKED = "_nmb_sequence_parallel_hooked"
+
+
+def register_sequence_parallel_gradient_hooks(module, group, *, recurse: bool = True) -> None:
+    """Sum, over the group, the gradients of ``module``'s parameters that are replicated
+    across sequence-parallel ranks (norm weights, biases of row-parallel layers): each rank
+    saw only its sequence block, so the full gradient is the sum.
+
+    For modules trained through ``.grad`` (plain autograd): a post-accumulate hook
+    all-reduces each parameter's gradient as soon as autograd has finished it. Registering
+    twice for the same parameter and group is a no-op. The fused GPT blocks of this
+    framework accumulate into ``main_grad`` instead and sum these gradients once per step
+    in the data-parallel strategy (``_reduce_sequence_parallel_grads``), without hooks.
+    """
+    if group is None or group.size == 1:
+        return
+    pg = _pg(group)
+    for p in module.parameters(recurse=recurse):
+        seen = getattr(p, _SP_HOOKED, None)
+        if seen is None:
+            seen = set()
+            setattr(p, _SP_HOOKED, seen)
+        if id(pg) in seen:
+            continue
+        seen.add(id(pg))
+
+        def _sum_over_sequence_ranks(param, _pg=pg):
+            if param.grad is not None:
+                dist.all_reduce(param.grad, group=_pg)
+
+        p.register_post_accumulate_grad_hook(_sum_over_sequence_ranks)
