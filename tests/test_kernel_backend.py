@@ -1,5 +1,5 @@
 """The kernel-backend seam (``nn.kernels``): linear, RMSNorm and local attention against
-plain PyTorch (CPU here; the same calls on a B200 in ``test_kernel_backend_gpu.py``)."""
+plain PyTorch (CPU here; the same calls on a B200 in ``test_zzz_kernel_backend_gpu.py``)."""
 
 import math
 
