@@ -42,6 +42,10 @@ struct CpSlots {
 };
 
 // acc[i] += sum over set bits s of mask: slot_s[i], once every rank's flag is current.
+// Waiting for every rank, not only the ranks in `mask`, is what makes each layer's
+// backward a barrier: with only the contributors' flags, a rank whose keys nobody sees
+// (the last rank of a causal layout) could run two layers ahead and reuse a return
+// slot's parity before its owner has read it (model-checked on the host).
 __global__ void cp_reduce_kernel(float4* __restrict__ acc, CpSlots slots, int n, uint32_t mask,
                                  int64_t n4, const uint32_t* flags, const uint32_t* epoch_ptr,
                                  int* status) {
