@@ -132,9 +132,9 @@ class B200KernelBackend:
         if dropout_p:
             raise NotImplementedError("attention-probability dropout is not implemented")
         s = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
-        to_bshd = (lambda t: t.transpose(1, 2).contiguous())
-        o = _AttentionFn.apply(to_bshd(q), to_bshd(k), to_bshd(v), bool(causal),
-                               int(sequence_offset), float(s))
+        # the kernels take [B, S, H, D] with contiguous heads
+        qb, kb, vb = (t.transpose(1, 2).contiguous() for t in (q, k, v))
+        o = _AttentionFn.apply(qb, kb, vb, bool(causal), int(sequence_offset), float(s))
         return o.transpose(1, 2)
 
 
