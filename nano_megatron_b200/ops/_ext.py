@@ -52,6 +52,8 @@ STATUS_NAMES = {
     0x201: "attention wait timed out",
     0x301: "peer flag wait timed out",
     0x302: "peer barrier wait timed out",
+    0x401: "data-parallel replica flag wait timed out",
+    0x501: "context-parallel flag wait timed out",
 }
 
 
