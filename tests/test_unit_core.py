@@ -400,3 +400,16 @@ def test_bench_clock_sampler_reads_nvml_by_uuid():
     assert seen["uuid"] == "GPU-1234-abcd"
     assert out["samples"] >= 4 and out["sm_max_mhz"] == 1965
     assert out["sm_mhz"] in (1800, 1965) and out["reasons"] == ["sw_power_cap"]
+
+
+def test_host_decodes_every_device_status_code():
+    """Every error code the kernels can write (csrc/common.cuh StatusCode) has a name in
+    the host decoder that Trainer.fit and bench.py raise with."""
+    import re
+    from pathlib import Path
+
+    from nano_megatron_b200.ops._ext import STATUS_NAMES
+
+    header = (Path(__file__).parents[1] / "nano_megatron_b200" / "csrc" / "common.cuh").read_text()
+    codes = {int(v, 16) for v in re.findall(r"kStatus\w+\s*=\s*(0x[0-9a-fA-F]+)", header)}
+    assert codes and codes - set(STATUS_NAMES) == set()
