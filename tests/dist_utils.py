@@ -69,16 +69,24 @@ def _gpu_entry(rank, world, port, fn, args, errq):
             dist.destroy_process_group()
 
 
+def free_port() -> int:
+    """A TCP port on 127.0.0.1 that nothing listens on right now, chosen by the OS (a
+    fixed random range collides when several tests or workers start rendezvous at once)."""
+    import socket
+
+    with socket.socket(socket.AF_INET, socket.SOCK_STREAM) as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
 def run_gpu_ranks(world: int, fn, *args, timeout: float = 300.0) -> None:
     """Run ``fn(rank, world, *args)`` as one process per GPU (rank r on cuda:r) with the
     torchrun environment set (NCCL rendezvous on 127.0.0.1, NVLS off); ``fn`` initialises
     its own process group. Re-raises the first failure; kills ranks that outlive
     ``timeout``."""
-    import random
-
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
-    port = random.randint(20000, 40000)
+    port = free_port()
     procs = [ctx.Process(target=_gpu_entry, args=(r, world, port, fn, args, errq))
              for r in range(world)]
     for p in procs:

@@ -74,13 +74,13 @@ def _worker(rank, world, port, errq, rs_in_kernel=False):
 def test_fused_tp_collectives_two_gpus(rs_in_kernel):
     if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
-    import random
+    from dist_utils import free_port
 
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
-    port = random.randint(20000, 40000)
+    port = free_port()
     procs = [ctx.Process(target=_worker, args=(r, WORLD, port, errq, rs_in_kernel))
              for r in range(WORLD)]
     for p in procs:

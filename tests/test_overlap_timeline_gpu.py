@@ -88,13 +88,13 @@ def _worker(rank, world, port, out_dir, errq):
 def test_ddp_all_reduce_overlaps_backward_gemms(tmp_path):
     if not torch.cuda.is_available() or torch.cuda.device_count() < WORLD:
         pytest.skip(f"needs {WORLD} GPUs")
-    import random
+    from dist_utils import free_port
 
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     errq = ctx.SimpleQueue()
-    port = random.randint(20000, 40000)
+    port = free_port()
     procs = [ctx.Process(target=_worker, args=(r, WORLD, port, str(tmp_path), errq))
              for r in range(WORLD)]
     for p in procs:

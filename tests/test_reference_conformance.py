@@ -300,7 +300,7 @@ LAYOUTS = {
 def test_multirank_training_curve_matches_reference(ref, tmp_path, layout):
     import json
     import os
-    import random
+    from dist_utils import free_port
     import subprocess
 
     import yaml
@@ -336,7 +336,7 @@ def test_multirank_training_curve_matches_reference(ref, tmp_path, layout):
     world = par["tensor"] * par["pipeline"] * par["context"] * par.get("expert", 1) * \
         (par["data"] or 1)
     env = dict(os.environ, PYTHONPATH=str(REF), OMP_NUM_THREADS="1")
-    port = random.randint(30000, 45000)
+    port = free_port()
     # the two frameworks train concurrently (independent processes and rendezvous)
     proc = subprocess.Popen([sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
                              "--nproc-per-node", str(world), "--master-addr", "127.0.0.1",
@@ -371,7 +371,7 @@ def test_multirank_training_curve_matches_reference(ref, tmp_path, layout):
 def _ref_cli_start(cfg: Path, tmp: Path, *extra: str, nproc: int = 1):
     """Start the reference's training CLI (torchrun for several ranks) in the background."""
     import os
-    import random
+    from dist_utils import free_port
     import subprocess
 
     env = dict(os.environ, PYTHONPATH=str(REF), OMP_NUM_THREADS="1")
@@ -380,7 +380,7 @@ def _ref_cli_start(cfg: Path, tmp: Path, *extra: str, nproc: int = 1):
     else:
         cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", "--nproc-per-node",
                str(nproc), "--master-addr", "127.0.0.1", "--master-port",
-               str(random.randint(30000, 45000)), "-m", "nano_megatron.cli.train", "--config",
+               str(free_port()), "-m", "nano_megatron.cli.train", "--config",
                str(cfg), *extra]
     return subprocess.Popen(cmd, env=env, stdout=subprocess.PIPE, stderr=subprocess.PIPE,
                             text=True, cwd=tmp)
