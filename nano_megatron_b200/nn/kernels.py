@@ -47,8 +47,8 @@ class KernelBackend(Protocol):
 class _LinearFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, bias):
-        rows = x.reshape(-1, x.shape[-1])
-        y = F.linear(rows.contiguous(), weight)
+        rows = x.reshape(-1, x.shape[-1]).contiguous()
+        y = F.linear(rows, weight)
         if bias is not None:
             y = y + bias
         ctx.save_for_backward(rows, weight)
