@@ -466,6 +466,34 @@ def unavailable(why: str) -> int:
     return 0
 
 
+def model_flops_per_token(m: dict) -> float:
+    """Training FLOPs per token of the GPT (forward + backward = 3 x forward): 6 x the
+    parameters of every matrix product (QKV, output, gate/up, down, LM head) plus causal
+    attention, 6 x layers x hidden x sequence (score and value products over half the
+    context on average). Recomputation under activation checkpointing is not counted."""
+    h, f, layers = m["hidden_size"], m["ffn_hidden_size"], m["layers"]
+    hq = m["heads"]
+    hkv = m.get("kv_heads") or hq
+    d = h // hq
+    per_layer = h * (hq + 2 * hkv) * d + h * h + h * 2 * f + f * h
+    return 6.0 * (layers * per_layer + m["vocab_size"] * h) + 6.0 * layers * h * m["seq_length"]
+
+
+def roofline(w: dict, tokens_per_s: float, n_gpus: int) -> dict:
+    """Model TFLOP/s per GPU and its fraction of the measured sustained bf16 GEMM rate
+    (``MEASURED_PEAKS.json``, when present)."""
+    per_gpu = model_flops_per_token(w["model"]) * tokens_per_s / n_gpus / 1e12
+    out = {"model_flops_per_token": model_flops_per_token(w["model"]),
+           "model_tflops_per_gpu": per_gpu}
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            sustained = json.load(fh).get("bf16_tflops_sustained")
+        if sustained:
+            out["frac_of_measured_bf16_sustained"] = per_gpu / float(sustained)
+    return out
+
+
 def report(args, rank, dev_ms, e2e_ms, e2e_wall_ms, clocks, launches, *, impl):
     w = WORKLOADS[args.config]
     seq, gb = w["model"]["seq_length"], w["global_batch"]
@@ -493,6 +521,10 @@ def report(args, rank, dev_ms, e2e_ms, e2e_wall_ms, clocks, launches, *, impl):
     }
     if launches is not None:
         line["gpu_launches"] = launches
+    try:
+        line["roofline"] = roofline(w, value, args.gpus)
+    except Exception as error:  # noqa: BLE001 - an annotation never costs the measurement
+        line["roofline"] = {"error": repr(error)}
     if rank == 0:
         print(json.dumps(line), flush=True)
 
