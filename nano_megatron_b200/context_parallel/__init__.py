@@ -20,7 +20,7 @@ holds chunks r and 2*CP-1-r of 2*CP equal chunks) so causal work is balanced.
 
 from __future__ import annotations
 
-from .attention import (AllGatherContextParallelAttention,
+from .attention import (AllGatherContextParallelAttention, ContextParallelAttention,
                         PeerAllGatherContextParallelAttention, PeerRingContextParallelAttention,
                         RingContextParallelAttention)
 from .utils import local_positions, shard_sequence, unshard_sequence
@@ -42,7 +42,8 @@ def build_context_parallel_attention(config, parallel):
     raise ValueError(f"unknown context-parallel backend {backend!r}")
 
 
-__all__ = ["AllGatherContextParallelAttention", "PeerAllGatherContextParallelAttention",
+__all__ = ["AllGatherContextParallelAttention", "ContextParallelAttention",
+           "PeerAllGatherContextParallelAttention",
            "PeerRingContextParallelAttention",
            "RingContextParallelAttention",
            "build_context_parallel_attention", "local_positions", "shard_sequence",

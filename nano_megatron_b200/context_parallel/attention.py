@@ -2,6 +2,8 @@
 
 from __future__ import annotations
 
+from typing import Protocol
+
 import torch
 import torch.distributed as dist
 
@@ -9,6 +11,27 @@ from nano_megatron_b200.ops import functional as F
 from nano_megatron_b200.tensor_parallel.comm import all_gather_dim0, reduce_scatter_dim0
 
 from .utils import chunk_ids, gathered_to_global_order, local_positions
+
+
+class ContextParallelAttention(Protocol):
+    """What the fused attention block (``models/gpt/blocks.py``) calls on its attention
+    core: the local core and every context-parallel core implement it.
+
+    ``forward`` writes the output of this rank's query rows into ``o`` ([S, B, Hq, D]
+    view) and returns the base-2 log-sum-exp [B, Hq, S]; ``backward`` writes dq, dk, dv.
+    q/k/v are [B, S, H, D] strided views of the fused QKV buffer; ``mb`` carries the
+    microbatch's positions and layer. ``applies_inverse_rope``: whether ``backward``
+    already returns gradients with respect to the pre-rotation q/k (else the block
+    applies the inverse rotation). The reference's interface of the same name takes and
+    returns [B, H, S, D] tensors (src/nano_megatron/context_parallel/interface.py:10-22);
+    that form is :func:`nano_megatron_b200.nn.kernels.B200KernelBackend.local_attention`.
+    """
+
+    applies_inverse_rope: bool
+
+    def forward(self, q, k, v, o, mb) -> torch.Tensor: ...
+
+    def backward(self, q, k, v, o, do, lse, dq, dk, dv, mb, inv_freq) -> None: ...
 
 
 class _CPBase:
