@@ -16,7 +16,6 @@ from __future__ import annotations
 import hashlib
 import json
 from pathlib import Path
-from typing import Any
 
 import numpy as np
 import torch

@@ -25,7 +25,7 @@ import torch
 from nano_megatron_b200.utils.profiling import nvtx_range
 
 from ..p2p import P2PCommunicator
-from .base import LossAccumulator, batch_labels, extract_loss
+from .base import LossAccumulator, extract_loss
 from .plans import build_1f1b_plan, build_gpipe_plan, build_interleaved_plan, validate_plan
 
 _DEBUG = os.environ.get("NMB_PP_DEBUG", "0") == "1"

@@ -16,13 +16,12 @@ from __future__ import annotations
 import math
 import time
 from pathlib import Path
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from typing import Any
 
 import torch
 import torch.distributed as dist
 
-from nano_megatron_b200.parallel.group_plan import GroupKey
 from nano_megatron_b200.utils.profiling import nvtx_range
 from nano_megatron_b200.utils.timing import DeviceStepTimer, StepPhaseTimer, summarize_phases
 
