@@ -12,8 +12,10 @@ from .strategies import (
 )
 from .zero3 import Zero3Strategy
 
-# the reference's spellings of the ZeRO strategy classes
+# the reference's spellings of the ZeRO strategy classes and of a bucket's parameter
+# range (same fields; this one also records whether the gradient is SP-replicated)
 ZeRO1Strategy, ZeRO2Strategy, ZeRO3Strategy = Zero1Strategy, Zero2Strategy, Zero3Strategy
+ParameterSlice = ParamSlice
 
 _STRATEGIES = {"ddp": DDPStrategy, "replicated": ReplicatedStrategy, "zero1": Zero1Strategy,
                "zero2": Zero2Strategy, "zero3": Zero3Strategy}
